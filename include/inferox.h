@@ -1,0 +1,265 @@
+/*
+ * inferox.h — C ABI of libinferox_b200.so, the sm_100a implementation of
+ * phraakture/inferox's token loop.
+ *
+ * The reference is a Rust crate with no FFI; its call surface is the Rust API
+ * of `ops`, `model` and `sampler`. Each entry point below names the reference
+ * item it replaces (path:line inside the reference crate). A Rust `cuda`
+ * module would bind these with `extern "C"` declarations.
+ *
+ * Conventions
+ *  - Every call returns ifx_status; IFX_OK is 0. ifx_last_error() gives a
+ *    thread-local message for the last failure on the calling thread.
+ *  - Model-level calls take and return HOST buffers (as the Rust API does);
+ *    the library owns all device memory behind ifx_model / ifx_kv.
+ *  - Op-level calls (ifx_op_*) take DEVICE pointers and a cudaStream_t passed
+ *    as void* (NULL = legacy default stream); they are asynchronous unless
+ *    stated otherwise. Shape mismatches that panic in the reference
+ *    (assert_eq!, ops.rs:16-18) return IFX_ERR_SHAPE instead.
+ *  - No call is re-entrant on the same ifx_model; one model per device.
+ */
+#ifndef INFEROX_H
+#define INFEROX_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* gguf::Error (src/gguf/error.rs:6-42) in declaration order, then the codes
+ * the GPU build adds. */
+typedef enum ifx_status {
+  IFX_OK = 0,
+  IFX_ERR_IO = 1,
+  IFX_ERR_INVALID_MAGIC = 2,
+  IFX_ERR_UNSUPPORTED_VERSION = 3,
+  IFX_ERR_UNKNOWN_VALUE_TYPE = 4,
+  IFX_ERR_UNKNOWN_TENSOR_TYPE = 5,
+  IFX_ERR_INVALID_UTF8 = 6,
+  IFX_ERR_INVALID_SHAPE = 7,
+  IFX_ERR_UNEXPECTED_EOF = 8,
+  IFX_ERR_TENSOR_NOT_FOUND = 9,
+  IFX_ERR_INVALID_TENSOR_INDEX = 10,
+  IFX_ERR_TENSOR_OFFSET_OVERFLOW = 11,
+  IFX_ERR_UNSUPPORTED_ARCHITECTURE = 12,
+  IFX_ERR_SHAPE = 20,            /* replaces ops.rs assert_eq! panics */
+  IFX_ERR_CUDA = 21,             /* CUDA runtime/driver failure */
+  IFX_ERR_NCCL = 22,             /* NCCL failure (tensor parallel) */
+  IFX_ERR_TIMEOUT = 23,          /* a bounded device wait gave up */
+  IFX_ERR_INVALID_ARGUMENT = 24, /* null pointer, zero size, bad enum */
+  IFX_ERR_OUT_OF_MEMORY = 25,
+  IFX_ERR_UNSUPPORTED = 26       /* valid input this build does not run */
+} ifx_status;
+
+/* TensorType ids (src/gguf/types.rs:68-99) the kernels accept. */
+enum {
+  IFX_TYPE_F32 = 0,
+  IFX_TYPE_F16 = 1,
+  IFX_TYPE_Q4_0 = 2,
+  IFX_TYPE_Q8_0 = 7,
+  IFX_TYPE_Q4_K = 12,
+  IFX_TYPE_Q6_K = 14,
+  IFX_TYPE_Q8_K = 15
+};
+
+const char *ifx_last_error(void);
+const char *ifx_status_name(ifx_status s);
+/* Library version, (major << 16) | minor. */
+int ifx_version(void);
+
+/* Config (src/model/config.rs:5-30), filled by Config::from_gguf rules
+ * (config.rs:34-84). */
+typedef struct ifx_config {
+  uint32_t vocab_size;
+  uint64_t hidden_size, n_layers, n_heads, n_kv_heads, head_dim;
+  uint64_t intermediate_size;
+  float norm_eps, rope_base;
+  uint64_t rope_dim, context_length;
+  char architecture[64];
+} ifx_config;
+
+/* Load options (no reference counterpart: device placement and the
+ * tensor-parallel split are new). */
+typedef struct ifx_load_opts {
+  int device;      /* CUDA device ordinal */
+  int tp_size;     /* tensor-parallel ranks (1, 2, 4, 8) */
+  int tp_rank;     /* this process's rank */
+  void *nccl_comm; /* ncclComm_t for tp_size > 1, owned by the caller */
+  int rope_compat; /* 1 (default): decode applies RoPE at position 0 and
+                      prefill at 0..n, exactly as forward.rs:243-244,371-372;
+                      0: true positions (cache offset + t) */
+  int use_graphs;  /* 1 (default): decode steps replay CUDA graphs */
+} ifx_load_opts;
+
+void ifx_load_opts_default(ifx_load_opts *o);
+
+typedef struct ifx_model ifx_model;
+typedef struct ifx_kv ifx_kv;
+
+/* Model::open (src/model/mod.rs:64-92): parse the GGUF (file.rs:57-116),
+ * read the config, wire blk.{i}.* tensors, then upload and repack every
+ * weight once (the per-call dequant of weights.rs:66-74 disappears). */
+ifx_status ifx_model_load(const char *path, const ifx_load_opts *opts,
+                          ifx_model **out);
+/* Same, from a GGUF image already in host memory (no file). */
+ifx_status ifx_model_load_mem(const void *bytes, size_t len,
+                              const ifx_load_opts *opts, ifx_model **out);
+void ifx_model_free(ifx_model *m);
+/* Model.config (src/model/mod.rs:54). */
+ifx_status ifx_model_config(const ifx_model *m, ifx_config *out);
+/* Quantised weight bytes one batch-1 decode step reads on this rank
+ * (every matmul weight + norms + one embedding row). */
+uint64_t ifx_model_decode_weight_bytes(const ifx_model *m);
+
+/* KvCache::new (src/model/cache.rs:16-24): device-resident, f16,
+ * [layer][kv_head][max_seq][head_dim]; sharded by kv-head under TP. */
+ifx_status ifx_kv_create(ifx_model *m, size_t max_seq_len, ifx_kv **out);
+void ifx_kv_free(ifx_kv *kv);
+/* KvCache::clear (cache.rs:26-28). */
+ifx_status ifx_kv_clear(ifx_kv *kv);
+/* KvCache::len (cache.rs:31-33). */
+size_t ifx_kv_len(const ifx_kv *kv);
+/* Test hook: copy layer `layer`'s K (which_v = 0) or V cache rows [0, len)
+ * to host as f32 [len, n_kv_heads_local * head_dim]. */
+ifx_status ifx_kv_read(const ifx_kv *kv, size_t layer, int which_v,
+                       float *out_host);
+
+/* Model::prefill (src/model/forward.rs:496-538): ids must all be < vocab
+ * (else IFX_ERR_INVALID_TENSOR_INDEX, forward.rs:501-503). logits_host is
+ * [n, vocab] (last_row_only = 0) or [vocab] (last_row_only = 1), or NULL. */
+ifx_status ifx_prefill(ifx_model *m, ifx_kv *kv, const uint32_t *ids, size_t n,
+                       float *logits_host, int last_row_only);
+/* Model::decode_step (forward.rs:543-586): token >= vocab gives
+ * IFX_ERR_INVALID_TENSOR_INDEX (forward.rs:552-554). logits_host: [vocab]
+ * or NULL (skip the copy back). */
+ifx_status ifx_decode_step(ifx_model *m, ifx_kv *kv, uint32_t token,
+                           float *logits_host);
+/* Model::generate (forward.rs:592-612): kv.clear, prefill, then max_tokens
+ * greedy steps; the decode loop runs on the device (argmax feeds the next
+ * embedding without a host round trip). out_tokens: [max_tokens]. */
+ifx_status ifx_generate(ifx_model *m, ifx_kv *kv, const uint32_t *prompt,
+                        size_t n_prompt, size_t max_tokens,
+                        uint32_t *out_tokens);
+
+/* Continue greedy decoding from the current cache state: feed `token`, then
+ * each step's argmax (last index on ties) to the next step, n_steps times,
+ * with no host round trip (the loop of forward.rs:605-609 on the device).
+ * out_tokens ([n_steps], nullable) receives the argmax after each step.
+ * device_ms (nullable) receives the CUDA-event time of the n_steps steps on
+ * the model's stream. */
+ifx_status ifx_decode_greedy(ifx_model *m, ifx_kv *kv, uint32_t token,
+                             size_t n_steps, uint32_t *out_tokens,
+                             float *device_ms);
+
+/* Sampler (src/sampler.rs:8-16). */
+typedef struct ifx_sampler {
+  float temperature; /* 0 = greedy argmax */
+  uint64_t top_k;    /* 0 disables */
+  float top_p;       /* 1.0 disables */
+} ifx_sampler;
+
+/* Sampler::sample (sampler.rs:28-73) on the device over the model's last
+ * logits (from the latest prefill/decode_step). The thread_rng draw is a
+ * counter-based Philox uniform from (seed, offset). */
+ifx_status ifx_sample(ifx_model *m, const ifx_sampler *s, uint64_t seed,
+                      uint64_t offset, uint32_t *token_out);
+
+/* ------------------------- op-level entry points ------------------------ */
+/* dequantize_f32 (src/gguf/dequant.rs:10-31): bit-exact with the
+ * reference's per-type loops (dequant.rs:40-232). */
+ifx_status ifx_op_dequantize(int type, const void *bytes_dev, size_t nbytes,
+                             float *out_dev, size_t n_out, void *stream);
+/* matmul (src/ops.rs:15-26): C[m,n] = A[m,k] B[k,n], f32. */
+ifx_status ifx_op_matmul(const float *a, const float *b, float *c, size_t m,
+                         size_t n, size_t k, void *stream);
+/* matmul_t (src/ops.rs:33-44): C[m,n] = A[m,k] B[n,k]^T, f32. */
+ifx_status ifx_op_matmul_t(const float *a, const float *b, float *c, size_t m,
+                           size_t n, size_t k, void *stream);
+
+/* A quantised weight matrix [rows, cols] uploaded and repacked for the fused
+ * kernels. Replaces tensor_f32_by_index's dequant (weights.rs:66-74). */
+typedef struct ifx_qmatrix ifx_qmatrix;
+ifx_status ifx_qmatrix_create(int type, const void *gguf_bytes_host,
+                              size_t nbytes, size_t rows, size_t cols,
+                              int device, ifx_qmatrix **out);
+void ifx_qmatrix_free(ifx_qmatrix *w);
+/* tensor_f32_by_index + matmul_t fused (forward.rs:366-368 and every other
+ * matmul_t site): C[m, rows] = A[m, cols] W^T with dequant in registers. */
+ifx_status ifx_op_matmul_t_q(const float *a_dev, const ifx_qmatrix *w,
+                             float *c_dev, size_t m, void *stream);
+
+/* rms_norm / rms_norm_rows (src/ops.rs:155-180), in place. */
+ifx_status ifx_op_rms_norm_rows(float *x, const float *w, float eps,
+                                size_t rows, size_t hidden, void *stream);
+/* silu (ops.rs:183-187) in place; swiglu (ops.rs:190-197). */
+ifx_status ifx_op_silu(float *x, size_t n, void *stream);
+ifx_status ifx_op_swiglu(const float *gate, const float *up, float *out,
+                         size_t n, void *stream);
+/* add_in_place (ops.rs:212-217). */
+ifx_status ifx_op_add_in_place(float *out, const float *b, size_t n,
+                               void *stream);
+/* softmax_rows (ops.rs:223-239), in place. */
+ifx_status ifx_op_softmax_rows(float *x, size_t rows, size_t cols,
+                               void *stream);
+/* embedding_lookup (ops.rs:246-258). Synchronous: an out-of-range id
+ * returns IFX_ERR_INVALID_TENSOR_INDEX (the reference panics). */
+ifx_status ifx_op_embedding_lookup(const float *emb, size_t emb_len,
+                                   const uint32_t *ids, size_t n_ids,
+                                   size_t hidden, float *out, void *stream);
+/* rope (ops.rs:265-287) over positions pos0..pos0+seq_len (the reference
+ * always uses pos0 = 0). */
+ifx_status ifx_op_rope(float *x, size_t seq_len, size_t n_heads,
+                       size_t head_dim, size_t rope_dim, float base,
+                       size_t pos0, void *stream);
+/* argmax (forward.rs:615-622 / sampler.rs:75-82): last index on ties. */
+ifx_status ifx_op_argmax(const float *x, size_t n, uint32_t *out_dev,
+                         void *stream);
+/* Sampler::sample with the uniform draw u in [0,1) supplied per call, so a
+ * host oracle can reproduce the pick (sampler.rs:28-73, rand 0.8.6
+ * WeightedIndex). Synchronous; token written to *token_host. */
+ifx_status ifx_op_sample_u(const float *logits_dev, size_t n,
+                           const ifx_sampler *s, float u,
+                           uint32_t *token_host, void *stream);
+
+/* --------------------------- measurement hooks -------------------------- */
+/* No reference counterpart. Launch one of the decode step's fused kernels
+ * `reps` times in isolation (cycling through the layers so the weights come
+ * from HBM, not L2) and report the CUDA-event time per launch and the
+ * algorithmic bytes one launch moves. which: "qkv", "attn", "wo", "w13",
+ * "w2", "logits". Requires a cache that has been decoded into (for "attn"). */
+ifx_status ifx_bench_kernel(ifx_model *m, ifx_kv *kv, const char *which,
+                            int reps, float *ms_per_launch,
+                            uint64_t *bytes_per_launch);
+
+/* ------------------- synthetic workload generator ----------------------- */
+/* No reference counterpart: the reference's tests build GGUF fixtures in
+ * code (TestGgufBuilder, forward.rs:655-727); these build the benchmark
+ * models. Weights are N(0, sigma) from a counter-based generator (splitmix64
+ * + Box-Muller) keyed by (seed, tensor index, element index); quantisers
+ * emit bytes under the reference's dequant semantics (dequant.rs:62-199). */
+typedef struct ifx_synth_spec {
+  uint32_t vocab, dim, n_layers, n_heads, n_kv_heads, ffn, context;
+  float rope_base, norm_eps, sigma;
+  int mix;  /* 0: every matmul weight and token_embd/output Q8_0 (tiny);
+               1: Q4_K_M mix (Q6_K for attn_v, even-layer ffn_down and the
+                  output/tied embedding, Q4_K elsewhere);
+               2: all Q4_0 (for tests) */
+  int tied; /* 1: no output.weight (logits use token_embd, forward.rs:573) */
+  uint64_t seed;
+  int threads; /* host threads for generation (0 = all) */
+} ifx_synth_spec;
+ifx_status ifx_synth_gguf(const ifx_synth_spec *spec, void **bytes_out,
+                          size_t *len_out);
+void ifx_synth_free(void *bytes);
+/* Quantise n f32 values (n a multiple of the block size) into GGUF bytes. */
+ifx_status ifx_quantize(int type, const float *x, size_t n, void *out);
+/* The weight generator itself: out[i] = N(0, sigma) sample i of `stream`. */
+ifx_status ifx_synth_normal(uint64_t seed, uint64_t stream, float sigma,
+                            float *out, size_t n);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* INFEROX_H */

@@ -1,0 +1,11 @@
+"""inferox_b200 — sm_100a implementation of phraakture/inferox's token loop.
+
+The compute lives in libinferox_b200.so (CUDA kernels + C ABI, see
+include/inferox.h); this package is the host-side mirror of the reference's
+Rust API. Import fails loudly if the library is missing: there is no CPU
+fallback.
+"""
+from ._lib import IfxError, header_symbols, lib  # noqa: F401
+from .model import KvCache, Model, Sampler, load_opts  # noqa: F401
+
+__all__ = ["Model", "KvCache", "Sampler", "IfxError", "load_opts", "lib", "header_symbols"]

@@ -1,0 +1,281 @@
+// Decode: split-K flash-decoding over the f16 KV cache (replaces the decode
+// attention loop of Layer::decode_step, src/model/forward.rs:375-414).
+// Prefill: causal attention within the prompt chunk (forward.rs:246-305).
+#include <algorithm>
+
+#include "attention.cuh"
+
+namespace ifx {
+
+namespace {
+
+constexpr int kAttnThreads = 128;
+constexpr int kMaxGroup = 8;  // q heads per kv head handled per CTA
+
+__device__ __forceinline__ void rope_pair(float &a, float &b, int i, int rope_dim, float base,
+                                          int pos) {
+  float inv = 1.0f / powf(base, (float)i / (float)rope_dim);
+  float ang = __fmul_rn((float)pos, inv);
+  float s, c;
+  sincosf(ang, &s, &c);
+  float x0 = __fsub_rn(__fmul_rn(a, c), __fmul_rn(b, s));
+  float x1 = __fadd_rn(__fmul_rn(a, s), __fmul_rn(b, c));
+  a = x0;
+  b = x1;
+}
+
+__global__ void __launch_bounds__(kAttnThreads) decode_attn_kernel(const __grid_constant__ DecodeAttnArgs a) {
+  extern __shared__ float sm[];
+  const int h = blockIdx.x, s = blockIdx.y, tid = threadIdx.x;
+  const int grp = a.H / a.G, hd = a.hd, NS = a.ns;
+  const int cap = (a.max_seq + NS - 1) / NS + 1;
+  float *qs = sm;               // [grp][hd]
+  float *sc = sm + grp * hd;    // [grp][cap]
+  __shared__ int s_last;
+
+  pdl_wait();
+  pdl_launch();
+
+  if (a.zero_ptr) {
+    const int nb = a.G * NS, b = h * NS + s;
+    for (int i = b * kAttnThreads + tid; i < a.zero_n; i += nb * kAttnThreads) a.zero_ptr[i] = 0.f;
+  }
+
+  const int pos = *a.pos;
+  const int len = pos + 1;
+  const int chunk = (len + NS - 1) / NS;
+  const int t0 = s * chunk, t1 = min(len, t0 + chunk);
+  const float *q = a.qkv + (size_t)h * grp * hd;
+  const int rpos = a.rope_compat ? 0 : pos;
+  for (int e = tid; e < grp * hd / 2; e += kAttnThreads) {
+    const int j = e / (hd / 2), i = 2 * (e % (hd / 2));
+    float x0 = q[j * hd + i], x1 = q[j * hd + i + 1];
+    if (i < a.rope_dim) rope_pair(x0, x1, i, a.rope_dim, a.rope_base, rpos);
+    qs[j * hd + i] = x0;
+    qs[j * hd + i + 1] = x1;
+  }
+  __half *kc = a.kc + (size_t)h * a.max_seq * hd;
+  __half *vc = a.vc + (size_t)h * a.max_seq * hd;
+  if (t0 <= pos && pos < t1) {
+    // append this token's K/V (forward.rs:375-378), K rotated like q
+    const float *kn = a.qkv + (size_t)a.H * hd + (size_t)h * hd;
+    const float *vn = a.qkv + (size_t)(a.H + a.G) * hd + (size_t)h * hd;
+    for (int e = tid; e < hd / 2; e += kAttnThreads) {
+      const int i = 2 * e;
+      float x0 = kn[i], x1 = kn[i + 1];
+      if (i < a.rope_dim) rope_pair(x0, x1, i, a.rope_dim, a.rope_base, rpos);
+      kc[(size_t)pos * hd + i] = __float2half_rn(x0);
+      kc[(size_t)pos * hd + i + 1] = __float2half_rn(x1);
+      vc[(size_t)pos * hd + i] = __float2half_rn(vn[i]);
+      vc[(size_t)pos * hd + i + 1] = __float2half_rn(vn[i + 1]);
+    }
+  }
+  __syncthreads();
+
+  const int warp = tid >> 5, lane = tid & 31;
+  const float sq = sqrtf((float)hd);
+  for (int t = t0 + warp; t < t1; t += kAttnThreads / 32) {
+    const __half *kr = kc + (size_t)t * hd;
+    float part[kMaxGroup];
+#pragma unroll
+    for (int j = 0; j < kMaxGroup; ++j) part[j] = 0.f;
+    for (int d = lane; d < hd; d += 32) {
+      const float kv = __half2float(kr[d]);
+#pragma unroll
+      for (int j = 0; j < kMaxGroup; ++j)
+        if (j < grp) part[j] = fmaf(qs[j * hd + d], kv, part[j]);
+    }
+#pragma unroll
+    for (int j = 0; j < kMaxGroup; ++j)
+      if (j < grp) {
+        float v = warp_sum(part[j]);
+        if (lane == 0) sc[j * cap + (t - t0)] = v / sq;  // forward.rs:396
+      }
+  }
+  __syncthreads();
+  const int nk = max(0, t1 - t0);
+  // per-head softmax statistics over this chunk
+  __shared__ float s_m[kMaxGroup], s_l[kMaxGroup];
+  for (int j = warp; j < grp; j += kAttnThreads / 32) {
+    float m = -INFINITY;
+    for (int t = lane; t < nk; t += 32) m = fmaxf(m, sc[j * cap + t]);
+    m = warp_max(m);
+    float l = 0.f;
+    for (int t = lane; t < nk; t += 32) {
+      const float p = (nk > 0) ? expf(sc[j * cap + t] - m) : 0.f;
+      sc[j * cap + t] = p;
+      l += p;
+    }
+    l = warp_sum(l);
+    if (lane == 0) {
+      s_m[j] = m;
+      s_l[j] = l;
+    }
+  }
+  __syncthreads();
+  float *po = a.part_o + (size_t)(h * NS + s) * grp * hd;
+  for (int e = tid; e < grp * hd; e += kAttnThreads) {
+    const int j = e / hd, d = e % hd;
+    float o = 0.f;
+    for (int t = 0; t < nk; ++t) o = fmaf(sc[j * cap + t], __half2float(vc[(size_t)(t0 + t) * hd + d]), o);
+    po[e] = o;
+  }
+  if (tid < grp) a.part_ml[(h * NS + s) * grp + tid] = make_float2(s_m[tid], s_l[tid]);
+  __threadfence();
+  __syncthreads();
+  if (tid == 0) {
+    const int prev = atomicAdd(&a.counters[h], 1);
+    s_last = (prev == NS - 1);
+  }
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+  // combine the NS partial softmaxes of this kv head
+  for (int e = tid; e < grp * hd; e += kAttnThreads) {
+    const int j = e / hd;
+    float M = -INFINITY;
+    for (int t = 0; t < NS; ++t) M = fmaxf(M, __ldcg(&a.part_ml[(h * NS + t) * grp + j].x));
+    float L = 0.f, O = 0.f;
+    for (int t = 0; t < NS; ++t) {
+      const float2 ml = __ldcg(&a.part_ml[(h * NS + t) * grp + j]);
+      const float w = (ml.y > 0.f) ? expf(ml.x - M) : 0.f;
+      L = fmaf(ml.y, w, L);
+      O = fmaf(__ldcg(&a.part_o[((size_t)(h * NS + t) * grp) * hd + e]), w, O);
+    }
+    a.attn_out[(size_t)h * grp * hd + e] = O / L;
+  }
+  if (tid == 0) a.counters[h] = 0;
+}
+
+// ------------------------------------------------------------ prefill ----
+constexpr int kPQ = 32;  // query rows per CTA
+constexpr int kPK = 32;  // keys per tile
+
+__global__ void __launch_bounds__(128) prefill_attn_kernel(PrefillAttnArgs a) {
+  extern __shared__ float sm[];
+  const int hq = blockIdx.x, qb = blockIdx.y, tid = threadIdx.x;
+  const int hd = a.hd, grp = a.H / a.G, hk = hq / grp;
+  const int r0 = qb * kPQ;
+  const int nq = min(kPQ, a.n - r0);
+  float *Qs = sm;                    // [kPQ][hd]
+  float *Ks = Qs + kPQ * hd;         // [kPK][hd+1]
+  float *Vs = Ks + kPK * (hd + 1);   // [kPK][hd]
+  float *S = Vs + kPK * hd;          // [kPQ][kPK]
+  float *mrow = S + kPQ * kPK;       // [kPQ]
+  float *lrow = mrow + kPQ;          // [kPQ]
+  float *alpha = lrow + kPQ;         // [kPQ]
+  const int qstride = a.H * hd, kstride = a.G * hd;
+  for (int e = tid; e < kPQ * hd; e += 128) {
+    const int r = e / hd, d = e % hd;
+    Qs[e] = (r < nq) ? a.q[(size_t)(r0 + r) * qstride + hq * hd + d] : 0.f;
+  }
+  if (tid < kPQ) {
+    mrow[tid] = -INFINITY;
+    lrow[tid] = 0.f;
+  }
+  // each thread owns output elements e = tid + 128*i of [kPQ][hd]
+  constexpr int kMaxOut = kPQ * 128 / 128;
+  float acc[kMaxOut];
+  const int nout = kPQ * hd / 128;
+#pragma unroll
+  for (int i = 0; i < kMaxOut; ++i) acc[i] = 0.f;
+  const float sq = sqrtf((float)hd);
+  const int kend = r0 + nq;  // causal: keys 0..r0+nq-1
+  __syncthreads();
+  for (int k0 = 0; k0 < kend; k0 += kPK) {
+    const int nk = min(kPK, kend - k0);
+    for (int e = tid; e < kPK * hd; e += 128) {
+      const int t = e / hd, d = e % hd;
+      const bool ok = t < nk;
+      Ks[t * (hd + 1) + d] = ok ? a.k[(size_t)(k0 + t) * kstride + hk * hd + d] : 0.f;
+      Vs[t * hd + d] = ok ? a.v[(size_t)(k0 + t) * kstride + hk * hd + d] : 0.f;
+    }
+    __syncthreads();
+    for (int e = tid; e < kPQ * kPK; e += 128) {
+      const int r = e / kPK, t = e % kPK;
+      float sc = -INFINITY;
+      if (t < nk && r < nq && k0 + t <= r0 + r) {  // causal mask, forward.rs:266-271
+        float s = 0.f;
+        for (int d = 0; d < hd; ++d) s = fmaf(Qs[r * hd + d], Ks[t * (hd + 1) + d], s);
+        sc = s / sq;
+      }
+      S[e] = sc;
+    }
+    __syncthreads();
+    if (tid < kPQ) {
+      const int r = tid;
+      float m = mrow[r];
+      float mt = -INFINITY;
+      for (int t = 0; t < kPK; ++t) mt = fmaxf(mt, S[r * kPK + t]);
+      const float mn = fmaxf(m, mt);
+      const float al = (mn == -INFINITY) ? 1.f : expf(m - mn);
+      float l = lrow[r] * al;
+      for (int t = 0; t < kPK; ++t) {
+        const float p = (S[r * kPK + t] == -INFINITY) ? 0.f : expf(S[r * kPK + t] - mn);
+        S[r * kPK + t] = p;
+        l += p;
+      }
+      mrow[r] = mn;
+      lrow[r] = l;
+      alpha[r] = al;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int i = 0; i < kMaxOut; ++i) {
+      if (i < nout) {
+        const int e = tid + 128 * i, r = e / hd, d = e % hd;
+        float o = acc[i] * alpha[r];
+        for (int t = 0; t < nk; ++t) o = fmaf(S[r * kPK + t], Vs[t * hd + d], o);
+        acc[i] = o;
+      }
+    }
+    __syncthreads();
+  }
+#pragma unroll
+  for (int i = 0; i < kMaxOut; ++i) {
+    if (i < nout) {
+      const int e = tid + 128 * i, r = e / hd, d = e % hd;
+      if (r < nq) a.out[(size_t)(r0 + r) * qstride + hq * hd + d] = acc[i] / lrow[r];
+    }
+  }
+}
+
+}  // namespace
+
+int decode_attention_smem(int grp, int max_seq, int ns) {
+  const int cap = (max_seq + ns - 1) / ns + 1;
+  return (grp * 128 + grp * cap) * (int)sizeof(float) + 64;
+}
+
+ifx_status decode_attention(const DecodeAttnArgs &a, cudaStream_t st, bool pdl) {
+  const int grp = a.H / a.G;
+  if (grp > kMaxGroup || a.hd > 256 || a.hd % 2) return fail(IFX_ERR_UNSUPPORTED, "attention shape");
+  const int cap = (a.max_seq + a.ns - 1) / a.ns + 1;
+  const size_t smem = (size_t)(grp * a.hd + grp * cap) * sizeof(float);
+  static size_t attr = 0;
+  if (smem > 48 * 1024 && smem > attr) {
+    IFX_CUDA(cudaFuncSetAttribute(decode_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  (int)smem));
+    attr = smem;
+  }
+  IFX_CUDA(launch(decode_attn_kernel, dim3(a.G, a.ns), dim3(kAttnThreads), smem, st, pdl, a));
+  return IFX_OK;
+}
+
+ifx_status prefill_attention(const PrefillAttnArgs &a, cudaStream_t st) {
+  if (a.hd > 128 || (kPQ * a.hd) % 128) return fail(IFX_ERR_UNSUPPORTED, "prefill attention head_dim");
+  const size_t smem =
+      (size_t)(kPQ * a.hd + kPK * (a.hd + 1) + kPK * a.hd + kPQ * kPK + 3 * kPQ) * sizeof(float);
+  static bool attr = false;
+  if (!attr) {
+    IFX_CUDA(cudaFuncSetAttribute(prefill_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  100 * 1024));
+    attr = true;
+  }
+  dim3 grid(a.H, (a.n + kPQ - 1) / kPQ);
+  prefill_attn_kernel<<<grid, 128, smem, st>>>(a);
+  IFX_CUDA(cudaGetLastError());
+  return IFX_OK;
+}
+
+}  // namespace ifx

@@ -1,0 +1,38 @@
+// Attention kernels over the device-resident KV cache.
+#pragma once
+#include "common.cuh"
+
+namespace ifx {
+
+struct DecodeAttnArgs {
+  const float *qkv;       // [H*hd | G*hd | G*hd] f32 projections of the new token
+  __half *kc, *vc;        // this layer's caches [G][max_seq][hd]
+  const int *pos;         // device: cache length before this token (= its position)
+  float *part_o;          // [G][NS][grp][hd]
+  float2 *part_ml;        // [G][NS][grp] (running max, running sum)
+  int *counters;          // [G], zero between launches
+  float *attn_out;        // [H*hd]
+  float *zero_ptr;        // buffer zeroed by this kernel (may be null)
+  int zero_n;
+  int H, G, hd, max_seq, ns;
+  int rope_compat;        // 1: RoPE at position 0 (identity), forward.rs:371-372
+  int rope_dim;
+  float rope_base;
+  int *err;
+};
+
+ifx_status decode_attention(const DecodeAttnArgs &a, cudaStream_t st, bool pdl);
+int decode_attention_smem(int grp, int max_seq, int ns);
+
+// Causal attention inside one prefill chunk (forward.rs:255-305): q/k/v rows
+// of the chunk only, position t attends to 0..=t of the chunk.
+struct PrefillAttnArgs {
+  const float *q;   // [n][H*hd]
+  const float *k;   // [n][G*hd]
+  const float *v;   // [n][G*hd]
+  float *out;       // [n][H*hd]
+  int n, H, G, hd;
+};
+ifx_status prefill_attention(const PrefillAttnArgs &a, cudaStream_t st);
+
+}  // namespace ifx

@@ -1,0 +1,305 @@
+// Prefill fused dequant GEMM, first version: the weight units of
+// qlayout.cuh and the staged activations stream through a shared-memory ring
+// with 1-D bulk async copies (producer warp, mbarriers); each consumer warp
+// dequantises its 16-row A fragments once per 16-column chunk (scales folded
+// in, f16) and reuses them across the 8 token n-tiles of the CTA's 64-token
+// block with mma.m16n8k16 (f32 accumulation).
+#include <algorithm>
+
+#include "gemm.cuh"
+
+namespace ifx {
+
+namespace {
+
+constexpr int kGThreads = 288;
+constexpr int kGStages = 3;
+
+__device__ __forceinline__ float silu_g(float v) {
+  float c = fminf(fmaxf(v, -80.0f), 80.0f);
+  return v * (1.0f / (1.0f + expf(-c)));
+}
+
+// X staging: one CTA per token row computes the row's transform and writes
+// its values into the fragment layout [mblock][chunk][nt][lane][4 halves].
+__global__ void stage_x_kernel(const float *X, const float *X2, const float *normw, float eps,
+                               int mode, int64_t M, int64_t K, __half *out) {
+  const int64_t t = blockIdx.x;  // token (row), may be >= M for padding
+  const int tid = threadIdx.x;
+  __shared__ float red[32];
+  __shared__ float s_inv;
+  float inv = 1.0f;
+  if (mode == GX_RMSNORM && t < M) {
+    float ss = 0.f;
+    for (int64_t k = tid; k < K; k += blockDim.x) {
+      const float v = X[t * K + k];
+      ss += v * v;
+    }
+    ss = warp_sum(ss);
+    if ((tid & 31) == 0) red[tid >> 5] = ss;
+    __syncthreads();
+    if (tid < 32) {
+      float v = tid < (int)(blockDim.x / 32) ? red[tid] : 0.f;
+      v = warp_sum(v);
+      if (tid == 0) s_inv = 1.0f / sqrtf(v / (float)K + eps);
+    }
+    __syncthreads();
+    inv = s_inv;
+  }
+  const int64_t mb = t / kGemmTokens, tt = t % kGemmTokens;
+  const int nt = (int)(tt / 8), g = (int)(tt % 8);
+  const int64_t nch = K / 16;
+  for (int64_t k = tid; k < K; k += blockDim.x) {
+    float v = 0.f;
+    if (t < M) {
+      if (mode == GX_RMSNORM) v = (X[t * K + k] * inv) * normw[k];
+      else if (mode == GX_SWIGLU) v = silu_g(X[t * K + k]) * X2[t * K + k];
+      else v = X[t * K + k];
+    }
+    const int64_t ch = k / 16;
+    const int kk = (int)(k % 16);
+    // B fragment: b0 = (k 2c, 2c+1), b1 = (k 2c+8, 2c+9) of column g
+    const int c = (kk % 8) / 2, hi = kk / 8, e = kk % 2;
+    const int lane = g * 4 + c;
+    const int64_t idx = (((mb * nch + ch) * 8 + nt) * 32 + lane) * 4 + hi * 2 + e;
+    out[idx] = __float2half_rn(v);
+  }
+}
+
+__device__ __forceinline__ uint32_t h2u(__half2 h) { return *reinterpret_cast<uint32_t *>(&h); }
+__device__ __forceinline__ __half2 u2h(uint32_t u) { return *reinterpret_cast<__half2 *>(&u); }
+
+// (v - sub) * scale + add with v the magic-biased f16 pair in `bits`.
+__device__ __forceinline__ uint32_t deq(uint32_t bits, __half2 sub, __half2 scale, __half2 add) {
+  return h2u(__hfma2(__hsub2(u2h(bits), sub), scale, add));
+}
+
+struct GemmArgs {
+  const uint8_t *w;
+  const uint8_t *x;   // staged fragments
+  float *C;
+  int64_t ldc, M;
+  int type, rows, kc, kunits, unit_bytes, wt_bytes, wt_qbytes, nch_total;
+  int accumulate;
+  int *err;
+};
+
+template <int TYPE>
+__device__ __forceinline__ void gemm_unit(const uint8_t *wt, const uint8_t *xs, int kc,
+                                          int wt_qbytes, int lane, float (&acc)[8][4]) {
+  const int g = lane >> 2, c = lane & 3;
+  const int nch = kc / 16;
+  const __half2 magic1024 = __float2half2_rn(1024.f);
+#pragma unroll 1
+  for (int ch = 0; ch < nch; ++ch) {
+    uint32_t a[4];
+    if (TYPE == IFX_TYPE_Q4_K) {
+      const uint32_t wd = reinterpret_cast<const uint32_t *>(wt)[((ch / 4) * 32 + lane) * 4 + ch % 4];
+      const uint8_t *hdr = wt + 2048;
+      const int grp = ch / 2;
+      __half2 sg[2], mg[2];
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const uint8_t *hb = hdr + 16 * (g + 8 * h);
+        const float d = h2f(*reinterpret_cast<const uint16_t *>(hb));
+        const float dm = h2f(*reinterpret_cast<const uint16_t *>(hb + 2));
+        const uint8_t *s = hb + 4;
+        uint32_t sc, mn;
+        if (grp < 4) {
+          sc = s[grp] & 63;
+          mn = s[grp + 4] & 63;
+        } else {
+          sc = (s[grp + 4] & 15) | ((s[grp - 4] >> 6) << 4);
+          mn = (s[grp + 4] >> 4) | ((s[grp] >> 6) << 4);
+        }
+        sg[h] = __float2half2_rn(d * (float)sc * (h ? 0.0625f : 1.0f));
+        mg[h] = __float2half2_rn(-(dm * (float)mn));
+      }
+      const uint32_t hi = wd >> 8;
+      a[0] = deq((wd & 0x000F000Fu) | 0x64006400u, magic1024, sg[0], mg[0]);
+      a[1] = deq((wd & 0x00F000F0u) | 0x64006400u, magic1024, sg[1], mg[1]);
+      a[2] = deq((hi & 0x000F000Fu) | 0x64006400u, magic1024, sg[0], mg[0]);
+      a[3] = deq((hi & 0x00F000F0u) | 0x64006400u, magic1024, sg[1], mg[1]);
+    } else if (TYPE == IFX_TYPE_Q6_K) {
+      const uint32_t wd = reinterpret_cast<const uint32_t *>(wt)[((ch / 4) * 32 + lane) * 4 + ch % 4];
+      const int t = ch / 2;
+      uint32_t H = reinterpret_cast<const uint32_t *>(wt + 2048)[((t / 4) * 32 + lane) * 4 + t % 4];
+      if (ch & 1) H >>= 8;
+      const uint8_t *scb = wt + 3072;
+      __half2 sg[2];
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const int row = g + 8 * h;
+        const float d = h2f(*reinterpret_cast<const uint16_t *>(scb + 256 + 2 * row));
+        sg[h] = __float2half2_rn(d * (float)scb[16 * row + ch] * (h ? 0.0625f : 1.0f));
+      }
+      const __half2 z = __float2half2_rn(0.f);
+      const __half2 sub0 = __float2half2_rn(1056.f), sub1 = __float2half2_rn(1536.f);
+      const uint32_t hi = wd >> 8, H4 = H >> 4;
+      a[0] = deq((wd & 0x000F000Fu) | ((H & 0x00030003u) << 4) | 0x64006400u, sub0, sg[0], z);
+      a[1] = deq((wd & 0x00F000F0u) | ((H & 0x000C000Cu) << 6) | 0x64006400u, sub1, sg[1], z);
+      a[2] = deq((hi & 0x000F000Fu) | ((H4 & 0x00030003u) << 4) | 0x64006400u, sub0, sg[0], z);
+      a[3] = deq((hi & 0x00F000F0u) | ((H4 & 0x000C000Cu) << 6) | 0x64006400u, sub1, sg[1], z);
+    } else if (TYPE == IFX_TYPE_Q4_0) {
+      const uint32_t wd = reinterpret_cast<const uint32_t *>(wt)[((ch / 4) * 32 + lane) * 4 + ch % 4];
+      const int nb = kc / 32, blk = ch / 2;
+      __half2 sg[2];
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const int row = g + 8 * h;
+        const float d = h2f(*reinterpret_cast<const uint16_t *>(wt + wt_qbytes + (row * nb + blk) * 2));
+        sg[h] = __float2half2_rn(d * (h ? 0.0625f : 1.0f));
+      }
+      const __half2 z = __float2half2_rn(0.f);
+      const __half2 sub0 = __float2half2_rn(1032.f), sub1 = __float2half2_rn(1152.f);
+      const uint32_t hi = wd >> 8;
+      a[0] = deq((wd & 0x000F000Fu) | 0x64006400u, sub0, sg[0], z);
+      a[1] = deq((wd & 0x00F000F0u) | 0x64006400u, sub1, sg[1], z);
+      a[2] = deq((hi & 0x000F000Fu) | 0x64006400u, sub0, sg[0], z);
+      a[3] = deq((hi & 0x00F000F0u) | 0x64006400u, sub1, sg[1], z);
+    } else {  // Q8_0
+      const uint2 w2 = reinterpret_cast<const uint2 *>(wt)[((ch / 2) * 32 + lane) * 2 + ch % 2];
+      const int nb = kc / 32, blk = ch / 2;
+      __half2 sg[2];
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const int row = g + 8 * h;
+        sg[h] = __float2half2_rn(h2f(*reinterpret_cast<const uint16_t *>(wt + wt_qbytes + (row * nb + blk) * 2)));
+      }
+      const __half2 z = __float2half2_rn(0.f);
+      const __half2 sub = __float2half2_rn(1152.f);
+      a[0] = deq(prmt(w2.x, 0x64646464u, 0x4140u), sub, sg[0], z);
+      a[1] = deq(prmt(w2.x, 0x64646464u, 0x4342u), sub, sg[1], z);
+      a[2] = deq(prmt(w2.y, 0x64646464u, 0x4140u), sub, sg[0], z);
+      a[3] = deq(prmt(w2.y, 0x64646464u, 0x4342u), sub, sg[1], z);
+    }
+    const uint2 *xb = reinterpret_cast<const uint2 *>(xs) + (size_t)ch * 8 * 32 + lane;
+#pragma unroll
+    for (int nt = 0; nt < 8; ++nt) {
+      const uint2 b = xb[nt * 32];
+      mma_16816(acc[nt], a[0], a[1], a[2], a[3], b.x, b.y, acc[nt]);
+    }
+  }
+}
+
+__global__ void __launch_bounds__(kGThreads, 1) gemm_kernel(const __grid_constant__ GemmArgs a) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  uint64_t *full_bar = reinterpret_cast<uint64_t *>(smem);
+  uint64_t *empty_bar = full_bar + kGStages;
+  const int xbytes = a.kc * 128;  // kc/16 chunks x 2 KB
+  const int stage_bytes = a.unit_bytes + xbytes;
+  uint8_t *ring = smem + 128;
+  const int mb = blockIdx.x, ctile = blockIdx.y;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int n = a.kunits;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kGStages; ++s) {
+      mbar_init(&full_bar[s], 1);
+      mbar_init(&empty_bar[s], 8);
+    }
+    fence_mbar_init();
+  }
+  __syncthreads();
+
+  if (warp == 8) {
+    if (lane == 0) {
+      for (int i = 0; i < n; ++i) {
+        const int st = i % kGStages;
+        const uint32_t ph = (uint32_t)(i / kGStages) & 1u;
+        if (i >= kGStages && !mbar_wait(&empty_bar[st], ph ^ 1u, a.err, 201)) break;
+        uint8_t *dst = ring + (size_t)st * stage_bytes;
+        const uint8_t *wsrc = a.w + ((size_t)ctile * a.kunits + i) * a.unit_bytes;
+        const uint8_t *xsrc = a.x + ((size_t)mb * a.nch_total + (size_t)i * (a.kc / 16)) * 2048;
+        mbar_arrive_expect_tx(&full_bar[st], (uint32_t)stage_bytes);
+        bulk_g2s(dst, wsrc, (uint32_t)a.unit_bytes, &full_bar[st]);
+        bulk_g2s(dst + a.unit_bytes, xsrc, (uint32_t)xbytes, &full_bar[st]);
+      }
+    }
+    return;
+  }
+
+  float acc[8][4];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.f;
+  for (int i = 0; i < n; ++i) {
+    const int st = i % kGStages;
+    const uint32_t ph = (uint32_t)(i / kGStages) & 1u;
+    if (!mbar_wait(&full_bar[st], ph, a.err, 202)) return;
+    const uint8_t *base = ring + (size_t)st * stage_bytes;
+    const uint8_t *wt = base + (size_t)warp * a.wt_bytes;
+    const uint8_t *xs = base + a.unit_bytes;
+    switch (a.type) {
+      case IFX_TYPE_Q4_K: gemm_unit<IFX_TYPE_Q4_K>(wt, xs, a.kc, a.wt_qbytes, lane, acc); break;
+      case IFX_TYPE_Q6_K: gemm_unit<IFX_TYPE_Q6_K>(wt, xs, a.kc, a.wt_qbytes, lane, acc); break;
+      case IFX_TYPE_Q4_0: gemm_unit<IFX_TYPE_Q4_0>(wt, xs, a.kc, a.wt_qbytes, lane, acc); break;
+      default: gemm_unit<IFX_TYPE_Q8_0>(wt, xs, a.kc, a.wt_qbytes, lane, acc); break;
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty_bar[st]);
+  }
+  // D[nt] = rows (g, g+8) x tokens (8nt + 2c, 8nt + 2c + 1)
+  const int g = lane >> 2, c = lane & 3;
+  const int r0 = ctile * 128 + warp * 16 + g;
+#pragma unroll
+  for (int nt = 0; nt < 8; ++nt)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int row = r0 + ((j & 2) ? 8 : 0);
+      const int64_t tok = (int64_t)mb * kGemmTokens + nt * 8 + 2 * c + (j & 1);
+      if (row < a.rows && tok < a.M) {
+        float *p = a.C + tok * a.ldc + row;
+        *p = a.accumulate ? (*p + acc[nt][j]) : acc[nt][j];
+      }
+    }
+}
+
+}  // namespace
+
+size_t gemm_xfrag_bytes(int64_t M, int64_t K) {
+  const int64_t mblocks = (M + kGemmTokens - 1) / kGemmTokens;
+  return (size_t)mblocks * (size_t)(K / 16) * 2048;
+}
+
+ifx_status gemm_stage_x(const float *X, const float *X2, const float *normw, float eps, int mode,
+                        int64_t M, int64_t K, void *xfrag, cudaStream_t st) {
+  if (K % 16) return fail(IFX_ERR_SHAPE, "gemm: K must be a multiple of 16");
+  const int64_t mpad = (M + kGemmTokens - 1) / kGemmTokens * kGemmTokens;
+  stage_x_kernel<<<(unsigned)mpad, 256, 0, st>>>(X, X2, normw, eps, mode, M, K,
+                                                 reinterpret_cast<__half *>(xfrag));
+  IFX_CUDA(cudaGetLastError());
+  return IFX_OK;
+}
+
+ifx_status gemm_run(const QMatrix &W, const void *xfrag, int64_t M, float *C, int64_t ldc,
+                    int accumulate, int *err, cudaStream_t st) {
+  GemmArgs a{};
+  a.w = W.d;
+  a.x = reinterpret_cast<const uint8_t *>(xfrag);
+  a.C = C;
+  a.ldc = ldc;
+  a.M = M;
+  a.type = W.L.type;
+  a.rows = (int)W.L.rows;
+  a.kc = W.L.kc;
+  a.kunits = W.L.kunits;
+  a.unit_bytes = W.L.unit_bytes;
+  a.wt_bytes = W.L.wt_bytes;
+  a.wt_qbytes = W.L.wt_qbytes;
+  a.nch_total = (int)(W.L.cols / 16);
+  a.accumulate = accumulate;
+  a.err = err;
+  const size_t smem = 128 + (size_t)kGStages * (a.unit_bytes + a.kc * 128);
+  static bool attr = false;
+  if (!attr) {
+    IFX_CUDA(cudaFuncSetAttribute(gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  227 * 1024));
+    attr = true;
+  }
+  dim3 grid((unsigned)((M + kGemmTokens - 1) / kGemmTokens), (unsigned)W.L.ctiles);
+  gemm_kernel<<<grid, kGThreads, smem, st>>>(a);
+  IFX_CUDA(cudaGetLastError());
+  return IFX_OK;
+}
+
+}  // namespace ifx

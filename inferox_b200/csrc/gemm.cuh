@@ -1,0 +1,25 @@
+// Batched (prefill) fused dequant GEMM: C[M, N] = f(X)[M, K] . W[N, K]^T
+// (replaces tensor_f32_by_index + matmul_t at m = seq_len,
+// src/model/forward.rs:239-241, 308, 321-334, 528).
+#pragma once
+#include "repack.h"
+
+namespace ifx {
+
+constexpr int kGemmTokens = 64;  // tokens per CTA tile (8 MMA n-tiles)
+
+enum GemmXMode { GX_PLAIN = 0, GX_RMSNORM = 1, GX_SWIGLU = 2 };
+
+// Scratch sized for M tokens and K columns (f16 B fragments of f(X)).
+size_t gemm_xfrag_bytes(int64_t M, int64_t K);
+
+// Stage f(X) (row-major f32 [M, K]; for SWIGLU X is gate and X2 is up) as
+// f16 fragments in `xfrag`. RMSNORM normalises each row with `normw`.
+ifx_status gemm_stage_x(const float *X, const float *X2, const float *normw, float eps, int mode,
+                        int64_t M, int64_t K, void *xfrag, cudaStream_t st);
+
+// C[M, rows] (ldc) = or += (accumulate) staged X . W^T.
+ifx_status gemm_run(const QMatrix &W, const void *xfrag, int64_t M, float *C, int64_t ldc,
+                    int accumulate, int *err, cudaStream_t st);
+
+}  // namespace ifx

@@ -1,0 +1,657 @@
+// The token loop on the device: Model::open / prefill / decode_step /
+// generate (src/model/forward.rs:496-612, src/model/mod.rs:64-92) behind the
+// C ABI of include/inferox.h.
+//
+// Decode step (batch 1), one CUDA graph per KV cache, every kernel launched
+// with programmatic dependent launch so each GEMV's weight stream starts
+// while its predecessor drains:
+//   embed   : dequant one row of token_embd (bit-exact) -> x; zero logits/qkv
+//   per layer l:
+//     QKV   : qkv  += [Wq;Wk;Wv] . rms_norm(x) * attn_norm          (GEMV)
+//     ATT   : append k,v (f16) at pos; split-K flash-decoding -> attn; zero gu
+//     WO    : x    += Wo . attn            (residual add fused, GEMV)
+//     W13   : gu   += [W1;W3] . rms_norm(x) * ffn_norm; zero qkv     (GEMV)
+//     W2    : x    += W2 . (silu(gate) * up)  (SwiGLU fused into staging)
+//   LOGITS  : logits += Wout . rms_norm(x) * output_norm            (GEMV)
+//   ARGMAX  : last-index argmax -> next token (feeds the next embed); pos++
+#include <algorithm>
+#include <cstdio>
+#include <cstring>
+#include <memory>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "attention.cuh"
+#include "gemm.cuh"
+#include "gemv.cuh"
+#include "gguf.h"
+#include "model.h"
+#include "ops.cuh"
+#include "quant.cuh"
+
+namespace ifx {
+
+namespace {
+
+__global__ void embed_kernel(const uint8_t *emb, int type, int D, const uint32_t *token,
+                             float *x, float *zero_a, int na, float *zero_b, int nb) {
+  pdl_wait();
+  pdl_launch();
+  const uint64_t base = (uint64_t)(*token) * (uint64_t)D;
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < D; i += gridDim.x * blockDim.x)
+    x[i] = dequant_elem(type, emb, base + i);
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < na; i += gridDim.x * blockDim.x)
+    zero_a[i] = 0.f;
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < nb; i += gridDim.x * blockDim.x)
+    zero_b[i] = 0.f;
+}
+
+__global__ void embed_rows_kernel(const uint8_t *emb, int type, int D, const uint32_t *ids,
+                                  float *x) {
+  const uint64_t base = (uint64_t)ids[blockIdx.x] * (uint64_t)D;
+  for (int i = threadIdx.x; i < D; i += blockDim.x)
+    x[(size_t)blockIdx.x * D + i] = dequant_elem(type, emb, base + i);
+}
+
+// Argmax over logits (last index on ties, forward.rs:615-622); the last CTA
+// publishes the token, optionally records it and advances the position.
+__global__ void argmax_step_kernel(const float *logits, int n, unsigned long long *key,
+                                   int *count, uint32_t *next_token, uint32_t *tokens,
+                                   int *n_out, int *pos, int record, int inc_pos) {
+  pdl_wait();
+  pdl_launch();
+  unsigned long long best = 0;
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
+    const float v = logits[i];
+    if (v != v) continue;
+    const unsigned long long k = ((unsigned long long)ordered_bits(v) << 32) | (unsigned)i;
+    best = k > best ? k : best;
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const unsigned long long other = __shfl_xor_sync(0xffffffffu, best, o);
+    best = other > best ? other : best;
+  }
+  if ((threadIdx.x & 31) == 0 && best) atomicMax(key, best);
+  __threadfence();
+  __syncthreads();
+  __shared__ int last;
+  if (threadIdx.x == 0) last = (atomicAdd(count, 1) == (int)gridDim.x - 1);
+  __syncthreads();
+  if (!last || threadIdx.x != 0) return;
+  __threadfence();
+  const unsigned long long k = atomicAdd(key, 0ull);
+  const uint32_t tok = (uint32_t)(k & 0xffffffffull);
+  *next_token = tok;
+  if (record) {
+    tokens[*n_out] = tok;
+    *n_out = *n_out + 1;
+  }
+  if (inc_pos) *pos = *pos + 1;
+  *key = 0;
+  *count = 0;
+}
+
+// K/V rows of a prefill chunk into the f16 cache at positions start + t
+// (forward.rs:246-253). k/v: [n][G*hd] f32; cache: [G][max_seq][hd].
+__global__ void kv_write_kernel(const float *k, const float *v, __half *kc, __half *vc, int n,
+                                int G, int hd, int max_seq, int start) {
+  const int t = blockIdx.x;
+  for (int e = threadIdx.x; e < G * hd; e += blockDim.x) {
+    const int g = e / hd, d = e % hd;
+    const size_t dst = ((size_t)g * max_seq + start + t) * hd + d;
+    kc[dst] = __float2half_rn(k[(size_t)t * G * hd + e]);
+    vc[dst] = __float2half_rn(v[(size_t)t * G * hd + e]);
+  }
+}
+
+__global__ void add_int_kernel(int *p, int v) { *p += v; }
+
+__global__ void kv_read_kernel(const __half *c, float *out, int len, int G, int hd, int max_seq) {
+  const int t = blockIdx.x;
+  for (int e = threadIdx.x; e < G * hd; e += blockDim.x) {
+    const int g = e / hd, d = e % hd;
+    out[(size_t)t * G * hd + e] = __half2float(c[((size_t)g * max_seq + t) * hd + d]);
+  }
+}
+
+template <typename T>
+ifx_status dalloc(T **p, size_t n) {
+  IFX_CUDA(cudaMalloc(reinterpret_cast<void **>(p), std::max<size_t>(n, 1) * sizeof(T)));
+  IFX_CUDA(cudaMemset(*p, 0, std::max<size_t>(n, 1) * sizeof(T)));
+  return IFX_OK;
+}
+
+}  // namespace
+
+// ------------------------------------------------------------------ load --
+static ifx_status upload_matrix(const GgufFile &f, const uint8_t *bytes, size_t len, int idx,
+                                uint64_t rows, uint64_t cols, uint8_t *staging, cudaStream_t st,
+                                QMatrix *out) {
+  uint64_t start, size;
+  IFX_TRY(gguf_tensor_range(f, len, idx, &start, &size));
+  const GgufTensor &t = f.tensors[idx];
+  if (t.n_elements() != rows * cols)
+    return fail(IFX_ERR_SHAPE, "tensor " + t.name + ": element count does not match the config");
+  if (!make_layout((int)t.type, (int64_t)rows, (int64_t)cols, &out->L))
+    return fail(IFX_ERR_UNSUPPORTED,
+                "tensor " + t.name + ": weight type " + std::to_string(t.type) +
+                    " is not supported by the fused kernels (Q4_0, Q8_0, Q4_K, Q6_K)");
+  IFX_CUDA(cudaMemcpyAsync(staging, bytes + start, size, cudaMemcpyHostToDevice, st));
+  IFX_CUDA(cudaMalloc(&out->d, out->L.total_bytes));
+  IFX_TRY(repack_to_device(out->L, staging, out->d, st));
+  IFX_CUDA(cudaStreamSynchronize(st));
+  return IFX_OK;
+}
+
+static ifx_status upload_norm(const GgufFile &f, const uint8_t *bytes, size_t len, int idx,
+                              uint64_t n, uint8_t *staging, cudaStream_t st, float **out) {
+  uint64_t start, size;
+  IFX_TRY(gguf_tensor_range(f, len, idx, &start, &size));
+  const GgufTensor &t = f.tensors[idx];
+  if (t.n_elements() != n) return fail(IFX_ERR_SHAPE, "tensor " + t.name + ": length mismatch");
+  IFX_TRY(dalloc(out, n));
+  IFX_CUDA(cudaMemcpyAsync(staging, bytes + start, size, cudaMemcpyHostToDevice, st));
+  IFX_TRY(op_dequantize((int)t.type, staging, size, *out, n, st));  // weights.rs:66-74 exactly
+  IFX_CUDA(cudaStreamSynchronize(st));
+  return IFX_OK;
+}
+
+ifx_status Model::load(const uint8_t *bytes, size_t len, const ifx_load_opts &o) {
+  opts = o;
+  if (opts.tp_size != 1 || opts.tp_rank != 0)
+    return fail(IFX_ERR_UNSUPPORTED, "tensor parallel loading is not built in this version");
+  GgufFile f;
+  IFX_TRY(gguf_parse(bytes, len, &f));  // host-only checks first: no GPU needed to reject a file
+  IFX_TRY(gguf_config(f, &cfg));
+  if (cfg.vocab_size == 0) return fail(IFX_ERR_SHAPE, "llama.vocab_size is missing or zero");
+  const uint64_t D = cfg.hidden_size, H = cfg.n_heads, G = cfg.n_kv_heads, hd = cfg.head_dim;
+  const uint64_t F = cfg.intermediate_size, V = cfg.vocab_size;
+  if (H * hd != D || H % G || hd % 2 || cfg.rope_dim > hd || cfg.rope_dim % 2)
+    return fail(IFX_ERR_SHAPE, "unsupported head geometry");
+  static const char *suffix[9] = {"attn_norm", "attn_q", "attn_k", "attn_v", "attn_output",
+                                  "ffn_norm", "ffn_gate", "ffn_up", "ffn_down"};
+  std::vector<std::array<int, 9>> idx(cfg.n_layers);
+  for (uint64_t l = 0; l < cfg.n_layers; ++l)
+    for (int s = 0; s < 9; ++s) {
+      const std::string nm = "blk." + std::to_string(l) + "." + suffix[s] + ".weight";
+      idx[l][s] = f.tensor_index(nm);
+      if (idx[l][s] < 0)  // model/mod.rs:72-74
+        return fail(IFX_ERR_TENSOR_NOT_FOUND, "tensor not found: blk." + std::to_string(l) + ".*");
+    }
+  const int i_emb = f.tensor_index("token_embd.weight");
+  if (i_emb < 0) return fail(IFX_ERR_TENSOR_NOT_FOUND, "tensor not found: token_embd.weight");
+  const int i_onorm = f.tensor_index("output_norm.weight");
+  if (i_onorm < 0) return fail(IFX_ERR_TENSOR_NOT_FOUND, "tensor not found: output_norm.weight");
+  const int i_out = f.tensor_index("output.weight");  // optional, forward.rs:573
+  device = opts.device;
+  IFX_CUDA(cudaSetDevice(device));
+  IFX_CUDA(cudaStreamCreateWithFlags(&stream, cudaStreamNonBlocking));
+
+  // staging buffer: the largest tensor
+  uint64_t max_bytes = 0;
+  for (size_t i = 0; i < f.tensors.size(); ++i) {
+    int64_t b = gguf_type_bytes(f.tensors[i].type, f.tensors[i].n_elements());
+    if (b > 0) max_bytes = std::max<uint64_t>(max_bytes, (uint64_t)b);
+  }
+  uint8_t *staging = nullptr;
+  IFX_CUDA(cudaMalloc(&staging, max_bytes + 256));
+  ifx_status st = IFX_OK;
+  auto guard = [&](ifx_status s) {
+    if (s != IFX_OK && st == IFX_OK) st = s;
+    return s == IFX_OK;
+  };
+  layers.resize(cfg.n_layers);
+  for (uint64_t l = 0; l < cfg.n_layers && st == IFX_OK; ++l) {
+    Layer &L = layers[l];
+    guard(upload_norm(f, bytes, len, idx[l][0], D, staging, stream, &L.attn_norm)) &&
+        guard(upload_matrix(f, bytes, len, idx[l][1], D, D, staging, stream, &L.wq)) &&
+        guard(upload_matrix(f, bytes, len, idx[l][2], G * hd, D, staging, stream, &L.wk)) &&
+        guard(upload_matrix(f, bytes, len, idx[l][3], G * hd, D, staging, stream, &L.wv)) &&
+        guard(upload_matrix(f, bytes, len, idx[l][4], D, D, staging, stream, &L.wo)) &&
+        guard(upload_norm(f, bytes, len, idx[l][5], D, staging, stream, &L.ffn_norm)) &&
+        guard(upload_matrix(f, bytes, len, idx[l][6], F, D, staging, stream, &L.w1)) &&
+        guard(upload_matrix(f, bytes, len, idx[l][7], F, D, staging, stream, &L.w3)) &&
+        guard(upload_matrix(f, bytes, len, idx[l][8], D, F, staging, stream, &L.w2));
+  }
+  if (st == IFX_OK) guard(upload_norm(f, bytes, len, i_onorm, D, staging, stream, &out_norm));
+  if (st == IFX_OK)
+    guard(upload_matrix(f, bytes, len, i_out >= 0 ? i_out : i_emb, V, D, staging, stream, &out_w));
+  if (st == IFX_OK) {
+    uint64_t s0, sz;
+    if (guard(gguf_tensor_range(f, len, i_emb, &s0, &sz))) {
+      const GgufTensor &t = f.tensors[i_emb];
+      emb_type = (int)t.type;
+      if (t.n_elements() != V * D) guard(fail(IFX_ERR_SHAPE, "token_embd.weight: element count"));
+      else if (!block_info(emb_type).elems)
+        guard(fail(IFX_ERR_UNSUPPORTED, "token_embd.weight: type not supported"));
+      else if (cudaMalloc(&emb_raw, sz) != cudaSuccess ||
+               cudaMemcpy(emb_raw, bytes + s0, sz, cudaMemcpyHostToDevice) != cudaSuccess)
+        guard(fail(IFX_ERR_CUDA, "token_embd upload"));
+      emb_row_bytes = (V ? sz / V : 0);
+    }
+  }
+  cudaFree(staging);
+  if (st != IFX_OK) return st;
+
+  // decode buffers
+  qkv_n = (int)((H + 2 * G) * hd);
+  IFX_TRY(dalloc(&x, D));
+  IFX_TRY(dalloc(&qkv, qkv_n));
+  IFX_TRY(dalloc(&attn, D));
+  IFX_TRY(dalloc(&gu, 2 * F));
+  IFX_TRY(dalloc(&logits, V));
+  IFX_TRY(dalloc(&err, 1));
+  IFX_TRY(dalloc(&next_token, 1));
+  IFX_TRY(dalloc(&amax_key, 1));
+  IFX_TRY(dalloc(&amax_count, 1));
+  IFX_TRY(dalloc(&n_out, 1));
+  ns = (int)std::max<uint64_t>(1, std::min<uint64_t>(32, kNumSMs / G));
+  IFX_TRY(dalloc(&part_o, H * ns * hd));
+  IFX_TRY(dalloc(&part_ml, H * ns));
+  IFX_TRY(dalloc(&counters, G));
+
+  // one GEMV plan (pointers + byte-balanced schedule) per call site
+  const float eps = cfg.norm_eps;
+  p_qkv.resize(cfg.n_layers);
+  p_wo.resize(cfg.n_layers);
+  p_w13.resize(cfg.n_layers);
+  p_w2.resize(cfg.n_layers);
+  for (uint64_t l = 0; l < cfg.n_layers; ++l) {
+    Layer &L = layers[l];
+    const QMatrix *mq[3] = {&L.wq, &L.wk, &L.wv};
+    float *yq[3] = {qkv, qkv + H * hd, qkv + (H + G) * hd};
+    const QMatrix *mo[1] = {&L.wo};
+    float *yo[1] = {x};
+    const QMatrix *m13[2] = {&L.w1, &L.w3};
+    float *y13[2] = {gu, gu + F};
+    const QMatrix *m2[1] = {&L.w2};
+    float *y2[1] = {x};
+    IFX_TRY(gemv_plan(mq, yq, 3, GEMV_RMSNORM, x, nullptr, L.attn_norm, eps, err, &p_qkv[l]));
+    IFX_TRY(gemv_plan(mo, yo, 1, GEMV_PLAIN, attn, nullptr, nullptr, eps, err, &p_wo[l]));
+    IFX_TRY(gemv_plan(m13, y13, 2, GEMV_RMSNORM, x, nullptr, L.ffn_norm, eps, err, &p_w13[l]));
+    IFX_TRY(gemv_plan(m2, y2, 1, GEMV_SWIGLU, gu, gu + F, nullptr, eps, err, &p_w2[l]));
+    p_w13[l].args.zero_ptr = qkv;  // qkv was consumed by ATT; the next QKV refills it
+    p_w13[l].args.zero_n = qkv_n;
+  }
+  const QMatrix *mout[1] = {&out_w};
+  float *yout[1] = {logits};
+  IFX_TRY(gemv_plan(mout, yout, 1, GEMV_RMSNORM, x, nullptr, out_norm, eps, err, &p_logits));
+
+  decode_bytes = 0;
+  for (auto &L : layers)
+    decode_bytes += L.wq.gguf_bytes() + L.wk.gguf_bytes() + L.wv.gguf_bytes() + L.wo.gguf_bytes() +
+                    L.w1.gguf_bytes() + L.w3.gguf_bytes() + L.w2.gguf_bytes() + 2 * D * 4;
+  decode_bytes += out_w.gguf_bytes() + D * 4 + emb_row_bytes;
+  IFX_CUDA(cudaStreamSynchronize(stream));
+  return IFX_OK;
+}
+
+Model::~Model() {
+  if (device >= 0) cudaSetDevice(device);
+  auto F = [](void *p) {
+    if (p) cudaFree(p);
+  };
+  for (auto &L : layers) {
+    F(L.attn_norm);
+    F(L.ffn_norm);
+    for (QMatrix *q : {&L.wq, &L.wk, &L.wv, &L.wo, &L.w1, &L.w3, &L.w2}) F(q->d);
+  }
+  F(out_w.d);
+  F(out_norm);
+  F(emb_raw);
+  for (auto *v : std::vector<void *>{x, qkv, attn, gu, logits, err, next_token, amax_key, amax_count,
+                                     n_out, part_o, part_ml, counters, ws, logits_all, ids_dev})
+    F(v);
+  for (size_t l = 0; l < p_qkv.size(); ++l) {
+    gemv_plan_free(&p_qkv[l]);
+    gemv_plan_free(&p_wo[l]);
+    gemv_plan_free(&p_w13[l]);
+    gemv_plan_free(&p_w2[l]);
+  }
+  gemv_plan_free(&p_logits);
+  if (stream) cudaStreamDestroy(stream);
+}
+
+// --------------------------------------------------------------- KV cache --
+ifx_status KvCache::create(Model *model, size_t max_seq_len) {
+  m = model;
+  max_seq = max_seq_len;
+  const ifx_config &c = m->cfg;
+  per_layer = (size_t)c.n_kv_heads * max_seq * c.head_dim;
+  IFX_CUDA(cudaSetDevice(m->device));
+  IFX_TRY(dalloc(&k, per_layer * c.n_layers));
+  IFX_TRY(dalloc(&v, per_layer * c.n_layers));
+  IFX_TRY(dalloc(&pos, 1));
+  IFX_TRY(dalloc(&tokens, max_seq + 1));
+  return IFX_OK;
+}
+
+KvCache::~KvCache() {
+  if (m) cudaSetDevice(m->device);
+  if (graph) cudaGraphExecDestroy(graph);
+  for (void *p : {(void *)k, (void *)v, (void *)pos, (void *)tokens})
+    if (p) cudaFree(p);
+}
+
+ifx_status KvCache::clear() {
+  len = 0;
+  IFX_CUDA(cudaMemsetAsync(pos, 0, sizeof(int), m->stream));
+  IFX_CUDA(cudaStreamSynchronize(m->stream));
+  return IFX_OK;
+}
+
+// ---------------------------------------------------------- decode step ---
+ifx_status Model::enqueue_decode(KvCache &kv, cudaStream_t st) {
+  const ifx_config &c = cfg;
+  const bool pdl = true;
+  const int D = (int)c.hidden_size, H = (int)c.n_heads, G = (int)c.n_kv_heads, hd = (int)c.head_dim;
+  IFX_CUDA(launch(embed_kernel, dim3(8), dim3(256), 0, st, pdl, (const uint8_t *)emb_raw, emb_type,
+                  D, (const uint32_t *)next_token, x, logits, (int)c.vocab_size, qkv, qkv_n));
+  for (uint64_t l = 0; l < c.n_layers; ++l) {
+    IFX_TRY(gemv_launch(p_qkv[l], st, pdl));
+    DecodeAttnArgs a{};
+    a.qkv = qkv;
+    a.kc = kv.k + l * kv.per_layer;
+    a.vc = kv.v + l * kv.per_layer;
+    a.pos = kv.pos;
+    a.part_o = part_o;
+    a.part_ml = part_ml;
+    a.counters = counters;
+    a.attn_out = attn;
+    a.zero_ptr = gu;
+    a.zero_n = (int)(2 * c.intermediate_size);
+    a.H = H;
+    a.G = G;
+    a.hd = hd;
+    a.max_seq = (int)kv.max_seq;
+    a.ns = ns;
+    a.rope_compat = opts.rope_compat;
+    a.rope_dim = (int)c.rope_dim;
+    a.rope_base = c.rope_base;
+    a.err = err;
+    IFX_TRY(decode_attention(a, st, pdl));
+    IFX_TRY(gemv_launch(p_wo[l], st, pdl));
+    IFX_TRY(gemv_launch(p_w13[l], st, pdl));
+    IFX_TRY(gemv_launch(p_w2[l], st, pdl));
+  }
+  IFX_TRY(gemv_launch(p_logits, st, pdl));
+  IFX_CUDA(launch(argmax_step_kernel, dim3(kNumSMs), dim3(256), 0, st, pdl, (const float *)logits,
+                  (int)c.vocab_size, amax_key, amax_count, next_token, kv.tokens, n_out, kv.pos, 1, 1));
+  (void)D;
+  return IFX_OK;
+}
+
+ifx_status Model::run_decode(KvCache &kv) {
+  if (!opts.use_graphs) return enqueue_decode(kv, stream);
+  if (!kv.graph) {
+    cudaGraph_t g;
+    IFX_CUDA(cudaStreamBeginCapture(stream, cudaStreamCaptureModeThreadLocal));
+    ifx_status s = enqueue_decode(kv, stream);
+    cudaError_t e = cudaStreamEndCapture(stream, &g);
+    if (s != IFX_OK) return s;
+    if (e != cudaSuccess) return cuda_fail(e, "cudaStreamEndCapture");
+    IFX_CUDA(cudaGraphInstantiate(&kv.graph, g, 0));
+    cudaGraphDestroy(g);
+  }
+  IFX_CUDA(cudaGraphLaunch(kv.graph, stream));
+  return IFX_OK;
+}
+
+ifx_status Model::check_err() {
+  int h = 0;
+  IFX_CUDA(cudaMemcpy(&h, err, sizeof(int), cudaMemcpyDeviceToHost));
+  if (h) {
+    cudaMemset(err, 0, sizeof(int));
+    return fail(IFX_ERR_TIMEOUT, "a bounded device wait gave up (code " + std::to_string(h) + ")");
+  }
+  return IFX_OK;
+}
+
+ifx_status Model::decode_step(KvCache &kv, uint32_t token, float *logits_host) {
+  if (token >= cfg.vocab_size)
+    return fail(IFX_ERR_INVALID_TENSOR_INDEX, "tensor index out of bounds: " + std::to_string(token));
+  if (kv.len >= kv.max_seq) return fail(IFX_ERR_INVALID_TENSOR_INDEX, "KV cache is full");
+  IFX_CUDA(cudaSetDevice(device));
+  IFX_CUDA(cudaMemcpyAsync(next_token, &token, sizeof(uint32_t), cudaMemcpyHostToDevice, stream));
+  IFX_CUDA(cudaMemsetAsync(n_out, 0, sizeof(int), stream));
+  IFX_TRY(run_decode(kv));
+  if (logits_host)
+    IFX_CUDA(cudaMemcpyAsync(logits_host, logits, cfg.vocab_size * sizeof(float),
+                             cudaMemcpyDeviceToHost, stream));
+  IFX_CUDA(cudaStreamSynchronize(stream));
+  kv.len += 1;
+  return check_err();
+}
+
+// --------------------------------------------------------------- prefill --
+ifx_status Model::ensure_ws(size_t n) {
+  if (n <= ws_tokens) return IFX_OK;
+  if (ws) cudaFree(ws);
+  if (ids_dev) cudaFree(ids_dev);
+  ws = nullptr;
+  ids_dev = nullptr;
+  const ifx_config &c = cfg;
+  const size_t D = c.hidden_size, Hh = c.n_heads * c.head_dim, kvd = c.n_kv_heads * c.head_dim;
+  const size_t F = c.intermediate_size;
+  const size_t xf = gemm_xfrag_bytes((int64_t)n, (int64_t)std::max(D, F));
+  const size_t floats = n * (D + Hh + 2 * kvd + Hh + 2 * F);
+  IFX_CUDA(cudaMalloc(&ws, floats * sizeof(float) + xf + 1024));
+  IFX_CUDA(cudaMalloc(&ids_dev, n * sizeof(uint32_t)));
+  float *p = reinterpret_cast<float *>(ws);
+  w_x = p; p += n * D;
+  w_q = p; p += n * Hh;
+  w_k = p; p += n * kvd;
+  w_v = p; p += n * kvd;
+  w_attn = p; p += n * Hh;
+  w_gate = p; p += n * F;
+  w_up = p; p += n * F;
+  w_xf = reinterpret_cast<uint8_t *>(reinterpret_cast<uintptr_t>(p + 64) & ~(uintptr_t)255);
+  ws_tokens = n;
+  return IFX_OK;
+}
+
+ifx_status Model::prefill(KvCache &kv, const uint32_t *ids, size_t n, float *logits_host,
+                          int last_row_only) {
+  const ifx_config &c = cfg;
+  for (size_t i = 0; i < n; ++i)
+    if (ids[i] >= c.vocab_size)  // forward.rs:501-503
+      return fail(IFX_ERR_INVALID_TENSOR_INDEX, "tensor index out of bounds: 0");
+  if (n == 0) return IFX_OK;
+  if (kv.len + n > kv.max_seq) return fail(IFX_ERR_INVALID_TENSOR_INDEX, "prompt exceeds the KV cache");
+  IFX_CUDA(cudaSetDevice(device));
+  IFX_TRY(ensure_ws(n));
+  cudaStream_t st = stream;
+  const int64_t N = (int64_t)n;
+  const int D = (int)c.hidden_size, H = (int)c.n_heads, G = (int)c.n_kv_heads, hd = (int)c.head_dim;
+  const int F = (int)c.intermediate_size;
+  const int Hh = H * hd, kvd = G * hd;
+  const int start = (int)kv.len;
+  IFX_CUDA(cudaMemcpyAsync(ids_dev, ids, n * sizeof(uint32_t), cudaMemcpyHostToDevice, st));
+  embed_rows_kernel<<<(unsigned)n, 256, 0, st>>>(emb_raw, emb_type, D, ids_dev, w_x);
+  IFX_CUDA(cudaGetLastError());
+  const int pos0 = opts.rope_compat ? 0 : start;  // forward.rs:243-244 ignores cache_start
+  for (uint64_t l = 0; l < c.n_layers; ++l) {
+    Layer &L = layers[l];
+    IFX_TRY(gemm_stage_x(w_x, nullptr, L.attn_norm, c.norm_eps, GX_RMSNORM, N, D, w_xf, st));
+    IFX_TRY(gemm_run(L.wq, w_xf, N, w_q, Hh, 0, err, st));
+    IFX_TRY(gemm_run(L.wk, w_xf, N, w_k, kvd, 0, err, st));
+    IFX_TRY(gemm_run(L.wv, w_xf, N, w_v, kvd, 0, err, st));
+    IFX_TRY(op_rope(w_q, n, H, hd, c.rope_dim, c.rope_base, pos0, st));
+    IFX_TRY(op_rope(w_k, n, G, hd, c.rope_dim, c.rope_base, pos0, st));
+    kv_write_kernel<<<(unsigned)n, 256, 0, st>>>(w_k, w_v, kv.k + l * kv.per_layer,
+                                                 kv.v + l * kv.per_layer, (int)n, G, hd,
+                                                 (int)kv.max_seq, start);
+    IFX_CUDA(cudaGetLastError());
+    PrefillAttnArgs pa{w_q, w_k, w_v, w_attn, (int)n, H, G, hd};
+    IFX_TRY(prefill_attention(pa, st));
+    IFX_TRY(gemm_stage_x(w_attn, nullptr, nullptr, 0.f, GX_PLAIN, N, Hh, w_xf, st));
+    IFX_TRY(gemm_run(L.wo, w_xf, N, w_x, D, 1, err, st));
+    IFX_TRY(gemm_stage_x(w_x, nullptr, L.ffn_norm, c.norm_eps, GX_RMSNORM, N, D, w_xf, st));
+    IFX_TRY(gemm_run(L.w1, w_xf, N, w_gate, F, 0, err, st));
+    IFX_TRY(gemm_run(L.w3, w_xf, N, w_up, F, 0, err, st));
+    IFX_TRY(gemm_stage_x(w_gate, w_up, nullptr, 0.f, GX_SWIGLU, N, F, w_xf, st));
+    IFX_TRY(gemm_run(L.w2, w_xf, N, w_x, D, 1, err, st));
+  }
+  add_int_kernel<<<1, 1, 0, st>>>(kv.pos, (int)n);  // forward.rs:520
+  IFX_CUDA(cudaGetLastError());
+  if (last_row_only || !logits_host) {
+    // logits of the last row into the decode logits buffer (GEMV)
+    IFX_CUDA(cudaMemsetAsync(logits, 0, c.vocab_size * sizeof(float), st));
+    GemvPlan p = p_logits;
+    const QMatrix *mo[1] = {&out_w};
+    float *yo[1] = {logits};
+    gemv_plan_rebind(&p, mo, yo, w_x + (size_t)(n - 1) * D, nullptr, out_norm);
+    IFX_TRY(gemv_launch(p, st, false));
+    if (logits_host)
+      IFX_CUDA(cudaMemcpyAsync(logits_host, logits, c.vocab_size * sizeof(float),
+                               cudaMemcpyDeviceToHost, st));
+  } else {
+    const size_t need = n * c.vocab_size;
+    if (need > logits_all_n) {
+      if (logits_all) cudaFree(logits_all);
+      logits_all = nullptr;
+      IFX_CUDA(cudaMalloc(&logits_all, need * sizeof(float)));
+      logits_all_n = need;
+    }
+    IFX_TRY(gemm_stage_x(w_x, nullptr, out_norm, c.norm_eps, GX_RMSNORM, N, D, w_xf, st));
+    IFX_TRY(gemm_run(out_w, w_xf, N, logits_all, c.vocab_size, 0, err, st));
+    IFX_CUDA(cudaMemcpyAsync(logits_host, logits_all, need * sizeof(float), cudaMemcpyDeviceToHost, st));
+    // keep the last row as "the model's last logits" for ifx_sample
+    IFX_CUDA(cudaMemcpyAsync(logits, logits_all + (n - 1) * c.vocab_size,
+                             c.vocab_size * sizeof(float), cudaMemcpyDeviceToDevice, st));
+  }
+  IFX_CUDA(cudaStreamSynchronize(st));
+  kv.len += n;
+  return check_err();
+}
+
+ifx_status Model::generate(KvCache &kv, const uint32_t *prompt, size_t n_prompt,
+                           size_t max_tokens, uint32_t *out) {
+  if (n_prompt == 0) return fail(IFX_ERR_SHAPE, "generate: empty prompt");
+  IFX_TRY(kv.clear());  // forward.rs:600
+  if (n_prompt + max_tokens > kv.max_seq)
+    return fail(IFX_ERR_INVALID_TENSOR_INDEX, "prompt + max_tokens exceeds the KV cache");
+  IFX_TRY(prefill(kv, prompt, n_prompt, nullptr, 1));
+  cudaStream_t st = stream;
+  IFX_CUDA(cudaMemsetAsync(n_out, 0, sizeof(int), st));
+  IFX_CUDA(launch(argmax_step_kernel, dim3(kNumSMs), dim3(256), 0, st, false, (const float *)logits,
+                  (int)cfg.vocab_size, amax_key, amax_count, next_token, kv.tokens, n_out, kv.pos, 1, 0));
+  for (size_t i = 0; i < max_tokens; ++i) IFX_TRY(run_decode(kv));
+  if (max_tokens)
+    IFX_CUDA(cudaMemcpyAsync(out, kv.tokens, max_tokens * sizeof(uint32_t), cudaMemcpyDeviceToHost, st));
+  IFX_CUDA(cudaStreamSynchronize(st));
+  kv.len += max_tokens;
+  return check_err();
+}
+
+ifx_status Model::decode_greedy(KvCache &kv, uint32_t token, size_t n, uint32_t *out,
+                                float *device_ms) {
+  if (token >= cfg.vocab_size)
+    return fail(IFX_ERR_INVALID_TENSOR_INDEX, "tensor index out of bounds: " + std::to_string(token));
+  if (kv.len + n > kv.max_seq) return fail(IFX_ERR_INVALID_TENSOR_INDEX, "KV cache is full");
+  IFX_CUDA(cudaSetDevice(device));
+  cudaStream_t st = stream;
+  IFX_CUDA(cudaMemcpyAsync(next_token, &token, sizeof(uint32_t), cudaMemcpyHostToDevice, st));
+  IFX_CUDA(cudaMemsetAsync(n_out, 0, sizeof(int), st));
+  cudaEvent_t e0 = nullptr, e1 = nullptr;
+  if (device_ms) {
+    IFX_CUDA(cudaEventCreate(&e0));
+    IFX_CUDA(cudaEventCreate(&e1));
+    IFX_CUDA(cudaEventRecord(e0, st));
+  }
+  for (size_t i = 0; i < n; ++i) IFX_TRY(run_decode(kv));
+  if (device_ms) IFX_CUDA(cudaEventRecord(e1, st));
+  if (out && n)
+    IFX_CUDA(cudaMemcpyAsync(out, kv.tokens, n * sizeof(uint32_t), cudaMemcpyDeviceToHost, st));
+  IFX_CUDA(cudaStreamSynchronize(st));
+  if (device_ms) {
+    IFX_CUDA(cudaEventElapsedTime(device_ms, e0, e1));
+    cudaEventDestroy(e0);
+    cudaEventDestroy(e1);
+  }
+  kv.len += n;
+  return check_err();
+}
+
+ifx_status Model::bench_kernel(KvCache &kv, const std::string &which, int reps, float *ms,
+                               uint64_t *bytes) {
+  if (reps < 1) return fail(IFX_ERR_INVALID_ARGUMENT, "bench_kernel: reps < 1");
+  IFX_CUDA(cudaSetDevice(device));
+  cudaStream_t st = stream;
+  const int L = (int)cfg.n_layers;
+  std::vector<GemvPlan> *plans = nullptr;
+  if (which == "qkv") plans = &p_qkv;
+  else if (which == "wo") plans = &p_wo;
+  else if (which == "w13") plans = &p_w13;
+  else if (which == "w2") plans = &p_w2;
+  else if (which != "logits" && which != "attn")
+    return fail(IFX_ERR_INVALID_ARGUMENT, "bench_kernel: unknown kernel " + which);
+  cudaEvent_t e0, e1;
+  IFX_CUDA(cudaEventCreate(&e0));
+  IFX_CUDA(cudaEventCreate(&e1));
+  uint64_t b = 0;
+  // one untimed pass so first-launch costs stay out of the timing
+  for (int pass = 0; pass < 2; ++pass) {
+    if (pass == 1) IFX_CUDA(cudaEventRecord(e0, st));
+    b = 0;
+    for (int r = 0; r < reps; ++r) {
+      const int l = r % L;
+      if (plans) {
+        IFX_TRY(gemv_launch((*plans)[l], st, false));
+        b += (*plans)[l].weight_bytes;
+      } else if (which == "logits") {
+        IFX_TRY(gemv_launch(p_logits, st, false));
+        b += p_logits.weight_bytes;
+      } else {
+        DecodeAttnArgs a{};
+        a.qkv = qkv;
+        a.kc = kv.k + l * kv.per_layer;
+        a.vc = kv.v + l * kv.per_layer;
+        a.pos = kv.pos;
+        a.part_o = part_o;
+        a.part_ml = part_ml;
+        a.counters = counters;
+        a.attn_out = attn;
+        a.H = (int)cfg.n_heads;
+        a.G = (int)cfg.n_kv_heads;
+        a.hd = (int)cfg.head_dim;
+        a.max_seq = (int)kv.max_seq;
+        a.ns = ns;
+        a.rope_compat = opts.rope_compat;
+        a.rope_dim = (int)cfg.rope_dim;
+        a.rope_base = cfg.rope_base;
+        a.err = err;
+        IFX_TRY(decode_attention(a, st, false));
+        b += 2ull * cfg.n_kv_heads * (kv.len + 1) * cfg.head_dim * sizeof(__half);
+      }
+    }
+  }
+  IFX_CUDA(cudaEventRecord(e1, st));
+  IFX_CUDA(cudaEventSynchronize(e1));
+  float t = 0.f;
+  IFX_CUDA(cudaEventElapsedTime(&t, e0, e1));
+  cudaEventDestroy(e0);
+  cudaEventDestroy(e1);
+  *ms = t / reps;
+  *bytes = b / (uint64_t)reps;
+  return check_err();
+}
+
+ifx_status Model::kv_read(const KvCache &kv, size_t layer, int which_v, float *out_host) {
+  if (layer >= cfg.n_layers) return fail(IFX_ERR_INVALID_TENSOR_INDEX, "layer out of range");
+  const int G = (int)cfg.n_kv_heads, hd = (int)cfg.head_dim;
+  if (kv.len == 0) return IFX_OK;
+  float *tmp = nullptr;
+  IFX_CUDA(cudaMalloc(&tmp, kv.len * G * hd * sizeof(float)));
+  const __half *src = (which_v ? kv.v : kv.k) + layer * kv.per_layer;
+  kv_read_kernel<<<(unsigned)kv.len, 256, 0, stream>>>(src, tmp, (int)kv.len, G, hd, (int)kv.max_seq);
+  cudaMemcpyAsync(out_host, tmp, kv.len * G * hd * sizeof(float), cudaMemcpyDeviceToHost, stream);
+  cudaStreamSynchronize(stream);
+  cudaFree(tmp);
+  IFX_CUDA(cudaGetLastError());
+  return IFX_OK;
+}
+
+}  // namespace ifx

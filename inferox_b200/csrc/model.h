@@ -1,0 +1,82 @@
+// Model / KV cache objects behind ifx_model and ifx_kv.
+#pragma once
+#include <array>
+#include <string>
+#include <vector>
+
+#include "common.cuh"
+#include "gemv.cuh"
+#include "repack.h"
+
+namespace ifx {
+
+struct Layer {  // Layer (src/model/mod.rs:18-31), weights resident on the device
+  float *attn_norm = nullptr, *ffn_norm = nullptr;
+  QMatrix wq, wk, wv, wo, w1, w3, w2;
+};
+
+struct Model;
+
+struct KvCache {  // KvCache (src/model/cache.rs:7-14), f16 on the device
+  Model *m = nullptr;
+  size_t max_seq = 0, len = 0, per_layer = 0;
+  __half *k = nullptr, *v = nullptr;  // [layer][kv_head][max_seq][head_dim]
+  int *pos = nullptr;                 // device copy of len (read by the kernels)
+  uint32_t *tokens = nullptr;         // generated tokens (device)
+  cudaGraphExec_t graph = nullptr;    // captured decode step for this cache
+  ifx_status create(Model *model, size_t max_seq_len);
+  ifx_status clear();
+  ~KvCache();
+};
+
+struct Model {
+  int device = -1;
+  ifx_load_opts opts{};
+  ifx_config cfg{};
+  cudaStream_t stream = nullptr;
+  std::vector<Layer> layers;
+  QMatrix out_w;
+  float *out_norm = nullptr;
+  uint8_t *emb_raw = nullptr;  // token_embd GGUF bytes (exact row dequant)
+  int emb_type = 0;
+  uint64_t emb_row_bytes = 0;
+  // decode state
+  float *x = nullptr, *qkv = nullptr, *attn = nullptr, *gu = nullptr, *logits = nullptr;
+  int qkv_n = 0;
+  float *part_o = nullptr;
+  float2 *part_ml = nullptr;
+  int *counters = nullptr, ns = 1;
+  int *err = nullptr;
+  uint32_t *next_token = nullptr;
+  unsigned long long *amax_key = nullptr;
+  int *amax_count = nullptr, *n_out = nullptr;
+  std::vector<GemvPlan> p_qkv, p_wo, p_w13, p_w2;
+  GemvPlan p_logits;
+  uint64_t decode_bytes = 0;
+  // prefill workspace
+  void *ws = nullptr;
+  size_t ws_tokens = 0;
+  float *w_x = nullptr, *w_q = nullptr, *w_k = nullptr, *w_v = nullptr, *w_attn = nullptr;
+  float *w_gate = nullptr, *w_up = nullptr;
+  uint8_t *w_xf = nullptr;
+  uint32_t *ids_dev = nullptr;
+  float *logits_all = nullptr;
+  size_t logits_all_n = 0;
+
+  ifx_status load(const uint8_t *bytes, size_t len, const ifx_load_opts &o);
+  ifx_status enqueue_decode(KvCache &kv, cudaStream_t st);
+  ifx_status run_decode(KvCache &kv);
+  ifx_status decode_step(KvCache &kv, uint32_t token, float *logits_host);
+  ifx_status prefill(KvCache &kv, const uint32_t *ids, size_t n, float *logits_host, int last_row_only);
+  ifx_status generate(KvCache &kv, const uint32_t *prompt, size_t n_prompt, size_t max_tokens,
+                      uint32_t *out);
+  ifx_status kv_read(const KvCache &kv, size_t layer, int which_v, float *out_host);
+  ifx_status decode_greedy(KvCache &kv, uint32_t token, size_t n, uint32_t *out, float *device_ms);
+  ifx_status bench_kernel(KvCache &kv, const std::string &which, int reps, float *ms,
+                          uint64_t *bytes);
+  ifx_status ensure_ws(size_t n);
+  ifx_status check_err();
+  ~Model();
+};
+
+}  // namespace ifx

@@ -1,0 +1,181 @@
+"""Host-side mirror of the reference's model API (src/model/mod.rs,
+src/model/forward.rs, src/model/cache.rs, src/sampler.rs) over the C ABI.
+
+    model = Model.open("model.gguf")              # Model::open
+    kv = model.kv_cache(max_seq)                   # KvCache::new
+    logits = model.prefill(ids, kv)                # Model::prefill
+    logits = model.decode_step(token, kv)          # Model::decode_step
+    tokens = model.generate(prompt, n, kv)         # Model::generate (greedy)
+    tok = Sampler(0.8, 40, 0.95).sample(model)     # Sampler::sample on device
+
+Errors raise IfxError whose `.name` is the gguf::Error variant
+(src/gguf/error.rs:6-42) or one of the GPU build's additions.
+"""
+from __future__ import annotations
+
+import ctypes as C
+from dataclasses import dataclass
+
+import numpy as np
+
+from ._lib import Config, IfxError, LoadOpts, SamplerC, check, lib
+
+
+def _u32(a):
+    return a.ctypes.data_as(C.POINTER(C.c_uint32))
+
+
+def _f32(a):
+    return a.ctypes.data_as(C.POINTER(C.c_float))
+
+
+def load_opts(device: int = 0, rope_compat: bool = True, use_graphs: bool = True,
+              tp_size: int = 1, tp_rank: int = 0, nccl_comm: int | None = None) -> LoadOpts:
+    o = LoadOpts()
+    lib.ifx_load_opts_default(C.byref(o))
+    o.device = device
+    o.rope_compat = 1 if rope_compat else 0
+    o.use_graphs = 1 if use_graphs else 0
+    o.tp_size = tp_size
+    o.tp_rank = tp_rank
+    o.nccl_comm = nccl_comm
+    return o
+
+
+class Model:
+    """A model resident on one GPU (weights uploaded and repacked once)."""
+
+    def __init__(self, handle: C.c_void_p):
+        self._h = handle
+        c = Config()
+        check(lib.ifx_model_config(self._h, C.byref(c)), "model_config")
+        self.config = c
+
+    @classmethod
+    def open(cls, path: str, **opts) -> "Model":
+        h = C.c_void_p()
+        o = load_opts(**opts)
+        check(lib.ifx_model_load(path.encode(), C.byref(o), C.byref(h)), "Model::open")
+        return cls(h)
+
+    @classmethod
+    def from_bytes(cls, data, **opts) -> "Model":
+        buf = np.frombuffer(data, dtype=np.uint8) if not isinstance(data, np.ndarray) else data
+        h = C.c_void_p()
+        o = load_opts(**opts)
+        check(lib.ifx_model_load_mem(buf.ctypes.data_as(C.c_void_p), buf.nbytes, C.byref(o),
+                                     C.byref(h)), "Model::open")
+        return cls(h)
+
+    def close(self):
+        if getattr(self, "_h", None) is not None and self._h.value:
+            lib.ifx_model_free(self._h)
+            self._h = None
+
+    def __del__(self):
+        self.close()
+
+    @property
+    def vocab(self) -> int:
+        return int(self.config.vocab_size)
+
+    def decode_weight_bytes(self) -> int:
+        return int(lib.ifx_model_decode_weight_bytes(self._h))
+
+    def kv_cache(self, max_seq: int | None = None) -> "KvCache":
+        return KvCache(self, max_seq or int(self.config.context_length))
+
+    def prefill(self, ids, kv: "KvCache", last_row_only: bool = False) -> np.ndarray:
+        ids = np.ascontiguousarray(ids, np.uint32)
+        rows = 1 if last_row_only else ids.size
+        out = np.empty(rows * self.vocab, np.float32)
+        check(lib.ifx_prefill(self._h, kv._h, _u32(ids), ids.size, _f32(out),
+                              1 if last_row_only else 0), "prefill")
+        return out.reshape(rows, self.vocab)
+
+    def decode_step(self, token: int, kv: "KvCache", want_logits: bool = True):
+        out = np.empty(self.vocab, np.float32) if want_logits else None
+        check(lib.ifx_decode_step(self._h, kv._h, int(token),
+                                  _f32(out) if want_logits else None), "decode_step")
+        return out
+
+    def decode_greedy(self, token: int, n_steps: int, kv: "KvCache", timed: bool = False):
+        """n_steps greedy steps fed on the device; returns (tokens, device_ms)."""
+        out = np.empty(max(n_steps, 1), np.uint32)
+        ms = C.c_float(0.0)
+        check(lib.ifx_decode_greedy(self._h, kv._h, int(token), n_steps, _u32(out),
+                                    C.byref(ms) if timed else None), "decode_greedy")
+        return out[:n_steps], (float(ms.value) if timed else None)
+
+    def bench_kernel(self, kv: "KvCache", which: str, reps: int):
+        """(ms per launch, algorithmic bytes per launch) of one fused kernel."""
+        ms = C.c_float(0.0)
+        b = C.c_uint64(0)
+        check(lib.ifx_bench_kernel(self._h, kv._h, which.encode(), reps, C.byref(ms), C.byref(b)),
+              "bench_kernel")
+        return float(ms.value), int(b.value)
+
+    def generate(self, prompt, max_tokens: int, kv: "KvCache") -> np.ndarray:
+        p = np.ascontiguousarray(prompt, np.uint32)
+        out = np.empty(max(max_tokens, 1), np.uint32)
+        check(lib.ifx_generate(self._h, kv._h, _u32(p), p.size, max_tokens, _u32(out)),
+              "generate")
+        return out[:max_tokens]
+
+
+class KvCache:
+    """Device-resident KV cache (f16, [layer][kv_head][max_seq][head_dim])."""
+
+    def __init__(self, model: Model, max_seq: int):
+        self._model = model
+        h = C.c_void_p()
+        check(lib.ifx_kv_create(model._h, max_seq, C.byref(h)), "KvCache::new")
+        self._h = h
+        self.max_seq = max_seq
+        self.kv_dim = int(model.config.n_kv_heads * model.config.head_dim)
+
+    def close(self):
+        if getattr(self, "_h", None) is not None and self._h.value:
+            lib.ifx_kv_free(self._h)
+            self._h = None
+
+    def __del__(self):
+        self.close()
+
+    def clear(self):
+        check(lib.ifx_kv_clear(self._h), "KvCache::clear")
+
+    def __len__(self) -> int:
+        return int(lib.ifx_kv_len(self._h))
+
+    def read(self, layer: int, which_v: bool) -> np.ndarray:
+        n = len(self)
+        out = np.empty(max(n * self.kv_dim, 1), np.float32)
+        check(lib.ifx_kv_read(self._h, layer, 1 if which_v else 0, _f32(out)), "kv_read")
+        return out[: n * self.kv_dim].reshape(n, self.kv_dim)
+
+
+@dataclass
+class Sampler:
+    """Sampler (src/sampler.rs:8-16); sampling runs on the device."""
+
+    temperature: float = 0.0
+    top_k: int = 0
+    top_p: float = 1.0
+
+    @classmethod
+    def greedy(cls) -> "Sampler":
+        return cls(0.0, 0, 1.0)
+
+    def _c(self) -> SamplerC:
+        return SamplerC(self.temperature, self.top_k, self.top_p)
+
+    def sample(self, model: Model, seed: int = 0, offset: int = 0) -> int:
+        """Sample from the model's latest logits (prefill or decode_step)."""
+        out = C.c_uint32()
+        s = self._c()
+        check(lib.ifx_sample(model._h, C.byref(s), seed, offset, C.byref(out)), "Sampler::sample")
+        return int(out.value)
+
+
+__all__ = ["Model", "KvCache", "Sampler", "IfxError", "load_opts"]

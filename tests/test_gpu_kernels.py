@@ -1,0 +1,221 @@
+"""GPU parity of the op-level kernels against the CPU oracle (oracle/refcpu.c).
+
+Integer / byte work (dequantisation, argmax, the AVX2-order matmul_t) must be
+bit-exact. The fused dequant GEMV/GEMM run on tensor cores with f16
+operands and f32 accumulation; their tolerance is derived from f16 rounding:
+|y - y_ref| <= TOL * ||w_row * x||_2, TOL stated per test.
+"""
+import numpy as np
+import pytest
+import torch
+
+from inferox_b200 import IfxError, ops, synth
+from oracle import refcpu as R
+
+pytestmark = pytest.mark.gpu
+
+DEV = "cuda:0"
+
+
+def cuda(a, dtype=None):
+    t = torch.from_numpy(np.ascontiguousarray(a))
+    if dtype is not None:
+        t = t.to(dtype)
+    return t.to(DEV)
+
+
+def random_blocks(ttype: int, nblocks: int, seed: int) -> bytes:
+    """Random block bytes with sane f16 scales (any bit pattern elsewhere)."""
+    rng = np.random.default_rng(seed)
+    bb = {2: 18, 7: 34, 12: 144, 14: 210, 15: 292}[ttype]
+    b = rng.integers(0, 256, size=(nblocks, bb), dtype=np.uint8)
+    scales = rng.uniform(-0.05, 0.05, size=(nblocks, 2)).astype(np.float16).view(np.uint8)
+    b[:, 0:2] = scales[:, 0:2]
+    if ttype in (12, 15):  # d and dmin
+        b[:, 2:4] = scales[:, 2:4]
+    return b.tobytes()
+
+
+@pytest.mark.parametrize("ttype,elems", [(2, 32), (7, 32), (12, 256), (14, 256), (15, 256)])
+def test_dequant_bit_exact(ttype, elems):
+    nb = 517
+    data = random_blocks(ttype, nb, seed=ttype)
+    ref = R.dequantize(ttype, data, nb * elems)
+    got = ops.dequantize(ttype, cuda(np.frombuffer(data, np.uint8)), nb * elems).cpu().numpy()
+    assert np.array_equal(ref.view(np.uint32), got.view(np.uint32))
+
+
+def test_dequant_f16_f32_exact():
+    h = np.arange(0, 65536, 7, dtype=np.uint16)
+    ref = R.dequantize(1, h.tobytes(), h.size)
+    got = ops.dequantize(1, cuda(h.view(np.uint8)), h.size).cpu().numpy()
+    assert np.array_equal(ref.view(np.uint32), got.view(np.uint32))
+    f = np.random.default_rng(1).standard_normal(1000).astype(np.float32)
+    got = ops.dequantize(0, cuda(f.view(np.uint8)), f.size).cpu().numpy()
+    assert np.array_equal(got, f)
+
+
+def test_dequant_reference_kats_on_gpu():  # dequant.rs:247-337 on the device
+    b = np.float16(0.5).tobytes() + bytes(((j << 4) | j) for j in range(16))
+    got = ops.dequantize(2, cuda(np.frombuffer(b, np.uint8)), 32).cpu().numpy()
+    assert np.allclose(got, [((j % 16) - 8) * 0.5 for j in range(32)])
+    blk = bytearray(np.float16(1.0).tobytes() + np.float16(0.0).tobytes())
+    blk += bytes([1, 1, 1, 1, 0, 0, 0, 0, 1, 1, 1, 1])
+    for _ in range(8):
+        for pair in range(16):
+            blk.append((((2 * pair + 1) % 32) << 4 & 0xFF) | (2 * pair))
+    got = ops.dequantize(12, cuda(np.frombuffer(bytes(blk), np.uint8)), 256).cpu().numpy()
+    assert np.allclose(got, [float((j % 32) % 16) for j in range(256)])
+
+
+def test_dequant_size_errors():
+    with pytest.raises(IfxError) as e:
+        ops.dequantize(7, cuda(np.zeros(33, np.uint8)), 32)
+    assert e.value.name == "UnexpectedEof"
+    with pytest.raises(IfxError) as e:
+        ops.dequantize(5, cuda(np.zeros(22, np.uint8)), 32)
+    assert e.value.name == "UnknownTensorType"
+
+
+def _qmatrix(ttype, rows, cols, seed):
+    w = synth.normal(seed, 0, 0.02, rows * cols)
+    q = synth.quantize(ttype, w)
+    wd = R.dequantize(ttype, q, rows * cols).reshape(rows, cols).astype(np.float64)
+    return ops.QMatrix(ttype, q, rows, cols), wd
+
+
+@pytest.mark.parametrize("ttype,rows,cols", [
+    (12, 4096, 4096), (14, 1024, 4096), (12, 300, 512), (14, 128256 // 64, 2048),
+    (2, 512, 1024), (7, 768, 288), (7, 288, 768), (7, 1000, 96), (12, 256, 14336),
+])
+def test_gemv_matches_oracle(ttype, rows, cols):
+    W, wd = _qmatrix(ttype, rows, cols, seed=rows + cols + ttype)
+    x = np.random.default_rng(rows).standard_normal(cols).astype(np.float32)
+    y = ops.matmul_t_q(cuda(x), W, 1).cpu().numpy().astype(np.float64)
+    ref = wd @ x.astype(np.float64)
+    scale = np.sqrt((wd * x[None, :]) ** 2 @ np.ones(cols)) + 1e-6
+    err = np.abs(y - ref) / scale
+    assert err.max() < 3e-3, (err.max(), np.argmax(err))
+
+
+@pytest.mark.parametrize("ttype,rows,cols,m", [
+    (12, 512, 1024, 5), (14, 384, 2048, 64), (12, 1024, 4096, 100), (2, 256, 512, 70),
+    (7, 288, 288, 16), (7, 768, 288, 130), (14, 256, 256, 1 + 64 * 3),
+])
+def test_gemm_matches_oracle(ttype, rows, cols, m):
+    W, wd = _qmatrix(ttype, rows, cols, seed=rows * 3 + m)
+    x = np.random.default_rng(m).standard_normal((m, cols)).astype(np.float32)
+    y = ops.matmul_t_q(cuda(x), W, m).cpu().numpy().reshape(m, rows).astype(np.float64)
+    ref = x.astype(np.float64) @ wd.T
+    scale = np.sqrt((x.astype(np.float64) ** 2) @ (wd.T ** 2)) + 1e-6
+    err = np.abs(y - ref) / scale
+    assert err.max() < 6e-3, err.max()
+
+
+def test_matmul_t_bit_exact():  # AVX2 lane order of ops.rs:106-149
+    rng = np.random.default_rng(0)
+    for m, n, k in [(1, 7, 288), (3, 5, 13), (2, 2, 2), (4, 9, 768)]:
+        a = rng.standard_normal(m * k).astype(np.float32)
+        b = rng.standard_normal(n * k).astype(np.float32)
+        ref = R.matmul_t(a, b, m, n, k)
+        got = ops.matmul_t(cuda(a), cuda(b), m, n, k).cpu().numpy()
+        assert np.array_equal(ref.view(np.uint32), got.view(np.uint32))
+
+
+def test_matmul_bit_exact():  # ops.rs:75-102
+    rng = np.random.default_rng(1)
+    for m, n, k in [(2, 4, 3), (1, 2, 3), (3, 17, 9)]:
+        a = rng.standard_normal(m * k).astype(np.float32)
+        b = rng.standard_normal(k * n).astype(np.float32)
+        ref = R.matmul(a, b, m, n, k)
+        got = ops.matmul(cuda(a), cuda(b), m, n, k).cpu().numpy()
+        assert np.array_equal(ref.view(np.uint32), got.view(np.uint32))
+
+
+def test_ops_reference_kats():  # ops.rs:293-416 on the device
+    c = ops.matmul(cuda(np.array([1, 2, 3, 4, 5, 6], np.float32)),
+                   cuda(np.array([1, 0, 1, 0, 0, 1, 0, 1, 1, 1, 0, 0], np.float32)), 2, 4, 3)
+    assert list(c.cpu().numpy()) == [4, 5, 1, 2, 10, 11, 4, 5]
+    x = cuda(np.array([1, 2, 3, 4], np.float32))
+    ops.rms_norm(x, cuda(np.ones(4, np.float32)), 1e-5)
+    s = np.float32(1) / np.sqrt(np.float32(7.5) + np.float32(1e-5), dtype=np.float32)
+    assert np.allclose(x.cpu().numpy(), np.array([1, 2, 3, 4], np.float32) * s, rtol=1e-6)
+    out = cuda(np.array([1, 2, 3], np.float32))
+    ops.add_in_place(out, cuda(np.array([0.5, 1.0, 1.5], np.float32)))
+    assert list(out.cpu().numpy()) == [1.5, 3.0, 4.5]
+    sm = cuda(np.array([1, 2, 3, 0, 0, 0], np.float32))
+    ops.softmax_rows(sm, 2, 3)
+    v = sm.cpu().numpy()
+    assert abs(v[:3].sum() - 1) < 1e-5 and abs(v[3:].sum() - 1) < 1e-5 and v[2] > v[1] > v[0]
+    with pytest.raises(IfxError) as e:
+        ops.rms_norm(cuda(np.ones(3, np.float32)), cuda(np.ones(4, np.float32)), 1e-5)
+    assert e.value.name == "Shape"
+
+
+def test_elementwise_ops_match_oracle():
+    rng = np.random.default_rng(2)
+    x = (rng.standard_normal(5000) * 4).astype(np.float32)
+    x[:4] = [100.0, -100.0, 0.0, -0.0]
+    g = (rng.standard_normal(5000) * 3).astype(np.float32)
+    u = rng.standard_normal(5000).astype(np.float32)
+    assert np.allclose(ops.silu(cuda(x)).cpu().numpy(), R.silu(x), rtol=2e-6, atol=1e-7)
+    assert np.allclose(ops.swiglu(cuda(g), cuda(u)).cpu().numpy(), R.swiglu(g, u), rtol=2e-6, atol=1e-7)
+    rows, hid = 7, 4096
+    xr = rng.standard_normal(rows * hid).astype(np.float32)
+    w = rng.uniform(0.5, 1.5, hid).astype(np.float32)
+    got = ops.rms_norm_rows(cuda(xr), cuda(w), 1e-5, rows).cpu().numpy()
+    assert np.allclose(got, R.rms_norm_rows(xr, w, 1e-5, rows), rtol=1e-5, atol=1e-6)
+    s = (rng.standard_normal(3 * 1000) * 5).astype(np.float32)
+    assert np.allclose(ops.softmax_rows(cuda(s), 3, 1000).cpu().numpy(), R.softmax_rows(s, 3, 1000),
+                       rtol=1e-5, atol=1e-9)
+
+
+@pytest.mark.parametrize("seq,heads,hd,rdim,base", [(1, 6, 48, 48, 1e4), (16, 32, 128, 128, 5e5),
+                                                    (37, 8, 64, 32, 1e4)])
+def test_rope_matches_oracle(seq, heads, hd, rdim, base):
+    x = np.random.default_rng(seq).standard_normal(seq * heads * hd).astype(np.float32)
+    got = ops.rope(cuda(x), seq, heads, hd, rdim, base).cpu().numpy()
+    ref = R.rope(x, seq, heads, hd, rdim, base)
+    assert np.allclose(got, ref, rtol=2e-5, atol=2e-5)
+    if seq == 1:
+        assert np.array_equal(got, x)  # position 0 is the identity (forward.rs:371-372)
+
+
+def test_embedding_lookup_and_oob():
+    emb = np.random.default_rng(3).standard_normal(100 * 8).astype(np.float32)
+    ids = np.array([3, 0, 99, 3], np.uint32)
+    got = ops.embedding_lookup(cuda(emb), cuda(ids.view(np.int32)), 8).cpu().numpy()
+    assert np.array_equal(got, R.embedding_lookup(emb, ids, 8))
+    with pytest.raises(IfxError) as e:
+        ops.embedding_lookup(cuda(emb), cuda(np.array([100], np.int32)), 8)
+    assert e.value.name == "InvalidTensorIndex"
+
+
+def test_argmax_last_index_on_ties():
+    v = np.zeros(128256, np.float32)
+    assert ops.argmax(cuda(v)) == 128255
+    v[[5, 77, 1000]] = 3.0
+    assert ops.argmax(cuda(v)) == 1000
+    r = np.random.default_rng(4).standard_normal(50000).astype(np.float32)
+    assert ops.argmax(cuda(r)) == R.argmax(r)
+
+
+@pytest.mark.parametrize("temp,top_k,top_p", [(1.0, 0, 1.0), (0.7, 40, 1.0), (1.0, 0, 0.9),
+                                              (0.8, 50, 0.95), (1.3, 3, 1.0)])
+def test_sampler_matches_oracle_given_uniform(temp, top_k, top_p):
+    rng = np.random.default_rng(int(temp * 100) + top_k)
+    logits = (rng.standard_normal(32000) * 2).astype(np.float32)
+    d = cuda(logits)
+    us = np.linspace(0.001, 0.999, 41)
+    agree = sum(ops.sample_u(d, temp, top_k, top_p, float(u)) == R.sample(logits, temp, top_k, top_p, float(u))
+                for u in us)
+    # the device sums in a different order, so a draw that lands within f32
+    # rounding of a cumulative boundary may pick the neighbour
+    assert agree >= len(us) - 2
+
+
+def test_sampler_greedy_and_topk_bounds():  # sampler.rs:88-123
+    assert ops.sample_u(cuda(np.array([1.0, 3.0, 2.0], np.float32)), 0.0, 0, 1.0, 0.5) == 1
+    for u in np.linspace(0, 0.999, 9):
+        assert ops.sample_u(cuda(np.array([0.0, 1.0, 0.0], np.float32)), 1.0, 0, 1.0, float(u)) < 3
+        assert ops.sample_u(cuda(np.array([10.0, 1.0, 1.0, 1.0], np.float32)), 1.0, 2, 1.0, float(u)) <= 1
