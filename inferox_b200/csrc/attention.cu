@@ -25,13 +25,39 @@ __device__ __forceinline__ void rope_pair(float &a, float &b, int i, int rope_di
 }
 
 __global__ void __launch_bounds__(kAttnThreads) decode_attn_kernel(const __grid_constant__ DecodeAttnArgs a) {
-  extern __shared__ float sm[];
+  extern __shared__ __align__(128) uint8_t smraw[];
   const int h = blockIdx.x, s = blockIdx.y, tid = threadIdx.x;
   const int grp = a.H / a.G, hd = a.hd, NS = a.ns;
   const int cap = (a.max_seq + NS - 1) / NS + 1;
-  float *qs = sm;               // [grp][hd]
-  float *sc = sm + grp * hd;    // [grp][cap]
+  __half *Ks = reinterpret_cast<__half *>(smraw);  // [cap][hd]
+  __half *Vs = Ks + (size_t)cap * hd;               // [cap][hd]
+  float *qs = reinterpret_cast<float *>(Vs + (size_t)cap * hd);  // [grp][hd]
+  float *sc = qs + grp * hd;                        // [grp][cap]
   __shared__ int s_last;
+  __shared__ __align__(8) uint64_t bar;
+
+  // Pre-wait: the cache rows [0, pos) of this layer and `pos` itself were
+  // written by kernels that completed before the previous kernel in the
+  // stream started its main phase, so this CTA's chunk can be fetched while
+  // the QKV GEMV is still draining.
+  const int pos = *a.pos;
+  const int len = pos + 1;
+  const int chunk = (len + NS - 1) / NS;
+  const int t0 = s * chunk, t1 = min(len, t0 + chunk);
+  const int nk = max(0, t1 - t0);
+  const int nold = max(0, min(t1, pos) - t0);  // rows already in the cache
+  __half *kc = a.kc + (size_t)h * a.max_seq * hd;
+  __half *vc = a.vc + (size_t)h * a.max_seq * hd;
+  const uint32_t row_bytes = (uint32_t)hd * 2u;
+  if (tid == 0) {
+    mbar_init(&bar, 1);
+    fence_mbar_init();
+    if (nold > 0) {
+      mbar_arrive_expect_tx(&bar, 2u * nold * row_bytes);
+      bulk_g2s(Ks, kc + (size_t)t0 * hd, nold * row_bytes, &bar);
+      bulk_g2s(Vs, vc + (size_t)t0 * hd, nold * row_bytes, &bar);
+    }
+  }
 
   pdl_wait();
   pdl_launch();
@@ -41,10 +67,6 @@ __global__ void __launch_bounds__(kAttnThreads) decode_attn_kernel(const __grid_
     for (int i = b * kAttnThreads + tid; i < a.zero_n; i += nb * kAttnThreads) a.zero_ptr[i] = 0.f;
   }
 
-  const int pos = *a.pos;
-  const int len = pos + 1;
-  const int chunk = (len + NS - 1) / NS;
-  const int t0 = s * chunk, t1 = min(len, t0 + chunk);
   const float *q = a.qkv + (size_t)h * grp * hd;
   const int rpos = a.rope_compat ? 0 : pos;
   for (int e = tid; e < grp * hd / 2; e += kAttnThreads) {
@@ -54,46 +76,49 @@ __global__ void __launch_bounds__(kAttnThreads) decode_attn_kernel(const __grid_
     qs[j * hd + i] = x0;
     qs[j * hd + i + 1] = x1;
   }
-  __half *kc = a.kc + (size_t)h * a.max_seq * hd;
-  __half *vc = a.vc + (size_t)h * a.max_seq * hd;
   if (t0 <= pos && pos < t1) {
     // append this token's K/V (forward.rs:375-378), K rotated like q
     const float *kn = a.qkv + (size_t)a.H * hd + (size_t)h * hd;
     const float *vn = a.qkv + (size_t)(a.H + a.G) * hd + (size_t)h * hd;
+    const int r = pos - t0;
     for (int e = tid; e < hd / 2; e += kAttnThreads) {
       const int i = 2 * e;
       float x0 = kn[i], x1 = kn[i + 1];
       if (i < a.rope_dim) rope_pair(x0, x1, i, a.rope_dim, a.rope_base, rpos);
-      kc[(size_t)pos * hd + i] = __float2half_rn(x0);
-      kc[(size_t)pos * hd + i + 1] = __float2half_rn(x1);
-      vc[(size_t)pos * hd + i] = __float2half_rn(vn[i]);
-      vc[(size_t)pos * hd + i + 1] = __float2half_rn(vn[i + 1]);
+      const __half2 kh = __floats2half2_rn(x0, x1), vh = __floats2half2_rn(vn[i], vn[i + 1]);
+      *reinterpret_cast<__half2 *>(kc + (size_t)pos * hd + i) = kh;
+      *reinterpret_cast<__half2 *>(vc + (size_t)pos * hd + i) = vh;
+      *reinterpret_cast<__half2 *>(Ks + (size_t)r * hd + i) = kh;
+      *reinterpret_cast<__half2 *>(Vs + (size_t)r * hd + i) = vh;
     }
   }
+  if (nold > 0) mbar_wait(&bar, 0, a.err, 301);
   __syncthreads();
 
-  const int warp = tid >> 5, lane = tid & 31;
+  // scores: one thread per (head j, position t); the 16-byte K chunks are
+  // visited in a rotated order so neighbouring threads hit different banks
   const float sq = sqrtf((float)hd);
-  for (int t = t0 + warp; t < t1; t += kAttnThreads / 32) {
-    const __half *kr = kc + (size_t)t * hd;
-    float part[kMaxGroup];
+  const int nch = hd / 8;
+  for (int e = tid; e < grp * nk; e += kAttnThreads) {
+    const int j = e / nk, t = e % nk;
+    const uint4 *kr = reinterpret_cast<const uint4 *>(Ks + (size_t)t * hd);
+    const float *qj = qs + j * hd;
+    float acc = 0.f;
+    for (int cc = 0; cc < nch; ++cc) {
+      const int c8 = (cc + t) % nch;
+      const uint4 kv = kr[c8];
+      const __half2 *k2 = reinterpret_cast<const __half2 *>(&kv);
 #pragma unroll
-    for (int j = 0; j < kMaxGroup; ++j) part[j] = 0.f;
-    for (int d = lane; d < hd; d += 32) {
-      const float kv = __half2float(kr[d]);
-#pragma unroll
-      for (int j = 0; j < kMaxGroup; ++j)
-        if (j < grp) part[j] = fmaf(qs[j * hd + d], kv, part[j]);
-    }
-#pragma unroll
-    for (int j = 0; j < kMaxGroup; ++j)
-      if (j < grp) {
-        float v = warp_sum(part[j]);
-        if (lane == 0) sc[j * cap + (t - t0)] = v / sq;  // forward.rs:396
+      for (int u = 0; u < 4; ++u) {
+        const float2 kf = __half22float2(k2[u]);
+        acc = fmaf(qj[c8 * 8 + 2 * u], kf.x, acc);
+        acc = fmaf(qj[c8 * 8 + 2 * u + 1], kf.y, acc);
       }
+    }
+    sc[j * cap + t] = acc / sq;  // forward.rs:396
   }
   __syncthreads();
-  const int nk = max(0, t1 - t0);
+  const int warp = tid >> 5, lane = tid & 31;
   // per-head softmax statistics over this chunk
   __shared__ float s_m[kMaxGroup], s_l[kMaxGroup];
   for (int j = warp; j < grp; j += kAttnThreads / 32) {
@@ -117,7 +142,7 @@ __global__ void __launch_bounds__(kAttnThreads) decode_attn_kernel(const __grid_
   for (int e = tid; e < grp * hd; e += kAttnThreads) {
     const int j = e / hd, d = e % hd;
     float o = 0.f;
-    for (int t = 0; t < nk; ++t) o = fmaf(sc[j * cap + t], __half2float(vc[(size_t)(t0 + t) * hd + d]), o);
+    for (int t = 0; t < nk; ++t) o = fmaf(sc[j * cap + t], __half2float(Vs[(size_t)t * hd + d]), o);
     po[e] = o;
   }
   if (tid < grp) a.part_ml[(h * NS + s) * grp + tid] = make_float2(s_m[tid], s_l[tid]);
@@ -242,16 +267,16 @@ __global__ void __launch_bounds__(128) prefill_attn_kernel(PrefillAttnArgs a) {
 
 }  // namespace
 
-int decode_attention_smem(int grp, int max_seq, int ns) {
+int decode_attention_smem(int grp, int hd, int max_seq, int ns) {
   const int cap = (max_seq + ns - 1) / ns + 1;
-  return (grp * 128 + grp * cap) * (int)sizeof(float) + 64;
+  return 2 * cap * hd * 2 + (grp * hd + grp * cap) * (int)sizeof(float);
 }
 
 ifx_status decode_attention(const DecodeAttnArgs &a, cudaStream_t st, bool pdl) {
   const int grp = a.H / a.G;
-  if (grp > kMaxGroup || a.hd > 256 || a.hd % 2) return fail(IFX_ERR_UNSUPPORTED, "attention shape");
-  const int cap = (a.max_seq + a.ns - 1) / a.ns + 1;
-  const size_t smem = (size_t)(grp * a.hd + grp * cap) * sizeof(float);
+  if (grp > kMaxGroup || a.hd > 256 || a.hd % 8) return fail(IFX_ERR_UNSUPPORTED, "attention shape");
+  const size_t smem = (size_t)decode_attention_smem(grp, a.hd, a.max_seq, a.ns);
+  if (smem > 200 * 1024) return fail(IFX_ERR_UNSUPPORTED, "attention: KV chunk too large for shared memory");
   static size_t attr = 0;
   if (smem > 48 * 1024 && smem > attr) {
     IFX_CUDA(cudaFuncSetAttribute(decode_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,

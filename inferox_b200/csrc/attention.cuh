@@ -22,7 +22,7 @@ struct DecodeAttnArgs {
 };
 
 ifx_status decode_attention(const DecodeAttnArgs &a, cudaStream_t st, bool pdl);
-int decode_attention_smem(int grp, int max_seq, int ns);
+int decode_attention_smem(int grp, int hd, int max_seq, int ns);
 
 // Causal attention inside one prefill chunk (forward.rs:255-305): q/k/v rows
 // of the chunk only, position t attends to 0..=t of the chunk.

@@ -126,8 +126,17 @@ __device__ __forceinline__ float warp_max(float v) {
   return v;
 }
 
-// f16 bits -> f32 (exact, subnormals kept): the `half` crate's to_f32.
+// f16 bits -> f32 (exact, subnormals kept). NaN payloads are not preserved;
+// use h2f_exact where bit-exactness with the `half` crate matters.
 __device__ __forceinline__ float h2f(uint16_t h) { return __half2float(__ushort_as_half(h)); }
+
+// The `half` crate's to_f32 bit for bit: NaNs keep their payload and get the
+// quiet bit set (0x7FC0_0000), which __half2float does not do.
+__device__ __forceinline__ float h2f_exact(uint16_t h) {
+  if ((h & 0x7c00u) == 0x7c00u && (h & 0x3ffu))
+    return __uint_as_float(((uint32_t)(h & 0x8000u) << 16) | 0x7fc00000u | ((uint32_t)(h & 0x3ffu) << 13));
+  return __half2float(__ushort_as_half(h));
+}
 
 // Launch helper: optionally attach the programmatic-stream-serialization
 // attribute so the kernel may begin while its predecessor drains.

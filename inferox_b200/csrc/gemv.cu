@@ -53,29 +53,36 @@ __device__ __forceinline__ void unit_q4k(const uint8_t *wt, const uint4 *xf, con
   const int g = lane >> 2, c = lane & 3;
   const uint4 *qv = reinterpret_cast<const uint4 *>(wt);
   const uint4 *sv = reinterpret_cast<const uint4 *>(wt + 2048);
-  float D[4] = {0.f, 0.f, 0.f, 0.f};
-  uint4 q[4];
+  // four independent accumulator chains (one per 64-column step); each step
+  // only fills its own two group columns, so summing them is exact
+  float Ds[4][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f},
+                    {0.f, 0.f, 0.f, 0.f}};
+  uint4 q[4], xb[8];
 #pragma unroll
   for (int s = 0; s < 4; ++s) q[s] = qv[s * 32 + lane];
+#pragma unroll
+  for (int p = 0; p < 8; ++p) xb[p] = xf[p * 4];
 #pragma unroll
   for (int s = 0; s < 4; ++s) {
     const uint32_t wds[4] = {q[s].x, q[s].y, q[s].z, q[s].w};
 #pragma unroll
     for (int p2 = 0; p2 < 2; ++p2) {
       const int pair = 2 * s + p2;  // chunk pair == quant group (32 columns)
-      const uint4 xb = xf[pair * 4];
       const uint32_t m = mk[pair];
 #pragma unroll
       for (int e = 0; e < 2; ++e) {
         const uint32_t wd = wds[2 * p2 + e];
         const uint32_t hi = wd >> 8;
-        const uint32_t b0 = (e ? xb.z : xb.x) & m;
-        const uint32_t b1 = (e ? xb.w : xb.y) & m;
-        mma_16816(D, wd & 0x000F000Fu, wd & 0x00F000F0u, hi & 0x000F000Fu, hi & 0x00F000F0u, b0,
-                  b1, D);
+        const uint32_t b0 = (e ? xb[pair].z : xb[pair].x) & m;
+        const uint32_t b1 = (e ? xb[pair].w : xb[pair].y) & m;
+        mma_16816(Ds[s], wd & 0x000F000Fu, wd & 0x00F000F0u, hi & 0x000F000Fu, hi & 0x00F000F0u,
+                  b0, b1, Ds[s]);
       }
     }
   }
+  float D[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) D[i] = (Ds[0][i] + Ds[1][i]) + (Ds[2][i] + Ds[3][i]);
   // D[0] = (g, group 2c), D[1] = (g, 2c+1), D[2] = (g+8, 2c), D[3] = (g+8, 2c+1)
   const float Sa = s16[4 * c] + s16[4 * c + 1];
   const float Sb = s16[4 * c + 2] + s16[4 * c + 3];
@@ -109,8 +116,15 @@ __device__ __forceinline__ void unit_q6k(const uint8_t *wt, const uint4 *xf, con
   const int g = lane >> 2, c = lane & 3;
   const uint4 *qv = reinterpret_cast<const uint4 *>(wt);
   const uint4 *hv = reinterpret_cast<const uint4 *>(wt + 2048);
-  float DL[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
-  float DH[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+  // eight independent chains: {low plane, 2-bit plane} x set (chunks 0-7 /
+  // 8-15) x chunk parity; parities fill disjoint columns, so they add exactly
+  float DLp[2][2][4], DHp[2][2][4];
+#pragma unroll
+  for (int a = 0; a < 2; ++a)
+#pragma unroll
+    for (int b = 0; b < 2; ++b)
+#pragma unroll
+      for (int i = 0; i < 4; ++i) DLp[a][b][i] = DHp[a][b][i] = 0.f;
   uint4 q[4], hq[2];
 #pragma unroll
   for (int s = 0; s < 4; ++s) q[s] = qv[s * 32 + lane];
@@ -137,13 +151,21 @@ __device__ __forceinline__ void unit_q6k(const uint8_t *wt, const uint4 *xf, con
         const uint32_t b1 = (e ? xb.w : xb.y) & m;
         const uint32_t H = e ? (Hw >> 8) : Hw;
         const uint32_t H4 = H >> 4;
-        mma_16816(DL[set], wd & 0x000F000Fu, wd & 0x00F000F0u, hi & 0x000F000Fu, hi & 0x00F000F0u,
-                  b0, b1, DL[set]);
-        mma_16816(DH[set], H & 0x00030003u, H & 0x000C000Cu, H4 & 0x00030003u, H4 & 0x000C000Cu,
-                  b0, b1, DH[set]);
+        mma_16816(DLp[set][e], wd & 0x000F000Fu, wd & 0x00F000F0u, hi & 0x000F000Fu,
+                  hi & 0x00F000F0u, b0, b1, DLp[set][e]);
+        mma_16816(DHp[set][e], H & 0x00030003u, H & 0x000C000Cu, H4 & 0x00030003u,
+                  H4 & 0x000C000Cu, b0, b1, DHp[set][e]);
       }
     }
   }
+  float DL[2][4], DH[2][4];
+#pragma unroll
+  for (int a = 0; a < 2; ++a)
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      DL[a][i] = DLp[a][0][i] + DLp[a][1][i];
+      DH[a][i] = DHp[a][0][i] + DHp[a][1][i];
+    }
   const uint8_t *scb = wt + 3072;
 #pragma unroll
   for (int h = 0; h < 2; ++h) {
@@ -307,7 +329,7 @@ __device__ void stage_x(const GemvArgs &a, int u0, int n, bool full, uint8_t *xw
   }
 }
 
-__global__ void __launch_bounds__(kGemvThreads, 1) gemv_b1_kernel(const __grid_constant__ GemvArgs a) {
+__global__ void __launch_bounds__(kGemvThreads, 2) gemv_b1_kernel(const __grid_constant__ GemvArgs a) {
   extern __shared__ __align__(128) uint8_t smem[];
   uint64_t *full_bar = reinterpret_cast<uint64_t *>(smem);
   uint64_t *empty_bar = full_bar + kGemvMaxStages;

@@ -247,7 +247,8 @@ ifx_status Model::load(const uint8_t *bytes, size_t len, const ifx_load_opts &o)
   IFX_TRY(dalloc(&amax_key, 1));
   IFX_TRY(dalloc(&amax_count, 1));
   IFX_TRY(dalloc(&n_out, 1));
-  ns = (int)std::max<uint64_t>(1, std::min<uint64_t>(32, kNumSMs / G));
+  // split-K factor of the decode attention: about two CTAs per SM in total
+  ns = (int)std::max<uint64_t>(1, std::min<uint64_t>(64, 2 * kNumSMs / G));
   IFX_TRY(dalloc(&part_o, H * ns * hd));
   IFX_TRY(dalloc(&part_ml, H * ns));
   IFX_TRY(dalloc(&counters, G));

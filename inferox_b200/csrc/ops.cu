@@ -340,6 +340,40 @@ __global__ void __launch_bounds__(kSampThreads) sample_kernel(
   for (size_t i = tid; i < n; i += kSampThreads)
     if (kept(p, i, ck, cp)) s2 += p[i];
   const float S2 = block_sum(s2, red);
+  if (top_k == 0 && !(top_p < 1.0f)) {
+    // Neither filter sorted the candidates, so WeightedIndex walks them in
+    // index order (sampler.rs:45-71): first i with cumsum(p[0..=i]) > u*S2,
+    // else the last index.
+    const size_t per = (n + kSampThreads - 1) / kSampThreads;
+    const size_t lo = tid * per, hi = lo + per < n ? lo + per : n;
+    float mine = 0.f;
+    for (size_t i = lo; i < hi; ++i) mine += p[i];
+    scan[2 + tid] = mine;
+    __syncthreads();
+    if (tid == 0) {
+      float run = 0.f;
+      for (int t = 0; t < kSampThreads; ++t) {
+        const float v = scan[2 + t];
+        scan[2 + t] = run;
+        run += v;
+      }
+    }
+    __shared__ unsigned long long first;
+    if (tid == 0) first = ~0ull;
+    __syncthreads();
+    float run = scan[2 + tid];
+    const float target = u * S2;
+    for (size_t i = lo; i < hi; ++i) {
+      run += p[i];
+      if (run > target) {
+        atomicMin(&first, (unsigned long long)i);
+        break;
+      }
+    }
+    __syncthreads();
+    if (tid == 0) *out = (first == ~0ull) ? (uint32_t)(n - 1) : (uint32_t)first;
+    return;
+  }
   Cut pick = find_cut(p, n, ck, cp, false, u * S2, false, hist, scan);
   if (tid == 0) {
     if (pick.found && pick.idx != 0xffffffffu) {

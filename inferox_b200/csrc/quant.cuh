@@ -39,24 +39,24 @@ __device__ __forceinline__ float dequant_elem(int type, const uint8_t *src, uint
       return __uint_as_float(b);
     }
     case IFX_TYPE_F16:
-      return h2f(ld_u16(src + 2 * e));
+      return h2f_exact(ld_u16(src + 2 * e));
     case IFX_TYPE_Q4_0: {  // dequant.rs:62-84
       const uint8_t *c = src + (e / 32) * 18;
       int j = (int)(e % 32);
-      float delta = h2f(ld_u16(c));
+      float delta = h2f_exact(ld_u16(c));
       uint8_t byte = c[2 + (j & 15)];
       int q = (j < 16) ? (byte & 15) : (byte >> 4);
       return __fmul_rn((float)(q - 8), delta);
     }
     case IFX_TYPE_Q8_0: {  // dequant.rs:93-111
       const uint8_t *c = src + (e / 32) * 34;
-      float delta = h2f(ld_u16(c));
+      float delta = h2f_exact(ld_u16(c));
       return __fmul_rn((float)(int8_t)c[2 + e % 32], delta);
     }
     case IFX_TYPE_Q4_K: {  // dequant.rs:123-163
       const uint8_t *c = src + (e / 256) * 144;
       int j = (int)(e % 256), g = j / 32, l = j % 32;
-      float d = h2f(ld_u16(c)), dmin = h2f(ld_u16(c + 2));
+      float d = h2f_exact(ld_u16(c)), dmin = h2f_exact(ld_u16(c + 2));
       const uint8_t *s = c + 4;
       uint32_t sc, mn;
       if (g < 4) {
@@ -75,7 +75,7 @@ __device__ __forceinline__ float dequant_elem(int type, const uint8_t *src, uint
     case IFX_TYPE_Q6_K: {  // dequant.rs:174-199 (scale byte read as u8)
       const uint8_t *c = src + (e / 256) * 210;
       int j = (int)(e % 256);
-      float d = h2f(ld_u16(c));
+      float d = h2f_exact(ld_u16(c));
       uint8_t qlb = c[18 + j / 2];
       uint32_t nib = (j % 2 == 0) ? (qlb & 15) : (qlb >> 4);
       uint32_t hb = (c[146 + j / 4] >> (2 * (j % 4))) & 3;
@@ -85,7 +85,7 @@ __device__ __forceinline__ float dequant_elem(int type, const uint8_t *src, uint
     case IFX_TYPE_Q8_K: {  // dequant.rs:210-232
       const uint8_t *c = src + (e / 256) * 292;
       int j = (int)(e % 256);
-      float d = h2f(ld_u16(c)), dmin = h2f(ld_u16(c + 2));
+      float d = h2f_exact(ld_u16(c)), dmin = h2f_exact(ld_u16(c + 2));
       float v = __fmul_rn(__fmul_rn(d, (float)c[4 + j / 8]), (float)(int8_t)c[36 + j]);
       return __fsub_rn(v, dmin);
     }

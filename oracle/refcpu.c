@@ -48,7 +48,9 @@ float rc_f16_to_f32(uint16_t h) {
       bits = sign | ((uint32_t)(127 - 15 - e) << 23) | (man << 13);
     }
   } else if (exp == 31) {
-    bits = sign | 0x7f800000u | (man << 13);
+    /* half 2.x f16_to_f32: infinities kept, NaNs keep their payload and get
+     * the quiet bit (0x7FC0_0000), in both its F16C and software paths */
+    bits = sign | (man ? 0x7fc00000u : 0x7f800000u) | (man << 13);
   } else {
     bits = sign | ((exp + 112u) << 23) | (man << 13);
   }

@@ -132,6 +132,11 @@ def test_f16_subnormal_and_specials():
         exp = np.frombuffer(struct.pack("<H", h), np.float16)[0].astype(np.float32)
         got = np.float32(R.f16_to_f32(h))
         assert (np.isnan(exp) and np.isnan(got)) or exp == got
+    # NaN: payload kept, quiet bit set (half 2.x f16_to_f32)
+    b = np.array([R.f16_to_f32(0x7C01)], np.float32).view(np.uint32)[0]
+    assert b == (0x7FC00000 | (1 << 13))
+    b = np.array([R.f16_to_f32(0xFE00)], np.float32).view(np.uint32)[0]
+    assert b == (0x80000000 | 0x7FC00000 | (0x200 << 13))
 
 
 # ---------------- ops.rs tests (ops.rs:293-416) ----------------------------
