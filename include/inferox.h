@@ -91,6 +91,9 @@ typedef struct ifx_load_opts {
                       prefill at 0..n, exactly as forward.rs:243-244,371-372;
                       0: true positions (cache offset + t) */
   int use_graphs;  /* 1 (default): decode steps replay CUDA graphs */
+  int persistent_decode; /* 1 (default): batch-1 decode steps run as one
+                            persistent cooperative kernel per token when the
+                            head geometry allows it; 0: one kernel per op */
 } ifx_load_opts;
 
 void ifx_load_opts_default(ifx_load_opts *o);

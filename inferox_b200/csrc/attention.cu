@@ -10,7 +10,8 @@ namespace ifx {
 namespace {
 
 constexpr int kAttnThreads = 128;
-constexpr int kMaxGroup = 8;  // q heads per kv head handled per CTA
+constexpr int kMaxGroup = 8;    // q heads per kv head handled per CTA
+constexpr int kMaxSplits = 64;  // split-K factor ceiling (model.cu picks <= 64)
 
 __device__ __forceinline__ void rope_pair(float &a, float &b, int i, int rope_dim, float base,
                                           int pos) {
@@ -58,6 +59,7 @@ __global__ void __launch_bounds__(kAttnThreads) decode_attn_kernel(const __grid_
       bulk_g2s(Vs, vc + (size_t)t0 * hd, nold * row_bytes, &bar);
     }
   }
+  __syncthreads();  // the barrier is initialised before any thread waits on it
 
   pdl_wait();
   pdl_launch();
@@ -107,10 +109,10 @@ __global__ void __launch_bounds__(kAttnThreads) decode_attn_kernel(const __grid_
     for (int cc = 0; cc < nch; ++cc) {
       const int c8 = (cc + t) % nch;
       const uint4 kv = kr[c8];
-      const __half2 *k2 = reinterpret_cast<const __half2 *>(&kv);
+      const uint32_t kw[4] = {kv.x, kv.y, kv.z, kv.w};
 #pragma unroll
       for (int u = 0; u < 4; ++u) {
-        const float2 kf = __half22float2(k2[u]);
+        const float2 kf = __half22float2(*reinterpret_cast<const __half2 *>(&kw[u]));
         acc = fmaf(qj[c8 * 8 + 2 * u], kf.x, acc);
         acc = fmaf(qj[c8 * 8 + 2 * u + 1], kf.y, acc);
       }
@@ -155,19 +157,48 @@ __global__ void __launch_bounds__(kAttnThreads) decode_attn_kernel(const __grid_
   __syncthreads();
   if (!s_last) return;
   __threadfence();
-  // combine the NS partial softmaxes of this kv head
-  for (int e = tid; e < grp * hd; e += kAttnThreads) {
-    const int j = e / hd;
+  // Combine the NS partial softmaxes of this kv head. All loads of a phase
+  // are issued together (one L2 round trip each) instead of a serial walk.
+  __shared__ float c_m[kMaxSplits * kMaxGroup], c_w[kMaxSplits * kMaxGroup], c_M[kMaxGroup],
+      c_L[kMaxGroup];
+  for (int e = tid; e < NS * grp; e += kAttnThreads) {
+    const float2 ml = __ldcg(&a.part_ml[h * NS * grp + e]);
+    c_m[e] = ml.x;
+    c_w[e] = ml.y;
+  }
+  __syncthreads();
+  if (tid < grp) {
     float M = -INFINITY;
-    for (int t = 0; t < NS; ++t) M = fmaxf(M, __ldcg(&a.part_ml[(h * NS + t) * grp + j].x));
-    float L = 0.f, O = 0.f;
+    for (int t = 0; t < NS; ++t)
+      if (c_w[t * grp + tid] > 0.f) M = fmaxf(M, c_m[t * grp + tid]);
+    float L = 0.f;
+    for (int t = 0; t < NS; ++t)
+      if (c_w[t * grp + tid] > 0.f) L = fmaf(c_w[t * grp + tid], expf(c_m[t * grp + tid] - M), L);
+    c_M[tid] = M;
+    c_L[tid] = L;
+  }
+  __syncthreads();
+  for (int e = tid; e < NS * grp; e += kAttnThreads) {
+    const int j = e % grp;
+    c_w[e] = (c_w[e] > 0.f) ? expf(c_m[e] - c_M[j]) / c_L[j] : 0.f;
+  }
+  __syncthreads();
+  const float4 *po4 = reinterpret_cast<const float4 *>(a.part_o + (size_t)h * NS * grp * hd);
+  float4 *out4 = reinterpret_cast<float4 *>(a.attn_out + (size_t)h * grp * hd);
+  const int n4 = grp * hd / 4;
+  for (int e4 = tid; e4 < n4; e4 += kAttnThreads) {
+    const int j = (e4 * 4) / hd;
+    float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll 8
     for (int t = 0; t < NS; ++t) {
-      const float2 ml = __ldcg(&a.part_ml[(h * NS + t) * grp + j]);
-      const float w = (ml.y > 0.f) ? expf(ml.x - M) : 0.f;
-      L = fmaf(ml.y, w, L);
-      O = fmaf(__ldcg(&a.part_o[((size_t)(h * NS + t) * grp) * hd + e]), w, O);
+      const float w = c_w[t * grp + j];
+      const float4 p = __ldcg(&po4[(size_t)t * n4 + e4]);
+      o.x = fmaf(w, p.x, o.x);
+      o.y = fmaf(w, p.y, o.y);
+      o.z = fmaf(w, p.z, o.z);
+      o.w = fmaf(w, p.w, o.w);
     }
-    a.attn_out[(size_t)h * grp * hd + e] = O / L;
+    out4[e4] = o;
   }
   if (tid == 0) a.counters[h] = 0;
 }
@@ -274,7 +305,8 @@ int decode_attention_smem(int grp, int hd, int max_seq, int ns) {
 
 ifx_status decode_attention(const DecodeAttnArgs &a, cudaStream_t st, bool pdl) {
   const int grp = a.H / a.G;
-  if (grp > kMaxGroup || a.hd > 256 || a.hd % 8) return fail(IFX_ERR_UNSUPPORTED, "attention shape");
+  if (grp > kMaxGroup || a.hd > 256 || a.hd % 8 || a.ns > kMaxSplits)
+    return fail(IFX_ERR_UNSUPPORTED, "attention shape");
   const size_t smem = (size_t)decode_attention_smem(grp, a.hd, a.max_seq, a.ns);
   if (smem > 200 * 1024) return fail(IFX_ERR_UNSUPPORTED, "attention: KV chunk too large for shared memory");
   static size_t attr = 0;

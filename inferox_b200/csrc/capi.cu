@@ -96,6 +96,7 @@ void ifx_load_opts_default(ifx_load_opts *o) {
   o->nccl_comm = nullptr;
   o->rope_compat = 1;
   o->use_graphs = 1;
+  o->persistent_decode = 1;
 }
 
 ifx_status ifx_model_load_mem(const void *bytes, size_t len, const ifx_load_opts *opts,

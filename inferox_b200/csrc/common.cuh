@@ -65,12 +65,29 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
 // can never hang the GPU. try_wait itself suspends for a while per poll.
 constexpr uint32_t kSpinLimit = 1u << 24;
 
+// A wait also gives up early once another thread has raised the flag, so
+// one lost arrival ends every waiter in the grid quickly.
 __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, int *err_flag,
                                           int code) {
-  for (uint32_t i = 0; i < kSpinLimit; ++i)
+  for (uint32_t i = 0; i < kSpinLimit; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
+    if (err_flag && (i & 1023u) == 1023u && *(volatile int *)err_flag) return false;
+  }
   if (err_flag) atomicExch(err_flag, code);
   return false;
+}
+
+// Wait for the bulk copies of ring positions [max(0, end - NS), end) to land
+// (positions before that had their slot refilled, so they completed). Used
+// before a producer leaves, so no copy into shared memory outlives the CTA.
+__device__ __forceinline__ void ring_drain(uint64_t *full_bar, int NS, uint32_t end) {
+  const uint32_t b = end > (uint32_t)NS ? end - (uint32_t)NS : 0u;
+  for (uint32_t rp = b; rp < end; ++rp) {
+    uint64_t *bar = &full_bar[rp % (uint32_t)NS];
+    const uint32_t ph = (rp / (uint32_t)NS) & 1u;
+    for (uint32_t i = 0; i < kSpinLimit && !mbar_try_wait(bar, ph); ++i) {
+    }
+  }
 }
 
 // 1-D bulk async copy global -> shared, completion counted on an mbarrier.
@@ -96,7 +113,9 @@ __device__ __forceinline__ void pdl_launch() {
 __device__ __forceinline__ void mma_16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2,
                                           uint32_t a3, uint32_t b0, uint32_t b1,
                                           const float (&c)[4]) {
-  asm volatile(
+  // not volatile: the MMA has no side effects, so the scheduler may move
+  // independent work (scale unpack, loads) across it
+  asm(
       "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
       "{%8,%9}, {%10,%11,%12,%13};\n"
       : "=f"(d[0]), "=f"(d[1]), "=f"(d[2]), "=f"(d[3])

@@ -1,0 +1,441 @@
+// Persistent batch-1 decode kernel (one cooperative launch per token).
+//
+// 148 CTAs x (16 consumer warps + 1 producer warp). The token step is a list
+// of phases (embed; per layer QKV GEMV, attention, combine, Wo GEMV, W1/W3
+// GEMV, W2 GEMV; logits GEMV; argmax). Phases that read the previous phase's
+// output are separated by a grid barrier (atomic counter with a bounded
+// spin). The producer warp does not take part in the barriers: weights do
+// not depend on activations, so it streams every GEMV phase's units for its
+// CTA into the shared-memory ring back to back, running ahead across phase
+// boundaries by as many stages as the ring holds. Barrier and staging time
+// of the consumers is therefore overlapped with weight streaming, which is
+// what separate kernel launches could not do.
+#include <algorithm>
+#include <vector>
+
+#include "decode_mega.cuh"
+#include "gemv_dev.cuh"
+#include "ops.cuh"
+#include "quant.cuh"
+
+namespace ifx {
+
+namespace {
+
+using namespace gemvdev;
+
+constexpr int kMaxGrp = 8;
+constexpr int kMaxSplitsMega = 128;
+
+__device__ __forceinline__ unsigned ld_acquire(const unsigned *p) {
+  unsigned v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// Grid barrier over all CTAs (consumer warps only). Bounded: polling stops
+// after 2^22 polls or as soon as any thread has raised the error flag.
+// Returns false (the same value in every consumer thread of the CTA) when the
+// error flag is set, so the CTA's consumers leave together; the host then
+// reports IFX_ERR_TIMEOUT.
+__device__ bool grid_barrier(unsigned *bar, unsigned target, int *err) {
+  __shared__ int s_err;
+  consumer_sync();
+  if (threadIdx.x == 0) {
+    __threadfence();
+    atomicAdd(bar, 1u);
+    uint32_t spins = 0;
+    while (ld_acquire(bar) < target) {
+      if (++spins > (1u << 22)) {
+        atomicExch(err, 401);
+        break;
+      }
+      if ((spins & 255u) == 0 && *(volatile int *)err) break;
+      __nanosleep(32);
+    }
+    __threadfence();
+    s_err = *(volatile int *)err;
+  }
+  consumer_sync();
+  return s_err == 0;
+}
+
+__device__ __forceinline__ void rope_pair_m(float &a, float &b, int i, int rope_dim, float base,
+                                            int pos) {
+  const float inv = 1.0f / powf(base, (float)i / (float)rope_dim);
+  const float ang = __fmul_rn((float)pos, inv);
+  float s, c;
+  sincosf(ang, &s, &c);
+  const float x0 = __fsub_rn(__fmul_rn(a, c), __fmul_rn(b, s));
+  const float x1 = __fadd_rn(__fmul_rn(a, s), __fmul_rn(b, c));
+  a = x0;
+  b = x1;
+}
+
+// ---------------------------------------------------------------- phases --
+__device__ void phase_embed(const MegaArgs &A) {
+  const int tid = threadIdx.x;
+  const uint64_t base = (uint64_t)(*A.next_token) * (uint64_t)A.D;
+  for (int i = blockIdx.x * kConsumerThreads + tid; i < A.D; i += gridDim.x * kConsumerThreads)
+    A.x[i] = dequant_elem(A.emb_type, A.emb, base + i);
+}
+
+// One (kv head, split) item of split-K decode attention: K/V rows of the
+// split into shared memory, scores (four threads per (head, row)), softmax
+// statistics, P.V, partial (max, sum, output) to global.
+__device__ void attn_item(const MegaArgs &A, const MegaAttn &at, int h, int s, uint8_t *scr) {
+  const int tid = threadIdx.x;
+  const int hd = A.hd, grp = A.H / A.G, NS = A.nsa;
+  const int pos = *A.pos;
+  const int len = pos + 1;
+  const int chunk = (len + NS - 1) / NS;
+  const int t0 = s * chunk, t1 = min(len, t0 + chunk);
+  const int nk = max(0, t1 - t0);
+  const int nold = max(0, min(t1, pos) - t0);
+  const int cap = (A.max_seq + NS - 1) / NS + 1;
+  const int n16 = hd / 8;  // 16-byte chunks per row
+  const int swz = (n16 & 7) ? 0 : 7;  // rows of 8+ chunks: chunk c of row t at c ^ (t & 7)
+  uint4 *Ks = reinterpret_cast<uint4 *>(scr);            // [cap][n16]
+  uint4 *Vs = Ks + (size_t)cap * n16;                     // [cap][n16]
+  float *qs = reinterpret_cast<float *>(Vs + (size_t)cap * n16);  // [grp][hd]
+  float *sc = qs + grp * hd;                              // [grp][cap]
+  float *stat = sc + grp * cap;                           // [grp][2]
+  const uint4 *kg = reinterpret_cast<const uint4 *>(at.kc + ((size_t)h * A.max_seq + t0) * hd);
+  const uint4 *vg = reinterpret_cast<const uint4 *>(at.vc + ((size_t)h * A.max_seq + t0) * hd);
+  for (int e = tid; e < nold * n16; e += kConsumerThreads) {
+    const int t = e / n16, c = e % n16;
+    const uint4 kv = kg[e], vv = vg[e];
+    Ks[t * n16 + (c ^ (t & swz))] = kv;
+    Vs[e] = vv;
+  }
+  const float *q = A.qkv + (size_t)h * grp * hd;
+  const int rpos = A.rope_compat ? 0 : pos;
+  for (int e = tid; e < grp * hd / 2; e += kConsumerThreads) {
+    const int j = e / (hd / 2), i = 2 * (e % (hd / 2));
+    float x0 = __ldcg(q + j * hd + i), x1 = __ldcg(q + j * hd + i + 1);
+    if (i < A.rope_dim) rope_pair_m(x0, x1, i, A.rope_dim, A.rope_base, rpos);
+    qs[j * hd + i] = x0;
+    qs[j * hd + i + 1] = x1;
+  }
+  if (t0 <= pos && pos < t1) {  // append this token's K/V (forward.rs:375-378)
+    const float *kn = A.qkv + (size_t)A.H * hd + (size_t)h * hd;
+    const float *vn = A.qkv + (size_t)(A.H + A.G) * hd + (size_t)h * hd;
+    const int r = pos - t0;
+    __half *kcp = at.kc + ((size_t)h * A.max_seq + pos) * hd;
+    __half *vcp = at.vc + ((size_t)h * A.max_seq + pos) * hd;
+    __half *Kh = reinterpret_cast<__half *>(Ks + (size_t)r * n16);
+    __half *Vh = reinterpret_cast<__half *>(Vs + (size_t)r * n16);
+    for (int e = tid; e < hd / 2; e += kConsumerThreads) {
+      const int i = 2 * e;
+      float x0 = __ldcg(kn + i), x1 = __ldcg(kn + i + 1);
+      if (i < A.rope_dim) rope_pair_m(x0, x1, i, A.rope_dim, A.rope_base, rpos);
+      const __half2 kh = __floats2half2_rn(x0, x1), vh = __floats2half2_rn(__ldcg(vn + i), __ldcg(vn + i + 1));
+      *reinterpret_cast<__half2 *>(kcp + i) = kh;
+      *reinterpret_cast<__half2 *>(vcp + i) = vh;
+      const int c = i / 8, o = i % 8;
+      *reinterpret_cast<__half2 *>(Kh + ((c ^ (r & swz)) * 8 + o)) = kh;
+      *reinterpret_cast<__half2 *>(Vh + i) = vh;
+    }
+  }
+  consumer_sync();
+  // scores: four adjacent threads share one (head j, row t), each a quarter
+  // of the head dimension, combined with two shuffles
+  const float isq = 1.0f / sqrtf((float)hd);
+  for (int base = 0; base < grp * nk * 4; base += kConsumerThreads) {
+    const int e = base + tid;
+    const bool ok = e < grp * nk * 4;
+    float acc = 0.f;
+    int j = 0, t = 0;
+    if (ok) {
+      const int qtr = e & 3;
+      const int jt = e >> 2;
+      j = jt / nk;
+      t = jt % nk;
+      const float4 *q4 = reinterpret_cast<const float4 *>(qs + j * hd);
+      for (int c = qtr; c < n16; c += 4) {
+        const uint4 kv = Ks[t * n16 + (c ^ (t & swz))];
+        const float4 qa = q4[2 * c], qb = q4[2 * c + 1];
+        const uint32_t kw[4] = {kv.x, kv.y, kv.z, kv.w};
+        const float2 k0 = __half22float2(*reinterpret_cast<const __half2 *>(&kw[0]));
+        const float2 k1 = __half22float2(*reinterpret_cast<const __half2 *>(&kw[1]));
+        const float2 k2 = __half22float2(*reinterpret_cast<const __half2 *>(&kw[2]));
+        const float2 k3 = __half22float2(*reinterpret_cast<const __half2 *>(&kw[3]));
+        acc = fmaf(qa.x, k0.x, acc);
+        acc = fmaf(qa.y, k0.y, acc);
+        acc = fmaf(qa.z, k1.x, acc);
+        acc = fmaf(qa.w, k1.y, acc);
+        acc = fmaf(qb.x, k2.x, acc);
+        acc = fmaf(qb.y, k2.y, acc);
+        acc = fmaf(qb.z, k3.x, acc);
+        acc = fmaf(qb.w, k3.y, acc);
+      }
+    }
+    acc += __shfl_xor_sync(0xffffffffu, acc, 1);
+    acc += __shfl_xor_sync(0xffffffffu, acc, 2);
+    if (ok && (tid & 3) == 0) sc[j * cap + t] = acc * isq;
+  }
+  consumer_sync();
+  const int warp = tid >> 5, lane = tid & 31;
+  if (warp < grp) {  // softmax statistics of this split, head j = warp
+    const int j = warp;
+    float m = -INFINITY;
+    for (int t = lane; t < nk; t += 32) m = fmaxf(m, sc[j * cap + t]);
+    m = warp_max(m);
+    float l = 0.f;
+    for (int t = lane; t < nk; t += 32) {
+      const float p = expf(sc[j * cap + t] - m);
+      sc[j * cap + t] = p;
+      l += p;
+    }
+    l = warp_sum(l);
+    if (lane == 0) {
+      stat[2 * j] = m;
+      stat[2 * j + 1] = l;
+    }
+  }
+  consumer_sync();
+  float *po = A.part_o + (size_t)(h * NS + s) * grp * hd;
+  const __half *Vh = reinterpret_cast<const __half *>(Vs);
+  for (int e = tid; e < grp * hd; e += kConsumerThreads) {
+    const int j = e / hd, d = e % hd;
+    float o0 = 0.f, o1 = 0.f, o2 = 0.f, o3 = 0.f;
+    int t = 0;
+    for (; t + 3 < nk; t += 4) {
+      o0 = fmaf(sc[j * cap + t], __half2float(Vh[(size_t)t * hd + d]), o0);
+      o1 = fmaf(sc[j * cap + t + 1], __half2float(Vh[(size_t)(t + 1) * hd + d]), o1);
+      o2 = fmaf(sc[j * cap + t + 2], __half2float(Vh[(size_t)(t + 2) * hd + d]), o2);
+      o3 = fmaf(sc[j * cap + t + 3], __half2float(Vh[(size_t)(t + 3) * hd + d]), o3);
+    }
+    for (; t < nk; ++t) o0 = fmaf(sc[j * cap + t], __half2float(Vh[(size_t)t * hd + d]), o0);
+    po[e] = (o0 + o1) + (o2 + o3);
+  }
+  if (tid < grp) {
+    const float m = nk > 0 ? stat[2 * tid] : -INFINITY, l = nk > 0 ? stat[2 * tid + 1] : 0.f;
+    A.part_ml[(h * NS + s) * grp + tid] = make_float2(m, l);
+  }
+  consumer_sync();  // scratch is reused by the next item
+}
+
+// Combine the splits of one query head: attn[hq] = sum_s w_s o_s / L.
+__device__ void combine_head(const MegaArgs &A, int hq, float *scr) {
+  const int tid = threadIdx.x;
+  const int hd = A.hd, grp = A.H / A.G, NS = A.nsa;
+  const int h = hq / grp, j = hq % grp;
+  float *wm = scr;  // [NS]
+  if (tid < 32) {
+    float M = -INFINITY;
+    for (int s = tid; s < NS; s += 32) {
+      const float2 ml = __ldcg(&A.part_ml[(h * NS + s) * grp + j]);
+      if (ml.y > 0.f) M = fmaxf(M, ml.x);
+    }
+    M = warp_max(M);
+    float L = 0.f;
+    for (int s = tid; s < NS; s += 32) {
+      const float2 ml = __ldcg(&A.part_ml[(h * NS + s) * grp + j]);
+      const float w = ml.y > 0.f ? expf(ml.x - M) : 0.f;
+      wm[s] = w;
+      L = fmaf(ml.y, w, L);
+    }
+    L = warp_sum(L);
+    for (int s = tid; s < NS; s += 32) wm[s] = wm[s] / L;
+  }
+  consumer_sync();
+  for (int d = tid; d < hd; d += kConsumerThreads) {
+    float o0 = 0.f, o1 = 0.f;
+    int s = 0;
+    for (; s + 1 < NS; s += 2) {
+      o0 = fmaf(wm[s], __ldcg(&A.part_o[((size_t)(h * NS + s) * grp + j) * hd + d]), o0);
+      o1 = fmaf(wm[s + 1], __ldcg(&A.part_o[((size_t)(h * NS + s + 1) * grp + j) * hd + d]), o1);
+    }
+    if (s < NS) o0 = fmaf(wm[s], __ldcg(&A.part_o[((size_t)(h * NS + s) * grp + j) * hd + d]), o0);
+    A.attn[(size_t)hq * hd + d] = o0 + o1;
+  }
+  consumer_sync();
+}
+
+__device__ void phase_argmax(const MegaArgs &A, float *scr) {
+  const int tid = threadIdx.x;
+  unsigned long long best = 0;
+  for (int i = blockIdx.x * kConsumerThreads + tid; i < A.V; i += gridDim.x * kConsumerThreads) {
+    const float v = __ldcg(&A.logits[i]);
+    if (v != v) continue;
+    const unsigned long long k = ((unsigned long long)ordered_bits(v) << 32) | (unsigned)i;
+    best = k > best ? k : best;
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const unsigned long long other = __shfl_xor_sync(0xffffffffu, best, o);
+    best = other > best ? other : best;
+  }
+  if ((tid & 31) == 0 && best) atomicMax(A.amax_key, best);
+  consumer_sync();
+  __shared__ int last;
+  if (tid == 0) {
+    __threadfence();
+    last = (atomicAdd(A.amax_count, 1) == (int)gridDim.x - 1);
+    if (last) {
+      __threadfence();
+      const unsigned long long k = atomicAdd(A.amax_key, 0ull);
+      const uint32_t tok = (uint32_t)(k & 0xffffffffull);
+      *A.next_token = tok;
+      A.tokens[*A.n_out] = tok;
+      *A.n_out = *A.n_out + 1;
+      *A.pos = *A.pos + 1;
+      *A.amax_key = 0;
+      *A.amax_count = 0;
+    }
+  }
+  (void)scr;
+}
+
+__global__ void __launch_bounds__(kGemvThreads, 1) decode_mega_kernel(const __grid_constant__ MegaArgs A) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  uint64_t *full_bar = reinterpret_cast<uint64_t *>(smem);
+  uint64_t *empty_bar = full_bar + kGemvMaxStages;
+  uint8_t *ring = smem + kGemvBarBytes;
+  uint8_t *scr = ring + (size_t)A.NS * A.slot_bytes;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < A.NS; ++s) {
+      mbar_init(&full_bar[s], 1);
+      mbar_init(&empty_bar[s], 8);
+    }
+    fence_mbar_init();
+  }
+  __syncthreads();
+
+  if (warp == kConsumerWarps) {
+    // producer: every GEMV phase's units for this CTA, back to back
+    if (lane == 0) {
+      uint32_t it = 0;
+      for (int p = 0; p < A.nph; ++p) {
+        const MegaPhase &P = A.ph[p];
+        if (P.kind != PH_GEMV) continue;
+        const int2 rg = P.g.sched[blockIdx.x];
+        const int n = rg.y - rg.x;
+        if (!gemv_produce(P.g, rg.x, n, it, ring, A.NS, A.slot_bytes, full_bar, empty_bar, A.err))
+          return;  // gemv_produce drained its copies
+        it += (uint32_t)n;
+      }
+      ring_drain(full_bar, A.NS, it);
+    }
+    return;
+  }
+
+  uint32_t it = 0;
+  for (int p = 0; p < A.nph; ++p) {
+    const MegaPhase &P = A.ph[p];
+    if (p > 0 && !grid_barrier(A.bar, (unsigned)p * gridDim.x, A.err)) return;
+    if (P.zero_ptr)
+      for (int i = blockIdx.x * kConsumerThreads + threadIdx.x; i < P.zero_n;
+           i += gridDim.x * kConsumerThreads)
+        P.zero_ptr[i] = 0.f;
+    switch (P.kind) {
+      case PH_EMBED:
+        phase_embed(A);
+        break;
+      case PH_GEMV: {
+        const int2 rg = P.g.sched[blockIdx.x];
+        const int n = rg.y - rg.x;
+        if (n > 0) {
+          const bool full = n >= P.g.kunits;
+          float *s16 = reinterpret_cast<float *>(scr + (size_t)P.g.win_units * P.g.kc * 2);
+          stage_x(P.g, rg.x, n, full, scr, s16);
+          consumer_sync();
+          // on a failed wait the warp carries on to the next grid barrier,
+          // which sees the error flag and ends the CTA's consumers together
+          gemv_consume(P.g, rg.x, n, it, ring, A.NS, A.slot_bytes, full_bar, empty_bar, scr, s16,
+                       full, A.err);
+          it += (uint32_t)n;
+        }
+        break;
+      }
+      case PH_ATTN: {
+        const int items = A.G * A.nsa;
+        for (int item = blockIdx.x; item < items; item += gridDim.x)
+          attn_item(A, P.at, item % A.G, item / A.G, scr);
+        break;
+      }
+      case PH_COMBINE:
+        for (int hq = blockIdx.x; hq < A.H; hq += gridDim.x)
+          combine_head(A, hq, reinterpret_cast<float *>(scr));
+        break;
+      case PH_ARGMAX:
+        phase_argmax(A, reinterpret_cast<float *>(scr));
+        break;
+      default:
+        break;
+    }
+  }
+}
+
+}  // namespace
+
+int mega_attn_splits(int G, int max_seq, int num_sms) {
+  int ns = std::max(1, num_sms / std::max(1, G));
+  ns = std::max(ns, (max_seq + 79) / 80);  // at most ~80 cached rows per item
+  return std::min(ns, kMaxSplitsMega);
+}
+
+size_t mega_attn_scratch(int grp, int hd, int max_seq, int nsa) {
+  const size_t cap = (size_t)(max_seq + nsa - 1) / nsa + 1;
+  return 2 * cap * hd * 2 + (size_t)grp * hd * 4 + (size_t)grp * cap * 4 + (size_t)grp * 8 + 64;
+}
+
+ifx_status mega_finalize(MegaPlan *plan, const std::vector<MegaPhase> &phases, int num_sms) {
+  MegaArgs &A = plan->args;
+  if (A.H / A.G > kMaxGrp || A.hd % 8 || A.hd > 256 || A.nsa > kMaxSplitsMega)
+    return fail(IFX_ERR_UNSUPPORTED, "persistent decode: unsupported head geometry");
+  size_t slot = 0, win = 0;
+  for (const MegaPhase &p : phases)
+    if (p.kind == PH_GEMV) {
+      slot = std::max<size_t>(slot, (size_t)p.g.slot_bytes);
+      win = std::max<size_t>(win, (size_t)p.g.win_units * (p.g.kc * 2 + p.g.kc / 16 * 4));
+    }
+  const size_t scratch = std::max<size_t>(
+      {win, mega_attn_scratch(A.H / A.G, A.hd, A.max_seq, A.nsa), (size_t)kMaxSplitsMega * 4});
+  constexpr size_t kCap = 220 * 1024;
+  if (kGemvBarBytes + 2 * slot + scratch > kCap)
+    return fail(IFX_ERR_UNSUPPORTED, "persistent decode: shared memory plan too large");
+  int NS = (int)std::min<size_t>(kGemvMaxStages, (kCap - kGemvBarBytes - scratch) / slot);
+  A.NS = NS;
+  A.slot_bytes = (int)slot;
+  A.scratch_bytes = (int)scratch;
+  A.nph = (int)phases.size();
+  IFX_CUDA(cudaMalloc(&plan->d_phases, sizeof(MegaPhase) * phases.size()));
+  IFX_CUDA(cudaMemcpy(plan->d_phases, phases.data(), sizeof(MegaPhase) * phases.size(),
+                      cudaMemcpyHostToDevice));
+  A.ph = plan->d_phases;
+  plan->smem = kGemvBarBytes + (size_t)NS * slot + scratch;
+  plan->grid = num_sms;
+  IFX_CUDA(cudaFuncSetAttribute(decode_mega_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                (int)kCap));
+  int per_sm = 0;
+  IFX_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, decode_mega_kernel, kGemvThreads,
+                                                         plan->smem));
+  if (per_sm < 1) return fail(IFX_ERR_UNSUPPORTED, "persistent decode kernel does not fit on an SM");
+  return IFX_OK;
+}
+
+ifx_status mega_launch(const MegaPlan &plan, cudaStream_t st) {
+  IFX_CUDA(cudaMemsetAsync(plan.args.bar, 0, sizeof(unsigned), st));
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(plan.grid);
+  cfg.blockDim = dim3(kGemvThreads);
+  cfg.dynamicSmemBytes = plan.smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeCooperative;  // all CTAs co-resident (grid barriers)
+  attr[0].val.cooperative = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  IFX_CUDA(cudaLaunchKernelEx(&cfg, decode_mega_kernel, plan.args));
+  return IFX_OK;
+}
+
+void mega_free(MegaPlan *plan) {
+  if (plan->d_phases) cudaFree(plan->d_phases);
+  plan->d_phases = nullptr;
+}
+
+}  // namespace ifx

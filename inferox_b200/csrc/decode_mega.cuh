@@ -1,0 +1,60 @@
+// Persistent batch-1 decode step: the whole token (embedding, every layer,
+// logits, argmax) in one cooperative launch of one CTA per SM.
+#pragma once
+#include "gemv.cuh"
+
+namespace ifx {
+
+enum MegaKind { PH_EMBED = 0, PH_GEMV = 1, PH_ATTN = 2, PH_COMBINE = 3, PH_ARGMAX = 4 };
+
+struct MegaAttn {
+  __half *kc, *vc;  // this layer's caches [G][max_seq][hd]
+};
+
+struct MegaPhase {
+  int kind;
+  GemvArgs g;   // PH_GEMV (sched has one entry per CTA)
+  MegaAttn at;  // PH_ATTN
+  float *zero_ptr;  // buffer this phase zeroes (a later phase accumulates into it)
+  int zero_n;
+};
+
+struct MegaArgs {
+  const MegaPhase *ph;
+  int nph;
+  int NS, slot_bytes, scratch_bytes;
+  unsigned *bar;  // grid barrier counter, zero at launch
+  int *err;
+  // token loop state
+  const uint8_t *emb;
+  int emb_type, D, V;
+  uint32_t *next_token;
+  float *x, *attn, *logits;
+  float *part_o;
+  float2 *part_ml;
+  int H, G, hd, max_seq, nsa, rope_compat, rope_dim;
+  float rope_base;
+  const float *qkv;
+  int *pos;
+  unsigned long long *amax_key;
+  int *amax_count;
+  uint32_t *tokens;
+  int *n_out;
+};
+
+struct MegaPlan {
+  MegaArgs args{};
+  MegaPhase *d_phases = nullptr;
+  size_t smem = 0;
+  int grid = 0;
+};
+
+// Attention split count for a cache of max_seq rows with G kv heads.
+int mega_attn_splits(int G, int max_seq, int num_sms);
+// Shared-memory bytes the attention phase needs.
+size_t mega_attn_scratch(int grp, int hd, int max_seq, int nsa);
+ifx_status mega_finalize(MegaPlan *plan, const std::vector<MegaPhase> &phases, int num_sms);
+ifx_status mega_launch(const MegaPlan &plan, cudaStream_t st);
+void mega_free(MegaPlan *plan);
+
+}  // namespace ifx

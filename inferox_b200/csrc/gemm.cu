@@ -101,17 +101,13 @@ __device__ __forceinline__ void gemm_unit(const uint8_t *wt, const uint8_t *xs, 
 #pragma unroll
       for (int h = 0; h < 2; ++h) {
         const uint8_t *hb = hdr + 16 * (g + 8 * h);
-        const float d = h2f(*reinterpret_cast<const uint16_t *>(hb));
-        const float dm = h2f(*reinterpret_cast<const uint16_t *>(hb + 2));
-        const uint8_t *s = hb + 4;
-        uint32_t sc, mn;
-        if (grp < 4) {
-          sc = s[grp] & 63;
-          mn = s[grp + 4] & 63;
-        } else {
-          sc = (s[grp + 4] & 15) | ((s[grp - 4] >> 6) << 4);
-          mn = (s[grp + 4] >> 4) | ((s[grp] >> 6) << 4);
-        }
+        // repacked header (repack.cu): word c' = field of groups (2c', 2c'+1)
+        // | byte c' of (d, dmin) << 24
+        const float d = h2f((uint16_t)(hb[3] | (hb[7] << 8)));
+        const float dm = h2f((uint16_t)(hb[11] | (hb[15] << 8)));
+        const uint32_t f = *reinterpret_cast<const uint32_t *>(hb + 4 * (grp >> 1));
+        const int j = grp & 1;
+        const uint32_t sc = (f >> (6 * j)) & 63u, mn = (f >> (12 + 6 * j)) & 63u;
         sg[h] = __float2half2_rn(d * (float)sc * (h ? 0.0625f : 1.0f));
         mg[h] = __float2half2_rn(-(dm * (float)mn));
       }

@@ -16,9 +16,10 @@ enum GemvMode {
 };
 
 constexpr int kGemvMaxSegs = 4;
-constexpr int kGemvMaxStages = 8;
-constexpr int kGemvThreads = 288;  // 8 consumer warps + 1 producer warp
-constexpr int kGemvRingBytes = 96 * 1024;
+constexpr int kGemvMaxStages = 16;
+constexpr int kGemvThreads = 544;  // 16 consumer warps + 1 producer warp
+constexpr int kGemvRingBytes = 176 * 1024;
+constexpr int kGemvBarBytes = 2 * kGemvMaxStages * 8;  // full + empty mbarriers
 
 struct GemvSeg {
   const uint8_t *w;  // repacked weights (device)
@@ -27,6 +28,7 @@ struct GemvSeg {
   int rows;          // valid output rows
   int unit_bytes, wt_bytes, wt_qbytes;
   int unit_begin;    // first global unit index of this segment
+  int units;         // units in this segment (ctiles * kunits)
 };
 
 struct GemvArgs {

@@ -1,0 +1,482 @@
+// Device-side building blocks of the fused dequant GEMV, shared by the
+// standalone GEMV kernel (gemv.cu) and the persistent decode kernel
+// (decode_mega.cu): per-type unit consumers (mma.m16n8k16 over the
+// fragment-ordered layout of qlayout.cuh) and the activation staging.
+#pragma once
+#include "gemv.cuh"
+
+namespace ifx {
+namespace gemvdev {
+
+__device__ __forceinline__ float silu_f(float v) {
+  // ops.rs:199-209: clamp to [-80, 80], x * 1/(1 + exp(-x))
+  float c = fminf(fmaxf(v, -80.0f), 80.0f);
+  return v * (1.0f / (1.0f + expf(-c)));
+}
+
+__device__ __forceinline__ int find_seg(const GemvArgs &a, int u) {
+  int s = 0;
+#pragma unroll
+  for (int i = 1; i < kGemvMaxSegs; ++i)
+    if (i < a.nseg && u >= a.seg[i].unit_begin) s = i;
+  return s;
+}
+
+// (float)v for 0 <= v < 2^23 without the conversion pipe: place v in the
+// mantissa of 2^23 and subtract 2^23 (both steps exact).
+__device__ __forceinline__ float u2f_small(uint32_t v) {
+  return __uint_as_float(0x4B000000u | v) - 8388608.0f;
+}
+
+// f16x2 multiply on raw register bits (runs on the FMA pipe, not the ALU)
+__device__ __forceinline__ uint32_t hmul2u(uint32_t a, uint32_t b) {
+  __half2 r = __hmul2(*reinterpret_cast<__half2 *>(&a), *reinterpret_cast<__half2 *>(&b));
+  return *reinterpret_cast<uint32_t *>(&r);
+}
+
+struct Acc2 {
+  float r0, r1;  // rows g and g+8
+};
+
+// ------------------------------------------------------------------ Q4_K --
+__device__ __forceinline__ void unit_q4k(const uint8_t *wt, const uint4 *xf, const float *s16,
+                                         const uint32_t (&mk)[8], int lane, Acc2 &acc) {
+  const int g = lane >> 2, c = lane & 3;
+  const uint4 *qv = reinterpret_cast<const uint4 *>(wt);
+  const uint4 *sv = reinterpret_cast<const uint4 *>(wt + 2048);
+  // four independent accumulator chains (one per 64-column step); each step
+  // only fills its own two group columns, so summing them is exact
+  float Ds[4][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f},
+                    {0.f, 0.f, 0.f, 0.f}};
+  uint4 q[4], xb[8];
+#pragma unroll
+  for (int s = 0; s < 4; ++s) q[s] = qv[s * 32 + lane];
+#pragma unroll
+  for (int p = 0; p < 8; ++p) xb[p] = xf[p * 4];
+#pragma unroll
+  for (int s = 0; s < 4; ++s) {
+    const uint32_t wds[4] = {q[s].x, q[s].y, q[s].z, q[s].w};
+#pragma unroll
+    for (int p2 = 0; p2 < 2; ++p2) {
+      const int pair = 2 * s + p2;  // chunk pair == quant group (32 columns)
+      const uint32_t m = mk[pair];
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const uint32_t wd = wds[2 * p2 + e];
+        const uint32_t hi = wd >> 8;
+        const uint32_t b0 = hmul2u(e ? xb[pair].z : xb[pair].x, m);
+        const uint32_t b1 = hmul2u(e ? xb[pair].w : xb[pair].y, m);
+        mma_16816(Ds[s], wd & 0x000F000Fu, wd & 0x00F000F0u, hi & 0x000F000Fu, hi & 0x00F000F0u,
+                  b0, b1, Ds[s]);
+      }
+    }
+  }
+  float D[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) D[i] = (Ds[0][i] + Ds[1][i]) + (Ds[2][i] + Ds[3][i]);
+  // D[0] = (g, group 2c), D[1] = (g, 2c+1), D[2] = (g+8, 2c), D[3] = (g+8, 2c+1)
+  const float Sa = s16[4 * c] + s16[4 * c + 1];
+  const float Sb = s16[4 * c + 2] + s16[4 * c + 3];
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    const uint4 hd = sv[g + 8 * h];
+    // repacked header (repack.cu): word c = this lane's 24-bit scale/min field
+    // | byte c of (d, dmin) in the top byte
+    const float d = h2f((uint16_t)prmt(hd.x, hd.y, 0x0073u)) * (h ? 1048576.0f : 16777216.0f);
+    const float dm = h2f((uint16_t)prmt(hd.z, hd.w, 0x0073u));
+    const uint32_t f = (c & 2) ? ((c & 1) ? hd.w : hd.z) : ((c & 1) ? hd.y : hd.x);
+    const float sca = u2f_small(f & 63u), scb = u2f_small((f >> 6) & 63u);
+    const float mna = u2f_small((f >> 12) & 63u), mnb = u2f_small((f >> 18) & 63u);
+    float r = h ? acc.r1 : acc.r0;
+    r = fmaf(d * sca, D[2 * h + 0], r);
+    r = fmaf(-(dm * mna), Sa, r);
+    r = fmaf(d * scb, D[2 * h + 1], r);
+    r = fmaf(-(dm * mnb), Sb, r);
+    if (h) acc.r1 = r; else acc.r0 = r;
+  }
+}
+
+// ------------------------------------------------------------------ Q6_K --
+__device__ __forceinline__ void unit_q6k(const uint8_t *wt, const uint4 *xf, const float *s16,
+                                         const uint32_t (&mk)[8], int lane, Acc2 &acc) {
+  const int g = lane >> 2, c = lane & 3;
+  const uint4 *qv = reinterpret_cast<const uint4 *>(wt);
+  const uint4 *hv = reinterpret_cast<const uint4 *>(wt + 2048);
+  // eight independent chains: {low plane, 2-bit plane} x set (chunks 0-7 /
+  // 8-15) x chunk parity; parities fill disjoint columns, so they add exactly
+  float DLp[2][2][4], DHp[2][2][4];
+#pragma unroll
+  for (int a = 0; a < 2; ++a)
+#pragma unroll
+    for (int b = 0; b < 2; ++b)
+#pragma unroll
+      for (int i = 0; i < 4; ++i) DLp[a][b][i] = DHp[a][b][i] = 0.f;
+  uint4 q[4], hq[2];
+#pragma unroll
+  for (int s = 0; s < 4; ++s) q[s] = qv[s * 32 + lane];
+#pragma unroll
+  for (int t = 0; t < 2; ++t) hq[t] = hv[t * 32 + lane];
+#pragma unroll
+  for (int s = 0; s < 4; ++s) {
+    const uint32_t wds[4] = {q[s].x, q[s].y, q[s].z, q[s].w};
+    const uint4 hh = hq[s >> 1];
+    const uint32_t hws[4] = {hh.x, hh.y, hh.z, hh.w};
+#pragma unroll
+    for (int p2 = 0; p2 < 2; ++p2) {
+      const int pair = 2 * s + p2;
+      const uint4 xb = xf[pair * 4];
+      const uint32_t Hw = hws[pair & 3];
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const int ch = 2 * pair + e;  // 16-column group index 0..15
+        const int set = ch >> 3, col = ch & 7;
+        const uint32_t m = mk[col];
+        const uint32_t wd = wds[2 * p2 + e];
+        const uint32_t hi = wd >> 8;
+        const uint32_t b0 = hmul2u(e ? xb.z : xb.x, m);
+        const uint32_t b1 = hmul2u(e ? xb.w : xb.y, m);
+        const uint32_t H = e ? (Hw >> 8) : Hw;
+        const uint32_t H4 = H >> 4;
+        mma_16816(DLp[set][e], wd & 0x000F000Fu, wd & 0x00F000F0u, hi & 0x000F000Fu,
+                  hi & 0x00F000F0u, b0, b1, DLp[set][e]);
+        mma_16816(DHp[set][e], H & 0x00030003u, H & 0x000C000Cu, H4 & 0x00030003u,
+                  H4 & 0x000C000Cu, b0, b1, DHp[set][e]);
+      }
+    }
+  }
+  float DL[2][4], DH[2][4];
+#pragma unroll
+  for (int a = 0; a < 2; ++a)
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      DL[a][i] = DLp[a][0][i] + DLp[a][1][i];
+      DH[a][i] = DHp[a][0][i] + DHp[a][1][i];
+    }
+  const uint8_t *scb = wt + 3072;
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    const int row = g + 8 * h;
+    const float d = h2f(*reinterpret_cast<const uint16_t *>(scb + 256 + 2 * row));
+    const uint4 sv = *reinterpret_cast<const uint4 *>(scb + 16 * row);
+    // scales for groups 2c, 2c+1 (set 0) and 8+2c, 9+2c (set 1)
+    const uint32_t w_lo = (c < 2) ? sv.x : sv.y;
+    const uint32_t w_hi = (c < 2) ? sv.z : sv.w;
+    const int sh = 16 * (c & 1);
+    float r = h ? acc.r1 : acc.r0;
+#pragma unroll
+    for (int set = 0; set < 2; ++set) {
+      const uint32_t sw = set ? w_hi : w_lo;
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        const int grp = 8 * set + 2 * c + j;
+        const float sc = u2f_small((sw >> (sh + 8 * j)) & 0xffu);
+        const float lo = DL[set][2 * h + j], hv2 = DH[set][2 * h + j];
+        const float dot = h ? (lo + 64.0f * hv2) * 1048576.0f : (lo + 16.0f * hv2) * 16777216.0f;
+        r = fmaf(d * sc, dot - 32.0f * s16[grp], r);
+      }
+    }
+    if (h) acc.r1 = r; else acc.r0 = r;
+  }
+}
+
+// ------------------------------------------------------- Q4_0 and Q8_0 --
+// Generic (runtime chunk count) paths; used by the tiny config and tests.
+__device__ __forceinline__ void unit_q4_0(const uint8_t *wt, int kc, int wt_qbytes,
+                                          const uint4 *xf, const float *s16, int lane, Acc2 &acc) {
+  const int g = lane >> 2, c = lane & 3;
+  const uint4 *qv = reinterpret_cast<const uint4 *>(wt);
+  const int nsteps = kc / 64, nb = kc / 32;
+  float D[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll 1
+  for (int s = 0; s < nsteps; ++s) {
+    const uint4 q = qv[s * 32 + lane];
+    const uint32_t wds[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+    for (int p2 = 0; p2 < 2; ++p2) {
+      const int pair = 2 * s + p2;
+      const uint4 xb = xf[pair * 4];
+      const uint32_t m = (g == pair) ? 0xffffffffu : 0u;
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const uint32_t wd = wds[2 * p2 + e];
+        const uint32_t hi = wd >> 8;
+        mma_16816(D, wd & 0x000F000Fu, wd & 0x00F000F0u, hi & 0x000F000Fu, hi & 0x00F000F0u,
+                  (e ? xb.z : xb.x) & m, (e ? xb.w : xb.y) & m, D);
+      }
+    }
+  }
+  const uint8_t *sc = wt + wt_qbytes;
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    const int row = g + 8 * h;
+    float r = h ? acc.r1 : acc.r0;
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      const int blk = 2 * c + j;
+      if (blk < nb) {
+        const float d = h2f(*reinterpret_cast<const uint16_t *>(sc + (row * nb + blk) * 2));
+        const float S = s16[2 * blk] + s16[2 * blk + 1];
+        const float T = D[2 * h + j] * (h ? 1048576.0f : 16777216.0f);
+        r = fmaf(d, T - 8.0f * S, r);
+      }
+    }
+    if (h) acc.r1 = r; else acc.r0 = r;
+  }
+}
+
+__device__ __forceinline__ void unit_q8_0(const uint8_t *wt, int kc, int wt_qbytes,
+                                          const uint4 *xf, const float *s16, int lane, Acc2 &acc) {
+  const int g = lane >> 2, c = lane & 3;
+  const uint4 *qv = reinterpret_cast<const uint4 *>(wt);
+  const int nb = kc / 32;
+  float D[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll 1
+  for (int s = 0; s < nb; ++s) {  // chunk pair s == block s
+    const uint4 q = qv[s * 32 + lane];
+    const uint4 xb = xf[s * 4];
+    const uint32_t m = (g == s) ? 0xffffffffu : 0u;
+    mma_16816(D, prmt(q.x, 0u, 0x4140u), prmt(q.x, 0u, 0x4342u), prmt(q.y, 0u, 0x4140u),
+              prmt(q.y, 0u, 0x4342u), xb.x & m, xb.y & m, D);
+    mma_16816(D, prmt(q.z, 0u, 0x4140u), prmt(q.z, 0u, 0x4342u), prmt(q.w, 0u, 0x4140u),
+              prmt(q.w, 0u, 0x4342u), xb.z & m, xb.w & m, D);
+  }
+  const uint8_t *sc = wt + wt_qbytes;
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    const int row = g + 8 * h;
+    float r = h ? acc.r1 : acc.r0;
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      const int blk = 2 * c + j;
+      if (blk < nb) {
+        const float d = h2f(*reinterpret_cast<const uint16_t *>(sc + (row * nb + blk) * 2));
+        const float S = s16[2 * blk] + s16[2 * blk + 1];
+        r = fmaf(d, D[2 * h + j] * 16777216.0f - 128.0f * S, r);
+      }
+    }
+    if (h) acc.r1 = r; else acc.r0 = r;
+  }
+}
+
+constexpr int kConsumerWarps = kGemvThreads / 32 - 1;
+constexpr int kConsumerThreads = kConsumerWarps * 32;
+
+// Named barrier over the consumer warps only (the producer warp has left).
+__device__ __forceinline__ void consumer_sync() {
+  asm volatile("bar.sync 1, %0;" ::"n"(kConsumerThreads) : "memory");
+}
+
+// Consumer-side input staging: f(x) as f16 B fragments + 16-column sums.
+// Every global read is a coalesced float4 issued up front (one L2 round trip
+// per pass), so the prologue costs ~1-2 us instead of dozens of serialized
+// round trips.
+static __device__ __noinline__ void stage_x(const GemvArgs &a, int u0, int n, bool full, uint8_t *xw, float *s16) {
+  const int tid = threadIdx.x;  // 0..kConsumerThreads-1
+  constexpr int T = kConsumerThreads;
+  const int nslots = full ? a.kunits : n;
+  const float4 *x4 = reinterpret_cast<const float4 *>(a.x);
+  float inv = 1.0f;
+  if (a.mode == GEMV_RMSNORM) {
+    __shared__ float red[kConsumerWarps];
+    float ss = 0.f;
+    const int K4 = a.K / 4;
+    int f = tid;
+    for (; f + 3 * T < K4; f += 4 * T) {  // four float4 loads in flight per thread
+      const float4 v0 = __ldcg(x4 + f), v1 = __ldcg(x4 + f + T), v2 = __ldcg(x4 + f + 2 * T),
+                   v3 = __ldcg(x4 + f + 3 * T);
+      ss += v0.x * v0.x + v0.y * v0.y + v0.z * v0.z + v0.w * v0.w;
+      ss += v1.x * v1.x + v1.y * v1.y + v1.z * v1.z + v1.w * v1.w;
+      ss += v2.x * v2.x + v2.y * v2.y + v2.z * v2.z + v2.w * v2.w;
+      ss += v3.x * v3.x + v3.y * v3.y + v3.z * v3.z + v3.w * v3.w;
+    }
+    for (; f < K4; f += T) {
+      const float4 v = __ldcg(x4 + f);
+      ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
+    }
+    ss = warp_sum(ss);
+    if ((tid & 31) == 0) red[tid >> 5] = ss;
+    consumer_sync();
+    float tot = 0.f;
+#pragma unroll
+    for (int i = 0; i < kConsumerWarps; ++i) tot += red[i];
+    inv = 1.0f / sqrtf(tot / (float)a.K + a.eps);
+  }
+  const int per_slot = a.kc / 4;  // float4s per slot
+  const int total = nslots * per_slot;
+  __half *xh = reinterpret_cast<__half *>(xw);
+  for (int base = 0; base < total; base += 4 * T) {
+    float4 v[4], w[4];
+    int kk[4];
+#pragma unroll
+    for (int r = 0; r < 4; ++r) v[r] = w[r] = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (int r = 0; r < 4; ++r) {  // issue all loads first
+      const int f = base + r * T + tid;
+      kk[r] = -1;
+      if (f < total) {
+        const int j = f / per_slot, o = (f % per_slot) * 4;
+        int kunit = j;
+        if (!full) {
+          const int u = u0 + j;
+          kunit = (u - a.seg[find_seg(a, u)].unit_begin) % a.kunits;
+        }
+        kk[r] = kunit * a.kc + o;
+        v[r] = __ldcg(x4 + kk[r] / 4);
+        if (a.mode == GEMV_RMSNORM) w[r] = reinterpret_cast<const float4 *>(a.normw)[kk[r] / 4];
+        else if (a.mode == GEMV_SWIGLU) w[r] = __ldcg(reinterpret_cast<const float4 *>(a.x2) + kk[r] / 4);
+      }
+    }
+#pragma unroll
+    for (int r = 0; r < 4; ++r) {
+      const int f = base + r * T + tid;
+      float y[4] = {v[r].x, v[r].y, v[r].z, v[r].w};
+      const float z[4] = {w[r].x, w[r].y, w[r].z, w[r].w};
+      if (kk[r] >= 0) {
+#pragma unroll
+        for (int t = 0; t < 4; ++t) {
+          if (a.mode == GEMV_RMSNORM) y[t] = (y[t] * inv) * z[t];
+          else if (a.mode == GEMV_SWIGLU) y[t] = silu_f(y[t]) * z[t];
+        }
+      }
+      const __half2 h01 = __floats2half2_rn(y[0], y[1]), h23 = __floats2half2_rn(y[2], y[3]);
+      // the 16-column sum of the f16 values the MMA sees: 4 lanes per group
+      float s = (__low2float(h01) + __high2float(h01)) + (__low2float(h23) + __high2float(h23));
+      s += __shfl_xor_sync(0xffffffffu, s, 1);
+      s += __shfl_xor_sync(0xffffffffu, s, 2);
+      if (kk[r] >= 0) {
+        const int j = f / per_slot, o = (f % per_slot) * 4;  // o: column within the slot
+        const int p = o / 32, rr = o % 32, hh = rr / 16, ss = rr % 16;  // ss = 0,4,8,12
+        // element ss at half index ((j*kc/32 + p)*4 + c)*8 + hh*4 + (ss/8)*2 + ss%2
+        const int c0 = (ss % 8) / 2;
+        const size_t ent = ((size_t)(j * (a.kc / 32) + p) * 4) * 8 + hh * 4 + (ss / 8) * 2;
+        *reinterpret_cast<__half2 *>(xh + ent + (size_t)c0 * 8) = h01;
+        *reinterpret_cast<__half2 *>(xh + ent + (size_t)(c0 + 1) * 8) = h23;
+        if ((tid & 3) == 0) s16[j * (a.kc / 16) + o / 16] = s;
+      }
+    }
+  }
+}
+
+// Producer side: stream units [u0, u0 + n) of one GEMV into the ring, ring
+// positions it, it + 1, ... (slot = position % NS). One thread calls this.
+__device__ __forceinline__ bool gemv_produce(const GemvArgs &a, int u0, int n, uint32_t it,
+                                             uint8_t *ring, int NS, int slot_bytes,
+                                             uint64_t *full_bar, uint64_t *empty_bar, int *err) {
+  for (int i = 0; i < n; ++i) {
+    const uint32_t rp = it + (uint32_t)i;
+    const int st = (int)(rp % (uint32_t)NS);
+    const uint32_t ph = (rp / (uint32_t)NS) & 1u;
+    if (rp >= (uint32_t)NS && !mbar_wait(&empty_bar[st], ph ^ 1u, err, 101)) {
+      ring_drain(full_bar, NS, rp);
+      return false;
+    }
+    const int u = u0 + i;
+    const int sg = find_seg(a, u);
+    const GemvSeg &S = a.seg[sg];
+    const uint8_t *src = S.w + (size_t)(u - S.unit_begin) * S.unit_bytes;
+    mbar_arrive_expect_tx(&full_bar[st], (uint32_t)S.unit_bytes);
+    bulk_g2s(ring + (size_t)st * slot_bytes, src, (uint32_t)S.unit_bytes, &full_bar[st]);
+  }
+  return true;
+}
+
+// Consumer side: the 16 consumer warps process units [u0, u0 + n) read from
+// ring positions it, it + 1, ...: two groups of eight warps take alternate
+// units (two units in flight), warp w owns warp tile w % 8, and row sums are
+// flushed with red.global.add whenever a warp's CTA tile or segment changes.
+// x fragments / 16-column sums must already be staged in xw / s16.
+__device__ __forceinline__ bool gemv_consume(const GemvArgs &a, int u0, int n, uint32_t it,
+                                             const uint8_t *ring, int NS, int slot_bytes,
+                                             uint64_t *full_bar, uint64_t *empty_bar,
+                                             const uint8_t *xw, const float *s16, bool full,
+                                             int *err) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = lane >> 2, c = lane & 3;
+  const int half = warp >> 3, wti = warp & 7;
+  uint32_t mk[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) mk[i] = (g == i) ? 0x3C003C00u : 0u;  // f16x2 (1, 1) or (0, 0)
+
+  Acc2 acc{0.f, 0.f};
+  // position of this warp's current unit: segment, index in segment, CTA
+  // tile, column unit (advanced incrementally: no divisions in the loop)
+  int sg = 0, local = 0, ctile = 0, kunit = 0;
+  if (half < n) {
+    const int u = u0 + half;
+    sg = find_seg(a, u);
+    local = u - a.seg[sg].unit_begin;
+    ctile = local / a.kunits;
+    kunit = local % a.kunits;
+  }
+  const int kunits = a.kunits;
+  int s_type = a.seg[sg].type, s_wtb = a.seg[sg].wt_bytes, s_wtq = a.seg[sg].wt_qbytes;
+  int s_rows = a.seg[sg].rows, s_units = a.seg[sg].units;
+  float *s_y = a.seg[sg].y;
+  for (int i = half; i < n; i += 2) {
+    const uint32_t rp = it + (uint32_t)i;
+    const int st = (int)(rp % (uint32_t)NS);
+    const uint32_t ph = (rp / (uint32_t)NS) & 1u;
+    const int slot = full ? kunit : i;
+    if (!mbar_wait(&full_bar[st], ph, err, 102)) return false;
+    const uint8_t *wt = ring + (size_t)st * slot_bytes + (size_t)wti * s_wtb;
+    const uint4 *xf = reinterpret_cast<const uint4 *>(xw) + (size_t)slot * (a.kc / 32) * 4 + c;
+    const float *sl = s16 + (size_t)slot * (a.kc / 16);
+    switch (s_type) {
+      case IFX_TYPE_Q4_K: unit_q4k(wt, xf, sl, mk, lane, acc); break;
+      case IFX_TYPE_Q6_K: unit_q6k(wt, xf, sl, mk, lane, acc); break;
+      case IFX_TYPE_Q4_0: unit_q4_0(wt, a.kc, s_wtq, xf, sl, lane, acc); break;
+      case IFX_TYPE_Q8_0: unit_q8_0(wt, a.kc, s_wtq, xf, sl, lane, acc); break;
+      default: break;
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty_bar[st]);
+
+    // advance two units; flush when this warp's CTA tile or segment changes
+    int nsg = sg, nlocal = local + 2, nct = ctile, nku = kunit + 2;
+    while (nku >= kunits) {
+      nku -= kunits;
+      ++nct;
+    }
+    bool seg_change = false;
+    while (nsg + 1 < a.nseg && nlocal >= a.seg[nsg].units) {
+      nlocal -= a.seg[nsg].units;
+      ++nsg;
+      seg_change = true;
+    }
+    if (seg_change) {
+      nct = nlocal / kunits;
+      nku = nlocal % kunits;
+    }
+    const bool last = i + 2 >= n;
+    if (last || seg_change || nct != ctile) {
+      float r0 = acc.r0, r1 = acc.r1;
+      r0 += __shfl_xor_sync(0xffffffffu, r0, 1);
+      r0 += __shfl_xor_sync(0xffffffffu, r0, 2);
+      r1 += __shfl_xor_sync(0xffffffffu, r1, 1);
+      r1 += __shfl_xor_sync(0xffffffffu, r1, 2);
+      if (c == 0) {
+        const int row = ctile * kCtaRows + wti * 16 + g;
+        if (row < s_rows) red_add_f32(s_y + row, r0);
+        if (row + 8 < s_rows) red_add_f32(s_y + row + 8, r1);
+      }
+      acc.r0 = acc.r1 = 0.f;
+    }
+    if (seg_change) {
+      s_type = a.seg[nsg].type;
+      s_wtb = a.seg[nsg].wt_bytes;
+      s_wtq = a.seg[nsg].wt_qbytes;
+      s_rows = a.seg[nsg].rows;
+      s_units = a.seg[nsg].units;
+      s_y = a.seg[nsg].y;
+    }
+    (void)s_units;
+    sg = nsg;
+    local = nlocal;
+    ctile = nct;
+    kunit = nku;
+  }
+  return true;
+}
+
+}  // namespace gemvdev
+}  // namespace ifx

@@ -332,8 +332,10 @@ ifx_status KvCache::create(Model *model, size_t max_seq_len) {
 KvCache::~KvCache() {
   if (m) cudaSetDevice(m->device);
   if (graph) cudaGraphExecDestroy(graph);
-  for (void *p : {(void *)k, (void *)v, (void *)pos, (void *)tokens})
+  for (void *p : {(void *)k, (void *)v, (void *)pos, (void *)tokens, (void *)part_o,
+                  (void *)part_ml, (void *)bar})
     if (p) cudaFree(p);
+  mega_free(&mega);
 }
 
 ifx_status KvCache::clear() {
@@ -384,7 +386,91 @@ ifx_status Model::enqueue_decode(KvCache &kv, cudaStream_t st) {
   return IFX_OK;
 }
 
+// The persistent decode plan of a cache: the token step as a phase list.
+ifx_status Model::build_mega(KvCache &kv) {
+  kv.mega_tried = true;
+  const ifx_config &c = cfg;
+  const int H = (int)c.n_heads, G = (int)c.n_kv_heads, hd = (int)c.head_dim;
+  if (hd % 8 || hd > 256 || H % G || H / G > 8) return IFX_OK;  // separate kernels instead
+  int dev_sms = 0;
+  IFX_CUDA(cudaDeviceGetAttribute(&dev_sms, cudaDevAttrMultiProcessorCount, device));
+  if (dev_sms != kNumSMs) return IFX_OK;
+  MegaArgs &A = kv.mega.args;
+  A.nsa = mega_attn_splits(G, (int)kv.max_seq, kNumSMs);
+  IFX_TRY(dalloc(&kv.part_o, (size_t)H * A.nsa * hd));
+  IFX_TRY(dalloc(&kv.part_ml, (size_t)H * A.nsa));
+  IFX_TRY(dalloc(&kv.bar, 1));
+  A.bar = kv.bar;
+  A.err = err;
+  A.emb = emb_raw;
+  A.emb_type = emb_type;
+  A.D = (int)c.hidden_size;
+  A.V = (int)c.vocab_size;
+  A.next_token = next_token;
+  A.x = x;
+  A.attn = attn;
+  A.logits = logits;
+  A.part_o = kv.part_o;
+  A.part_ml = kv.part_ml;
+  A.H = H;
+  A.G = G;
+  A.hd = hd;
+  A.max_seq = (int)kv.max_seq;
+  A.rope_compat = opts.rope_compat;
+  A.rope_dim = (int)c.rope_dim;
+  A.rope_base = c.rope_base;
+  A.qkv = qkv;
+  A.pos = kv.pos;
+  A.amax_key = amax_key;
+  A.amax_count = amax_count;
+  A.tokens = kv.tokens;
+  A.n_out = n_out;
+  std::vector<MegaPhase> ph;
+  auto gemv = [&](const GemvPlan &p, float *zero, int zn) {
+    MegaPhase m{};
+    m.kind = PH_GEMV;
+    m.g = p.args;
+    m.g.zero_ptr = nullptr;  // zeroing is a phase duty here
+    m.zero_ptr = zero;
+    m.zero_n = zn;
+    ph.push_back(m);
+  };
+  auto simple = [&](int kind, float *zero, int zn) {
+    MegaPhase m{};
+    m.kind = kind;
+    m.zero_ptr = zero;
+    m.zero_n = zn;
+    ph.push_back(m);
+  };
+  simple(PH_EMBED, logits, (int)c.vocab_size);
+  for (uint64_t l = 0; l < c.n_layers; ++l) {
+    gemv(p_qkv[l], nullptr, 0);
+    MegaPhase at{};
+    at.kind = PH_ATTN;
+    at.at.kc = kv.k + l * kv.per_layer;
+    at.at.vc = kv.v + l * kv.per_layer;
+    at.zero_ptr = gu;  // consumed by the previous layer's W2, refilled by W13
+    at.zero_n = (int)(2 * c.intermediate_size);
+    ph.push_back(at);
+    simple(PH_COMBINE, nullptr, 0);
+    gemv(p_wo[l], nullptr, 0);
+    gemv(p_w13[l], qkv, qkv_n);  // qkv was consumed by ATTN; the next QKV refills it
+    gemv(p_w2[l], nullptr, 0);
+  }
+  gemv(p_logits, nullptr, 0);
+  simple(PH_ARGMAX, nullptr, 0);
+  ifx_status s = mega_finalize(&kv.mega, ph, kNumSMs);
+  if (s != IFX_OK) {
+    mega_free(&kv.mega);
+    return IFX_OK;  // too large for the persistent kernel: separate kernels
+  }
+  kv.mega_ready = true;
+  return IFX_OK;
+}
+
 ifx_status Model::run_decode(KvCache &kv) {
+  if (opts.persistent_decode && !kv.mega_tried) IFX_TRY(build_mega(kv));
+  if (kv.mega_ready) return mega_launch(kv.mega, stream);
   if (!opts.use_graphs) return enqueue_decode(kv, stream);
   if (!kv.graph) {
     cudaGraph_t g;

@@ -5,6 +5,7 @@
 #include <vector>
 
 #include "common.cuh"
+#include "decode_mega.cuh"
 #include "gemv.cuh"
 #include "repack.h"
 
@@ -24,6 +25,11 @@ struct KvCache {  // KvCache (src/model/cache.rs:7-14), f16 on the device
   int *pos = nullptr;                 // device copy of len (read by the kernels)
   uint32_t *tokens = nullptr;         // generated tokens (device)
   cudaGraphExec_t graph = nullptr;    // captured decode step for this cache
+  MegaPlan mega;                      // persistent decode plan for this cache
+  bool mega_ready = false, mega_tried = false;
+  float *part_o = nullptr;            // split-K partials of the persistent kernel
+  float2 *part_ml = nullptr;
+  unsigned *bar = nullptr;
   ifx_status create(Model *model, size_t max_seq_len);
   ifx_status clear();
   ~KvCache();
@@ -65,6 +71,7 @@ struct Model {
 
   ifx_status load(const uint8_t *bytes, size_t len, const ifx_load_opts &o);
   ifx_status enqueue_decode(KvCache &kv, cudaStream_t st);
+  ifx_status build_mega(KvCache &kv);
   ifx_status run_decode(KvCache &kv);
   ifx_status decode_step(KvCache &kv, uint32_t token, float *logits_host);
   ifx_status prefill(KvCache &kv, const uint32_t *ids, size_t n, float *logits_host, int last_row_only);

@@ -116,9 +116,35 @@ __global__ void repack_kernel(QLayout L, const uint8_t *__restrict__ src,
   // scales
   uint8_t *sc = out + L.wt_qbytes;
   if (L.type == IFX_TYPE_Q4_K) {
-    for (int idx = threadIdx.x; idx < 16 * 16; idx += blockDim.x) {
-      int r = idx / 16, b = idx % 16;
-      sc[idx] = valid(r) ? src[((row0 + r) * (L.cols / 256) + kunit) * 144 + b] : 0;
+    // 16 bytes per row = four 32-bit words; word c holds the 24-bit field
+    // sc[2c] | sc[2c+1] << 6 | mn[2c] << 12 | mn[2c+1] << 18 (the two groups
+    // lane c of the GEMV epilogue needs, unpacked from the 6-bit encoding of
+    // dequant.rs:141-149) and, in its top byte, byte c of (d, dmin) as f16.
+    for (int r = threadIdx.x; r < 16; r += blockDim.x) {
+      uint8_t *o = sc + 16 * r;
+      if (!valid(r)) {
+        for (int b = 0; b < 16; ++b) o[b] = 0;
+        continue;
+      }
+      const uint8_t *blk = src + ((row0 + r) * (L.cols / 256) + kunit) * 144;
+      const uint8_t *s = blk + 4;
+      uint32_t scv[8], mnv[8];
+      for (int g = 0; g < 8; ++g) {
+        if (g < 4) {
+          scv[g] = s[g] & 63;
+          mnv[g] = s[g + 4] & 63;
+        } else {
+          scv[g] = (s[g + 4] & 15) | ((s[g - 4] >> 6) << 4);
+          mnv[g] = (s[g + 4] >> 4) | ((s[g] >> 6) << 4);
+        }
+      }
+      for (int c = 0; c < 4; ++c) {
+        const uint32_t f = scv[2 * c] | (scv[2 * c + 1] << 6) | (mnv[2 * c] << 12) | (mnv[2 * c + 1] << 18);
+        o[4 * c + 0] = (uint8_t)(f & 0xff);
+        o[4 * c + 1] = (uint8_t)((f >> 8) & 0xff);
+        o[4 * c + 2] = (uint8_t)((f >> 16) & 0xff);
+        o[4 * c + 3] = blk[c];  // d (bytes 0-1) and dmin (bytes 2-3)
+      }
     }
   } else if (L.type == IFX_TYPE_Q6_K) {
     for (int idx = threadIdx.x; idx < 16 * 16; idx += blockDim.x) {

@@ -30,7 +30,8 @@ def _f32(a):
 
 
 def load_opts(device: int = 0, rope_compat: bool = True, use_graphs: bool = True,
-              tp_size: int = 1, tp_rank: int = 0, nccl_comm: int | None = None) -> LoadOpts:
+              tp_size: int = 1, tp_rank: int = 0, nccl_comm: int | None = None,
+              persistent_decode: bool = True) -> LoadOpts:
     o = LoadOpts()
     lib.ifx_load_opts_default(C.byref(o))
     o.device = device
@@ -39,6 +40,7 @@ def load_opts(device: int = 0, rope_compat: bool = True, use_graphs: bool = True
     o.tp_size = tp_size
     o.tp_rank = tp_rank
     o.nccl_comm = nccl_comm
+    o.persistent_decode = 1 if persistent_decode else 0
     return o
 
 
