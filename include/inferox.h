@@ -225,6 +225,24 @@ ifx_status ifx_op_argmax(const float *x, size_t n, uint32_t *out_dev,
 ifx_status ifx_op_sample_u(const float *logits_dev, size_t n,
                            const ifx_sampler *s, float u,
                            uint32_t *token_host, void *stream);
+/* No counterpart in the reference (its sampler is host code). The same pick
+ * as ifx_op_sample_u, for callers that cannot allocate device memory on this
+ * path: a host runtime that reserves its whole device budget up front and
+ * forbids later allocation, or a serving loop that must not pay for
+ * cudaMalloc/cudaFree (cudaFree synchronises the whole device) on every
+ * token. Its scratch is a static device array reserved when the library
+ * loads, so n is limited to IFX_SAMPLE_STATIC_MAX logits; larger n returns
+ * IFX_ERR_INVALID_ARGUMENT. The token is written to token_dev (device
+ * memory) on `stream`; the call does not synchronise. The first call on a
+ * device looks up the scratch address with that device current; if that
+ * first call could fall inside a stream capture, make one call on the device
+ * before the capture begins. Every call on a device uses the same scratch:
+ * calls whose work overlaps in time (other streams, other threads) race, so
+ * order them on one stream or serialise them. */
+#define IFX_SAMPLE_STATIC_MAX 262144
+ifx_status ifx_op_sample_u_static(const float *logits_dev, size_t n,
+                                  const ifx_sampler *s, float u,
+                                  uint32_t *token_dev, void *stream);
 
 /* --------------------------- measurement hooks -------------------------- */
 /* No reference counterpart. Launch one of the decode step's fused kernels

@@ -117,6 +117,7 @@ def _load():
         "ifx_op_rope": (st, [vp, sz, sz, sz, sz, C.c_float, sz, vp]),
         "ifx_op_argmax": (st, [vp, sz, vp, vp]),
         "ifx_op_sample_u": (st, [vp, sz, C.POINTER(SamplerC), C.c_float, u32p, vp]),
+        "ifx_op_sample_u_static": (st, [vp, sz, C.POINTER(SamplerC), C.c_float, vp, vp]),
         "ifx_synth_gguf": (st, [C.POINTER(SynthSpec), C.POINTER(vp), C.POINTER(sz)]),
         "ifx_synth_free": (None, [vp]),
         "ifx_quantize": (st, [C.c_int, vp, sz, vp]),

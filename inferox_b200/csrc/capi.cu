@@ -422,4 +422,11 @@ ifx_status ifx_op_sample_u(const float *logits_dev, size_t n, const ifx_sampler 
   return st;
 }
 
+ifx_status ifx_op_sample_u_static(const float *logits_dev, size_t n, const ifx_sampler *s,
+                                  float u, uint32_t *token_dev, void *stream) {
+  if (!logits_dev || !s || !token_dev) return fail(IFX_ERR_INVALID_ARGUMENT, "sample_u_static: null");
+  return op_sample_u_static(logits_dev, n, s->temperature, s->top_k, s->top_p, u, token_dev,
+                            S(stream));
+}
+
 }  // extern "C"

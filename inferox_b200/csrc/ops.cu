@@ -2,6 +2,8 @@
 // These back the op-level C ABI used by parity tests; the token loop uses
 // the fused kernels (gemv.cu, attention.cu, model.cu) instead.
 #include <algorithm>
+#include <mutex>
+#include <string>
 
 #include "ops.cuh"
 #include "quant.cuh"
@@ -518,6 +520,63 @@ ifx_status op_sample_philox(const float *logits, size_t n, float temperature, ui
                             float top_p, uint64_t seed, uint64_t offset, uint32_t *out_dev,
                             cudaStream_t st) {
   return sample_common(logits, n, temperature, top_k, top_p, 0.f, 1, seed, offset, out_dev, st);
+}
+
+// ------------------------------------------- sampler with static scratch --
+// Backing store of op_sample_u_static: one file-scope device array, so that
+// call allocates nothing. Layout: kStaticSampleMax f32 probabilities, then
+// (at byte offset 4 * kStaticSampleMax, a multiple of 256) the 64-bit argmax
+// key of the greedy case. 1 MiB + 256 B per device, reserved at module load.
+static __device__ __align__(256) float g_sample_scratch[kStaticSampleMax + 64];
+static_assert(kStaticSampleMax == IFX_SAMPLE_STATIC_MAX, "header and library limits differ");
+
+namespace {
+constexpr int kStaticMaxDevices = 64;
+std::mutex g_scratch_mu;
+float *g_scratch_ptr[kStaticMaxDevices] = {};
+
+// Address of g_sample_scratch on the current device, looked up once per
+// device (the first call on a device does the lookup with that device
+// current; later calls only read the cached pointer).
+ifx_status static_scratch(float **out) {
+  int dev = 0;
+  IFX_CUDA(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= kStaticMaxDevices)
+    return fail(IFX_ERR_UNSUPPORTED, "sample_u_static: device ordinal " + std::to_string(dev) +
+                                         " beyond the " + std::to_string(kStaticMaxDevices) +
+                                         " devices this build tracks");
+  std::lock_guard<std::mutex> lock(g_scratch_mu);
+  if (!g_scratch_ptr[dev]) {
+    void *ptr = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&ptr, g_sample_scratch);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(g_sample_scratch)");
+    g_scratch_ptr[dev] = static_cast<float *>(ptr);
+  }
+  *out = g_scratch_ptr[dev];
+  return IFX_OK;
+}
+}  // namespace
+
+ifx_status op_sample_u_static(const float *logits, size_t n, float temperature, uint64_t top_k,
+                              float top_p, float u, uint32_t *out_dev, cudaStream_t st) {
+  if (!n) return fail(IFX_ERR_SHAPE, "sample: empty logits");
+  if (n > kStaticSampleMax)
+    return fail(IFX_ERR_INVALID_ARGUMENT,
+                "sample_u_static: " + std::to_string(n) + " logits exceed the static scratch of " +
+                    std::to_string(kStaticSampleMax) + " entries; use ifx_op_sample_u");
+  float *scratch = nullptr;
+  IFX_TRY(static_scratch(&scratch));
+  if (temperature == 0.0f) {
+    // the argmax key is combined with atomicMax and must start at zero
+    auto *key = reinterpret_cast<unsigned long long *>(scratch + kStaticSampleMax);
+    IFX_CUDA(cudaMemsetAsync(key, 0, sizeof(unsigned long long), st));
+    return op_argmax(logits, n, key, out_dev, st);
+  }
+  // p (the first n floats) is written in full before it is read: no clearing
+  sample_kernel<<<1, kSampThreads, 0, st>>>(logits, scratch, n, temperature, top_k, top_p, u, 0,
+                                             0, 0, out_dev);
+  IFX_CUDA(cudaGetLastError());
+  return IFX_OK;
 }
 
 }  // namespace ifx

@@ -28,6 +28,13 @@ ifx_status op_argmax(const float *x, size_t n, unsigned long long *key_dev, uint
                      cudaStream_t st);
 ifx_status op_sample_u(const float *logits, size_t n, float temperature, uint64_t top_k,
                        float top_p, float u, uint32_t *out_dev, cudaStream_t st);
+// Largest logits count op_sample_u_static accepts (its scratch is static).
+constexpr size_t kStaticSampleMax = 262144;
+// op_sample_u with its scratch in a static device array: allocates nothing,
+// writes the token to out_dev on the stream without synchronising. Calls
+// that overlap in time on one device share the scratch and race.
+ifx_status op_sample_u_static(const float *logits, size_t n, float temperature, uint64_t top_k,
+                              float top_p, float u, uint32_t *out_dev, cudaStream_t st);
 // Sampler::sample with a Philox uniform (seed, offset) computed on device.
 ifx_status op_sample_philox(const float *logits, size_t n, float temperature, uint64_t top_k,
                             float top_p, uint64_t seed, uint64_t offset, uint32_t *out_dev,
