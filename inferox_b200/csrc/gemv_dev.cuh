@@ -266,6 +266,24 @@ __device__ __forceinline__ void consumer_sync() {
   asm volatile("bar.sync 1, %0;" ::"n"(kConsumerThreads) : "memory");
 }
 
+// One segment's fields, held in registers by the loops below. Reading
+// GemvArgs through a reference (a __grid_constant__ parameter, or a phase
+// record in global memory) inside a loop turns every field into a load that
+// the mbarrier asm statements' memory clobbers force to be repeated; the
+// loops therefore only touch these copies and re-read GemvArgs when a
+// segment boundary is crossed.
+struct SegView {
+  const uint8_t *w;
+  float *y;
+  int type, rows, unit_bytes, wt_bytes, wt_qbytes, begin, units;
+};
+
+__device__ __forceinline__ SegView load_seg(const GemvArgs &a, int s) {
+  const GemvSeg &S = a.seg[s];
+  return SegView{S.w, S.y, S.type, S.rows, S.unit_bytes, S.wt_bytes, S.wt_qbytes, S.unit_begin,
+                 S.units};
+}
+
 // Consumer-side input staging: f(x) as f16 B fragments + 16-column sums.
 // Every global read is a coalesced float4 issued up front (one L2 round trip
 // per pass), so the prologue costs ~1-2 us instead of dozens of serialized
@@ -273,13 +291,19 @@ __device__ __forceinline__ void consumer_sync() {
 static __device__ __noinline__ void stage_x(const GemvArgs &a, int u0, int n, bool full, uint8_t *xw, float *s16) {
   const int tid = threadIdx.x;  // 0..kConsumerThreads-1
   constexpr int T = kConsumerThreads;
-  const int nslots = full ? a.kunits : n;
+  const int mode = a.mode, K = a.K, kc = a.kc, kunits = a.kunits, nseg = a.nseg;
   const float4 *x4 = reinterpret_cast<const float4 *>(a.x);
+  const float4 *w4 = reinterpret_cast<const float4 *>(mode == GEMV_RMSNORM ? a.normw : a.x2);
+  const float eps = a.eps;
+  int sb[kGemvMaxSegs];  // segment first units (increasing); unused ones never match
+#pragma unroll
+  for (int i = 0; i < kGemvMaxSegs; ++i) sb[i] = i < nseg ? a.seg[i].unit_begin : 0x7fffffff;
+  const int nslots = full ? kunits : n;
   float inv = 1.0f;
-  if (a.mode == GEMV_RMSNORM) {
+  if (mode == GEMV_RMSNORM) {
     __shared__ float red[kConsumerWarps];
     float ss = 0.f;
-    const int K4 = a.K / 4;
+    const int K4 = K / 4;
     int f = tid;
     for (; f + 3 * T < K4; f += 4 * T) {  // four float4 loads in flight per thread
       const float4 v0 = __ldcg(x4 + f), v1 = __ldcg(x4 + f + T), v2 = __ldcg(x4 + f + 2 * T),
@@ -299,9 +323,9 @@ static __device__ __noinline__ void stage_x(const GemvArgs &a, int u0, int n, bo
     float tot = 0.f;
 #pragma unroll
     for (int i = 0; i < kConsumerWarps; ++i) tot += red[i];
-    inv = 1.0f / sqrtf(tot / (float)a.K + a.eps);
+    inv = 1.0f / sqrtf(tot / (float)K + eps);
   }
-  const int per_slot = a.kc / 4;  // float4s per slot
+  const int per_slot = kc / 4;  // float4s per slot
   const int total = nslots * per_slot;
   __half *xh = reinterpret_cast<__half *>(xw);
   for (int base = 0; base < total; base += 4 * T) {
@@ -318,12 +342,14 @@ static __device__ __noinline__ void stage_x(const GemvArgs &a, int u0, int n, bo
         int kunit = j;
         if (!full) {
           const int u = u0 + j;
-          kunit = (u - a.seg[find_seg(a, u)].unit_begin) % a.kunits;
+          int b = sb[0];
+#pragma unroll
+          for (int i = 1; i < kGemvMaxSegs; ++i) b = u >= sb[i] ? sb[i] : b;
+          kunit = (u - b) % kunits;
         }
-        kk[r] = kunit * a.kc + o;
+        kk[r] = kunit * kc + o;
         v[r] = __ldcg(x4 + kk[r] / 4);
-        if (a.mode == GEMV_RMSNORM) w[r] = reinterpret_cast<const float4 *>(a.normw)[kk[r] / 4];
-        else if (a.mode == GEMV_SWIGLU) w[r] = __ldcg(reinterpret_cast<const float4 *>(a.x2) + kk[r] / 4);
+        if (mode != GEMV_PLAIN) w[r] = mode == GEMV_SWIGLU ? __ldcg(w4 + kk[r] / 4) : w4[kk[r] / 4];
       }
     }
 #pragma unroll
@@ -334,8 +360,8 @@ static __device__ __noinline__ void stage_x(const GemvArgs &a, int u0, int n, bo
       if (kk[r] >= 0) {
 #pragma unroll
         for (int t = 0; t < 4; ++t) {
-          if (a.mode == GEMV_RMSNORM) y[t] = (y[t] * inv) * z[t];
-          else if (a.mode == GEMV_SWIGLU) y[t] = silu_f(y[t]) * z[t];
+          if (mode == GEMV_RMSNORM) y[t] = (y[t] * inv) * z[t];
+          else if (mode == GEMV_SWIGLU) y[t] = silu_f(y[t]) * z[t];
         }
       }
       const __half2 h01 = __floats2half2_rn(y[0], y[1]), h23 = __floats2half2_rn(y[2], y[3]);
@@ -348,20 +374,61 @@ static __device__ __noinline__ void stage_x(const GemvArgs &a, int u0, int n, bo
         const int p = o / 32, rr = o % 32, hh = rr / 16, ss = rr % 16;  // ss = 0,4,8,12
         // element ss at half index ((j*kc/32 + p)*4 + c)*8 + hh*4 + (ss/8)*2 + ss%2
         const int c0 = (ss % 8) / 2;
-        const size_t ent = ((size_t)(j * (a.kc / 32) + p) * 4) * 8 + hh * 4 + (ss / 8) * 2;
+        const size_t ent = ((size_t)(j * (kc / 32) + p) * 4) * 8 + hh * 4 + (ss / 8) * 2;
         *reinterpret_cast<__half2 *>(xh + ent + (size_t)c0 * 8) = h01;
         *reinterpret_cast<__half2 *>(xh + ent + (size_t)(c0 + 1) * 8) = h23;
-        if ((tid & 3) == 0) s16[j * (a.kc / 16) + o / 16] = s;
+        if ((tid & 3) == 0) s16[j * (kc / 16) + o / 16] = s;
       }
     }
   }
 }
 
-// Producer side: stream units [u0, u0 + n) of one GEMV into the ring, ring
-// positions it, it + 1, ... (slot = position % NS). One thread calls this.
+// Unit ranges of the two consumer halves: half 0 takes the first
+// ceil(n/2) units of the CTA's range [u0, u0 + n), half 1 the rest, each
+// walking its run in order. Ring position p holds half (p & 1)'s unit p >> 1,
+// so the positions alternate between the halves (with an odd n the last
+// position, n - 1, is even and belongs to half 0).
+__device__ __forceinline__ int half_begin(int n, int half) { return half ? (n + 1) >> 1 : 0; }
+__device__ __forceinline__ int half_count(int n, int half) { return half ? n >> 1 : (n + 1) >> 1; }
+
+// Walks the units of one half run, one segment at a time, for the producer.
+struct UnitCursor {
+  int sg, left;
+  SegView S;
+  const uint8_t *src;
+  __device__ __forceinline__ void init(const GemvArgs &a, int u) {
+    sg = find_seg(a, u);
+    S = load_seg(a, sg);
+    src = S.w + (size_t)(u - S.begin) * S.unit_bytes;
+    left = S.begin + S.units - u;
+  }
+  // source of the current unit, then advance (the run never passes the
+  // last segment)
+  __device__ __forceinline__ const uint8_t *next(const GemvArgs &a, int &bytes) {
+    if (left <= 0) {
+      ++sg;
+      S = load_seg(a, sg);
+      src = S.w;
+      left = S.units;
+    }
+    const uint8_t *p = src;
+    bytes = S.unit_bytes;
+    src += S.unit_bytes;
+    --left;
+    return p;
+  }
+};
+
+// Producer side: stream the CTA's units [u0, u0 + n) of one GEMV into the
+// ring, ring positions it, it + 1, ... (slot = position % NS), alternating
+// between the two halves' runs. One thread calls this.
 __device__ __forceinline__ bool gemv_produce(const GemvArgs &a, int u0, int n, uint32_t it,
                                              uint8_t *ring, int NS, int slot_bytes,
                                              uint64_t *full_bar, uint64_t *empty_bar, int *err) {
+  if (n <= 0) return true;
+  UnitCursor c0, c1;  // two named cursors: an indexed pair would live in local memory
+  c0.init(a, u0);
+  if (n > 1) c1.init(a, u0 + half_begin(n, 1));
   for (int i = 0; i < n; ++i) {
     const uint32_t rp = it + (uint32_t)i;
     const int st = (int)(rp % (uint32_t)NS);
@@ -370,20 +437,69 @@ __device__ __forceinline__ bool gemv_produce(const GemvArgs &a, int u0, int n, u
       ring_drain(full_bar, NS, rp);
       return false;
     }
-    const int u = u0 + i;
-    const int sg = find_seg(a, u);
-    const GemvSeg &S = a.seg[sg];
-    const uint8_t *src = S.w + (size_t)(u - S.unit_begin) * S.unit_bytes;
-    mbar_arrive_expect_tx(&full_bar[st], (uint32_t)S.unit_bytes);
-    bulk_g2s(ring + (size_t)st * slot_bytes, src, (uint32_t)S.unit_bytes, &full_bar[st]);
+    int bytes;
+    const uint8_t *src = (i & 1) ? c1.next(a, bytes) : c0.next(a, bytes);
+    mbar_arrive_expect_tx(&full_bar[st], (uint32_t)bytes);
+    bulk_g2s(ring + (size_t)st * slot_bytes, src, (uint32_t)bytes, &full_bar[st]);
   }
   return true;
 }
 
-// Consumer side: the 16 consumer warps process units [u0, u0 + n) read from
-// ring positions it, it + 1, ...: two groups of eight warps take alternate
-// units (two units in flight), warp w owns warp tile w % 8, and row sums are
-// flushed with red.global.add whenever a warp's CTA tile or segment changes.
+// Adds a warp's row sums to the output rows of CTA tile `ctile`.
+__device__ __forceinline__ void flush_rows(Acc2 &acc, const SegView &S, int ctile, int wti, int lane) {
+  float r0 = acc.r0, r1 = acc.r1;
+  r0 += __shfl_xor_sync(0xffffffffu, r0, 1);
+  r0 += __shfl_xor_sync(0xffffffffu, r0, 2);
+  r1 += __shfl_xor_sync(0xffffffffu, r1, 1);
+  r1 += __shfl_xor_sync(0xffffffffu, r1, 2);
+  if ((lane & 3) == 0) {
+    const int row = ctile * kCtaRows + wti * 16 + (lane >> 2);
+    if (row < S.rows) red_add_f32(S.y + row, r0);
+    if (row + 8 < S.rows) red_add_f32(S.y + row + 8, r1);
+  }
+  acc.r0 = acc.r1 = 0.f;
+}
+
+// `cnt` consecutive units of one segment (type TYPE) for one warp: the k-th
+// unit of the half's run sits at ring position it + 2 (k0 + k) + half.
+template <int TYPE>
+__device__ __forceinline__ bool consume_run(const SegView &S, int k0, int cnt, int half, int hbeg,
+                                            uint32_t it, const uint8_t *ring, int NS,
+                                            int slot_bytes, uint64_t *full_bar,
+                                            uint64_t *empty_bar, const uint8_t *xw,
+                                            const float *s16, bool full, int kc, int kunits,
+                                            const uint32_t (&mk)[8], int &ctile, int &kunit,
+                                            Acc2 &acc, int *err) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, wti = warp & 7;
+  const int xstep = (kc / 32) * 4, sstep = kc / 16;
+  for (int k = 0; k < cnt; ++k) {
+    const uint32_t rp = it + 2u * (uint32_t)(k0 + k) + (uint32_t)half;
+    const int st = (int)(rp % (uint32_t)NS);
+    const uint32_t ph = (rp / (uint32_t)NS) & 1u;
+    const int slot = full ? kunit : hbeg + k0 + k;
+    if (!mbar_wait(&full_bar[st], ph, err, 102)) return false;
+    const uint8_t *wt = ring + (size_t)st * slot_bytes + (size_t)wti * S.wt_bytes;
+    const uint4 *xf = reinterpret_cast<const uint4 *>(xw) + (size_t)slot * xstep + (lane & 3);
+    const float *sl = s16 + (size_t)slot * sstep;
+    if (TYPE == IFX_TYPE_Q4_K) unit_q4k(wt, xf, sl, mk, lane, acc);
+    else if (TYPE == IFX_TYPE_Q6_K) unit_q6k(wt, xf, sl, mk, lane, acc);
+    else if (TYPE == IFX_TYPE_Q4_0) unit_q4_0(wt, kc, S.wt_qbytes, xf, sl, lane, acc);
+    else unit_q8_0(wt, kc, S.wt_qbytes, xf, sl, lane, acc);
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty_bar[st]);
+    if (++kunit == kunits) {  // end of a CTA tile: its rows are complete here
+      flush_rows(acc, S, ctile, wti, lane);
+      kunit = 0;
+      ++ctile;
+    }
+  }
+  return true;
+}
+
+// Consumer side: the 16 consumer warps process the CTA's units [u0, u0 + n)
+// in two halves of eight warps (see half_begin); warp w owns warp tile w % 8
+// of every unit of its half's run, and row sums are flushed with
+// red.global.add at each CTA-tile end and at the end of each segment run.
 // x fragments / 16-column sums must already be staged in xw / s16.
 __device__ __forceinline__ bool gemv_consume(const GemvArgs &a, int u0, int n, uint32_t it,
                                              const uint8_t *ring, int NS, int slot_bytes,
@@ -391,89 +507,49 @@ __device__ __forceinline__ bool gemv_consume(const GemvArgs &a, int u0, int n, u
                                              const uint8_t *xw, const float *s16, bool full,
                                              int *err) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int g = lane >> 2, c = lane & 3;
-  const int half = warp >> 3, wti = warp & 7;
+  const int g = lane >> 2, half = warp >> 3, wti = warp & 7;
+  const int hbeg = half_begin(n, half), hcnt = half_count(n, half);
+  if (hcnt <= 0) return true;
   uint32_t mk[8];
 #pragma unroll
   for (int i = 0; i < 8; ++i) mk[i] = (g == i) ? 0x3C003C00u : 0u;  // f16x2 (1, 1) or (0, 0)
-
+  const int kunits = a.kunits, kc = a.kc;
+  int sg = find_seg(a, u0 + hbeg);
+  SegView S = load_seg(a, sg);
+  const int local = u0 + hbeg - S.begin;
+  int ctile = local / kunits, kunit = local % kunits;
+  int seg_left = S.units - local;
   Acc2 acc{0.f, 0.f};
-  // position of this warp's current unit: segment, index in segment, CTA
-  // tile, column unit (advanced incrementally: no divisions in the loop)
-  int sg = 0, local = 0, ctile = 0, kunit = 0;
-  if (half < n) {
-    const int u = u0 + half;
-    sg = find_seg(a, u);
-    local = u - a.seg[sg].unit_begin;
-    ctile = local / a.kunits;
-    kunit = local % a.kunits;
-  }
-  const int kunits = a.kunits;
-  int s_type = a.seg[sg].type, s_wtb = a.seg[sg].wt_bytes, s_wtq = a.seg[sg].wt_qbytes;
-  int s_rows = a.seg[sg].rows, s_units = a.seg[sg].units;
-  float *s_y = a.seg[sg].y;
-  for (int i = half; i < n; i += 2) {
-    const uint32_t rp = it + (uint32_t)i;
-    const int st = (int)(rp % (uint32_t)NS);
-    const uint32_t ph = (rp / (uint32_t)NS) & 1u;
-    const int slot = full ? kunit : i;
-    if (!mbar_wait(&full_bar[st], ph, err, 102)) return false;
-    const uint8_t *wt = ring + (size_t)st * slot_bytes + (size_t)wti * s_wtb;
-    const uint4 *xf = reinterpret_cast<const uint4 *>(xw) + (size_t)slot * (a.kc / 32) * 4 + c;
-    const float *sl = s16 + (size_t)slot * (a.kc / 16);
-    switch (s_type) {
-      case IFX_TYPE_Q4_K: unit_q4k(wt, xf, sl, mk, lane, acc); break;
-      case IFX_TYPE_Q6_K: unit_q6k(wt, xf, sl, mk, lane, acc); break;
-      case IFX_TYPE_Q4_0: unit_q4_0(wt, a.kc, s_wtq, xf, sl, lane, acc); break;
-      case IFX_TYPE_Q8_0: unit_q8_0(wt, a.kc, s_wtq, xf, sl, lane, acc); break;
-      default: break;
+  for (int k = 0; k < hcnt;) {
+    const int cnt = min(hcnt - k, seg_left);
+    bool ok;
+    switch (S.type) {
+      case IFX_TYPE_Q4_K:
+        ok = consume_run<IFX_TYPE_Q4_K>(S, k, cnt, half, hbeg, it, ring, NS, slot_bytes, full_bar,
+                                        empty_bar, xw, s16, full, kc, kunits, mk, ctile, kunit, acc, err);
+        break;
+      case IFX_TYPE_Q6_K:
+        ok = consume_run<IFX_TYPE_Q6_K>(S, k, cnt, half, hbeg, it, ring, NS, slot_bytes, full_bar,
+                                        empty_bar, xw, s16, full, kc, kunits, mk, ctile, kunit, acc, err);
+        break;
+      case IFX_TYPE_Q4_0:
+        ok = consume_run<IFX_TYPE_Q4_0>(S, k, cnt, half, hbeg, it, ring, NS, slot_bytes, full_bar,
+                                        empty_bar, xw, s16, full, kc, kunits, mk, ctile, kunit, acc, err);
+        break;
+      default:
+        ok = consume_run<IFX_TYPE_Q8_0>(S, k, cnt, half, hbeg, it, ring, NS, slot_bytes, full_bar,
+                                        empty_bar, xw, s16, full, kc, kunits, mk, ctile, kunit, acc, err);
+        break;
     }
-    __syncwarp();
-    if (lane == 0) mbar_arrive(&empty_bar[st]);
-
-    // advance two units; flush when this warp's CTA tile or segment changes
-    int nsg = sg, nlocal = local + 2, nct = ctile, nku = kunit + 2;
-    while (nku >= kunits) {
-      nku -= kunits;
-      ++nct;
+    if (!ok) return false;
+    if (kunit != 0) flush_rows(acc, S, ctile, wti, lane);  // a partial tile ends the run
+    k += cnt;
+    if (k < hcnt) {  // next segment, from its first unit
+      ++sg;
+      S = load_seg(a, sg);
+      ctile = kunit = 0;
+      seg_left = S.units;
     }
-    bool seg_change = false;
-    while (nsg + 1 < a.nseg && nlocal >= a.seg[nsg].units) {
-      nlocal -= a.seg[nsg].units;
-      ++nsg;
-      seg_change = true;
-    }
-    if (seg_change) {
-      nct = nlocal / kunits;
-      nku = nlocal % kunits;
-    }
-    const bool last = i + 2 >= n;
-    if (last || seg_change || nct != ctile) {
-      float r0 = acc.r0, r1 = acc.r1;
-      r0 += __shfl_xor_sync(0xffffffffu, r0, 1);
-      r0 += __shfl_xor_sync(0xffffffffu, r0, 2);
-      r1 += __shfl_xor_sync(0xffffffffu, r1, 1);
-      r1 += __shfl_xor_sync(0xffffffffu, r1, 2);
-      if (c == 0) {
-        const int row = ctile * kCtaRows + wti * 16 + g;
-        if (row < s_rows) red_add_f32(s_y + row, r0);
-        if (row + 8 < s_rows) red_add_f32(s_y + row + 8, r1);
-      }
-      acc.r0 = acc.r1 = 0.f;
-    }
-    if (seg_change) {
-      s_type = a.seg[nsg].type;
-      s_wtb = a.seg[nsg].wt_bytes;
-      s_wtq = a.seg[nsg].wt_qbytes;
-      s_rows = a.seg[nsg].rows;
-      s_units = a.seg[nsg].units;
-      s_y = a.seg[nsg].y;
-    }
-    (void)s_units;
-    sg = nsg;
-    local = nlocal;
-    ctile = nct;
-    kunit = nku;
   }
   return true;
 }
