@@ -34,11 +34,17 @@ __device__ __forceinline__ unsigned ld_acquire(const unsigned *p) {
 }
 
 // Grid barrier over all CTAs (consumer warps only). Bounded: polling stops
-// after 2^22 polls or as soon as any thread has raised the error flag.
+// after 2^24 polls (well over a second) or as soon as any thread has raised
+// the error flag.
 // Returns false (the same value in every consumer thread of the CTA) when the
 // error flag is set, so the CTA's consumers leave together; the host then
 // reports IFX_ERR_TIMEOUT.
-__device__ bool grid_barrier(unsigned *bar, unsigned target, int *err) {
+//
+// Thread 0 also waits (bounded) for the shared-memory copy of the next phase
+// record (mbarrier `rec`, phase parity `rec_par`) and folds a failed wait
+// into the same verdict, so every consumer thread sees one answer.
+__device__ bool grid_barrier(unsigned *bar, unsigned target, int *err, uint64_t *rec,
+                             uint32_t rec_par) {
   __shared__ int s_err;
   consumer_sync();
   if (threadIdx.x == 0) {
@@ -46,18 +52,26 @@ __device__ bool grid_barrier(unsigned *bar, unsigned target, int *err) {
     atomicAdd(bar, 1u);
     uint32_t spins = 0;
     while (ld_acquire(bar) < target) {
-      if (++spins > (1u << 22)) {
+      if (++spins > (1u << 24)) {
         atomicExch(err, 401);
         break;
       }
       if ((spins & 255u) == 0 && *(volatile int *)err) break;
-      __nanosleep(32);
     }
     __threadfence();
-    s_err = *(volatile int *)err;
+    const bool rec_ok = mbar_wait(rec, rec_par, err, 404);
+    s_err = rec_ok ? *(volatile int *)err : 1;
   }
   consumer_sync();
   return s_err == 0;
+}
+
+// Same verdict for phase 0 (no grid barrier before it).
+__device__ bool first_record(uint64_t *rec, int *err) {
+  __shared__ int s_ok;
+  if (threadIdx.x == 0) s_ok = mbar_wait(rec, 0u, err, 404) ? 1 : 0;
+  consumer_sync();
+  return s_ok != 0;
 }
 
 __device__ __forceinline__ void rope_pair_m(float &a, float &b, int i, int rope_dim, float base,
@@ -292,17 +306,35 @@ __global__ void __launch_bounds__(kGemvThreads, 1) decode_mega_kernel(const __gr
   extern __shared__ __align__(128) uint8_t smem[];
   uint64_t *full_bar = reinterpret_cast<uint64_t *>(smem);
   uint64_t *empty_bar = full_bar + kGemvMaxStages;
-  uint8_t *ring = smem + kGemvBarBytes;
-  uint8_t *scr = ring + (size_t)A.NS * A.slot_bytes;
+  uint64_t *xbar = reinterpret_cast<uint64_t *>(smem + kGemvBarBytes);  // [0] phase records, [1] ranges
+  MegaPhase *s_ph = reinterpret_cast<MegaPhase *>(smem + A.off_ph);     // two records
+  const int2 *s_rg = reinterpret_cast<const int2 *>(smem + A.off_rg);   // this CTA's ranges
+  uint8_t *ring = smem + A.off_ring;
+  uint8_t *scr = smem + A.off_scr;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
     for (int s = 0; s < A.NS; ++s) {
       mbar_init(&full_bar[s], 1);
       mbar_init(&empty_bar[s], 8);
     }
+    mbar_init(&xbar[0], 1);
+    mbar_init(&xbar[1], 1);
     fence_mbar_init();
   }
   __syncthreads();
+  if (threadIdx.x == 0) {  // this CTA's range table and the first phase record
+    const uint32_t rg_bytes = (uint32_t)(A.nph_pad * sizeof(int2));
+    mbar_arrive_expect_tx(&xbar[1], rg_bytes);
+    bulk_g2s(smem + A.off_rg, A.rg + (size_t)blockIdx.x * A.nph_pad, rg_bytes, &xbar[1]);
+    mbar_arrive_expect_tx(&xbar[0], (uint32_t)sizeof(MegaPhase));
+    bulk_g2s(&s_ph[0], &A.ph[0], (uint32_t)sizeof(MegaPhase), &xbar[0]);
+  }
+  // every thread waits for the range table; the CTA then agrees on the outcome
+  const bool have_rg = __syncthreads_and(mbar_wait(&xbar[1], 0u, A.err, 403)) != 0;
+  if (!have_rg) {
+    if (threadIdx.x == 0) mbar_wait(&xbar[0], 0u, nullptr, 0);  // first record copy lands
+    return;
+  }
 
   if (warp == kConsumerWarps) {
     // producer: every GEMV phase's units for this CTA, back to back
@@ -311,7 +343,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) decode_mega_kernel(const __gr
       for (int p = 0; p < A.nph; ++p) {
         const MegaPhase &P = A.ph[p];
         if (P.kind != PH_GEMV) continue;
-        const int2 rg = P.g.sched[blockIdx.x];
+        const int2 rg = s_rg[p];
         const int n = rg.y - rg.x;
         if (!gemv_produce(P.g, rg.x, n, it, ring, A.NS, A.slot_bytes, full_bar, empty_bar, A.err))
           return;  // gemv_produce drained its copies
@@ -323,9 +355,21 @@ __global__ void __launch_bounds__(kGemvThreads, 1) decode_mega_kernel(const __gr
   }
 
   uint32_t it = 0;
+  int issued = 1, landed = 0;  // phase-record copies (thread 0's view)
   for (int p = 0; p < A.nph; ++p) {
-    const MegaPhase &P = A.ph[p];
-    if (p > 0 && !grid_barrier(A.bar, (unsigned)p * gridDim.x, A.err)) return;
+    // the record of phase p was requested during phase p - 1 into the buffer
+    // of phase p - 2, which every consumer finished before the last barrier
+    const bool ok = p > 0 ? grid_barrier(A.bar, (unsigned)p * gridDim.x, A.err, &xbar[0],
+                                         (uint32_t)p & 1u)
+                          : first_record(&xbar[0], A.err);
+    if (!ok) break;  // the same answer in every consumer thread
+    landed = p + 1;
+    if (threadIdx.x == 0 && p + 1 < A.nph) {
+      mbar_arrive_expect_tx(&xbar[0], (uint32_t)sizeof(MegaPhase));
+      bulk_g2s(&s_ph[(p + 1) & 1], &A.ph[p + 1], (uint32_t)sizeof(MegaPhase), &xbar[0]);
+      issued = p + 2;
+    }
+    const MegaPhase &P = s_ph[p & 1];
     if (P.zero_ptr)
       for (int i = blockIdx.x * kConsumerThreads + threadIdx.x; i < P.zero_n;
            i += gridDim.x * kConsumerThreads)
@@ -335,7 +379,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) decode_mega_kernel(const __gr
         phase_embed(A);
         break;
       case PH_GEMV: {
-        const int2 rg = P.g.sched[blockIdx.x];
+        const int2 rg = s_rg[p];
         const int n = rg.y - rg.x;
         if (n > 0) {
           const bool full = n >= P.g.kunits;
@@ -367,6 +411,9 @@ __global__ void __launch_bounds__(kGemvThreads, 1) decode_mega_kernel(const __gr
         break;
     }
   }
+  // leave no record copy in flight: after an early exit the last requested
+  // record (copy number issued - 1) may still be landing
+  if (threadIdx.x == 0 && issued > landed) mbar_wait(&xbar[0], (uint32_t)(issued - 1) & 1u, nullptr, 0);
 }
 
 }  // namespace
@@ -384,6 +431,7 @@ size_t mega_attn_scratch(int grp, int hd, int max_seq, int nsa) {
 
 ifx_status mega_finalize(MegaPlan *plan, const std::vector<MegaPhase> &phases, int num_sms) {
   MegaArgs &A = plan->args;
+  static_assert(sizeof(MegaPhase) % 16 == 0, "phase records move by bulk copy");
   if (A.H / A.G > kMaxGrp || A.hd % 8 || A.hd > 256 || A.nsa > kMaxSplitsMega)
     return fail(IFX_ERR_UNSUPPORTED, "persistent decode: unsupported head geometry");
   size_t slot = 0, win = 0;
@@ -395,18 +443,39 @@ ifx_status mega_finalize(MegaPlan *plan, const std::vector<MegaPhase> &phases, i
   const size_t scratch = std::max<size_t>(
       {win, mega_attn_scratch(A.H / A.G, A.hd, A.max_seq, A.nsa), (size_t)kMaxSplitsMega * 4});
   constexpr size_t kCap = 220 * 1024;
-  if (kGemvBarBytes + 2 * slot + scratch > kCap)
+  A.nph = (int)phases.size();
+  A.nph_pad = (A.nph + 1) & ~1;
+  // carve-up: stage barriers | 2 extra barriers | 2 phase records | ranges | ring | scratch
+  const size_t off_ph = kGemvBarBytes + 64;
+  const size_t off_rg = off_ph + 2 * sizeof(MegaPhase);
+  const size_t off_ring = (off_rg + (size_t)A.nph_pad * sizeof(int2) + 127) & ~(size_t)127;
+  if (off_ring + 2 * slot + scratch > kCap)
     return fail(IFX_ERR_UNSUPPORTED, "persistent decode: shared memory plan too large");
-  int NS = (int)std::min<size_t>(kGemvMaxStages, (kCap - kGemvBarBytes - scratch) / slot);
+  int NS = (int)std::min<size_t>(kGemvMaxStages, (kCap - off_ring - scratch) / slot);
   A.NS = NS;
   A.slot_bytes = (int)slot;
   A.scratch_bytes = (int)scratch;
-  A.nph = (int)phases.size();
+  A.off_ph = (int)off_ph;
+  A.off_rg = (int)off_rg;
+  A.off_ring = (int)off_ring;
+  A.off_scr = (int)(off_ring + (size_t)NS * slot);
+  // per-CTA unit ranges of every phase (zero-length outside GEMV phases)
+  std::vector<int2> rg((size_t)num_sms * A.nph_pad, make_int2(0, 0));
+  std::vector<int2> sched(num_sms);
+  for (int p = 0; p < A.nph; ++p) {
+    if (phases[p].kind != PH_GEMV) continue;
+    IFX_CUDA(cudaMemcpy(sched.data(), phases[p].g.sched, sizeof(int2) * num_sms,
+                        cudaMemcpyDeviceToHost));
+    for (int b = 0; b < num_sms; ++b) rg[(size_t)b * A.nph_pad + p] = sched[b];
+  }
+  IFX_CUDA(cudaMalloc(&plan->d_rg, sizeof(int2) * rg.size()));
+  IFX_CUDA(cudaMemcpy(plan->d_rg, rg.data(), sizeof(int2) * rg.size(), cudaMemcpyHostToDevice));
+  A.rg = plan->d_rg;
   IFX_CUDA(cudaMalloc(&plan->d_phases, sizeof(MegaPhase) * phases.size()));
   IFX_CUDA(cudaMemcpy(plan->d_phases, phases.data(), sizeof(MegaPhase) * phases.size(),
                       cudaMemcpyHostToDevice));
   A.ph = plan->d_phases;
-  plan->smem = kGemvBarBytes + (size_t)NS * slot + scratch;
+  plan->smem = (size_t)A.off_scr + scratch;
   plan->grid = num_sms;
   IFX_CUDA(cudaFuncSetAttribute(decode_mega_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                 (int)kCap));
@@ -435,7 +504,9 @@ ifx_status mega_launch(const MegaPlan &plan, cudaStream_t st) {
 
 void mega_free(MegaPlan *plan) {
   if (plan->d_phases) cudaFree(plan->d_phases);
+  if (plan->d_rg) cudaFree(plan->d_rg);
   plan->d_phases = nullptr;
+  plan->d_rg = nullptr;
 }
 
 }  // namespace ifx

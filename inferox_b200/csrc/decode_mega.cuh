@@ -11,7 +11,9 @@ struct MegaAttn {
   __half *kc, *vc;  // this layer's caches [G][max_seq][hd]
 };
 
-struct MegaPhase {
+// 16-byte aligned (and so a multiple of 16 in size): the kernel moves
+// records into shared memory with bulk async copies.
+struct __align__(16) MegaPhase {
   int kind;
   GemvArgs g;   // PH_GEMV (sched has one entry per CTA)
   MegaAttn at;  // PH_ATTN
@@ -22,6 +24,10 @@ struct MegaPhase {
 struct MegaArgs {
   const MegaPhase *ph;
   int nph;
+  const int2 *rg;  // [grid][nph_pad]: each CTA's unit range per phase
+  int nph_pad;     // nph rounded up to even (rows are 16-byte multiples)
+  // dynamic shared memory carve-up (byte offsets)
+  int off_ph, off_rg, off_ring, off_scr;
   int NS, slot_bytes, scratch_bytes;
   unsigned *bar;  // grid barrier counter, zero at launch
   int *err;
@@ -45,6 +51,7 @@ struct MegaArgs {
 struct MegaPlan {
   MegaArgs args{};
   MegaPhase *d_phases = nullptr;
+  int2 *d_rg = nullptr;
   size_t smem = 0;
   int grid = 0;
 };

@@ -285,9 +285,31 @@ __device__ __forceinline__ SegView load_seg(const GemvArgs &a, int s) {
 }
 
 // Consumer-side input staging: f(x) as f16 B fragments + 16-column sums.
-// Every global read is a coalesced float4 issued up front (one L2 round trip
-// per pass), so the prologue costs ~1-2 us instead of dozens of serialized
-// round trips.
+// Every global read is a coalesced float4 issued up front. When the staged
+// columns fit in one pass (up to 4 float4 per thread: K <= 8192 for a full
+// CTA range) all loads go out in one round, the RMSNorm sum of squares is
+// taken from those same values (or from one extra set of loads issued in the
+// same round), and the normalised values are formed from registers after a
+// single consumer barrier.
+static __device__ __forceinline__ void emit_x4(float (&y)[4], bool valid, int f, int per_slot,
+                                               int kc, __half *xh, float *s16, int tid) {
+  const __half2 h01 = __floats2half2_rn(y[0], y[1]), h23 = __floats2half2_rn(y[2], y[3]);
+  // the 16-column sum of the f16 values the MMA sees: 4 lanes per group
+  float s = (__low2float(h01) + __high2float(h01)) + (__low2float(h23) + __high2float(h23));
+  s += __shfl_xor_sync(0xffffffffu, s, 1);
+  s += __shfl_xor_sync(0xffffffffu, s, 2);
+  if (valid) {
+    const int j = f / per_slot, o = (f % per_slot) * 4;  // o: column within the slot
+    const int p = o / 32, rr = o % 32, hh = rr / 16, ss = rr % 16;  // ss = 0,4,8,12
+    // element ss at half index ((j*kc/32 + p)*4 + c)*8 + hh*4 + (ss/8)*2 + ss%2
+    const int c0 = (ss % 8) / 2;
+    const size_t ent = ((size_t)(j * (kc / 32) + p) * 4) * 8 + hh * 4 + (ss / 8) * 2;
+    *reinterpret_cast<__half2 *>(xh + ent + (size_t)c0 * 8) = h01;
+    *reinterpret_cast<__half2 *>(xh + ent + (size_t)(c0 + 1) * 8) = h23;
+    if ((tid & 3) == 0) s16[j * (kc / 16) + o / 16] = s;
+  }
+}
+
 static __device__ __noinline__ void stage_x(const GemvArgs &a, int u0, int n, bool full, uint8_t *xw, float *s16) {
   const int tid = threadIdx.x;  // 0..kConsumerThreads-1
   constexpr int T = kConsumerThreads;
@@ -295,25 +317,21 @@ static __device__ __noinline__ void stage_x(const GemvArgs &a, int u0, int n, bo
   const float4 *x4 = reinterpret_cast<const float4 *>(a.x);
   const float4 *w4 = reinterpret_cast<const float4 *>(mode == GEMV_RMSNORM ? a.normw : a.x2);
   const float eps = a.eps;
+  const bool norm = mode == GEMV_RMSNORM;
   int sb[kGemvMaxSegs];  // segment first units (increasing); unused ones never match
 #pragma unroll
   for (int i = 0; i < kGemvMaxSegs; ++i) sb[i] = i < nseg ? a.seg[i].unit_begin : 0x7fffffff;
   const int nslots = full ? kunits : n;
+  const int per_slot = kc / 4;  // float4s per slot
+  const int total = nslots * per_slot;
+  const int K4 = K / 4;
+  __shared__ float red[kConsumerWarps];
+  __half *xh = reinterpret_cast<__half *>(xw);
+  const bool one_pass = total <= 4 * T;
   float inv = 1.0f;
-  if (mode == GEMV_RMSNORM) {
-    __shared__ float red[kConsumerWarps];
+  if (norm && !one_pass) {  // sum of squares first (several staging passes follow)
     float ss = 0.f;
-    const int K4 = K / 4;
-    int f = tid;
-    for (; f + 3 * T < K4; f += 4 * T) {  // four float4 loads in flight per thread
-      const float4 v0 = __ldcg(x4 + f), v1 = __ldcg(x4 + f + T), v2 = __ldcg(x4 + f + 2 * T),
-                   v3 = __ldcg(x4 + f + 3 * T);
-      ss += v0.x * v0.x + v0.y * v0.y + v0.z * v0.z + v0.w * v0.w;
-      ss += v1.x * v1.x + v1.y * v1.y + v1.z * v1.z + v1.w * v1.w;
-      ss += v2.x * v2.x + v2.y * v2.y + v2.z * v2.z + v2.w * v2.w;
-      ss += v3.x * v3.x + v3.y * v3.y + v3.z * v3.z + v3.w * v3.w;
-    }
-    for (; f < K4; f += T) {
+    for (int f = tid; f < K4; f += T) {
       const float4 v = __ldcg(x4 + f);
       ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
     }
@@ -325,9 +343,6 @@ static __device__ __noinline__ void stage_x(const GemvArgs &a, int u0, int n, bo
     for (int i = 0; i < kConsumerWarps; ++i) tot += red[i];
     inv = 1.0f / sqrtf(tot / (float)K + eps);
   }
-  const int per_slot = kc / 4;  // float4s per slot
-  const int total = nslots * per_slot;
-  __half *xh = reinterpret_cast<__half *>(xw);
   for (int base = 0; base < total; base += 4 * T) {
     float4 v[4], w[4];
     int kk[4];
@@ -352,6 +367,28 @@ static __device__ __noinline__ void stage_x(const GemvArgs &a, int u0, int n, bo
         if (mode != GEMV_PLAIN) w[r] = mode == GEMV_SWIGLU ? __ldcg(w4 + kk[r] / 4) : w4[kk[r] / 4];
       }
     }
+    if (norm && one_pass) {
+      // a full range stages every column of x exactly once, so its loads
+      // give the sum of squares; otherwise read x once more in this round
+      float ss = 0.f;
+      if (full) {
+#pragma unroll
+        for (int r = 0; r < 4; ++r)
+          ss += v[r].x * v[r].x + v[r].y * v[r].y + v[r].z * v[r].z + v[r].w * v[r].w;
+      } else {
+        for (int f = tid; f < K4; f += T) {
+          const float4 t = __ldcg(x4 + f);
+          ss += t.x * t.x + t.y * t.y + t.z * t.z + t.w * t.w;
+        }
+      }
+      ss = warp_sum(ss);
+      if ((tid & 31) == 0) red[tid >> 5] = ss;
+      consumer_sync();
+      float tot = 0.f;
+#pragma unroll
+      for (int i = 0; i < kConsumerWarps; ++i) tot += red[i];
+      inv = 1.0f / sqrtf(tot / (float)K + eps);
+    }
 #pragma unroll
     for (int r = 0; r < 4; ++r) {
       const int f = base + r * T + tid;
@@ -364,21 +401,7 @@ static __device__ __noinline__ void stage_x(const GemvArgs &a, int u0, int n, bo
           else if (mode == GEMV_SWIGLU) y[t] = silu_f(y[t]) * z[t];
         }
       }
-      const __half2 h01 = __floats2half2_rn(y[0], y[1]), h23 = __floats2half2_rn(y[2], y[3]);
-      // the 16-column sum of the f16 values the MMA sees: 4 lanes per group
-      float s = (__low2float(h01) + __high2float(h01)) + (__low2float(h23) + __high2float(h23));
-      s += __shfl_xor_sync(0xffffffffu, s, 1);
-      s += __shfl_xor_sync(0xffffffffu, s, 2);
-      if (kk[r] >= 0) {
-        const int j = f / per_slot, o = (f % per_slot) * 4;  // o: column within the slot
-        const int p = o / 32, rr = o % 32, hh = rr / 16, ss = rr % 16;  // ss = 0,4,8,12
-        // element ss at half index ((j*kc/32 + p)*4 + c)*8 + hh*4 + (ss/8)*2 + ss%2
-        const int c0 = (ss % 8) / 2;
-        const size_t ent = ((size_t)(j * (kc / 32) + p) * 4) * 8 + hh * 4 + (ss / 8) * 2;
-        *reinterpret_cast<__half2 *>(xh + ent + (size_t)c0 * 8) = h01;
-        *reinterpret_cast<__half2 *>(xh + ent + (size_t)(c0 + 1) * 8) = h23;
-        if ((tid & 3) == 0) s16[j * (kc / 16) + o / 16] = s;
-      }
+      emit_x4(y, kk[r] >= 0, f, per_slot, kc, xh, s16, tid);
     }
   }
 }
