@@ -48,8 +48,9 @@ __device__ bool grid_barrier(unsigned *bar, unsigned target, int *err, uint64_t 
   __shared__ int s_err;
   consumer_sync();
   if (threadIdx.x == 0) {
-    __threadfence();
-    atomicAdd(bar, 1u);
+    // release: the CTA's writes (ordered before this thread by the barrier
+    // above) become visible to any CTA that acquires the counter
+    asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(bar) : "memory");
     uint32_t spins = 0;
     while (ld_acquire(bar) < target) {
       if (++spins > (1u << 24)) {
@@ -58,7 +59,6 @@ __device__ bool grid_barrier(unsigned *bar, unsigned target, int *err, uint64_t 
       }
       if ((spins & 255u) == 0 && *(volatile int *)err) break;
     }
-    __threadfence();
     const bool rec_ok = mbar_wait(rec, rec_par, err, 404);
     s_err = rec_ok ? *(volatile int *)err : 1;
   }
@@ -267,6 +267,80 @@ __device__ void combine_head(const MegaArgs &A, int hq, float *scr) {
   consumer_sync();
 }
 
+// Staging of the Wo GEMV straight from the attention splits: column
+// hq * hd + d of the attention output is sum_s w_s o_s[d] with
+// w_s = exp(m_s - M) / sum_s' exp(m_s' - M) l_s' over the splits of query
+// head hq (splits with no rows carry l = 0 and get weight 0). Writes the f16
+// fragments and 16-column sums exactly as stage_x does for a plain input.
+__device__ __noinline__ void stage_combine(const MegaArgs &A, const GemvArgs &g, int u0, int n,
+                                           bool full, uint8_t *xw, float *s16, float *wts) {
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  constexpr int T = kConsumerThreads;
+  const int hd = A.hd, grp = A.H / A.G, NS = A.nsa, H = A.H;
+  const int kc = g.kc, kunits = g.kunits;
+  // 1. split weights of every query head (one warp per head)
+  for (int hq = warp; hq < H; hq += kConsumerWarps) {
+    const int h = hq / grp, j = hq % grp;
+    float M = -INFINITY;
+    for (int s = lane; s < NS; s += 32) {
+      const float2 ml = __ldcg(&A.part_ml[(h * NS + s) * grp + j]);
+      if (ml.y > 0.f) M = fmaxf(M, ml.x);
+    }
+    M = warp_max(M);
+    float L = 0.f;
+    for (int s = lane; s < NS; s += 32) {
+      const float2 ml = __ldcg(&A.part_ml[(h * NS + s) * grp + j]);
+      const float w = ml.y > 0.f ? expf(ml.x - M) : 0.f;
+      wts[hq * NS + s] = w;
+      L = fmaf(ml.y, w, L);
+    }
+    L = warp_sum(L);
+    const float invL = 1.0f / L;
+    __syncwarp();
+    for (int s = lane; s < NS; s += 32) wts[hq * NS + s] *= invL;
+  }
+  consumer_sync();
+  // 2. combined columns of the staged slots, four at a time (hd % 4 == 0)
+  const int nslots = full ? kunits : n;
+  const int per_slot = kc / 4, total = nslots * per_slot;
+  const int nseg = g.nseg;
+  int sb[kGemvMaxSegs];
+#pragma unroll
+  for (int i = 0; i < kGemvMaxSegs; ++i) sb[i] = i < nseg ? g.seg[i].unit_begin : 0x7fffffff;
+  __half *xh = reinterpret_cast<__half *>(xw);
+  for (int base = 0; base < total; base += T) {
+    const int f = base + tid;
+    float y[4] = {0.f, 0.f, 0.f, 0.f};
+    const bool valid = f < total;
+    if (valid) {
+      const int jj = f / per_slot, o = (f % per_slot) * 4;
+      int kunit = jj;
+      if (!full) {
+        const int u = u0 + jj;
+        int b = sb[0];
+#pragma unroll
+        for (int i = 1; i < kGemvMaxSegs; ++i) b = u >= sb[i] ? sb[i] : b;
+        kunit = (u - b) % kunits;
+      }
+      const int col = kunit * kc + o;
+      const int hq = col / hd, d = col % hd;
+      const int h = hq / grp, j = hq % grp;
+      const float *w = wts + hq * NS;
+      const float4 *po = reinterpret_cast<const float4 *>(A.part_o + ((size_t)h * NS * grp + j) * hd + d);
+      const size_t sstride = (size_t)grp * hd / 4;  // float4 stride between splits
+      for (int s = 0; s < NS; ++s) {
+        const float4 v = __ldcg(po + s * sstride);
+        const float ws = w[s];
+        y[0] = fmaf(ws, v.x, y[0]);
+        y[1] = fmaf(ws, v.y, y[1]);
+        y[2] = fmaf(ws, v.z, y[2]);
+        y[3] = fmaf(ws, v.w, y[3]);
+      }
+    }
+    emit_x4(y, valid, f, per_slot, kc, xh, s16, tid);
+  }
+}
+
 __device__ void phase_argmax(const MegaArgs &A, float *scr) {
   const int tid = threadIdx.x;
   unsigned long long best = 0;
@@ -384,7 +458,10 @@ __global__ void __launch_bounds__(kGemvThreads, 1) decode_mega_kernel(const __gr
         if (n > 0) {
           const bool full = n >= P.g.kunits;
           float *s16 = reinterpret_cast<float *>(scr + (size_t)P.g.win_units * P.g.kc * 2);
-          stage_x(P.g, rg.x, n, full, scr, s16);
+          if (P.combine)
+            stage_combine(A, P.g, rg.x, n, full, scr, s16, s16 + (size_t)P.g.win_units * (P.g.kc / 16));
+          else
+            stage_x(P.g, rg.x, n, full, scr, s16);
           consumer_sync();
           // on a failed wait the warp carries on to the next grid barrier,
           // which sees the error flag and ends the CTA's consumers together
@@ -438,7 +515,9 @@ ifx_status mega_finalize(MegaPlan *plan, const std::vector<MegaPhase> &phases, i
   for (const MegaPhase &p : phases)
     if (p.kind == PH_GEMV) {
       slot = std::max<size_t>(slot, (size_t)p.g.slot_bytes);
-      win = std::max<size_t>(win, (size_t)p.g.win_units * (p.g.kc * 2 + p.g.kc / 16 * 4));
+      size_t w = (size_t)p.g.win_units * (p.g.kc * 2 + p.g.kc / 16 * 4);
+      if (p.combine) w += (size_t)A.H * A.nsa * 4;  // split weights of every head
+      win = std::max<size_t>(win, w);
     }
   const size_t scratch = std::max<size_t>(
       {win, mega_attn_scratch(A.H / A.G, A.hd, A.max_seq, A.nsa), (size_t)kMaxSplitsMega * 4});

@@ -19,6 +19,8 @@ struct __align__(16) MegaPhase {
   MegaAttn at;  // PH_ATTN
   float *zero_ptr;  // buffer this phase zeroes (a later phase accumulates into it)
   int zero_n;
+  int combine;      // PH_GEMV over the attention output: stage it by combining the
+                    // attention splits on the fly (no separate combine phase)
 };
 
 struct MegaArgs {

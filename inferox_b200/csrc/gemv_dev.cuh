@@ -452,10 +452,11 @@ __device__ __forceinline__ bool gemv_produce(const GemvArgs &a, int u0, int n, u
   UnitCursor c0, c1;  // two named cursors: an indexed pair would live in local memory
   c0.init(a, u0);
   if (n > 1) c1.init(a, u0 + half_begin(n, 1));
+  // slot and phase parity of ring position it + i, advanced without divisions
+  int st = (int)(it % (uint32_t)NS);
+  uint32_t ph = (it / (uint32_t)NS) & 1u;
   for (int i = 0; i < n; ++i) {
     const uint32_t rp = it + (uint32_t)i;
-    const int st = (int)(rp % (uint32_t)NS);
-    const uint32_t ph = (rp / (uint32_t)NS) & 1u;
     if (rp >= (uint32_t)NS && !mbar_wait(&empty_bar[st], ph ^ 1u, err, 101)) {
       ring_drain(full_bar, NS, rp);
       return false;
@@ -464,6 +465,10 @@ __device__ __forceinline__ bool gemv_produce(const GemvArgs &a, int u0, int n, u
     const uint8_t *src = (i & 1) ? c1.next(a, bytes) : c0.next(a, bytes);
     mbar_arrive_expect_tx(&full_bar[st], (uint32_t)bytes);
     bulk_g2s(ring + (size_t)st * slot_bytes, src, (uint32_t)bytes, &full_bar[st]);
+    if (++st == NS) {
+      st = 0;
+      ph ^= 1u;
+    }
   }
   return true;
 }
@@ -495,10 +500,12 @@ __device__ __forceinline__ bool consume_run(const SegView &S, int k0, int cnt, i
                                             Acc2 &acc, int *err) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, wti = warp & 7;
   const int xstep = (kc / 32) * 4, sstep = kc / 16;
+  // slot and phase parity of this warp's ring positions (step 2, NS >= 2),
+  // advanced without divisions
+  const uint32_t rp0 = it + 2u * (uint32_t)k0 + (uint32_t)half;
+  int st = (int)(rp0 % (uint32_t)NS);
+  uint32_t ph = (rp0 / (uint32_t)NS) & 1u;
   for (int k = 0; k < cnt; ++k) {
-    const uint32_t rp = it + 2u * (uint32_t)(k0 + k) + (uint32_t)half;
-    const int st = (int)(rp % (uint32_t)NS);
-    const uint32_t ph = (rp / (uint32_t)NS) & 1u;
     const int slot = full ? kunit : hbeg + k0 + k;
     if (!mbar_wait(&full_bar[st], ph, err, 102)) return false;
     const uint8_t *wt = ring + (size_t)st * slot_bytes + (size_t)wti * S.wt_bytes;
@@ -510,6 +517,11 @@ __device__ __forceinline__ bool consume_run(const SegView &S, int k0, int cnt, i
     else unit_q8_0(wt, kc, S.wt_qbytes, xf, sl, lane, acc);
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty_bar[st]);
+    st += 2;
+    if (st >= NS) {
+      st -= NS;
+      ph ^= 1u;
+    }
     if (++kunit == kunits) {  // end of a CTA tile: its rows are complete here
       flush_rows(acc, S, ctile, wti, lane);
       kunit = 0;

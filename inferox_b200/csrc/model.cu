@@ -452,8 +452,8 @@ ifx_status Model::build_mega(KvCache &kv) {
     at.zero_ptr = gu;  // consumed by the previous layer's W2, refilled by W13
     at.zero_n = (int)(2 * c.intermediate_size);
     ph.push_back(at);
-    simple(PH_COMBINE, nullptr, 0);
     gemv(p_wo[l], nullptr, 0);
+    ph.back().combine = 1;  // Wo stages its input from the attention splits
     gemv(p_w13[l], qkv, qkv_n);  // qkv was consumed by ATTN; the next QKV refills it
     gemv(p_w2[l], nullptr, 0);
   }
