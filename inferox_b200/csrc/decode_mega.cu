@@ -87,73 +87,101 @@ __device__ __forceinline__ void rope_pair_m(float &a, float &b, int i, int rope_
 }
 
 // ---------------------------------------------------------------- phases --
-__device__ void phase_embed(const MegaArgs &A) {
+__device__ __noinline__ void phase_embed(const MegaArgs &A) {
   const int tid = threadIdx.x;
   const uint64_t base = (uint64_t)(*A.next_token) * (uint64_t)A.D;
   for (int i = blockIdx.x * kConsumerThreads + tid; i < A.D; i += gridDim.x * kConsumerThreads)
     A.x[i] = dequant_elem(A.emb_type, A.emb, base + i);
 }
 
-// One (kv head, split) item of split-K decode attention: K/V rows of the
-// split into shared memory, scores (four threads per (head, row)), softmax
-// statistics, P.V, partial (max, sum, output) to global.
-__device__ void attn_item(const MegaArgs &A, const MegaAttn &at, int h, int s, uint8_t *scr) {
+// Split-K decode attention. Item (h, s) covers cache rows [t0, t1) of kv
+// head h: chunk = ceil((pos + 1) / nsa), t0 = s * chunk. Rows below pos are
+// already in the cache; row pos (this token) is appended from qkv.
+struct AttnSpan {
+  int t0, t1, nk, nold;
+};
+
+__device__ __forceinline__ AttnSpan attn_span(int pos, int nsa, int s) {
+  const int len = pos + 1;
+  const int chunk = (len + nsa - 1) / nsa;
+  AttnSpan r;
+  r.t0 = s * chunk;
+  r.t1 = min(len, r.t0 + chunk);
+  r.nk = max(0, r.t1 - r.t0);
+  r.nold = max(0, min(r.t1, pos) - r.t0);
+  return r;
+}
+
+// Thread 0: bulk-copy the cached K and V rows [t0, t0 + nold) of kv head h
+// (layer `layer`) into the attention buffer, completing on `kvbar`. With no
+// rows the barrier is completed by a plain arrive.
+__device__ __noinline__ void attn_fetch(const MegaArgs &A, int layer, int h, int s, int pos, uint8_t *abuf,
+                           uint64_t *kvbar) {
+  const AttnSpan sp = attn_span(pos, A.nsa, s);
+  const int hd = A.hd;
+  const int cap = (A.max_seq + A.nsa - 1) / A.nsa + 1;
+  const uint32_t bytes = (uint32_t)sp.nold * (uint32_t)hd * 2u;
+  if (bytes == 0) {
+    mbar_arrive(kvbar);
+    return;
+  }
+  const size_t row0 = (size_t)layer * A.kv_layer_elems + ((size_t)h * A.max_seq + sp.t0) * hd;
+  mbar_arrive_expect_tx(kvbar, 2u * bytes);
+  bulk_g2s(abuf, A.kc0 + row0, bytes, kvbar);
+  bulk_g2s(abuf + (size_t)cap * hd * 2, A.vc0 + row0, bytes, kvbar);
+}
+
+// One (kv head, split) item: scores of the grp query heads against the
+// item's rows (cached rows from the attention buffer, this token's row from
+// qkv), softmax statistics, P.V; partial (max, sum, output) to global.
+// The cached rows must have landed (kvbar waited by the caller).
+__device__ __noinline__ void attn_item(const MegaArgs &A, const MegaAttn &at, int h, int s, int pos,
+                          uint8_t *abuf) {
   const int tid = threadIdx.x;
   const int hd = A.hd, grp = A.H / A.G, NS = A.nsa;
-  const int pos = *A.pos;
-  const int len = pos + 1;
-  const int chunk = (len + NS - 1) / NS;
-  const int t0 = s * chunk, t1 = min(len, t0 + chunk);
-  const int nk = max(0, t1 - t0);
-  const int nold = max(0, min(t1, pos) - t0);
+  const AttnSpan sp = attn_span(pos, NS, s);
+  const int t0 = sp.t0, nk = sp.nk;
   const int cap = (A.max_seq + NS - 1) / NS + 1;
   const int n16 = hd / 8;  // 16-byte chunks per row
-  const int swz = (n16 & 7) ? 0 : 7;  // rows of 8+ chunks: chunk c of row t at c ^ (t & 7)
-  uint4 *Ks = reinterpret_cast<uint4 *>(scr);            // [cap][n16]
-  uint4 *Vs = Ks + (size_t)cap * n16;                     // [cap][n16]
-  float *qs = reinterpret_cast<float *>(Vs + (size_t)cap * n16);  // [grp][hd]
-  float *sc = qs + grp * hd;                              // [grp][cap]
-  float *stat = sc + grp * cap;                           // [grp][2]
-  const uint4 *kg = reinterpret_cast<const uint4 *>(at.kc + ((size_t)h * A.max_seq + t0) * hd);
-  const uint4 *vg = reinterpret_cast<const uint4 *>(at.vc + ((size_t)h * A.max_seq + t0) * hd);
-  for (int e = tid; e < nold * n16; e += kConsumerThreads) {
-    const int t = e / n16, c = e % n16;
-    const uint4 kv = kg[e], vv = vg[e];
-    Ks[t * n16 + (c ^ (t & swz))] = kv;
-    Vs[e] = vv;
-  }
-  const float *q = A.qkv + (size_t)h * grp * hd;
+  const uint4 *Ks = reinterpret_cast<const uint4 *>(abuf);             // [cap][n16]
+  uint4 *Vs4 = reinterpret_cast<uint4 *>(abuf + (size_t)cap * hd * 2);  // [cap][n16]
+  float *qs = reinterpret_cast<float *>(abuf + (size_t)cap * hd * 4);    // [grp][hd]
+  float *sc = qs + grp * hd;                                              // [grp][cap]
+  float *stat = sc + grp * cap;                                           // [grp][2]
+  // RoPE at position 0 is the identity (the reference's decode, forward.rs:371-372)
   const int rpos = A.rope_compat ? 0 : pos;
+  const float *q = A.qkv + (size_t)h * grp * hd;
   for (int e = tid; e < grp * hd / 2; e += kConsumerThreads) {
     const int j = e / (hd / 2), i = 2 * (e % (hd / 2));
     float x0 = __ldcg(q + j * hd + i), x1 = __ldcg(q + j * hd + i + 1);
-    if (i < A.rope_dim) rope_pair_m(x0, x1, i, A.rope_dim, A.rope_base, rpos);
+    if (rpos != 0 && i < A.rope_dim) rope_pair_m(x0, x1, i, A.rope_dim, A.rope_base, rpos);
     qs[j * hd + i] = x0;
     qs[j * hd + i + 1] = x1;
   }
-  if (t0 <= pos && pos < t1) {  // append this token's K/V (forward.rs:375-378)
+  if (t0 <= pos && pos < sp.t1) {  // append this token's K/V (forward.rs:375-378)
     const float *kn = A.qkv + (size_t)A.H * hd + (size_t)h * hd;
     const float *vn = A.qkv + (size_t)(A.H + A.G) * hd + (size_t)h * hd;
     const int r = pos - t0;
     __half *kcp = at.kc + ((size_t)h * A.max_seq + pos) * hd;
     __half *vcp = at.vc + ((size_t)h * A.max_seq + pos) * hd;
-    __half *Kh = reinterpret_cast<__half *>(Ks + (size_t)r * n16);
-    __half *Vh = reinterpret_cast<__half *>(Vs + (size_t)r * n16);
+    __half *Kh = reinterpret_cast<__half *>(abuf) + (size_t)r * hd;
+    __half *Vh = reinterpret_cast<__half *>(Vs4) + (size_t)r * hd;
     for (int e = tid; e < hd / 2; e += kConsumerThreads) {
       const int i = 2 * e;
       float x0 = __ldcg(kn + i), x1 = __ldcg(kn + i + 1);
-      if (i < A.rope_dim) rope_pair_m(x0, x1, i, A.rope_dim, A.rope_base, rpos);
-      const __half2 kh = __floats2half2_rn(x0, x1), vh = __floats2half2_rn(__ldcg(vn + i), __ldcg(vn + i + 1));
+      if (rpos != 0 && i < A.rope_dim) rope_pair_m(x0, x1, i, A.rope_dim, A.rope_base, rpos);
+      const __half2 kh = __floats2half2_rn(x0, x1);
+      const __half2 vh = __floats2half2_rn(__ldcg(vn + i), __ldcg(vn + i + 1));
       *reinterpret_cast<__half2 *>(kcp + i) = kh;
       *reinterpret_cast<__half2 *>(vcp + i) = vh;
-      const int c = i / 8, o = i % 8;
-      *reinterpret_cast<__half2 *>(Kh + ((c ^ (r & swz)) * 8 + o)) = kh;
+      *reinterpret_cast<__half2 *>(Kh + i) = kh;
       *reinterpret_cast<__half2 *>(Vh + i) = vh;
     }
   }
   consumer_sync();
-  // scores: four adjacent threads share one (head j, row t), each a quarter
-  // of the head dimension, combined with two shuffles
+  // scores: four adjacent threads share one (head j, row t); thread qtr
+  // takes chunks qtr, qtr + 4, ... of the row, rotated by t & 7 so the eight
+  // rows a warp reads at once fall on different banks
   const float isq = 1.0f / sqrtf((float)hd);
   for (int base = 0; base < grp * nk * 4; base += kConsumerThreads) {
     const int e = base + tid;
@@ -161,19 +189,19 @@ __device__ void attn_item(const MegaArgs &A, const MegaAttn &at, int h, int s, u
     float acc = 0.f;
     int j = 0, t = 0;
     if (ok) {
-      const int qtr = e & 3;
-      const int jt = e >> 2;
+      const int qtr = e & 3, jt = e >> 2;
       j = jt / nk;
-      t = jt % nk;
+      t = jt - j * nk;
       const float4 *q4 = reinterpret_cast<const float4 *>(qs + j * hd);
-      for (int c = qtr; c < n16; c += 4) {
-        const uint4 kv = Ks[t * n16 + (c ^ (t & swz))];
+      int c = qtr + (t & 7);  // any rotation keeps each quarter's chunk set a partition
+      for (int cc = qtr; cc < n16; cc += 4) {
+        while (c >= n16) c -= n16;
+        const uint4 kv = Ks[t * n16 + c];
         const float4 qa = q4[2 * c], qb = q4[2 * c + 1];
-        const uint32_t kw[4] = {kv.x, kv.y, kv.z, kv.w};
-        const float2 k0 = __half22float2(*reinterpret_cast<const __half2 *>(&kw[0]));
-        const float2 k1 = __half22float2(*reinterpret_cast<const __half2 *>(&kw[1]));
-        const float2 k2 = __half22float2(*reinterpret_cast<const __half2 *>(&kw[2]));
-        const float2 k3 = __half22float2(*reinterpret_cast<const __half2 *>(&kw[3]));
+        const float2 k0 = __half22float2(*reinterpret_cast<const __half2 *>(&kv.x));
+        const float2 k1 = __half22float2(*reinterpret_cast<const __half2 *>(&kv.y));
+        const float2 k2 = __half22float2(*reinterpret_cast<const __half2 *>(&kv.z));
+        const float2 k3 = __half22float2(*reinterpret_cast<const __half2 *>(&kv.w));
         acc = fmaf(qa.x, k0.x, acc);
         acc = fmaf(qa.y, k0.y, acc);
         acc = fmaf(qa.z, k1.x, acc);
@@ -182,6 +210,7 @@ __device__ void attn_item(const MegaArgs &A, const MegaAttn &at, int h, int s, u
         acc = fmaf(qb.y, k2.y, acc);
         acc = fmaf(qb.z, k3.x, acc);
         acc = fmaf(qb.w, k3.y, acc);
+        c += 4;
       }
     }
     acc += __shfl_xor_sync(0xffffffffu, acc, 1);
@@ -209,7 +238,7 @@ __device__ void attn_item(const MegaArgs &A, const MegaAttn &at, int h, int s, u
   }
   consumer_sync();
   float *po = A.part_o + (size_t)(h * NS + s) * grp * hd;
-  const __half *Vh = reinterpret_cast<const __half *>(Vs);
+  const __half *Vh = reinterpret_cast<const __half *>(Vs4);
   for (int e = tid; e < grp * hd; e += kConsumerThreads) {
     const int j = e / hd, d = e % hd;
     float o0 = 0.f, o1 = 0.f, o2 = 0.f, o3 = 0.f;
@@ -227,80 +256,22 @@ __device__ void attn_item(const MegaArgs &A, const MegaAttn &at, int h, int s, u
     const float m = nk > 0 ? stat[2 * tid] : -INFINITY, l = nk > 0 ? stat[2 * tid + 1] : 0.f;
     A.part_ml[(h * NS + s) * grp + tid] = make_float2(m, l);
   }
-  consumer_sync();  // scratch is reused by the next item
-}
-
-// Combine the splits of one query head: attn[hq] = sum_s w_s o_s / L.
-__device__ void combine_head(const MegaArgs &A, int hq, float *scr) {
-  const int tid = threadIdx.x;
-  const int hd = A.hd, grp = A.H / A.G, NS = A.nsa;
-  const int h = hq / grp, j = hq % grp;
-  float *wm = scr;  // [NS]
-  if (tid < 32) {
-    float M = -INFINITY;
-    for (int s = tid; s < NS; s += 32) {
-      const float2 ml = __ldcg(&A.part_ml[(h * NS + s) * grp + j]);
-      if (ml.y > 0.f) M = fmaxf(M, ml.x);
-    }
-    M = warp_max(M);
-    float L = 0.f;
-    for (int s = tid; s < NS; s += 32) {
-      const float2 ml = __ldcg(&A.part_ml[(h * NS + s) * grp + j]);
-      const float w = ml.y > 0.f ? expf(ml.x - M) : 0.f;
-      wm[s] = w;
-      L = fmaf(ml.y, w, L);
-    }
-    L = warp_sum(L);
-    for (int s = tid; s < NS; s += 32) wm[s] = wm[s] / L;
-  }
-  consumer_sync();
-  for (int d = tid; d < hd; d += kConsumerThreads) {
-    float o0 = 0.f, o1 = 0.f;
-    int s = 0;
-    for (; s + 1 < NS; s += 2) {
-      o0 = fmaf(wm[s], __ldcg(&A.part_o[((size_t)(h * NS + s) * grp + j) * hd + d]), o0);
-      o1 = fmaf(wm[s + 1], __ldcg(&A.part_o[((size_t)(h * NS + s + 1) * grp + j) * hd + d]), o1);
-    }
-    if (s < NS) o0 = fmaf(wm[s], __ldcg(&A.part_o[((size_t)(h * NS + s) * grp + j) * hd + d]), o0);
-    A.attn[(size_t)hq * hd + d] = o0 + o1;
-  }
-  consumer_sync();
+  consumer_sync();  // the buffer is reused by the next item
 }
 
 // Staging of the Wo GEMV straight from the attention splits: column
-// hq * hd + d of the attention output is sum_s w_s o_s[d] with
-// w_s = exp(m_s - M) / sum_s' exp(m_s' - M) l_s' over the splits of query
-// head hq (splits with no rows carry l = 0 and get weight 0). Writes the f16
-// fragments and 16-column sums exactly as stage_x does for a plain input.
+// hq * hd + d of the attention output is sum_s w_s o_s[d] / sum_s w_s l_s with
+// w_s = exp(m_s - M) over the splits of query head hq (splits with no rows
+// carry l = 0 and weight 0). Each staged group of four columns is combined
+// in one pass with a running maximum, so all of its loads go out together.
+// Writes the f16 fragments and 16-column sums exactly as stage_x does for a
+// plain input.
 __device__ __noinline__ void stage_combine(const MegaArgs &A, const GemvArgs &g, int u0, int n,
-                                           bool full, uint8_t *xw, float *s16, float *wts) {
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+                                           bool full, uint8_t *xw, float *s16) {
+  const int tid = threadIdx.x;
   constexpr int T = kConsumerThreads;
-  const int hd = A.hd, grp = A.H / A.G, NS = A.nsa, H = A.H;
+  const int hd = A.hd, grp = A.H / A.G, NS = A.nsa;
   const int kc = g.kc, kunits = g.kunits;
-  // 1. split weights of every query head (one warp per head)
-  for (int hq = warp; hq < H; hq += kConsumerWarps) {
-    const int h = hq / grp, j = hq % grp;
-    float M = -INFINITY;
-    for (int s = lane; s < NS; s += 32) {
-      const float2 ml = __ldcg(&A.part_ml[(h * NS + s) * grp + j]);
-      if (ml.y > 0.f) M = fmaxf(M, ml.x);
-    }
-    M = warp_max(M);
-    float L = 0.f;
-    for (int s = lane; s < NS; s += 32) {
-      const float2 ml = __ldcg(&A.part_ml[(h * NS + s) * grp + j]);
-      const float w = ml.y > 0.f ? expf(ml.x - M) : 0.f;
-      wts[hq * NS + s] = w;
-      L = fmaf(ml.y, w, L);
-    }
-    L = warp_sum(L);
-    const float invL = 1.0f / L;
-    __syncwarp();
-    for (int s = lane; s < NS; s += 32) wts[hq * NS + s] *= invL;
-  }
-  consumer_sync();
-  // 2. combined columns of the staged slots, four at a time (hd % 4 == 0)
   const int nslots = full ? kunits : n;
   const int per_slot = kc / 4, total = nslots * per_slot;
   const int nseg = g.nseg;
@@ -325,23 +296,35 @@ __device__ __noinline__ void stage_combine(const MegaArgs &A, const GemvArgs &g,
       const int col = kunit * kc + o;
       const int hq = col / hd, d = col % hd;
       const int h = hq / grp, j = hq % grp;
-      const float *w = wts + hq * NS;
-      const float4 *po = reinterpret_cast<const float4 *>(A.part_o + ((size_t)h * NS * grp + j) * hd + d);
+      const float2 *ml = A.part_ml + (size_t)h * NS * grp + j;  // split stride grp
+      const float4 *po =
+          reinterpret_cast<const float4 *>(A.part_o + ((size_t)h * NS * grp + j) * hd + d);
       const size_t sstride = (size_t)grp * hd / 4;  // float4 stride between splits
+      float M = -INFINITY, L = 0.f;
+#pragma unroll 6
       for (int s = 0; s < NS; ++s) {
+        const float2 v2 = __ldcg(ml + (size_t)s * grp);
         const float4 v = __ldcg(po + s * sstride);
-        const float ws = w[s];
-        y[0] = fmaf(ws, v.x, y[0]);
-        y[1] = fmaf(ws, v.y, y[1]);
-        y[2] = fmaf(ws, v.z, y[2]);
-        y[3] = fmaf(ws, v.w, y[3]);
+        if (v2.y > 0.f) {
+          const float Mn = fmaxf(M, v2.x);
+          const float r = expf(M - Mn), w = expf(v2.x - Mn);  // exp(-inf) = 0 on the first split
+          L = fmaf(L, r, w * v2.y);
+          y[0] = fmaf(y[0], r, w * v.x);
+          y[1] = fmaf(y[1], r, w * v.y);
+          y[2] = fmaf(y[2], r, w * v.z);
+          y[3] = fmaf(y[3], r, w * v.w);
+          M = Mn;
+        }
       }
+      const float invL = 1.0f / L;
+#pragma unroll
+      for (int t = 0; t < 4; ++t) y[t] *= invL;
     }
     emit_x4(y, valid, f, per_slot, kc, xh, s16, tid);
   }
 }
 
-__device__ void phase_argmax(const MegaArgs &A, float *scr) {
+__device__ __noinline__ void phase_argmax(const MegaArgs &A, float *scr) {
   const int tid = threadIdx.x;
   unsigned long long best = 0;
   for (int i = blockIdx.x * kConsumerThreads + tid; i < A.V; i += gridDim.x * kConsumerThreads) {
@@ -380,11 +363,13 @@ __global__ void __launch_bounds__(kGemvThreads, 1) decode_mega_kernel(const __gr
   extern __shared__ __align__(128) uint8_t smem[];
   uint64_t *full_bar = reinterpret_cast<uint64_t *>(smem);
   uint64_t *empty_bar = full_bar + kGemvMaxStages;
-  uint64_t *xbar = reinterpret_cast<uint64_t *>(smem + kGemvBarBytes);  // [0] phase records, [1] ranges
+  // [0] phase records, [1] ranges, [2] cached K/V rows of an attention item
+  uint64_t *xbar = reinterpret_cast<uint64_t *>(smem + kGemvBarBytes);
   MegaPhase *s_ph = reinterpret_cast<MegaPhase *>(smem + A.off_ph);     // two records
   const int2 *s_rg = reinterpret_cast<const int2 *>(smem + A.off_rg);   // this CTA's ranges
   uint8_t *ring = smem + A.off_ring;
-  uint8_t *scr = smem + A.off_scr;
+  uint8_t *abuf = smem + A.off_scr;   // attention item buffer
+  uint8_t *scr = smem + A.off_stage;  // x staging of the GEMV phases
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
     for (int s = 0; s < A.NS; ++s) {
@@ -393,6 +378,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) decode_mega_kernel(const __gr
     }
     mbar_init(&xbar[0], 1);
     mbar_init(&xbar[1], 1);
+    mbar_init(&xbar[2], 1);
     fence_mbar_init();
   }
   __syncthreads();
@@ -429,7 +415,10 @@ __global__ void __launch_bounds__(kGemvThreads, 1) decode_mega_kernel(const __gr
   }
 
   uint32_t it = 0;
-  int issued = 1, landed = 0;  // phase-record copies (thread 0's view)
+  int issued = 1, landed = 0;    // phase-record copies (thread 0's view)
+  int kv_issued = 0, kv_done = 0;  // K/V row fetches (thread 0's view)
+  const int pos = *A.pos;        // this step's position (advanced after the last phase)
+  __shared__ int s_kv_ok;
   for (int p = 0; p < A.nph; ++p) {
     // the record of phase p was requested during phase p - 1 into the buffer
     // of phase p - 2, which every consumer finished before the last barrier
@@ -453,13 +442,17 @@ __global__ void __launch_bounds__(kGemvThreads, 1) decode_mega_kernel(const __gr
         phase_embed(A);
         break;
       case PH_GEMV: {
+        if (P.attn_prefetch && threadIdx.x == 0 && (int)blockIdx.x < A.G * A.nsa) {
+          attn_fetch(A, P.attn_prefetch - 1, blockIdx.x % A.G, blockIdx.x / A.G, pos, abuf, &xbar[2]);
+          ++kv_issued;
+        }
         const int2 rg = s_rg[p];
         const int n = rg.y - rg.x;
         if (n > 0) {
           const bool full = n >= P.g.kunits;
           float *s16 = reinterpret_cast<float *>(scr + (size_t)P.g.win_units * P.g.kc * 2);
           if (P.combine)
-            stage_combine(A, P.g, rg.x, n, full, scr, s16, s16 + (size_t)P.g.win_units * (P.g.kc / 16));
+            stage_combine(A, P.g, rg.x, n, full, scr, s16);
           else
             stage_x(P.g, rg.x, n, full, scr, s16);
           consumer_sync();
@@ -473,14 +466,23 @@ __global__ void __launch_bounds__(kGemvThreads, 1) decode_mega_kernel(const __gr
       }
       case PH_ATTN: {
         const int items = A.G * A.nsa;
-        for (int item = blockIdx.x; item < items; item += gridDim.x)
-          attn_item(A, P.at, item % A.G, item / A.G, scr);
+        for (int item = blockIdx.x; item < items; item += gridDim.x) {
+          if (threadIdx.x == 0) {
+            // the first item's rows were fetched during the QKV phase
+            if (item != (int)blockIdx.x) {
+              attn_fetch(A, P.at.layer, item % A.G, item / A.G, pos, abuf, &xbar[2]);
+              ++kv_issued;
+            }
+            // a failed wait leaves garbage rows; the next grid barrier then
+            // ends the step with the error flag set
+            s_kv_ok = mbar_wait(&xbar[2], (uint32_t)kv_done & 1u, A.err, 405);
+            ++kv_done;
+          }
+          consumer_sync();
+          attn_item(A, P.at, item % A.G, item / A.G, pos, abuf);
+        }
         break;
       }
-      case PH_COMBINE:
-        for (int hq = blockIdx.x; hq < A.H; hq += gridDim.x)
-          combine_head(A, hq, reinterpret_cast<float *>(scr));
-        break;
       case PH_ARGMAX:
         phase_argmax(A, reinterpret_cast<float *>(scr));
         break;
@@ -491,6 +493,8 @@ __global__ void __launch_bounds__(kGemvThreads, 1) decode_mega_kernel(const __gr
   // leave no record copy in flight: after an early exit the last requested
   // record (copy number issued - 1) may still be landing
   if (threadIdx.x == 0 && issued > landed) mbar_wait(&xbar[0], (uint32_t)(issued - 1) & 1u, nullptr, 0);
+  if (threadIdx.x == 0 && kv_issued > kv_done) mbar_wait(&xbar[2], (uint32_t)kv_done & 1u, nullptr, 0);
+  (void)s_kv_ok;
 }
 
 }  // namespace
@@ -516,11 +520,12 @@ ifx_status mega_finalize(MegaPlan *plan, const std::vector<MegaPhase> &phases, i
     if (p.kind == PH_GEMV) {
       slot = std::max<size_t>(slot, (size_t)p.g.slot_bytes);
       size_t w = (size_t)p.g.win_units * (p.g.kc * 2 + p.g.kc / 16 * 4);
-      if (p.combine) w += (size_t)A.H * A.nsa * 4;  // split weights of every head
       win = std::max<size_t>(win, w);
     }
-  const size_t scratch = std::max<size_t>(
-      {win, mega_attn_scratch(A.H / A.G, A.hd, A.max_seq, A.nsa), (size_t)kMaxSplitsMega * 4});
+  // attention buffer (filled during the QKV phase) and staging area side by side
+  const size_t attn_bytes =
+      (mega_attn_scratch(A.H / A.G, A.hd, A.max_seq, A.nsa) + 127) & ~(size_t)127;
+  const size_t scratch = attn_bytes + win;
   constexpr size_t kCap = 220 * 1024;
   A.nph = (int)phases.size();
   A.nph_pad = (A.nph + 1) & ~1;
@@ -530,7 +535,10 @@ ifx_status mega_finalize(MegaPlan *plan, const std::vector<MegaPhase> &phases, i
   const size_t off_ring = (off_rg + (size_t)A.nph_pad * sizeof(int2) + 127) & ~(size_t)127;
   if (off_ring + 2 * slot + scratch > kCap)
     return fail(IFX_ERR_UNSUPPORTED, "persistent decode: shared memory plan too large");
-  int NS = (int)std::min<size_t>(kGemvMaxStages, (kCap - off_ring - scratch) / slot);
+  // even: every use of a slot then belongs to the same consumer half (see
+  // the stage count in gemv_plan)
+  int NS = (int)std::min<size_t>(kGemvMaxStages, (kCap - off_ring - scratch) / slot) & ~1;
+  if (NS < 2) return fail(IFX_ERR_UNSUPPORTED, "persistent decode: ring needs two slots");
   A.NS = NS;
   A.slot_bytes = (int)slot;
   A.scratch_bytes = (int)scratch;
@@ -538,6 +546,7 @@ ifx_status mega_finalize(MegaPlan *plan, const std::vector<MegaPhase> &phases, i
   A.off_rg = (int)off_rg;
   A.off_ring = (int)off_ring;
   A.off_scr = (int)(off_ring + (size_t)NS * slot);
+  A.off_stage = (int)(A.off_scr + attn_bytes);
   // per-CTA unit ranges of every phase (zero-length outside GEMV phases)
   std::vector<int2> rg((size_t)num_sms * A.nph_pad, make_int2(0, 0));
   std::vector<int2> sched(num_sms);

@@ -5,10 +5,11 @@
 
 namespace ifx {
 
-enum MegaKind { PH_EMBED = 0, PH_GEMV = 1, PH_ATTN = 2, PH_COMBINE = 3, PH_ARGMAX = 4 };
+enum MegaKind { PH_EMBED = 0, PH_GEMV = 1, PH_ATTN = 2, PH_ARGMAX = 4 };
 
 struct MegaAttn {
   __half *kc, *vc;  // this layer's caches [G][max_seq][hd]
+  int layer;
 };
 
 // 16-byte aligned (and so a multiple of 16 in size): the kernel moves
@@ -21,6 +22,8 @@ struct __align__(16) MegaPhase {
   int zero_n;
   int combine;      // PH_GEMV over the attention output: stage it by combining the
                     // attention splits on the fly (no separate combine phase)
+  int attn_prefetch;  // layer + 1 on the QKV GEMV: during it, fetch this CTA's first
+                      // attention item's cached K/V rows of that layer (0: none)
 };
 
 struct MegaArgs {
@@ -29,7 +32,7 @@ struct MegaArgs {
   const int2 *rg;  // [grid][nph_pad]: each CTA's unit range per phase
   int nph_pad;     // nph rounded up to even (rows are 16-byte multiples)
   // dynamic shared memory carve-up (byte offsets)
-  int off_ph, off_rg, off_ring, off_scr;
+  int off_ph, off_rg, off_ring, off_scr, off_stage;  // off_scr: attention buffer
   int NS, slot_bytes, scratch_bytes;
   unsigned *bar;  // grid barrier counter, zero at launch
   int *err;
@@ -43,6 +46,8 @@ struct MegaArgs {
   int H, G, hd, max_seq, nsa, rope_compat, rope_dim;
   float rope_base;
   const float *qkv;
+  const __half *kc0, *vc0;  // layer 0 of the K and V caches
+  size_t kv_layer_elems;    // elements per layer of one cache
   int *pos;
   unsigned long long *amax_key;
   int *amax_count;

@@ -116,7 +116,13 @@ ifx_status gemv_plan(const QMatrix *const *mats, float *const *ys, int nseg, int
   a.eps = eps;
   a.err = err;
   a.slot_bytes = slot;
-  a.nstages = std::min(kGemvMaxStages, std::max(2, kGemvRingBytes / slot));
+  // An even stage count is required: ring position p belongs to consumer
+  // half p & 1, and with an even count every use of a slot belongs to the
+  // same half, which consumes its positions in order. With an odd count the
+  // two halves alternate on a slot, one half can wait on a slot whose
+  // previous use (the other half's) has not landed, and the parity wait then
+  // passes a phase early.
+  a.nstages = std::min(kGemvMaxStages, std::max(2, kGemvRingBytes / slot)) & ~1;
 
   // byte-balanced contiguous ranges, one per CTA
   // one schedule entry per SM (the persistent decode kernel indexes it by
@@ -147,7 +153,7 @@ ifx_status gemv_plan(const QMatrix *const *mats, float *const *ys, int nseg, int
   constexpr size_t kSmemCap = 220 * 1024;
   const size_t win_bytes = (size_t)win * (a.kc * 2 + a.kc / 16 * 4);
   while (a.nstages > 2 && kGemvBarBytes + (size_t)a.nstages * a.slot_bytes + win_bytes > kSmemCap)
-    --a.nstages;
+    a.nstages -= 2;
   const size_t smem = kGemvBarBytes + (size_t)a.nstages * a.slot_bytes + win_bytes;
   if (smem > kSmemCap) return fail(IFX_ERR_SHAPE, "gemv: shared memory plan too large");
   IFX_CUDA(cudaMalloc(&plan->d_sched, sizeof(int2) * G));

@@ -420,6 +420,9 @@ ifx_status Model::build_mega(KvCache &kv) {
   A.rope_dim = (int)c.rope_dim;
   A.rope_base = c.rope_base;
   A.qkv = qkv;
+  A.kc0 = kv.k;
+  A.vc0 = kv.v;
+  A.kv_layer_elems = kv.per_layer;
   A.pos = kv.pos;
   A.amax_key = amax_key;
   A.amax_count = amax_count;
@@ -445,10 +448,12 @@ ifx_status Model::build_mega(KvCache &kv) {
   simple(PH_EMBED, logits, (int)c.vocab_size);
   for (uint64_t l = 0; l < c.n_layers; ++l) {
     gemv(p_qkv[l], nullptr, 0);
+    ph.back().attn_prefetch = (int)l + 1;  // this layer's K/V rows land during QKV
     MegaPhase at{};
     at.kind = PH_ATTN;
     at.at.kc = kv.k + l * kv.per_layer;
     at.at.vc = kv.v + l * kv.per_layer;
+    at.at.layer = (int)l;
     at.zero_ptr = gu;  // consumed by the previous layer's W2, refilled by W13
     at.zero_n = (int)(2 * c.intermediate_size);
     ph.push_back(at);

@@ -128,7 +128,11 @@ def test_graph_and_eager_decode_agree(tiny):
 @pytest.mark.parametrize("shape", ["tiny", "gqa128"])
 def test_persistent_and_per_op_decode_agree(shape):
     """The persistent one-launch decode step and the per-op kernels compute the
-    same step (to float-atomic ordering), including the generated tokens."""
+    same step, including the generated tokens. Both are held to the oracle at
+    the parity bar. Between themselves they differ only in summation order
+    (attention scores, split combine, float atomics) ahead of the f16 rounding
+    of staged activations, which can move single staged values by one f16 ulp
+    (2^-11 relative): hence 5e-3 between the two paths."""
     if shape == "tiny":
         g = synth.build("tiny")
         vocab = 32000
@@ -139,12 +143,16 @@ def test_persistent_and_per_op_decode_agree(shape):
     prompt = synth.prompt_ids(vocab, 33, seq_index=1)
     a = Model.from_bytes(g, persistent_decode=True)
     b = Model.from_bytes(g, persistent_decode=False)
-    ka, kb = a.kv_cache(300), b.kv_cache(300)
+    o = R.Model(g)
+    ka, kb, ko = a.kv_cache(300), b.kv_cache(300), o.kv_cache(int(o.config.n_layers), 300)
     a.prefill(prompt, ka, True)
     b.prefill(prompt, kb, True)
+    o.prefill(prompt, ko, True)
     for t in (5, 77, vocab - 1, 3):
-        la, lb = a.decode_step(t, ka), b.decode_step(t, kb)
-        assert np.allclose(la, lb, atol=1e-3, rtol=1e-3), float(np.max(np.abs(la - lb)))
+        la, lb, lo = a.decode_step(t, ka), b.decode_step(t, kb), o.decode_step(t, ko)
+        assert close(la, lo) and close(lb, lo), (float(np.max(np.abs(la - lo))),
+                                                 float(np.max(np.abs(lb - lo))))
+        assert np.allclose(la, lb, atol=5e-3, rtol=5e-3), float(np.max(np.abs(la - lb)))
     ta, _ = a.decode_greedy(9, 40, ka)
     tb, _ = b.decode_greedy(9, 40, kb)
     assert len(ka) == len(kb) == 33 + 4 + 40
