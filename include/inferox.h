@@ -245,6 +245,11 @@ ifx_status ifx_op_sample_u_static(const float *logits_dev, size_t n,
                                   uint32_t *token_dev, void *stream);
 
 /* --------------------------- measurement hooks -------------------------- */
+/* No reference counterpart. Kernels one decode step on this cache launches:
+ * 1 when the step runs as the persistent decode kernel, else the per-op
+ * count (3 + 5 * n_layers). Meaningful once the cache has been decoded into
+ * (the persistent plan is built by the first decode step); 0 before that. */
+int ifx_kv_decode_kernels(const ifx_kv *kv);
 /* No reference counterpart. Launch one of the decode step's fused kernels
  * `reps` times in isolation (cycling through the layers so the weights come
  * from HBM, not L2) and report the CUDA-event time per launch and the

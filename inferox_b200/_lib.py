@@ -95,6 +95,7 @@ def _load():
         "ifx_kv_free": (None, [vp]),
         "ifx_kv_clear": (st, [vp]),
         "ifx_kv_len": (sz, [vp]),
+        "ifx_kv_decode_kernels": (C.c_int, [vp]),
         "ifx_kv_read": (st, [vp, sz, C.c_int, fp]),
         "ifx_prefill": (st, [vp, vp, u32p, sz, fp, C.c_int]),
         "ifx_decode_step": (st, [vp, vp, C.c_uint32, fp]),

@@ -172,6 +172,13 @@ ifx_status ifx_kv_clear(ifx_kv *kv) {
 
 size_t ifx_kv_len(const ifx_kv *kv) { return kv ? kv->kv.len : 0; }
 
+int ifx_kv_decode_kernels(const ifx_kv *kv) {
+  if (!kv || !kv->kv.m) return 0;
+  if (kv->kv.mega_ready) return 1;
+  if (!kv->kv.mega_tried && kv->kv.m->opts.persistent_decode) return 0;  // not decided yet
+  return 3 + 5 * (int)kv->kv.m->cfg.n_layers;
+}
+
 ifx_status ifx_kv_read(const ifx_kv *kv, size_t layer, int which_v, float *out_host) {
   if (!kv || !out_host) return fail(IFX_ERR_INVALID_ARGUMENT, "kv_read: null");
   return kv->kv.m->kv_read(kv->kv, layer, which_v, out_host);

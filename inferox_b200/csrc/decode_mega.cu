@@ -1,8 +1,11 @@
 // Persistent batch-1 decode kernel (one cooperative launch per token).
 //
 // 148 CTAs x (16 consumer warps + 1 producer warp). The token step is a list
-// of phases (embed; per layer QKV GEMV, attention, combine, Wo GEMV, W1/W3
-// GEMV, W2 GEMV; logits GEMV; argmax). Phases that read the previous phase's
+// of phases (embed; per layer QKV GEMV, attention, Wo GEMV, W1/W3 GEMV, W2
+// GEMV; logits GEMV; argmax). The attention phase's split-K partials are
+// combined by the CTA that finishes each kv head's last split, and the cached
+// K/V rows of each CTA's first attention item are bulk-copied into shared
+// memory during the QKV phase. Phases that read the previous phase's
 // output are separated by a grid barrier (atomic counter with a bounded
 // spin). The producer warp does not take part in the barriers: weights do
 // not depend on activations, so it streams every GEMV phase's units for its
@@ -259,68 +262,54 @@ __device__ __noinline__ void attn_item(const MegaArgs &A, const MegaAttn &at, in
   consumer_sync();  // the buffer is reused by the next item
 }
 
-// Staging of the Wo GEMV straight from the attention splits: column
-// hq * hd + d of the attention output is sum_s w_s o_s[d] / sum_s w_s l_s with
-// w_s = exp(m_s - M) over the splits of query head hq (splits with no rows
-// carry l = 0 and weight 0). Each staged group of four columns is combined
-// in one pass with a running maximum, so all of its loads go out together.
-// Writes the f16 fragments and 16-column sums exactly as stage_x does for a
-// plain input.
-__device__ __noinline__ void stage_combine(const MegaArgs &A, const GemvArgs &g, int u0, int n,
-                                           bool full, uint8_t *xw, float *s16) {
-  const int tid = threadIdx.x;
-  constexpr int T = kConsumerThreads;
+// Combine of the splits of kv head h (its grp query heads), run by the CTA
+// that finished the head's last split: attn[hq][d] = sum_s w_s o_s[d] with
+// w_s = exp(m_s - M) / sum_s' exp(m_s' - M) l_s' (splits with no rows carry
+// l = 0 and weight 0). Two load rounds: the (m, l) pairs, then the partial
+// outputs. `wbuf` holds 3 * grp * nsa floats.
+__device__ __noinline__ void combine_kv_head(const MegaArgs &A, int h, float *wbuf) {
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int hd = A.hd, grp = A.H / A.G, NS = A.nsa;
-  const int kc = g.kc, kunits = g.kunits;
-  const int nslots = full ? kunits : n;
-  const int per_slot = kc / 4, total = nslots * per_slot;
-  const int nseg = g.nseg;
-  int sb[kGemvMaxSegs];
-#pragma unroll
-  for (int i = 0; i < kGemvMaxSegs; ++i) sb[i] = i < nseg ? g.seg[i].unit_begin : 0x7fffffff;
-  __half *xh = reinterpret_cast<__half *>(xw);
-  for (int base = 0; base < total; base += T) {
-    const int f = base + tid;
-    float y[4] = {0.f, 0.f, 0.f, 0.f};
-    const bool valid = f < total;
-    if (valid) {
-      const int jj = f / per_slot, o = (f % per_slot) * 4;
-      int kunit = jj;
-      if (!full) {
-        const int u = u0 + jj;
-        int b = sb[0];
-#pragma unroll
-        for (int i = 1; i < kGemvMaxSegs; ++i) b = u >= sb[i] ? sb[i] : b;
-        kunit = (u - b) % kunits;
-      }
-      const int col = kunit * kc + o;
-      const int hq = col / hd, d = col % hd;
-      const int h = hq / grp, j = hq % grp;
-      const float2 *ml = A.part_ml + (size_t)h * NS * grp + j;  // split stride grp
-      const float4 *po =
-          reinterpret_cast<const float4 *>(A.part_o + ((size_t)h * NS * grp + j) * hd + d);
-      const size_t sstride = (size_t)grp * hd / 4;  // float4 stride between splits
-      float M = -INFINITY, L = 0.f;
-#pragma unroll 6
-      for (int s = 0; s < NS; ++s) {
-        const float2 v2 = __ldcg(ml + (size_t)s * grp);
-        const float4 v = __ldcg(po + s * sstride);
-        if (v2.y > 0.f) {
-          const float Mn = fmaxf(M, v2.x);
-          const float r = expf(M - Mn), w = expf(v2.x - Mn);  // exp(-inf) = 0 on the first split
-          L = fmaf(L, r, w * v2.y);
-          y[0] = fmaf(y[0], r, w * v.x);
-          y[1] = fmaf(y[1], r, w * v.y);
-          y[2] = fmaf(y[2], r, w * v.z);
-          y[3] = fmaf(y[3], r, w * v.w);
-          M = Mn;
-        }
-      }
-      const float invL = 1.0f / L;
-#pragma unroll
-      for (int t = 0; t < 4; ++t) y[t] *= invL;
+  float2 *ml = reinterpret_cast<float2 *>(wbuf);  // [grp][NS]
+  float *wn = wbuf + 2 * grp * NS;                 // [grp][NS]
+  for (int e = tid; e < grp * NS; e += kConsumerThreads) {
+    const int j = e / NS, s = e - j * NS;
+    ml[e] = __ldcg(&A.part_ml[(h * NS + s) * grp + j]);
+  }
+  consumer_sync();
+  if (warp < grp) {
+    const int j = warp;
+    float M = -INFINITY;
+    for (int s = lane; s < NS; s += 32)
+      if (ml[j * NS + s].y > 0.f) M = fmaxf(M, ml[j * NS + s].x);
+    M = warp_max(M);
+    float L = 0.f;
+    for (int s = lane; s < NS; s += 32) {
+      const float2 v = ml[j * NS + s];
+      const float w = v.y > 0.f ? expf(v.x - M) : 0.f;
+      wn[j * NS + s] = w;
+      L = fmaf(v.y, w, L);
     }
-    emit_x4(y, valid, f, per_slot, kc, xh, s16, tid);
+    L = warp_sum(L);
+    const float invL = 1.0f / L;
+    __syncwarp();
+    for (int s = lane; s < NS; s += 32) wn[j * NS + s] *= invL;
+  }
+  consumer_sync();
+  const size_t sstride = (size_t)grp * hd;  // floats between splits
+  for (int e = tid; e < grp * hd; e += kConsumerThreads) {
+    const int j = e / hd, d = e - j * hd;
+    const float *po = A.part_o + ((size_t)h * NS * grp + j) * hd + d;
+    const float *w = wn + j * NS;
+    float o0 = 0.f, o1 = 0.f;
+    int s = 0;
+#pragma unroll 4
+    for (; s + 1 < NS; s += 2) {
+      o0 = fmaf(w[s], __ldcg(po + s * sstride), o0);
+      o1 = fmaf(w[s + 1], __ldcg(po + (s + 1) * sstride), o1);
+    }
+    if (s < NS) o0 = fmaf(w[s], __ldcg(po + s * sstride), o0);
+    A.attn[(size_t)(h * grp + j) * hd + d] = o0 + o1;
   }
 }
 
@@ -418,7 +407,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) decode_mega_kernel(const __gr
   int issued = 1, landed = 0;    // phase-record copies (thread 0's view)
   int kv_issued = 0, kv_done = 0;  // K/V row fetches (thread 0's view)
   const int pos = *A.pos;        // this step's position (advanced after the last phase)
-  __shared__ int s_kv_ok;
+  __shared__ int s_kv_ok, s_last;
   for (int p = 0; p < A.nph; ++p) {
     // the record of phase p was requested during phase p - 1 into the buffer
     // of phase p - 2, which every consumer finished before the last barrier
@@ -451,10 +440,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) decode_mega_kernel(const __gr
         if (n > 0) {
           const bool full = n >= P.g.kunits;
           float *s16 = reinterpret_cast<float *>(scr + (size_t)P.g.win_units * P.g.kc * 2);
-          if (P.combine)
-            stage_combine(A, P.g, rg.x, n, full, scr, s16);
-          else
-            stage_x(P.g, rg.x, n, full, scr, s16);
+          stage_x(P.g, rg.x, n, full, scr, s16);
           consumer_sync();
           // on a failed wait the warp carries on to the next grid barrier,
           // which sees the error flag and ends the CTA's consumers together
@@ -479,7 +465,22 @@ __global__ void __launch_bounds__(kGemvThreads, 1) decode_mega_kernel(const __gr
             ++kv_done;
           }
           consumer_sync();
-          attn_item(A, P.at, item % A.G, item / A.G, pos, abuf);
+          const int h = item % A.G;
+          attn_item(A, P.at, h, item / A.G, pos, abuf);
+          // split-K fixup: the CTA that finishes kv head h's last split
+          // combines the head (release by every item, acquire by the last)
+          if (threadIdx.x == 0) {
+            __threadfence();
+            // the counters run over all layers of the step (zeroed per launch)
+            s_last = atomicAdd(&A.bar[1 + h], 1u) ==
+                     (unsigned)((P.at.layer + 1) * A.nsa) - 1u;
+          }
+          consumer_sync();
+          if (s_last) {
+            __threadfence();
+            combine_kv_head(A, h, reinterpret_cast<float *>(abuf));
+            consumer_sync();  // the buffer is reused by the next item
+          }
         }
         break;
       }
@@ -524,7 +525,9 @@ ifx_status mega_finalize(MegaPlan *plan, const std::vector<MegaPhase> &phases, i
     }
   // attention buffer (filled during the QKV phase) and staging area side by side
   const size_t attn_bytes =
-      (mega_attn_scratch(A.H / A.G, A.hd, A.max_seq, A.nsa) + 127) & ~(size_t)127;
+      (std::max(mega_attn_scratch(A.H / A.G, A.hd, A.max_seq, A.nsa),
+                (size_t)3 * (A.H / A.G) * A.nsa * sizeof(float)) +  // the head combine
+       127) & ~(size_t)127;
   const size_t scratch = attn_bytes + win;
   constexpr size_t kCap = 220 * 1024;
   A.nph = (int)phases.size();
@@ -575,7 +578,7 @@ ifx_status mega_finalize(MegaPlan *plan, const std::vector<MegaPhase> &phases, i
 }
 
 ifx_status mega_launch(const MegaPlan &plan, cudaStream_t st) {
-  IFX_CUDA(cudaMemsetAsync(plan.args.bar, 0, sizeof(unsigned), st));
+  IFX_CUDA(cudaMemsetAsync(plan.args.bar, 0, sizeof(unsigned) * (1 + plan.args.G), st));
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(plan.grid);
   cfg.blockDim = dim3(kGemvThreads);

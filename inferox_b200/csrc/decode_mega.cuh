@@ -20,8 +20,6 @@ struct __align__(16) MegaPhase {
   MegaAttn at;  // PH_ATTN
   float *zero_ptr;  // buffer this phase zeroes (a later phase accumulates into it)
   int zero_n;
-  int combine;      // PH_GEMV over the attention output: stage it by combining the
-                    // attention splits on the fly (no separate combine phase)
   int attn_prefetch;  // layer + 1 on the QKV GEMV: during it, fetch this CTA's first
                       // attention item's cached K/V rows of that layer (0: none)
 };
@@ -34,7 +32,8 @@ struct MegaArgs {
   // dynamic shared memory carve-up (byte offsets)
   int off_ph, off_rg, off_ring, off_scr, off_stage;  // off_scr: attention buffer
   int NS, slot_bytes, scratch_bytes;
-  unsigned *bar;  // grid barrier counter, zero at launch
+  unsigned *bar;  // [0] grid barrier counter, [1 + h] finished splits of kv head h;
+                  // all zeroed at every launch
   int *err;
   // token loop state
   const uint8_t *emb;

@@ -399,7 +399,7 @@ ifx_status Model::build_mega(KvCache &kv) {
   A.nsa = mega_attn_splits(G, (int)kv.max_seq, kNumSMs);
   IFX_TRY(dalloc(&kv.part_o, (size_t)H * A.nsa * hd));
   IFX_TRY(dalloc(&kv.part_ml, (size_t)H * A.nsa));
-  IFX_TRY(dalloc(&kv.bar, 1));
+  IFX_TRY(dalloc(&kv.bar, 1 + (size_t)G));  // barrier counter + per-kv-head split counters
   A.bar = kv.bar;
   A.err = err;
   A.emb = emb_raw;
@@ -457,8 +457,7 @@ ifx_status Model::build_mega(KvCache &kv) {
     at.zero_ptr = gu;  // consumed by the previous layer's W2, refilled by W13
     at.zero_n = (int)(2 * c.intermediate_size);
     ph.push_back(at);
-    gemv(p_wo[l], nullptr, 0);
-    ph.back().combine = 1;  // Wo stages its input from the attention splits
+    gemv(p_wo[l], nullptr, 0);  // the attention phase leaves the combined heads in attn
     gemv(p_w13[l], qkv, qkv_n);  // qkv was consumed by ATTN; the next QKV refills it
     gemv(p_w2[l], nullptr, 0);
   }

@@ -150,6 +150,10 @@ class KvCache:
     def __len__(self) -> int:
         return int(lib.ifx_kv_len(self._h))
 
+    def decode_kernels(self) -> int:
+        """Kernels one decode step launches on this cache (1: persistent kernel)."""
+        return int(lib.ifx_kv_decode_kernels(self._h))
+
     def read(self, layer: int, which_v: bool) -> np.ndarray:
         n = len(self)
         out = np.empty(max(n * self.kv_dim, 1), np.float32)
