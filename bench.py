@@ -30,6 +30,10 @@ sys.path.insert(0, ROOT)
 CONFIG = "8b"
 PROMPT = 1024
 METRIC = "decode tok/s @8B Q4_K_M batch 1 as % of HBM roofline; prefill tok/s"
+# DRAM bytes (read + write) per algorithmic byte of decode_mega_kernel, from
+# the ncu capture summarised in profiles/decode_mega_kernel_8b_4layers.md
+# (976.6 MB + 15.1 MB over 973.2 MB); traffic scales with the weight bytes.
+TRAFFIC_PER_ALGO_BYTE = 1.019
 
 
 def peaks():
@@ -154,7 +158,7 @@ def run_ours(args):
     from inferox_b200 import Model, synth
 
     t0 = time.time()
-    g = synth.build(CONFIG)
+    g = synth.build(CONFIG, **({"n_layers": args.layers} if args.layers else {}))
     t_gen = time.time() - t0
     t0 = time.time()
     m = Model.from_bytes(g, device=local)
@@ -232,7 +236,8 @@ def run_ours(args):
         "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "q4_k/q6_k weights, f16 tensor-core math, f32 accumulate",
         "data": "synthetic (seeded N(0,0.02) weights quantised Q4_K_M; seeded uniform prompt ids)",
-        "config": {"workload": "llama3-8b-shaped Q4_K_M: 1024-token prompt prefill, then batch-1 greedy decode",
+        "config": {"workload": "llama3-8b-shaped Q4_K_M: 1024-token prompt prefill, then batch-1 greedy decode"
+                               + (f" (profiling case: {L} layers)" if args.layers else ""),
                    "model": "llama-3-8b-shaped", "global_batch": world, "seq_len": PROMPT,
                    "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
                    "l2": "no flush needed: 4.6 GB of weights per step >> 126 MB L2"},
@@ -246,7 +251,8 @@ def run_ours(args):
         "roofline": {"bound": "hbm",
                      "kernel": "decode_mega_kernel" if kernels_per_step == 1 else "per-op step",
                      "achieved": step_gbs, "peak": hbm, "unit": "GB/s", "frac": step_gbs / hbm,
-                     "traffic": None, "peak_kind": peak_kind},
+                     "traffic": TRAFFIC_PER_ALGO_BYTE * step_bytes if kernels_per_step == 1 else None,
+                     "traffic_unit": "bytes per launch", "peak_kind": peak_kind},
         "kernels": kern,
         "e2e": e2e,
         "gpu_launches": args.steps * kernels_per_step,
@@ -267,6 +273,9 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--layers", type=int, default=0,
+                    help="profiling only: an 8B-shaped model with this many layers "
+                         "(0 = the full 32); the line's config names it")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
