@@ -244,6 +244,26 @@ ifx_status ifx_op_sample_u_static(const float *logits_dev, size_t n,
                                   const ifx_sampler *s, float u,
                                   uint32_t *token_dev, void *stream);
 
+/* ------------------------- tensor parallelism --------------------------- */
+/* No reference counterpart (the reference is single-threaded CPU code).
+ * Megatron split across tp_size GPUs of one box: Wq/Wk/Wv, W1/W3 and the
+ * vocab projection by rows, Wo/W2 by their input dimension, the KV cache by
+ * kv head; an NCCL all-reduce after Wo and after W2, an all-gather of the
+ * vocab slices. ifx_load_opts.nccl_comm must be a communicator of the NCCL
+ * library instance this library uses; these make one: rank 0 calls
+ * ifx_tp_unique_id, the caller sends the 128 bytes to every rank, then every
+ * rank calls ifx_tp_comm_create (collective: it returns once all joined). */
+ifx_status ifx_tp_unique_id(void *id_out /* 128 bytes */);
+ifx_status ifx_tp_comm_create(const void *id, int nranks, int rank, int device,
+                              void **comm_out);
+void ifx_tp_comm_destroy(void *comm);
+/* Host only: the shard of a GGUF-layout weight [rows, cols] that `rank` of
+ * `tp` holds (split_k = 0: a block of rows; 1: a block of every row's input
+ * dimension). out NULL: *out_bytes receives the shard size only. */
+ifx_status ifx_tp_shard(int type, const void *gguf_bytes, size_t nbytes,
+                        size_t rows, size_t cols, int split_k, int tp, int rank,
+                        void *out, size_t *out_bytes);
+
 /* --------------------------- measurement hooks -------------------------- */
 /* No reference counterpart. Kernels one decode step on this cache launches:
  * 1 when the step runs as the persistent decode kernel, else the per-op

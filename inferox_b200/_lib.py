@@ -96,6 +96,10 @@ def _load():
         "ifx_kv_clear": (st, [vp]),
         "ifx_kv_len": (sz, [vp]),
         "ifx_kv_decode_kernels": (C.c_int, [vp]),
+        "ifx_tp_unique_id": (st, [vp]),
+        "ifx_tp_comm_create": (st, [vp, C.c_int, C.c_int, C.c_int, C.POINTER(vp)]),
+        "ifx_tp_comm_destroy": (None, [vp]),
+        "ifx_tp_shard": (st, [C.c_int, vp, sz, sz, sz, C.c_int, C.c_int, C.c_int, vp, C.POINTER(sz)]),
         "ifx_kv_read": (st, [vp, sz, C.c_int, fp]),
         "ifx_prefill": (st, [vp, vp, u32p, sz, fp, C.c_int]),
         "ifx_decode_step": (st, [vp, vp, C.c_uint32, fp]),

@@ -12,6 +12,7 @@
 #include "gemv.cuh"
 #include "model.h"
 #include "ops.cuh"
+#include "tp.h"
 
 struct ifx_model {
   ifx::Model m;
@@ -434,6 +435,48 @@ ifx_status ifx_op_sample_u_static(const float *logits_dev, size_t n, const ifx_s
   if (!logits_dev || !s || !token_dev) return fail(IFX_ERR_INVALID_ARGUMENT, "sample_u_static: null");
   return op_sample_u_static(logits_dev, n, s->temperature, s->top_k, s->top_p, u, token_dev,
                             S(stream));
+}
+
+ifx_status ifx_tp_unique_id(void *id_out) {
+  if (!id_out) return fail(IFX_ERR_INVALID_ARGUMENT, "tp_unique_id: null");
+  const NcclApi *api = nullptr;
+  IFX_TRY(nccl_api(&api));
+  ncclUniqueId id;
+  IFX_NCCL(api, api->GetUniqueId(&id));
+  memcpy(id_out, &id, sizeof(id));
+  return IFX_OK;
+}
+
+ifx_status ifx_tp_comm_create(const void *id, int nranks, int rank, int device, void **comm_out) {
+  if (!id || !comm_out || nranks < 1 || rank < 0 || rank >= nranks)
+    return fail(IFX_ERR_INVALID_ARGUMENT, "tp_comm_create: bad argument");
+  const NcclApi *api = nullptr;
+  IFX_TRY(nccl_api(&api));
+  IFX_CUDA(cudaSetDevice(device));
+  ncclUniqueId uid;
+  memcpy(&uid, id, sizeof(uid));
+  ncclComm_t c = nullptr;
+  IFX_NCCL(api, api->CommInitRank(&c, nranks, uid, rank));
+  *comm_out = c;
+  return IFX_OK;
+}
+
+void ifx_tp_comm_destroy(void *comm) {
+  const NcclApi *api = nullptr;
+  if (comm && nccl_api(&api) == IFX_OK) api->CommDestroy((ncclComm_t)comm);
+}
+
+ifx_status ifx_tp_shard(int type, const void *gguf_bytes, size_t nbytes, size_t rows, size_t cols,
+                        int split_k, int tp, int rank, void *out, size_t *out_bytes) {
+  if (!gguf_bytes || !out_bytes) return fail(IFX_ERR_INVALID_ARGUMENT, "tp_shard: null");
+  IFX_GUARD({
+    std::vector<uint8_t> sh;
+    IFX_TRY(tp_shard(type, static_cast<const uint8_t *>(gguf_bytes), nbytes, rows, cols, split_k,
+                     tp, rank, &sh));
+    *out_bytes = sh.size();
+    if (out) memcpy(out, sh.data(), sh.size());
+    return IFX_OK;
+  })
 }
 
 }  // extern "C"

@@ -27,6 +27,7 @@
 #include "gemv.cuh"
 #include "gguf.h"
 #include "model.h"
+#include "tp.h"
 #include "ops.cuh"
 #include "quant.cuh"
 
@@ -56,16 +57,19 @@ __global__ void embed_rows_kernel(const uint8_t *emb, int type, int D, const uin
 
 // Argmax over logits (last index on ties, forward.rs:615-622); the last CTA
 // publishes the token, optionally records it and advances the position.
+// With publish = 0 (a vocab shard under tensor parallelism) the key of the
+// shard's maximum is left in *key (indices offset by v0) for the all-reduce.
 __global__ void argmax_step_kernel(const float *logits, int n, unsigned long long *key,
                                    int *count, uint32_t *next_token, uint32_t *tokens,
-                                   int *n_out, int *pos, int record, int inc_pos) {
+                                   int *n_out, int *pos, int record, int inc_pos, int v0,
+                                   int publish) {
   pdl_wait();
   pdl_launch();
   unsigned long long best = 0;
   for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
     const float v = logits[i];
     if (v != v) continue;
-    const unsigned long long k = ((unsigned long long)ordered_bits(v) << 32) | (unsigned)i;
+    const unsigned long long k = ((unsigned long long)ordered_bits(v) << 32) | (unsigned)(i + v0);
     best = k > best ? k : best;
   }
 #pragma unroll
@@ -81,6 +85,10 @@ __global__ void argmax_step_kernel(const float *logits, int n, unsigned long lon
   __syncthreads();
   if (!last || threadIdx.x != 0) return;
   __threadfence();
+  if (!publish) {
+    *count = 0;
+    return;
+  }
   const unsigned long long k = atomicAdd(key, 0ull);
   const uint32_t tok = (uint32_t)(k & 0xffffffffull);
   *next_token = tok;
@@ -108,6 +116,31 @@ __global__ void kv_write_kernel(const float *k, const float *v, __half *kc, __ha
 
 __global__ void add_int_kernel(int *p, int v) { *p += v; }
 
+// in: [tp][n][vl] (rank-major, as gathered); out: [n][tp * vl].
+__global__ void shard_interleave_kernel(const float *in, float *out, int n, int vl, int tp) {
+  const int t = blockIdx.x;
+  for (int e = threadIdx.x; e < tp * vl; e += blockDim.x) {
+    const int r = e / vl, j = e - r * vl;
+    out[(size_t)t * tp * vl + e] = in[((size_t)r * n + t) * vl + j];
+  }
+}
+
+// After the all-reduce of the shards' keys: publish the global argmax and
+// clear this rank's shard key for the next step.
+__global__ void token_publish_kernel(const unsigned long long *key_global,
+                                     unsigned long long *key_local, uint32_t *next_token,
+                                     uint32_t *tokens, int *n_out, int *pos, int record,
+                                     int inc_pos) {
+  const uint32_t tok = (uint32_t)(*key_global & 0xffffffffull);
+  *next_token = tok;
+  if (record) {
+    tokens[*n_out] = tok;
+    *n_out = *n_out + 1;
+  }
+  if (inc_pos) *pos = *pos + 1;
+  *key_local = 0;
+}
+
 __global__ void kv_read_kernel(const __half *c, float *out, int len, int G, int hd, int max_seq) {
   const int t = blockIdx.x;
   for (int e = threadIdx.x; e < G * hd; e += blockDim.x) {
@@ -126,19 +159,31 @@ ifx_status dalloc(T **p, size_t n) {
 }  // namespace
 
 // ------------------------------------------------------------------ load --
+// A weight [rows, cols] uploaded and repacked; under tensor parallelism only
+// this rank's shard (split_k = 0: a block of rows; 1: a block of the input
+// dimension of every row) is kept.
 static ifx_status upload_matrix(const GgufFile &f, const uint8_t *bytes, size_t len, int idx,
                                 uint64_t rows, uint64_t cols, uint8_t *staging, cudaStream_t st,
-                                QMatrix *out) {
+                                QMatrix *out, int tp = 1, int rank = 0, int split_k = 0) {
   uint64_t start, size;
   IFX_TRY(gguf_tensor_range(f, len, idx, &start, &size));
   const GgufTensor &t = f.tensors[idx];
   if (t.n_elements() != rows * cols)
     return fail(IFX_ERR_SHAPE, "tensor " + t.name + ": element count does not match the config");
+  const uint8_t *src = bytes + start;
+  std::vector<uint8_t> shard;
+  if (tp > 1) {
+    IFX_TRY(tp_shard((int)t.type, src, size, rows, cols, split_k, tp, rank, &shard));
+    if (split_k) cols /= tp;
+    else rows /= tp;
+    src = shard.data();
+    size = shard.size();
+  }
   if (!make_layout((int)t.type, (int64_t)rows, (int64_t)cols, &out->L))
     return fail(IFX_ERR_UNSUPPORTED,
                 "tensor " + t.name + ": weight type " + std::to_string(t.type) +
                     " is not supported by the fused kernels (Q4_0, Q8_0, Q4_K, Q6_K)");
-  IFX_CUDA(cudaMemcpyAsync(staging, bytes + start, size, cudaMemcpyHostToDevice, st));
+  IFX_CUDA(cudaMemcpyAsync(staging, src, size, cudaMemcpyHostToDevice, st));
   IFX_CUDA(cudaMalloc(&out->d, out->L.total_bytes));
   IFX_TRY(repack_to_device(out->L, staging, out->d, st));
   IFX_CUDA(cudaStreamSynchronize(st));
@@ -160,8 +205,12 @@ static ifx_status upload_norm(const GgufFile &f, const uint8_t *bytes, size_t le
 
 ifx_status Model::load(const uint8_t *bytes, size_t len, const ifx_load_opts &o) {
   opts = o;
-  if (opts.tp_size != 1 || opts.tp_rank != 0)
-    return fail(IFX_ERR_UNSUPPORTED, "tensor parallel loading is not built in this version");
+  tp = opts.tp_size;
+  rank = opts.tp_rank;
+  if (tp < 1 || tp > 8 || rank < 0 || rank >= tp)
+    return fail(IFX_ERR_INVALID_ARGUMENT, "tp_size must be 1..8 and 0 <= tp_rank < tp_size");
+  if (tp > 1 && !opts.nccl_comm)
+    return fail(IFX_ERR_INVALID_ARGUMENT, "tensor parallel loading needs nccl_comm");
   GgufFile f;
   IFX_TRY(gguf_parse(bytes, len, &f));  // host-only checks first: no GPU needed to reject a file
   IFX_TRY(gguf_config(f, &cfg));
@@ -170,6 +219,19 @@ ifx_status Model::load(const uint8_t *bytes, size_t len, const ifx_load_opts &o)
   const uint64_t F = cfg.intermediate_size, V = cfg.vocab_size;
   if (H * hd != D || H % G || hd % 2 || cfg.rope_dim > hd || cfg.rope_dim % 2)
     return fail(IFX_ERR_SHAPE, "unsupported head geometry");
+  // Megatron split: q/k/v by heads, W1/W3 and the vocab by rows, Wo/W2 by
+  // their input dimension; a rank's q heads map onto its own kv heads
+  if (G % tp || F % tp || V % tp)
+    return fail(IFX_ERR_SHAPE, "tensor parallel: kv heads, ffn rows and vocab must divide by tp_size");
+  Hl = H / tp;
+  Gl = G / tp;
+  Fl = F / tp;
+  Vl = V / tp;
+  v0 = Vl * (uint64_t)rank;
+  if (tp > 1) {
+    comm = opts.nccl_comm;
+    IFX_TRY(nccl_api(&nccl));
+  }
   static const char *suffix[9] = {"attn_norm", "attn_q", "attn_k", "attn_v", "attn_output",
                                   "ffn_norm", "ffn_gate", "ffn_up", "ffn_down"};
   std::vector<std::array<int, 9>> idx(cfg.n_layers);
@@ -206,18 +268,19 @@ ifx_status Model::load(const uint8_t *bytes, size_t len, const ifx_load_opts &o)
   for (uint64_t l = 0; l < cfg.n_layers && st == IFX_OK; ++l) {
     Layer &L = layers[l];
     guard(upload_norm(f, bytes, len, idx[l][0], D, staging, stream, &L.attn_norm)) &&
-        guard(upload_matrix(f, bytes, len, idx[l][1], D, D, staging, stream, &L.wq)) &&
-        guard(upload_matrix(f, bytes, len, idx[l][2], G * hd, D, staging, stream, &L.wk)) &&
-        guard(upload_matrix(f, bytes, len, idx[l][3], G * hd, D, staging, stream, &L.wv)) &&
-        guard(upload_matrix(f, bytes, len, idx[l][4], D, D, staging, stream, &L.wo)) &&
+        guard(upload_matrix(f, bytes, len, idx[l][1], D, D, staging, stream, &L.wq, tp, rank, 0)) &&
+        guard(upload_matrix(f, bytes, len, idx[l][2], G * hd, D, staging, stream, &L.wk, tp, rank, 0)) &&
+        guard(upload_matrix(f, bytes, len, idx[l][3], G * hd, D, staging, stream, &L.wv, tp, rank, 0)) &&
+        guard(upload_matrix(f, bytes, len, idx[l][4], D, D, staging, stream, &L.wo, tp, rank, 1)) &&
         guard(upload_norm(f, bytes, len, idx[l][5], D, staging, stream, &L.ffn_norm)) &&
-        guard(upload_matrix(f, bytes, len, idx[l][6], F, D, staging, stream, &L.w1)) &&
-        guard(upload_matrix(f, bytes, len, idx[l][7], F, D, staging, stream, &L.w3)) &&
-        guard(upload_matrix(f, bytes, len, idx[l][8], D, F, staging, stream, &L.w2));
+        guard(upload_matrix(f, bytes, len, idx[l][6], F, D, staging, stream, &L.w1, tp, rank, 0)) &&
+        guard(upload_matrix(f, bytes, len, idx[l][7], F, D, staging, stream, &L.w3, tp, rank, 0)) &&
+        guard(upload_matrix(f, bytes, len, idx[l][8], D, F, staging, stream, &L.w2, tp, rank, 1));
   }
   if (st == IFX_OK) guard(upload_norm(f, bytes, len, i_onorm, D, staging, stream, &out_norm));
   if (st == IFX_OK)
-    guard(upload_matrix(f, bytes, len, i_out >= 0 ? i_out : i_emb, V, D, staging, stream, &out_w));
+    guard(upload_matrix(f, bytes, len, i_out >= 0 ? i_out : i_emb, V, D, staging, stream, &out_w,
+                        tp, rank, 0));
   if (st == IFX_OK) {
     uint64_t s0, sz;
     if (guard(gguf_tensor_range(f, len, i_emb, &s0, &sz))) {
@@ -235,23 +298,30 @@ ifx_status Model::load(const uint8_t *bytes, size_t len, const ifx_load_opts &o)
   cudaFree(staging);
   if (st != IFX_OK) return st;
 
-  // decode buffers
-  qkv_n = (int)((H + 2 * G) * hd);
+  // decode buffers (this rank's heads / rows; x and the gathered logits whole)
+  qkv_n = (int)((Hl + 2 * Gl) * hd);
   IFX_TRY(dalloc(&x, D));
   IFX_TRY(dalloc(&qkv, qkv_n));
-  IFX_TRY(dalloc(&attn, D));
-  IFX_TRY(dalloc(&gu, 2 * F));
+  IFX_TRY(dalloc(&attn, Hl * hd));
+  IFX_TRY(dalloc(&gu, 2 * Fl));
   IFX_TRY(dalloc(&logits, V));
+  if (tp > 1) {
+    IFX_TRY(dalloc(&y, D));
+    IFX_TRY(dalloc(&logits_local, Vl));
+    IFX_TRY(dalloc(&key_global, 1));
+  } else {
+    logits_local = logits;
+  }
   IFX_TRY(dalloc(&err, 1));
   IFX_TRY(dalloc(&next_token, 1));
   IFX_TRY(dalloc(&amax_key, 1));
   IFX_TRY(dalloc(&amax_count, 1));
   IFX_TRY(dalloc(&n_out, 1));
   // split-K factor of the decode attention: about two CTAs per SM in total
-  ns = (int)std::max<uint64_t>(1, std::min<uint64_t>(64, 2 * kNumSMs / G));
-  IFX_TRY(dalloc(&part_o, H * ns * hd));
-  IFX_TRY(dalloc(&part_ml, H * ns));
-  IFX_TRY(dalloc(&counters, G));
+  ns = (int)std::max<uint64_t>(1, std::min<uint64_t>(64, 2 * kNumSMs / Gl));
+  IFX_TRY(dalloc(&part_o, Hl * ns * hd));
+  IFX_TRY(dalloc(&part_ml, Hl * ns));
+  IFX_TRY(dalloc(&counters, Gl));
 
   // one GEMV plan (pointers + byte-balanced schedule) per call site
   const float eps = cfg.norm_eps;
@@ -262,22 +332,25 @@ ifx_status Model::load(const uint8_t *bytes, size_t len, const ifx_load_opts &o)
   for (uint64_t l = 0; l < cfg.n_layers; ++l) {
     Layer &L = layers[l];
     const QMatrix *mq[3] = {&L.wq, &L.wk, &L.wv};
-    float *yq[3] = {qkv, qkv + H * hd, qkv + (H + G) * hd};
+    float *yq[3] = {qkv, qkv + Hl * hd, qkv + (Hl + Gl) * hd};
+    // the row-parallel layers accumulate into a partial buffer under tensor
+    // parallelism (all-reduced into x), into x itself otherwise
+    float *acc = tp > 1 ? y : x;
     const QMatrix *mo[1] = {&L.wo};
-    float *yo[1] = {x};
+    float *yo[1] = {acc};
     const QMatrix *m13[2] = {&L.w1, &L.w3};
-    float *y13[2] = {gu, gu + F};
+    float *y13[2] = {gu, gu + Fl};
     const QMatrix *m2[1] = {&L.w2};
-    float *y2[1] = {x};
+    float *y2[1] = {acc};
     IFX_TRY(gemv_plan(mq, yq, 3, GEMV_RMSNORM, x, nullptr, L.attn_norm, eps, err, &p_qkv[l]));
     IFX_TRY(gemv_plan(mo, yo, 1, GEMV_PLAIN, attn, nullptr, nullptr, eps, err, &p_wo[l]));
     IFX_TRY(gemv_plan(m13, y13, 2, GEMV_RMSNORM, x, nullptr, L.ffn_norm, eps, err, &p_w13[l]));
-    IFX_TRY(gemv_plan(m2, y2, 1, GEMV_SWIGLU, gu, gu + F, nullptr, eps, err, &p_w2[l]));
+    IFX_TRY(gemv_plan(m2, y2, 1, GEMV_SWIGLU, gu, gu + Fl, nullptr, eps, err, &p_w2[l]));
     p_w13[l].args.zero_ptr = qkv;  // qkv was consumed by ATT; the next QKV refills it
     p_w13[l].args.zero_n = qkv_n;
   }
   const QMatrix *mout[1] = {&out_w};
-  float *yout[1] = {logits};
+  float *yout[1] = {logits_local};
   IFX_TRY(gemv_plan(mout, yout, 1, GEMV_RMSNORM, x, nullptr, out_norm, eps, err, &p_logits));
 
   decode_bytes = 0;
@@ -303,8 +376,10 @@ Model::~Model() {
   F(out_norm);
   F(emb_raw);
   for (auto *v : std::vector<void *>{x, qkv, attn, gu, logits, err, next_token, amax_key, amax_count,
-                                     n_out, part_o, part_ml, counters, ws, logits_all, ids_dev})
+                                     n_out, part_o, part_ml, counters, ws, logits_all, ids_dev,
+                                     y, key_global, logits_all_local})
     F(v);
+  if (logits_local != logits) F(logits_local);
   for (size_t l = 0; l < p_qkv.size(); ++l) {
     gemv_plan_free(&p_qkv[l]);
     gemv_plan_free(&p_wo[l]);
@@ -320,7 +395,7 @@ ifx_status KvCache::create(Model *model, size_t max_seq_len) {
   m = model;
   max_seq = max_seq_len;
   const ifx_config &c = m->cfg;
-  per_layer = (size_t)c.n_kv_heads * max_seq * c.head_dim;
+  per_layer = (size_t)m->Gl * max_seq * c.head_dim;  // this rank's kv heads
   IFX_CUDA(cudaSetDevice(m->device));
   IFX_TRY(dalloc(&k, per_layer * c.n_layers));
   IFX_TRY(dalloc(&v, per_layer * c.n_layers));
@@ -348,10 +423,10 @@ ifx_status KvCache::clear() {
 // ---------------------------------------------------------- decode step ---
 ifx_status Model::enqueue_decode(KvCache &kv, cudaStream_t st) {
   const ifx_config &c = cfg;
-  const bool pdl = true;
-  const int D = (int)c.hidden_size, H = (int)c.n_heads, G = (int)c.n_kv_heads, hd = (int)c.head_dim;
+  const bool pdl = tp == 1;  // NCCL work sits between the kernels under tensor parallelism
+  const int D = (int)c.hidden_size, H = (int)Hl, G = (int)Gl, hd = (int)c.head_dim;
   IFX_CUDA(launch(embed_kernel, dim3(8), dim3(256), 0, st, pdl, (const uint8_t *)emb_raw, emb_type,
-                  D, (const uint32_t *)next_token, x, logits, (int)c.vocab_size, qkv, qkv_n));
+                  D, (const uint32_t *)next_token, x, logits_local, (int)Vl, qkv, qkv_n));
   for (uint64_t l = 0; l < c.n_layers; ++l) {
     IFX_TRY(gemv_launch(p_qkv[l], st, pdl));
     DecodeAttnArgs a{};
@@ -364,7 +439,7 @@ ifx_status Model::enqueue_decode(KvCache &kv, cudaStream_t st) {
     a.counters = counters;
     a.attn_out = attn;
     a.zero_ptr = gu;
-    a.zero_n = (int)(2 * c.intermediate_size);
+    a.zero_n = (int)(2 * Fl);
     a.H = H;
     a.G = G;
     a.hd = hd;
@@ -375,14 +450,60 @@ ifx_status Model::enqueue_decode(KvCache &kv, cudaStream_t st) {
     a.rope_base = c.rope_base;
     a.err = err;
     IFX_TRY(decode_attention(a, st, pdl));
-    IFX_TRY(gemv_launch(p_wo[l], st, pdl));
-    IFX_TRY(gemv_launch(p_w13[l], st, pdl));
-    IFX_TRY(gemv_launch(p_w2[l], st, pdl));
+    if (tp > 1) {
+      IFX_TRY(tp_partial_begin(D, st));
+      IFX_TRY(gemv_launch(p_wo[l], st, pdl));
+      IFX_TRY(tp_partial_end(D, st));
+      IFX_TRY(gemv_launch(p_w13[l], st, pdl));
+      IFX_TRY(tp_partial_begin(D, st));
+      IFX_TRY(gemv_launch(p_w2[l], st, pdl));
+      IFX_TRY(tp_partial_end(D, st));
+    } else {
+      IFX_TRY(gemv_launch(p_wo[l], st, pdl));
+      IFX_TRY(gemv_launch(p_w13[l], st, pdl));
+      IFX_TRY(gemv_launch(p_w2[l], st, pdl));
+    }
   }
   IFX_TRY(gemv_launch(p_logits, st, pdl));
-  IFX_CUDA(launch(argmax_step_kernel, dim3(kNumSMs), dim3(256), 0, st, pdl, (const float *)logits,
-                  (int)c.vocab_size, amax_key, amax_count, next_token, kv.tokens, n_out, kv.pos, 1, 1));
+  if (tp > 1) {
+    // the argmax of this rank's vocab slice as a 64-bit key, the maximum
+    // over ranks (ties go to the highest global index), then the token
+    const NcclApi *N = nccl;
+    IFX_CUDA(launch(argmax_step_kernel, dim3(kNumSMs), dim3(256), 0, st, false,
+                    (const float *)logits_local, (int)Vl, amax_key, amax_count, next_token,
+                    kv.tokens, n_out, kv.pos, 0, 0, (int)v0, 0));
+    IFX_NCCL(N, N->AllReduce(amax_key, key_global, 1, ncclUint64, ncclMax, (ncclComm_t)comm, st));
+    token_publish_kernel<<<1, 1, 0, st>>>(key_global, amax_key, next_token, kv.tokens, n_out,
+                                          kv.pos, 1, 1);
+    IFX_CUDA(cudaGetLastError());
+    IFX_NCCL(N, N->AllGather(logits_local, logits, Vl, ncclFloat32, (ncclComm_t)comm, st));
+  } else {
+    IFX_CUDA(launch(argmax_step_kernel, dim3(kNumSMs), dim3(256), 0, st, pdl, (const float *)logits,
+                    (int)c.vocab_size, amax_key, amax_count, next_token, kv.tokens, n_out, kv.pos, 1,
+                    1, 0, 1));
+  }
   (void)D;
+  return IFX_OK;
+}
+
+// Row-parallel layers under tensor parallelism: the partial buffer starts as
+// the residual on rank 0 and as zeros elsewhere, the layer accumulates its
+// slice into it, and the all-reduce leaves the full sum (residual + layer
+// output) in x on every rank.
+ifx_status Model::tp_partial_begin(size_t n, cudaStream_t st, float *part, const float *resid) {
+  if (!part) part = y;
+  if (!resid) resid = x;
+  if (rank == 0)
+    IFX_CUDA(cudaMemcpyAsync(part, resid, n * sizeof(float), cudaMemcpyDeviceToDevice, st));
+  else
+    IFX_CUDA(cudaMemsetAsync(part, 0, n * sizeof(float), st));
+  return IFX_OK;
+}
+
+ifx_status Model::tp_partial_end(size_t n, cudaStream_t st, const float *part, float *out) {
+  if (!part) part = y;
+  if (!out) out = x;
+  IFX_NCCL(nccl, nccl->AllReduce(part, out, n, ncclFloat32, ncclSum, (ncclComm_t)comm, st));
   return IFX_OK;
 }
 
@@ -391,6 +512,7 @@ ifx_status Model::build_mega(KvCache &kv) {
   kv.mega_tried = true;
   const ifx_config &c = cfg;
   const int H = (int)c.n_heads, G = (int)c.n_kv_heads, hd = (int)c.head_dim;
+  if (tp > 1) return IFX_OK;  // the all-reduces run between the per-op kernels
   if (hd % 8 || hd > 256 || H % G || H / G > 8) return IFX_OK;  // separate kernels instead
   int dev_sms = 0;
   IFX_CUDA(cudaDeviceGetAttribute(&dev_sms, cudaDevAttrMultiProcessorCount, device));
@@ -524,10 +646,10 @@ ifx_status Model::ensure_ws(size_t n) {
   ws = nullptr;
   ids_dev = nullptr;
   const ifx_config &c = cfg;
-  const size_t D = c.hidden_size, Hh = c.n_heads * c.head_dim, kvd = c.n_kv_heads * c.head_dim;
-  const size_t F = c.intermediate_size;
+  const size_t D = c.hidden_size, Hh = Hl * c.head_dim, kvd = Gl * c.head_dim;
+  const size_t F = Fl;
   const size_t xf = gemm_xfrag_bytes((int64_t)n, (int64_t)std::max(D, F));
-  const size_t floats = n * (D + Hh + 2 * kvd + Hh + 2 * F);
+  const size_t floats = n * (D + Hh + 2 * kvd + Hh + 2 * F + (tp > 1 ? D : 0));
   IFX_CUDA(cudaMalloc(&ws, floats * sizeof(float) + xf + 1024));
   IFX_CUDA(cudaMalloc(&ids_dev, n * sizeof(uint32_t)));
   float *p = reinterpret_cast<float *>(ws);
@@ -538,6 +660,10 @@ ifx_status Model::ensure_ws(size_t n) {
   w_attn = p; p += n * Hh;
   w_gate = p; p += n * F;
   w_up = p; p += n * F;
+  if (tp > 1) {
+    w_y = p;
+    p += n * D;
+  }
   w_xf = reinterpret_cast<uint8_t *>(reinterpret_cast<uintptr_t>(p + 64) & ~(uintptr_t)255);
   ws_tokens = n;
   return IFX_OK;
@@ -555,8 +681,8 @@ ifx_status Model::prefill(KvCache &kv, const uint32_t *ids, size_t n, float *log
   IFX_TRY(ensure_ws(n));
   cudaStream_t st = stream;
   const int64_t N = (int64_t)n;
-  const int D = (int)c.hidden_size, H = (int)c.n_heads, G = (int)c.n_kv_heads, hd = (int)c.head_dim;
-  const int F = (int)c.intermediate_size;
+  const int D = (int)c.hidden_size, H = (int)Hl, G = (int)Gl, hd = (int)c.head_dim;
+  const int F = (int)Fl;
   const int Hh = H * hd, kvd = G * hd;
   const int start = (int)kv.len;
   IFX_CUDA(cudaMemcpyAsync(ids_dev, ids, n * sizeof(uint32_t), cudaMemcpyHostToDevice, st));
@@ -578,23 +704,38 @@ ifx_status Model::prefill(KvCache &kv, const uint32_t *ids, size_t n, float *log
     PrefillAttnArgs pa{w_q, w_k, w_v, w_attn, (int)n, H, G, hd};
     IFX_TRY(prefill_attention(pa, st));
     IFX_TRY(gemm_stage_x(w_attn, nullptr, nullptr, 0.f, GX_PLAIN, N, Hh, w_xf, st));
-    IFX_TRY(gemm_run(L.wo, w_xf, N, w_x, D, 1, err, st));
+    if (tp > 1) {
+      IFX_TRY(tp_partial_begin((size_t)N * D, st, w_y, w_x));
+      IFX_TRY(gemm_run(L.wo, w_xf, N, w_y, D, 1, err, st));
+      IFX_TRY(tp_partial_end((size_t)N * D, st, w_y, w_x));
+    } else {
+      IFX_TRY(gemm_run(L.wo, w_xf, N, w_x, D, 1, err, st));
+    }
     IFX_TRY(gemm_stage_x(w_x, nullptr, L.ffn_norm, c.norm_eps, GX_RMSNORM, N, D, w_xf, st));
     IFX_TRY(gemm_run(L.w1, w_xf, N, w_gate, F, 0, err, st));
     IFX_TRY(gemm_run(L.w3, w_xf, N, w_up, F, 0, err, st));
     IFX_TRY(gemm_stage_x(w_gate, w_up, nullptr, 0.f, GX_SWIGLU, N, F, w_xf, st));
-    IFX_TRY(gemm_run(L.w2, w_xf, N, w_x, D, 1, err, st));
+    if (tp > 1) {
+      IFX_TRY(tp_partial_begin((size_t)N * D, st, w_y, w_x));
+      IFX_TRY(gemm_run(L.w2, w_xf, N, w_y, D, 1, err, st));
+      IFX_TRY(tp_partial_end((size_t)N * D, st, w_y, w_x));
+    } else {
+      IFX_TRY(gemm_run(L.w2, w_xf, N, w_x, D, 1, err, st));
+    }
   }
   add_int_kernel<<<1, 1, 0, st>>>(kv.pos, (int)n);  // forward.rs:520
   IFX_CUDA(cudaGetLastError());
   if (last_row_only || !logits_host) {
-    // logits of the last row into the decode logits buffer (GEMV)
-    IFX_CUDA(cudaMemsetAsync(logits, 0, c.vocab_size * sizeof(float), st));
+    // logits of the last row into the decode logits buffer (GEMV; under
+    // tensor parallelism this rank's vocab slice, then gathered)
+    IFX_CUDA(cudaMemsetAsync(logits_local, 0, Vl * sizeof(float), st));
     GemvPlan p = p_logits;
     const QMatrix *mo[1] = {&out_w};
-    float *yo[1] = {logits};
+    float *yo[1] = {logits_local};
     gemv_plan_rebind(&p, mo, yo, w_x + (size_t)(n - 1) * D, nullptr, out_norm);
     IFX_TRY(gemv_launch(p, st, false));
+    if (tp > 1)
+      IFX_NCCL(nccl, nccl->AllGather(logits_local, logits, Vl, ncclFloat32, (ncclComm_t)comm, st));
     if (logits_host)
       IFX_CUDA(cudaMemcpyAsync(logits_host, logits, c.vocab_size * sizeof(float),
                                cudaMemcpyDeviceToHost, st));
@@ -607,7 +748,23 @@ ifx_status Model::prefill(KvCache &kv, const uint32_t *ids, size_t n, float *log
       logits_all_n = need;
     }
     IFX_TRY(gemm_stage_x(w_x, nullptr, out_norm, c.norm_eps, GX_RMSNORM, N, D, w_xf, st));
-    IFX_TRY(gemm_run(out_w, w_xf, N, logits_all, c.vocab_size, 0, err, st));
+    if (tp > 1) {
+      // [n][Vl] per rank, gathered rank-major, then interleaved to [n][V]
+      const size_t loc = n * Vl;
+      if (2 * loc * tp > logits_all_local_n) {
+        if (logits_all_local) cudaFree(logits_all_local);
+        logits_all_local = nullptr;
+        IFX_CUDA(cudaMalloc(&logits_all_local, 2 * loc * tp * sizeof(float)));
+        logits_all_local_n = 2 * loc * tp;
+      }
+      float *mine = logits_all_local, *gathered = logits_all_local + loc * tp;
+      IFX_TRY(gemm_run(out_w, w_xf, N, mine, (int)Vl, 0, err, st));
+      IFX_NCCL(nccl, nccl->AllGather(mine, gathered, loc, ncclFloat32, (ncclComm_t)comm, st));
+      shard_interleave_kernel<<<(unsigned)n, 256, 0, st>>>(gathered, logits_all, (int)n, (int)Vl, tp);
+      IFX_CUDA(cudaGetLastError());
+    } else {
+      IFX_TRY(gemm_run(out_w, w_xf, N, logits_all, c.vocab_size, 0, err, st));
+    }
     IFX_CUDA(cudaMemcpyAsync(logits_host, logits_all, need * sizeof(float), cudaMemcpyDeviceToHost, st));
     // keep the last row as "the model's last logits" for ifx_sample
     IFX_CUDA(cudaMemcpyAsync(logits, logits_all + (n - 1) * c.vocab_size,
@@ -628,7 +785,8 @@ ifx_status Model::generate(KvCache &kv, const uint32_t *prompt, size_t n_prompt,
   cudaStream_t st = stream;
   IFX_CUDA(cudaMemsetAsync(n_out, 0, sizeof(int), st));
   IFX_CUDA(launch(argmax_step_kernel, dim3(kNumSMs), dim3(256), 0, st, false, (const float *)logits,
-                  (int)cfg.vocab_size, amax_key, amax_count, next_token, kv.tokens, n_out, kv.pos, 1, 0));
+                  (int)cfg.vocab_size, amax_key, amax_count, next_token, kv.tokens, n_out, kv.pos, 1, 0,
+                  0, 1));
   for (size_t i = 0; i < max_tokens; ++i) IFX_TRY(run_decode(kv));
   if (max_tokens)
     IFX_CUDA(cudaMemcpyAsync(out, kv.tokens, max_tokens * sizeof(uint32_t), cudaMemcpyDeviceToHost, st));
@@ -705,8 +863,8 @@ ifx_status Model::bench_kernel(KvCache &kv, const std::string &which, int reps, 
         a.part_ml = part_ml;
         a.counters = counters;
         a.attn_out = attn;
-        a.H = (int)cfg.n_heads;
-        a.G = (int)cfg.n_kv_heads;
+        a.H = (int)Hl;
+        a.G = (int)Gl;
         a.hd = (int)cfg.head_dim;
         a.max_seq = (int)kv.max_seq;
         a.ns = ns;
@@ -715,7 +873,7 @@ ifx_status Model::bench_kernel(KvCache &kv, const std::string &which, int reps, 
         a.rope_base = cfg.rope_base;
         a.err = err;
         IFX_TRY(decode_attention(a, st, false));
-        b += 2ull * cfg.n_kv_heads * (kv.len + 1) * cfg.head_dim * sizeof(__half);
+        b += 2ull * Gl * (kv.len + 1) * cfg.head_dim * sizeof(__half);
       }
     }
   }
@@ -732,7 +890,7 @@ ifx_status Model::bench_kernel(KvCache &kv, const std::string &which, int reps, 
 
 ifx_status Model::kv_read(const KvCache &kv, size_t layer, int which_v, float *out_host) {
   if (layer >= cfg.n_layers) return fail(IFX_ERR_INVALID_TENSOR_INDEX, "layer out of range");
-  const int G = (int)cfg.n_kv_heads, hd = (int)cfg.head_dim;
+  const int G = (int)Gl, hd = (int)cfg.head_dim;
   if (kv.len == 0) return IFX_OK;
   float *tmp = nullptr;
   IFX_CUDA(cudaMalloc(&tmp, kv.len * G * hd * sizeof(float)));

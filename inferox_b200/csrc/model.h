@@ -38,7 +38,18 @@ struct KvCache {  // KvCache (src/model/cache.rs:7-14), f16 on the device
 struct Model {
   int device = -1;
   ifx_load_opts opts{};
-  ifx_config cfg{};
+  ifx_config cfg{};  // the checkpoint's (global) config
+  // tensor parallelism: this rank's share of the heads, FFN rows and vocab
+  int tp = 1, rank = 0;
+  void *comm = nullptr;  // ncclComm_t, owned by the caller
+  const struct NcclApi *nccl = nullptr;
+  uint64_t Hl = 0, Gl = 0, Fl = 0, Vl = 0, v0 = 0;
+  float *y = nullptr;               // partial sums of the row-parallel layers
+  float *logits_local = nullptr;    // this rank's vocab slice (== logits at tp 1)
+  unsigned long long *key_global = nullptr;
+  float *w_y = nullptr;             // prefill partial sums [n][D]
+  float *logits_all_local = nullptr;
+  size_t logits_all_local_n = 0;
   cudaStream_t stream = nullptr;
   std::vector<Layer> layers;
   QMatrix out_w;
@@ -82,6 +93,10 @@ struct Model {
   ifx_status bench_kernel(KvCache &kv, const std::string &which, int reps, float *ms,
                           uint64_t *bytes);
   ifx_status ensure_ws(size_t n);
+  ifx_status tp_partial_begin(size_t n, cudaStream_t st, float *part = nullptr,
+                              const float *resid = nullptr);
+  ifx_status tp_partial_end(size_t n, cudaStream_t st, const float *part = nullptr,
+                            float *out = nullptr);
   ifx_status check_err();
   ~Model();
 };

@@ -1,0 +1,99 @@
+"""Tensor-parallel decode and prefill on two GPUs against the CPU oracle.
+
+Two spawned ranks, each on its own GPU, load the same synthetic GGUF with
+tp_size 2 through a communicator made by the library (ifx_tp_unique_id /
+ifx_tp_comm_create), run a prefill and greedy decode steps, and hand their
+(all-gathered, hence full) logits to the parent, which holds them to the
+oracle at the parity bar and to each other bit for bit. The ranks do no
+checking themselves, so neither can leave the other waiting in a
+collective; the parent kills both if they do not report in time. Skipped
+with fewer than two GPUs.
+"""
+import os
+
+import numpy as np
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+from inferox_b200 import synth, tp
+from oracle import refcpu as R
+
+pytestmark = pytest.mark.gpu
+
+ATOL, RTOL = 2e-2, 1e-2
+R.set_threads(os.cpu_count() or 8)
+
+
+def _rank(rank, world, uid, g, prompt, steps, q):
+    try:
+        os.environ["NCCL_NVLS_ENABLE"] = "0"
+        from inferox_b200 import Model
+        comm = tp.Comm(uid, world, rank, rank)
+        m = Model.from_bytes(g, device=rank, tp_size=world, tp_rank=rank, nccl_comm=comm.handle)
+        kv = m.kv_cache(128)
+        out = {"prefill_last": m.prefill(prompt, kv, True)[0]}
+        out["prefill_all"] = m.prefill(prompt, m.kv_cache(128), False)
+        logs = []
+        for t in steps:
+            logs.append(m.decode_step(int(t), kv))
+        out["decode"] = np.stack(logs)
+        toks, _ = m.decode_greedy(int(steps[-1]), 6, kv)
+        out["greedy"] = toks
+        out["kernels"] = kv.decode_kernels()
+        del kv, m
+        comm.close()
+        q.put((rank, out))
+    except Exception as e:
+        q.put((rank, repr(e)))
+
+
+def _close(a, b):
+    return np.all(np.abs(a - b) <= ATOL + RTOL * np.abs(b))
+
+
+@pytest.mark.parametrize("mix", [1, 0])  # Q4_K_M mix; all Q8_0
+def test_tp2_matches_oracle(mix):
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    g = synth.build(None, vocab=2048, dim=512, n_layers=2, n_heads=8, n_kv_heads=2, ffn=1024,
+                    context=128, rope_base=500000.0, mix=mix, seed=21)
+    prompt = synth.prompt_ids(2048, 10, seed=3)
+    o = R.Model(g)
+    okv = o.kv_cache(2, 128)
+    ref_last = o.prefill(prompt, okv, True)[0]
+    ref_all = o.prefill(prompt, o.kv_cache(2, 128), False)
+    steps = [int(R.argmax(ref_last))]
+    ref_dec = []
+    for _ in range(4):
+        r = o.decode_step(steps[-1], okv)
+        ref_dec.append(r)
+        steps.append(int(R.argmax(r)))
+    steps = steps[:4]
+    uid = tp.unique_id()
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_rank, args=(r, 2, uid, g, prompt, steps, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = {}
+    try:
+        for _ in procs:
+            r, out = q.get(timeout=240)
+            res[r] = out
+    finally:
+        for p in procs:
+            p.join(timeout=30)
+            if p.is_alive():
+                p.kill()
+    for r in (0, 1):
+        assert isinstance(res.get(r), dict), res.get(r)
+    a, b = res[0], res[1]
+    for k in ("prefill_last", "prefill_all", "decode"):
+        assert np.array_equal(a[k], b[k]), k  # gathered logits are the same on both ranks
+    assert _close(a["prefill_last"], ref_last), float(np.max(np.abs(a["prefill_last"] - ref_last)))
+    assert _close(a["prefill_all"], ref_all), float(np.max(np.abs(a["prefill_all"] - ref_all)))
+    for i, r in enumerate(ref_dec):
+        assert _close(a["decode"][i], r), (i, float(np.max(np.abs(a["decode"][i] - r))))
+    assert np.array_equal(a["greedy"], b["greedy"])
+    assert a["kernels"] == 3 + 5 * 2  # per-op kernels with the collectives between them
