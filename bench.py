@@ -155,19 +155,31 @@ def run_ours(args):
                                  device_id=torch.device("cuda", local))
         dist = dist_
 
-    from inferox_b200 import Model, synth
+    from inferox_b200 import Model, synth, tp
 
+    # several GPUs: tensor parallelism over all of them (one sequence, the
+    # weights split N ways) unless --replicas asks for one sequence per GPU
+    tp_mode = world > 1 and not args.replicas
+    comm = None
     t0 = time.time()
     g = synth.build(CONFIG, **({"n_layers": args.layers} if args.layers else {}))
     t_gen = time.time() - t0
     t0 = time.time()
-    m = Model.from_bytes(g, device=local)
+    if tp_mode:
+        uid = torch.zeros(128, dtype=torch.uint8, device="cuda")
+        if rank == 0:
+            uid.copy_(torch.frombuffer(bytearray(tp.unique_id()), dtype=torch.uint8))
+        dist.broadcast(uid, 0)
+        comm = tp.Comm(bytes(uid.cpu().numpy()), world, rank, local)
+        m = Model.from_bytes(g, device=local, tp_size=world, tp_rank=rank, nccl_comm=comm.handle)
+    else:
+        m = Model.from_bytes(g, device=local)
     t_load = time.time() - t0
     cfg = m.config
     L, G, hd, V = int(cfg.n_layers), int(cfg.n_kv_heads), int(cfg.head_dim), int(cfg.vocab_size)
     max_seq = PROMPT + 2 * (args.warmup + args.steps) + 16
     kv = m.kv_cache(max_seq)
-    prompt = synth.prompt_ids(V, PROMPT, seq_index=rank)
+    prompt = synth.prompt_ids(V, PROMPT, seq_index=0 if tp_mode else rank)
 
     # prefill: one untimed pass, then a timed one (wall clock around a
     # synchronous call; the prefill is a single device-bound call)
@@ -193,7 +205,8 @@ def run_ours(args):
         t = torch.tensor([ms_step], device="cuda")
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms_step = float(t.item())
-    value = world * 1000.0 / ms_step
+    seqs = 1 if tp_mode else world  # sequences decoded per step by the whole job
+    value = seqs * 1000.0 / ms_step
 
     # end to end through the reference-facing call: ifx_decode_step with the
     # token from host memory and the logits copied back to host every step
@@ -206,7 +219,7 @@ def run_ours(args):
         lg = m.decode_step(tok, kv, want_logits=True)
         tok = int(lg.argmax())
     e2e_s = time.perf_counter() - te
-    e2e = {"value": world * e2e_steps / e2e_s, "unit": "tok/s", "h2d_bytes_per_step": 4,
+    e2e = {"value": seqs * e2e_steps / e2e_s, "unit": "tok/s", "h2d_bytes_per_step": 4,
            "d2h_bytes_per_step": V * 4}
 
     # per-kernel figures of the per-op path (each fused kernel timed alone,
@@ -219,14 +232,23 @@ def run_ours(args):
         kern[which] = {"ms": ms, "bytes": b, "gbs": b / (ms * 1e-3) / 1e9}
     # whole-step algorithmic bytes: every weight once + K/V at the mean context
     ctx_mean = ctx0 + args.steps / 2
-    kv_bytes = 2 * L * G * hd * 2 * ctx_mean
+    # per GPU: under tensor parallelism each rank reads its shard of the
+    # weights (decode_weight_bytes is this rank's) and its kv heads
+    kv_bytes = 2 * L * (G // world if tp_mode else G) * hd * 2 * ctx_mean
     step_bytes = m.decode_weight_bytes() + kv_bytes
     step_gbs = step_bytes / (ms_step * 1e-3) / 1e9
 
-    if rank != 0:
+    def finish():
+        nonlocal m, kv
+        del kv, m  # the cache's CUDA graph holds NCCL work: release it first
+        if comm:
+            comm.close()
         if dist:
             dist.barrier()
             dist.destroy_process_group()
+
+    if rank != 0:
+        finish()
         return
     base = None
     if world == 1 and not args.no_cpu_baseline:
@@ -234,12 +256,14 @@ def run_ours(args):
     line = {
         "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "q4_k/q6_k weights, f16 tensor-core math, f32 accumulate",
+        "scaling": "strong" if tp_mode else "weak", "vs_baseline": None,
+        "dtype": "q4_k/q6_k weights, f16 tensor-core math, f32 accumulate",
         "data": "synthetic (seeded N(0,0.02) weights quantised Q4_K_M; seeded uniform prompt ids)",
         "config": {"workload": "llama3-8b-shaped Q4_K_M: 1024-token prompt prefill, then batch-1 greedy decode"
                                + (f" (profiling case: {L} layers)" if args.layers else ""),
-                   "model": "llama-3-8b-shaped", "global_batch": world, "seq_len": PROMPT,
-                   "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
+                   "model": "llama-3-8b-shaped", "global_batch": seqs, "seq_len": PROMPT,
+                   "parallelism": (f"tp{world} (NCCL all-reduce after Wo and W2)" if tp_mode
+                                   else f"replicas x{world}" if world > 1 else "single GPU"),
                    "l2": "no flush needed: 4.6 GB of weights per step >> 126 MB L2"},
         "hbm_roofline": {"bytes_per_step": step_bytes, "achieved_gbs": step_gbs, "peak_gbs": hbm,
                          "frac": step_gbs / hbm, "peak": peak_kind,
@@ -261,9 +285,7 @@ def run_ours(args):
         "setup_s": {"synth": t_gen, "load": t_load},
     }
     print(json.dumps(line), flush=True)
-    if dist:
-        dist.barrier()
-        dist.destroy_process_group()
+    finish()
 
 
 def main():
@@ -273,6 +295,9 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--replicas", action="store_true",
+                    help="with several GPUs: one independent sequence per GPU instead of "
+                         "tensor parallelism over all of them")
     ap.add_argument("--layers", type=int, default=0,
                     help="profiling only: an 8B-shaped model with this many layers "
                          "(0 = the full 32); the line's config names it")
