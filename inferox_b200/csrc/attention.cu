@@ -319,7 +319,177 @@ ifx_status decode_attention(const DecodeAttnArgs &a, cudaStream_t st, bool pdl) 
   return IFX_OK;
 }
 
+// Prefill attention on tensor cores (flash-attention style): a CTA takes one
+// query head and 64 query rows (4 warps x 16), streams 64-key blocks of K
+// and V (f32 from the prefill workspace, converted to f16 into shared
+// memory; V transposed), computes S = Q K^T with mma.m16n8k16 (f16 in, f32
+// accumulate), applies the causal chunk mask (key <= query row, keys of this
+// chunk only: forward.rs:266-274), keeps an online softmax per row in
+// registers and accumulates O += P V with P re-used from the S fragments.
+constexpr int kTQ = 64;  // query rows per CTA
+constexpr int kTK = 64;  // keys per block
+
+__device__ __forceinline__ uint32_t pack_h2(float x, float y) {
+  __half2 h = __floats2half2_rn(x, y);
+  return *reinterpret_cast<uint32_t *>(&h);
+}
+
+template <int HD>
+__global__ void __launch_bounds__(128) prefill_attn_tc_kernel(PrefillAttnArgs a) {
+  constexpr int KS = HD + 8;   // K row stride (halves): the 8 rows a fragment load touches
+  constexpr int VS = kTK + 8;  // Vt row stride             fall on distinct banks
+  extern __shared__ __align__(16) __half smh[];
+  __half *Ks = smh;             // [kTK][KS]
+  __half *Vt = smh + kTK * KS;  // [HD][VS]
+  const int hq = blockIdx.x, qb = blockIdx.y, tid = threadIdx.x;
+  const int warp = tid >> 5, lane = tid & 31, g = lane >> 2, c = lane & 3;
+  const int grp = a.H / a.G, hk = hq / grp;
+  const int qstride = a.H * HD, kstride = a.G * HD;
+  const int r0 = qb * kTQ;
+  const int row_a = r0 + warp * 16 + g, row_b = row_a + 8;
+  const bool va = row_a < a.n, vb = row_b < a.n;
+  // this warp's 16 query rows as A fragments (row-major 16 x HD)
+  uint32_t qa[HD / 16][4];
+  {
+    const float *qra = a.q + (size_t)(va ? row_a : 0) * qstride + hq * HD;
+    const float *qrb = a.q + (size_t)(vb ? row_b : 0) * qstride + hq * HD;
+#pragma unroll
+    for (int ks = 0; ks < HD / 16; ++ks) {
+      const int d0 = ks * 16 + 2 * c;
+      const float2 x0 = va ? *reinterpret_cast<const float2 *>(qra + d0) : make_float2(0.f, 0.f);
+      const float2 x1 = vb ? *reinterpret_cast<const float2 *>(qrb + d0) : make_float2(0.f, 0.f);
+      const float2 x2 = va ? *reinterpret_cast<const float2 *>(qra + d0 + 8) : make_float2(0.f, 0.f);
+      const float2 x3 = vb ? *reinterpret_cast<const float2 *>(qrb + d0 + 8) : make_float2(0.f, 0.f);
+      qa[ks][0] = pack_h2(x0.x, x0.y);
+      qa[ks][1] = pack_h2(x1.x, x1.y);
+      qa[ks][2] = pack_h2(x2.x, x2.y);
+      qa[ks][3] = pack_h2(x3.x, x3.y);
+    }
+  }
+  float o[HD / 8][4];
+#pragma unroll
+  for (int nt = 0; nt < HD / 8; ++nt) o[nt][0] = o[nt][1] = o[nt][2] = o[nt][3] = 0.f;
+  float m_a = -INFINITY, m_b = -INFINITY, l_a = 0.f, l_b = 0.f;
+  const float scale = 1.0f / sqrtf((float)HD);
+  const int kend = min(a.n, r0 + kTQ);  // causal: no key beyond the block's last row
+  for (int kb = 0; kb < kend; kb += kTK) {  // kb <= r0: every row has a key per block
+    __syncthreads();  // the previous block's K/V are no longer read
+    for (int e = tid; e < kTK * HD / 4; e += 128) {
+      const int t = e / (HD / 4), d = (e % (HD / 4)) * 4;
+      float4 kv = make_float4(0.f, 0.f, 0.f, 0.f), vv = kv;
+      if (kb + t < a.n) {
+        kv = *reinterpret_cast<const float4 *>(a.k + (size_t)(kb + t) * kstride + hk * HD + d);
+        vv = *reinterpret_cast<const float4 *>(a.v + (size_t)(kb + t) * kstride + hk * HD + d);
+      }
+      *reinterpret_cast<uint2 *>(Ks + t * KS + d) = make_uint2(pack_h2(kv.x, kv.y), pack_h2(kv.z, kv.w));
+      Vt[(d + 0) * VS + t] = __float2half_rn(vv.x);
+      Vt[(d + 1) * VS + t] = __float2half_rn(vv.y);
+      Vt[(d + 2) * VS + t] = __float2half_rn(vv.z);
+      Vt[(d + 3) * VS + t] = __float2half_rn(vv.w);
+    }
+    __syncthreads();
+    float sv[kTK / 8][4];
+#pragma unroll
+    for (int nt = 0; nt < kTK / 8; ++nt) {
+      sv[nt][0] = sv[nt][1] = sv[nt][2] = sv[nt][3] = 0.f;
+      const __half *kr = Ks + (nt * 8 + g) * KS + 2 * c;
+#pragma unroll
+      for (int ks = 0; ks < HD / 16; ++ks) {
+        const uint32_t b0 = *reinterpret_cast<const uint32_t *>(kr + ks * 16);
+        const uint32_t b1 = *reinterpret_cast<const uint32_t *>(kr + ks * 16 + 8);
+        mma_16816(sv[nt], qa[ks][0], qa[ks][1], qa[ks][2], qa[ks][3], b0, b1, sv[nt]);
+      }
+    }
+    float mx_a = -INFINITY, mx_b = -INFINITY;
+#pragma unroll
+    for (int nt = 0; nt < kTK / 8; ++nt)
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        const int key = kb + nt * 8 + 2 * c + j;
+        const bool kin = key < a.n;
+        sv[nt][j] = (kin && key <= row_a) ? sv[nt][j] * scale : -INFINITY;
+        sv[nt][2 + j] = (kin && key <= row_b) ? sv[nt][2 + j] * scale : -INFINITY;
+        mx_a = fmaxf(mx_a, sv[nt][j]);
+        mx_b = fmaxf(mx_b, sv[nt][2 + j]);
+      }
+    mx_a = fmaxf(mx_a, __shfl_xor_sync(0xffffffffu, mx_a, 1));
+    mx_a = fmaxf(mx_a, __shfl_xor_sync(0xffffffffu, mx_a, 2));
+    mx_b = fmaxf(mx_b, __shfl_xor_sync(0xffffffffu, mx_b, 1));
+    mx_b = fmaxf(mx_b, __shfl_xor_sync(0xffffffffu, mx_b, 2));
+    const float mn_a = fmaxf(m_a, mx_a), mn_b = fmaxf(m_b, mx_b);
+    const float al_a = mn_a == -INFINITY ? 1.f : expf(m_a - mn_a);
+    const float al_b = mn_b == -INFINITY ? 1.f : expf(m_b - mn_b);
+    m_a = mn_a;
+    m_b = mn_b;
+    l_a *= al_a;
+    l_b *= al_b;
+#pragma unroll
+    for (int nt = 0; nt < HD / 8; ++nt) {
+      o[nt][0] *= al_a;
+      o[nt][1] *= al_a;
+      o[nt][2] *= al_b;
+      o[nt][3] *= al_b;
+    }
+#pragma unroll
+    for (int nt = 0; nt < kTK / 8; ++nt)
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        const float pa = sv[nt][j] == -INFINITY ? 0.f : expf(sv[nt][j] - mn_a);
+        const float pb = sv[nt][2 + j] == -INFINITY ? 0.f : expf(sv[nt][2 + j] - mn_b);
+        sv[nt][j] = pa;
+        sv[nt][2 + j] = pb;
+        l_a += pa;
+        l_b += pb;
+      }
+#pragma unroll
+    for (int k2 = 0; k2 < kTK / 16; ++k2) {
+      const uint32_t p0 = pack_h2(sv[2 * k2][0], sv[2 * k2][1]);
+      const uint32_t p1 = pack_h2(sv[2 * k2][2], sv[2 * k2][3]);
+      const uint32_t p2 = pack_h2(sv[2 * k2 + 1][0], sv[2 * k2 + 1][1]);
+      const uint32_t p3 = pack_h2(sv[2 * k2 + 1][2], sv[2 * k2 + 1][3]);
+#pragma unroll
+      for (int nt = 0; nt < HD / 8; ++nt) {
+        const __half *vr = Vt + (nt * 8 + g) * VS + k2 * 16 + 2 * c;
+        const uint32_t b0 = *reinterpret_cast<const uint32_t *>(vr);
+        const uint32_t b1 = *reinterpret_cast<const uint32_t *>(vr + 8);
+        mma_16816(o[nt], p0, p1, p2, p3, b0, b1, o[nt]);
+      }
+    }
+  }
+  l_a += __shfl_xor_sync(0xffffffffu, l_a, 1);
+  l_a += __shfl_xor_sync(0xffffffffu, l_a, 2);
+  l_b += __shfl_xor_sync(0xffffffffu, l_b, 1);
+  l_b += __shfl_xor_sync(0xffffffffu, l_b, 2);
+  const float ia = 1.0f / l_a, ib = 1.0f / l_b;
+#pragma unroll
+  for (int nt = 0; nt < HD / 8; ++nt) {
+    const int d = nt * 8 + 2 * c;
+    if (va)
+      *reinterpret_cast<float2 *>(a.out + (size_t)row_a * qstride + hq * HD + d) =
+          make_float2(o[nt][0] * ia, o[nt][1] * ia);
+    if (vb)
+      *reinterpret_cast<float2 *>(a.out + (size_t)row_b * qstride + hq * HD + d) =
+          make_float2(o[nt][2] * ib, o[nt][3] * ib);
+  }
+}
+
+template <int HD>
+static ifx_status launch_prefill_tc(const PrefillAttnArgs &a, cudaStream_t st) {
+  const size_t smem = (size_t)(kTK * (HD + 8) + HD * (kTK + 8)) * sizeof(__half);
+  dim3 grid(a.H, (a.n + kTQ - 1) / kTQ);
+  prefill_attn_tc_kernel<HD><<<grid, 128, smem, st>>>(a);
+  IFX_CUDA(cudaGetLastError());
+  return IFX_OK;
+}
+
 ifx_status prefill_attention(const PrefillAttnArgs &a, cudaStream_t st) {
+  switch (a.hd) {  // tensor-core path for the common head sizes
+    case 48: return launch_prefill_tc<48>(a, st);
+    case 64: return launch_prefill_tc<64>(a, st);
+    case 96: return launch_prefill_tc<96>(a, st);
+    case 128: return launch_prefill_tc<128>(a, st);
+    default: break;
+  }
   if (a.hd > 128 || (kPQ * a.hd) % 128) return fail(IFX_ERR_UNSUPPORTED, "prefill attention head_dim");
   const size_t smem =
       (size_t)(kPQ * a.hd + kPK * (a.hd + 1) + kPK * a.hd + kPQ * kPK + 3 * kPQ) * sizeof(float);
