@@ -439,7 +439,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) decode_mega_kernel(const __gr
         const int n = rg.y - rg.x;
         if (n > 0) {
           const bool full = n >= P.g.kunits;
-          float *s16 = reinterpret_cast<float *>(scr + (size_t)P.g.win_units * P.g.kc * 2);
+          float *s16 = reinterpret_cast<float *>(scr + (size_t)P.g.win_units * P.g.kc * 4);
           stage_x(P.g, rg.x, n, full, scr, s16);
           consumer_sync();
           // on a failed wait the warp carries on to the next grid barrier,
@@ -520,7 +520,7 @@ ifx_status mega_finalize(MegaPlan *plan, const std::vector<MegaPhase> &phases, i
   for (const MegaPhase &p : phases)
     if (p.kind == PH_GEMV) {
       slot = std::max<size_t>(slot, (size_t)p.g.slot_bytes);
-      size_t w = (size_t)p.g.win_units * (p.g.kc * 2 + p.g.kc / 16 * 4);
+      size_t w = (size_t)p.g.win_units * (p.g.kc * 4 + p.g.kc / 16 * 4);  // x hi + lo, sums
       win = std::max<size_t>(win, w);
     }
   // attention buffer (filled during the QKV phase) and staging area side by side

@@ -1,9 +1,13 @@
-// Prefill fused dequant GEMM, first version: the weight units of
-// qlayout.cuh and the staged activations stream through a shared-memory ring
-// with 1-D bulk async copies (producer warp, mbarriers); each consumer warp
-// dequantises its 16-row A fragments once per 16-column chunk (scales folded
-// in, f16) and reuses them across the 8 token n-tiles of the CTA's 64-token
-// block with mma.m16n8k16 (f32 accumulation).
+// Prefill fused dequant GEMM: the weight units of qlayout.cuh and the staged
+// activations stream through a shared-memory ring with 1-D bulk async copies
+// (producer warp, mbarriers). Each consumer warp turns its 16-row A fragments
+// into exact small integers in f16 (the quantised values, bias removed) once
+// per 16-column chunk and reuses them across the 8 token n-tiles of the
+// CTA's 64-token block with mma.m16n8k16. x is staged as two f16 planes
+// (x ~= hi + lo, about 22 bits), both multiplied into a per-scale-group f32
+// accumulator, and each group's scale (and Q4_K's min, through per-token
+// group sums of x) is applied in f32 — so the only rounding left is f32
+// accumulation order.
 #include <algorithm>
 
 #include "gemm.cuh"
@@ -13,7 +17,8 @@ namespace ifx {
 namespace {
 
 constexpr int kGThreads = 288;
-constexpr int kGStages = 3;
+constexpr int kGStages = 2;
+constexpr int kXChunkBytes = 4096;  // one 16-column chunk of a 64-token block, hi + lo planes
 
 __device__ __forceinline__ float silu_g(float v) {
   float c = fminf(fmaxf(v, -80.0f), 80.0f);
@@ -48,21 +53,32 @@ __global__ void stage_x_kernel(const float *X, const float *X2, const float *nor
   }
   const int64_t mb = t / kGemmTokens, tt = t % kGemmTokens;
   const int nt = (int)(tt / 8), g = (int)(tt % 8);
-  const int64_t nch = K / 16;
-  for (int64_t k = tid; k < K; k += blockDim.x) {
+  const int64_t nch = K / 16, ngr = K / 32;
+  float *sums = reinterpret_cast<float *>(out + (size_t)((M + kGemmTokens - 1) / kGemmTokens) *
+                                                    (size_t)nch * (kXChunkBytes / 2));
+  for (int64_t k0 = 0; k0 < K; k0 += blockDim.x) {  // blockDim.x % 32 == 0: a warp covers one group
+    const int64_t k = k0 + tid;
     float v = 0.f;
-    if (t < M) {
+    if (t < M && k < K) {
       if (mode == GX_RMSNORM) v = (X[t * K + k] * inv) * normw[k];
       else if (mode == GX_SWIGLU) v = silu_g(X[t * K + k]) * X2[t * K + k];
       else v = X[t * K + k];
     }
-    const int64_t ch = k / 16;
-    const int kk = (int)(k % 16);
-    // B fragment: b0 = (k 2c, 2c+1), b1 = (k 2c+8, 2c+9) of column g
-    const int c = (kk % 8) / 2, hi = kk / 8, e = kk % 2;
-    const int lane = g * 4 + c;
-    const int64_t idx = (((mb * nch + ch) * 8 + nt) * 32 + lane) * 4 + hi * 2 + e;
-    out[idx] = __float2half_rn(v);
+    const __half hv = __float2half_rn(v);
+    const __half lv = __float2half_rn(v - __half2float(hv));
+    float gs = __half2float(hv) + __half2float(lv);  // what the MMAs see
+    gs = warp_sum(gs);
+    if (k < K) {
+      const int64_t ch = k / 16;
+      const int kk = (int)(k % 16);
+      // B fragment: b0 = (k 2c, 2c+1), b1 = (k 2c+8, 2c+9) of column g
+      const int c = (kk % 8) / 2, hi = kk / 8, e = kk % 2;
+      const int lane = g * 4 + c;
+      const int64_t idx = ((((mb * nch + ch) * 2) * 8 + nt) * 32 + lane) * 4 + hi * 2 + e;
+      out[idx] = hv;
+      out[idx + 8 * 32 * 4] = lv;  // the lo plane follows the hi plane of the chunk
+      if ((tid & 31) == 0) sums[(mb * ngr + k / 32) * kGemmTokens + tt] = gs;
+    }
   }
 }
 
@@ -77,6 +93,7 @@ __device__ __forceinline__ uint32_t deq(uint32_t bits, __half2 sub, __half2 scal
 struct GemmArgs {
   const uint8_t *w;
   const uint8_t *x;   // staged fragments
+  const float *sums;  // per-token sums of x over 32-column groups
   float *C;
   int64_t ldc, M;
   int type, rows, kc, kunits, unit_bytes, wt_bytes, wt_qbytes, nch_total;
@@ -85,19 +102,71 @@ struct GemmArgs {
 };
 
 template <int TYPE>
-__device__ __forceinline__ void gemm_unit(const uint8_t *wt, const uint8_t *xs, int kc,
-                                          int wt_qbytes, int lane, float (&acc)[8][4]) {
+__device__ __forceinline__ void gemm_unit(const uint8_t *wt, const uint8_t *xs, const float *sx,
+                                          int kc, int wt_qbytes, int lane, float (&acc)[8][4]) {
   const int g = lane >> 2, c = lane & 3;
-  const int nch = kc / 16;
-  const __half2 magic1024 = __float2half2_rn(1024.f);
+  // chunks per scale group: Q6_K scales every 16 columns, the others every 32
+  constexpr int cpg = (TYPE == IFX_TYPE_Q6_K) ? 1 : 2;
+  const int ngr = kc / 16 / cpg;
+  const __half2 b1024 = __float2half2_rn(1024.f);
 #pragma unroll 1
-  for (int ch = 0; ch < nch; ++ch) {
-    uint32_t a[4];
+  for (int gi = 0; gi < ngr; ++gi) {
+    float tmp[8][4];
+#pragma unroll
+    for (int nt = 0; nt < 8; ++nt) tmp[nt][0] = tmp[nt][1] = tmp[nt][2] = tmp[nt][3] = 0.f;
+#pragma unroll
+    for (int cc = 0; cc < cpg; ++cc) {
+      const int ch = gi * cpg + cc;
+      // exact integer A fragments; rows g+8 come from the high nibble and
+      // carry a factor 16 (Q4_K, Q6_K, Q4_0), folded into their scale below
+      uint32_t a[4];
+      if (TYPE == IFX_TYPE_Q4_K) {
+        const uint32_t wd = reinterpret_cast<const uint32_t *>(wt)[((ch / 4) * 32 + lane) * 4 + ch % 4];
+        const uint32_t hi = wd >> 8;
+        a[0] = h2u(__hsub2(u2h((wd & 0x000F000Fu) | 0x64006400u), b1024));
+        a[1] = h2u(__hsub2(u2h((wd & 0x00F000F0u) | 0x64006400u), b1024));
+        a[2] = h2u(__hsub2(u2h((hi & 0x000F000Fu) | 0x64006400u), b1024));
+        a[3] = h2u(__hsub2(u2h((hi & 0x00F000F0u) | 0x64006400u), b1024));
+      } else if (TYPE == IFX_TYPE_Q6_K) {
+        const uint32_t wd = reinterpret_cast<const uint32_t *>(wt)[((ch / 4) * 32 + lane) * 4 + ch % 4];
+        const int t = ch / 2;
+        uint32_t H = reinterpret_cast<const uint32_t *>(wt + 2048)[((t / 4) * 32 + lane) * 4 + t % 4];
+        if (ch & 1) H >>= 8;
+        const __half2 sub0 = __float2half2_rn(1056.f), sub1 = __float2half2_rn(1536.f);
+        const uint32_t hi = wd >> 8, H4 = H >> 4;
+        a[0] = h2u(__hsub2(u2h((wd & 0x000F000Fu) | ((H & 0x00030003u) << 4) | 0x64006400u), sub0));
+        a[1] = h2u(__hsub2(u2h((wd & 0x00F000F0u) | ((H & 0x000C000Cu) << 6) | 0x64006400u), sub1));
+        a[2] = h2u(__hsub2(u2h((hi & 0x000F000Fu) | ((H4 & 0x00030003u) << 4) | 0x64006400u), sub0));
+        a[3] = h2u(__hsub2(u2h((hi & 0x00F000F0u) | ((H4 & 0x000C000Cu) << 6) | 0x64006400u), sub1));
+      } else if (TYPE == IFX_TYPE_Q4_0) {
+        const uint32_t wd = reinterpret_cast<const uint32_t *>(wt)[((ch / 4) * 32 + lane) * 4 + ch % 4];
+        const __half2 sub0 = __float2half2_rn(1032.f), sub1 = __float2half2_rn(1152.f);
+        const uint32_t hi = wd >> 8;
+        a[0] = h2u(__hsub2(u2h((wd & 0x000F000Fu) | 0x64006400u), sub0));
+        a[1] = h2u(__hsub2(u2h((wd & 0x00F000F0u) | 0x64006400u), sub1));
+        a[2] = h2u(__hsub2(u2h((hi & 0x000F000Fu) | 0x64006400u), sub0));
+        a[3] = h2u(__hsub2(u2h((hi & 0x00F000F0u) | 0x64006400u), sub1));
+      } else {  // Q8_0: bytes q + 128
+        const uint2 w2 = reinterpret_cast<const uint2 *>(wt)[((ch / 2) * 32 + lane) * 2 + ch % 2];
+        const __half2 sub = __float2half2_rn(1152.f);
+        a[0] = h2u(__hsub2(u2h(prmt(w2.x, 0x64646464u, 0x4140u)), sub));
+        a[1] = h2u(__hsub2(u2h(prmt(w2.x, 0x64646464u, 0x4342u)), sub));
+        a[2] = h2u(__hsub2(u2h(prmt(w2.y, 0x64646464u, 0x4140u)), sub));
+        a[3] = h2u(__hsub2(u2h(prmt(w2.y, 0x64646464u, 0x4342u)), sub));
+      }
+      const uint2 *xb = reinterpret_cast<const uint2 *>(xs + (size_t)ch * kXChunkBytes) + lane;
+#pragma unroll
+      for (int nt = 0; nt < 8; ++nt) {
+        const uint2 bh = xb[nt * 32], bl = xb[256 + nt * 32];
+        mma_16816(tmp[nt], a[0], a[1], a[2], a[3], bh.x, bh.y, tmp[nt]);
+        mma_16816(tmp[nt], a[0], a[1], a[2], a[3], bl.x, bl.y, tmp[nt]);
+      }
+    }
+    // this group's scales for rows g (sA) and g+8 (sB), f32
+    float sA, sB, mA = 0.f, mB = 0.f;
     if (TYPE == IFX_TYPE_Q4_K) {
-      const uint32_t wd = reinterpret_cast<const uint32_t *>(wt)[((ch / 4) * 32 + lane) * 4 + ch % 4];
       const uint8_t *hdr = wt + 2048;
-      const int grp = ch / 2;
-      __half2 sg[2], mg[2];
+      float sc2[2], mn2[2];
 #pragma unroll
       for (int h = 0; h < 2; ++h) {
         const uint8_t *hb = hdr + 16 * (g + 8 * h);
@@ -105,75 +174,44 @@ __device__ __forceinline__ void gemm_unit(const uint8_t *wt, const uint8_t *xs, 
         // | byte c' of (d, dmin) << 24
         const float d = h2f((uint16_t)(hb[3] | (hb[7] << 8)));
         const float dm = h2f((uint16_t)(hb[11] | (hb[15] << 8)));
-        const uint32_t f = *reinterpret_cast<const uint32_t *>(hb + 4 * (grp >> 1));
-        const int j = grp & 1;
-        const uint32_t sc = (f >> (6 * j)) & 63u, mn = (f >> (12 + 6 * j)) & 63u;
-        sg[h] = __float2half2_rn(d * (float)sc * (h ? 0.0625f : 1.0f));
-        mg[h] = __float2half2_rn(-(dm * (float)mn));
+        const uint32_t f = *reinterpret_cast<const uint32_t *>(hb + 4 * (gi >> 1));
+        const int j = gi & 1;
+        sc2[h] = d * (float)((f >> (6 * j)) & 63u);
+        mn2[h] = dm * (float)((f >> (12 + 6 * j)) & 63u);
       }
-      const uint32_t hi = wd >> 8;
-      a[0] = deq((wd & 0x000F000Fu) | 0x64006400u, magic1024, sg[0], mg[0]);
-      a[1] = deq((wd & 0x00F000F0u) | 0x64006400u, magic1024, sg[1], mg[1]);
-      a[2] = deq((hi & 0x000F000Fu) | 0x64006400u, magic1024, sg[0], mg[0]);
-      a[3] = deq((hi & 0x00F000F0u) | 0x64006400u, magic1024, sg[1], mg[1]);
+      sA = sc2[0];
+      sB = sc2[1] * 0.0625f;
+      mA = mn2[0];
+      mB = mn2[1];
     } else if (TYPE == IFX_TYPE_Q6_K) {
-      const uint32_t wd = reinterpret_cast<const uint32_t *>(wt)[((ch / 4) * 32 + lane) * 4 + ch % 4];
-      const int t = ch / 2;
-      uint32_t H = reinterpret_cast<const uint32_t *>(wt + 2048)[((t / 4) * 32 + lane) * 4 + t % 4];
-      if (ch & 1) H >>= 8;
       const uint8_t *scb = wt + 3072;
-      __half2 sg[2];
-#pragma unroll
-      for (int h = 0; h < 2; ++h) {
-        const int row = g + 8 * h;
-        const float d = h2f(*reinterpret_cast<const uint16_t *>(scb + 256 + 2 * row));
-        sg[h] = __float2half2_rn(d * (float)scb[16 * row + ch] * (h ? 0.0625f : 1.0f));
-      }
-      const __half2 z = __float2half2_rn(0.f);
-      const __half2 sub0 = __float2half2_rn(1056.f), sub1 = __float2half2_rn(1536.f);
-      const uint32_t hi = wd >> 8, H4 = H >> 4;
-      a[0] = deq((wd & 0x000F000Fu) | ((H & 0x00030003u) << 4) | 0x64006400u, sub0, sg[0], z);
-      a[1] = deq((wd & 0x00F000F0u) | ((H & 0x000C000Cu) << 6) | 0x64006400u, sub1, sg[1], z);
-      a[2] = deq((hi & 0x000F000Fu) | ((H4 & 0x00030003u) << 4) | 0x64006400u, sub0, sg[0], z);
-      a[3] = deq((hi & 0x00F000F0u) | ((H4 & 0x000C000Cu) << 6) | 0x64006400u, sub1, sg[1], z);
-    } else if (TYPE == IFX_TYPE_Q4_0) {
-      const uint32_t wd = reinterpret_cast<const uint32_t *>(wt)[((ch / 4) * 32 + lane) * 4 + ch % 4];
-      const int nb = kc / 32, blk = ch / 2;
-      __half2 sg[2];
-#pragma unroll
-      for (int h = 0; h < 2; ++h) {
-        const int row = g + 8 * h;
-        const float d = h2f(*reinterpret_cast<const uint16_t *>(wt + wt_qbytes + (row * nb + blk) * 2));
-        sg[h] = __float2half2_rn(d * (h ? 0.0625f : 1.0f));
-      }
-      const __half2 z = __float2half2_rn(0.f);
-      const __half2 sub0 = __float2half2_rn(1032.f), sub1 = __float2half2_rn(1152.f);
-      const uint32_t hi = wd >> 8;
-      a[0] = deq((wd & 0x000F000Fu) | 0x64006400u, sub0, sg[0], z);
-      a[1] = deq((wd & 0x00F000F0u) | 0x64006400u, sub1, sg[1], z);
-      a[2] = deq((hi & 0x000F000Fu) | 0x64006400u, sub0, sg[0], z);
-      a[3] = deq((hi & 0x00F000F0u) | 0x64006400u, sub1, sg[1], z);
-    } else {  // Q8_0
-      const uint2 w2 = reinterpret_cast<const uint2 *>(wt)[((ch / 2) * 32 + lane) * 2 + ch % 2];
-      const int nb = kc / 32, blk = ch / 2;
-      __half2 sg[2];
-#pragma unroll
-      for (int h = 0; h < 2; ++h) {
-        const int row = g + 8 * h;
-        sg[h] = __float2half2_rn(h2f(*reinterpret_cast<const uint16_t *>(wt + wt_qbytes + (row * nb + blk) * 2)));
-      }
-      const __half2 z = __float2half2_rn(0.f);
-      const __half2 sub = __float2half2_rn(1152.f);
-      a[0] = deq(prmt(w2.x, 0x64646464u, 0x4140u), sub, sg[0], z);
-      a[1] = deq(prmt(w2.x, 0x64646464u, 0x4342u), sub, sg[1], z);
-      a[2] = deq(prmt(w2.y, 0x64646464u, 0x4140u), sub, sg[0], z);
-      a[3] = deq(prmt(w2.y, 0x64646464u, 0x4342u), sub, sg[1], z);
+      const float dA = h2f(*reinterpret_cast<const uint16_t *>(scb + 256 + 2 * g));
+      const float dB = h2f(*reinterpret_cast<const uint16_t *>(scb + 256 + 2 * (g + 8)));
+      sA = dA * (float)scb[16 * g + gi];
+      sB = dB * (float)scb[16 * (g + 8) + gi] * 0.0625f;
+    } else {
+      const int nb = kc / 32;
+      sA = h2f(*reinterpret_cast<const uint16_t *>(wt + wt_qbytes + (g * nb + gi) * 2));
+      sB = h2f(*reinterpret_cast<const uint16_t *>(wt + wt_qbytes + ((g + 8) * nb + gi) * 2));
+      if (TYPE == IFX_TYPE_Q4_0) sB *= 0.0625f;
     }
-    const uint2 *xb = reinterpret_cast<const uint2 *>(xs) + (size_t)ch * 8 * 32 + lane;
 #pragma unroll
     for (int nt = 0; nt < 8; ++nt) {
-      const uint2 b = xb[nt * 32];
-      mma_16816(acc[nt], a[0], a[1], a[2], a[3], b.x, b.y, acc[nt]);
+      acc[nt][0] = fmaf(sA, tmp[nt][0], acc[nt][0]);
+      acc[nt][1] = fmaf(sA, tmp[nt][1], acc[nt][1]);
+      acc[nt][2] = fmaf(sB, tmp[nt][2], acc[nt][2]);
+      acc[nt][3] = fmaf(sB, tmp[nt][3], acc[nt][3]);
+    }
+    if (TYPE == IFX_TYPE_Q4_K) {  // - dmin * min * sum_k x_k over the group, per token
+      const float *sg = sx + gi * kGemmTokens + 2 * c;
+#pragma unroll
+      for (int nt = 0; nt < 8; ++nt) {
+        const float2 xs2 = *reinterpret_cast<const float2 *>(sg + nt * 8);
+        acc[nt][0] = fmaf(-mA, xs2.x, acc[nt][0]);
+        acc[nt][1] = fmaf(-mA, xs2.y, acc[nt][1]);
+        acc[nt][2] = fmaf(-mB, xs2.x, acc[nt][2]);
+        acc[nt][3] = fmaf(-mB, xs2.y, acc[nt][3]);
+      }
     }
   }
 }
@@ -182,8 +220,9 @@ __global__ void __launch_bounds__(kGThreads, 1) gemm_kernel(const __grid_constan
   extern __shared__ __align__(128) uint8_t smem[];
   uint64_t *full_bar = reinterpret_cast<uint64_t *>(smem);
   uint64_t *empty_bar = full_bar + kGStages;
-  const int xbytes = a.kc * 128;  // kc/16 chunks x 2 KB
-  const int stage_bytes = a.unit_bytes + xbytes;
+  const int xbytes = a.kc / 16 * kXChunkBytes;              // x hi + lo of the unit's columns
+  const int sbytes = a.kc / 32 * kGemmTokens * (int)sizeof(float);  // per-token group sums
+  const int stage_bytes = a.unit_bytes + xbytes + sbytes;
   uint8_t *ring = smem + 128;
   const int mb = blockIdx.x, ctile = blockIdx.y;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -206,10 +245,13 @@ __global__ void __launch_bounds__(kGThreads, 1) gemm_kernel(const __grid_constan
         if (i >= kGStages && !mbar_wait(&empty_bar[st], ph ^ 1u, a.err, 201)) break;
         uint8_t *dst = ring + (size_t)st * stage_bytes;
         const uint8_t *wsrc = a.w + ((size_t)ctile * a.kunits + i) * a.unit_bytes;
-        const uint8_t *xsrc = a.x + ((size_t)mb * a.nch_total + (size_t)i * (a.kc / 16)) * 2048;
+        const uint8_t *xsrc = a.x + ((size_t)mb * a.nch_total + (size_t)i * (a.kc / 16)) * kXChunkBytes;
+        const uint8_t *ssrc = reinterpret_cast<const uint8_t *>(
+            a.sums + ((size_t)mb * (a.nch_total / 2) + (size_t)i * (a.kc / 32)) * kGemmTokens);
         mbar_arrive_expect_tx(&full_bar[st], (uint32_t)stage_bytes);
         bulk_g2s(dst, wsrc, (uint32_t)a.unit_bytes, &full_bar[st]);
         bulk_g2s(dst + a.unit_bytes, xsrc, (uint32_t)xbytes, &full_bar[st]);
+        bulk_g2s(dst + a.unit_bytes + xbytes, ssrc, (uint32_t)sbytes, &full_bar[st]);
       }
     }
     return;
@@ -225,11 +267,12 @@ __global__ void __launch_bounds__(kGThreads, 1) gemm_kernel(const __grid_constan
     const uint8_t *base = ring + (size_t)st * stage_bytes;
     const uint8_t *wt = base + (size_t)warp * a.wt_bytes;
     const uint8_t *xs = base + a.unit_bytes;
+    const float *sx = reinterpret_cast<const float *>(xs + a.kc / 16 * kXChunkBytes);
     switch (a.type) {
-      case IFX_TYPE_Q4_K: gemm_unit<IFX_TYPE_Q4_K>(wt, xs, a.kc, a.wt_qbytes, lane, acc); break;
-      case IFX_TYPE_Q6_K: gemm_unit<IFX_TYPE_Q6_K>(wt, xs, a.kc, a.wt_qbytes, lane, acc); break;
-      case IFX_TYPE_Q4_0: gemm_unit<IFX_TYPE_Q4_0>(wt, xs, a.kc, a.wt_qbytes, lane, acc); break;
-      default: gemm_unit<IFX_TYPE_Q8_0>(wt, xs, a.kc, a.wt_qbytes, lane, acc); break;
+      case IFX_TYPE_Q4_K: gemm_unit<IFX_TYPE_Q4_K>(wt, xs, sx, a.kc, a.wt_qbytes, lane, acc); break;
+      case IFX_TYPE_Q6_K: gemm_unit<IFX_TYPE_Q6_K>(wt, xs, sx, a.kc, a.wt_qbytes, lane, acc); break;
+      case IFX_TYPE_Q4_0: gemm_unit<IFX_TYPE_Q4_0>(wt, xs, sx, a.kc, a.wt_qbytes, lane, acc); break;
+      default: gemm_unit<IFX_TYPE_Q8_0>(wt, xs, sx, a.kc, a.wt_qbytes, lane, acc); break;
     }
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty_bar[st]);
@@ -252,14 +295,21 @@ __global__ void __launch_bounds__(kGThreads, 1) gemm_kernel(const __grid_constan
 
 }  // namespace
 
+// Staged x of an M x K input: the hi/lo fragments of every 16-column chunk
+// of every 64-token block, then the per-token 32-column group sums.
+static size_t xfrag_frag_bytes(int64_t M, int64_t K) {
+  const int64_t mblocks = (M + kGemmTokens - 1) / kGemmTokens;
+  return (size_t)mblocks * (size_t)(K / 16) * kXChunkBytes;
+}
+
 size_t gemm_xfrag_bytes(int64_t M, int64_t K) {
   const int64_t mblocks = (M + kGemmTokens - 1) / kGemmTokens;
-  return (size_t)mblocks * (size_t)(K / 16) * 2048;
+  return xfrag_frag_bytes(M, K) + (size_t)mblocks * (size_t)(K / 32) * kGemmTokens * sizeof(float);
 }
 
 ifx_status gemm_stage_x(const float *X, const float *X2, const float *normw, float eps, int mode,
                         int64_t M, int64_t K, void *xfrag, cudaStream_t st) {
-  if (K % 16) return fail(IFX_ERR_SHAPE, "gemm: K must be a multiple of 16");
+  if (K % 32) return fail(IFX_ERR_SHAPE, "gemm: K must be a multiple of 32");
   const int64_t mpad = (M + kGemmTokens - 1) / kGemmTokens * kGemmTokens;
   stage_x_kernel<<<(unsigned)mpad, 256, 0, st>>>(X, X2, normw, eps, mode, M, K,
                                                  reinterpret_cast<__half *>(xfrag));
@@ -272,6 +322,7 @@ ifx_status gemm_run(const QMatrix &W, const void *xfrag, int64_t M, float *C, in
   GemmArgs a{};
   a.w = W.d;
   a.x = reinterpret_cast<const uint8_t *>(xfrag);
+  a.sums = reinterpret_cast<const float *>(a.x + xfrag_frag_bytes(M, W.L.cols));
   a.C = C;
   a.ldc = ldc;
   a.M = M;
@@ -285,7 +336,9 @@ ifx_status gemm_run(const QMatrix &W, const void *xfrag, int64_t M, float *C, in
   a.nch_total = (int)(W.L.cols / 16);
   a.accumulate = accumulate;
   a.err = err;
-  const size_t smem = 128 + (size_t)kGStages * (a.unit_bytes + a.kc * 128);
+  const size_t smem = 128 + (size_t)kGStages * (a.unit_bytes + a.kc / 16 * kXChunkBytes +
+                                                a.kc / 32 * kGemmTokens * sizeof(float));
+  if (smem > 227 * 1024) return fail(IFX_ERR_UNSUPPORTED, "gemm: shared memory plan too large");
   static bool attr = false;
   if (!attr) {
     IFX_CUDA(cudaFuncSetAttribute(gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,

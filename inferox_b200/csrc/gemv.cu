@@ -37,7 +37,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_b1_kernel(const __grid_c
   uint64_t *empty_bar = full_bar + kGemvMaxStages;
   uint8_t *ring = smem + kGemvBarBytes;
   uint8_t *xw = ring + (size_t)a.nstages * a.slot_bytes;
-  float *s16 = reinterpret_cast<float *>(xw + (size_t)a.win_units * a.kc * 2);
+  float *s16 = reinterpret_cast<float *>(xw + (size_t)a.win_units * a.kc * 4);  // after hi + lo
 
   const int2 rg = a.sched[blockIdx.x];
   const int u0 = rg.x, n = rg.y - rg.x;
@@ -151,7 +151,7 @@ ifx_status gemv_plan(const QMatrix *const *mats, float *const *ys, int nseg, int
   a.win_units = win;
   // shrink the ring until the whole plan fits the per-block shared memory cap
   constexpr size_t kSmemCap = 220 * 1024;
-  const size_t win_bytes = (size_t)win * (a.kc * 2 + a.kc / 16 * 4);
+  const size_t win_bytes = (size_t)win * (a.kc * 4 + a.kc / 16 * 4);  // x hi + lo planes, sums
   while (a.nstages > 2 && kGemvBarBytes + (size_t)a.nstages * a.slot_bytes + win_bytes > kSmemCap)
     a.nstages -= 2;
   const size_t smem = kGemvBarBytes + (size_t)a.nstages * a.slot_bytes + win_bytes;

@@ -39,8 +39,12 @@ struct Acc2 {
 };
 
 // ------------------------------------------------------------------ Q4_K --
-__device__ __forceinline__ void unit_q4k(const uint8_t *wt, const uint4 *xf, const float *s16,
-                                         const uint32_t (&mk)[8], int lane, Acc2 &acc) {
+// x is staged as two f16 planes, x ~= hi + lo (hi = f16(x), lo = f16(x - hi)),
+// `xlo` uint4s after the hi plane; the integer weights are exact in f16, so
+// A.hi + A.lo carries x to about 22 bits and the products to f32 accuracy.
+__device__ __forceinline__ void unit_q4k(const uint8_t *wt, const uint4 *xf, int xlo,
+                                         const float *s16, const uint32_t (&mk)[8], int lane,
+                                         Acc2 &acc) {
   const int g = lane >> 2, c = lane & 3;
   const uint4 *qv = reinterpret_cast<const uint4 *>(wt);
   const uint4 *sv = reinterpret_cast<const uint4 *>(wt + 2048);
@@ -48,26 +52,27 @@ __device__ __forceinline__ void unit_q4k(const uint8_t *wt, const uint4 *xf, con
   // only fills its own two group columns, so summing them is exact
   float Ds[4][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f},
                     {0.f, 0.f, 0.f, 0.f}};
-  uint4 q[4], xb[8];
+  uint4 q[4];
 #pragma unroll
   for (int s = 0; s < 4; ++s) q[s] = qv[s * 32 + lane];
-#pragma unroll
-  for (int p = 0; p < 8; ++p) xb[p] = xf[p * 4];
 #pragma unroll
   for (int s = 0; s < 4; ++s) {
     const uint32_t wds[4] = {q[s].x, q[s].y, q[s].z, q[s].w};
 #pragma unroll
     for (int p2 = 0; p2 < 2; ++p2) {
       const int pair = 2 * s + p2;  // chunk pair == quant group (32 columns)
+      const uint4 xh = xf[pair * 4], xl = xf[xlo + pair * 4];
       const uint32_t m = mk[pair];
 #pragma unroll
       for (int e = 0; e < 2; ++e) {
         const uint32_t wd = wds[2 * p2 + e];
         const uint32_t hi = wd >> 8;
-        const uint32_t b0 = hmul2u(e ? xb[pair].z : xb[pair].x, m);
-        const uint32_t b1 = hmul2u(e ? xb[pair].w : xb[pair].y, m);
-        mma_16816(Ds[s], wd & 0x000F000Fu, wd & 0x00F000F0u, hi & 0x000F000Fu, hi & 0x00F000F0u,
-                  b0, b1, Ds[s]);
+        const uint32_t a0 = wd & 0x000F000Fu, a1 = wd & 0x00F000F0u;
+        const uint32_t a2 = hi & 0x000F000Fu, a3 = hi & 0x00F000F0u;
+        mma_16816(Ds[s], a0, a1, a2, a3, hmul2u(e ? xh.z : xh.x, m), hmul2u(e ? xh.w : xh.y, m),
+                  Ds[s]);
+        mma_16816(Ds[s], a0, a1, a2, a3, hmul2u(e ? xl.z : xl.x, m), hmul2u(e ? xl.w : xl.y, m),
+                  Ds[s]);
       }
     }
   }
@@ -97,8 +102,9 @@ __device__ __forceinline__ void unit_q4k(const uint8_t *wt, const uint4 *xf, con
 }
 
 // ------------------------------------------------------------------ Q6_K --
-__device__ __forceinline__ void unit_q6k(const uint8_t *wt, const uint4 *xf, const float *s16,
-                                         const uint32_t (&mk)[8], int lane, Acc2 &acc) {
+__device__ __forceinline__ void unit_q6k(const uint8_t *wt, const uint4 *xf, int xlo,
+                                         const float *s16, const uint32_t (&mk)[8], int lane,
+                                         Acc2 &acc) {
   const int g = lane >> 2, c = lane & 3;
   const uint4 *qv = reinterpret_cast<const uint4 *>(wt);
   const uint4 *hv = reinterpret_cast<const uint4 *>(wt + 2048);
@@ -124,7 +130,7 @@ __device__ __forceinline__ void unit_q6k(const uint8_t *wt, const uint4 *xf, con
 #pragma unroll
     for (int p2 = 0; p2 < 2; ++p2) {
       const int pair = 2 * s + p2;
-      const uint4 xb = xf[pair * 4];
+      const uint4 xb = xf[pair * 4], xl = xf[xlo + pair * 4];
       const uint32_t Hw = hws[pair & 3];
 #pragma unroll
       for (int e = 0; e < 2; ++e) {
@@ -135,12 +141,18 @@ __device__ __forceinline__ void unit_q6k(const uint8_t *wt, const uint4 *xf, con
         const uint32_t hi = wd >> 8;
         const uint32_t b0 = hmul2u(e ? xb.z : xb.x, m);
         const uint32_t b1 = hmul2u(e ? xb.w : xb.y, m);
+        const uint32_t l0 = hmul2u(e ? xl.z : xl.x, m);
+        const uint32_t l1 = hmul2u(e ? xl.w : xl.y, m);
         const uint32_t H = e ? (Hw >> 8) : Hw;
         const uint32_t H4 = H >> 4;
-        mma_16816(DLp[set][e], wd & 0x000F000Fu, wd & 0x00F000F0u, hi & 0x000F000Fu,
-                  hi & 0x00F000F0u, b0, b1, DLp[set][e]);
-        mma_16816(DHp[set][e], H & 0x00030003u, H & 0x000C000Cu, H4 & 0x00030003u,
-                  H4 & 0x000C000Cu, b0, b1, DHp[set][e]);
+        const uint32_t a0 = wd & 0x000F000Fu, a1 = wd & 0x00F000F0u;
+        const uint32_t a2 = hi & 0x000F000Fu, a3 = hi & 0x00F000F0u;
+        const uint32_t h0 = H & 0x00030003u, h1 = H & 0x000C000Cu;
+        const uint32_t h2 = H4 & 0x00030003u, h3 = H4 & 0x000C000Cu;
+        mma_16816(DLp[set][e], a0, a1, a2, a3, b0, b1, DLp[set][e]);
+        mma_16816(DHp[set][e], h0, h1, h2, h3, b0, b1, DHp[set][e]);
+        mma_16816(DLp[set][e], a0, a1, a2, a3, l0, l1, DLp[set][e]);
+        mma_16816(DHp[set][e], h0, h1, h2, h3, l0, l1, DHp[set][e]);
       }
     }
   }
@@ -182,7 +194,8 @@ __device__ __forceinline__ void unit_q6k(const uint8_t *wt, const uint4 *xf, con
 // ------------------------------------------------------- Q4_0 and Q8_0 --
 // Generic (runtime chunk count) paths; used by the tiny config and tests.
 __device__ __forceinline__ void unit_q4_0(const uint8_t *wt, int kc, int wt_qbytes,
-                                          const uint4 *xf, const float *s16, int lane, Acc2 &acc) {
+                                          const uint4 *xf, int xlo, const float *s16, int lane,
+                                          Acc2 &acc) {
   const int g = lane >> 2, c = lane & 3;
   const uint4 *qv = reinterpret_cast<const uint4 *>(wt);
   const int nsteps = kc / 64, nb = kc / 32;
@@ -194,14 +207,16 @@ __device__ __forceinline__ void unit_q4_0(const uint8_t *wt, int kc, int wt_qbyt
 #pragma unroll
     for (int p2 = 0; p2 < 2; ++p2) {
       const int pair = 2 * s + p2;
-      const uint4 xb = xf[pair * 4];
+      const uint4 xb = xf[pair * 4], xl = xf[xlo + pair * 4];
       const uint32_t m = (g == pair) ? 0xffffffffu : 0u;
 #pragma unroll
       for (int e = 0; e < 2; ++e) {
         const uint32_t wd = wds[2 * p2 + e];
         const uint32_t hi = wd >> 8;
-        mma_16816(D, wd & 0x000F000Fu, wd & 0x00F000F0u, hi & 0x000F000Fu, hi & 0x00F000F0u,
-                  (e ? xb.z : xb.x) & m, (e ? xb.w : xb.y) & m, D);
+        const uint32_t a0 = wd & 0x000F000Fu, a1 = wd & 0x00F000F0u;
+        const uint32_t a2 = hi & 0x000F000Fu, a3 = hi & 0x00F000F0u;
+        mma_16816(D, a0, a1, a2, a3, (e ? xb.z : xb.x) & m, (e ? xb.w : xb.y) & m, D);
+        mma_16816(D, a0, a1, a2, a3, (e ? xl.z : xl.x) & m, (e ? xl.w : xl.y) & m, D);
       }
     }
   }
@@ -225,7 +240,8 @@ __device__ __forceinline__ void unit_q4_0(const uint8_t *wt, int kc, int wt_qbyt
 }
 
 __device__ __forceinline__ void unit_q8_0(const uint8_t *wt, int kc, int wt_qbytes,
-                                          const uint4 *xf, const float *s16, int lane, Acc2 &acc) {
+                                          const uint4 *xf, int xlo, const float *s16, int lane,
+                                          Acc2 &acc) {
   const int g = lane >> 2, c = lane & 3;
   const uint4 *qv = reinterpret_cast<const uint4 *>(wt);
   const int nb = kc / 32;
@@ -233,12 +249,16 @@ __device__ __forceinline__ void unit_q8_0(const uint8_t *wt, int kc, int wt_qbyt
 #pragma unroll 1
   for (int s = 0; s < nb; ++s) {  // chunk pair s == block s
     const uint4 q = qv[s * 32 + lane];
-    const uint4 xb = xf[s * 4];
+    const uint4 xb = xf[s * 4], xl = xf[xlo + s * 4];
     const uint32_t m = (g == s) ? 0xffffffffu : 0u;
-    mma_16816(D, prmt(q.x, 0u, 0x4140u), prmt(q.x, 0u, 0x4342u), prmt(q.y, 0u, 0x4140u),
-              prmt(q.y, 0u, 0x4342u), xb.x & m, xb.y & m, D);
-    mma_16816(D, prmt(q.z, 0u, 0x4140u), prmt(q.z, 0u, 0x4342u), prmt(q.w, 0u, 0x4140u),
-              prmt(q.w, 0u, 0x4342u), xb.z & m, xb.w & m, D);
+    const uint32_t a0 = prmt(q.x, 0u, 0x4140u), a1 = prmt(q.x, 0u, 0x4342u);
+    const uint32_t a2 = prmt(q.y, 0u, 0x4140u), a3 = prmt(q.y, 0u, 0x4342u);
+    const uint32_t a4 = prmt(q.z, 0u, 0x4140u), a5 = prmt(q.z, 0u, 0x4342u);
+    const uint32_t a6 = prmt(q.w, 0u, 0x4140u), a7 = prmt(q.w, 0u, 0x4342u);
+    mma_16816(D, a0, a1, a2, a3, xb.x & m, xb.y & m, D);
+    mma_16816(D, a4, a5, a6, a7, xb.z & m, xb.w & m, D);
+    mma_16816(D, a0, a1, a2, a3, xl.x & m, xl.y & m, D);
+    mma_16816(D, a4, a5, a6, a7, xl.z & m, xl.w & m, D);
   }
   const uint8_t *sc = wt + wt_qbytes;
 #pragma unroll
@@ -292,10 +312,13 @@ __device__ __forceinline__ SegView load_seg(const GemvArgs &a, int s) {
 // same round), and the normalised values are formed from registers after a
 // single consumer barrier.
 static __device__ __forceinline__ void emit_x4(float (&y)[4], bool valid, int f, int per_slot,
-                                               int kc, __half *xh, float *s16, int tid) {
+                                               int kc, __half *xh, float *s16, int tid, int xlo) {
   const __half2 h01 = __floats2half2_rn(y[0], y[1]), h23 = __floats2half2_rn(y[2], y[3]);
-  // the 16-column sum of the f16 values the MMA sees: 4 lanes per group
-  float s = (__low2float(h01) + __high2float(h01)) + (__low2float(h23) + __high2float(h23));
+  const __half2 l01 = __floats2half2_rn(y[0] - __low2float(h01), y[1] - __high2float(h01));
+  const __half2 l23 = __floats2half2_rn(y[2] - __low2float(h23), y[3] - __high2float(h23));
+  // the 16-column sum of the values the MMAs see (hi + lo): 4 lanes per group
+  float s = ((__low2float(h01) + __low2float(l01)) + (__high2float(h01) + __high2float(l01))) +
+            ((__low2float(h23) + __low2float(l23)) + (__high2float(h23) + __high2float(l23)));
   s += __shfl_xor_sync(0xffffffffu, s, 1);
   s += __shfl_xor_sync(0xffffffffu, s, 2);
   if (valid) {
@@ -306,6 +329,8 @@ static __device__ __forceinline__ void emit_x4(float (&y)[4], bool valid, int f,
     const size_t ent = ((size_t)(j * (kc / 32) + p) * 4) * 8 + hh * 4 + (ss / 8) * 2;
     *reinterpret_cast<__half2 *>(xh + ent + (size_t)c0 * 8) = h01;
     *reinterpret_cast<__half2 *>(xh + ent + (size_t)(c0 + 1) * 8) = h23;
+    *reinterpret_cast<__half2 *>(xh + (size_t)xlo * 8 + ent + (size_t)c0 * 8) = l01;
+    *reinterpret_cast<__half2 *>(xh + (size_t)xlo * 8 + ent + (size_t)(c0 + 1) * 8) = l23;
     if ((tid & 3) == 0) s16[j * (kc / 16) + o / 16] = s;
   }
 }
@@ -328,6 +353,7 @@ static __device__ __noinline__ void stage_x(const GemvArgs &a, int u0, int n, bo
   __shared__ float red[kConsumerWarps];
   __half *xh = reinterpret_cast<__half *>(xw);
   const bool one_pass = total <= 4 * T;
+  const int xlo = a.win_units * kc / 8;  // the lo plane, in uint4s after the hi plane
   float inv = 1.0f;
   if (norm && !one_pass) {  // sum of squares first (several staging passes follow)
     float ss = 0.f;
@@ -401,7 +427,7 @@ static __device__ __noinline__ void stage_x(const GemvArgs &a, int u0, int n, bo
           else if (mode == GEMV_SWIGLU) y[t] = silu_f(y[t]) * z[t];
         }
       }
-      emit_x4(y, kk[r] >= 0, f, per_slot, kc, xh, s16, tid);
+      emit_x4(y, kk[r] >= 0, f, per_slot, kc, xh, s16, tid, xlo);
     }
   }
 }
@@ -496,10 +522,11 @@ __device__ __forceinline__ bool consume_run(const SegView &S, int k0, int cnt, i
                                             int slot_bytes, uint64_t *full_bar,
                                             uint64_t *empty_bar, const uint8_t *xw,
                                             const float *s16, bool full, int kc, int kunits,
-                                            const uint32_t (&mk)[8], int &ctile, int &kunit,
-                                            Acc2 &acc, int *err) {
+                                            int xlo_uint4, const uint32_t (&mk)[8], int &ctile,
+                                            int &kunit, Acc2 &acc, int *err) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, wti = warp & 7;
   const int xstep = (kc / 32) * 4, sstep = kc / 16;
+  const int xlo = xlo_uint4;
   // slot and phase parity of this warp's ring positions (step 2, NS >= 2),
   // advanced without divisions
   const uint32_t rp0 = it + 2u * (uint32_t)k0 + (uint32_t)half;
@@ -511,10 +538,10 @@ __device__ __forceinline__ bool consume_run(const SegView &S, int k0, int cnt, i
     const uint8_t *wt = ring + (size_t)st * slot_bytes + (size_t)wti * S.wt_bytes;
     const uint4 *xf = reinterpret_cast<const uint4 *>(xw) + (size_t)slot * xstep + (lane & 3);
     const float *sl = s16 + (size_t)slot * sstep;
-    if (TYPE == IFX_TYPE_Q4_K) unit_q4k(wt, xf, sl, mk, lane, acc);
-    else if (TYPE == IFX_TYPE_Q6_K) unit_q6k(wt, xf, sl, mk, lane, acc);
-    else if (TYPE == IFX_TYPE_Q4_0) unit_q4_0(wt, kc, S.wt_qbytes, xf, sl, lane, acc);
-    else unit_q8_0(wt, kc, S.wt_qbytes, xf, sl, lane, acc);
+    if (TYPE == IFX_TYPE_Q4_K) unit_q4k(wt, xf, xlo, sl, mk, lane, acc);
+    else if (TYPE == IFX_TYPE_Q6_K) unit_q6k(wt, xf, xlo, sl, mk, lane, acc);
+    else if (TYPE == IFX_TYPE_Q4_0) unit_q4_0(wt, kc, S.wt_qbytes, xf, xlo, sl, lane, acc);
+    else unit_q8_0(wt, kc, S.wt_qbytes, xf, xlo, sl, lane, acc);
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty_bar[st]);
     st += 2;
@@ -549,6 +576,7 @@ __device__ __forceinline__ bool gemv_consume(const GemvArgs &a, int u0, int n, u
 #pragma unroll
   for (int i = 0; i < 8; ++i) mk[i] = (g == i) ? 0x3C003C00u : 0u;  // f16x2 (1, 1) or (0, 0)
   const int kunits = a.kunits, kc = a.kc;
+  const int xlo = a.win_units * kc / 8;  // lo plane offset in uint4s
   int sg = find_seg(a, u0 + hbeg);
   SegView S = load_seg(a, sg);
   const int local = u0 + hbeg - S.begin;
@@ -561,19 +589,19 @@ __device__ __forceinline__ bool gemv_consume(const GemvArgs &a, int u0, int n, u
     switch (S.type) {
       case IFX_TYPE_Q4_K:
         ok = consume_run<IFX_TYPE_Q4_K>(S, k, cnt, half, hbeg, it, ring, NS, slot_bytes, full_bar,
-                                        empty_bar, xw, s16, full, kc, kunits, mk, ctile, kunit, acc, err);
+                                        empty_bar, xw, s16, full, kc, kunits, xlo, mk, ctile, kunit, acc, err);
         break;
       case IFX_TYPE_Q6_K:
         ok = consume_run<IFX_TYPE_Q6_K>(S, k, cnt, half, hbeg, it, ring, NS, slot_bytes, full_bar,
-                                        empty_bar, xw, s16, full, kc, kunits, mk, ctile, kunit, acc, err);
+                                        empty_bar, xw, s16, full, kc, kunits, xlo, mk, ctile, kunit, acc, err);
         break;
       case IFX_TYPE_Q4_0:
         ok = consume_run<IFX_TYPE_Q4_0>(S, k, cnt, half, hbeg, it, ring, NS, slot_bytes, full_bar,
-                                        empty_bar, xw, s16, full, kc, kunits, mk, ctile, kunit, acc, err);
+                                        empty_bar, xw, s16, full, kc, kunits, xlo, mk, ctile, kunit, acc, err);
         break;
       default:
         ok = consume_run<IFX_TYPE_Q8_0>(S, k, cnt, half, hbeg, it, ring, NS, slot_bytes, full_bar,
-                                        empty_bar, xw, s16, full, kc, kunits, mk, ctile, kunit, acc, err);
+                                        empty_bar, xw, s16, full, kc, kunits, xlo, mk, ctile, kunit, acc, err);
         break;
     }
     if (!ok) return false;
