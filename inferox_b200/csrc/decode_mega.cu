@@ -361,6 +361,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) decode_mega_kernel(const __gr
   uint8_t *scr = smem + A.off_stage;  // x staging of the GEMV phases
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
+    g_xzero = make_uint4(0u, 0u, 0u, 0u);
     for (int s = 0; s < A.NS; ++s) {
       mbar_init(&full_bar[s], 1);
       mbar_init(&empty_bar[s], 8);

@@ -45,6 +45,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_b1_kernel(const __grid_c
   const int NS = a.nstages;
 
   if (threadIdx.x == 0) {
+    g_xzero = make_uint4(0u, 0u, 0u, 0u);
     for (int s = 0; s < NS; ++s) {
       mbar_init(&full_bar[s], 1);
       mbar_init(&empty_bar[s], 8);

@@ -8,6 +8,11 @@
 namespace ifx {
 namespace gemvdev {
 
+// 16 zero bytes in shared memory (set by the kernels at start): the B
+// fragment of a lane whose MMA column is not the current quantisation group
+// is loaded from here instead of being masked after the load.
+__shared__ uint4 g_xzero;
+
 __device__ __forceinline__ float silu_f(float v) {
   // ops.rs:199-209: clamp to [-80, 80], x * 1/(1 + exp(-x))
   float c = fminf(fmaxf(v, -80.0f), 80.0f);
@@ -61,18 +66,18 @@ __device__ __forceinline__ void unit_q4k(const uint8_t *wt, const uint4 *xf, int
 #pragma unroll
     for (int p2 = 0; p2 < 2; ++p2) {
       const int pair = 2 * s + p2;  // chunk pair == quant group (32 columns)
-      const uint4 xh = xf[pair * 4], xl = xf[xlo + pair * 4];
-      const uint32_t m = mk[pair];
+      // MMA column g accumulates group g: other lanes feed zeros
+      const bool mine = g == pair;
+      const uint4 xh = *(mine ? xf + pair * 4 : &g_xzero);
+      const uint4 xl = *(mine ? xf + xlo + pair * 4 : &g_xzero);
 #pragma unroll
       for (int e = 0; e < 2; ++e) {
         const uint32_t wd = wds[2 * p2 + e];
         const uint32_t hi = wd >> 8;
         const uint32_t a0 = wd & 0x000F000Fu, a1 = wd & 0x00F000F0u;
         const uint32_t a2 = hi & 0x000F000Fu, a3 = hi & 0x00F000F0u;
-        mma_16816(Ds[s], a0, a1, a2, a3, hmul2u(e ? xh.z : xh.x, m), hmul2u(e ? xh.w : xh.y, m),
-                  Ds[s]);
-        mma_16816(Ds[s], a0, a1, a2, a3, hmul2u(e ? xl.z : xl.x, m), hmul2u(e ? xl.w : xl.y, m),
-                  Ds[s]);
+        mma_16816(Ds[s], a0, a1, a2, a3, e ? xh.z : xh.x, e ? xh.w : xh.y, Ds[s]);
+        mma_16816(Ds[s], a0, a1, a2, a3, e ? xl.z : xl.x, e ? xl.w : xl.y, Ds[s]);
       }
     }
   }
@@ -207,16 +212,17 @@ __device__ __forceinline__ void unit_q4_0(const uint8_t *wt, int kc, int wt_qbyt
 #pragma unroll
     for (int p2 = 0; p2 < 2; ++p2) {
       const int pair = 2 * s + p2;
-      const uint4 xb = xf[pair * 4], xl = xf[xlo + pair * 4];
-      const uint32_t m = (g == pair) ? 0xffffffffu : 0u;
+      const bool mine = g == pair;
+      const uint4 xb = *(mine ? xf + pair * 4 : &g_xzero);
+      const uint4 xl = *(mine ? xf + xlo + pair * 4 : &g_xzero);
 #pragma unroll
       for (int e = 0; e < 2; ++e) {
         const uint32_t wd = wds[2 * p2 + e];
         const uint32_t hi = wd >> 8;
         const uint32_t a0 = wd & 0x000F000Fu, a1 = wd & 0x00F000F0u;
         const uint32_t a2 = hi & 0x000F000Fu, a3 = hi & 0x00F000F0u;
-        mma_16816(D, a0, a1, a2, a3, (e ? xb.z : xb.x) & m, (e ? xb.w : xb.y) & m, D);
-        mma_16816(D, a0, a1, a2, a3, (e ? xl.z : xl.x) & m, (e ? xl.w : xl.y) & m, D);
+        mma_16816(D, a0, a1, a2, a3, e ? xb.z : xb.x, e ? xb.w : xb.y, D);
+        mma_16816(D, a0, a1, a2, a3, e ? xl.z : xl.x, e ? xl.w : xl.y, D);
       }
     }
   }
@@ -249,16 +255,17 @@ __device__ __forceinline__ void unit_q8_0(const uint8_t *wt, int kc, int wt_qbyt
 #pragma unroll 1
   for (int s = 0; s < nb; ++s) {  // chunk pair s == block s
     const uint4 q = qv[s * 32 + lane];
-    const uint4 xb = xf[s * 4], xl = xf[xlo + s * 4];
-    const uint32_t m = (g == s) ? 0xffffffffu : 0u;
+    const bool mine = g == s;
+    const uint4 xb = *(mine ? xf + s * 4 : &g_xzero);
+    const uint4 xl = *(mine ? xf + xlo + s * 4 : &g_xzero);
     const uint32_t a0 = prmt(q.x, 0u, 0x4140u), a1 = prmt(q.x, 0u, 0x4342u);
     const uint32_t a2 = prmt(q.y, 0u, 0x4140u), a3 = prmt(q.y, 0u, 0x4342u);
     const uint32_t a4 = prmt(q.z, 0u, 0x4140u), a5 = prmt(q.z, 0u, 0x4342u);
     const uint32_t a6 = prmt(q.w, 0u, 0x4140u), a7 = prmt(q.w, 0u, 0x4342u);
-    mma_16816(D, a0, a1, a2, a3, xb.x & m, xb.y & m, D);
-    mma_16816(D, a4, a5, a6, a7, xb.z & m, xb.w & m, D);
-    mma_16816(D, a0, a1, a2, a3, xl.x & m, xl.y & m, D);
-    mma_16816(D, a4, a5, a6, a7, xl.z & m, xl.w & m, D);
+    mma_16816(D, a0, a1, a2, a3, xb.x, xb.y, D);
+    mma_16816(D, a4, a5, a6, a7, xb.z, xb.w, D);
+    mma_16816(D, a0, a1, a2, a3, xl.x, xl.y, D);
+    mma_16816(D, a4, a5, a6, a7, xl.z, xl.w, D);
   }
   const uint8_t *sc = wt + wt_qbytes;
 #pragma unroll
