@@ -139,6 +139,13 @@ ifx_status ifx_prefill(ifx_model *m, ifx_kv *kv, const uint32_t *ids, size_t n,
  * or NULL (skip the copy back). */
 ifx_status ifx_decode_step(ifx_model *m, ifx_kv *kv, uint32_t token,
                            float *logits_host);
+/* Model::forward / Model::forward_last_token_logits (forward.rs:448-495):
+ * the layers over the whole prompt with attention over every position (no
+ * causal mask), RoPE at positions 0..n, no KV cache. logits_host: [n, vocab]
+ * (last_row_only = 0) or [vocab] (1). ids >= vocab give
+ * IFX_ERR_INVALID_TENSOR_INDEX (forward.rs:453-455). */
+ifx_status ifx_forward(ifx_model *m, const uint32_t *ids, size_t n,
+                       float *logits_host, int last_row_only);
 /* Model::generate (forward.rs:592-612): kv.clear, prefill, then max_tokens
  * greedy steps; the decode loop runs on the device (argmax feeds the next
  * embedding without a host round trip). out_tokens: [max_tokens]. */

@@ -103,6 +103,7 @@ def _load():
         "ifx_kv_read": (st, [vp, sz, C.c_int, fp]),
         "ifx_prefill": (st, [vp, vp, u32p, sz, fp, C.c_int]),
         "ifx_decode_step": (st, [vp, vp, C.c_uint32, fp]),
+        "ifx_forward": (st, [vp, u32p, sz, fp, C.c_int]),
         "ifx_generate": (st, [vp, vp, u32p, sz, sz, u32p]),
         "ifx_sample": (st, [vp, C.POINTER(SamplerC), C.c_uint64, C.c_uint64, u32p]),
         "ifx_decode_greedy": (st, [vp, vp, C.c_uint32, sz, u32p, fp]),

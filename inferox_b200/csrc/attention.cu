@@ -236,7 +236,7 @@ __global__ void __launch_bounds__(128) prefill_attn_kernel(PrefillAttnArgs a) {
 #pragma unroll
   for (int i = 0; i < kMaxOut; ++i) acc[i] = 0.f;
   const float sq = sqrtf((float)hd);
-  const int kend = r0 + nq;  // causal: keys 0..r0+nq-1
+  const int kend = a.causal ? r0 + nq : a.n;  // causal: keys 0..r0+nq-1
   __syncthreads();
   for (int k0 = 0; k0 < kend; k0 += kPK) {
     const int nk = min(kPK, kend - k0);
@@ -250,7 +250,7 @@ __global__ void __launch_bounds__(128) prefill_attn_kernel(PrefillAttnArgs a) {
     for (int e = tid; e < kPQ * kPK; e += 128) {
       const int r = e / kPK, t = e % kPK;
       float sc = -INFINITY;
-      if (t < nk && r < nq && k0 + t <= r0 + r) {  // causal mask, forward.rs:266-271
+      if (t < nk && r < nq && (!a.causal || k0 + t <= r0 + r)) {  // causal mask, forward.rs:266-271
         float s = 0.f;
         for (int d = 0; d < hd; ++d) s = fmaf(Qs[r * hd + d], Ks[t * (hd + 1) + d], s);
         sc = s / sq;
@@ -371,8 +371,10 @@ __global__ void __launch_bounds__(128) prefill_attn_tc_kernel(PrefillAttnArgs a)
   for (int nt = 0; nt < HD / 8; ++nt) o[nt][0] = o[nt][1] = o[nt][2] = o[nt][3] = 0.f;
   float m_a = -INFINITY, m_b = -INFINITY, l_a = 0.f, l_b = 0.f;
   const float scale = 1.0f / sqrtf((float)HD);
-  const int kend = min(a.n, r0 + kTQ);  // causal: no key beyond the block's last row
-  for (int kb = 0; kb < kend; kb += kTK) {  // kb <= r0: every row has a key per block
+  const int kend = a.causal ? min(a.n, r0 + kTQ) : a.n;  // causal: no key beyond the block's last row
+  // causal: kb <= r0, so every row has a key in every block; otherwise every
+  // block holds keys for every row
+  for (int kb = 0; kb < kend; kb += kTK) {
     __syncthreads();  // the previous block's K/V are no longer read
     for (int e = tid; e < kTK * HD / 4; e += 128) {
       const int t = e / (HD / 4), d = (e % (HD / 4)) * 4;
@@ -407,8 +409,8 @@ __global__ void __launch_bounds__(128) prefill_attn_tc_kernel(PrefillAttnArgs a)
       for (int j = 0; j < 2; ++j) {
         const int key = kb + nt * 8 + 2 * c + j;
         const bool kin = key < a.n;
-        sv[nt][j] = (kin && key <= row_a) ? sv[nt][j] * scale : -INFINITY;
-        sv[nt][2 + j] = (kin && key <= row_b) ? sv[nt][2 + j] * scale : -INFINITY;
+        sv[nt][j] = (kin && (!a.causal || key <= row_a)) ? sv[nt][j] * scale : -INFINITY;
+        sv[nt][2 + j] = (kin && (!a.causal || key <= row_b)) ? sv[nt][2 + j] * scale : -INFINITY;
         mx_a = fmaxf(mx_a, sv[nt][j]);
         mx_b = fmaxf(mx_b, sv[nt][2 + j]);
       }

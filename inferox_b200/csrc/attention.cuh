@@ -32,6 +32,7 @@ struct PrefillAttnArgs {
   const float *v;   // [n][G*hd]
   float *out;       // [n][H*hd]
   int n, H, G, hd;
+  int causal = 1;   // 0: every row attends to every key (Model::forward, forward.rs:100-150)
 };
 ifx_status prefill_attention(const PrefillAttnArgs &a, cudaStream_t st);
 

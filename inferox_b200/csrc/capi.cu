@@ -192,6 +192,12 @@ ifx_status ifx_prefill(ifx_model *m, ifx_kv *kv, const uint32_t *ids, size_t n, 
   IFX_GUARD({ return m->m.prefill(kv->kv, ids, n, logits_host, last_row_only); })
 }
 
+ifx_status ifx_forward(ifx_model *m, const uint32_t *ids, size_t n, float *logits_host,
+                       int last_row_only) {
+  if (!m || (!ids && n)) return fail(IFX_ERR_INVALID_ARGUMENT, "forward: null argument");
+  IFX_GUARD({ return m->m.forward(ids, n, logits_host, last_row_only); })
+}
+
 ifx_status ifx_decode_step(ifx_model *m, ifx_kv *kv, uint32_t token, float *logits_host) {
   if (!m || !kv) return fail(IFX_ERR_INVALID_ARGUMENT, "decode_step: null argument");
   if (kv->kv.m != &m->m) return fail(IFX_ERR_INVALID_ARGUMENT, "decode_step: kv belongs to another model");

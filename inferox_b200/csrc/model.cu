@@ -671,12 +671,26 @@ ifx_status Model::ensure_ws(size_t n) {
 
 ifx_status Model::prefill(KvCache &kv, const uint32_t *ids, size_t n, float *logits_host,
                           int last_row_only) {
+  return run_prompt(&kv, ids, n, logits_host, last_row_only);
+}
+
+// Model::forward (forward.rs:448-482): the layers over the whole prompt with
+// attention over every position (no mask), RoPE at positions 0..n, no cache.
+ifx_status Model::forward(const uint32_t *ids, size_t n, float *logits_host, int last_row_only) {
+  return run_prompt(nullptr, ids, n, logits_host, last_row_only);
+}
+
+// Shared body of prefill (kvp set: causal attention, K/V appended to the
+// cache) and forward (kvp null: full attention, no cache).
+ifx_status Model::run_prompt(KvCache *kvp, const uint32_t *ids, size_t n, float *logits_host,
+                             int last_row_only) {
   const ifx_config &c = cfg;
   for (size_t i = 0; i < n; ++i)
-    if (ids[i] >= c.vocab_size)  // forward.rs:501-503
+    if (ids[i] >= c.vocab_size)  // forward.rs:453-455, 501-503
       return fail(IFX_ERR_INVALID_TENSOR_INDEX, "tensor index out of bounds: 0");
   if (n == 0) return IFX_OK;
-  if (kv.len + n > kv.max_seq) return fail(IFX_ERR_INVALID_TENSOR_INDEX, "prompt exceeds the KV cache");
+  if (kvp && kvp->len + n > kvp->max_seq)
+    return fail(IFX_ERR_INVALID_TENSOR_INDEX, "prompt exceeds the KV cache");
   IFX_CUDA(cudaSetDevice(device));
   IFX_TRY(ensure_ws(n));
   cudaStream_t st = stream;
@@ -684,7 +698,7 @@ ifx_status Model::prefill(KvCache &kv, const uint32_t *ids, size_t n, float *log
   const int D = (int)c.hidden_size, H = (int)Hl, G = (int)Gl, hd = (int)c.head_dim;
   const int F = (int)Fl;
   const int Hh = H * hd, kvd = G * hd;
-  const int start = (int)kv.len;
+  const int start = kvp ? (int)kvp->len : 0;
   IFX_CUDA(cudaMemcpyAsync(ids_dev, ids, n * sizeof(uint32_t), cudaMemcpyHostToDevice, st));
   embed_rows_kernel<<<(unsigned)n, 256, 0, st>>>(emb_raw, emb_type, D, ids_dev, w_x);
   IFX_CUDA(cudaGetLastError());
@@ -697,11 +711,14 @@ ifx_status Model::prefill(KvCache &kv, const uint32_t *ids, size_t n, float *log
     IFX_TRY(gemm_run(L.wv, w_xf, N, w_v, kvd, 0, err, st));
     IFX_TRY(op_rope(w_q, n, H, hd, c.rope_dim, c.rope_base, pos0, st));
     IFX_TRY(op_rope(w_k, n, G, hd, c.rope_dim, c.rope_base, pos0, st));
-    kv_write_kernel<<<(unsigned)n, 256, 0, st>>>(w_k, w_v, kv.k + l * kv.per_layer,
-                                                 kv.v + l * kv.per_layer, (int)n, G, hd,
-                                                 (int)kv.max_seq, start);
-    IFX_CUDA(cudaGetLastError());
-    PrefillAttnArgs pa{w_q, w_k, w_v, w_attn, (int)n, H, G, hd};
+    if (kvp) {
+      KvCache &kv = *kvp;
+      kv_write_kernel<<<(unsigned)n, 256, 0, st>>>(w_k, w_v, kv.k + l * kv.per_layer,
+                                                   kv.v + l * kv.per_layer, (int)n, G, hd,
+                                                   (int)kv.max_seq, start);
+      IFX_CUDA(cudaGetLastError());
+    }
+    PrefillAttnArgs pa{w_q, w_k, w_v, w_attn, (int)n, H, G, hd, kvp ? 1 : 0};
     IFX_TRY(prefill_attention(pa, st));
     IFX_TRY(gemm_stage_x(w_attn, nullptr, nullptr, 0.f, GX_PLAIN, N, Hh, w_xf, st));
     if (tp > 1) {
@@ -723,8 +740,10 @@ ifx_status Model::prefill(KvCache &kv, const uint32_t *ids, size_t n, float *log
       IFX_TRY(gemm_run(L.w2, w_xf, N, w_x, D, 1, err, st));
     }
   }
-  add_int_kernel<<<1, 1, 0, st>>>(kv.pos, (int)n);  // forward.rs:520
-  IFX_CUDA(cudaGetLastError());
+  if (kvp) {
+    add_int_kernel<<<1, 1, 0, st>>>(kvp->pos, (int)n);  // forward.rs:520
+    IFX_CUDA(cudaGetLastError());
+  }
   if (last_row_only || !logits_host) {
     // logits of the last row into the decode logits buffer (GEMV; under
     // tensor parallelism this rank's vocab slice, then gathered)
@@ -771,7 +790,7 @@ ifx_status Model::prefill(KvCache &kv, const uint32_t *ids, size_t n, float *log
                              c.vocab_size * sizeof(float), cudaMemcpyDeviceToDevice, st));
   }
   IFX_CUDA(cudaStreamSynchronize(st));
-  kv.len += n;
+  if (kvp) kvp->len += n;
   return check_err();
 }
 

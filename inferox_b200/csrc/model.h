@@ -86,6 +86,9 @@ struct Model {
   ifx_status run_decode(KvCache &kv);
   ifx_status decode_step(KvCache &kv, uint32_t token, float *logits_host);
   ifx_status prefill(KvCache &kv, const uint32_t *ids, size_t n, float *logits_host, int last_row_only);
+  ifx_status forward(const uint32_t *ids, size_t n, float *logits_host, int last_row_only);
+  ifx_status run_prompt(KvCache *kvp, const uint32_t *ids, size_t n, float *logits_host,
+                        int last_row_only);
   ifx_status generate(KvCache &kv, const uint32_t *prompt, size_t n_prompt, size_t max_tokens,
                       uint32_t *out);
   ifx_status kv_read(const KvCache &kv, size_t layer, int which_v, float *out_host);

@@ -95,6 +95,15 @@ class Model:
                               1 if last_row_only else 0), "prefill")
         return out.reshape(rows, self.vocab)
 
+    def forward(self, ids, last_row_only: bool = False) -> np.ndarray:
+        """Model::forward / forward_last_token_logits: full attention, no cache."""
+        ids = np.ascontiguousarray(ids, np.uint32)
+        rows = 1 if last_row_only else ids.size
+        out = np.empty(rows * self.vocab, np.float32)
+        check(lib.ifx_forward(self._h, _u32(ids), ids.size, _f32(out), 1 if last_row_only else 0),
+              "forward")
+        return out.reshape(rows, self.vocab)
+
     def decode_step(self, token: int, kv: "KvCache", want_logits: bool = True):
         out = np.empty(self.vocab, np.float32) if want_logits else None
         check(lib.ifx_decode_step(self._h, kv._h, int(token),

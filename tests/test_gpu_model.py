@@ -221,3 +221,25 @@ def test_model_open_from_file(tmp_path):
     with pytest.raises(IfxError) as e:
         Model.open(str(tmp_path / "missing.gguf"))
     assert e.value.name == "Io"
+
+
+@pytest.mark.parametrize("mix,heads,kv_heads", [(0, 6, 6), (1, 8, 2)])
+def test_forward_matches_oracle(mix, heads, kv_heads):
+    """Model::forward (forward.rs:448-495): full attention over the prompt, no
+    cache, every row's logits; forward_last_token_logits is its last row."""
+    dim = 288 if mix == 0 else 512
+    g = synth.build(None, vocab=2048, dim=dim, n_layers=2, n_heads=heads, n_kv_heads=kv_heads,
+                    ffn=768 if mix == 0 else 1024, context=64, mix=mix, seed=17)
+    m, o = Model.from_bytes(g), R.Model(g)
+    ids = synth.prompt_ids(2048, 11, seed=9)
+    got, ref = m.forward(ids), o.forward(ids)
+    assert got.shape == (11, 2048)
+    assert close(got, ref.reshape(11, 2048)), float(np.max(np.abs(got - ref.reshape(11, 2048))))
+    last = m.forward(ids, last_row_only=True)
+    assert np.allclose(last[0], got[-1], atol=1e-5, rtol=1e-5)
+    # the non-causal rows differ from a prefill of the same prompt (causal)
+    pre = m.prefill(ids, m.kv_cache(64))
+    assert not np.allclose(pre[0], got[0], atol=1e-3)
+    with pytest.raises(IfxError) as e:
+        m.forward([1, 2, 2048])
+    assert e.value.name == "InvalidTensorIndex"
