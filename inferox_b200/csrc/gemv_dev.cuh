@@ -313,7 +313,7 @@ __device__ __forceinline__ SegView load_seg(const GemvArgs &a, int s) {
 
 // Consumer-side input staging: f(x) as f16 B fragments + 16-column sums.
 // Every global read is a coalesced float4 issued up front. When the staged
-// columns fit in one pass (up to 4 float4 per thread: K <= 8192 for a full
+// columns fit in one pass (up to 2 float4 per thread: K <= 4096 for a full
 // CTA range) all loads go out in one round, the RMSNorm sum of squares is
 // taken from those same values (or from one extra set of loads issued in the
 // same round), and the normalised values are formed from registers after a
@@ -359,7 +359,8 @@ static __device__ __noinline__ void stage_x(const GemvArgs &a, int u0, int n, bo
   const int K4 = K / 4;
   __shared__ float red[kConsumerWarps];
   __half *xh = reinterpret_cast<__half *>(xw);
-  const bool one_pass = total <= 4 * T;
+  constexpr int R = 2;  // float4s per thread per pass (kept small: no spills)
+  const bool one_pass = total <= R * T;
   const int xlo = a.win_units * kc / 8;  // the lo plane, in uint4s after the hi plane
   float inv = 1.0f;
   if (norm && !one_pass) {  // sum of squares first (several staging passes follow)
@@ -376,13 +377,13 @@ static __device__ __noinline__ void stage_x(const GemvArgs &a, int u0, int n, bo
     for (int i = 0; i < kConsumerWarps; ++i) tot += red[i];
     inv = 1.0f / sqrtf(tot / (float)K + eps);
   }
-  for (int base = 0; base < total; base += 4 * T) {
-    float4 v[4], w[4];
-    int kk[4];
+  for (int base = 0; base < total; base += R * T) {
+    float4 v[R], w[R];
+    int kk[R];
 #pragma unroll
-    for (int r = 0; r < 4; ++r) v[r] = w[r] = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int r = 0; r < R; ++r) v[r] = w[r] = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
-    for (int r = 0; r < 4; ++r) {  // issue all loads first
+    for (int r = 0; r < R; ++r) {  // issue all loads first
       const int f = base + r * T + tid;
       kk[r] = -1;
       if (f < total) {
@@ -406,7 +407,7 @@ static __device__ __noinline__ void stage_x(const GemvArgs &a, int u0, int n, bo
       float ss = 0.f;
       if (full) {
 #pragma unroll
-        for (int r = 0; r < 4; ++r)
+        for (int r = 0; r < R; ++r)
           ss += v[r].x * v[r].x + v[r].y * v[r].y + v[r].z * v[r].z + v[r].w * v[r].w;
       } else {
         for (int f = tid; f < K4; f += T) {
@@ -423,7 +424,7 @@ static __device__ __noinline__ void stage_x(const GemvArgs &a, int u0, int n, bo
       inv = 1.0f / sqrtf(tot / (float)K + eps);
     }
 #pragma unroll
-    for (int r = 0; r < 4; ++r) {
+    for (int r = 0; r < R; ++r) {
       const int f = base + r * T + tid;
       float y[4] = {v[r].x, v[r].y, v[r].z, v[r].w};
       const float z[4] = {w[r].x, w[r].y, w[r].z, w[r].w};
