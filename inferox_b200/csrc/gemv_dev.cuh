@@ -33,28 +33,50 @@ __device__ __forceinline__ float u2f_small(uint32_t v) {
   return __uint_as_float(0x4B000000u | v) - 8388608.0f;
 }
 
-// f16x2 multiply on raw register bits (runs on the FMA pipe, not the ALU)
-__device__ __forceinline__ uint32_t hmul2u(uint32_t a, uint32_t b) {
-  __half2 r = __hmul2(*reinterpret_cast<__half2 *>(&a), *reinterpret_cast<__half2 *>(&b));
-  return *reinterpret_cast<uint32_t *>(&r);
-}
-
 struct Acc2 {
   float r0, r1;  // rows g and g+8
 };
 
-// ------------------------------------------------------------------ Q4_K --
 // x is staged as two f16 planes, x ~= hi + lo (hi = f16(x), lo = f16(x - hi)),
 // `xlo` uint4s after the hi plane; the integer weights are exact in f16, so
 // A.hi + A.lo carries x to about 22 bits and the products to f32 accuracy.
+//
+// Column layout of every MMA below: a k-step covers one quantisation group,
+// and of the eight B columns only two are non-zero: column (group & 3)
+// carries the hi plane and column (group & 3) + 4 the lo plane, so one MMA
+// takes both planes. An accumulator therefore holds at most four groups;
+// groups 0-3 and 4-7 of a unit go to different accumulators (E and F), and
+// fold_hilo adds the hi and lo columns of each group across lanes c and
+// c ^ 2. Lane g loads its B fragment from the hi plane (g < 4) or the lo
+// plane (g >= 4) when g & 3 is the group's column, and from the shared zero
+// vector otherwise.
+__device__ __forceinline__ const uint4 *xplane(const uint4 *xf, int xlo, int g) {
+  return g < 4 ? xf : xf + xlo;
+}
+
+// E: groups 0-3 (hi in columns 0-3, lo in 4-7); F: groups 4-7, likewise.
+// Returns in lane c = lane & 3 the totals of groups 2c and 2c + 1 for rows
+// g (D[0], D[1]) and g + 8 (D[2], D[3]), the C-fragment layout of a single
+// group-per-column accumulation.
+__device__ __forceinline__ void fold_hilo(const float (&E)[4], const float (&F)[4], int c,
+                                          float (&D)[4]) {
+  const bool lowc = c < 2;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float recv = __shfl_xor_sync(0xffffffffu, lowc ? F[i] : E[i], 2);
+    D[i] = (lowc ? E[i] : F[i]) + recv;
+  }
+}
+
+// ------------------------------------------------------------------ Q4_K --
 __device__ __forceinline__ void unit_q4k(const uint8_t *wt, const uint4 *xf, int xlo,
-                                         const float *s16, const uint32_t (&mk)[8], int lane,
-                                         Acc2 &acc) {
-  const int g = lane >> 2, c = lane & 3;
+                                         const float *s16, int lane, Acc2 &acc) {
+  const int g = lane >> 2, c = lane & 3, gq = g & 3;
+  const uint4 *xp = xplane(xf, xlo, g);
   const uint4 *qv = reinterpret_cast<const uint4 *>(wt);
   const uint4 *sv = reinterpret_cast<const uint4 *>(wt + 2048);
-  // four independent accumulator chains (one per 64-column step); each step
-  // only fills its own two group columns, so summing them is exact
+  // four independent accumulator chains, one per 64-column step (two
+  // groups); steps 0-1 hold groups 0-3, steps 2-3 groups 4-7
   float Ds[4][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f},
                     {0.f, 0.f, 0.f, 0.f}};
   uint4 q[4];
@@ -65,25 +87,25 @@ __device__ __forceinline__ void unit_q4k(const uint8_t *wt, const uint4 *xf, int
     const uint32_t wds[4] = {q[s].x, q[s].y, q[s].z, q[s].w};
 #pragma unroll
     for (int p2 = 0; p2 < 2; ++p2) {
-      const int pair = 2 * s + p2;  // chunk pair == quant group (32 columns)
-      // MMA column g accumulates group g: other lanes feed zeros
-      const bool mine = g == pair;
-      const uint4 xh = *(mine ? xf + pair * 4 : &g_xzero);
-      const uint4 xl = *(mine ? xf + xlo + pair * 4 : &g_xzero);
+      const int grp = 2 * s + p2;  // chunk pair == quant group (32 columns)
+      const uint4 xb = *(gq == (grp & 3) ? xp + grp * 4 : &g_xzero);
 #pragma unroll
       for (int e = 0; e < 2; ++e) {
         const uint32_t wd = wds[2 * p2 + e];
         const uint32_t hi = wd >> 8;
         const uint32_t a0 = wd & 0x000F000Fu, a1 = wd & 0x00F000F0u;
         const uint32_t a2 = hi & 0x000F000Fu, a3 = hi & 0x00F000F0u;
-        mma_16816(Ds[s], a0, a1, a2, a3, e ? xh.z : xh.x, e ? xh.w : xh.y, Ds[s]);
-        mma_16816(Ds[s], a0, a1, a2, a3, e ? xl.z : xl.x, e ? xl.w : xl.y, Ds[s]);
+        mma_16816(Ds[s], a0, a1, a2, a3, e ? xb.z : xb.x, e ? xb.w : xb.y, Ds[s]);
       }
     }
   }
-  float D[4];
+  float E[4], F[4], D[4];
 #pragma unroll
-  for (int i = 0; i < 4; ++i) D[i] = (Ds[0][i] + Ds[1][i]) + (Ds[2][i] + Ds[3][i]);
+  for (int i = 0; i < 4; ++i) {  // disjoint columns: these sums are exact
+    E[i] = Ds[0][i] + Ds[1][i];
+    F[i] = Ds[2][i] + Ds[3][i];
+  }
+  fold_hilo(E, F, c, D);
   // D[0] = (g, group 2c), D[1] = (g, 2c+1), D[2] = (g+8, 2c), D[3] = (g+8, 2c+1)
   const float Sa = s16[4 * c] + s16[4 * c + 1];
   const float Sb = s16[4 * c + 2] + s16[4 * c + 3];
@@ -107,21 +129,21 @@ __device__ __forceinline__ void unit_q4k(const uint8_t *wt, const uint4 *xf, int
 }
 
 // ------------------------------------------------------------------ Q6_K --
+// Sixteen 16-column groups per unit; accumulator set t = chunk >> 2 holds
+// chunks 4t..4t+3 (hi columns 0-3, lo columns 4-7), one set per 64-column
+// step, separately for the low-nibble plane (DL) and the 2-bit plane (DH).
 __device__ __forceinline__ void unit_q6k(const uint8_t *wt, const uint4 *xf, int xlo,
-                                         const float *s16, const uint32_t (&mk)[8], int lane,
-                                         Acc2 &acc) {
-  const int g = lane >> 2, c = lane & 3;
+                                         const float *s16, int lane, Acc2 &acc) {
+  const int g = lane >> 2, c = lane & 3, gq = g & 3;
+  const uint4 *xp = xplane(xf, xlo, g);
+  const uint2 *zero2 = reinterpret_cast<const uint2 *>(&g_xzero);
   const uint4 *qv = reinterpret_cast<const uint4 *>(wt);
   const uint4 *hv = reinterpret_cast<const uint4 *>(wt + 2048);
-  // eight independent chains: {low plane, 2-bit plane} x set (chunks 0-7 /
-  // 8-15) x chunk parity; parities fill disjoint columns, so they add exactly
-  float DLp[2][2][4], DHp[2][2][4];
+  float DL[4][4], DH[4][4];
 #pragma unroll
-  for (int a = 0; a < 2; ++a)
+  for (int a = 0; a < 4; ++a)
 #pragma unroll
-    for (int b = 0; b < 2; ++b)
-#pragma unroll
-      for (int i = 0; i < 4; ++i) DLp[a][b][i] = DHp[a][b][i] = 0.f;
+    for (int i = 0; i < 4; ++i) DL[a][i] = DH[a][i] = 0.f;
   uint4 q[4], hq[2];
 #pragma unroll
   for (int s = 0; s < 4; ++s) q[s] = qv[s * 32 + lane];
@@ -135,47 +157,44 @@ __device__ __forceinline__ void unit_q6k(const uint8_t *wt, const uint4 *xf, int
 #pragma unroll
     for (int p2 = 0; p2 < 2; ++p2) {
       const int pair = 2 * s + p2;
-      const uint4 xb = xf[pair * 4], xl = xf[xlo + pair * 4];
       const uint32_t Hw = hws[pair & 3];
 #pragma unroll
       for (int e = 0; e < 2; ++e) {
-        const int ch = 2 * pair + e;  // 16-column group index 0..15
-        const int set = ch >> 3, col = ch & 7;
-        const uint32_t m = mk[col];
+        const int ch = 2 * pair + e;  // 16-column group index 0..15; set = s
+        const uint2 xb =
+            *(gq == (ch & 3) ? reinterpret_cast<const uint2 *>(xp + pair * 4) + e : zero2);
         const uint32_t wd = wds[2 * p2 + e];
         const uint32_t hi = wd >> 8;
-        const uint32_t b0 = hmul2u(e ? xb.z : xb.x, m);
-        const uint32_t b1 = hmul2u(e ? xb.w : xb.y, m);
-        const uint32_t l0 = hmul2u(e ? xl.z : xl.x, m);
-        const uint32_t l1 = hmul2u(e ? xl.w : xl.y, m);
         const uint32_t H = e ? (Hw >> 8) : Hw;
         const uint32_t H4 = H >> 4;
         const uint32_t a0 = wd & 0x000F000Fu, a1 = wd & 0x00F000F0u;
         const uint32_t a2 = hi & 0x000F000Fu, a3 = hi & 0x00F000F0u;
         const uint32_t h0 = H & 0x00030003u, h1 = H & 0x000C000Cu;
         const uint32_t h2 = H4 & 0x00030003u, h3 = H4 & 0x000C000Cu;
-        mma_16816(DLp[set][e], a0, a1, a2, a3, b0, b1, DLp[set][e]);
-        mma_16816(DHp[set][e], h0, h1, h2, h3, b0, b1, DHp[set][e]);
-        mma_16816(DLp[set][e], a0, a1, a2, a3, l0, l1, DLp[set][e]);
-        mma_16816(DHp[set][e], h0, h1, h2, h3, l0, l1, DHp[set][e]);
+        mma_16816(DL[s], a0, a1, a2, a3, xb.x, xb.y, DL[s]);
+        mma_16816(DH[s], h0, h1, h2, h3, xb.x, xb.y, DH[s]);
       }
     }
   }
-  float DL[2][4], DH[2][4];
+  // q = low + 16 * high; rows g + 8 carry both planes scaled by 16 and 4
+  float T[4][4];
 #pragma unroll
-  for (int a = 0; a < 2; ++a)
+  for (int t = 0; t < 4; ++t)
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      DL[a][i] = DLp[a][0][i] + DLp[a][1][i];
-      DH[a][i] = DHp[a][0][i] + DHp[a][1][i];
-    }
+    for (int i = 0; i < 4; ++i)
+      T[t][i] = i < 2 ? (DL[t][i] + 16.0f * DH[t][i]) * 16777216.0f
+                      : (DL[t][i] + 64.0f * DH[t][i]) * 1048576.0f;
+  // U[0]: chunks 2c, 2c+1 (sets 0, 1); U[1]: chunks 8+2c, 9+2c (sets 2, 3)
+  float U[2][4];
+  fold_hilo(T[0], T[1], c, U[0]);
+  fold_hilo(T[2], T[3], c, U[1]);
   const uint8_t *scb = wt + 3072;
 #pragma unroll
   for (int h = 0; h < 2; ++h) {
     const int row = g + 8 * h;
     const float d = h2f(*reinterpret_cast<const uint16_t *>(scb + 256 + 2 * row));
     const uint4 sv = *reinterpret_cast<const uint4 *>(scb + 16 * row);
-    // scales for groups 2c, 2c+1 (set 0) and 8+2c, 9+2c (set 1)
+    // scales for groups 2c, 2c+1 (chunks 0-7) and 8+2c, 9+2c (chunks 8-15)
     const uint32_t w_lo = (c < 2) ? sv.x : sv.y;
     const uint32_t w_hi = (c < 2) ? sv.z : sv.w;
     const int sh = 16 * (c & 1);
@@ -187,9 +206,7 @@ __device__ __forceinline__ void unit_q6k(const uint8_t *wt, const uint4 *xf, int
       for (int j = 0; j < 2; ++j) {
         const int grp = 8 * set + 2 * c + j;
         const float sc = u2f_small((sw >> (sh + 8 * j)) & 0xffu);
-        const float lo = DL[set][2 * h + j], hv2 = DH[set][2 * h + j];
-        const float dot = h ? (lo + 64.0f * hv2) * 1048576.0f : (lo + 16.0f * hv2) * 16777216.0f;
-        r = fmaf(d * sc, dot - 32.0f * s16[grp], r);
+        r = fmaf(d * sc, U[set][2 * h + j] - 32.0f * s16[grp], r);
       }
     }
     if (h) acc.r1 = r; else acc.r0 = r;
@@ -197,35 +214,38 @@ __device__ __forceinline__ void unit_q6k(const uint8_t *wt, const uint4 *xf, int
 }
 
 // ------------------------------------------------------- Q4_0 and Q8_0 --
-// Generic (runtime chunk count) paths; used by the tiny config and tests.
+// Runtime chunk count (kc <= 256: at most eight 32-column blocks per unit).
 __device__ __forceinline__ void unit_q4_0(const uint8_t *wt, int kc, int wt_qbytes,
                                           const uint4 *xf, int xlo, const float *s16, int lane,
                                           Acc2 &acc) {
-  const int g = lane >> 2, c = lane & 3;
+  const int g = lane >> 2, c = lane & 3, gq = g & 3;
+  const uint4 *xp = xplane(xf, xlo, g);
   const uint4 *qv = reinterpret_cast<const uint4 *>(wt);
   const int nsteps = kc / 64, nb = kc / 32;
-  float D[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll 1
-  for (int s = 0; s < nsteps; ++s) {
-    const uint4 q = qv[s * 32 + lane];
-    const uint32_t wds[4] = {q.x, q.y, q.z, q.w};
+  float E[4] = {0.f, 0.f, 0.f, 0.f}, F[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-    for (int p2 = 0; p2 < 2; ++p2) {
-      const int pair = 2 * s + p2;
-      const bool mine = g == pair;
-      const uint4 xb = *(mine ? xf + pair * 4 : &g_xzero);
-      const uint4 xl = *(mine ? xf + xlo + pair * 4 : &g_xzero);
+  for (int s = 0; s < 4; ++s) {
+    if (s < nsteps) {
+      const uint4 q = qv[s * 32 + lane];
+      const uint32_t wds[4] = {q.x, q.y, q.z, q.w};
 #pragma unroll
-      for (int e = 0; e < 2; ++e) {
-        const uint32_t wd = wds[2 * p2 + e];
-        const uint32_t hi = wd >> 8;
-        const uint32_t a0 = wd & 0x000F000Fu, a1 = wd & 0x00F000F0u;
-        const uint32_t a2 = hi & 0x000F000Fu, a3 = hi & 0x00F000F0u;
-        mma_16816(D, a0, a1, a2, a3, e ? xb.z : xb.x, e ? xb.w : xb.y, D);
-        mma_16816(D, a0, a1, a2, a3, e ? xl.z : xl.x, e ? xl.w : xl.y, D);
+      for (int p2 = 0; p2 < 2; ++p2) {
+        const int blk = 2 * s + p2;
+        const uint4 xb = *(gq == (blk & 3) ? xp + blk * 4 : &g_xzero);
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          const uint32_t wd = wds[2 * p2 + e];
+          const uint32_t hi = wd >> 8;
+          const uint32_t a0 = wd & 0x000F000Fu, a1 = wd & 0x00F000F0u;
+          const uint32_t a2 = hi & 0x000F000Fu, a3 = hi & 0x00F000F0u;
+          if (s < 2) mma_16816(E, a0, a1, a2, a3, e ? xb.z : xb.x, e ? xb.w : xb.y, E);
+          else mma_16816(F, a0, a1, a2, a3, e ? xb.z : xb.x, e ? xb.w : xb.y, F);
+        }
       }
     }
   }
+  float D[4];
+  fold_hilo(E, F, c, D);
   const uint8_t *sc = wt + wt_qbytes;
 #pragma unroll
   for (int h = 0; h < 2; ++h) {
@@ -248,25 +268,31 @@ __device__ __forceinline__ void unit_q4_0(const uint8_t *wt, int kc, int wt_qbyt
 __device__ __forceinline__ void unit_q8_0(const uint8_t *wt, int kc, int wt_qbytes,
                                           const uint4 *xf, int xlo, const float *s16, int lane,
                                           Acc2 &acc) {
-  const int g = lane >> 2, c = lane & 3;
+  const int g = lane >> 2, c = lane & 3, gq = g & 3;
+  const uint4 *xp = xplane(xf, xlo, g);
   const uint4 *qv = reinterpret_cast<const uint4 *>(wt);
   const int nb = kc / 32;
-  float D[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll 1
-  for (int s = 0; s < nb; ++s) {  // chunk pair s == block s
-    const uint4 q = qv[s * 32 + lane];
-    const bool mine = g == s;
-    const uint4 xb = *(mine ? xf + s * 4 : &g_xzero);
-    const uint4 xl = *(mine ? xf + xlo + s * 4 : &g_xzero);
-    const uint32_t a0 = prmt(q.x, 0u, 0x4140u), a1 = prmt(q.x, 0u, 0x4342u);
-    const uint32_t a2 = prmt(q.y, 0u, 0x4140u), a3 = prmt(q.y, 0u, 0x4342u);
-    const uint32_t a4 = prmt(q.z, 0u, 0x4140u), a5 = prmt(q.z, 0u, 0x4342u);
-    const uint32_t a6 = prmt(q.w, 0u, 0x4140u), a7 = prmt(q.w, 0u, 0x4342u);
-    mma_16816(D, a0, a1, a2, a3, xb.x, xb.y, D);
-    mma_16816(D, a4, a5, a6, a7, xb.z, xb.w, D);
-    mma_16816(D, a0, a1, a2, a3, xl.x, xl.y, D);
-    mma_16816(D, a4, a5, a6, a7, xl.z, xl.w, D);
+  float E[4] = {0.f, 0.f, 0.f, 0.f}, F[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+  for (int s = 0; s < 8; ++s) {  // chunk pair s == block s
+    if (s < nb) {
+      const uint4 q = qv[s * 32 + lane];
+      const uint4 xb = *(gq == (s & 3) ? xp + s * 4 : &g_xzero);
+      const uint32_t a0 = prmt(q.x, 0u, 0x4140u), a1 = prmt(q.x, 0u, 0x4342u);
+      const uint32_t a2 = prmt(q.y, 0u, 0x4140u), a3 = prmt(q.y, 0u, 0x4342u);
+      const uint32_t a4 = prmt(q.z, 0u, 0x4140u), a5 = prmt(q.z, 0u, 0x4342u);
+      const uint32_t a6 = prmt(q.w, 0u, 0x4140u), a7 = prmt(q.w, 0u, 0x4342u);
+      if (s < 4) {
+        mma_16816(E, a0, a1, a2, a3, xb.x, xb.y, E);
+        mma_16816(E, a4, a5, a6, a7, xb.z, xb.w, E);
+      } else {
+        mma_16816(F, a0, a1, a2, a3, xb.x, xb.y, F);
+        mma_16816(F, a4, a5, a6, a7, xb.z, xb.w, F);
+      }
+    }
   }
+  float D[4];
+  fold_hilo(E, F, c, D);
   const uint8_t *sc = wt + wt_qbytes;
 #pragma unroll
   for (int h = 0; h < 2; ++h) {
@@ -530,7 +556,7 @@ __device__ __forceinline__ bool consume_run(const SegView &S, int k0, int cnt, i
                                             int slot_bytes, uint64_t *full_bar,
                                             uint64_t *empty_bar, const uint8_t *xw,
                                             const float *s16, bool full, int kc, int kunits,
-                                            int xlo_uint4, const uint32_t (&mk)[8], int &ctile,
+                                            int xlo_uint4, int &ctile,
                                             int &kunit, Acc2 &acc, int *err) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, wti = warp & 7;
   const int xstep = (kc / 32) * 4, sstep = kc / 16;
@@ -546,8 +572,8 @@ __device__ __forceinline__ bool consume_run(const SegView &S, int k0, int cnt, i
     const uint8_t *wt = ring + (size_t)st * slot_bytes + (size_t)wti * S.wt_bytes;
     const uint4 *xf = reinterpret_cast<const uint4 *>(xw) + (size_t)slot * xstep + (lane & 3);
     const float *sl = s16 + (size_t)slot * sstep;
-    if (TYPE == IFX_TYPE_Q4_K) unit_q4k(wt, xf, xlo, sl, mk, lane, acc);
-    else if (TYPE == IFX_TYPE_Q6_K) unit_q6k(wt, xf, xlo, sl, mk, lane, acc);
+    if (TYPE == IFX_TYPE_Q4_K) unit_q4k(wt, xf, xlo, sl, lane, acc);
+    else if (TYPE == IFX_TYPE_Q6_K) unit_q6k(wt, xf, xlo, sl, lane, acc);
     else if (TYPE == IFX_TYPE_Q4_0) unit_q4_0(wt, kc, S.wt_qbytes, xf, xlo, sl, lane, acc);
     else unit_q8_0(wt, kc, S.wt_qbytes, xf, xlo, sl, lane, acc);
     __syncwarp();
@@ -577,12 +603,9 @@ __device__ __forceinline__ bool gemv_consume(const GemvArgs &a, int u0, int n, u
                                              const uint8_t *xw, const float *s16, bool full,
                                              int *err) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int g = lane >> 2, half = warp >> 3, wti = warp & 7;
+  const int half = warp >> 3, wti = warp & 7;
   const int hbeg = half_begin(n, half), hcnt = half_count(n, half);
   if (hcnt <= 0) return true;
-  uint32_t mk[8];
-#pragma unroll
-  for (int i = 0; i < 8; ++i) mk[i] = (g == i) ? 0x3C003C00u : 0u;  // f16x2 (1, 1) or (0, 0)
   const int kunits = a.kunits, kc = a.kc;
   const int xlo = a.win_units * kc / 8;  // lo plane offset in uint4s
   int sg = find_seg(a, u0 + hbeg);
@@ -597,19 +620,19 @@ __device__ __forceinline__ bool gemv_consume(const GemvArgs &a, int u0, int n, u
     switch (S.type) {
       case IFX_TYPE_Q4_K:
         ok = consume_run<IFX_TYPE_Q4_K>(S, k, cnt, half, hbeg, it, ring, NS, slot_bytes, full_bar,
-                                        empty_bar, xw, s16, full, kc, kunits, xlo, mk, ctile, kunit, acc, err);
+                                        empty_bar, xw, s16, full, kc, kunits, xlo, ctile, kunit, acc, err);
         break;
       case IFX_TYPE_Q6_K:
         ok = consume_run<IFX_TYPE_Q6_K>(S, k, cnt, half, hbeg, it, ring, NS, slot_bytes, full_bar,
-                                        empty_bar, xw, s16, full, kc, kunits, xlo, mk, ctile, kunit, acc, err);
+                                        empty_bar, xw, s16, full, kc, kunits, xlo, ctile, kunit, acc, err);
         break;
       case IFX_TYPE_Q4_0:
         ok = consume_run<IFX_TYPE_Q4_0>(S, k, cnt, half, hbeg, it, ring, NS, slot_bytes, full_bar,
-                                        empty_bar, xw, s16, full, kc, kunits, xlo, mk, ctile, kunit, acc, err);
+                                        empty_bar, xw, s16, full, kc, kunits, xlo, ctile, kunit, acc, err);
         break;
       default:
         ok = consume_run<IFX_TYPE_Q8_0>(S, k, cnt, half, hbeg, it, ring, NS, slot_bytes, full_bar,
-                                        empty_bar, xw, s16, full, kc, kunits, xlo, mk, ctile, kunit, acc, err);
+                                        empty_bar, xw, s16, full, kc, kunits, xlo, ctile, kunit, acc, err);
         break;
     }
     if (!ok) return false;
