@@ -304,12 +304,15 @@ static size_t xfrag_frag_bytes(int64_t M, int64_t K) {
 
 size_t gemm_xfrag_bytes(int64_t M, int64_t K) {
   const int64_t mblocks = (M + kGemmTokens - 1) / kGemmTokens;
-  return xfrag_frag_bytes(M, K) + (size_t)mblocks * (size_t)(K / 32) * kGemmTokens * sizeof(float);
+  const size_t sync_bytes =
+      xfrag_frag_bytes(M, K) + (size_t)mblocks * (size_t)(K / 32) * kGemmTokens * sizeof(float);
+  return tc_gemm_eligible(K) ? std::max(sync_bytes, tc_xtile_bytes(M, K)) : sync_bytes;
 }
 
 ifx_status gemm_stage_x(const float *X, const float *X2, const float *normw, float eps, int mode,
                         int64_t M, int64_t K, void *xfrag, cudaStream_t st) {
   if (K % 32) return fail(IFX_ERR_SHAPE, "gemm: K must be a multiple of 32");
+  if (tc_gemm_eligible(K)) return tc_stage_x(X, X2, normw, eps, mode, M, K, xfrag, st);
   const int64_t mpad = (M + kGemmTokens - 1) / kGemmTokens * kGemmTokens;
   stage_x_kernel<<<(unsigned)mpad, 256, 0, st>>>(X, X2, normw, eps, mode, M, K,
                                                  reinterpret_cast<__half *>(xfrag));
@@ -319,6 +322,7 @@ ifx_status gemm_stage_x(const float *X, const float *X2, const float *normw, flo
 
 ifx_status gemm_run(const QMatrix &W, const void *xfrag, int64_t M, float *C, int64_t ldc,
                     int accumulate, int *err, cudaStream_t st) {
+  if (tc_gemm_eligible(W.L.cols)) return tc_gemm_run(W, xfrag, M, C, ldc, accumulate, err, st);
   GemmArgs a{};
   a.w = W.d;
   a.x = reinterpret_cast<const uint8_t *>(xfrag);

@@ -22,4 +22,15 @@ ifx_status gemm_stage_x(const float *X, const float *X2, const float *normw, flo
 ifx_status gemm_run(const QMatrix &W, const void *xfrag, int64_t M, float *C, int64_t ldc,
                     int accumulate, int *err, cudaStream_t st);
 
+// The tensor-memory (tcgen05) GEMM of tcgemm.cu: used by gemm_stage_x and
+// gemm_run whenever K is a multiple of 64 (the mma.sync kernel above covers
+// the rest).
+bool tc_gemm_eligible(int64_t K);
+int tc_gemm_ntile(int64_t M);
+size_t tc_xtile_bytes(int64_t M, int64_t K);
+ifx_status tc_stage_x(const float *X, const float *X2, const float *normw, float eps, int mode,
+                      int64_t M, int64_t K, void *xt, cudaStream_t st);
+ifx_status tc_gemm_run(const QMatrix &W, const void *xt, int64_t M, float *C, int64_t ldc,
+                       int accumulate, int *err, cudaStream_t st);
+
 }  // namespace ifx

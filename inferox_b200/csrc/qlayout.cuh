@@ -65,11 +65,11 @@ inline bool make_layout(int type, int64_t rows, int64_t cols, QLayout *L) {
     case IFX_TYPE_Q8_0: {
       if (cols % 32) return false;
       q.kc = 0;
-      for (int kc = 192; kc >= 32; kc -= 32)
-        if (cols % kc == 0 && kc * 17 * kWarpTiles <= kMaxUnitBytes) {
-          q.kc = kc;
-          break;
-        }
+      // multiples of 64 first: the tensor-memory GEMM stages 64-column k-blocks
+      for (int kc = 192; kc >= 64 && !q.kc; kc -= 64)
+        if (cols % kc == 0 && kc * 17 * kWarpTiles <= kMaxUnitBytes) q.kc = kc;
+      for (int kc = 192; kc >= 32 && !q.kc; kc -= 32)
+        if (cols % kc == 0 && kc * 17 * kWarpTiles <= kMaxUnitBytes) q.kc = kc;
       if (!q.kc) return false;
       break;
     }

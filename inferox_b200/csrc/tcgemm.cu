@@ -1,0 +1,517 @@
+// Prefill GEMM on the 5th-generation tensor cores: C[M, rows] (+)= f(X) . W^T
+// with tcgen05.mma (kind::f16, 128 x N x 16 per instruction, f32
+// accumulators in tensor memory).
+//
+// One CTA computes a 128-row x N-token tile (N <= 256) over the whole K:
+//   * warp 0 (one lane) bulk-copies the activation tiles of each 64-column
+//     k-block into shared memory (pre-swizzled images written by
+//     tc_stage_x_kernel, so a 1-D bulk copy lands them in the canonical
+//     128-byte-swizzle K-major layout the MMA reads);
+//   * warps 4-11 dequantise the weight rows of the k-block from the
+//     repacked units (qlayout.cuh) straight into the same layout, one
+//     16-row warp tile each;
+//   * warp 1 (one lane) issues the MMAs and commits their completion to
+//     the stage's "empty" barrier; warp 2 owns the tensor-memory allocation;
+//   * warps 4-7 (one per 32-lane quarter of tensor memory) read the
+//     accumulators back with tcgen05.ld and write C.
+//
+// Precision: the reference dequantises to f32 and multiplies in f32. Here
+// each dequantised weight w (f32, the reference's formula) is split as
+// w * 2^8 ~= a_hi + a_lo (two f16, about 22 bits) and each activation as
+// x ~= x_hi + x_lo; three MMAs accumulate a_hi x_hi + a_hi x_lo + a_lo x_hi
+// in f32 (the dropped a_lo x_lo term is below 2^-22 relative), and the
+// epilogue removes the 2^8. Weight magnitudes up to 255 are representable.
+#include <algorithm>
+
+#include "gemm.cuh"
+
+namespace ifx {
+
+namespace {
+
+constexpr int kTcRows = 128;   // weight rows per CTA (MMA M)
+constexpr int kTcKB = 64;      // k per pipeline stage: one 128-byte swizzle row of f16
+constexpr int kTcStages = 2;
+constexpr int kTcThreads = 384;
+constexpr int kTcDeq0 = 4;     // first dequantising warp; warps 4..11, one 16-row tile each
+constexpr float kTcAScale = 256.0f;
+constexpr int kATile = kTcRows * kTcKB * 2;  // bytes of one A plane per stage (16 KB)
+
+// Byte offset of element (r, k), 0 <= k < 64, in a K-major tile with the
+// 128-byte swizzle: 8-row atoms of 128-byte rows, stacked every 1024 bytes;
+// 16-byte chunk k/8 of row r sits at chunk (k/8) ^ (r % 8).
+__host__ __device__ __forceinline__ uint32_t sw128(int r, int k) {
+  return (uint32_t)((r >> 3) * 1024 + (r & 7) * 128 + ((((k >> 3) ^ r) & 7) << 4) + (k & 7) * 2);
+}
+
+// Shared-memory matrix descriptor (tcgen05): start address >> 4, leading
+// byte offset 16 (unused by swizzled K-major layouts), stride byte offset
+// 1024 (between 8-row atoms), descriptor version 1, 128-byte swizzle.
+__device__ __forceinline__ uint64_t umma_desc(uint32_t saddr) {
+  return (uint64_t)((saddr & 0x3FFFFu) >> 4) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) |
+         ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
+}
+
+// Instruction descriptor, kind::f16: f32 accumulator, f16 A and B, both
+// K-major, M = 128, N = n.
+__host__ __device__ constexpr uint32_t idesc_f16(int n) {
+  return (1u << 4) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(kTcRows >> 4) << 24);
+}
+
+__device__ __forceinline__ void umma_f16(uint32_t tmem_d, uint64_t a, uint64_t b, uint32_t idesc,
+                                         uint32_t accumulate) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(tmem_d),
+      "l"(a), "l"(b), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// Arrives on `bar` once every MMA this thread issued so far has completed.
+__device__ __forceinline__ void umma_commit(uint64_t *bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                   smem_u32(bar))
+               : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+// Generic-proxy shared-memory writes become visible to the tensor core.
+__device__ __forceinline__ void fence_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
+  uint32_t r[32];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, "
+      "%12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, "
+      "%30, %31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]),
+        "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]),
+        "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+__device__ __forceinline__ float silu_t(float v) {
+  float c = fminf(fmaxf(v, -80.0f), 80.0f);
+  return v * (1.0f / (1.0f + expf(-c)));
+}
+
+// Activation staging: token t's row of f(X) as hi/lo f16 planes in the tile
+// images [token tile][k-block][plane][ntile x 64 f16, swizzled]. One CTA per
+// token (padding tokens of the last tile are zero); each thread writes
+// 16-byte chunks (8 consecutive columns) of both planes.
+__global__ void tc_stage_x_kernel(const float *X, const float *X2, const float *normw, float eps,
+                                  int mode, int64_t M, int64_t K, int ntile, uint8_t *out) {
+  const int64_t t = blockIdx.x;
+  const int tid = threadIdx.x;
+  __shared__ float red[32];
+  __shared__ float s_inv;
+  float inv = 1.0f;
+  if (mode == GX_RMSNORM && t < M) {
+    float ss = 0.f;
+    for (int64_t k = tid; k < K; k += blockDim.x) {
+      const float v = X[t * K + k];
+      ss += v * v;
+    }
+    ss = warp_sum(ss);
+    if ((tid & 31) == 0) red[tid >> 5] = ss;
+    __syncthreads();
+    if (tid < 32) {
+      float v = tid < (int)(blockDim.x / 32) ? red[tid] : 0.f;
+      v = warp_sum(v);
+      if (tid == 0) s_inv = 1.0f / sqrtf(v / (float)K + eps);
+    }
+    __syncthreads();
+    inv = s_inv;
+  }
+  const int64_t tt = t / ntile;
+  const int n = (int)(t % ntile);
+  const int64_t nkb = K / kTcKB;
+  const size_t tile = (size_t)ntile * 128;
+  for (int64_t c8 = tid; c8 < K / 8; c8 += blockDim.x) {
+    const int64_t k0 = c8 * 8;
+    float v[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      float y = 0.f;
+      if (t < M) {
+        const int64_t k = k0 + j;
+        if (mode == GX_RMSNORM) y = (X[t * K + k] * inv) * normw[k];
+        else if (mode == GX_SWIGLU) y = silu_t(X[t * K + k]) * X2[t * K + k];
+        else y = X[t * K + k];
+      }
+      v[j] = y;
+    }
+    uint32_t hw[4], lw[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const __half2 h = __floats2half2_rn(v[2 * j], v[2 * j + 1]);
+      const __half2 l = __floats2half2_rn(v[2 * j] - __low2float(h), v[2 * j + 1] - __high2float(h));
+      hw[j] = *reinterpret_cast<const uint32_t *>(&h);
+      lw[j] = *reinterpret_cast<const uint32_t *>(&l);
+    }
+    const int64_t kb = k0 / kTcKB;
+    const size_t base = (size_t)((tt * nkb + kb) * 2) * tile + sw128(n, (int)(k0 % kTcKB));
+    *reinterpret_cast<uint4 *>(out + base) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+    *reinterpret_cast<uint4 *>(out + base + tile) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+  }
+}
+
+struct TcArgs {
+  const uint8_t *w;   // repacked units
+  const uint8_t *xt;  // staged activation tiles
+  float *C;
+  int64_t ldc;
+  int M, type, rows, kc, kunits, unit_bytes, wt_bytes, wt_qbytes, nkb, ntile, tmem_cols;
+  int accumulate;
+  int *err;
+};
+
+// Raw words of one k-block (four 16-column chunks) for lane (g, c) of a warp
+// tile: loaded one k-block ahead of their use.
+struct TcRaw {
+  uint4 q, q2;        // quantised words (q2: second half of a Q8_0 block)
+  uint32_t s0, s1;    // per-row scale words (rows g, g + 8)
+  uint2 h;            // Q6_K 2-bit plane words
+  uint4 hd0, hd1;     // Q4_K row headers (rows g, g + 8)
+};
+
+template <int TYPE>
+__device__ __forceinline__ void tc_fetch(const TcArgs &a, int ctile, int wt, int kb, int lane,
+                                         TcRaw &R) {
+  const int g = lane >> 2;
+  const int bpu = a.kc / kTcKB;  // k-blocks per unit
+  const int unit = kb / bpu, sub = kb - unit * bpu;
+  const uint8_t *wp = a.w + ((size_t)ctile * a.kunits + unit) * a.unit_bytes + (size_t)wt * a.wt_bytes;
+  if (TYPE == IFX_TYPE_Q8_0) {
+    const uint4 *qv = reinterpret_cast<const uint4 *>(wp);
+    R.q = qv[(2 * sub) * 32 + lane];
+    R.q2 = qv[(2 * sub + 1) * 32 + lane];
+  } else {
+    R.q = reinterpret_cast<const uint4 *>(wp)[sub * 32 + lane];
+  }
+  if (TYPE == IFX_TYPE_Q4_K) {
+    const uint4 *hd = reinterpret_cast<const uint4 *>(wp + 2048);
+    R.hd0 = hd[g];
+    R.hd1 = hd[g + 8];
+  } else if (TYPE == IFX_TYPE_Q6_K) {
+    const uint32_t *hp = reinterpret_cast<const uint32_t *>(wp + 2048);
+    R.h = *reinterpret_cast<const uint2 *>(hp + ((sub / 2) * 32 + lane) * 4 + (2 * sub) % 4);
+    const uint8_t *scb = wp + 3072;
+    R.s0 = *reinterpret_cast<const uint32_t *>(scb + 16 * g + 4 * sub);
+    R.s1 = *reinterpret_cast<const uint32_t *>(scb + 16 * (g + 8) + 4 * sub);
+    R.hd0.x = *reinterpret_cast<const uint16_t *>(scb + 256 + 2 * g);
+    R.hd0.y = *reinterpret_cast<const uint16_t *>(scb + 256 + 2 * (g + 8));
+  } else {  // Q4_0, Q8_0: f16 scales of the two 32-column blocks of the k-block
+    const int nb = a.kc / 32;
+    const uint8_t *sc = wp + a.wt_qbytes;
+    R.s0 = *reinterpret_cast<const uint32_t *>(sc + (g * nb + 2 * sub) * 2);
+    R.s1 = *reinterpret_cast<const uint32_t *>(sc + ((g + 8) * nb + 2 * sub) * 2);
+  }
+}
+
+// Dequantises the fetched k-block into the A planes (rows 16 wt + {g, g+8}).
+// v[] order per chunk: (g, 2c), (g, 2c+1), (g+8, 2c), (g+8, 2c+1),
+// (g, 2c+8), (g, 2c+9), (g+8, 2c+8), (g+8, 2c+9) — the mma.m16n8k16
+// A-fragment positions the repacked layout stores.
+template <int TYPE>
+__device__ __forceinline__ void tc_emit(const TcArgs &a, const TcRaw &R, int wt, int kb, int lane,
+                                        uint8_t *ahi, uint8_t *alo) {
+  const int g = lane >> 2, c = lane & 3;
+  const int bpu = a.kc / kTcKB;
+  const int sub = kb % bpu;
+  const uint32_t words[4] = {R.q.x, R.q.y, R.q.z, R.q.w};
+  const int r0 = 16 * wt + g;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {  // 16-column chunk i of the k-block
+    float v[8];
+    if (TYPE == IFX_TYPE_Q4_K || TYPE == IFX_TYPE_Q4_0) {
+      const uint32_t wd = words[i];
+      const float q[8] = {(float)(wd & 15u),         (float)((wd >> 16) & 15u),
+                          (float)((wd >> 4) & 15u),  (float)((wd >> 20) & 15u),
+                          (float)((wd >> 8) & 15u),  (float)((wd >> 24) & 15u),
+                          (float)((wd >> 12) & 15u), (float)(wd >> 28)};
+      if (TYPE == IFX_TYPE_Q4_K) {
+        // dequant.rs:151-158: dall = d * sc, dm = dmin * mn, y = dall * q - dm
+        const int gi = 2 * sub + (i >> 1), j = gi & 1;  // 32-column group within the unit
+        float dall[2], dmn[2];
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const uint4 hd = h ? R.hd1 : R.hd0;
+          const float d = h2f((uint16_t)(((hd.x >> 24) & 0xffu) | (((hd.y >> 24) & 0xffu) << 8)));
+          const float dm = h2f((uint16_t)(((hd.z >> 24) & 0xffu) | (((hd.w >> 24) & 0xffu) << 8)));
+          const uint32_t wsel = gi >> 1;
+          const uint32_t f = wsel == 0 ? hd.x : wsel == 1 ? hd.y : wsel == 2 ? hd.z : hd.w;
+          dall[h] = __fmul_rn(d, (float)((f >> (6 * j)) & 63u));
+          dmn[h] = __fmul_rn(dm, (float)((f >> (12 + 6 * j)) & 63u));
+        }
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          const int h = (e >> 1) & 1;
+          v[e] = __fsub_rn(__fmul_rn(dall[h], q[e]), dmn[h]);
+        }
+      } else {
+        // dequant.rs:62-84: (q - 8) * d
+        const int blk = i >> 1;
+        const float d0 = h2f((uint16_t)(blk ? (R.s0 >> 16) : (R.s0 & 0xffffu)));
+        const float d1 = h2f((uint16_t)(blk ? (R.s1 >> 16) : (R.s1 & 0xffffu)));
+#pragma unroll
+        for (int e = 0; e < 8; ++e) v[e] = __fmul_rn(q[e] - 8.0f, ((e >> 1) & 1) ? d1 : d0);
+      }
+    } else if (TYPE == IFX_TYPE_Q6_K) {
+      // dequant.rs:189-196: q = low nibble | 2 high bits << 4, y = (d * sc) * (q - 32)
+      const uint32_t wd = words[i];
+      uint32_t H = (i >> 1) ? R.h.y : R.h.x;
+      if (i & 1) H >>= 8;
+      const float q[8] = {(float)((wd & 15u) | ((H & 3u) << 4)),
+                          (float)(((wd >> 16) & 15u) | (((H >> 16) & 3u) << 4)),
+                          (float)(((wd >> 4) & 15u) | (((H >> 2) & 3u) << 4)),
+                          (float)(((wd >> 20) & 15u) | (((H >> 18) & 3u) << 4)),
+                          (float)(((wd >> 8) & 15u) | (((H >> 4) & 3u) << 4)),
+                          (float)(((wd >> 24) & 15u) | (((H >> 20) & 3u) << 4)),
+                          (float)(((wd >> 12) & 15u) | (((H >> 6) & 3u) << 4)),
+                          (float)((wd >> 28) | (((H >> 22) & 3u) << 4))};
+      const float d0 = h2f((uint16_t)R.hd0.x), d1 = h2f((uint16_t)R.hd0.y);
+      const float sc0 = (float)((R.s0 >> (8 * i)) & 0xffu), sc1 = (float)((R.s1 >> (8 * i)) & 0xffu);
+      const float ds0 = __fmul_rn(d0, sc0), ds1 = __fmul_rn(d1, sc1);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) v[e] = __fmul_rn(((e >> 1) & 1) ? ds1 : ds0, q[e] - 32.0f);
+    } else {  // Q8_0, dequant.rs:93-111: q * d (bytes stored as q + 128)
+      const uint4 Q = (i >> 1) ? R.q2 : R.q;  // chunk pair (i / 2), chunk i % 2 of it
+      const uint32_t wa = (i & 1) ? Q.z : Q.x, wb = (i & 1) ? Q.w : Q.y;
+      const int blk = i >> 1;
+      const float d0 = h2f((uint16_t)(blk ? (R.s0 >> 16) : (R.s0 & 0xffffu)));
+      const float d1 = h2f((uint16_t)(blk ? (R.s1 >> 16) : (R.s1 & 0xffffu)));
+      const float q[8] = {(float)((int)(wa & 0xffu) - 128),         (float)((int)((wa >> 8) & 0xffu) - 128),
+                          (float)((int)((wa >> 16) & 0xffu) - 128), (float)((int)(wa >> 24) - 128),
+                          (float)((int)(wb & 0xffu) - 128),         (float)((int)((wb >> 8) & 0xffu) - 128),
+                          (float)((int)((wb >> 16) & 0xffu) - 128), (float)((int)(wb >> 24) - 128)};
+#pragma unroll
+      for (int e = 0; e < 8; ++e) v[e] = __fmul_rn(q[e], ((e >> 1) & 1) ? d1 : d0);
+    }
+    // hi/lo split of w * 2^8 and the stores: (row, k) pairs (2c, 2c+1) and (2c+8, 2c+9)
+#pragma unroll
+    for (int p = 0; p < 4; ++p) {  // p: (g, 2c) (g+8, 2c) (g, 2c+8) (g+8, 2c+8)
+      const int e = (p & 1) * 2 + (p >> 1) * 4;
+      const float x0 = v[e] * kTcAScale, x1 = v[e + 1] * kTcAScale;
+      const __half2 h = __floats2half2_rn(x0, x1);
+      const __half2 l = __floats2half2_rn(x0 - __low2float(h), x1 - __high2float(h));
+      const uint32_t off = sw128(r0 + 8 * (p & 1), 16 * i + 2 * c + 8 * (p >> 1));
+      *reinterpret_cast<__half2 *>(ahi + off) = h;
+      *reinterpret_cast<__half2 *>(alo + off) = l;
+    }
+  }
+}
+
+template <int TYPE>
+__device__ __forceinline__ void tc_dequant_loop(const TcArgs &a, int ctile, int wt, int lane,
+                                                uint8_t *stages, int stage_bytes,
+                                                uint64_t *a_full, uint64_t *empty) {
+  TcRaw R{}, Rn{};
+  tc_fetch<TYPE>(a, ctile, wt, 0, lane, R);
+  for (int kb = 0; kb < a.nkb; ++kb) {
+    const int s = kb % kTcStages;
+    const uint32_t ph = (uint32_t)(kb / kTcStages) & 1u;
+    if (kb + 1 < a.nkb) tc_fetch<TYPE>(a, ctile, wt, kb + 1, lane, Rn);  // one k-block ahead
+    if (kb >= kTcStages && !mbar_wait(&empty[s], ph ^ 1u, a.err, 302)) return;
+    uint8_t *ahi = stages + (size_t)s * stage_bytes;
+    tc_emit<TYPE>(a, R, wt, kb, lane, ahi, ahi + kATile);
+    fence_async_smem();
+    mbar_arrive(&a_full[s]);
+    R = Rn;
+  }
+}
+
+__global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_constant__ TcArgs a) {
+  extern __shared__ uint8_t smem_raw[];
+  __shared__ __align__(8) uint64_t a_full[kTcStages], b_full[kTcStages], empty[kTcStages], done;
+  __shared__ uint32_t tmem_slot;
+  // 1024-byte alignment for the swizzled tiles
+  const uint32_t pad = (1024u - (smem_u32(smem_raw) & 1023u)) & 1023u;
+  uint8_t *stages = smem_raw + pad;
+  const int btile = a.ntile * 128;                  // bytes of one B plane per stage
+  const int stage_bytes = 2 * kATile + 2 * btile;   // A hi, A lo, B hi, B lo
+  const int ctile = blockIdx.x, tt = blockIdx.y;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kTcStages; ++s) {
+      mbar_init(&a_full[s], 32 * (kTcThreads / 32 - kTcDeq0));
+      mbar_init(&b_full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(&done, 1);
+    fence_mbar_init();
+  }
+  if (warp == 2) {  // tensor-memory allocation (whole warp)
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smem_u32(&tmem_slot)),
+                 "r"(a.tmem_cols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {  // activation tiles
+      int issued = 0;
+      for (int kb = 0; kb < a.nkb; ++kb) {
+        const int s = kb % kTcStages;
+        const uint32_t ph = (uint32_t)(kb / kTcStages) & 1u;
+        if (kb >= kTcStages && !mbar_wait(&empty[s], ph ^ 1u, a.err, 301)) break;
+        uint8_t *bdst = stages + (size_t)s * stage_bytes + 2 * kATile;
+        const uint8_t *src = a.xt + (size_t)(((int64_t)tt * a.nkb + kb) * 2) * btile;
+        mbar_arrive_expect_tx(&b_full[s], (uint32_t)(2 * btile));
+        bulk_g2s(bdst, src, (uint32_t)(2 * btile), &b_full[s]);
+        issued = kb + 1;
+      }
+      // no copy may outlive the CTA: wait (bounded) for the last ones to land
+      for (int kb = std::max(0, issued - kTcStages); kb < issued; ++kb)
+        mbar_wait(&b_full[kb % kTcStages], (uint32_t)(kb / kTcStages) & 1u, nullptr, 0);
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {  // MMA issue
+      const uint32_t idesc = idesc_f16(a.ntile);
+      for (int kb = 0; kb < a.nkb; ++kb) {
+        const int s = kb % kTcStages;
+        const uint32_t ph = (uint32_t)(kb / kTcStages) & 1u;
+        if (!mbar_wait(&a_full[s], ph, a.err, 303)) break;
+        if (!mbar_wait(&b_full[s], ph, a.err, 304)) break;
+        tc_fence_after();
+        const uint32_t base = smem_u32(stages + (size_t)s * stage_bytes);
+        const uint32_t ah = base, al = base + kATile, bh = base + 2 * kATile, bl = bh + btile;
+#pragma unroll
+        for (int j = 0; j < kTcKB / 16; ++j) {  // 32 bytes of K per MMA
+          const uint32_t o = 32u * j;
+          umma_f16(tmem, umma_desc(ah + o), umma_desc(bh + o), idesc, (kb | j) != 0);
+          umma_f16(tmem, umma_desc(ah + o), umma_desc(bl + o), idesc, 1u);
+          umma_f16(tmem, umma_desc(al + o), umma_desc(bh + o), idesc, 1u);
+        }
+        umma_commit(&empty[s]);  // frees the stage once these MMAs have read it
+      }
+      umma_commit(&done);  // every MMA issued above has completed
+    }
+  } else if (warp >= kTcDeq0) {
+    const int wt = warp - kTcDeq0;
+    switch (a.type) {
+      case IFX_TYPE_Q4_K:
+        tc_dequant_loop<IFX_TYPE_Q4_K>(a, ctile, wt, lane, stages, stage_bytes, a_full, empty);
+        break;
+      case IFX_TYPE_Q6_K:
+        tc_dequant_loop<IFX_TYPE_Q6_K>(a, ctile, wt, lane, stages, stage_bytes, a_full, empty);
+        break;
+      case IFX_TYPE_Q4_0:
+        tc_dequant_loop<IFX_TYPE_Q4_0>(a, ctile, wt, lane, stages, stage_bytes, a_full, empty);
+        break;
+      default:
+        tc_dequant_loop<IFX_TYPE_Q8_0>(a, ctile, wt, lane, stages, stage_bytes, a_full, empty);
+        break;
+    }
+    if (warp < kTcDeq0 + 4) {  // epilogue: warp w reads tensor-memory lanes 32 (w % 4) ..
+      const bool ok = mbar_wait(&done, 0u, a.err, 305);
+      tc_fence_after();
+      const int q = warp & 3;
+      const int row = ctile * kTcRows + 32 * q + lane;
+      for (int c0 = 0; c0 < a.ntile; c0 += 32) {
+        float v[32];
+        tmem_ld32(tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)c0, v);
+        if (ok && row < a.rows) {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            const int64_t tok = (int64_t)tt * a.ntile + c0 + j;
+            if (tok < a.M) {
+              float *p = a.C + tok * a.ldc + row;
+              const float r = v[j] * (1.0f / kTcAScale);
+              *p = a.accumulate ? (*p + r) : r;
+            }
+          }
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 2) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
+                 "r"(a.tmem_cols)
+                 : "memory");
+  }
+}
+
+}  // namespace
+
+int tc_gemm_ntile(int64_t M) {
+  const int64_t n = (M + 31) / 32 * 32;
+  return (int)std::min<int64_t>(256, std::max<int64_t>(32, n));
+}
+
+bool tc_gemm_eligible(int64_t K) { return K % kTcKB == 0; }
+
+size_t tc_xtile_bytes(int64_t M, int64_t K) {
+  const int nt = tc_gemm_ntile(M);
+  const int64_t tiles = (M + nt - 1) / nt;
+  return (size_t)tiles * (size_t)(K / kTcKB) * 2 * (size_t)nt * 128;
+}
+
+ifx_status tc_stage_x(const float *X, const float *X2, const float *normw, float eps, int mode,
+                      int64_t M, int64_t K, void *xt, cudaStream_t st) {
+  const int nt = tc_gemm_ntile(M);
+  const int64_t mpad = (M + nt - 1) / nt * nt;
+  tc_stage_x_kernel<<<(unsigned)mpad, 256, 0, st>>>(X, X2, normw, eps, mode, M, K, nt,
+                                                    reinterpret_cast<uint8_t *>(xt));
+  IFX_CUDA(cudaGetLastError());
+  return IFX_OK;
+}
+
+ifx_status tc_gemm_run(const QMatrix &W, const void *xt, int64_t M, float *C, int64_t ldc,
+                       int accumulate, int *err, cudaStream_t st) {
+  if (W.L.kc % kTcKB || W.L.cols % kTcKB)
+    return fail(IFX_ERR_UNSUPPORTED, "tc gemm: K blocks must be multiples of 64 columns");
+  TcArgs a{};
+  a.w = W.d;
+  a.xt = reinterpret_cast<const uint8_t *>(xt);
+  a.C = C;
+  a.ldc = ldc;
+  a.M = (int)M;
+  a.type = W.L.type;
+  a.rows = (int)W.L.rows;
+  a.kc = W.L.kc;
+  a.kunits = W.L.kunits;
+  a.unit_bytes = W.L.unit_bytes;
+  a.wt_bytes = W.L.wt_bytes;
+  a.wt_qbytes = W.L.wt_qbytes;
+  a.nkb = (int)(W.L.cols / kTcKB);
+  a.ntile = tc_gemm_ntile(M);
+  a.tmem_cols = a.ntile <= 32 ? 32 : a.ntile <= 64 ? 64 : a.ntile <= 128 ? 128 : 256;
+  a.accumulate = accumulate;
+  a.err = err;
+  const size_t smem = 1024 + (size_t)kTcStages * (2 * kATile + 2 * (size_t)a.ntile * 128);
+  if (smem > 226 * 1024) return fail(IFX_ERR_UNSUPPORTED, "tc gemm: shared memory plan too large");
+  static size_t attr = 0;  // the kernel's opt-in dynamic shared memory so far
+  if (smem > attr) {
+    IFX_CUDA(cudaFuncSetAttribute(tc_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  (int)smem));
+    attr = smem;
+  }
+  dim3 grid((unsigned)W.L.ctiles, (unsigned)((M + a.ntile - 1) / a.ntile));
+  tc_gemm_kernel<<<grid, kTcThreads, smem, st>>>(a);
+  IFX_CUDA(cudaGetLastError());
+  return IFX_OK;
+}
+
+}  // namespace ifx

@@ -112,6 +112,22 @@ def test_gemm_matches_oracle(ttype, rows, cols, m):
     assert err.max() < 6e-3, err.max()
 
 
+@pytest.mark.parametrize("ttype,rows,cols,m", [
+    (12, 640, 1024, 300), (14, 256, 2048, 33), (2, 384, 512, 257), (7, 512, 1024, 96),
+    (12, 200, 768, 2),
+])
+def test_gemm_tensor_memory_precision(ttype, rows, cols, m):
+    """K a multiple of 64: the tcgen05 GEMM (hi/lo f16 operands, f32 accumulation in
+    tensor memory) carries about 22 bits, far inside the loose bound above."""
+    W, wd = _qmatrix(ttype, rows, cols, seed=rows + 7 * m)
+    x = np.random.default_rng(m + 1).standard_normal((m, cols)).astype(np.float32)
+    y = ops.matmul_t_q(cuda(x), W, m).cpu().numpy().reshape(m, rows).astype(np.float64)
+    ref = x.astype(np.float64) @ wd.T
+    scale = np.sqrt((x.astype(np.float64) ** 2) @ (wd.T ** 2)) + 1e-6
+    err = np.abs(y - ref) / scale
+    assert err.max() < 1e-4, err.max()
+
+
 def test_matmul_t_bit_exact():  # AVX2 lane order of ops.rs:106-149
     rng = np.random.default_rng(0)
     for m, n, k in [(1, 7, 288), (3, 5, 13), (2, 2, 2), (4, 9, 768)]:
