@@ -3,10 +3,10 @@
 // accumulators in tensor memory).
 //
 // One CTA computes a 128-row x N-token tile (N <= 256) over the whole K:
-//   * warp 0 (one lane) bulk-copies the activation tiles of each 64-column
+//   * warp 0 (one lane) bulk-copies the activation tiles of each 32-column
 //     k-block into shared memory (pre-swizzled images written by
 //     tc_stage_x_kernel, so a 1-D bulk copy lands them in the canonical
-//     128-byte-swizzle K-major layout the MMA reads);
+//     64-byte-swizzle K-major layout the MMA reads);
 //   * warps 4-11 dequantise the weight rows of the k-block from the
 //     repacked units (qlayout.cuh) straight into the same layout, one
 //     16-row warp tile each;
@@ -30,26 +30,29 @@ namespace ifx {
 namespace {
 
 constexpr int kTcRows = 128;   // weight rows per CTA (MMA M)
-constexpr int kTcKB = 64;      // k per pipeline stage: one 128-byte swizzle row of f16
-constexpr int kTcStages = 2;
+constexpr int kTcKB = 32;      // k per pipeline stage: one 64-byte swizzle row of f16
+constexpr int kTcStages = 4;   // four stages of 48 KB at N = 256: copies land well ahead
 constexpr int kTcThreads = 384;
 constexpr int kTcDeq0 = 4;     // first dequantising warp; warps 4..11, one 16-row tile each
 constexpr float kTcAScale = 256.0f;
-constexpr int kATile = kTcRows * kTcKB * 2;  // bytes of one A plane per stage (16 KB)
+constexpr int kTcFetch = 64;   // columns a dequantising lane fetches at once (two stages)
+constexpr int kATile = kTcRows * kTcKB * 2;  // bytes of one A plane per stage (8 KB)
 
-// Byte offset of element (r, k), 0 <= k < 64, in a K-major tile with the
-// 128-byte swizzle: 8-row atoms of 128-byte rows, stacked every 1024 bytes;
-// 16-byte chunk k/8 of row r sits at chunk (k/8) ^ (r % 8).
-__host__ __device__ __forceinline__ uint32_t sw128(int r, int k) {
-  return (uint32_t)((r >> 3) * 1024 + (r & 7) * 128 + ((((k >> 3) ^ r) & 7) << 4) + (k & 7) * 2);
+// Byte offset of element (r, k), 0 <= k < 32, in a K-major tile with the
+// 64-byte swizzle: 8-row atoms of 64-byte rows, stacked every 512 bytes;
+// 16-byte chunk k/8 of row r sits at chunk (k/8) ^ ((r % 8) / 2) (address
+// bits [4, 6) XOR bits [7, 9) of a 512-byte aligned atom).
+__host__ __device__ __forceinline__ uint32_t sw64(int r, int k) {
+  return (uint32_t)((r >> 3) * 512 + (r & 7) * 64 + ((((k >> 3) ^ ((r & 7) >> 1)) & 3) << 4) +
+                    (k & 7) * 2);
 }
 
 // Shared-memory matrix descriptor (tcgen05): start address >> 4, leading
 // byte offset 16 (unused by swizzled K-major layouts), stride byte offset
-// 1024 (between 8-row atoms), descriptor version 1, 128-byte swizzle.
+// 512 (between 8-row atoms), descriptor version 1, 64-byte swizzle (4).
 __device__ __forceinline__ uint64_t umma_desc(uint32_t saddr) {
-  return (uint64_t)((saddr & 0x3FFFFu) >> 4) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) |
-         ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
+  return (uint64_t)((saddr & 0x3FFFFu) >> 4) | ((uint64_t)1 << 16) | ((uint64_t)(512 >> 4) << 32) |
+         ((uint64_t)1 << 46) | ((uint64_t)4 << 61);
 }
 
 // Instruction descriptor, kind::f16: f32 accumulator, f16 A and B, both
@@ -80,26 +83,29 @@ __device__ __forceinline__ void tc_fence_before() {
 __device__ __forceinline__ void tc_fence_after() {
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
 }
+// Starts pulling [p, p + bytes) into L2 (16-byte aligned, multiple of 16).
+__device__ __forceinline__ void prefetch_l2(const void *p, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+}
+
 // Generic-proxy shared-memory writes become visible to the tensor core.
 __device__ __forceinline__ void fence_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 
-__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
-  uint32_t r[32];
+// Sixteen consecutive 32-bit columns of this thread's tensor-memory lane.
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
+  uint32_t r[16];
   asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, "
-      "%12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, "
-      "%30, %31}, [%32];"
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, "
+      "%12, %13, %14, %15}, [%16];"
       : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
         "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
-        "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]),
-        "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]),
-        "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        "=r"(r[14]), "=r"(r[15])
       : "r"(taddr));
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 #pragma unroll
-  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
 }
 
 __device__ __forceinline__ float silu_t(float v) {
@@ -108,7 +114,7 @@ __device__ __forceinline__ float silu_t(float v) {
 }
 
 // Activation staging: token t's row of f(X) as hi/lo f16 planes in the tile
-// images [token tile][k-block][plane][ntile x 64 f16, swizzled]. One CTA per
+// images [token tile][k-block][plane][ntile x 32 f16, swizzled]. One CTA per
 // token (padding tokens of the last tile are zero); each thread writes
 // 16-byte chunks (8 consecutive columns) of both planes.
 __global__ void tc_stage_x_kernel(const float *X, const float *X2, const float *normw, float eps,
@@ -138,7 +144,7 @@ __global__ void tc_stage_x_kernel(const float *X, const float *X2, const float *
   const int64_t tt = t / ntile;
   const int n = (int)(t % ntile);
   const int64_t nkb = K / kTcKB;
-  const size_t tile = (size_t)ntile * 128;
+  const size_t tile = (size_t)ntile * kTcKB * 2;
   for (int64_t c8 = tid; c8 < K / 8; c8 += blockDim.x) {
     const int64_t k0 = c8 * 8;
     float v[8];
@@ -162,7 +168,7 @@ __global__ void tc_stage_x_kernel(const float *X, const float *X2, const float *
       lw[j] = *reinterpret_cast<const uint32_t *>(&l);
     }
     const int64_t kb = k0 / kTcKB;
-    const size_t base = (size_t)((tt * nkb + kb) * 2) * tile + sw128(n, (int)(k0 % kTcKB));
+    const size_t base = (size_t)((tt * nkb + kb) * 2) * tile + sw64(n, (int)(k0 % kTcKB));
     *reinterpret_cast<uint4 *>(out + base) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
     *reinterpret_cast<uint4 *>(out + base + tile) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
   }
@@ -178,8 +184,8 @@ struct TcArgs {
   int *err;
 };
 
-// Raw words of one k-block (four 16-column chunks) for lane (g, c) of a warp
-// tile: loaded one k-block ahead of their use.
+// Raw words of one 64-column fetch block (four 16-column chunks, two
+// stages) for lane (g, c) of a warp tile: loaded one block ahead of use.
 struct TcRaw {
   uint4 q, q2;        // quantised words (q2: second half of a Q8_0 block)
   uint32_t s0, s1;    // per-row scale words (rows g, g + 8)
@@ -191,7 +197,7 @@ template <int TYPE>
 __device__ __forceinline__ void tc_fetch(const TcArgs &a, int ctile, int wt, int kb, int lane,
                                          TcRaw &R) {
   const int g = lane >> 2;
-  const int bpu = a.kc / kTcKB;  // k-blocks per unit
+  const int bpu = a.kc / kTcFetch;  // fetch blocks per unit
   const int unit = kb / bpu, sub = kb - unit * bpu;
   const uint8_t *wp = a.w + ((size_t)ctile * a.kunits + unit) * a.unit_bytes + (size_t)wt * a.wt_bytes;
   if (TYPE == IFX_TYPE_Q8_0) {
@@ -221,95 +227,118 @@ __device__ __forceinline__ void tc_fetch(const TcArgs &a, int ctile, int wt, int
   }
 }
 
-// Dequantises the fetched k-block into the A planes (rows 16 wt + {g, g+8}).
-// v[] order per chunk: (g, 2c), (g, 2c+1), (g+8, 2c), (g+8, 2c+1),
-// (g, 2c+8), (g, 2c+9), (g+8, 2c+8), (g+8, 2c+9) — the mma.m16n8k16
-// A-fragment positions the repacked layout stores.
+__device__ __forceinline__ __half2 u2h2(uint32_t u) { return *reinterpret_cast<__half2 *>(&u); }
+
+// Splits w * 2^8 for a pair of weights into hi/lo f16 pairs and stores them.
+__device__ __forceinline__ void tc_store_pair(float x0, float x1, uint8_t *ahi, uint8_t *alo,
+                                              uint32_t off) {
+  const __half2 h = __floats2half2_rn(x0, x1);
+  const float2 hf = __half22float2(h);
+  *reinterpret_cast<__half2 *>(ahi + off) = h;
+  *reinterpret_cast<__half2 *>(alo + off) = __floats2half2_rn(x0 - hf.x, x1 - hf.y);
+}
+
+// Dequantises half `half` (chunks 2 half, 2 half + 1) of the fetched block
+// into one stage's A planes (rows 16 wt + {g, g+8}, 32 columns). The
+// quantised values become exact small integers in f16 first (the bits OR-ed
+// under the exponent of 1024, then 1024 plus the type's bias subtracted —
+// rows g + 8 come from the high nibble and carry a factor 16, folded into
+// their scale), as the repacked A-fragment layout allows: register a0 holds
+// (row g, columns 2c, 2c+1), a1 (row g+8, same columns), a2 (row g, 2c+8,
+// 2c+9), a3 (row g+8, 2c+8, 2c+9) of the chunk. One 32-column stage is one
+// Q4_K group, two Q6_K scale groups, one Q4_0 / Q8_0 block: the scales are
+// decoded once per stage, pre-multiplied by 2^8.
 template <int TYPE>
-__device__ __forceinline__ void tc_emit(const TcArgs &a, const TcRaw &R, int wt, int kb, int lane,
-                                        uint8_t *ahi, uint8_t *alo) {
+__device__ __forceinline__ void tc_emit(const TcArgs &a, const TcRaw &R, int wt, int kb, int half,
+                                        int lane, uint8_t *ahi, uint8_t *alo) {
   const int g = lane >> 2, c = lane & 3;
-  const int bpu = a.kc / kTcKB;
+  const int bpu = a.kc / kTcFetch;
   const int sub = kb % bpu;
   const uint32_t words[4] = {R.q.x, R.q.y, R.q.z, R.q.w};
   const int r0 = 16 * wt + g;
+  // per-row (g, g+8) multiplier and offset of this stage: w = mul * q' - off
+  float mul0, mul1, off0 = 0.f, off1 = 0.f;
+  if (TYPE == IFX_TYPE_Q4_K) {
+    // dequant.rs:151-158: dall = d * sc, dm = dmin * mn, y = dall * q - dm
+    const int gi = 2 * sub + half, j = gi & 1;  // the stage's 32-column group
+    float dall[2], dmn[2];
 #pragma unroll
-  for (int i = 0; i < 4; ++i) {  // 16-column chunk i of the k-block
-    float v[8];
+    for (int h = 0; h < 2; ++h) {
+      const uint4 hd = h ? R.hd1 : R.hd0;
+      const float d = h2f((uint16_t)prmt(hd.x, hd.y, 0x0073u));
+      const float dm = h2f((uint16_t)prmt(hd.z, hd.w, 0x0073u));
+      const uint32_t f = sub == 0 ? hd.x : sub == 1 ? hd.y : sub == 2 ? hd.z : hd.w;
+      dall[h] = d * (float)((f >> (6 * j)) & 63u);
+      dmn[h] = dm * (float)((f >> (12 + 6 * j)) & 63u);
+    }
+    mul0 = dall[0] * kTcAScale;
+    mul1 = dall[1] * (kTcAScale / 16.f);
+    off0 = dmn[0] * kTcAScale;
+    off1 = dmn[1] * kTcAScale;
+  } else if (TYPE == IFX_TYPE_Q6_K) {
+    mul0 = h2f((uint16_t)R.hd0.x) * kTcAScale;  // d; the 16-column scales follow per chunk
+    mul1 = h2f((uint16_t)R.hd0.y) * (kTcAScale / 16.f);
+  } else {  // Q4_0 / Q8_0: the f16 scale of the stage's 32-column block
+    mul0 = h2f((uint16_t)(half ? (R.s0 >> 16) : (R.s0 & 0xffffu))) * kTcAScale;
+    mul1 = h2f((uint16_t)(half ? (R.s1 >> 16) : (R.s1 & 0xffffu))) *
+           (TYPE == IFX_TYPE_Q4_0 ? kTcAScale / 16.f : kTcAScale);
+  }
+#pragma unroll
+  for (int ii = 0; ii < 2; ++ii) {
+    const int i = 2 * half + ii;  // 16-column chunk of the fetch block
+    uint32_t av[4];
+    float m0 = mul0, m1 = mul1;
     if (TYPE == IFX_TYPE_Q4_K || TYPE == IFX_TYPE_Q4_0) {
-      const uint32_t wd = words[i];
-      const float q[8] = {(float)(wd & 15u),         (float)((wd >> 16) & 15u),
-                          (float)((wd >> 4) & 15u),  (float)((wd >> 20) & 15u),
-                          (float)((wd >> 8) & 15u),  (float)((wd >> 24) & 15u),
-                          (float)((wd >> 12) & 15u), (float)(wd >> 28)};
-      if (TYPE == IFX_TYPE_Q4_K) {
-        // dequant.rs:151-158: dall = d * sc, dm = dmin * mn, y = dall * q - dm
-        const int gi = 2 * sub + (i >> 1), j = gi & 1;  // 32-column group within the unit
-        float dall[2], dmn[2];
+      const uint32_t wd = words[i], hi = wd >> 8;
+      const __half2 sub0 = __float2half2_rn(TYPE == IFX_TYPE_Q4_K ? 1024.f : 1032.f);
+      const __half2 sub1 = __float2half2_rn(TYPE == IFX_TYPE_Q4_K ? 1024.f : 1152.f);
+      av[0] = wd & 0x000F000Fu;
+      av[1] = wd & 0x00F000F0u;
+      av[2] = hi & 0x000F000Fu;
+      av[3] = hi & 0x00F000F0u;
 #pragma unroll
-        for (int h = 0; h < 2; ++h) {
-          const uint4 hd = h ? R.hd1 : R.hd0;
-          const float d = h2f((uint16_t)(((hd.x >> 24) & 0xffu) | (((hd.y >> 24) & 0xffu) << 8)));
-          const float dm = h2f((uint16_t)(((hd.z >> 24) & 0xffu) | (((hd.w >> 24) & 0xffu) << 8)));
-          const uint32_t wsel = gi >> 1;
-          const uint32_t f = wsel == 0 ? hd.x : wsel == 1 ? hd.y : wsel == 2 ? hd.z : hd.w;
-          dall[h] = __fmul_rn(d, (float)((f >> (6 * j)) & 63u));
-          dmn[h] = __fmul_rn(dm, (float)((f >> (12 + 6 * j)) & 63u));
-        }
-#pragma unroll
-        for (int e = 0; e < 8; ++e) {
-          const int h = (e >> 1) & 1;
-          v[e] = __fsub_rn(__fmul_rn(dall[h], q[e]), dmn[h]);
-        }
-      } else {
-        // dequant.rs:62-84: (q - 8) * d
-        const int blk = i >> 1;
-        const float d0 = h2f((uint16_t)(blk ? (R.s0 >> 16) : (R.s0 & 0xffffu)));
-        const float d1 = h2f((uint16_t)(blk ? (R.s1 >> 16) : (R.s1 & 0xffffu)));
-#pragma unroll
-        for (int e = 0; e < 8; ++e) v[e] = __fmul_rn(q[e] - 8.0f, ((e >> 1) & 1) ? d1 : d0);
+      for (int r = 0; r < 4; ++r) {
+        const __half2 v = __hsub2(u2h2(av[r] | 0x64006400u), (r & 1) ? sub1 : sub0);
+        av[r] = *reinterpret_cast<const uint32_t *>(&v);
       }
     } else if (TYPE == IFX_TYPE_Q6_K) {
       // dequant.rs:189-196: q = low nibble | 2 high bits << 4, y = (d * sc) * (q - 32)
-      const uint32_t wd = words[i];
+      const uint32_t wd = words[i], hi = wd >> 8;
       uint32_t H = (i >> 1) ? R.h.y : R.h.x;
       if (i & 1) H >>= 8;
-      const float q[8] = {(float)((wd & 15u) | ((H & 3u) << 4)),
-                          (float)(((wd >> 16) & 15u) | (((H >> 16) & 3u) << 4)),
-                          (float)(((wd >> 4) & 15u) | (((H >> 2) & 3u) << 4)),
-                          (float)(((wd >> 20) & 15u) | (((H >> 18) & 3u) << 4)),
-                          (float)(((wd >> 8) & 15u) | (((H >> 4) & 3u) << 4)),
-                          (float)(((wd >> 24) & 15u) | (((H >> 20) & 3u) << 4)),
-                          (float)(((wd >> 12) & 15u) | (((H >> 6) & 3u) << 4)),
-                          (float)((wd >> 28) | (((H >> 22) & 3u) << 4))};
-      const float d0 = h2f((uint16_t)R.hd0.x), d1 = h2f((uint16_t)R.hd0.y);
-      const float sc0 = (float)((R.s0 >> (8 * i)) & 0xffu), sc1 = (float)((R.s1 >> (8 * i)) & 0xffu);
-      const float ds0 = __fmul_rn(d0, sc0), ds1 = __fmul_rn(d1, sc1);
+      const uint32_t H4 = H >> 4;
+      const __half2 sub0 = __float2half2_rn(1056.f), sub1 = __float2half2_rn(1536.f);
+      av[0] = (wd & 0x000F000Fu) | ((H & 0x00030003u) << 4);
+      av[1] = (wd & 0x00F000F0u) | ((H & 0x000C000Cu) << 6);
+      av[2] = (hi & 0x000F000Fu) | ((H4 & 0x00030003u) << 4);
+      av[3] = (hi & 0x00F000F0u) | ((H4 & 0x000C000Cu) << 6);
 #pragma unroll
-      for (int e = 0; e < 8; ++e) v[e] = __fmul_rn(((e >> 1) & 1) ? ds1 : ds0, q[e] - 32.0f);
+      for (int r = 0; r < 4; ++r) {
+        const __half2 v = __hsub2(u2h2(av[r] | 0x64006400u), (r & 1) ? sub1 : sub0);
+        av[r] = *reinterpret_cast<const uint32_t *>(&v);
+      }
+      m0 *= (float)((R.s0 >> (8 * i)) & 0xffu);  // u8 scale of the 16-column chunk
+      m1 *= (float)((R.s1 >> (8 * i)) & 0xffu);
     } else {  // Q8_0, dequant.rs:93-111: q * d (bytes stored as q + 128)
       const uint4 Q = (i >> 1) ? R.q2 : R.q;  // chunk pair (i / 2), chunk i % 2 of it
       const uint32_t wa = (i & 1) ? Q.z : Q.x, wb = (i & 1) ? Q.w : Q.y;
-      const int blk = i >> 1;
-      const float d0 = h2f((uint16_t)(blk ? (R.s0 >> 16) : (R.s0 & 0xffffu)));
-      const float d1 = h2f((uint16_t)(blk ? (R.s1 >> 16) : (R.s1 & 0xffffu)));
-      const float q[8] = {(float)((int)(wa & 0xffu) - 128),         (float)((int)((wa >> 8) & 0xffu) - 128),
-                          (float)((int)((wa >> 16) & 0xffu) - 128), (float)((int)(wa >> 24) - 128),
-                          (float)((int)(wb & 0xffu) - 128),         (float)((int)((wb >> 8) & 0xffu) - 128),
-                          (float)((int)((wb >> 16) & 0xffu) - 128), (float)((int)(wb >> 24) - 128)};
+      const __half2 sub = __float2half2_rn(1152.f);
+      av[0] = prmt(wa, 0x64646464u, 0x4140u);
+      av[1] = prmt(wa, 0x64646464u, 0x4342u);
+      av[2] = prmt(wb, 0x64646464u, 0x4140u);
+      av[3] = prmt(wb, 0x64646464u, 0x4342u);
 #pragma unroll
-      for (int e = 0; e < 8; ++e) v[e] = __fmul_rn(q[e], ((e >> 1) & 1) ? d1 : d0);
+      for (int r = 0; r < 4; ++r) {
+        const __half2 v = __hsub2(u2h2(av[r]), sub);
+        av[r] = *reinterpret_cast<const uint32_t *>(&v);
+      }
     }
-    // hi/lo split of w * 2^8 and the stores: (row, k) pairs (2c, 2c+1) and (2c+8, 2c+9)
 #pragma unroll
-    for (int p = 0; p < 4; ++p) {  // p: (g, 2c) (g+8, 2c) (g, 2c+8) (g+8, 2c+8)
-      const int e = (p & 1) * 2 + (p >> 1) * 4;
-      const float x0 = v[e] * kTcAScale, x1 = v[e + 1] * kTcAScale;
-      const __half2 h = __floats2half2_rn(x0, x1);
-      const __half2 l = __floats2half2_rn(x0 - __low2float(h), x1 - __high2float(h));
-      const uint32_t off = sw128(r0 + 8 * (p & 1), 16 * i + 2 * c + 8 * (p >> 1));
-      *reinterpret_cast<__half2 *>(ahi + off) = h;
-      *reinterpret_cast<__half2 *>(alo + off) = l;
+    for (int r = 0; r < 4; ++r) {  // r: (g, 2c) (g+8, 2c) (g, 2c+8) (g+8, 2c+8)
+      const float2 q = __half22float2(u2h2(av[r]));
+      const float m = (r & 1) ? m1 : m0, o = (r & 1) ? off1 : off0;
+      const float x0 = fmaf(m, q.x, -o), x1 = fmaf(m, q.y, -o);
+      tc_store_pair(x0, x1, ahi, alo, sw64(r0 + 8 * (r & 1), 16 * ii + 2 * c + 8 * (r >> 1)));
     }
   }
 }
@@ -319,16 +348,21 @@ __device__ __forceinline__ void tc_dequant_loop(const TcArgs &a, int ctile, int 
                                                 uint8_t *stages, int stage_bytes,
                                                 uint64_t *a_full, uint64_t *empty) {
   TcRaw R{}, Rn{};
+  const int nfb = a.nkb / 2;  // fetch blocks (two stages each)
   tc_fetch<TYPE>(a, ctile, wt, 0, lane, R);
-  for (int kb = 0; kb < a.nkb; ++kb) {
-    const int s = kb % kTcStages;
-    const uint32_t ph = (uint32_t)(kb / kTcStages) & 1u;
-    if (kb + 1 < a.nkb) tc_fetch<TYPE>(a, ctile, wt, kb + 1, lane, Rn);  // one k-block ahead
-    if (kb >= kTcStages && !mbar_wait(&empty[s], ph ^ 1u, a.err, 302)) return;
-    uint8_t *ahi = stages + (size_t)s * stage_bytes;
-    tc_emit<TYPE>(a, R, wt, kb, lane, ahi, ahi + kATile);
-    fence_async_smem();
-    mbar_arrive(&a_full[s]);
+  for (int fb = 0; fb < nfb; ++fb) {
+    if (fb + 1 < nfb) tc_fetch<TYPE>(a, ctile, wt, fb + 1, lane, Rn);  // one block ahead
+#pragma unroll
+    for (int half = 0; half < 2; ++half) {
+      const int kb = 2 * fb + half;
+      const int s = kb % kTcStages;
+      const uint32_t ph = (uint32_t)(kb / kTcStages) & 1u;
+      if (kb >= kTcStages && !mbar_wait(&empty[s], ph ^ 1u, a.err, 302)) return;
+      uint8_t *ahi = stages + (size_t)s * stage_bytes;
+      tc_emit<TYPE>(a, R, wt, fb, half, lane, ahi, ahi + kATile);
+      fence_async_smem();
+      mbar_arrive(&a_full[s]);
+    }
     R = Rn;
   }
 }
@@ -340,7 +374,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_con
   // 1024-byte alignment for the swizzled tiles
   const uint32_t pad = (1024u - (smem_u32(smem_raw) & 1023u)) & 1023u;
   uint8_t *stages = smem_raw + pad;
-  const int btile = a.ntile * 128;                  // bytes of one B plane per stage
+  const int btile = a.ntile * kTcKB * 2;            // bytes of one B plane per stage
   const int stage_bytes = 2 * kATile + 2 * btile;   // A hi, A lo, B hi, B lo
   const int ctile = blockIdx.x, tt = blockIdx.y;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -367,11 +401,18 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_con
   const uint32_t tmem = tmem_slot;
 
   if (warp == 0) {
-    if (lane == 0) {  // activation tiles
+    if (lane == 0) {  // activation tiles; the row tile's weight units are pulled into L2
+      // two units ahead of the dequantising warps, so their loads hit L2
+      const int kpu = a.kc / kTcKB;  // k-blocks per unit
+      const uint8_t *wrow = a.w + (size_t)ctile * a.kunits * a.unit_bytes;
+      for (int u = 0; u < 2 && u < a.kunits; ++u)
+        prefetch_l2(wrow + (size_t)u * a.unit_bytes, (uint32_t)a.unit_bytes);
       int issued = 0;
       for (int kb = 0; kb < a.nkb; ++kb) {
         const int s = kb % kTcStages;
         const uint32_t ph = (uint32_t)(kb / kTcStages) & 1u;
+        if (kb % kpu == 0 && kb / kpu + 2 < a.kunits)
+          prefetch_l2(wrow + (size_t)(kb / kpu + 2) * a.unit_bytes, (uint32_t)a.unit_bytes);
         if (kb >= kTcStages && !mbar_wait(&empty[s], ph ^ 1u, a.err, 301)) break;
         uint8_t *bdst = stages + (size_t)s * stage_bytes + 2 * kATile;
         const uint8_t *src = a.xt + (size_t)(((int64_t)tt * a.nkb + kb) * 2) * btile;
@@ -426,18 +467,23 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_con
       tc_fence_after();
       const int q = warp & 3;
       const int row = ctile * kTcRows + 32 * q + lane;
-      for (int c0 = 0; c0 < a.ntile; c0 += 32) {
-        float v[32];
-        tmem_ld32(tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)c0, v);
+      for (int c0 = 0; c0 < a.ntile; c0 += 16) {
+        float v[16];
+        tmem_ld16(tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)c0, v);
         if (ok && row < a.rows) {
+          const int64_t tok0 = (int64_t)tt * a.ntile + c0;
+          float *p = a.C + tok0 * a.ldc + row;
+          if (a.accumulate) {  // all 16 reads in flight before the first write
+            float old[16];
 #pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            const int64_t tok = (int64_t)tt * a.ntile + c0 + j;
-            if (tok < a.M) {
-              float *p = a.C + tok * a.ldc + row;
-              const float r = v[j] * (1.0f / kTcAScale);
-              *p = a.accumulate ? (*p + r) : r;
-            }
+            for (int j = 0; j < 16; ++j) old[j] = tok0 + j < a.M ? p[(int64_t)j * a.ldc] : 0.f;
+#pragma unroll
+            for (int j = 0; j < 16; ++j)
+              if (tok0 + j < a.M) p[(int64_t)j * a.ldc] = old[j] + v[j] * (1.0f / kTcAScale);
+          } else {
+#pragma unroll
+            for (int j = 0; j < 16; ++j)
+              if (tok0 + j < a.M) p[(int64_t)j * a.ldc] = v[j] * (1.0f / kTcAScale);
           }
         }
       }
@@ -460,12 +506,12 @@ int tc_gemm_ntile(int64_t M) {
   return (int)std::min<int64_t>(256, std::max<int64_t>(32, n));
 }
 
-bool tc_gemm_eligible(int64_t K) { return K % kTcKB == 0; }
+bool tc_gemm_eligible(int64_t K) { return K % kTcFetch == 0; }
 
 size_t tc_xtile_bytes(int64_t M, int64_t K) {
   const int nt = tc_gemm_ntile(M);
   const int64_t tiles = (M + nt - 1) / nt;
-  return (size_t)tiles * (size_t)(K / kTcKB) * 2 * (size_t)nt * 128;
+  return (size_t)tiles * (size_t)(K / kTcKB) * 2 * (size_t)nt * kTcKB * 2;
 }
 
 ifx_status tc_stage_x(const float *X, const float *X2, const float *normw, float eps, int mode,
@@ -480,7 +526,7 @@ ifx_status tc_stage_x(const float *X, const float *X2, const float *normw, float
 
 ifx_status tc_gemm_run(const QMatrix &W, const void *xt, int64_t M, float *C, int64_t ldc,
                        int accumulate, int *err, cudaStream_t st) {
-  if (W.L.kc % kTcKB || W.L.cols % kTcKB)
+  if (W.L.kc % kTcFetch || W.L.cols % kTcFetch)
     return fail(IFX_ERR_UNSUPPORTED, "tc gemm: K blocks must be multiples of 64 columns");
   TcArgs a{};
   a.w = W.d;
@@ -500,7 +546,7 @@ ifx_status tc_gemm_run(const QMatrix &W, const void *xt, int64_t M, float *C, in
   a.tmem_cols = a.ntile <= 32 ? 32 : a.ntile <= 64 ? 64 : a.ntile <= 128 ? 128 : 256;
   a.accumulate = accumulate;
   a.err = err;
-  const size_t smem = 1024 + (size_t)kTcStages * (2 * kATile + 2 * (size_t)a.ntile * 128);
+  const size_t smem = 1024 + (size_t)kTcStages * (2 * kATile + 2 * (size_t)a.ntile * kTcKB * 2);
   if (smem > 226 * 1024) return fail(IFX_ERR_UNSUPPORTED, "tc gemm: shared memory plan too large");
   static size_t attr = 0;  // the kernel's opt-in dynamic shared memory so far
   if (smem > attr) {
