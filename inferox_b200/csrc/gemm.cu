@@ -320,6 +320,15 @@ ifx_status gemm_stage_x(const float *X, const float *X2, const float *normw, flo
   return IFX_OK;
 }
 
+ifx_status gemm_run_multi(const QMatrix *const *W, float *const *C, const int64_t *ldc, int n,
+                          const void *xfrag, int64_t M, int accumulate, int *err,
+                          cudaStream_t st) {
+  if (n >= 1 && tc_gemm_eligible(W[0]->L.cols))
+    return tc_gemm_run_multi(W, C, ldc, n, xfrag, M, accumulate, err, st);
+  for (int i = 0; i < n; ++i) IFX_TRY(gemm_run(*W[i], xfrag, M, C[i], ldc[i], accumulate, err, st));
+  return IFX_OK;
+}
+
 ifx_status gemm_run(const QMatrix &W, const void *xfrag, int64_t M, float *C, int64_t ldc,
                     int accumulate, int *err, cudaStream_t st) {
   if (tc_gemm_eligible(W.L.cols)) return tc_gemm_run(W, xfrag, M, C, ldc, accumulate, err, st);

@@ -32,5 +32,14 @@ ifx_status tc_stage_x(const float *X, const float *X2, const float *normw, float
                       int64_t M, int64_t K, void *xt, cudaStream_t st);
 ifx_status tc_gemm_run(const QMatrix &W, const void *xt, int64_t M, float *C, int64_t ldc,
                        int accumulate, int *err, cudaStream_t st);
+ifx_status tc_gemm_run_multi(const QMatrix *const *W, float *const *C, const int64_t *ldc, int n,
+                             const void *xt, int64_t M, int accumulate, int *err,
+                             cudaStream_t st);
+
+// n (<= 3) matrices with the same K over one staged input: a single launch on
+// the tensor-memory path (their row tiles side by side), in turn otherwise.
+ifx_status gemm_run_multi(const QMatrix *const *W, float *const *C, const int64_t *ldc, int n,
+                          const void *xfrag, int64_t M, int accumulate, int *err,
+                          cudaStream_t st);
 
 }  // namespace ifx

@@ -706,9 +706,12 @@ ifx_status Model::run_prompt(KvCache *kvp, const uint32_t *ids, size_t n, float 
   for (uint64_t l = 0; l < c.n_layers; ++l) {
     Layer &L = layers[l];
     IFX_TRY(gemm_stage_x(w_x, nullptr, L.attn_norm, c.norm_eps, GX_RMSNORM, N, D, w_xf, st));
-    IFX_TRY(gemm_run(L.wq, w_xf, N, w_q, Hh, 0, err, st));
-    IFX_TRY(gemm_run(L.wk, w_xf, N, w_k, kvd, 0, err, st));
-    IFX_TRY(gemm_run(L.wv, w_xf, N, w_v, kvd, 0, err, st));
+    {  // Wq, Wk, Wv over one staged input
+      const QMatrix *ws[3] = {&L.wq, &L.wk, &L.wv};
+      float *cs[3] = {w_q, w_k, w_v};
+      const int64_t ls[3] = {Hh, kvd, kvd};
+      IFX_TRY(gemm_run_multi(ws, cs, ls, 3, w_xf, N, 0, err, st));
+    }
     IFX_TRY(op_rope(w_q, n, H, hd, c.rope_dim, c.rope_base, pos0, st));
     IFX_TRY(op_rope(w_k, n, G, hd, c.rope_dim, c.rope_base, pos0, st));
     if (kvp) {
@@ -729,8 +732,12 @@ ifx_status Model::run_prompt(KvCache *kvp, const uint32_t *ids, size_t n, float 
       IFX_TRY(gemm_run(L.wo, w_xf, N, w_x, D, 1, err, st));
     }
     IFX_TRY(gemm_stage_x(w_x, nullptr, L.ffn_norm, c.norm_eps, GX_RMSNORM, N, D, w_xf, st));
-    IFX_TRY(gemm_run(L.w1, w_xf, N, w_gate, F, 0, err, st));
-    IFX_TRY(gemm_run(L.w3, w_xf, N, w_up, F, 0, err, st));
+    {  // W1, W3 over one staged input
+      const QMatrix *ws[2] = {&L.w1, &L.w3};
+      float *cs[2] = {w_gate, w_up};
+      const int64_t ls[2] = {F, F};
+      IFX_TRY(gemm_run_multi(ws, cs, ls, 2, w_xf, N, 0, err, st));
+    }
     IFX_TRY(gemm_stage_x(w_gate, w_up, nullptr, 0.f, GX_SWIGLU, N, F, w_xf, st));
     if (tp > 1) {
       IFX_TRY(tp_partial_begin((size_t)N * D, st, w_y, w_x));

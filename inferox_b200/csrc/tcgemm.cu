@@ -174,12 +174,21 @@ __global__ void tc_stage_x_kernel(const float *X, const float *X2, const float *
   }
 }
 
-struct TcArgs {
-  const uint8_t *w;   // repacked units
-  const uint8_t *xt;  // staged activation tiles
+constexpr int kTcMaxSegs = 3;
+
+// One weight matrix of a launch; its row tiles are CTAs [ctile0, ctile0 + ctiles).
+struct TcSeg {
+  const uint8_t *w;  // repacked units
   float *C;
   int64_t ldc;
-  int M, type, rows, kc, kunits, unit_bytes, wt_bytes, wt_qbytes, nkb, ntile, tmem_cols;
+  int type, rows, kc, kunits, unit_bytes, wt_bytes, wt_qbytes, ctile0, ctiles;
+};
+
+struct TcArgs {
+  TcSeg seg[kTcMaxSegs];  // matrices sharing K and the staged input
+  int nseg;
+  const uint8_t *xt;  // staged activation tiles
+  int M, nkb, ntile, tmem_cols;
   int accumulate;
   int *err;
 };
@@ -194,7 +203,7 @@ struct TcRaw {
 };
 
 template <int TYPE>
-__device__ __forceinline__ void tc_fetch(const TcArgs &a, int ctile, int wt, int kb, int lane,
+__device__ __forceinline__ void tc_fetch(const TcSeg &a, int ctile, int wt, int kb, int lane,
                                          TcRaw &R) {
   const int g = lane >> 2;
   const int bpu = a.kc / kTcFetch;  // fetch blocks per unit
@@ -249,7 +258,7 @@ __device__ __forceinline__ void tc_store_pair(float x0, float x1, uint8_t *ahi, 
 // Q4_K group, two Q6_K scale groups, one Q4_0 / Q8_0 block: the scales are
 // decoded once per stage, pre-multiplied by 2^8.
 template <int TYPE>
-__device__ __forceinline__ void tc_emit(const TcArgs &a, const TcRaw &R, int wt, int kb, int half,
+__device__ __forceinline__ void tc_emit(const TcSeg &a, const TcRaw &R, int wt, int kb, int half,
                                         int lane, uint8_t *ahi, uint8_t *alo) {
   const int g = lane >> 2, c = lane & 3;
   const int bpu = a.kc / kTcFetch;
@@ -344,14 +353,14 @@ __device__ __forceinline__ void tc_emit(const TcArgs &a, const TcRaw &R, int wt,
 }
 
 template <int TYPE>
-__device__ __forceinline__ void tc_dequant_loop(const TcArgs &a, int ctile, int wt, int lane,
-                                                uint8_t *stages, int stage_bytes,
+__device__ __forceinline__ void tc_dequant_loop(const TcArgs &a, const TcSeg &S, int ctile, int wt,
+                                                int lane, uint8_t *stages, int stage_bytes,
                                                 uint64_t *a_full, uint64_t *empty) {
   TcRaw R{}, Rn{};
   const int nfb = a.nkb / 2;  // fetch blocks (two stages each)
-  tc_fetch<TYPE>(a, ctile, wt, 0, lane, R);
+  tc_fetch<TYPE>(S, ctile, wt, 0, lane, R);
   for (int fb = 0; fb < nfb; ++fb) {
-    if (fb + 1 < nfb) tc_fetch<TYPE>(a, ctile, wt, fb + 1, lane, Rn);  // one block ahead
+    if (fb + 1 < nfb) tc_fetch<TYPE>(S, ctile, wt, fb + 1, lane, Rn);  // one block ahead
 #pragma unroll
     for (int half = 0; half < 2; ++half) {
       const int kb = 2 * fb + half;
@@ -359,7 +368,7 @@ __device__ __forceinline__ void tc_dequant_loop(const TcArgs &a, int ctile, int 
       const uint32_t ph = (uint32_t)(kb / kTcStages) & 1u;
       if (kb >= kTcStages && !mbar_wait(&empty[s], ph ^ 1u, a.err, 302)) return;
       uint8_t *ahi = stages + (size_t)s * stage_bytes;
-      tc_emit<TYPE>(a, R, wt, fb, half, lane, ahi, ahi + kATile);
+      tc_emit<TYPE>(S, R, wt, fb, half, lane, ahi, ahi + kATile);
       fence_async_smem();
       mbar_arrive(&a_full[s]);
     }
@@ -376,7 +385,12 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_con
   uint8_t *stages = smem_raw + pad;
   const int btile = a.ntile * kTcKB * 2;            // bytes of one B plane per stage
   const int stage_bytes = 2 * kATile + 2 * btile;   // A hi, A lo, B hi, B lo
-  const int ctile = blockIdx.x, tt = blockIdx.y;
+  int si = 0;  // this CTA's matrix
+#pragma unroll
+  for (int i = 1; i < kTcMaxSegs; ++i)
+    if (i < a.nseg && (int)blockIdx.x >= a.seg[i].ctile0) si = i;
+  const TcSeg &S = a.seg[si];
+  const int ctile = (int)blockIdx.x - S.ctile0, tt = blockIdx.y;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
   if (threadIdx.x == 0) {
@@ -403,16 +417,16 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_con
   if (warp == 0) {
     if (lane == 0) {  // activation tiles; the row tile's weight units are pulled into L2
       // two units ahead of the dequantising warps, so their loads hit L2
-      const int kpu = a.kc / kTcKB;  // k-blocks per unit
-      const uint8_t *wrow = a.w + (size_t)ctile * a.kunits * a.unit_bytes;
-      for (int u = 0; u < 2 && u < a.kunits; ++u)
-        prefetch_l2(wrow + (size_t)u * a.unit_bytes, (uint32_t)a.unit_bytes);
+      const int kpu = S.kc / kTcKB;  // k-blocks per unit
+      const uint8_t *wrow = S.w + (size_t)ctile * S.kunits * S.unit_bytes;
+      for (int u = 0; u < 2 && u < S.kunits; ++u)
+        prefetch_l2(wrow + (size_t)u * S.unit_bytes, (uint32_t)S.unit_bytes);
       int issued = 0;
       for (int kb = 0; kb < a.nkb; ++kb) {
         const int s = kb % kTcStages;
         const uint32_t ph = (uint32_t)(kb / kTcStages) & 1u;
-        if (kb % kpu == 0 && kb / kpu + 2 < a.kunits)
-          prefetch_l2(wrow + (size_t)(kb / kpu + 2) * a.unit_bytes, (uint32_t)a.unit_bytes);
+        if (kb % kpu == 0 && kb / kpu + 2 < S.kunits)
+          prefetch_l2(wrow + (size_t)(kb / kpu + 2) * S.unit_bytes, (uint32_t)S.unit_bytes);
         if (kb >= kTcStages && !mbar_wait(&empty[s], ph ^ 1u, a.err, 301)) break;
         uint8_t *bdst = stages + (size_t)s * stage_bytes + 2 * kATile;
         const uint8_t *src = a.xt + (size_t)(((int64_t)tt * a.nkb + kb) * 2) * btile;
@@ -448,18 +462,18 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_con
     }
   } else if (warp >= kTcDeq0) {
     const int wt = warp - kTcDeq0;
-    switch (a.type) {
+    switch (S.type) {
       case IFX_TYPE_Q4_K:
-        tc_dequant_loop<IFX_TYPE_Q4_K>(a, ctile, wt, lane, stages, stage_bytes, a_full, empty);
+        tc_dequant_loop<IFX_TYPE_Q4_K>(a, S, ctile, wt, lane, stages, stage_bytes, a_full, empty);
         break;
       case IFX_TYPE_Q6_K:
-        tc_dequant_loop<IFX_TYPE_Q6_K>(a, ctile, wt, lane, stages, stage_bytes, a_full, empty);
+        tc_dequant_loop<IFX_TYPE_Q6_K>(a, S, ctile, wt, lane, stages, stage_bytes, a_full, empty);
         break;
       case IFX_TYPE_Q4_0:
-        tc_dequant_loop<IFX_TYPE_Q4_0>(a, ctile, wt, lane, stages, stage_bytes, a_full, empty);
+        tc_dequant_loop<IFX_TYPE_Q4_0>(a, S, ctile, wt, lane, stages, stage_bytes, a_full, empty);
         break;
       default:
-        tc_dequant_loop<IFX_TYPE_Q8_0>(a, ctile, wt, lane, stages, stage_bytes, a_full, empty);
+        tc_dequant_loop<IFX_TYPE_Q8_0>(a, S, ctile, wt, lane, stages, stage_bytes, a_full, empty);
         break;
     }
     if (warp < kTcDeq0 + 4) {  // epilogue: warp w reads tensor-memory lanes 32 (w % 4) ..
@@ -470,20 +484,21 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_con
       for (int c0 = 0; c0 < a.ntile; c0 += 16) {
         float v[16];
         tmem_ld16(tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)c0, v);
-        if (ok && row < a.rows) {
+        if (ok && row < S.rows) {
           const int64_t tok0 = (int64_t)tt * a.ntile + c0;
-          float *p = a.C + tok0 * a.ldc + row;
+          const int64_t ldc = S.ldc;
+          float *p = S.C + tok0 * ldc + row;
           if (a.accumulate) {  // all 16 reads in flight before the first write
             float old[16];
 #pragma unroll
-            for (int j = 0; j < 16; ++j) old[j] = tok0 + j < a.M ? p[(int64_t)j * a.ldc] : 0.f;
+            for (int j = 0; j < 16; ++j) old[j] = tok0 + j < a.M ? p[(int64_t)j * ldc] : 0.f;
 #pragma unroll
             for (int j = 0; j < 16; ++j)
-              if (tok0 + j < a.M) p[(int64_t)j * a.ldc] = old[j] + v[j] * (1.0f / kTcAScale);
+              if (tok0 + j < a.M) p[(int64_t)j * ldc] = old[j] + v[j] * (1.0f / kTcAScale);
           } else {
 #pragma unroll
             for (int j = 0; j < 16; ++j)
-              if (tok0 + j < a.M) p[(int64_t)j * a.ldc] = v[j] * (1.0f / kTcAScale);
+              if (tok0 + j < a.M) p[(int64_t)j * ldc] = v[j] * (1.0f / kTcAScale);
           }
         }
       }
@@ -524,24 +539,35 @@ ifx_status tc_stage_x(const float *X, const float *X2, const float *normw, float
   return IFX_OK;
 }
 
-ifx_status tc_gemm_run(const QMatrix &W, const void *xt, int64_t M, float *C, int64_t ldc,
-                       int accumulate, int *err, cudaStream_t st) {
-  if (W.L.kc % kTcFetch || W.L.cols % kTcFetch)
-    return fail(IFX_ERR_UNSUPPORTED, "tc gemm: K blocks must be multiples of 64 columns");
+ifx_status tc_gemm_run_multi(const QMatrix *const *W, float *const *C, const int64_t *ldc, int n,
+                             const void *xt, int64_t M, int accumulate, int *err,
+                             cudaStream_t st) {
+  if (n < 1 || n > kTcMaxSegs) return fail(IFX_ERR_INVALID_ARGUMENT, "tc gemm: 1 to 3 matrices");
   TcArgs a{};
-  a.w = W.d;
+  int ct = 0;
+  for (int i = 0; i < n; ++i) {
+    const QLayout &L = W[i]->L;
+    if (L.kc % kTcFetch || L.cols % kTcFetch || L.cols != W[0]->L.cols)
+      return fail(IFX_ERR_UNSUPPORTED, "tc gemm: K blocks must be multiples of 64 columns");
+    TcSeg &S = a.seg[i];
+    S.w = W[i]->d;
+    S.C = C[i];
+    S.ldc = ldc[i];
+    S.type = L.type;
+    S.rows = (int)L.rows;
+    S.kc = L.kc;
+    S.kunits = L.kunits;
+    S.unit_bytes = L.unit_bytes;
+    S.wt_bytes = L.wt_bytes;
+    S.wt_qbytes = L.wt_qbytes;
+    S.ctile0 = ct;
+    S.ctiles = L.ctiles;
+    ct += L.ctiles;
+  }
+  a.nseg = n;
   a.xt = reinterpret_cast<const uint8_t *>(xt);
-  a.C = C;
-  a.ldc = ldc;
   a.M = (int)M;
-  a.type = W.L.type;
-  a.rows = (int)W.L.rows;
-  a.kc = W.L.kc;
-  a.kunits = W.L.kunits;
-  a.unit_bytes = W.L.unit_bytes;
-  a.wt_bytes = W.L.wt_bytes;
-  a.wt_qbytes = W.L.wt_qbytes;
-  a.nkb = (int)(W.L.cols / kTcKB);
+  a.nkb = (int)(W[0]->L.cols / kTcKB);
   a.ntile = tc_gemm_ntile(M);
   a.tmem_cols = a.ntile <= 32 ? 32 : a.ntile <= 64 ? 64 : a.ntile <= 128 ? 128 : 256;
   a.accumulate = accumulate;
@@ -554,10 +580,18 @@ ifx_status tc_gemm_run(const QMatrix &W, const void *xt, int64_t M, float *C, in
                                   (int)smem));
     attr = smem;
   }
-  dim3 grid((unsigned)W.L.ctiles, (unsigned)((M + a.ntile - 1) / a.ntile));
+  dim3 grid((unsigned)ct, (unsigned)((M + a.ntile - 1) / a.ntile));
   tc_gemm_kernel<<<grid, kTcThreads, smem, st>>>(a);
   IFX_CUDA(cudaGetLastError());
   return IFX_OK;
+}
+
+ifx_status tc_gemm_run(const QMatrix &W, const void *xt, int64_t M, float *C, int64_t ldc,
+                       int accumulate, int *err, cudaStream_t st) {
+  const QMatrix *w[1] = {&W};
+  float *c[1] = {C};
+  const int64_t l[1] = {ldc};
+  return tc_gemm_run_multi(w, c, l, 1, xt, M, accumulate, err, st);
 }
 
 }  // namespace ifx
