@@ -163,6 +163,33 @@ ifx_status ifx_decode_greedy(ifx_model *m, ifx_kv *kv, uint32_t token,
                              size_t n_steps, uint32_t *out_tokens,
                              float *device_ms);
 
+/* Batched decode: `batch` (1-32) independent sequences sharing every weight
+ * read of a step. The reference's KvCache holds one sequence
+ * (src/model/cache.rs:7-13); this is that cache times `batch`, each
+ * sequence with its own length, prefilled one at a time and decoded
+ * together (Model::decode_step, forward.rs:543-586, for every sequence at
+ * once). Single GPU only (IFX_ERR_UNSUPPORTED under tensor parallelism). */
+typedef struct ifx_kv_batch ifx_kv_batch;
+ifx_status ifx_kv_batch_create(ifx_model *m, size_t max_seq_len, int batch,
+                               ifx_kv_batch **out);
+void ifx_kv_batch_free(ifx_kv_batch *kb);
+/* KvCache::len (cache.rs:31-33) of sequence `seq`. */
+ifx_status ifx_kv_batch_len(const ifx_kv_batch *kb, int seq, size_t *len);
+/* Model::prefill (forward.rs:496-538) of sequence `seq` of the batch. */
+ifx_status ifx_prefill_seq(ifx_model *m, ifx_kv_batch *kb, int seq,
+                           const uint32_t *ids, size_t n, float *logits_host,
+                           int last_row_only);
+/* One decode step of every sequence: tokens [batch]; logits_host
+ * [batch, vocab] and argmax_host [batch] (last index on ties) are nullable. */
+ifx_status ifx_decode_step_batch(ifx_model *m, ifx_kv_batch *kb,
+                                 const uint32_t *tokens, float *logits_host,
+                                 uint32_t *argmax_host);
+/* n_steps greedy steps of every sequence, each step's argmax fed to the next
+ * on the device; out_tokens [n_steps, batch] and device_ms are nullable. */
+ifx_status ifx_decode_greedy_batch(ifx_model *m, ifx_kv_batch *kb,
+                                   const uint32_t *tokens, size_t n_steps,
+                                   uint32_t *out_tokens, float *device_ms);
+
 /* Sampler (src/sampler.rs:8-16). */
 typedef struct ifx_sampler {
   float temperature; /* 0 = greedy argmax */

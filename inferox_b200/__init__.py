@@ -6,6 +6,6 @@ Rust API. Import fails loudly if the library is missing: there is no CPU
 fallback.
 """
 from ._lib import IfxError, header_symbols, lib  # noqa: F401
-from .model import KvCache, Model, Sampler, load_opts  # noqa: F401
+from .model import KvBatch, KvCache, Model, Sampler, load_opts  # noqa: F401
 
-__all__ = ["Model", "KvCache", "Sampler", "IfxError", "load_opts", "lib", "header_symbols"]
+__all__ = ["Model", "KvCache", "KvBatch", "Sampler", "IfxError", "load_opts", "lib", "header_symbols"]

@@ -108,6 +108,12 @@ def _load():
         "ifx_sample": (st, [vp, C.POINTER(SamplerC), C.c_uint64, C.c_uint64, u32p]),
         "ifx_decode_greedy": (st, [vp, vp, C.c_uint32, sz, u32p, fp]),
         "ifx_bench_kernel": (st, [vp, vp, C.c_char_p, C.c_int, fp, C.POINTER(C.c_uint64)]),
+        "ifx_kv_batch_create": (st, [vp, sz, C.c_int, C.POINTER(vp)]),
+        "ifx_kv_batch_free": (None, [vp]),
+        "ifx_kv_batch_len": (st, [vp, C.c_int, C.POINTER(sz)]),
+        "ifx_prefill_seq": (st, [vp, vp, C.c_int, u32p, sz, fp, C.c_int]),
+        "ifx_decode_step_batch": (st, [vp, vp, u32p, fp, u32p]),
+        "ifx_decode_greedy_batch": (st, [vp, vp, u32p, sz, u32p, fp]),
         "ifx_op_dequantize": (st, [C.c_int, vp, sz, vp, sz, vp]),
         "ifx_op_matmul": (st, [vp, vp, vp, sz, sz, sz, vp]),
         "ifx_op_matmul_t": (st, [vp, vp, vp, sz, sz, sz, vp]),

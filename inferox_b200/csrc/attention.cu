@@ -27,8 +27,15 @@ __device__ __forceinline__ void rope_pair(float &a, float &b, int i, int rope_di
 
 __global__ void __launch_bounds__(kAttnThreads) decode_attn_kernel(const __grid_constant__ DecodeAttnArgs a) {
   extern __shared__ __align__(128) uint8_t smraw[];
-  const int h = blockIdx.x, s = blockIdx.y, tid = threadIdx.x;
+  const int h = blockIdx.x, s = blockIdx.y, b = blockIdx.z, tid = threadIdx.x;
   const int grp = a.H / a.G, hd = a.hd, NS = a.ns;
+  // this sequence's slices of the inputs, caches, partials and output
+  const float *qkv = a.qkv + (size_t)b * a.qkv_stride;
+  __half *kcb = a.kc + (size_t)b * a.kv_seq_stride, *vcb = a.vc + (size_t)b * a.kv_seq_stride;
+  float *part_o = a.part_o + (size_t)b * a.G * NS * grp * hd;
+  float2 *part_ml = a.part_ml + (size_t)b * a.G * NS * grp;
+  int *counters = a.counters + (size_t)b * a.G;
+  float *attn_out = a.attn_out + (size_t)b * a.H * hd;
   const int cap = (a.max_seq + NS - 1) / NS + 1;
   __half *Ks = reinterpret_cast<__half *>(smraw);  // [cap][hd]
   __half *Vs = Ks + (size_t)cap * hd;               // [cap][hd]
@@ -41,14 +48,14 @@ __global__ void __launch_bounds__(kAttnThreads) decode_attn_kernel(const __grid_
   // written by kernels that completed before the previous kernel in the
   // stream started its main phase, so this CTA's chunk can be fetched while
   // the QKV GEMV is still draining.
-  const int pos = *a.pos;
+  const int pos = a.pos[b];
   const int len = pos + 1;
   const int chunk = (len + NS - 1) / NS;
   const int t0 = s * chunk, t1 = min(len, t0 + chunk);
   const int nk = max(0, t1 - t0);
   const int nold = max(0, min(t1, pos) - t0);  // rows already in the cache
-  __half *kc = a.kc + (size_t)h * a.max_seq * hd;
-  __half *vc = a.vc + (size_t)h * a.max_seq * hd;
+  __half *kc = kcb + (size_t)h * a.max_seq * hd;
+  __half *vc = vcb + (size_t)h * a.max_seq * hd;
   const uint32_t row_bytes = (uint32_t)hd * 2u;
   if (tid == 0) {
     mbar_init(&bar, 1);
@@ -64,12 +71,12 @@ __global__ void __launch_bounds__(kAttnThreads) decode_attn_kernel(const __grid_
   pdl_wait();
   pdl_launch();
 
-  if (a.zero_ptr) {
+  if (a.zero_ptr && b == 0) {
     const int nb = a.G * NS, b = h * NS + s;
     for (int i = b * kAttnThreads + tid; i < a.zero_n; i += nb * kAttnThreads) a.zero_ptr[i] = 0.f;
   }
 
-  const float *q = a.qkv + (size_t)h * grp * hd;
+  const float *q = qkv + (size_t)h * grp * hd;
   const int rpos = a.rope_compat ? 0 : pos;
   for (int e = tid; e < grp * hd / 2; e += kAttnThreads) {
     const int j = e / (hd / 2), i = 2 * (e % (hd / 2));
@@ -80,8 +87,8 @@ __global__ void __launch_bounds__(kAttnThreads) decode_attn_kernel(const __grid_
   }
   if (t0 <= pos && pos < t1) {
     // append this token's K/V (forward.rs:375-378), K rotated like q
-    const float *kn = a.qkv + (size_t)a.H * hd + (size_t)h * hd;
-    const float *vn = a.qkv + (size_t)(a.H + a.G) * hd + (size_t)h * hd;
+    const float *kn = qkv + (size_t)a.H * hd + (size_t)h * hd;
+    const float *vn = qkv + (size_t)(a.H + a.G) * hd + (size_t)h * hd;
     const int r = pos - t0;
     for (int e = tid; e < hd / 2; e += kAttnThreads) {
       const int i = 2 * e;
@@ -140,18 +147,18 @@ __global__ void __launch_bounds__(kAttnThreads) decode_attn_kernel(const __grid_
     }
   }
   __syncthreads();
-  float *po = a.part_o + (size_t)(h * NS + s) * grp * hd;
+  float *po = part_o + (size_t)(h * NS + s) * grp * hd;
   for (int e = tid; e < grp * hd; e += kAttnThreads) {
     const int j = e / hd, d = e % hd;
     float o = 0.f;
     for (int t = 0; t < nk; ++t) o = fmaf(sc[j * cap + t], __half2float(Vs[(size_t)t * hd + d]), o);
     po[e] = o;
   }
-  if (tid < grp) a.part_ml[(h * NS + s) * grp + tid] = make_float2(s_m[tid], s_l[tid]);
+  if (tid < grp) part_ml[(h * NS + s) * grp + tid] = make_float2(s_m[tid], s_l[tid]);
   __threadfence();
   __syncthreads();
   if (tid == 0) {
-    const int prev = atomicAdd(&a.counters[h], 1);
+    const int prev = atomicAdd(&counters[h], 1);
     s_last = (prev == NS - 1);
   }
   __syncthreads();
@@ -162,7 +169,7 @@ __global__ void __launch_bounds__(kAttnThreads) decode_attn_kernel(const __grid_
   __shared__ float c_m[kMaxSplits * kMaxGroup], c_w[kMaxSplits * kMaxGroup], c_M[kMaxGroup],
       c_L[kMaxGroup];
   for (int e = tid; e < NS * grp; e += kAttnThreads) {
-    const float2 ml = __ldcg(&a.part_ml[h * NS * grp + e]);
+    const float2 ml = __ldcg(&part_ml[h * NS * grp + e]);
     c_m[e] = ml.x;
     c_w[e] = ml.y;
   }
@@ -183,8 +190,8 @@ __global__ void __launch_bounds__(kAttnThreads) decode_attn_kernel(const __grid_
     c_w[e] = (c_w[e] > 0.f) ? expf(c_m[e] - c_M[j]) / c_L[j] : 0.f;
   }
   __syncthreads();
-  const float4 *po4 = reinterpret_cast<const float4 *>(a.part_o + (size_t)h * NS * grp * hd);
-  float4 *out4 = reinterpret_cast<float4 *>(a.attn_out + (size_t)h * grp * hd);
+  const float4 *po4 = reinterpret_cast<const float4 *>(part_o + (size_t)h * NS * grp * hd);
+  float4 *out4 = reinterpret_cast<float4 *>(attn_out + (size_t)h * grp * hd);
   const int n4 = grp * hd / 4;
   for (int e4 = tid; e4 < n4; e4 += kAttnThreads) {
     const int j = (e4 * 4) / hd;
@@ -200,7 +207,7 @@ __global__ void __launch_bounds__(kAttnThreads) decode_attn_kernel(const __grid_
     }
     out4[e4] = o;
   }
-  if (tid == 0) a.counters[h] = 0;
+  if (tid == 0) counters[h] = 0;
 }
 
 // ------------------------------------------------------------ prefill ----
@@ -315,7 +322,7 @@ ifx_status decode_attention(const DecodeAttnArgs &a, cudaStream_t st, bool pdl) 
                                   (int)smem));
     attr = smem;
   }
-  IFX_CUDA(launch(decode_attn_kernel, dim3(a.G, a.ns), dim3(kAttnThreads), smem, st, pdl, a));
+  IFX_CUDA(launch(decode_attn_kernel, dim3(a.G, a.ns, a.batch), dim3(kAttnThreads), smem, st, pdl, a));
   return IFX_OK;
 }
 

@@ -19,6 +19,11 @@ struct DecodeAttnArgs {
   int rope_dim;
   float rope_base;
   int *err;
+  // batched decode (gridDim.z = sequences): sequence b reads qkv + b * qkv_stride,
+  // its caches at kc/vc + b * kv_seq_stride, its position pos[b], and uses its
+  // own partials, counters and output row (attn_out + b * H * hd)
+  int64_t qkv_stride = 0, kv_seq_stride = 0;
+  int batch = 1;
 };
 
 ifx_status decode_attention(const DecodeAttnArgs &a, cudaStream_t st, bool pdl);

@@ -23,6 +23,9 @@ struct ifx_kv {
 struct ifx_qmatrix {
   ifx::QMatrix q;
 };
+struct ifx_kv_batch {
+  ifx::KvBatch kb;
+};
 
 namespace ifx {
 
@@ -216,6 +219,50 @@ ifx_status ifx_decode_greedy(ifx_model *m, ifx_kv *kv, uint32_t token, size_t n_
   if (!m || !kv) return fail(IFX_ERR_INVALID_ARGUMENT, "decode_greedy: null argument");
   if (kv->kv.m != &m->m) return fail(IFX_ERR_INVALID_ARGUMENT, "decode_greedy: kv belongs to another model");
   IFX_GUARD({ return m->m.decode_greedy(kv->kv, token, n_steps, out_tokens, device_ms); })
+}
+
+ifx_status ifx_kv_batch_create(ifx_model *m, size_t max_seq_len, int batch, ifx_kv_batch **out) {
+  if (!m || !out || !max_seq_len) return fail(IFX_ERR_INVALID_ARGUMENT, "kv_batch_create: bad argument");
+  IFX_GUARD({
+    ifx_kv_batch *kb = new ifx_kv_batch();
+    ifx_status s = kb->kb.create(&m->m, max_seq_len, batch);
+    if (s != IFX_OK) {
+      delete kb;
+      return s;
+    }
+    *out = kb;
+    return IFX_OK;
+  })
+}
+
+void ifx_kv_batch_free(ifx_kv_batch *kb) { delete kb; }
+
+ifx_status ifx_kv_batch_len(const ifx_kv_batch *kb, int seq, size_t *len) {
+  if (!kb || !len || seq < 0 || seq >= kb->kb.batch)
+    return fail(IFX_ERR_INVALID_ARGUMENT, "kv_batch_len: bad argument");
+  *len = kb->kb.len[(size_t)seq];
+  return IFX_OK;
+}
+
+ifx_status ifx_prefill_seq(ifx_model *m, ifx_kv_batch *kb, int seq, const uint32_t *ids, size_t n,
+                           float *logits_host, int last_row_only) {
+  if (!m || !kb || (!ids && n)) return fail(IFX_ERR_INVALID_ARGUMENT, "prefill_seq: null argument");
+  if (kb->kb.m != &m->m) return fail(IFX_ERR_INVALID_ARGUMENT, "prefill_seq: batch belongs to another model");
+  IFX_GUARD({ return m->m.prefill_seq(kb->kb, seq, ids, n, logits_host, last_row_only); })
+}
+
+ifx_status ifx_decode_step_batch(ifx_model *m, ifx_kv_batch *kb, const uint32_t *tokens,
+                                 float *logits_host, uint32_t *argmax_host) {
+  if (!m || !kb || !tokens) return fail(IFX_ERR_INVALID_ARGUMENT, "decode_step_batch: null argument");
+  if (kb->kb.m != &m->m) return fail(IFX_ERR_INVALID_ARGUMENT, "decode_step_batch: batch belongs to another model");
+  IFX_GUARD({ return m->m.decode_batch(kb->kb, tokens, logits_host, argmax_host); })
+}
+
+ifx_status ifx_decode_greedy_batch(ifx_model *m, ifx_kv_batch *kb, const uint32_t *tokens,
+                                   size_t n_steps, uint32_t *out_tokens, float *device_ms) {
+  if (!m || !kb || !tokens) return fail(IFX_ERR_INVALID_ARGUMENT, "decode_greedy_batch: null argument");
+  if (kb->kb.m != &m->m) return fail(IFX_ERR_INVALID_ARGUMENT, "decode_greedy_batch: batch belongs to another model");
+  IFX_GUARD({ return m->m.decode_greedy_batch(kb->kb, tokens, n_steps, out_tokens, device_ms); })
 }
 
 ifx_status ifx_bench_kernel(ifx_model *m, ifx_kv *kv, const char *which, int reps,

@@ -18,7 +18,9 @@ namespace {
 
 constexpr int kGThreads = 288;
 constexpr int kGStages = 2;
-constexpr int kXChunkBytes = 4096;  // one 16-column chunk of a 64-token block, hi + lo planes
+// One 16-column chunk of a block of 8 * NT tokens, hi + lo planes: NT n-tiles
+// x 32 lanes x 4 halves x 2 planes x 2 bytes.
+__host__ __device__ constexpr int xchunk_bytes(int nt) { return nt * 512; }
 
 __device__ __forceinline__ float silu_g(float v) {
   float c = fminf(fmaxf(v, -80.0f), 80.0f);
@@ -26,9 +28,10 @@ __device__ __forceinline__ float silu_g(float v) {
 }
 
 // X staging: one CTA per token row computes the row's transform and writes
-// its values into the fragment layout [mblock][chunk][nt][lane][4 halves].
+// its values into the fragment layout [mblock][chunk][plane][nt][lane][4
+// halves] of blocks of 8 * NT tokens, then the per-token 32-column sums.
 __global__ void stage_x_kernel(const float *X, const float *X2, const float *normw, float eps,
-                               int mode, int64_t M, int64_t K, __half *out) {
+                               int mode, int64_t M, int64_t K, int NT, __half *out) {
   const int64_t t = blockIdx.x;  // token (row), may be >= M for padding
   const int tid = threadIdx.x;
   __shared__ float red[32];
@@ -51,11 +54,12 @@ __global__ void stage_x_kernel(const float *X, const float *X2, const float *nor
     __syncthreads();
     inv = s_inv;
   }
-  const int64_t mb = t / kGemmTokens, tt = t % kGemmTokens;
+  const int tokb = 8 * NT;
+  const int64_t mb = t / tokb, tt = t % tokb;
   const int nt = (int)(tt / 8), g = (int)(tt % 8);
   const int64_t nch = K / 16, ngr = K / 32;
-  float *sums = reinterpret_cast<float *>(out + (size_t)((M + kGemmTokens - 1) / kGemmTokens) *
-                                                    (size_t)nch * (kXChunkBytes / 2));
+  float *sums = reinterpret_cast<float *>(out + (size_t)((M + tokb - 1) / tokb) * (size_t)nch *
+                                                    (size_t)(xchunk_bytes(NT) / 2));
   for (int64_t k0 = 0; k0 < K; k0 += blockDim.x) {  // blockDim.x % 32 == 0: a warp covers one group
     const int64_t k = k0 + tid;
     float v = 0.f;
@@ -74,10 +78,10 @@ __global__ void stage_x_kernel(const float *X, const float *X2, const float *nor
       // B fragment: b0 = (k 2c, 2c+1), b1 = (k 2c+8, 2c+9) of column g
       const int c = (kk % 8) / 2, hi = kk / 8, e = kk % 2;
       const int lane = g * 4 + c;
-      const int64_t idx = ((((mb * nch + ch) * 2) * 8 + nt) * 32 + lane) * 4 + hi * 2 + e;
+      const int64_t idx = ((((mb * nch + ch) * 2) * NT + nt) * 32 + lane) * 4 + hi * 2 + e;
       out[idx] = hv;
-      out[idx + 8 * 32 * 4] = lv;  // the lo plane follows the hi plane of the chunk
-      if ((tid & 31) == 0) sums[(mb * ngr + k / 32) * kGemmTokens + tt] = gs;
+      out[idx + NT * 32 * 4] = lv;  // the lo plane follows the hi plane of the chunk
+      if ((tid & 31) == 0) sums[(mb * ngr + k / 32) * tokb + tt] = gs;
     }
   }
 }
@@ -97,13 +101,14 @@ struct GemmArgs {
   float *C;
   int64_t ldc, M;
   int type, rows, kc, kunits, unit_bytes, wt_bytes, wt_qbytes, nch_total;
-  int accumulate;
+  int accumulate;  // C += result (else C = result)
+  int atomic;      // C += result with atomic adds (K split over gridDim.z CTAs)
   int *err;
 };
 
-template <int TYPE>
+template <int TYPE, int NT>
 __device__ __forceinline__ void gemm_unit(const uint8_t *wt, const uint8_t *xs, const float *sx,
-                                          int kc, int wt_qbytes, int lane, float (&acc)[8][4]) {
+                                          int kc, int wt_qbytes, int lane, float (&acc)[NT][4]) {
   const int g = lane >> 2, c = lane & 3;
   // chunks per scale group: Q6_K scales every 16 columns, the others every 32
   constexpr int cpg = (TYPE == IFX_TYPE_Q6_K) ? 1 : 2;
@@ -111,9 +116,9 @@ __device__ __forceinline__ void gemm_unit(const uint8_t *wt, const uint8_t *xs, 
   const __half2 b1024 = __float2half2_rn(1024.f);
 #pragma unroll 1
   for (int gi = 0; gi < ngr; ++gi) {
-    float tmp[8][4];
+    float tmp[NT][4];
 #pragma unroll
-    for (int nt = 0; nt < 8; ++nt) tmp[nt][0] = tmp[nt][1] = tmp[nt][2] = tmp[nt][3] = 0.f;
+    for (int nt = 0; nt < NT; ++nt) tmp[nt][0] = tmp[nt][1] = tmp[nt][2] = tmp[nt][3] = 0.f;
 #pragma unroll
     for (int cc = 0; cc < cpg; ++cc) {
       const int ch = gi * cpg + cc;
@@ -154,10 +159,10 @@ __device__ __forceinline__ void gemm_unit(const uint8_t *wt, const uint8_t *xs, 
         a[2] = h2u(__hsub2(u2h(prmt(w2.y, 0x64646464u, 0x4140u)), sub));
         a[3] = h2u(__hsub2(u2h(prmt(w2.y, 0x64646464u, 0x4342u)), sub));
       }
-      const uint2 *xb = reinterpret_cast<const uint2 *>(xs + (size_t)ch * kXChunkBytes) + lane;
+      const uint2 *xb = reinterpret_cast<const uint2 *>(xs + (size_t)ch * xchunk_bytes(NT)) + lane;
 #pragma unroll
-      for (int nt = 0; nt < 8; ++nt) {
-        const uint2 bh = xb[nt * 32], bl = xb[256 + nt * 32];
+      for (int nt = 0; nt < NT; ++nt) {
+        const uint2 bh = xb[nt * 32], bl = xb[NT * 32 + nt * 32];
         mma_16816(tmp[nt], a[0], a[1], a[2], a[3], bh.x, bh.y, tmp[nt]);
         mma_16816(tmp[nt], a[0], a[1], a[2], a[3], bl.x, bl.y, tmp[nt]);
       }
@@ -196,16 +201,16 @@ __device__ __forceinline__ void gemm_unit(const uint8_t *wt, const uint8_t *xs, 
       if (TYPE == IFX_TYPE_Q4_0) sB *= 0.0625f;
     }
 #pragma unroll
-    for (int nt = 0; nt < 8; ++nt) {
+    for (int nt = 0; nt < NT; ++nt) {
       acc[nt][0] = fmaf(sA, tmp[nt][0], acc[nt][0]);
       acc[nt][1] = fmaf(sA, tmp[nt][1], acc[nt][1]);
       acc[nt][2] = fmaf(sB, tmp[nt][2], acc[nt][2]);
       acc[nt][3] = fmaf(sB, tmp[nt][3], acc[nt][3]);
     }
     if (TYPE == IFX_TYPE_Q4_K) {  // - dmin * min * sum_k x_k over the group, per token
-      const float *sg = sx + gi * kGemmTokens + 2 * c;
+      const float *sg = sx + gi * (8 * NT) + 2 * c;
 #pragma unroll
-      for (int nt = 0; nt < 8; ++nt) {
+      for (int nt = 0; nt < NT; ++nt) {
         const float2 xs2 = *reinterpret_cast<const float2 *>(sg + nt * 8);
         acc[nt][0] = fmaf(-mA, xs2.x, acc[nt][0]);
         acc[nt][1] = fmaf(-mA, xs2.y, acc[nt][1]);
@@ -216,17 +221,23 @@ __device__ __forceinline__ void gemm_unit(const uint8_t *wt, const uint8_t *xs, 
   }
 }
 
+// Blocks of 8 * NT tokens x 128 weight rows; gridDim.z splits K (each z
+// takes a contiguous share of the row tile's units, results added
+// atomically).
+template <int NT>
 __global__ void __launch_bounds__(kGThreads, 1) gemm_kernel(const __grid_constant__ GemmArgs a) {
   extern __shared__ __align__(128) uint8_t smem[];
   uint64_t *full_bar = reinterpret_cast<uint64_t *>(smem);
   uint64_t *empty_bar = full_bar + kGStages;
-  const int xbytes = a.kc / 16 * kXChunkBytes;              // x hi + lo of the unit's columns
-  const int sbytes = a.kc / 32 * kGemmTokens * (int)sizeof(float);  // per-token group sums
+  constexpr int tokb = 8 * NT;
+  const int xbytes = a.kc / 16 * xchunk_bytes(NT);           // x hi + lo of the unit's columns
+  const int sbytes = a.kc / 32 * tokb * (int)sizeof(float);  // per-token group sums
   const int stage_bytes = a.unit_bytes + xbytes + sbytes;
   uint8_t *ring = smem + 128;
   const int mb = blockIdx.x, ctile = blockIdx.y;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int n = a.kunits;
+  const int upc = (a.kunits + gridDim.z - 1) / gridDim.z;  // units per K split
+  const int u0 = blockIdx.z * upc, n = max(0, min(a.kunits, u0 + upc) - u0);
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kGStages; ++s) {
@@ -244,10 +255,12 @@ __global__ void __launch_bounds__(kGThreads, 1) gemm_kernel(const __grid_constan
         const uint32_t ph = (uint32_t)(i / kGStages) & 1u;
         if (i >= kGStages && !mbar_wait(&empty_bar[st], ph ^ 1u, a.err, 201)) break;
         uint8_t *dst = ring + (size_t)st * stage_bytes;
-        const uint8_t *wsrc = a.w + ((size_t)ctile * a.kunits + i) * a.unit_bytes;
-        const uint8_t *xsrc = a.x + ((size_t)mb * a.nch_total + (size_t)i * (a.kc / 16)) * kXChunkBytes;
+        const int u = u0 + i;
+        const uint8_t *wsrc = a.w + ((size_t)ctile * a.kunits + u) * a.unit_bytes;
+        const uint8_t *xsrc =
+            a.x + ((size_t)mb * a.nch_total + (size_t)u * (a.kc / 16)) * xchunk_bytes(NT);
         const uint8_t *ssrc = reinterpret_cast<const uint8_t *>(
-            a.sums + ((size_t)mb * (a.nch_total / 2) + (size_t)i * (a.kc / 32)) * kGemmTokens);
+            a.sums + ((size_t)mb * (a.nch_total / 2) + (size_t)u * (a.kc / 32)) * tokb);
         mbar_arrive_expect_tx(&full_bar[st], (uint32_t)stage_bytes);
         bulk_g2s(dst, wsrc, (uint32_t)a.unit_bytes, &full_bar[st]);
         bulk_g2s(dst + a.unit_bytes, xsrc, (uint32_t)xbytes, &full_bar[st]);
@@ -257,9 +270,10 @@ __global__ void __launch_bounds__(kGThreads, 1) gemm_kernel(const __grid_constan
     return;
   }
 
-  float acc[8][4];
+  if (n == 0) return;  // an empty K split (the producer issued nothing either)
+  float acc[NT][4];
 #pragma unroll
-  for (int i = 0; i < 8; ++i) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.f;
+  for (int i = 0; i < NT; ++i) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.f;
   for (int i = 0; i < n; ++i) {
     const int st = i % kGStages;
     const uint32_t ph = (uint32_t)(i / kGStages) & 1u;
@@ -267,12 +281,12 @@ __global__ void __launch_bounds__(kGThreads, 1) gemm_kernel(const __grid_constan
     const uint8_t *base = ring + (size_t)st * stage_bytes;
     const uint8_t *wt = base + (size_t)warp * a.wt_bytes;
     const uint8_t *xs = base + a.unit_bytes;
-    const float *sx = reinterpret_cast<const float *>(xs + a.kc / 16 * kXChunkBytes);
+    const float *sx = reinterpret_cast<const float *>(xs + a.kc / 16 * xchunk_bytes(NT));
     switch (a.type) {
-      case IFX_TYPE_Q4_K: gemm_unit<IFX_TYPE_Q4_K>(wt, xs, sx, a.kc, a.wt_qbytes, lane, acc); break;
-      case IFX_TYPE_Q6_K: gemm_unit<IFX_TYPE_Q6_K>(wt, xs, sx, a.kc, a.wt_qbytes, lane, acc); break;
-      case IFX_TYPE_Q4_0: gemm_unit<IFX_TYPE_Q4_0>(wt, xs, sx, a.kc, a.wt_qbytes, lane, acc); break;
-      default: gemm_unit<IFX_TYPE_Q8_0>(wt, xs, sx, a.kc, a.wt_qbytes, lane, acc); break;
+      case IFX_TYPE_Q4_K: gemm_unit<IFX_TYPE_Q4_K, NT>(wt, xs, sx, a.kc, a.wt_qbytes, lane, acc); break;
+      case IFX_TYPE_Q6_K: gemm_unit<IFX_TYPE_Q6_K, NT>(wt, xs, sx, a.kc, a.wt_qbytes, lane, acc); break;
+      case IFX_TYPE_Q4_0: gemm_unit<IFX_TYPE_Q4_0, NT>(wt, xs, sx, a.kc, a.wt_qbytes, lane, acc); break;
+      default: gemm_unit<IFX_TYPE_Q8_0, NT>(wt, xs, sx, a.kc, a.wt_qbytes, lane, acc); break;
     }
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty_bar[st]);
@@ -281,41 +295,98 @@ __global__ void __launch_bounds__(kGThreads, 1) gemm_kernel(const __grid_constan
   const int g = lane >> 2, c = lane & 3;
   const int r0 = ctile * 128 + warp * 16 + g;
 #pragma unroll
-  for (int nt = 0; nt < 8; ++nt)
+  for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
       const int row = r0 + ((j & 2) ? 8 : 0);
-      const int64_t tok = (int64_t)mb * kGemmTokens + nt * 8 + 2 * c + (j & 1);
+      const int64_t tok = (int64_t)mb * tokb + nt * 8 + 2 * c + (j & 1);
       if (row < a.rows && tok < a.M) {
         float *p = a.C + tok * a.ldc + row;
-        *p = a.accumulate ? (*p + acc[nt][j]) : acc[nt][j];
+        if (a.atomic) red_add_f32(p, acc[nt][j]);
+        else *p = a.accumulate ? (*p + acc[nt][j]) : acc[nt][j];
       }
     }
 }
 
 }  // namespace
 
-// Staged x of an M x K input: the hi/lo fragments of every 16-column chunk
-// of every 64-token block, then the per-token 32-column group sums.
-static size_t xfrag_frag_bytes(int64_t M, int64_t K) {
-  const int64_t mblocks = (M + kGemmTokens - 1) / kGemmTokens;
-  return (size_t)mblocks * (size_t)(K / 16) * kXChunkBytes;
+// Staged x of an M x K input in blocks of 8 * NT tokens: the hi/lo
+// fragments of every 16-column chunk of every block, then the per-token
+// 32-column group sums.
+static size_t xfrag_frag_bytes(int64_t M, int64_t K, int NT) {
+  const int64_t tokb = 8 * NT, mblocks = (M + tokb - 1) / tokb;
+  return (size_t)mblocks * (size_t)(K / 16) * (size_t)xchunk_bytes(NT);
 }
 
+static size_t xfrag_bytes(int64_t M, int64_t K, int NT) {
+  const int64_t tokb = 8 * NT, mblocks = (M + tokb - 1) / tokb;
+  return xfrag_frag_bytes(M, K, NT) + (size_t)mblocks * (size_t)(K / 32) * tokb * sizeof(float);
+}
+
+static int small_nt(int64_t M) { return M <= 16 ? 2 : 4; }
+
 size_t gemm_xfrag_bytes(int64_t M, int64_t K) {
-  const int64_t mblocks = (M + kGemmTokens - 1) / kGemmTokens;
-  const size_t sync_bytes =
-      xfrag_frag_bytes(M, K) + (size_t)mblocks * (size_t)(K / 32) * kGemmTokens * sizeof(float);
+  const size_t sync_bytes = xfrag_bytes(M, K, kGemmTokens / 8);
   return tc_gemm_eligible(K) ? std::max(sync_bytes, tc_xtile_bytes(M, K)) : sync_bytes;
+}
+
+size_t gemm_small_xfrag_bytes(int64_t M, int64_t K) { return xfrag_bytes(M, K, small_nt(M)); }
+
+static ifx_status stage_sync(const float *X, const float *X2, const float *normw, float eps,
+                             int mode, int64_t M, int64_t K, int NT, void *xfrag, cudaStream_t st) {
+  if (K % 32) return fail(IFX_ERR_SHAPE, "gemm: K must be a multiple of 32");
+  const int64_t tokb = 8 * NT, mpad = (M + tokb - 1) / tokb * tokb;
+  stage_x_kernel<<<(unsigned)mpad, 256, 0, st>>>(X, X2, normw, eps, mode, M, K, NT,
+                                                 reinterpret_cast<__half *>(xfrag));
+  IFX_CUDA(cudaGetLastError());
+  return IFX_OK;
 }
 
 ifx_status gemm_stage_x(const float *X, const float *X2, const float *normw, float eps, int mode,
                         int64_t M, int64_t K, void *xfrag, cudaStream_t st) {
   if (K % 32) return fail(IFX_ERR_SHAPE, "gemm: K must be a multiple of 32");
   if (tc_gemm_eligible(K)) return tc_stage_x(X, X2, normw, eps, mode, M, K, xfrag, st);
-  const int64_t mpad = (M + kGemmTokens - 1) / kGemmTokens * kGemmTokens;
-  stage_x_kernel<<<(unsigned)mpad, 256, 0, st>>>(X, X2, normw, eps, mode, M, K,
-                                                 reinterpret_cast<__half *>(xfrag));
+  return stage_sync(X, X2, normw, eps, mode, M, K, kGemmTokens / 8, xfrag, st);
+}
+
+ifx_status gemm_small_stage_x(const float *X, const float *X2, const float *normw, float eps,
+                              int mode, int64_t M, int64_t K, void *xfrag, cudaStream_t st) {
+  if (M > kGemmSmallMax) return fail(IFX_ERR_UNSUPPORTED, "gemm: small batch above 32 tokens");
+  return stage_sync(X, X2, normw, eps, mode, M, K, small_nt(M), xfrag, st);
+}
+
+template <int NT>
+static ifx_status launch_sync(const QMatrix &W, const void *xfrag, int64_t M, float *C,
+                              int64_t ldc, int accumulate, int ksplit, int *err, cudaStream_t st) {
+  GemmArgs a{};
+  a.w = W.d;
+  a.x = reinterpret_cast<const uint8_t *>(xfrag);
+  a.sums = reinterpret_cast<const float *>(a.x + xfrag_frag_bytes(M, W.L.cols, NT));
+  a.C = C;
+  a.ldc = ldc;
+  a.M = M;
+  a.type = W.L.type;
+  a.rows = (int)W.L.rows;
+  a.kc = W.L.kc;
+  a.kunits = W.L.kunits;
+  a.unit_bytes = W.L.unit_bytes;
+  a.wt_bytes = W.L.wt_bytes;
+  a.wt_qbytes = W.L.wt_qbytes;
+  a.nch_total = (int)(W.L.cols / 16);
+  a.accumulate = accumulate;
+  a.atomic = ksplit > 1 ? 1 : 0;
+  a.err = err;
+  const size_t smem = 128 + (size_t)kGStages * (a.unit_bytes + a.kc / 16 * xchunk_bytes(NT) +
+                                                a.kc / 32 * 8 * NT * sizeof(float));
+  if (smem > 226 * 1024) return fail(IFX_ERR_UNSUPPORTED, "gemm: shared memory plan too large");
+  static size_t attr = 0;
+  if (smem > attr) {
+    IFX_CUDA(cudaFuncSetAttribute(gemm_kernel<NT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  (int)smem));
+    attr = smem;
+  }
+  dim3 grid((unsigned)((M + 8 * NT - 1) / (8 * NT)), (unsigned)W.L.ctiles, (unsigned)ksplit);
+  gemm_kernel<NT><<<grid, kGThreads, smem, st>>>(a);
   IFX_CUDA(cudaGetLastError());
   return IFX_OK;
 }
@@ -332,36 +403,16 @@ ifx_status gemm_run_multi(const QMatrix *const *W, float *const *C, const int64_
 ifx_status gemm_run(const QMatrix &W, const void *xfrag, int64_t M, float *C, int64_t ldc,
                     int accumulate, int *err, cudaStream_t st) {
   if (tc_gemm_eligible(W.L.cols)) return tc_gemm_run(W, xfrag, M, C, ldc, accumulate, err, st);
-  GemmArgs a{};
-  a.w = W.d;
-  a.x = reinterpret_cast<const uint8_t *>(xfrag);
-  a.sums = reinterpret_cast<const float *>(a.x + xfrag_frag_bytes(M, W.L.cols));
-  a.C = C;
-  a.ldc = ldc;
-  a.M = M;
-  a.type = W.L.type;
-  a.rows = (int)W.L.rows;
-  a.kc = W.L.kc;
-  a.kunits = W.L.kunits;
-  a.unit_bytes = W.L.unit_bytes;
-  a.wt_bytes = W.L.wt_bytes;
-  a.wt_qbytes = W.L.wt_qbytes;
-  a.nch_total = (int)(W.L.cols / 16);
-  a.accumulate = accumulate;
-  a.err = err;
-  const size_t smem = 128 + (size_t)kGStages * (a.unit_bytes + a.kc / 16 * kXChunkBytes +
-                                                a.kc / 32 * kGemmTokens * sizeof(float));
-  if (smem > 227 * 1024) return fail(IFX_ERR_UNSUPPORTED, "gemm: shared memory plan too large");
-  static bool attr = false;
-  if (!attr) {
-    IFX_CUDA(cudaFuncSetAttribute(gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                  227 * 1024));
-    attr = true;
-  }
-  dim3 grid((unsigned)((M + kGemmTokens - 1) / kGemmTokens), (unsigned)W.L.ctiles);
-  gemm_kernel<<<grid, kGThreads, smem, st>>>(a);
-  IFX_CUDA(cudaGetLastError());
-  return IFX_OK;
+  return launch_sync<kGemmTokens / 8>(W, xfrag, M, C, ldc, accumulate, 1, err, st);
+}
+
+ifx_status gemm_small_run(const QMatrix &W, const void *xfrag, int64_t M, float *C, int64_t ldc,
+                          int *err, cudaStream_t st) {
+  if (M > kGemmSmallMax) return fail(IFX_ERR_UNSUPPORTED, "gemm: small batch above 32 tokens");
+  // enough K splits for about two CTAs per SM, never more than the units
+  const int ksplit = std::max(1, std::min(W.L.kunits, (2 * kNumSMs + W.L.ctiles - 1) / W.L.ctiles));
+  if (small_nt(M) == 2) return launch_sync<2>(W, xfrag, M, C, ldc, 1, ksplit, err, st);
+  return launch_sync<4>(W, xfrag, M, C, ldc, 1, ksplit, err, st);
 }
 
 }  // namespace ifx

@@ -22,6 +22,17 @@ ifx_status gemm_stage_x(const float *X, const float *X2, const float *normw, flo
 ifx_status gemm_run(const QMatrix &W, const void *xfrag, int64_t M, float *C, int64_t ldc,
                     int accumulate, int *err, cudaStream_t st);
 
+// Small batches (batched decode, M <= 32 tokens): the exact-integer
+// mma.sync kernel with blocks of 16 or 32 tokens and K split over enough
+// CTAs to fill the GPU. C += X W^T with atomic adds, so C must hold its
+// initial value (zeros, or the residual the result is added to).
+constexpr int kGemmSmallMax = 32;
+size_t gemm_small_xfrag_bytes(int64_t M, int64_t K);
+ifx_status gemm_small_stage_x(const float *X, const float *X2, const float *normw, float eps,
+                              int mode, int64_t M, int64_t K, void *xfrag, cudaStream_t st);
+ifx_status gemm_small_run(const QMatrix &W, const void *xfrag, int64_t M, float *C, int64_t ldc,
+                          int *err, cudaStream_t st);
+
 // The tensor-memory (tcgen05) GEMM of tcgemm.cu: used by gemm_stage_x and
 // gemm_run whenever K is a multiple of 64 (the mma.sync kernel above covers
 // the rest).

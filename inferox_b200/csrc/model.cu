@@ -116,6 +116,37 @@ __global__ void kv_write_kernel(const float *k, const float *v, __half *kc, __ha
 
 __global__ void add_int_kernel(int *p, int v) { *p += v; }
 
+__global__ void add_ones_kernel(int *p, int n) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) p[i] += 1;
+}
+
+// Row-wise argmax of x [rows][n] (last index on ties, NaN skipped:
+// forward.rs:615-622), one CTA per row.
+__global__ void argmax_rows_kernel(const float *x, int n, uint32_t *out) {
+  const float *r = x + (size_t)blockIdx.x * n;
+  unsigned long long best = 0;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    const float v = r[i];
+    if (v != v) continue;
+    const unsigned long long k = ((unsigned long long)ordered_bits(v) << 32) | (unsigned)i;
+    best = k > best ? k : best;
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const unsigned long long t = __shfl_xor_sync(0xffffffffu, best, o);
+    best = t > best ? t : best;
+  }
+  __shared__ unsigned long long w[32];
+  if ((threadIdx.x & 31) == 0) w[threadIdx.x >> 5] = best;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    for (int i = 1; i < (int)(blockDim.x >> 5); ++i) best = w[i] > best ? w[i] : best;
+    best = w[0] > best ? w[0] : best;
+    out[blockIdx.x] = (uint32_t)(best & 0xffffffffull);
+  }
+}
+
 // in: [tp][n][vl] (rank-major, as gathered); out: [n][tp * vl].
 __global__ void shard_interleave_kernel(const float *in, float *out, int n, int vl, int tp) {
   const int t = blockIdx.x;
@@ -405,12 +436,58 @@ ifx_status KvCache::create(Model *model, size_t max_seq_len) {
 }
 
 KvCache::~KvCache() {
+  if (!owner) return;
   if (m) cudaSetDevice(m->device);
   if (graph) cudaGraphExecDestroy(graph);
   for (void *p : {(void *)k, (void *)v, (void *)pos, (void *)tokens, (void *)part_o,
                   (void *)part_ml, (void *)bar})
     if (p) cudaFree(p);
   mega_free(&mega);
+}
+
+ifx_status KvBatch::create(Model *model, size_t max_seq_len, int nseq) {
+  m = model;
+  batch = nseq;
+  max_seq = max_seq_len;
+  const ifx_config &c = m->cfg;
+  if (m->tp > 1) return fail(IFX_ERR_UNSUPPORTED, "batched decode: tensor parallelism not supported");
+  if (nseq < 1 || nseq > kGemmSmallMax)
+    return fail(IFX_ERR_INVALID_ARGUMENT, "batched decode: 1 to 32 sequences");
+  const int G = (int)m->Gl, H = (int)m->Hl, hd = (int)c.head_dim, grp = H / G;
+  per_layer = (size_t)G * max_seq * hd;
+  // split-K factor: about two CTAs per SM, and a K/V chunk that fits in shared memory
+  ns = std::max(1, (2 * kNumSMs + nseq * G - 1) / (nseq * G));
+  while (ns < 64 && decode_attention_smem(grp, hd, (int)max_seq, ns) > 160 * 1024) ++ns;
+  ns = std::min(ns, 64);
+  const size_t D = c.hidden_size, F = m->Fl, V = c.vocab_size;
+  const size_t qkvw = (size_t)(H + 2 * G) * hd;
+  IFX_CUDA(cudaSetDevice(m->device));
+  IFX_TRY(dalloc(&k, per_layer * c.n_layers * nseq));
+  IFX_TRY(dalloc(&v, per_layer * c.n_layers * nseq));
+  IFX_TRY(dalloc(&pos, (size_t)nseq));
+  IFX_TRY(dalloc(&x, nseq * D));
+  IFX_TRY(dalloc(&qkv, nseq * qkvw));
+  IFX_TRY(dalloc(&attn, (size_t)nseq * H * hd));
+  IFX_TRY(dalloc(&gate, nseq * F));
+  IFX_TRY(dalloc(&up, nseq * F));
+  IFX_TRY(dalloc(&logits, nseq * V));
+  IFX_TRY(dalloc(&part_o, (size_t)nseq * H * ns * hd));
+  IFX_TRY(dalloc(&part_ml, (size_t)nseq * H * ns));
+  IFX_TRY(dalloc(&counters, (size_t)nseq * G));
+  IFX_TRY(dalloc(&ids, (size_t)nseq));
+  IFX_TRY(dalloc(&out, (size_t)nseq));
+  const size_t kmax = std::max<size_t>(std::max<size_t>(D, F), (size_t)H * hd);
+  IFX_CUDA(cudaMalloc(&xf, gemm_small_xfrag_bytes(nseq, (int64_t)kmax)));
+  len.assign((size_t)nseq, 0);
+  return IFX_OK;
+}
+
+KvBatch::~KvBatch() {
+  if (m) cudaSetDevice(m->device);
+  for (void *p : {(void *)k, (void *)v, (void *)pos, (void *)x, (void *)qkv, (void *)attn,
+                  (void *)gate, (void *)up, (void *)logits, (void *)part_o, (void *)part_ml,
+                  (void *)counters, (void *)xf, (void *)ids, (void *)out})
+    if (p) cudaFree(p);
 }
 
 ifx_status KvCache::clear() {
@@ -678,6 +755,162 @@ ifx_status Model::prefill(KvCache &kv, const uint32_t *ids, size_t n, float *log
 // attention over every position (no mask), RoPE at positions 0..n, no cache.
 ifx_status Model::forward(const uint32_t *ids, size_t n, float *logits_host, int last_row_only) {
   return run_prompt(nullptr, ids, n, logits_host, last_row_only);
+}
+
+// ------------------------------------------------------ batched decode --
+static ifx_status cuda_ok(cudaError_t e) {
+  return e == cudaSuccess ? IFX_OK : cuda_fail(e, "batched greedy decode");
+}
+
+// Prefill of sequence `seq` of a batch: Model::prefill on a KvCache view of
+// that sequence's cache slice.
+ifx_status Model::prefill_seq(KvBatch &kb, int seq, const uint32_t *ids, size_t n,
+                              float *logits_host, int last_row_only) {
+  if (seq < 0 || seq >= kb.batch) return fail(IFX_ERR_INVALID_ARGUMENT, "batch: no such sequence");
+  KvCache view;
+  view.owner = false;
+  view.m = this;
+  view.max_seq = kb.max_seq;
+  view.per_layer = kb.per_layer;
+  view.k = kb.k + (size_t)seq * cfg.n_layers * kb.per_layer;
+  view.v = kb.v + (size_t)seq * cfg.n_layers * kb.per_layer;
+  view.pos = kb.pos + seq;
+  view.len = kb.len[(size_t)seq];
+  view.mega_tried = true;  // never planned for the persistent kernel
+  const ifx_status s = run_prompt(&view, ids, n, logits_host, last_row_only);
+  kb.len[(size_t)seq] = view.len;
+  return s;
+}
+
+// One decode step of every sequence of the batch (Model::decode_step,
+// forward.rs:543-586, for B tokens at once): each weight matrix is read once
+// by the small-batch GEMM (exact integer weights, K split over the GPU,
+// results added atomically, so outputs start zeroed and the residual
+// projections add straight into x), attention runs per (sequence, kv head,
+// split) at each sequence's own position, then the logits and their argmax.
+ifx_status Model::enqueue_decode_batch(KvBatch &kb, cudaStream_t st) {
+  const ifx_config &c = cfg;
+  const int B = kb.batch, D = (int)c.hidden_size, H = (int)Hl, G = (int)Gl, hd = (int)c.head_dim;
+  const int F = (int)Fl, V = (int)c.vocab_size, Hh = H * hd;
+  const int64_t qkvw = (int64_t)(H + 2 * G) * hd;
+  const float eps = c.norm_eps;
+  embed_rows_kernel<<<(unsigned)B, 256, 0, st>>>(emb_raw, emb_type, D, kb.ids, kb.x);
+  IFX_CUDA(cudaGetLastError());
+  for (uint64_t l = 0; l < c.n_layers; ++l) {
+    Layer &L = layers[l];
+    IFX_CUDA(cudaMemsetAsync(kb.qkv, 0, sizeof(float) * (size_t)B * qkvw, st));
+    IFX_TRY(gemm_small_stage_x(kb.x, nullptr, L.attn_norm, eps, GX_RMSNORM, B, D, kb.xf, st));
+    IFX_TRY(gemm_small_run(L.wq, kb.xf, B, kb.qkv, qkvw, err, st));
+    IFX_TRY(gemm_small_run(L.wk, kb.xf, B, kb.qkv + Hh, qkvw, err, st));
+    IFX_TRY(gemm_small_run(L.wv, kb.xf, B, kb.qkv + Hh + G * hd, qkvw, err, st));
+    DecodeAttnArgs a{};
+    a.qkv = kb.qkv;
+    a.qkv_stride = qkvw;
+    a.kc = kb.k + l * kb.per_layer;
+    a.vc = kb.v + l * kb.per_layer;
+    a.kv_seq_stride = (int64_t)(c.n_layers * kb.per_layer);
+    a.pos = kb.pos;
+    a.part_o = kb.part_o;
+    a.part_ml = kb.part_ml;
+    a.counters = kb.counters;
+    a.attn_out = kb.attn;
+    a.H = H;
+    a.G = G;
+    a.hd = hd;
+    a.max_seq = (int)kb.max_seq;
+    a.ns = kb.ns;
+    a.rope_compat = opts.rope_compat;
+    a.rope_dim = (int)c.rope_dim;
+    a.rope_base = c.rope_base;
+    a.err = err;
+    a.batch = B;
+    IFX_TRY(decode_attention(a, st, false));
+    IFX_TRY(gemm_small_stage_x(kb.attn, nullptr, nullptr, 0.f, GX_PLAIN, B, Hh, kb.xf, st));
+    IFX_TRY(gemm_small_run(L.wo, kb.xf, B, kb.x, D, err, st));  // x += attn Wo^T
+    IFX_CUDA(cudaMemsetAsync(kb.gate, 0, sizeof(float) * (size_t)B * F, st));
+    IFX_CUDA(cudaMemsetAsync(kb.up, 0, sizeof(float) * (size_t)B * F, st));
+    IFX_TRY(gemm_small_stage_x(kb.x, nullptr, L.ffn_norm, eps, GX_RMSNORM, B, D, kb.xf, st));
+    IFX_TRY(gemm_small_run(L.w1, kb.xf, B, kb.gate, F, err, st));
+    IFX_TRY(gemm_small_run(L.w3, kb.xf, B, kb.up, F, err, st));
+    IFX_TRY(gemm_small_stage_x(kb.gate, kb.up, nullptr, 0.f, GX_SWIGLU, B, F, kb.xf, st));
+    IFX_TRY(gemm_small_run(L.w2, kb.xf, B, kb.x, D, err, st));  // x += swiglu W2^T
+  }
+  IFX_CUDA(cudaMemsetAsync(kb.logits, 0, sizeof(float) * (size_t)B * V, st));
+  IFX_TRY(gemm_small_stage_x(kb.x, nullptr, out_norm, eps, GX_RMSNORM, B, D, kb.xf, st));
+  IFX_TRY(gemm_small_run(out_w, kb.xf, B, kb.logits, V, err, st));
+  argmax_rows_kernel<<<(unsigned)B, 256, 0, st>>>(kb.logits, V, kb.out);
+  add_ones_kernel<<<1, 32, 0, st>>>(kb.pos, B);
+  IFX_CUDA(cudaGetLastError());
+  return IFX_OK;
+}
+
+ifx_status Model::decode_batch(KvBatch &kb, const uint32_t *tokens, float *logits_host,
+                               uint32_t *argmax_host) {
+  for (int b = 0; b < kb.batch; ++b) {
+    if (tokens[b] >= cfg.vocab_size)
+      return fail(IFX_ERR_INVALID_TENSOR_INDEX,
+                  "tensor index out of bounds: " + std::to_string(tokens[b]));
+    if (kb.len[(size_t)b] >= kb.max_seq) return fail(IFX_ERR_INVALID_TENSOR_INDEX, "KV cache is full");
+  }
+  IFX_CUDA(cudaSetDevice(device));
+  cudaStream_t st = stream;
+  IFX_CUDA(cudaMemcpyAsync(kb.ids, tokens, sizeof(uint32_t) * kb.batch, cudaMemcpyHostToDevice, st));
+  IFX_TRY(enqueue_decode_batch(kb, st));
+  if (logits_host)
+    IFX_CUDA(cudaMemcpyAsync(logits_host, kb.logits, sizeof(float) * kb.batch * cfg.vocab_size,
+                             cudaMemcpyDeviceToHost, st));
+  if (argmax_host)
+    IFX_CUDA(cudaMemcpyAsync(argmax_host, kb.out, sizeof(uint32_t) * kb.batch,
+                             cudaMemcpyDeviceToHost, st));
+  IFX_CUDA(cudaStreamSynchronize(st));
+  for (auto &n : kb.len) n += 1;
+  return check_err();
+}
+
+// n greedy steps of every sequence, each step's argmax fed to the next on
+// the device; out[i * batch + b] is sequence b's token of step i.
+ifx_status Model::decode_greedy_batch(KvBatch &kb, const uint32_t *tokens, size_t n,
+                                      uint32_t *out, float *device_ms) {
+  for (int b = 0; b < kb.batch; ++b) {
+    if (tokens[b] >= cfg.vocab_size)
+      return fail(IFX_ERR_INVALID_TENSOR_INDEX,
+                  "tensor index out of bounds: " + std::to_string(tokens[b]));
+    if (kb.len[(size_t)b] + n > kb.max_seq) return fail(IFX_ERR_INVALID_TENSOR_INDEX, "KV cache is full");
+  }
+  IFX_CUDA(cudaSetDevice(device));
+  cudaStream_t st = stream;
+  uint32_t *toks = nullptr;  // every step's tokens, copied out once at the end
+  IFX_TRY(dalloc(&toks, std::max<size_t>(1, n) * kb.batch));
+  IFX_CUDA(cudaMemcpyAsync(kb.ids, tokens, sizeof(uint32_t) * kb.batch, cudaMemcpyHostToDevice, st));
+  cudaEvent_t e0 = nullptr, e1 = nullptr;
+  if (device_ms) {
+    IFX_CUDA(cudaEventCreate(&e0));
+    IFX_CUDA(cudaEventCreate(&e1));
+    IFX_CUDA(cudaEventRecord(e0, st));
+  }
+  ifx_status s = IFX_OK;
+  for (size_t i = 0; i < n && s == IFX_OK; ++i) {
+    s = enqueue_decode_batch(kb, st);
+    if (s == IFX_OK)
+      s = cuda_ok(cudaMemcpyAsync(kb.ids, kb.out, sizeof(uint32_t) * kb.batch,
+                                  cudaMemcpyDeviceToDevice, st));
+    if (s == IFX_OK)
+      s = cuda_ok(cudaMemcpyAsync(toks + i * kb.batch, kb.out, sizeof(uint32_t) * kb.batch,
+                                  cudaMemcpyDeviceToDevice, st));
+  }
+  if (device_ms && s == IFX_OK) s = cuda_ok(cudaEventRecord(e1, st));
+  if (s == IFX_OK && out && n)
+    s = cuda_ok(cudaMemcpyAsync(out, toks, sizeof(uint32_t) * n * kb.batch, cudaMemcpyDeviceToHost, st));
+  cudaStreamSynchronize(st);
+  cudaFree(toks);
+  if (device_ms) {
+    if (s == IFX_OK) s = cuda_ok(cudaEventElapsedTime(device_ms, e0, e1));
+    cudaEventDestroy(e0);
+    cudaEventDestroy(e1);
+  }
+  IFX_TRY(s);
+  for (auto &l : kb.len) l += n;
+  return check_err();
 }
 
 // Shared body of prefill (kvp set: causal attention, K/V appended to the

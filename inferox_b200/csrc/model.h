@@ -30,9 +30,34 @@ struct KvCache {  // KvCache (src/model/cache.rs:7-14), f16 on the device
   float *part_o = nullptr;            // split-K partials of the persistent kernel
   float2 *part_ml = nullptr;
   unsigned *bar = nullptr;
+  bool owner = true;                  // false: a view into a KvBatch's memory
   ifx_status create(Model *model, size_t max_seq_len);
   ifx_status clear();
   ~KvCache();
+};
+
+// B independent sequences decoded together, so one step reads every weight
+// once for all of them (the reference's KvCache is single-sequence,
+// src/model/cache.rs:7-13). Sequence b's cache has the layout of a KvCache
+// at k/v + b * n_layers * per_layer, so a prompt is prefilled through a
+// KvCache view of it.
+struct KvBatch {
+  Model *m = nullptr;
+  int batch = 0, ns = 1;
+  size_t max_seq = 0, per_layer = 0;
+  __half *k = nullptr, *v = nullptr;  // [batch][layer][kv_head][max_seq][head_dim]
+  int *pos = nullptr;                 // device [batch]: each sequence's length
+  std::vector<size_t> len;            // host mirror of pos
+  // step workspace: [batch][...] rows
+  float *x = nullptr, *qkv = nullptr, *attn = nullptr, *gate = nullptr, *up = nullptr;
+  float *logits = nullptr;
+  float *part_o = nullptr;
+  float2 *part_ml = nullptr;
+  int *counters = nullptr;
+  uint8_t *xf = nullptr;
+  uint32_t *ids = nullptr, *out = nullptr;  // the step's input tokens and argmax
+  ifx_status create(Model *model, size_t max_seq_len, int nseq);
+  ~KvBatch();
 };
 
 struct Model {
@@ -95,6 +120,13 @@ struct Model {
   ifx_status decode_greedy(KvCache &kv, uint32_t token, size_t n, uint32_t *out, float *device_ms);
   ifx_status bench_kernel(KvCache &kv, const std::string &which, int reps, float *ms,
                           uint64_t *bytes);
+  ifx_status prefill_seq(KvBatch &kb, int seq, const uint32_t *ids, size_t n, float *logits_host,
+                         int last_row_only);
+  ifx_status enqueue_decode_batch(KvBatch &kb, cudaStream_t st);
+  ifx_status decode_batch(KvBatch &kb, const uint32_t *tokens, float *logits_host,
+                          uint32_t *argmax_host);
+  ifx_status decode_greedy_batch(KvBatch &kb, const uint32_t *tokens, size_t n, uint32_t *out,
+                                 float *device_ms);
   ifx_status ensure_ws(size_t n);
   ifx_status tp_partial_begin(size_t n, cudaStream_t st, float *part = nullptr,
                               const float *resid = nullptr);

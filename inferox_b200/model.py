@@ -87,6 +87,10 @@ class Model:
     def kv_cache(self, max_seq: int | None = None) -> "KvCache":
         return KvCache(self, max_seq or int(self.config.context_length))
 
+    def kv_batch(self, batch: int, max_seq: int | None = None) -> "KvBatch":
+        """`batch` independent sequences decoded together (one weight read per step)."""
+        return KvBatch(self, batch, max_seq or int(self.config.context_length))
+
     def prefill(self, ids, kv: "KvCache", last_row_only: bool = False) -> np.ndarray:
         ids = np.ascontiguousarray(ids, np.uint32)
         rows = 1 if last_row_only else ids.size
@@ -170,6 +174,59 @@ class KvCache:
         return out[: n * self.kv_dim].reshape(n, self.kv_dim)
 
 
+class KvBatch:
+    """`batch` KV caches decoded together: prefill each sequence, then step all."""
+
+    def __init__(self, model: Model, batch: int, max_seq: int):
+        self._model = model
+        h = C.c_void_p()
+        check(lib.ifx_kv_batch_create(model._h, max_seq, batch, C.byref(h)), "kv_batch_create")
+        self._h = h
+        self.batch, self.max_seq = batch, max_seq
+
+    def close(self):
+        if getattr(self, "_h", None) is not None and self._h.value:
+            lib.ifx_kv_batch_free(self._h)
+            self._h = None
+
+    def __del__(self):
+        self.close()
+
+    def len(self, seq: int) -> int:
+        n = C.c_size_t(0)
+        check(lib.ifx_kv_batch_len(self._h, seq, C.byref(n)), "kv_batch_len")
+        return int(n.value)
+
+    def prefill(self, seq: int, ids, last_row_only: bool = False) -> np.ndarray:
+        m = self._model
+        ids = np.ascontiguousarray(ids, np.uint32)
+        rows = 1 if last_row_only else ids.size
+        out = np.empty(rows * m.vocab, np.float32)
+        check(lib.ifx_prefill_seq(m._h, self._h, seq, _u32(ids), ids.size, _f32(out),
+                                  1 if last_row_only else 0), "prefill_seq")
+        return out.reshape(rows, m.vocab)
+
+    def decode_step(self, tokens, want_logits: bool = True):
+        """One step of every sequence: (logits [batch, vocab] or None, argmax [batch])."""
+        m = self._model
+        t = np.ascontiguousarray(tokens, np.uint32)
+        logits = np.empty(self.batch * m.vocab, np.float32) if want_logits else None
+        amax = np.empty(self.batch, np.uint32)
+        check(lib.ifx_decode_step_batch(m._h, self._h, _u32(t), _f32(logits) if want_logits else None,
+                                        _u32(amax)), "decode_step_batch")
+        return (logits.reshape(self.batch, m.vocab) if want_logits else None), amax
+
+    def decode_greedy(self, tokens, n_steps: int, timed: bool = False):
+        """n_steps greedy steps of every sequence: (tokens [n_steps, batch], device_ms)."""
+        m = self._model
+        t = np.ascontiguousarray(tokens, np.uint32)
+        out = np.empty(max(n_steps, 1) * self.batch, np.uint32)
+        ms = C.c_float(0.0)
+        check(lib.ifx_decode_greedy_batch(m._h, self._h, _u32(t), n_steps, _u32(out),
+                                          C.byref(ms) if timed else None), "decode_greedy_batch")
+        return out[: n_steps * self.batch].reshape(n_steps, self.batch), (float(ms.value) if timed else None)
+
+
 @dataclass
 class Sampler:
     """Sampler (src/sampler.rs:8-16); sampling runs on the device."""
@@ -193,4 +250,4 @@ class Sampler:
         return int(out.value)
 
 
-__all__ = ["Model", "KvCache", "Sampler", "IfxError", "load_opts"]
+__all__ = ["Model", "KvCache", "KvBatch", "Sampler", "IfxError", "load_opts"]
