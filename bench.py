@@ -230,6 +230,23 @@ def run_ours(args):
     for which in ("w13", "w2", "qkv", "wo", "logits", "attn"):
         ms, b = m.bench_kernel(kv, which, 2 * L if which != "logits" else 8)
         kern[which] = {"ms": ms, "bytes": b, "gbs": b / (ms * 1e-3) / 1e9}
+    # batched decode (the config's batch-16 workload: independent seeded
+    # prompts, each prefilled, then all 16 decoded together; one weight read
+    # per step for the 16 tokens), single GPU only
+    batch = None
+    if not tp_mode and args.batch > 1:
+        B = args.batch
+        kb = m.kv_batch(B, PROMPT + args.batch_steps + 16)
+        firsts = [int(np.argmax(kb.prefill(b, synth.prompt_ids(V, PROMPT, seq_index=b), True)[0]))
+                  for b in range(B)]
+        kb.decode_greedy(firsts, 3)
+        torch.cuda.synchronize()
+        _, bms = kb.decode_greedy(firsts, args.batch_steps, timed=True)
+        batch = {"batch": B, "steps": args.batch_steps, "ms_per_step": bms / args.batch_steps,
+                 "tok_s": B * args.batch_steps / (bms * 1e-3),
+                 "context": f"{PROMPT}-token prompts, {args.batch_steps} timed steps after 3"}
+        del kb
+
     # whole-step algorithmic bytes: every weight once + K/V at the mean context
     ctx_mean = ctx0 + args.steps / 2
     # per GPU: under tensor parallelism each rank reads its shard of the
@@ -269,6 +286,7 @@ def run_ours(args):
                          "frac": step_gbs / hbm, "peak": peak_kind,
                          "roofline_tok_s": hbm * 1e9 / step_bytes},
         "prefill": {"tokens": PROMPT, "s": prefill_s, "tok_s": PROMPT / prefill_s},
+        "batched_decode": batch,
         # the dominant kernel is the decode step itself: with the persistent
         # path one launch per token, so achieved = algorithmic step bytes over
         # the device time of one step
@@ -295,6 +313,9 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--batch", type=int, default=16,
+                    help="also time batched decode of this many sequences (0/1: skip)")
+    ap.add_argument("--batch-steps", type=int, default=32)
     ap.add_argument("--replicas", action="store_true",
                     help="with several GPUs: one independent sequence per GPU instead of "
                          "tensor parallelism over all of them")

@@ -27,12 +27,18 @@ __device__ __forceinline__ float silu_g(float v) {
   return v * (1.0f / (1.0f + expf(-c)));
 }
 
-// X staging: one CTA per token row computes the row's transform and writes
-// its values into the fragment layout [mblock][chunk][plane][nt][lane][4
-// halves] of blocks of 8 * NT tokens, then the per-token 32-column sums.
+// X staging: CTA (t, y) computes the transform of columns [y * kStageCols,
+// (y + 1) * kStageCols) of token row t (the RMSNorm statistic over the whole
+// row) and writes them into the fragment layout [mblock][chunk][plane][nt]
+// [lane][4 halves] of blocks of 8 * NT tokens, then the per-token 32-column
+// sums.
+constexpr int kStageCols = 2048;
+
 __global__ void stage_x_kernel(const float *X, const float *X2, const float *normw, float eps,
                                int mode, int64_t M, int64_t K, int NT, __half *out) {
   const int64_t t = blockIdx.x;  // token (row), may be >= M for padding
+  const int64_t kbeg = (int64_t)blockIdx.y * kStageCols;
+  const int64_t kend = std::min<int64_t>(K, kbeg + kStageCols);
   const int tid = threadIdx.x;
   __shared__ float red[32];
   __shared__ float s_inv;
@@ -60,10 +66,10 @@ __global__ void stage_x_kernel(const float *X, const float *X2, const float *nor
   const int64_t nch = K / 16, ngr = K / 32;
   float *sums = reinterpret_cast<float *>(out + (size_t)((M + tokb - 1) / tokb) * (size_t)nch *
                                                     (size_t)(xchunk_bytes(NT) / 2));
-  for (int64_t k0 = 0; k0 < K; k0 += blockDim.x) {  // blockDim.x % 32 == 0: a warp covers one group
+  for (int64_t k0 = kbeg; k0 < kend; k0 += blockDim.x) {  // a warp covers one 32-column group
     const int64_t k = k0 + tid;
     float v = 0.f;
-    if (t < M && k < K) {
+    if (t < M && k < kend) {
       if (mode == GX_RMSNORM) v = (X[t * K + k] * inv) * normw[k];
       else if (mode == GX_SWIGLU) v = silu_g(X[t * K + k]) * X2[t * K + k];
       else v = X[t * K + k];
@@ -72,7 +78,7 @@ __global__ void stage_x_kernel(const float *X, const float *X2, const float *nor
     const __half lv = __float2half_rn(v - __half2float(hv));
     float gs = __half2float(hv) + __half2float(lv);  // what the MMAs see
     gs = warp_sum(gs);
-    if (k < K) {
+    if (k < kend) {
       const int64_t ch = k / 16;
       const int kk = (int)(k % 16);
       // B fragment: b0 = (k 2c, 2c+1), b1 = (k 2c+8, 2c+9) of column g
@@ -87,6 +93,15 @@ __global__ void stage_x_kernel(const float *X, const float *X2, const float *nor
 }
 
 __device__ __forceinline__ uint32_t h2u(__half2 h) { return *reinterpret_cast<uint32_t *>(&h); }
+
+// (float)(v & 63) and (float)(v & 255) on the FP32 pipe: the integer placed in
+// the mantissa of 2^23, then 2^23 subtracted (both exact).
+__device__ __forceinline__ float u2f6(uint32_t v) {
+  return __uint_as_float(0x4B000000u | (v & 63u)) - 8388608.0f;
+}
+__device__ __forceinline__ float u2f8(uint32_t v) {
+  return __uint_as_float(0x4B000000u | (v & 255u)) - 8388608.0f;
+}
 __device__ __forceinline__ __half2 u2h(uint32_t u) { return *reinterpret_cast<__half2 *>(&u); }
 
 // (v - sub) * scale + add with v the magic-biased f16 pair in `bits`.
@@ -114,6 +129,21 @@ __device__ __forceinline__ void gemm_unit(const uint8_t *wt, const uint8_t *xs, 
   constexpr int cpg = (TYPE == IFX_TYPE_Q6_K) ? 1 : 2;
   const int ngr = kc / 16 / cpg;
   const __half2 b1024 = __float2half2_rn(1024.f);
+  // per-row quantities shared by every group of the unit, read once: Q4_K
+  // d/dmin and the 16-byte row headers, Q6_K d
+  float dA = 0.f, dB = 0.f, dmA = 0.f, dmB = 0.f;
+  uint4 hA = make_uint4(0u, 0u, 0u, 0u), hB = hA;
+  if (TYPE == IFX_TYPE_Q4_K) {
+    hA = *reinterpret_cast<const uint4 *>(wt + 2048 + 16 * g);
+    hB = *reinterpret_cast<const uint4 *>(wt + 2048 + 16 * (g + 8));
+    dA = h2f((uint16_t)prmt(hA.x, hA.y, 0x0073u));
+    dmA = h2f((uint16_t)prmt(hA.z, hA.w, 0x0073u));
+    dB = h2f((uint16_t)prmt(hB.x, hB.y, 0x0073u));
+    dmB = h2f((uint16_t)prmt(hB.z, hB.w, 0x0073u));
+  } else if (TYPE == IFX_TYPE_Q6_K) {
+    dA = h2f(*reinterpret_cast<const uint16_t *>(wt + 3072 + 256 + 2 * g));
+    dB = h2f(*reinterpret_cast<const uint16_t *>(wt + 3072 + 256 + 2 * (g + 8))) * 0.0625f;
+  }
 #pragma unroll 1
   for (int gi = 0; gi < ngr; ++gi) {
     float tmp[NT][4];
@@ -170,30 +200,19 @@ __device__ __forceinline__ void gemm_unit(const uint8_t *wt, const uint8_t *xs, 
     // this group's scales for rows g (sA) and g+8 (sB), f32
     float sA, sB, mA = 0.f, mB = 0.f;
     if (TYPE == IFX_TYPE_Q4_K) {
-      const uint8_t *hdr = wt + 2048;
-      float sc2[2], mn2[2];
-#pragma unroll
-      for (int h = 0; h < 2; ++h) {
-        const uint8_t *hb = hdr + 16 * (g + 8 * h);
-        // repacked header (repack.cu): word c' = field of groups (2c', 2c'+1)
-        // | byte c' of (d, dmin) << 24
-        const float d = h2f((uint16_t)(hb[3] | (hb[7] << 8)));
-        const float dm = h2f((uint16_t)(hb[11] | (hb[15] << 8)));
-        const uint32_t f = *reinterpret_cast<const uint32_t *>(hb + 4 * (gi >> 1));
-        const int j = gi & 1;
-        sc2[h] = d * (float)((f >> (6 * j)) & 63u);
-        mn2[h] = dm * (float)((f >> (12 + 6 * j)) & 63u);
-      }
-      sA = sc2[0];
-      sB = sc2[1] * 0.0625f;
-      mA = mn2[0];
-      mB = mn2[1];
+      // repacked header (repack.cu): word c' = the 6-bit fields of groups
+      // (2c', 2c'+1) | byte c' of (d, dmin) << 24
+      const int wsel = gi >> 1, sh = 6 * (gi & 1);
+      const uint32_t fA = wsel == 0 ? hA.x : wsel == 1 ? hA.y : wsel == 2 ? hA.z : hA.w;
+      const uint32_t fB = wsel == 0 ? hB.x : wsel == 1 ? hB.y : wsel == 2 ? hB.z : hB.w;
+      sA = dA * u2f6(fA >> sh);
+      sB = dB * u2f6(fB >> sh) * 0.0625f;
+      mA = dmA * u2f6(fA >> (12 + sh));
+      mB = dmB * u2f6(fB >> (12 + sh));
     } else if (TYPE == IFX_TYPE_Q6_K) {
       const uint8_t *scb = wt + 3072;
-      const float dA = h2f(*reinterpret_cast<const uint16_t *>(scb + 256 + 2 * g));
-      const float dB = h2f(*reinterpret_cast<const uint16_t *>(scb + 256 + 2 * (g + 8)));
-      sA = dA * (float)scb[16 * g + gi];
-      sB = dB * (float)scb[16 * (g + 8) + gi] * 0.0625f;
+      sA = dA * u2f8(scb[16 * g + gi]);
+      sB = dB * u2f8(scb[16 * (g + 8) + gi]);
     } else {
       const int nb = kc / 32;
       sA = h2f(*reinterpret_cast<const uint16_t *>(wt + wt_qbytes + (g * nb + gi) * 2));
@@ -336,8 +355,9 @@ static ifx_status stage_sync(const float *X, const float *X2, const float *normw
                              int mode, int64_t M, int64_t K, int NT, void *xfrag, cudaStream_t st) {
   if (K % 32) return fail(IFX_ERR_SHAPE, "gemm: K must be a multiple of 32");
   const int64_t tokb = 8 * NT, mpad = (M + tokb - 1) / tokb * tokb;
-  stage_x_kernel<<<(unsigned)mpad, 256, 0, st>>>(X, X2, normw, eps, mode, M, K, NT,
-                                                 reinterpret_cast<__half *>(xfrag));
+  const dim3 grid((unsigned)mpad, (unsigned)((K + kStageCols - 1) / kStageCols));
+  stage_x_kernel<<<grid, 256, 0, st>>>(X, X2, normw, eps, mode, M, K, NT,
+                                       reinterpret_cast<__half *>(xfrag));
   IFX_CUDA(cudaGetLastError());
   return IFX_OK;
 }

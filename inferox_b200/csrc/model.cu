@@ -116,17 +116,18 @@ __global__ void kv_write_kernel(const float *k, const float *v, __half *kc, __ha
 
 __global__ void add_int_kernel(int *p, int v) { *p += v; }
 
-__global__ void add_ones_kernel(int *p, int n) {
-  const int i = blockIdx.x * blockDim.x + threadIdx.x;
-  if (i < n) p[i] += 1;
-}
-
 // Row-wise argmax of x [rows][n] (last index on ties, NaN skipped:
-// forward.rs:615-622), one CTA per row.
-__global__ void argmax_rows_kernel(const float *x, int n, uint32_t *out) {
+// forward.rs:615-622): CTA (row, part) reduces a contiguous part of the row
+// to a 64-bit key (ordered value bits << 32 | index) and takes the maximum
+// with keys[row] (zeroed before); argmax_keys_kernel extracts the indices.
+constexpr int kArgmaxParts = 32;
+
+__global__ void argmax_rows_kernel(const float *x, int n, unsigned long long *keys) {
   const float *r = x + (size_t)blockIdx.x * n;
+  const int per = (n + kArgmaxParts - 1) / kArgmaxParts;
+  const int i0 = blockIdx.y * per, i1 = min(n, i0 + per);
   unsigned long long best = 0;
-  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+  for (int i = i0 + threadIdx.x; i < i1; i += blockDim.x) {
     const float v = r[i];
     if (v != v) continue;
     const unsigned long long k = ((unsigned long long)ordered_bits(v) << 32) | (unsigned)i;
@@ -143,7 +144,17 @@ __global__ void argmax_rows_kernel(const float *x, int n, uint32_t *out) {
   if (threadIdx.x == 0) {
     for (int i = 1; i < (int)(blockDim.x >> 5); ++i) best = w[i] > best ? w[i] : best;
     best = w[0] > best ? w[0] : best;
-    out[blockIdx.x] = (uint32_t)(best & 0xffffffffull);
+    if (best) atomicMax(&keys[blockIdx.x], best);
+  }
+}
+
+// The step's tokens from the row keys; every sequence's position advances.
+__global__ void argmax_keys_kernel(const unsigned long long *keys, int rows, uint32_t *out,
+                                   int *pos) {
+  const int i = threadIdx.x;
+  if (i < rows) {
+    out[i] = (uint32_t)(keys[i] & 0xffffffffull);
+    pos[i] += 1;
   }
 }
 
@@ -427,6 +438,7 @@ ifx_status KvCache::create(Model *model, size_t max_seq_len) {
   max_seq = max_seq_len;
   const ifx_config &c = m->cfg;
   per_layer = (size_t)m->Gl * max_seq * c.head_dim;  // this rank's kv heads
+  dev = m->device;
   IFX_CUDA(cudaSetDevice(m->device));
   IFX_TRY(dalloc(&k, per_layer * c.n_layers));
   IFX_TRY(dalloc(&v, per_layer * c.n_layers));
@@ -437,7 +449,7 @@ ifx_status KvCache::create(Model *model, size_t max_seq_len) {
 
 KvCache::~KvCache() {
   if (!owner) return;
-  if (m) cudaSetDevice(m->device);
+  if (dev >= 0) cudaSetDevice(dev);
   if (graph) cudaGraphExecDestroy(graph);
   for (void *p : {(void *)k, (void *)v, (void *)pos, (void *)tokens, (void *)part_o,
                   (void *)part_ml, (void *)bar})
@@ -455,12 +467,15 @@ ifx_status KvBatch::create(Model *model, size_t max_seq_len, int nseq) {
     return fail(IFX_ERR_INVALID_ARGUMENT, "batched decode: 1 to 32 sequences");
   const int G = (int)m->Gl, H = (int)m->Hl, hd = (int)c.head_dim, grp = H / G;
   per_layer = (size_t)G * max_seq * hd;
-  // split-K factor: about two CTAs per SM, and a K/V chunk that fits in shared memory
+  // split-K factor: at least two CTAs per SM, and chunks of at most 64 cache
+  // rows (small shared-memory footprint, several CTAs per SM)
   ns = std::max(1, (2 * kNumSMs + nseq * G - 1) / (nseq * G));
-  while (ns < 64 && decode_attention_smem(grp, hd, (int)max_seq, ns) > 160 * 1024) ++ns;
+  ns = std::max(ns, (int)((max_seq + 63) / 64));
   ns = std::min(ns, 64);
+  while (ns < 64 && decode_attention_smem(grp, hd, (int)max_seq, ns) > 160 * 1024) ++ns;
   const size_t D = c.hidden_size, F = m->Fl, V = c.vocab_size;
   const size_t qkvw = (size_t)(H + 2 * G) * hd;
+  dev = m->device;
   IFX_CUDA(cudaSetDevice(m->device));
   IFX_TRY(dalloc(&k, per_layer * c.n_layers * nseq));
   IFX_TRY(dalloc(&v, per_layer * c.n_layers * nseq));
@@ -476,6 +491,7 @@ ifx_status KvBatch::create(Model *model, size_t max_seq_len, int nseq) {
   IFX_TRY(dalloc(&counters, (size_t)nseq * G));
   IFX_TRY(dalloc(&ids, (size_t)nseq));
   IFX_TRY(dalloc(&out, (size_t)nseq));
+  IFX_TRY(dalloc(&keys, (size_t)nseq));
   const size_t kmax = std::max<size_t>(std::max<size_t>(D, F), (size_t)H * hd);
   IFX_CUDA(cudaMalloc(&xf, gemm_small_xfrag_bytes(nseq, (int64_t)kmax)));
   len.assign((size_t)nseq, 0);
@@ -483,10 +499,10 @@ ifx_status KvBatch::create(Model *model, size_t max_seq_len, int nseq) {
 }
 
 KvBatch::~KvBatch() {
-  if (m) cudaSetDevice(m->device);
+  if (dev >= 0) cudaSetDevice(dev);
   for (void *p : {(void *)k, (void *)v, (void *)pos, (void *)x, (void *)qkv, (void *)attn,
                   (void *)gate, (void *)up, (void *)logits, (void *)part_o, (void *)part_ml,
-                  (void *)counters, (void *)xf, (void *)ids, (void *)out})
+                  (void *)counters, (void *)xf, (void *)ids, (void *)out, (void *)keys})
     if (p) cudaFree(p);
 }
 
@@ -838,8 +854,9 @@ ifx_status Model::enqueue_decode_batch(KvBatch &kb, cudaStream_t st) {
   IFX_CUDA(cudaMemsetAsync(kb.logits, 0, sizeof(float) * (size_t)B * V, st));
   IFX_TRY(gemm_small_stage_x(kb.x, nullptr, out_norm, eps, GX_RMSNORM, B, D, kb.xf, st));
   IFX_TRY(gemm_small_run(out_w, kb.xf, B, kb.logits, V, err, st));
-  argmax_rows_kernel<<<(unsigned)B, 256, 0, st>>>(kb.logits, V, kb.out);
-  add_ones_kernel<<<1, 32, 0, st>>>(kb.pos, B);
+  IFX_CUDA(cudaMemsetAsync(kb.keys, 0, sizeof(unsigned long long) * (size_t)B, st));
+  argmax_rows_kernel<<<dim3((unsigned)B, kArgmaxParts), 256, 0, st>>>(kb.logits, V, kb.keys);
+  argmax_keys_kernel<<<1, 32, 0, st>>>(kb.keys, B, kb.out, kb.pos);
   IFX_CUDA(cudaGetLastError());
   return IFX_OK;
 }

@@ -31,6 +31,8 @@ struct KvCache {  // KvCache (src/model/cache.rs:7-14), f16 on the device
   float2 *part_ml = nullptr;
   unsigned *bar = nullptr;
   bool owner = true;                  // false: a view into a KvBatch's memory
+  int dev = -1;                       // device of the allocations (the destructor must
+                                      // not read the model: it may be freed first)
   ifx_status create(Model *model, size_t max_seq_len);
   ifx_status clear();
   ~KvCache();
@@ -56,6 +58,8 @@ struct KvBatch {
   int *counters = nullptr;
   uint8_t *xf = nullptr;
   uint32_t *ids = nullptr, *out = nullptr;  // the step's input tokens and argmax
+  unsigned long long *keys = nullptr;       // per-sequence argmax keys
+  int dev = -1;                             // device of the allocations
   ifx_status create(Model *model, size_t max_seq_len, int nseq);
   ~KvBatch();
 };
