@@ -306,6 +306,28 @@ def run_ours(args):
     finish()
 
 
+def run_gemm_case(spec: str):
+    """Profiling case for one fused dequant matmul (prefill-sized m goes to the
+    tcgen05 GEMM): four calls on a seeded matrix; prints the CUDA-event time."""
+    import numpy as np
+    import torch
+    from inferox_b200 import ops, synth
+    rows, cols, m, ttype = (int(v) for v in spec.split(","))
+    rng = np.random.default_rng(0)
+    w = (rng.standard_normal(rows * cols) * 0.02).astype(np.float32)
+    W = ops.QMatrix(ttype, synth.quantize(ttype, w), rows, cols)
+    x = torch.from_numpy(rng.standard_normal((m, cols)).astype(np.float32)).cuda()
+    ops.matmul_t_q(x, W, m)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(3):
+        ops.matmul_t_q(x, W, m)
+    e1.record()
+    torch.cuda.synchronize()
+    print(json.dumps({"gemm": spec, "ms_per_call_incl_staging_and_alloc": e0.elapsed_time(e1) / 3}))
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -313,6 +335,9 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--gemm", default="",
+                    help="profiling only: ROWS,COLS,M,TYPE — four calls of the fused dequant "
+                         "matmul (ifx_op_matmul_t_q) on a seeded matrix, then exit")
     ap.add_argument("--batch", type=int, default=16,
                     help="also time batched decode of this many sequences (0/1: skip)")
     ap.add_argument("--batch-steps", type=int, default=32)
@@ -325,7 +350,9 @@ def main():
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
-    if args.impl == "reference":
+    if args.gemm:
+        run_gemm_case(args.gemm)
+    elif args.impl == "reference":
         run_reference(args)
     else:
         run_ours(args)
