@@ -95,10 +95,11 @@ __global__ void __launch_bounds__(kAttnThreads) decode_attn_kernel(const __grid_
       float x0 = kn[i], x1 = kn[i + 1];
       if (i < a.rope_dim) rope_pair(x0, x1, i, a.rope_dim, a.rope_base, rpos);
       const __half2 kh = __floats2half2_rn(x0, x1), vh = __floats2half2_rn(vn[i], vn[i + 1]);
-      *reinterpret_cast<__half2 *>(kc + (size_t)pos * hd + i) = kh;
-      *reinterpret_cast<__half2 *>(vc + (size_t)pos * hd + i) = vh;
-      *reinterpret_cast<__half2 *>(Ks + (size_t)r * hd + i) = kh;
-      *reinterpret_cast<__half2 *>(Vs + (size_t)r * hd + i) = vh;
+      const int ip = kv_col(pos, i, hd);
+      *reinterpret_cast<__half2 *>(kc + (size_t)pos * hd + ip) = kh;
+      *reinterpret_cast<__half2 *>(vc + (size_t)pos * hd + ip) = vh;
+      *reinterpret_cast<__half2 *>(Ks + (size_t)r * hd + ip) = kh;
+      *reinterpret_cast<__half2 *>(Vs + (size_t)r * hd + ip) = vh;
     }
   }
   if (nold > 0) mbar_wait(&bar, 0, a.err, 301);
@@ -113,9 +114,10 @@ __global__ void __launch_bounds__(kAttnThreads) decode_attn_kernel(const __grid_
     const uint4 *kr = reinterpret_cast<const uint4 *>(Ks + (size_t)t * hd);
     const float *qj = qs + j * hd;
     float acc = 0.f;
+    const int key = kv_col(t0 + t, 0, hd) >> 3;  // chunk permutation of this cache row
     for (int cc = 0; cc < nch; ++cc) {
       const int c8 = (cc + t) % nch;
-      const uint4 kv = kr[c8];
+      const uint4 kv = kr[c8 ^ key];
       const uint32_t kw[4] = {kv.x, kv.y, kv.z, kv.w};
 #pragma unroll
       for (int u = 0; u < 4; ++u) {
@@ -151,7 +153,8 @@ __global__ void __launch_bounds__(kAttnThreads) decode_attn_kernel(const __grid_
   for (int e = tid; e < grp * hd; e += kAttnThreads) {
     const int j = e / hd, d = e % hd;
     float o = 0.f;
-    for (int t = 0; t < nk; ++t) o = fmaf(sc[j * cap + t], __half2float(Vs[(size_t)t * hd + d]), o);
+    for (int t = 0; t < nk; ++t)
+      o = fmaf(sc[j * cap + t], __half2float(Vs[(size_t)t * hd + kv_col(t0 + t, d, hd)]), o);
     po[e] = o;
   }
   if (tid < grp) part_ml[(h * NS + s) * grp + tid] = make_float2(s_m[tid], s_l[tid]);

@@ -22,6 +22,17 @@ ifx_status cuda_fail(cudaError_t e, const char *what);
 
 constexpr int kNumSMs = 148;
 
+// Position of element i (0 <= i < hd) of K/V cache row t (t: the row's
+// position in the cache) inside that row. For head sizes that are a multiple
+// of 64 the 16-byte chunks of a row are XOR-permuted by t % 8, so eight
+// consecutive rows read at one logical chunk fall on eight different
+// shared-memory bank groups (the tensor-core decode attention reads them with
+// ldmatrix); other head sizes keep the plain order. Even i and i + 1 stay
+// adjacent, so half2 accesses are unaffected.
+__host__ __device__ __forceinline__ int kv_col(int t, int i, int hd) {
+  return (hd & 63) ? i : (i ^ ((t & 7) << 3));
+}
+
 // ---------------------------------------------------------------- PTX ----
 __device__ __forceinline__ uint32_t smem_u32(const void *p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -121,6 +132,22 @@ __device__ __forceinline__ void mma_16816(float (&d)[4], uint32_t a0, uint32_t a
       : "=f"(d[0]), "=f"(d[1]), "=f"(d[2]), "=f"(d[3])
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "f"(c[0]), "f"(c[1]), "f"(c[2]),
         "f"(c[3]));
+}
+
+// Four 8x8 b16 matrices from shared memory (lanes 8q..8q+7 give the row
+// addresses of matrix q), in the mma.m16n8k16 fragment layout; `_t`
+// transposes each matrix.
+__device__ __forceinline__ void ldsm_x4(uint32_t (&r)[4], uint32_t addr) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(addr)
+               : "memory");
+}
+__device__ __forceinline__ void ldsm_x4_t(uint32_t (&r)[4], uint32_t addr) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(addr)
+               : "memory");
 }
 
 __device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {

@@ -104,6 +104,12 @@ struct AttnSpan {
   int t0, t1, nk, nold;
 };
 
+// Cache rows one item can hold (the largest split plus this token's row),
+// rounded up to whole 16-row MMA tiles.
+__host__ __device__ __forceinline__ int attn_cap(int max_seq, int nsa) {
+  return ((max_seq + nsa - 1) / nsa + 1 + 15) & ~15;
+}
+
 __device__ __forceinline__ AttnSpan attn_span(int pos, int nsa, int s) {
   const int len = pos + 1;
   const int chunk = (len + nsa - 1) / nsa;
@@ -122,7 +128,7 @@ __device__ __noinline__ void attn_fetch(const MegaArgs &A, int layer, int h, int
                            uint64_t *kvbar) {
   const AttnSpan sp = attn_span(pos, A.nsa, s);
   const int hd = A.hd;
-  const int cap = (A.max_seq + A.nsa - 1) / A.nsa + 1;
+  const int cap = attn_cap(A.max_seq, A.nsa);
   const uint32_t bytes = (uint32_t)sp.nold * (uint32_t)hd * 2u;
   if (bytes == 0) {
     mbar_arrive(kvbar);
@@ -144,7 +150,7 @@ __device__ __noinline__ void attn_item(const MegaArgs &A, const MegaAttn &at, in
   const int hd = A.hd, grp = A.H / A.G, NS = A.nsa;
   const AttnSpan sp = attn_span(pos, NS, s);
   const int t0 = sp.t0, nk = sp.nk;
-  const int cap = (A.max_seq + NS - 1) / NS + 1;
+  const int cap = attn_cap(A.max_seq, NS);
   const int n16 = hd / 8;  // 16-byte chunks per row
   const uint4 *Ks = reinterpret_cast<const uint4 *>(abuf);             // [cap][n16]
   uint4 *Vs4 = reinterpret_cast<uint4 *>(abuf + (size_t)cap * hd * 2);  // [cap][n16]
@@ -170,15 +176,15 @@ __device__ __noinline__ void attn_item(const MegaArgs &A, const MegaAttn &at, in
     __half *Kh = reinterpret_cast<__half *>(abuf) + (size_t)r * hd;
     __half *Vh = reinterpret_cast<__half *>(Vs4) + (size_t)r * hd;
     for (int e = tid; e < hd / 2; e += kConsumerThreads) {
-      const int i = 2 * e;
+      const int i = 2 * e, ip = kv_col(pos, i, hd);
       float x0 = __ldcg(kn + i), x1 = __ldcg(kn + i + 1);
       if (rpos != 0 && i < A.rope_dim) rope_pair_m(x0, x1, i, A.rope_dim, A.rope_base, rpos);
       const __half2 kh = __floats2half2_rn(x0, x1);
       const __half2 vh = __floats2half2_rn(__ldcg(vn + i), __ldcg(vn + i + 1));
-      *reinterpret_cast<__half2 *>(kcp + i) = kh;
-      *reinterpret_cast<__half2 *>(vcp + i) = vh;
-      *reinterpret_cast<__half2 *>(Kh + i) = kh;
-      *reinterpret_cast<__half2 *>(Vh + i) = vh;
+      *reinterpret_cast<__half2 *>(kcp + ip) = kh;
+      *reinterpret_cast<__half2 *>(vcp + ip) = vh;
+      *reinterpret_cast<__half2 *>(Kh + ip) = kh;
+      *reinterpret_cast<__half2 *>(Vh + ip) = vh;
     }
   }
   consumer_sync();
@@ -197,9 +203,10 @@ __device__ __noinline__ void attn_item(const MegaArgs &A, const MegaAttn &at, in
       t = jt - j * nk;
       const float4 *q4 = reinterpret_cast<const float4 *>(qs + j * hd);
       int c = qtr + (t & 7);  // any rotation keeps each quarter's chunk set a partition
+      const int key = kv_col(t0 + t, 0, hd) >> 3;  // chunk permutation of this cache row
       for (int cc = qtr; cc < n16; cc += 4) {
         while (c >= n16) c -= n16;
-        const uint4 kv = Ks[t * n16 + c];
+        const uint4 kv = Ks[t * n16 + (c ^ key)];
         const float4 qa = q4[2 * c], qb = q4[2 * c + 1];
         const float2 k0 = __half22float2(*reinterpret_cast<const __half2 *>(&kv.x));
         const float2 k1 = __half22float2(*reinterpret_cast<const __half2 *>(&kv.y));
@@ -247,13 +254,157 @@ __device__ __noinline__ void attn_item(const MegaArgs &A, const MegaAttn &at, in
     float o0 = 0.f, o1 = 0.f, o2 = 0.f, o3 = 0.f;
     int t = 0;
     for (; t + 3 < nk; t += 4) {
-      o0 = fmaf(sc[j * cap + t], __half2float(Vh[(size_t)t * hd + d]), o0);
-      o1 = fmaf(sc[j * cap + t + 1], __half2float(Vh[(size_t)(t + 1) * hd + d]), o1);
-      o2 = fmaf(sc[j * cap + t + 2], __half2float(Vh[(size_t)(t + 2) * hd + d]), o2);
-      o3 = fmaf(sc[j * cap + t + 3], __half2float(Vh[(size_t)(t + 3) * hd + d]), o3);
+      o0 = fmaf(sc[j * cap + t], __half2float(Vh[(size_t)t * hd + kv_col(t0 + t, d, hd)]), o0);
+      o1 = fmaf(sc[j * cap + t + 1], __half2float(Vh[(size_t)(t + 1) * hd + kv_col(t0 + t + 1, d, hd)]), o1);
+      o2 = fmaf(sc[j * cap + t + 2], __half2float(Vh[(size_t)(t + 2) * hd + kv_col(t0 + t + 2, d, hd)]), o2);
+      o3 = fmaf(sc[j * cap + t + 3], __half2float(Vh[(size_t)(t + 3) * hd + kv_col(t0 + t + 3, d, hd)]), o3);
     }
-    for (; t < nk; ++t) o0 = fmaf(sc[j * cap + t], __half2float(Vh[(size_t)t * hd + d]), o0);
+    for (; t < nk; ++t)
+      o0 = fmaf(sc[j * cap + t], __half2float(Vh[(size_t)t * hd + kv_col(t0 + t, d, hd)]), o0);
     po[e] = (o0 + o1) + (o2 + o3);
+  }
+  if (tid < grp) {
+    const float m = nk > 0 ? stat[2 * tid] : -INFINITY, l = nk > 0 ? stat[2 * tid + 1] : 0.f;
+    A.part_ml[(h * NS + s) * grp + tid] = make_float2(m, l);
+  }
+  consumer_sync();  // the buffer is reused by the next item
+}
+
+// The same item on tensor cores (head size a multiple of 64, at most four
+// query heads per kv head): S = K Q^T with the cached K rows as the A operand
+// (ldmatrix from the chunk-swizzled rows, conflict-free) and the query heads
+// as B columns — column j the hi f16 plane of head j, column 4 + j its lo
+// plane (about 22 bits), added across lanes afterwards; softmax statistics
+// over the item's rows; O = V^T P with V^T from ldmatrix.trans and P as hi/lo
+// columns the same way. Output format as attn_item.
+__device__ __noinline__ void attn_item_tc(const MegaArgs &A, const MegaAttn &at, int h, int s,
+                                          int pos, uint8_t *abuf) {
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, c = lane & 3;
+  const int hd = A.hd, grp = A.H / A.G, NS = A.nsa;
+  const AttnSpan sp = attn_span(pos, NS, s);
+  const int t0 = sp.t0, nk = sp.nk, nk16 = (nk + 15) & ~15;
+  const int cap = attn_cap(A.max_seq, NS);
+  const int qs = hd + 8, ps = cap + 8;  // padded row strides (conflict-free B loads)
+  __half *Ks = reinterpret_cast<__half *>(abuf);  // [cap][hd], rows chunk-swizzled
+  __half *Vs = Ks + (size_t)cap * hd;               // [cap][hd]
+  __half *qh = Vs + (size_t)cap * hd;               // [2][4][qs]
+  float *sc = reinterpret_cast<float *>(qh + 2 * 4 * qs);  // [4][cap]
+  __half *ph = reinterpret_cast<__half *>(sc + 4 * cap);   // [2][4][ps]
+  float *stat = reinterpret_cast<float *>(ph + 2 * 4 * ps);  // [4][2]
+  // RoPE at position 0 is the identity (the reference's decode, forward.rs:371-372)
+  const int rpos = A.rope_compat ? 0 : pos;
+  const float *q = A.qkv + (size_t)h * grp * hd;
+  for (int e = tid; e < 4 * hd / 2; e += kConsumerThreads) {
+    const int j = e / (hd / 2), i = 2 * (e % (hd / 2));
+    float x0 = 0.f, x1 = 0.f;
+    if (j < grp) {
+      x0 = __ldcg(q + j * hd + i);
+      x1 = __ldcg(q + j * hd + i + 1);
+      if (rpos != 0 && i < A.rope_dim) rope_pair_m(x0, x1, i, A.rope_dim, A.rope_base, rpos);
+    }
+    const __half2 hi = __floats2half2_rn(x0, x1);
+    *reinterpret_cast<__half2 *>(qh + j * qs + i) = hi;
+    *reinterpret_cast<__half2 *>(qh + (4 + j) * qs + i) =
+        __floats2half2_rn(x0 - __low2float(hi), x1 - __high2float(hi));
+  }
+  if (t0 <= pos && pos < sp.t1) {  // append this token's K/V (forward.rs:375-378)
+    const float *kn = A.qkv + (size_t)A.H * hd + (size_t)h * hd;
+    const float *vn = A.qkv + (size_t)(A.H + A.G) * hd + (size_t)h * hd;
+    const int r = pos - t0;
+    __half *kcp = at.kc + ((size_t)h * A.max_seq + pos) * hd;
+    __half *vcp = at.vc + ((size_t)h * A.max_seq + pos) * hd;
+    for (int e = tid; e < hd / 2; e += kConsumerThreads) {
+      const int i = 2 * e, ip = kv_col(pos, i, hd);
+      float x0 = __ldcg(kn + i), x1 = __ldcg(kn + i + 1);
+      if (rpos != 0 && i < A.rope_dim) rope_pair_m(x0, x1, i, A.rope_dim, A.rope_base, rpos);
+      const __half2 kh = __floats2half2_rn(x0, x1);
+      const __half2 vh = __floats2half2_rn(__ldcg(vn + i), __ldcg(vn + i + 1));
+      *reinterpret_cast<__half2 *>(kcp + ip) = kh;
+      *reinterpret_cast<__half2 *>(vcp + ip) = vh;
+      *reinterpret_cast<__half2 *>(Ks + (size_t)r * hd + ip) = kh;
+      *reinterpret_cast<__half2 *>(Vs + (size_t)r * hd + ip) = vh;
+    }
+  }
+  // V rows [nk, nk16) enter P V with p = 0: they must be finite
+  for (int e = tid; e < (nk16 - nk) * hd / 2; e += kConsumerThreads)
+    *reinterpret_cast<__half2 *>(Vs + (size_t)nk * hd + 2 * e) = __floats2half2_rn(0.f, 0.f);
+  consumer_sync();
+  // scores: warp w takes 16-row tile w
+  const float isq = 1.0f / sqrtf((float)hd);
+  for (int mt = warp; mt < nk16 / 16; mt += kConsumerWarps) {
+    float D[4] = {0.f, 0.f, 0.f, 0.f};
+    const int row = 16 * mt + (lane & 7) + 8 * ((lane >> 3) & 1);
+    const int key = kv_col(t0 + row, 0, hd) >> 3;
+    const __half *qp = qh + g * qs + 2 * c;  // column g: plane g / 4, head g % 4
+    for (int ks = 0; ks < hd / 16; ++ks) {
+      uint32_t a[4];
+      ldsm_x4(a, smem_u32(Ks + (size_t)row * hd + (((2 * ks + (lane >> 4)) ^ key) << 3)));
+      const uint32_t b0 = *reinterpret_cast<const uint32_t *>(qp + 16 * ks);
+      const uint32_t b1 = *reinterpret_cast<const uint32_t *>(qp + 16 * ks + 8);
+      mma_16816(D, a[0], a[1], a[2], a[3], b0, b1, D);
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) D[i] += __shfl_xor_sync(0xffffffffu, D[i], 2);  // hi + lo
+    if (c < 2) {
+      const int ra = 16 * mt + g, rb = ra + 8;
+#pragma unroll
+      for (int jj = 0; jj < 2; ++jj) {
+        const int j = 2 * c + jj;
+        if (j < grp) {
+          sc[j * cap + ra] = ra < nk ? D[jj] * isq : -INFINITY;
+          sc[j * cap + rb] = rb < nk ? D[2 + jj] * isq : -INFINITY;
+        }
+      }
+    }
+  }
+  consumer_sync();
+  if (warp < 4) {  // softmax statistics of this split, head j = warp; p as hi/lo planes
+    const int j = warp;
+    float m = -INFINITY;
+    if (j < grp)
+      for (int t = lane; t < nk; t += 32) m = fmaxf(m, sc[j * cap + t]);
+    m = warp_max(m);
+    float l = 0.f;
+    for (int t = lane; t < nk16; t += 32) {
+      const float p = (j < grp && t < nk) ? expf(sc[j * cap + t] - m) : 0.f;
+      const __half hp = __float2half_rn(p);
+      ph[j * ps + t] = hp;
+      ph[(4 + j) * ps + t] = __float2half_rn(p - __half2float(hp));
+      l += p;
+    }
+    l = warp_sum(l);
+    if (lane == 0) {
+      stat[2 * j] = m;
+      stat[2 * j + 1] = l;
+    }
+  }
+  consumer_sync();
+  // O^T = V^T P: warp w takes dims [16 w, 16 w + 16)
+  float *po = A.part_o + (size_t)(h * NS + s) * grp * hd;
+  for (int mt = warp; mt < hd / 16; mt += kConsumerWarps) {
+    float D[4] = {0.f, 0.f, 0.f, 0.f};
+    const __half *pp = ph + g * ps + 2 * c;
+    for (int ks = 0; ks < nk16 / 16; ++ks) {
+      const int t = 16 * ks + (lane & 7) + 8 * (lane >> 4);
+      const int chunk = (2 * mt + ((lane >> 3) & 1)) ^ (kv_col(t0 + t, 0, hd) >> 3);
+      uint32_t a[4];
+      ldsm_x4_t(a, smem_u32(Vs + (size_t)t * hd + (chunk << 3)));
+      const uint32_t b0 = *reinterpret_cast<const uint32_t *>(pp + 16 * ks);
+      const uint32_t b1 = *reinterpret_cast<const uint32_t *>(pp + 16 * ks + 8);
+      mma_16816(D, a[0], a[1], a[2], a[3], b0, b1, D);
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) D[i] += __shfl_xor_sync(0xffffffffu, D[i], 2);
+    if (c < 2) {
+#pragma unroll
+      for (int jj = 0; jj < 2; ++jj) {
+        const int j = 2 * c + jj;
+        if (j < grp) {
+          po[j * hd + 16 * mt + g] = D[jj];
+          po[j * hd + 16 * mt + g + 8] = D[2 + jj];
+        }
+      }
+    }
   }
   if (tid < grp) {
     const float m = nk > 0 ? stat[2 * tid] : -INFINITY, l = nk > 0 ? stat[2 * tid + 1] : 0.f;
@@ -467,7 +618,10 @@ __global__ void __launch_bounds__(kGemvThreads, 1) decode_mega_kernel(const __gr
           }
           consumer_sync();
           const int h = item % A.G;
-          attn_item(A, P.at, h, item / A.G, pos, abuf);
+          if (A.attn_tc)
+            attn_item_tc(A, P.at, h, item / A.G, pos, abuf);
+          else
+            attn_item(A, P.at, h, item / A.G, pos, abuf);
           // split-K fixup: the CTA that finishes kv head h's last split
           // combines the head (release by every item, acquire by the last)
           if (threadIdx.x == 0) {
@@ -508,8 +662,12 @@ int mega_attn_splits(int G, int max_seq, int num_sms) {
 }
 
 size_t mega_attn_scratch(int grp, int hd, int max_seq, int nsa) {
-  const size_t cap = (size_t)(max_seq + nsa - 1) / nsa + 1;
-  return 2 * cap * hd * 2 + (size_t)grp * hd * 4 + (size_t)grp * cap * 4 + (size_t)grp * 8 + 64;
+  const size_t cap = (size_t)attn_cap(max_seq, nsa);
+  const size_t scalar = 2 * cap * hd * 2 + (size_t)grp * hd * 4 + (size_t)grp * cap * 4 + (size_t)grp * 8 + 64;
+  // tensor-core items: K, V | q hi/lo [2][4][hd + 8] | scores [4][cap] | p hi/lo [2][4][cap + 8] | stats
+  const size_t tc = 2 * cap * hd * 2 + 2 * 4 * ((size_t)hd + 8) * 2 + 4 * cap * 4 +
+                    2 * 4 * (cap + 8) * 2 + 4 * 8 + 64;
+  return std::max(scalar, tc);
 }
 
 ifx_status mega_finalize(MegaPlan *plan, const std::vector<MegaPhase> &phases, int num_sms) {

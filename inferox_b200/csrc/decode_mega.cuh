@@ -43,6 +43,7 @@ struct MegaArgs {
   float *part_o;
   float2 *part_ml;
   int H, G, hd, max_seq, nsa, rope_compat, rope_dim;
+  int attn_tc;  // 1: attention items on tensor cores (head size a multiple of 64, <= 4 q heads per kv head)
   float rope_base;
   const float *qkv;
   const __half *kc0, *vc0;  // layer 0 of the K and V caches

@@ -108,7 +108,7 @@ __global__ void kv_write_kernel(const float *k, const float *v, __half *kc, __ha
   const int t = blockIdx.x;
   for (int e = threadIdx.x; e < G * hd; e += blockDim.x) {
     const int g = e / hd, d = e % hd;
-    const size_t dst = ((size_t)g * max_seq + start + t) * hd + d;
+    const size_t dst = ((size_t)g * max_seq + start + t) * hd + kv_col(start + t, d, hd);
     kc[dst] = __float2half_rn(k[(size_t)t * G * hd + e]);
     vc[dst] = __float2half_rn(v[(size_t)t * G * hd + e]);
   }
@@ -187,7 +187,7 @@ __global__ void kv_read_kernel(const __half *c, float *out, int len, int G, int 
   const int t = blockIdx.x;
   for (int e = threadIdx.x; e < G * hd; e += blockDim.x) {
     const int g = e / hd, d = e % hd;
-    out[(size_t)t * G * hd + e] = __half2float(c[((size_t)g * max_seq + t) * hd + d]);
+    out[(size_t)t * G * hd + e] = __half2float(c[((size_t)g * max_seq + t) * hd + kv_col(t, d, hd)]);
   }
 }
 
@@ -612,6 +612,7 @@ ifx_status Model::build_mega(KvCache &kv) {
   if (dev_sms != kNumSMs) return IFX_OK;
   MegaArgs &A = kv.mega.args;
   A.nsa = mega_attn_splits(G, (int)kv.max_seq, kNumSMs);
+  A.attn_tc = (hd % 64 == 0 && hd <= 256 && H / G <= 4) ? 1 : 0;
   IFX_TRY(dalloc(&kv.part_o, (size_t)H * A.nsa * hd));
   IFX_TRY(dalloc(&kv.part_ml, (size_t)H * A.nsa));
   IFX_TRY(dalloc(&kv.bar, 1 + (size_t)G));  // barrier counter + per-kv-head split counters
