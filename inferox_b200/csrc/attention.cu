@@ -25,6 +25,18 @@ __device__ __forceinline__ void rope_pair(float &a, float &b, int i, int rope_di
   b = x1;
 }
 
+// Cache rows one split can hold (its chunk plus this token's row), rounded
+// up to whole 16-row MMA tiles.
+__host__ __device__ __forceinline__ int attn_rows(int max_seq, int ns) {
+  return ((max_seq + ns - 1) / ns + 1 + 15) & ~15;
+}
+
+// TC: scores and P V on tensor cores (head size a multiple of 64, at most four
+// query heads per kv head): S = K Q^T with the chunk-swizzled cache rows as
+// ldmatrix A fragments and the query heads as B columns (column j the hi f16
+// plane of head j, column 4 + j its lo plane), O^T = V^T P the same way with
+// ldmatrix.trans; otherwise FMA loops.
+template <bool TC>
 __global__ void __launch_bounds__(kAttnThreads) decode_attn_kernel(const __grid_constant__ DecodeAttnArgs a) {
   extern __shared__ __align__(128) uint8_t smraw[];
   const int h = blockIdx.x, s = blockIdx.y, b = blockIdx.z, tid = threadIdx.x;
@@ -36,11 +48,17 @@ __global__ void __launch_bounds__(kAttnThreads) decode_attn_kernel(const __grid_
   float2 *part_ml = a.part_ml + (size_t)b * a.G * NS * grp;
   int *counters = a.counters + (size_t)b * a.G;
   float *attn_out = a.attn_out + (size_t)b * a.H * hd;
-  const int cap = (a.max_seq + NS - 1) / NS + 1;
+  const int cap = attn_rows(a.max_seq, NS);
   __half *Ks = reinterpret_cast<__half *>(smraw);  // [cap][hd]
   __half *Vs = Ks + (size_t)cap * hd;               // [cap][hd]
-  float *qs = reinterpret_cast<float *>(Vs + (size_t)cap * hd);  // [grp][hd]
-  float *sc = qs + grp * hd;                        // [grp][cap]
+  // FMA path: q [grp][hd] f32, scores [grp][cap]; tensor-core path: q hi/lo
+  // [8][hd + 8] halves, scores [4][cap], p hi/lo [8][cap + 8] halves
+  const int qs_ = hd + 8, ps_ = cap + 8;
+  float *qs = reinterpret_cast<float *>(Vs + (size_t)cap * hd);
+  __half *qh = Vs + (size_t)cap * hd;
+  float *sc = TC ? reinterpret_cast<float *>(qh + 8 * qs_) : qs + grp * hd;
+  __half *ph = reinterpret_cast<__half *>(sc + 4 * cap);
+  __shared__ float s_m[kMaxGroup], s_l[kMaxGroup];
   __shared__ int s_last;
   __shared__ __align__(8) uint64_t bar;
 
@@ -78,12 +96,23 @@ __global__ void __launch_bounds__(kAttnThreads) decode_attn_kernel(const __grid_
 
   const float *q = qkv + (size_t)h * grp * hd;
   const int rpos = a.rope_compat ? 0 : pos;
-  for (int e = tid; e < grp * hd / 2; e += kAttnThreads) {
+  for (int e = tid; e < (TC ? 4 : grp) * hd / 2; e += kAttnThreads) {
     const int j = e / (hd / 2), i = 2 * (e % (hd / 2));
-    float x0 = q[j * hd + i], x1 = q[j * hd + i + 1];
-    if (i < a.rope_dim) rope_pair(x0, x1, i, a.rope_dim, a.rope_base, rpos);
-    qs[j * hd + i] = x0;
-    qs[j * hd + i + 1] = x1;
+    float x0 = 0.f, x1 = 0.f;
+    if (j < grp) {
+      x0 = q[j * hd + i];
+      x1 = q[j * hd + i + 1];
+      if (i < a.rope_dim) rope_pair(x0, x1, i, a.rope_dim, a.rope_base, rpos);
+    }
+    if (TC) {
+      const __half2 hi = __floats2half2_rn(x0, x1);
+      *reinterpret_cast<__half2 *>(qh + j * qs_ + i) = hi;
+      *reinterpret_cast<__half2 *>(qh + (4 + j) * qs_ + i) =
+          __floats2half2_rn(x0 - __low2float(hi), x1 - __high2float(hi));
+    } else {
+      qs[j * hd + i] = x0;
+      qs[j * hd + i + 1] = x1;
+    }
   }
   if (t0 <= pos && pos < t1) {
     // append this token's K/V (forward.rs:375-378), K rotated like q
@@ -105,6 +134,86 @@ __global__ void __launch_bounds__(kAttnThreads) decode_attn_kernel(const __grid_
   if (nold > 0) mbar_wait(&bar, 0, a.err, 301);
   __syncthreads();
 
+  float *po = part_o + (size_t)(h * NS + s) * grp * hd;
+  if constexpr (TC) {
+    const int warp = tid >> 5, lane = tid & 31, g = lane >> 2, c = lane & 3;
+    const int nk16 = (nk + 15) & ~15;
+    // V rows [nk, nk16) enter P V with p = 0: they must be finite
+    for (int e = tid; e < (nk16 - nk) * hd / 2; e += kAttnThreads)
+      *reinterpret_cast<__half2 *>(Vs + (size_t)nk * hd + 2 * e) = __floats2half2_rn(0.f, 0.f);
+    const float isq = 1.0f / sqrtf((float)hd);
+    for (int mt = warp; mt < nk16 / 16; mt += kAttnThreads / 32) {
+      float D[4] = {0.f, 0.f, 0.f, 0.f};
+      const int row = 16 * mt + (lane & 7) + 8 * ((lane >> 3) & 1);
+      const int key = kv_col(t0 + row, 0, hd) >> 3;
+      const __half *qp = qh + g * qs_ + 2 * c;  // column g: plane g / 4, head g % 4
+      for (int ks = 0; ks < hd / 16; ++ks) {
+        uint32_t av[4];
+        ldsm_x4(av, smem_u32(Ks + (size_t)row * hd + (((2 * ks + (lane >> 4)) ^ key) << 3)));
+        mma_16816(D, av[0], av[1], av[2], av[3], *reinterpret_cast<const uint32_t *>(qp + 16 * ks),
+                  *reinterpret_cast<const uint32_t *>(qp + 16 * ks + 8), D);
+      }
+#pragma unroll
+      for (int i2 = 0; i2 < 4; ++i2) D[i2] += __shfl_xor_sync(0xffffffffu, D[i2], 2);  // hi + lo
+      if (c < 2) {
+        const int ra = 16 * mt + g, rb = ra + 8;
+#pragma unroll
+        for (int jj = 0; jj < 2; ++jj) {
+          const int j2 = 2 * c + jj;
+          if (j2 < grp) {
+            sc[j2 * cap + ra] = ra < nk ? D[jj] * isq : -INFINITY;  // forward.rs:396
+            sc[j2 * cap + rb] = rb < nk ? D[2 + jj] * isq : -INFINITY;
+          }
+        }
+      }
+    }
+    __syncthreads();
+    {  // softmax statistics of this split (warp j = head j); p as hi/lo planes
+      const int j2 = warp;
+      float m = -INFINITY;
+      if (j2 < grp)
+        for (int t = lane; t < nk; t += 32) m = fmaxf(m, sc[j2 * cap + t]);
+      m = warp_max(m);
+      float l = 0.f;
+      for (int t = lane; t < nk16; t += 32) {
+        const float p = (j2 < grp && t < nk) ? expf(sc[j2 * cap + t] - m) : 0.f;
+        const __half hp = __float2half_rn(p);
+        ph[j2 * ps_ + t] = hp;
+        ph[(4 + j2) * ps_ + t] = __float2half_rn(p - __half2float(hp));
+        l += p;
+      }
+      l = warp_sum(l);
+      if (lane == 0 && j2 < grp) {
+        s_m[j2] = m;
+        s_l[j2] = l;
+      }
+    }
+    __syncthreads();
+    for (int mt = warp; mt < hd / 16; mt += kAttnThreads / 32) {
+      float D[4] = {0.f, 0.f, 0.f, 0.f};
+      const __half *pp = ph + g * ps_ + 2 * c;
+      for (int ks = 0; ks < nk16 / 16; ++ks) {
+        const int t = 16 * ks + (lane & 7) + 8 * (lane >> 4);
+        const int ch = (2 * mt + ((lane >> 3) & 1)) ^ (kv_col(t0 + t, 0, hd) >> 3);
+        uint32_t av[4];
+        ldsm_x4_t(av, smem_u32(Vs + (size_t)t * hd + (ch << 3)));
+        mma_16816(D, av[0], av[1], av[2], av[3], *reinterpret_cast<const uint32_t *>(pp + 16 * ks),
+                  *reinterpret_cast<const uint32_t *>(pp + 16 * ks + 8), D);
+      }
+#pragma unroll
+      for (int i2 = 0; i2 < 4; ++i2) D[i2] += __shfl_xor_sync(0xffffffffu, D[i2], 2);
+      if (c < 2) {
+#pragma unroll
+        for (int jj = 0; jj < 2; ++jj) {
+          const int j2 = 2 * c + jj;
+          if (j2 < grp) {
+            po[j2 * hd + 16 * mt + g] = D[jj];
+            po[j2 * hd + 16 * mt + g + 8] = D[2 + jj];
+          }
+        }
+      }
+    }
+  } else {
   // scores: one thread per (head j, position t); the 16-byte K chunks are
   // visited in a rotated order so neighbouring threads hit different banks
   const float sq = sqrtf((float)hd);
@@ -131,7 +240,6 @@ __global__ void __launch_bounds__(kAttnThreads) decode_attn_kernel(const __grid_
   __syncthreads();
   const int warp = tid >> 5, lane = tid & 31;
   // per-head softmax statistics over this chunk
-  __shared__ float s_m[kMaxGroup], s_l[kMaxGroup];
   for (int j = warp; j < grp; j += kAttnThreads / 32) {
     float m = -INFINITY;
     for (int t = lane; t < nk; t += 32) m = fmaxf(m, sc[j * cap + t]);
@@ -149,13 +257,13 @@ __global__ void __launch_bounds__(kAttnThreads) decode_attn_kernel(const __grid_
     }
   }
   __syncthreads();
-  float *po = part_o + (size_t)(h * NS + s) * grp * hd;
   for (int e = tid; e < grp * hd; e += kAttnThreads) {
     const int j = e / hd, d = e % hd;
     float o = 0.f;
     for (int t = 0; t < nk; ++t)
       o = fmaf(sc[j * cap + t], __half2float(Vs[(size_t)t * hd + kv_col(t0 + t, d, hd)]), o);
     po[e] = o;
+  }
   }
   if (tid < grp) part_ml[(h * NS + s) * grp + tid] = make_float2(s_m[tid], s_l[tid]);
   __threadfence();
@@ -308,8 +416,12 @@ __global__ void __launch_bounds__(128) prefill_attn_kernel(PrefillAttnArgs a) {
 
 }  // namespace
 
+static bool attn_tc_shape(int grp, int hd) { return hd % 64 == 0 && hd <= 256 && grp <= 4; }
+
 int decode_attention_smem(int grp, int hd, int max_seq, int ns) {
-  const int cap = (max_seq + ns - 1) / ns + 1;
+  const int cap = attn_rows(max_seq, ns);
+  if (attn_tc_shape(grp, hd))
+    return 2 * cap * hd * 2 + 8 * (hd + 8) * 2 + 4 * cap * 4 + 8 * (cap + 8) * 2;
   return 2 * cap * hd * 2 + (grp * hd + grp * cap) * (int)sizeof(float);
 }
 
@@ -319,13 +431,19 @@ ifx_status decode_attention(const DecodeAttnArgs &a, cudaStream_t st, bool pdl) 
     return fail(IFX_ERR_UNSUPPORTED, "attention shape");
   const size_t smem = (size_t)decode_attention_smem(grp, a.hd, a.max_seq, a.ns);
   if (smem > 200 * 1024) return fail(IFX_ERR_UNSUPPORTED, "attention: KV chunk too large for shared memory");
-  static size_t attr = 0;
-  if (smem > 48 * 1024 && smem > attr) {
-    IFX_CUDA(cudaFuncSetAttribute(decode_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                  (int)smem));
-    attr = smem;
+  const bool tc = attn_tc_shape(grp, a.hd);
+  static size_t attr[2] = {0, 0};
+  if (smem > attr[tc]) {  // the static arrays count against the 48 KB default too
+    IFX_CUDA(cudaFuncSetAttribute(tc ? decode_attn_kernel<true> : decode_attn_kernel<false>,
+                                  cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    attr[tc] = smem;
   }
-  IFX_CUDA(launch(decode_attn_kernel, dim3(a.G, a.ns, a.batch), dim3(kAttnThreads), smem, st, pdl, a));
+  if (tc)
+    IFX_CUDA(launch(decode_attn_kernel<true>, dim3(a.G, a.ns, a.batch), dim3(kAttnThreads), smem,
+                    st, pdl, a));
+  else
+    IFX_CUDA(launch(decode_attn_kernel<false>, dim3(a.G, a.ns, a.batch), dim3(kAttnThreads), smem,
+                    st, pdl, a));
   return IFX_OK;
 }
 
