@@ -418,9 +418,83 @@ __device__ __noinline__ void attn_item_tc(const MegaArgs &A, const MegaAttn &at,
 // w_s = exp(m_s - M) / sum_s' exp(m_s' - M) l_s' (splits with no rows carry
 // l = 0 and weight 0). Two load rounds: the (m, l) pairs, then the partial
 // outputs. `wbuf` holds 3 * grp * nsa floats.
+// Fast form for grp * hd <= 512 and nsa <= 2 * kCombineLoads: warps 0-7
+// own the output float4s (two threads each, alternate splits), and issue all
+// their partial loads at once, while warps 8-11 fetch the (m, l) pairs and
+// form the weights; one memory round trip instead of three.
+constexpr int kCombineLoads = 12;
+
+__device__ __forceinline__ void combine_kv_head_fast(const MegaArgs &A, int h, float *wbuf) {
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int hd = A.hd, grp = A.H / A.G, NS = A.nsa;
+  float2 *ml = reinterpret_cast<float2 *>(wbuf);  // [grp][NS]
+  float *wn = wbuf + 2 * grp * NS;                 // [grp][NS]
+  const int F = grp * hd / 4;                      // output float4s
+  const int f = tid >> 1, half = tid & 1;
+  const bool mine = tid < 256 && f < F;
+  const int j = mine ? (4 * f) / hd : 0;
+  const float4 *po4 = reinterpret_cast<const float4 *>(A.part_o + (size_t)h * NS * grp * hd) + f;
+  const size_t s4 = (size_t)grp * hd / 4;  // float4s between splits
+  float4 v[kCombineLoads];
+#pragma unroll
+  for (int i = 0; i < kCombineLoads; ++i) {
+    const int sp = half + 2 * i;
+    v[i] = (mine && sp < NS) ? __ldcg(po4 + sp * s4) : make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+  if (warp >= 8 && warp < 8 + grp) {  // the weights of head warp - 8
+    const int jj = warp - 8;
+    float2 t[4];
+#pragma unroll
+    for (int r = 0; r < 4; ++r) {
+      const int sp = lane + 32 * r;
+      t[r] = sp < NS ? __ldcg(&A.part_ml[(h * NS + sp) * grp + jj]) : make_float2(-INFINITY, 0.f);
+    }
+    float M = -INFINITY;
+#pragma unroll
+    for (int r = 0; r < 4; ++r)
+      if (t[r].y > 0.f) M = fmaxf(M, t[r].x);
+    M = warp_max(M);
+    float L = 0.f, w[4];
+#pragma unroll
+    for (int r = 0; r < 4; ++r) {
+      w[r] = t[r].y > 0.f ? expf(t[r].x - M) : 0.f;
+      L = fmaf(t[r].y, w[r], L);
+    }
+    L = warp_sum(L);
+    const float invL = 1.0f / L;
+#pragma unroll
+    for (int r = 0; r < 4; ++r)
+      if (lane + 32 * r < NS) wn[jj * NS + lane + 32 * r] = w[r] * invL;
+  }
+  consumer_sync();
+  float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
+  if (mine) {
+    const float *w = wn + j * NS;
+#pragma unroll
+    for (int i = 0; i < kCombineLoads; ++i) {
+      const int sp = half + 2 * i;
+      const float ws = sp < NS ? w[sp] : 0.f;
+      o.x = fmaf(ws, v[i].x, o.x);
+      o.y = fmaf(ws, v[i].y, o.y);
+      o.z = fmaf(ws, v[i].z, o.z);
+      o.w = fmaf(ws, v[i].w, o.w);
+    }
+  }
+  // the two threads of a float4 (lanes 2k, 2k + 1) add their halves of the splits
+  o.x += __shfl_xor_sync(0xffffffffu, o.x, 1);
+  o.y += __shfl_xor_sync(0xffffffffu, o.y, 1);
+  o.z += __shfl_xor_sync(0xffffffffu, o.z, 1);
+  o.w += __shfl_xor_sync(0xffffffffu, o.w, 1);
+  if (mine && half == 0) reinterpret_cast<float4 *>(A.attn + (size_t)h * grp * hd)[f] = o;
+}
+
 __device__ __noinline__ void combine_kv_head(const MegaArgs &A, int h, float *wbuf) {
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int hd = A.hd, grp = A.H / A.G, NS = A.nsa;
+  if (grp * hd <= 512 && NS <= 2 * kCombineLoads && NS <= 128 && grp <= 8) {
+    combine_kv_head_fast(A, h, wbuf);
+    return;
+  }
   float2 *ml = reinterpret_cast<float2 *>(wbuf);  // [grp][NS]
   float *wn = wbuf + 2 * grp * NS;                 // [grp][NS]
   for (int e = tid; e < grp * NS; e += kConsumerThreads) {
