@@ -7,10 +7,14 @@ One "step" is one batch-1 greedy decode step (all 32 layers + logits +
 argmax) over a context that starts after a 1024-token prompt prefill. The
 weights (4.6 GB of quantised bytes per step) are far larger than L2, so no
 flush is needed between steps. `value` is device-timed with CUDA events over
-K graph replays whose inputs are already in HBM; `e2e` is the same metric
-through the C ABI's ifx_decode_step with host buffers (token H2D, logits D2H
-every step). With --gpus N > 1 each rank runs an independent replica (tensor
-parallelism is not in this build); value = sum over ranks.
+K persistent-kernel launches whose inputs are already in HBM; `e2e` is the
+same metric through the C ABI's ifx_decode_step with host buffers (token H2D,
+logits D2H every step). With --gpus N > 1 (under torchrun) each rank decodes
+an independent sequence (replicas, weak scaling, value = N / the slowest
+rank's step time) and a tensor-parallel leg decodes one sequence over all N
+GPUs (`tensor_parallel` in the line); --tp makes tensor parallelism the
+headline instead (strong scaling). `batched_decode` times 16 sequences per
+GPU decoded together.
 """
 from __future__ import annotations
 
@@ -158,8 +162,10 @@ def run_ours(args):
     from inferox_b200 import Model, synth, tp
 
     # several GPUs: tensor parallelism over all of them (one sequence, the
-    # weights split N ways) unless --replicas asks for one sequence per GPU
-    tp_mode = world > 1 and not args.replicas
+    # weights split N ways) with --tp; by default one independent sequence per
+    # GPU (replicas: weak scaling, no collective on the data path), with a
+    # tensor-parallel leg measured afterwards
+    tp_mode = world > 1 and args.tp
     comm = None
     t0 = time.time()
     g = synth.build(CONFIG, **({"n_layers": args.layers} if args.layers else {}))
@@ -242,10 +248,42 @@ def run_ours(args):
         kb.decode_greedy(firsts, 3)
         torch.cuda.synchronize()
         _, bms = kb.decode_greedy(firsts, args.batch_steps, timed=True)
-        batch = {"batch": B, "steps": args.batch_steps, "ms_per_step": bms / args.batch_steps,
-                 "tok_s": B * args.batch_steps / (bms * 1e-3),
+        if dist:
+            t = torch.tensor([bms], device="cuda")
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            bms = float(t.item())
+        batch = {"batch": B * world, "per_gpu_batch": B, "steps": args.batch_steps,
+                 "ms_per_step": bms / args.batch_steps,
+                 "tok_s": world * B * args.batch_steps / (bms * 1e-3),
                  "context": f"{PROMPT}-token prompts, {args.batch_steps} timed steps after 3"}
         del kb
+
+    # tensor-parallel leg (several GPUs, replicas mode): one sequence over all
+    # of them, Megatron split with NCCL all-reduces, device-timed like `value`
+    tpleg = None
+    if world > 1 and not tp_mode and not args.no_tp_leg:
+        uid = torch.zeros(128, dtype=torch.uint8, device="cuda")
+        if rank == 0:
+            uid.copy_(torch.frombuffer(bytearray(tp.unique_id()), dtype=torch.uint8))
+        dist.broadcast(uid, 0)
+        tcomm = tp.Comm(bytes(uid.cpu().numpy()), world, rank, local)
+        mt = Model.from_bytes(g, device=local, tp_size=world, tp_rank=rank, nccl_comm=tcomm.handle)
+        kvt = mt.kv_cache(max_seq)
+        p0 = synth.prompt_ids(V, PROMPT, seq_index=0)
+        tpf = time.perf_counter()
+        f0 = int(np.argmax(mt.prefill(p0, kvt, last_row_only=True)[0]))
+        tp_prefill_s = time.perf_counter() - tpf
+        mt.decode_greedy(f0, args.warmup, kvt)
+        dist.barrier()
+        torch.cuda.synchronize()
+        _, tms = mt.decode_greedy(f0, args.steps, kvt, timed=True)
+        t = torch.tensor([tms / args.steps], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        tpleg = {"n_gpus": world, "tok_s": 1000.0 / float(t.item()), "ms_per_step": float(t.item()),
+                 "prefill_tok_s": PROMPT / tp_prefill_s, "scaling": "strong",
+                 "parallelism": f"tp{world} (NCCL all-reduce after Wo and W2)"}
+        del kvt, mt  # the cache's CUDA graph holds NCCL work: release it before the comm
+        tcomm.close()
 
     # whole-step algorithmic bytes: every weight once + K/V at the mean context
     ctx_mean = ctx0 + args.steps / 2
@@ -287,6 +325,7 @@ def run_ours(args):
                          "roofline_tok_s": hbm * 1e9 / step_bytes},
         "prefill": {"tokens": PROMPT, "s": prefill_s, "tok_s": PROMPT / prefill_s},
         "batched_decode": batch,
+        "tensor_parallel": tpleg,
         # the dominant kernel is the decode step itself: with the persistent
         # path one launch per token, so achieved = algorithmic step bytes over
         # the device time of one step
@@ -341,9 +380,13 @@ def main():
     ap.add_argument("--batch", type=int, default=16,
                     help="also time batched decode of this many sequences (0/1: skip)")
     ap.add_argument("--batch-steps", type=int, default=32)
+    ap.add_argument("--tp", action="store_true",
+                    help="with several GPUs: decode one sequence with tensor parallelism over "
+                         "all of them (strong scaling) instead of one sequence per GPU")
     ap.add_argument("--replicas", action="store_true",
-                    help="with several GPUs: one independent sequence per GPU instead of "
-                         "tensor parallelism over all of them")
+                    help="one independent sequence per GPU (the default with several GPUs)")
+    ap.add_argument("--no-tp-leg", action="store_true",
+                    help="with several GPUs: skip the tensor-parallel leg")
     ap.add_argument("--layers", type=int, default=0,
                     help="profiling only: an 8B-shaped model with this many layers "
                          "(0 = the full 32); the line's config names it")
