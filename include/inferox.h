@@ -50,7 +50,9 @@ typedef enum ifx_status {
   IFX_ERR_TIMEOUT = 23,          /* a bounded device wait gave up */
   IFX_ERR_INVALID_ARGUMENT = 24, /* null pointer, zero size, bad enum */
   IFX_ERR_OUT_OF_MEMORY = 25,
-  IFX_ERR_UNSUPPORTED = 26       /* valid input this build does not run */
+  IFX_ERR_UNSUPPORTED = 26,      /* valid input this build does not run */
+  IFX_ERR_JSON = 27,             /* TokenizerError::Json (tokenizer/mod.rs:232) */
+  IFX_ERR_UNSUPPORTED_MODEL = 28 /* TokenizerError::UnsupportedModel (mod.rs:233) */
 } ifx_status;
 
 /* TensorType ids (src/gguf/types.rs:68-99) the kernels accept. */
@@ -312,6 +314,34 @@ int ifx_kv_decode_kernels(const ifx_kv *kv);
 ifx_status ifx_bench_kernel(ifx_model *m, ifx_kv *kv, const char *which,
                             int reps, float *ms_per_launch,
                             uint64_t *bytes_per_launch);
+
+/* ------------------------------ tokenizer ------------------------------- */
+/* The reference's byte-level BPE tokenizer over a Hugging Face
+ * tokenizer.json (BpeTokenizer, src/tokenizer/mod.rs:23-226; GPT-2 byte
+ * tables, bytes.rs:10-35). Host code; needs no GPU. Errors: IFX_ERR_IO
+ * (TokenizerError::Io, including a file that is not UTF-8), IFX_ERR_JSON
+ * (TokenizerError::Json: malformed JSON or a schema mismatch),
+ * IFX_ERR_UNSUPPORTED_MODEL (model.type other than "BPE"). */
+typedef struct ifx_tokenizer ifx_tokenizer;
+/* BpeTokenizer::from_file (mod.rs:61-64). */
+ifx_status ifx_tokenizer_load(const char *path, ifx_tokenizer **out);
+/* BpeTokenizer::from_json (mod.rs:67-110); `json` is UTF-8, `len` bytes. */
+ifx_status ifx_tokenizer_load_json(const char *json, size_t len,
+                                   ifx_tokenizer **out);
+void ifx_tokenizer_free(ifx_tokenizer *t);
+/* Tokenizer::encode (mod.rs:194-204) of `len` bytes of UTF-8 text. Sets
+ * *n_ids to the id count; IFX_ERR_SHAPE (nothing written) when it exceeds
+ * `cap`, so a caller can size the buffer with a first call of cap 0. */
+ifx_status ifx_tokenizer_encode(const ifx_tokenizer *t, const char *text,
+                                size_t len, uint32_t *ids, size_t cap,
+                                size_t *n_ids);
+/* Tokenizer::decode (mod.rs:206-225): UTF-8 bytes (not NUL-terminated)
+ * into `text`; *len and IFX_ERR_SHAPE as for encode. */
+ifx_status ifx_tokenizer_decode(const ifx_tokenizer *t, const uint32_t *ids,
+                                size_t n, char *text, size_t cap,
+                                size_t *len);
+/* Number of vocabulary entries (model.vocab). */
+ifx_status ifx_tokenizer_vocab_size(const ifx_tokenizer *t, size_t *n);
 
 /* ------------------- synthetic workload generator ----------------------- */
 /* No reference counterpart: the reference's tests build GGUF fixtures in

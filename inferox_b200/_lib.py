@@ -18,7 +18,8 @@ STATUS = {
     5: "UnknownTensorType", 6: "InvalidUtf8", 7: "InvalidShape", 8: "UnexpectedEof",
     9: "TensorNotFound", 10: "InvalidTensorIndex", 11: "TensorOffsetOverflow",
     12: "UnsupportedArchitecture", 20: "Shape", 21: "Cuda", 22: "Nccl", 23: "Timeout",
-    24: "InvalidArgument", 25: "OutOfMemory", 26: "Unsupported",
+    24: "InvalidArgument", 25: "OutOfMemory", 26: "Unsupported", 27: "Json",
+    28: "UnsupportedModel",
 }
 
 TYPE_F32, TYPE_F16, TYPE_Q4_0, TYPE_Q8_0, TYPE_Q4_K, TYPE_Q6_K, TYPE_Q8_K = 0, 1, 2, 7, 12, 14, 15
@@ -130,6 +131,12 @@ def _load():
         "ifx_op_argmax": (st, [vp, sz, vp, vp]),
         "ifx_op_sample_u": (st, [vp, sz, C.POINTER(SamplerC), C.c_float, u32p, vp]),
         "ifx_op_sample_u_static": (st, [vp, sz, C.POINTER(SamplerC), C.c_float, vp, vp]),
+        "ifx_tokenizer_load": (st, [C.c_char_p, C.POINTER(vp)]),
+        "ifx_tokenizer_load_json": (st, [C.c_char_p, sz, C.POINTER(vp)]),
+        "ifx_tokenizer_free": (None, [vp]),
+        "ifx_tokenizer_encode": (st, [vp, C.c_char_p, sz, u32p, sz, C.POINTER(sz)]),
+        "ifx_tokenizer_decode": (st, [vp, u32p, sz, C.c_char_p, sz, C.POINTER(sz)]),
+        "ifx_tokenizer_vocab_size": (st, [vp, C.POINTER(sz)]),
         "ifx_synth_gguf": (st, [C.POINTER(SynthSpec), C.POINTER(vp), C.POINTER(sz)]),
         "ifx_synth_free": (None, [vp]),
         "ifx_quantize": (st, [C.c_int, vp, sz, vp]),

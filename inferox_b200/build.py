@@ -21,6 +21,8 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 CSRC = os.path.join(HERE, "csrc")
 BUILD = os.path.join(HERE, "_build")
 LIB = os.path.join(HERE, "libinferox_b200.so")
+CLI_SRC = os.path.join(HERE, "cli", "ifx.cpp")
+CLI = os.path.join(HERE, "ifx")  # the command-line program (src/main.rs)
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FLAGS = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC,-O3", "--expt-relaxed-constexpr",
@@ -67,7 +69,21 @@ def build(clean: bool = False, verbose: bool = False) -> str:
         r = subprocess.run(cmd, capture_output=True, text=True)
         if r.returncode != 0:
             raise RuntimeError(f"link failed:\n{r.stderr}")
+    build_cli()
     return LIB
+
+
+def build_cli() -> str:
+    """The `ifx` program: host C++ over the library (rpath: its own folder)."""
+    deps = [CLI_SRC, LIB, os.path.join(CSRC, "gguf.h")]
+    if os.path.exists(CLI) and os.path.getmtime(CLI) >= max(os.path.getmtime(d) for d in deps):
+        return CLI
+    cmd = ["g++", "-O2", "-std=c++17", "-Wall", CLI_SRC, "-o", CLI, f"-L{HERE}", "-linferox_b200",
+           "-Wl,-rpath,$ORIGIN"]
+    r = subprocess.run(cmd, capture_output=True, text=True)
+    if r.returncode != 0:
+        raise RuntimeError(f"ifx build failed:\n{r.stderr}")
+    return CLI
 
 
 if __name__ == "__main__":

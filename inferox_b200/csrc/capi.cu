@@ -85,6 +85,8 @@ const char *ifx_status_name(ifx_status s) {
     case IFX_ERR_INVALID_ARGUMENT: return "InvalidArgument";
     case IFX_ERR_OUT_OF_MEMORY: return "OutOfMemory";
     case IFX_ERR_UNSUPPORTED: return "Unsupported";
+    case IFX_ERR_JSON: return "Json";
+    case IFX_ERR_UNSUPPORTED_MODEL: return "UnsupportedModel";
   }
   return "Unknown";
 }

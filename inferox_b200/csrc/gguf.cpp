@@ -113,7 +113,18 @@ bool read_value(Reader &r, uint32_t vt, GgufValue *v) {
         return false;
       }
       uint64_t n = r.u64();
-      for (uint64_t k = 0; k < n && !r.err; ++k) read_value(r, it, nullptr);
+      if (v) {
+        v->arr_type = it;
+        v->arr_len = n;
+      }
+      for (uint64_t k = 0; k < n && !r.err; ++k) {
+        if (v && k < GgufValue::kArrayPreview) {
+          v->items.emplace_back();
+          read_value(r, it, &v->items.back());
+        } else {
+          read_value(r, it, nullptr);
+        }
+      }
       break;
     }
     case 10: { uint64_t x = 0; r.read(&x, 8); if (v) v->u = x; break; }

@@ -16,6 +16,12 @@ struct GgufValue {
   int64_t i = 0;
   double f = 0;
   std::string s;
+  // arrays: element type, length and the first kArrayPreview items (what
+  // Value's Display shows, value.rs:86-99); the rest are parsed and dropped
+  uint32_t arr_type = 0;
+  uint64_t arr_len = 0;
+  std::vector<GgufValue> items;
+  static constexpr uint64_t kArrayPreview = 9;
 };
 
 struct GgufTensor {
