@@ -96,7 +96,14 @@ typedef struct ifx_load_opts {
   int persistent_decode; /* 1 (default): batch-1 decode steps run as one
                             persistent cooperative kernel per token when the
                             head geometry allows it; 0: one kernel per op */
+  int kquant_layout; /* IFX_KQUANT_REFERENCE (default): type ids and Q4_K /
+                        Q6_K bytes as the reference reads them
+                        (types.rs:70-100, dequant.rs:123-199);
+                        IFX_KQUANT_GGML: a file written by llama.cpp (ggml
+                        ids, ggml block orders, int8 Q6_K scales) */
 } ifx_load_opts;
+
+enum { IFX_KQUANT_REFERENCE = 0, IFX_KQUANT_GGML = 1 };
 
 void ifx_load_opts_default(ifx_load_opts *o);
 
@@ -314,6 +321,18 @@ int ifx_kv_decode_kernels(const ifx_kv *kv);
 ifx_status ifx_bench_kernel(ifx_model *m, ifx_kv *kv, const char *which,
                             int reps, float *ms_per_launch,
                             uint64_t *bytes_per_launch);
+
+/* No reference counterpart (the reference reads only its own byte orders).
+ * Tensor bytes of ggml type id `ggml_type` in llama.cpp's block order,
+ * rewritten into the reference's order (dequant.rs:123-199), as a load with
+ * IFX_KQUANT_GGML does: Q4_K and Q6_K blocks are permuted, Q4_0 / Q8_0 /
+ * F32 / F16 copied. *type_out receives the reference's type id;
+ * *signed_scales_out is 1 for Q6_K, whose scale bytes keep llama.cpp's int8
+ * meaning (the reference would read them as u8). Host code; needs no GPU.
+ * `dst` holds nbytes; it may equal `src` only for the copied types. */
+ifx_status ifx_kquant_from_ggml(uint32_t ggml_type, const void *src,
+                                size_t nbytes, void *dst, int *type_out,
+                                int *signed_scales_out);
 
 /* ------------------------------ tokenizer ------------------------------- */
 /* The reference's byte-level BPE tokenizer over a Hugging Face

@@ -50,7 +50,7 @@ class LoadOpts(C.Structure):
     _fields_ = [
         ("device", C.c_int), ("tp_size", C.c_int), ("tp_rank", C.c_int),
         ("nccl_comm", C.c_void_p), ("rope_compat", C.c_int), ("use_graphs", C.c_int),
-        ("persistent_decode", C.c_int),
+        ("persistent_decode", C.c_int), ("kquant_layout", C.c_int),
     ]
 
 
@@ -131,6 +131,7 @@ def _load():
         "ifx_op_argmax": (st, [vp, sz, vp, vp]),
         "ifx_op_sample_u": (st, [vp, sz, C.POINTER(SamplerC), C.c_float, u32p, vp]),
         "ifx_op_sample_u_static": (st, [vp, sz, C.POINTER(SamplerC), C.c_float, vp, vp]),
+        "ifx_kquant_from_ggml": (st, [C.c_uint32, vp, sz, vp, C.POINTER(C.c_int), C.POINTER(C.c_int)]),
         "ifx_tokenizer_load": (st, [C.c_char_p, C.POINTER(vp)]),
         "ifx_tokenizer_load_json": (st, [C.c_char_p, sz, C.POINTER(vp)]),
         "ifx_tokenizer_free": (None, [vp]),

@@ -102,6 +102,11 @@ __device__ __forceinline__ float u2f6(uint32_t v) {
 __device__ __forceinline__ float u2f8(uint32_t v) {
   return __uint_as_float(0x4B000000u | (v & 255u)) - 8388608.0f;
 }
+// A Q6_K scale byte as u8 (smask 0, the reference) or int8 (smask 0x80,
+// llama.cpp): (v ^ smask) - smask, with bias = 2^23 + smask (exact).
+__device__ __forceinline__ float s2f8(uint32_t v, uint32_t smask, float bias) {
+  return __uint_as_float(0x4B000000u | ((v & 255u) ^ smask)) - bias;
+}
 __device__ __forceinline__ __half2 u2h(uint32_t u) { return *reinterpret_cast<__half2 *>(&u); }
 
 // (v - sub) * scale + add with v the magic-biased f16 pair in `bits`.
@@ -118,12 +123,14 @@ struct GemmArgs {
   int type, rows, kc, kunits, unit_bytes, wt_bytes, wt_qbytes, nch_total;
   int accumulate;  // C += result (else C = result)
   int atomic;      // C += result with atomic adds (K split over gridDim.z CTAs)
+  uint32_t smask;  // 0x80: Q6_K scale bytes are int8 (llama.cpp), else 0
   int *err;
 };
 
 template <int TYPE, int NT>
 __device__ __forceinline__ void gemm_unit(const uint8_t *wt, const uint8_t *xs, const float *sx,
-                                          int kc, int wt_qbytes, int lane, float (&acc)[NT][4]) {
+                                          int kc, int wt_qbytes, uint32_t smask, int lane,
+                                          float (&acc)[NT][4]) {
   const int g = lane >> 2, c = lane & 3;
   // chunks per scale group: Q6_K scales every 16 columns, the others every 32
   constexpr int cpg = (TYPE == IFX_TYPE_Q6_K) ? 1 : 2;
@@ -211,8 +218,9 @@ __device__ __forceinline__ void gemm_unit(const uint8_t *wt, const uint8_t *xs, 
       mB = dmB * u2f6(fB >> (12 + sh));
     } else if (TYPE == IFX_TYPE_Q6_K) {
       const uint8_t *scb = wt + 3072;
-      sA = dA * u2f8(scb[16 * g + gi]);
-      sB = dB * u2f8(scb[16 * (g + 8) + gi]);
+      const float sbias = 8388608.0f + (float)smask;
+      sA = dA * s2f8(scb[16 * g + gi], smask, sbias);
+      sB = dB * s2f8(scb[16 * (g + 8) + gi], smask, sbias);
     } else {
       const int nb = kc / 32;
       sA = h2f(*reinterpret_cast<const uint16_t *>(wt + wt_qbytes + (g * nb + gi) * 2));
@@ -302,10 +310,10 @@ __global__ void __launch_bounds__(kGThreads, 1) gemm_kernel(const __grid_constan
     const uint8_t *xs = base + a.unit_bytes;
     const float *sx = reinterpret_cast<const float *>(xs + a.kc / 16 * xchunk_bytes(NT));
     switch (a.type) {
-      case IFX_TYPE_Q4_K: gemm_unit<IFX_TYPE_Q4_K, NT>(wt, xs, sx, a.kc, a.wt_qbytes, lane, acc); break;
-      case IFX_TYPE_Q6_K: gemm_unit<IFX_TYPE_Q6_K, NT>(wt, xs, sx, a.kc, a.wt_qbytes, lane, acc); break;
-      case IFX_TYPE_Q4_0: gemm_unit<IFX_TYPE_Q4_0, NT>(wt, xs, sx, a.kc, a.wt_qbytes, lane, acc); break;
-      default: gemm_unit<IFX_TYPE_Q8_0, NT>(wt, xs, sx, a.kc, a.wt_qbytes, lane, acc); break;
+      case IFX_TYPE_Q4_K: gemm_unit<IFX_TYPE_Q4_K, NT>(wt, xs, sx, a.kc, a.wt_qbytes, a.smask, lane, acc); break;
+      case IFX_TYPE_Q6_K: gemm_unit<IFX_TYPE_Q6_K, NT>(wt, xs, sx, a.kc, a.wt_qbytes, a.smask, lane, acc); break;
+      case IFX_TYPE_Q4_0: gemm_unit<IFX_TYPE_Q4_0, NT>(wt, xs, sx, a.kc, a.wt_qbytes, a.smask, lane, acc); break;
+      default: gemm_unit<IFX_TYPE_Q8_0, NT>(wt, xs, sx, a.kc, a.wt_qbytes, a.smask, lane, acc); break;
     }
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty_bar[st]);
@@ -392,6 +400,7 @@ static ifx_status launch_sync(const QMatrix &W, const void *xfrag, int64_t M, fl
   a.unit_bytes = W.L.unit_bytes;
   a.wt_bytes = W.L.wt_bytes;
   a.wt_qbytes = W.L.wt_qbytes;
+  a.smask = W.L.q6_s8 ? 0x80u : 0u;
   a.nch_total = (int)(W.L.cols / 16);
   a.accumulate = accumulate;
   a.atomic = ksplit > 1 ? 1 : 0;

@@ -97,7 +97,7 @@ ifx_status gemv_plan(const QMatrix *const *mats, float *const *ys, int nseg, int
     GemvSeg &S = a.seg[i];
     S.w = mats[i]->d;
     S.y = ys[i];
-    S.type = L.type;
+    S.type = L.type | (L.q6_s8 ? 0x80 << 8 : 0);
     S.rows = (int)L.rows;
     S.unit_bytes = L.unit_bytes;
     S.wt_bytes = L.wt_bytes;

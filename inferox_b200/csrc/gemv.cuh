@@ -24,7 +24,8 @@ constexpr int kGemvBarBytes = 2 * kGemvMaxStages * 8;  // full + empty mbarriers
 struct GemvSeg {
   const uint8_t *w;  // repacked weights (device)
   float *y;          // output, accumulated with red.global.add
-  int type;
+  int type;          // low byte: IFX_TYPE_*; bits 8-15: Q6_K scale mask (0x80:
+                     // int8 scale bytes as llama.cpp writes them, 0: u8)
   int rows;          // valid output rows
   int unit_bytes, wt_bytes, wt_qbytes;
   int unit_begin;    // first global unit index of this segment

@@ -32,6 +32,11 @@ __device__ __forceinline__ int find_seg(const GemvArgs &a, int u) {
 __device__ __forceinline__ float u2f_small(uint32_t v) {
   return __uint_as_float(0x4B000000u | v) - 8388608.0f;
 }
+// A scale byte v as u8 (smask 0) or int8 (smask 0x80): (v ^ smask) placed in
+// the mantissa of 2^23, minus bias = 2^23 + smask (both exact).
+__device__ __forceinline__ float sc2f(uint32_t v, uint32_t smask, float bias) {
+  return __uint_as_float(0x4B000000u | (v ^ smask)) - bias;
+}
 
 struct Acc2 {
   float r0, r1;  // rows g and g+8
@@ -132,8 +137,10 @@ __device__ __forceinline__ void unit_q4k(const uint8_t *wt, const uint4 *xf, int
 // Sixteen 16-column groups per unit; accumulator set t = chunk >> 2 holds
 // chunks 4t..4t+3 (hi columns 0-3, lo columns 4-7), one set per 64-column
 // step, separately for the low-nibble plane (DL) and the 2-bit plane (DH).
+// smask 0x80 reads the scale bytes as int8 (llama.cpp), 0 as u8 (the
+// reference): (b ^ smask) - smask.
 __device__ __forceinline__ void unit_q6k(const uint8_t *wt, const uint4 *xf, int xlo,
-                                         const float *s16, int lane, Acc2 &acc) {
+                                         const float *s16, int lane, uint32_t smask, Acc2 &acc) {
   const int g = lane >> 2, c = lane & 3, gq = g & 3;
   const uint4 *xp = xplane(xf, xlo, g);
   const uint2 *zero2 = reinterpret_cast<const uint2 *>(&g_xzero);
@@ -189,6 +196,7 @@ __device__ __forceinline__ void unit_q6k(const uint8_t *wt, const uint4 *xf, int
   fold_hilo(T[0], T[1], c, U[0]);
   fold_hilo(T[2], T[3], c, U[1]);
   const uint8_t *scb = wt + 3072;
+  const float sbias = 8388608.0f + (float)smask;
 #pragma unroll
   for (int h = 0; h < 2; ++h) {
     const int row = g + 8 * h;
@@ -205,7 +213,7 @@ __device__ __forceinline__ void unit_q6k(const uint8_t *wt, const uint4 *xf, int
 #pragma unroll
       for (int j = 0; j < 2; ++j) {
         const int grp = 8 * set + 2 * c + j;
-        const float sc = u2f_small((sw >> (sh + 8 * j)) & 0xffu);
+        const float sc = sc2f((sw >> (sh + 8 * j)) & 0xffu, smask, sbias);
         r = fmaf(d * sc, U[set][2 * h + j] - 32.0f * s16[grp], r);
       }
     }
@@ -328,7 +336,7 @@ __device__ __forceinline__ void consumer_sync() {
 struct SegView {
   const uint8_t *w;
   float *y;
-  int type, rows, unit_bytes, wt_bytes, wt_qbytes, begin, units;
+  int type, rows, unit_bytes, wt_bytes, wt_qbytes, begin, units;  // type as in GemvSeg
 };
 
 __device__ __forceinline__ SegView load_seg(const GemvArgs &a, int s) {
@@ -573,7 +581,7 @@ __device__ __forceinline__ bool consume_run(const SegView &S, int k0, int cnt, i
     const uint4 *xf = reinterpret_cast<const uint4 *>(xw) + (size_t)slot * xstep + (lane & 3);
     const float *sl = s16 + (size_t)slot * sstep;
     if (TYPE == IFX_TYPE_Q4_K) unit_q4k(wt, xf, xlo, sl, lane, acc);
-    else if (TYPE == IFX_TYPE_Q6_K) unit_q6k(wt, xf, xlo, sl, lane, acc);
+    else if (TYPE == IFX_TYPE_Q6_K) unit_q6k(wt, xf, xlo, sl, lane, (uint32_t)S.type >> 8, acc);
     else if (TYPE == IFX_TYPE_Q4_0) unit_q4_0(wt, kc, S.wt_qbytes, xf, xlo, sl, lane, acc);
     else unit_q8_0(wt, kc, S.wt_qbytes, xf, xlo, sl, lane, acc);
     __syncwarp();
@@ -617,7 +625,7 @@ __device__ __forceinline__ bool gemv_consume(const GemvArgs &a, int u0, int n, u
   for (int k = 0; k < hcnt;) {
     const int cnt = min(hcnt - k, seg_left);
     bool ok;
-    switch (S.type) {
+    switch (S.type & 0xff) {
       case IFX_TYPE_Q4_K:
         ok = consume_run<IFX_TYPE_Q4_K>(S, k, cnt, half, hbeg, it, ring, NS, slot_bytes, full_bar,
                                         empty_bar, xw, s16, full, kc, kunits, xlo, ctile, kunit, acc, err);

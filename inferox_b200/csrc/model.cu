@@ -25,6 +25,7 @@
 #include "attention.cuh"
 #include "gemm.cuh"
 #include "gemv.cuh"
+#include "kquant.h"
 #include "gguf.h"
 #include "model.h"
 #include "tp.h"
@@ -201,27 +202,43 @@ ifx_status dalloc(T **p, size_t n) {
 }  // namespace
 
 // ------------------------------------------------------------------ load --
+// A tensor's bytes in the reference's block order: llama.cpp-ordered Q4_K /
+// Q6_K blocks (ggml = true) are permuted into `conv` and *type becomes the
+// converted type (kTypeQ6KS8 for Q6_K); anything else is used in place.
+static ifx_status reference_order(bool ggml, const uint8_t **src, uint64_t size, int *type,
+                                  std::vector<uint8_t> *conv) {
+  if (!ggml || (*type != IFX_TYPE_Q4_K && *type != IFX_TYPE_Q6_K)) return IFX_OK;
+  conv->resize(size);
+  IFX_TRY(ggml_to_reference(*type, *src, size, conv->data(), type));
+  *src = conv->data();
+  return IFX_OK;
+}
+
 // A weight [rows, cols] uploaded and repacked; under tensor parallelism only
 // this rank's shard (split_k = 0: a block of rows; 1: a block of the input
 // dimension of every row) is kept.
 static ifx_status upload_matrix(const GgufFile &f, const uint8_t *bytes, size_t len, int idx,
                                 uint64_t rows, uint64_t cols, uint8_t *staging, cudaStream_t st,
-                                QMatrix *out, int tp = 1, int rank = 0, int split_k = 0) {
+                                QMatrix *out, int tp = 1, int rank = 0, int split_k = 0,
+                                bool ggml = false) {
   uint64_t start, size;
   IFX_TRY(gguf_tensor_range(f, len, idx, &start, &size));
   const GgufTensor &t = f.tensors[idx];
   if (t.n_elements() != rows * cols)
     return fail(IFX_ERR_SHAPE, "tensor " + t.name + ": element count does not match the config");
   const uint8_t *src = bytes + start;
+  int type = (int)t.type;
+  std::vector<uint8_t> conv;
+  IFX_TRY(reference_order(ggml, &src, size, &type, &conv));
   std::vector<uint8_t> shard;
   if (tp > 1) {
-    IFX_TRY(tp_shard((int)t.type, src, size, rows, cols, split_k, tp, rank, &shard));
+    IFX_TRY(tp_shard(type, src, size, rows, cols, split_k, tp, rank, &shard));
     if (split_k) cols /= tp;
     else rows /= tp;
     src = shard.data();
     size = shard.size();
   }
-  if (!make_layout((int)t.type, (int64_t)rows, (int64_t)cols, &out->L))
+  if (!make_layout(type, (int64_t)rows, (int64_t)cols, &out->L))
     return fail(IFX_ERR_UNSUPPORTED,
                 "tensor " + t.name + ": weight type " + std::to_string(t.type) +
                     " is not supported by the fused kernels (Q4_0, Q8_0, Q4_K, Q6_K)");
@@ -253,8 +270,20 @@ ifx_status Model::load(const uint8_t *bytes, size_t len, const ifx_load_opts &o)
     return fail(IFX_ERR_INVALID_ARGUMENT, "tp_size must be 1..8 and 0 <= tp_rank < tp_size");
   if (tp > 1 && !opts.nccl_comm)
     return fail(IFX_ERR_INVALID_ARGUMENT, "tensor parallel loading needs nccl_comm");
+  if (opts.kquant_layout != IFX_KQUANT_REFERENCE && opts.kquant_layout != IFX_KQUANT_GGML)
+    return fail(IFX_ERR_INVALID_ARGUMENT, "kquant_layout must be IFX_KQUANT_REFERENCE or IFX_KQUANT_GGML");
+  const bool ggml = opts.kquant_layout == IFX_KQUANT_GGML;
   GgufFile f;
   IFX_TRY(gguf_parse(bytes, len, &f));  // host-only checks first: no GPU needed to reject a file
+  if (ggml) {
+    // llama.cpp's type ids (Q8_0 = 8, ...) onto the reference's; a type with
+    // no counterpart gets an id no size is known for, so any use of it fails
+    // as an unknown tensor type
+    for (GgufTensor &t : f.tensors) {
+      const int r = ggml_type_to_reference(t.type);
+      t.type = r < 0 ? 0xFFFFu : (uint32_t)r;
+    }
+  }
   IFX_TRY(gguf_config(f, &cfg));
   if (cfg.vocab_size == 0) return fail(IFX_ERR_SHAPE, "llama.vocab_size is missing or zero");
   const uint64_t D = cfg.hidden_size, H = cfg.n_heads, G = cfg.n_kv_heads, hd = cfg.head_dim;
@@ -310,29 +339,32 @@ ifx_status Model::load(const uint8_t *bytes, size_t len, const ifx_load_opts &o)
   for (uint64_t l = 0; l < cfg.n_layers && st == IFX_OK; ++l) {
     Layer &L = layers[l];
     guard(upload_norm(f, bytes, len, idx[l][0], D, staging, stream, &L.attn_norm)) &&
-        guard(upload_matrix(f, bytes, len, idx[l][1], D, D, staging, stream, &L.wq, tp, rank, 0)) &&
-        guard(upload_matrix(f, bytes, len, idx[l][2], G * hd, D, staging, stream, &L.wk, tp, rank, 0)) &&
-        guard(upload_matrix(f, bytes, len, idx[l][3], G * hd, D, staging, stream, &L.wv, tp, rank, 0)) &&
-        guard(upload_matrix(f, bytes, len, idx[l][4], D, D, staging, stream, &L.wo, tp, rank, 1)) &&
+        guard(upload_matrix(f, bytes, len, idx[l][1], D, D, staging, stream, &L.wq, tp, rank, 0, ggml)) &&
+        guard(upload_matrix(f, bytes, len, idx[l][2], G * hd, D, staging, stream, &L.wk, tp, rank, 0, ggml)) &&
+        guard(upload_matrix(f, bytes, len, idx[l][3], G * hd, D, staging, stream, &L.wv, tp, rank, 0, ggml)) &&
+        guard(upload_matrix(f, bytes, len, idx[l][4], D, D, staging, stream, &L.wo, tp, rank, 1, ggml)) &&
         guard(upload_norm(f, bytes, len, idx[l][5], D, staging, stream, &L.ffn_norm)) &&
-        guard(upload_matrix(f, bytes, len, idx[l][6], F, D, staging, stream, &L.w1, tp, rank, 0)) &&
-        guard(upload_matrix(f, bytes, len, idx[l][7], F, D, staging, stream, &L.w3, tp, rank, 0)) &&
-        guard(upload_matrix(f, bytes, len, idx[l][8], D, F, staging, stream, &L.w2, tp, rank, 1));
+        guard(upload_matrix(f, bytes, len, idx[l][6], F, D, staging, stream, &L.w1, tp, rank, 0, ggml)) &&
+        guard(upload_matrix(f, bytes, len, idx[l][7], F, D, staging, stream, &L.w3, tp, rank, 0, ggml)) &&
+        guard(upload_matrix(f, bytes, len, idx[l][8], D, F, staging, stream, &L.w2, tp, rank, 1, ggml));
   }
   if (st == IFX_OK) guard(upload_norm(f, bytes, len, i_onorm, D, staging, stream, &out_norm));
   if (st == IFX_OK)
     guard(upload_matrix(f, bytes, len, i_out >= 0 ? i_out : i_emb, V, D, staging, stream, &out_w,
-                        tp, rank, 0));
+                        tp, rank, 0, ggml));
   if (st == IFX_OK) {
     uint64_t s0, sz;
     if (guard(gguf_tensor_range(f, len, i_emb, &s0, &sz))) {
       const GgufTensor &t = f.tensors[i_emb];
       emb_type = (int)t.type;
+      const uint8_t *esrc = bytes + s0;
+      std::vector<uint8_t> conv;
       if (t.n_elements() != V * D) guard(fail(IFX_ERR_SHAPE, "token_embd.weight: element count"));
       else if (!block_info(emb_type).elems)
         guard(fail(IFX_ERR_UNSUPPORTED, "token_embd.weight: type not supported"));
-      else if (cudaMalloc(&emb_raw, sz) != cudaSuccess ||
-               cudaMemcpy(emb_raw, bytes + s0, sz, cudaMemcpyHostToDevice) != cudaSuccess)
+      else if (guard(reference_order(ggml, &esrc, sz, &emb_type, &conv)) &&
+               (cudaMalloc(&emb_raw, sz) != cudaSuccess ||
+                cudaMemcpy(emb_raw, esrc, sz, cudaMemcpyHostToDevice) != cudaSuccess))
         guard(fail(IFX_ERR_CUDA, "token_embd upload"));
       emb_row_bytes = (V ? sz / V : 0);
     }

@@ -40,13 +40,20 @@ struct QLayout {
   int wt_bytes = 0;
   int unit_bytes = 0;
   uint64_t total_bytes = 0;
+  int q6_s8 = 0;     // Q6_K scale bytes are int8 (llama.cpp), not u8
 };
 
 // Largest unit that still fits the GEMV's shared-memory stage.
 constexpr int kMaxUnitBytes = 27 * 1024;
 
 // Fills `L` for a [rows, cols] matrix of `type`; false if unsupported.
+// kTypeQ6KS8 gives the Q6_K layout with q6_s8 set.
 inline bool make_layout(int type, int64_t rows, int64_t cols, QLayout *L) {
+  if (type == kTypeQ6KS8) {
+    if (!make_layout(IFX_TYPE_Q6_K, rows, cols, L)) return false;
+    L->q6_s8 = 1;
+    return true;
+  }
   QLayout q;
   q.type = type;
   q.rows = rows;

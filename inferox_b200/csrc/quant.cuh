@@ -13,6 +13,13 @@ struct BlockInfo {
   int elems, bytes;
 };
 
+// Internal type id (never in a file): Q6_K blocks in the reference's byte
+// order whose sixteen scale bytes are int8, as llama.cpp writes and reads
+// them (the reference reads them as u8, dequant.rs:195). Loads with
+// kquant_layout = IFX_KQUANT_GGML permute llama.cpp's Q6_K blocks into the
+// reference's order and tag them with this id.
+constexpr int kTypeQ6KS8 = 0x100 | IFX_TYPE_Q6_K;
+
 __host__ __device__ inline BlockInfo block_info(int type) {
   switch (type) {
     case IFX_TYPE_F32: return {1, 4};
@@ -21,6 +28,7 @@ __host__ __device__ inline BlockInfo block_info(int type) {
     case IFX_TYPE_Q8_0: return {32, 34};
     case IFX_TYPE_Q4_K: return {256, 144};
     case IFX_TYPE_Q6_K: return {256, 210};
+    case kTypeQ6KS8: return {256, 210};
     case IFX_TYPE_Q8_K: return {256, 292};
     default: return {0, 0};
   }
@@ -81,6 +89,16 @@ __device__ __forceinline__ float dequant_elem(int type, const uint8_t *src, uint
       uint32_t hb = (c[146 + j / 4] >> (2 * (j % 4))) & 3;
       int q = (int)(nib | (hb << 4));
       return __fmul_rn(__fmul_rn(d, (float)c[2 + j / 16]), (float)(q - 32));
+    }
+    case kTypeQ6KS8: {  // the same with int8 scales: y = (d * sc) * (q - 32)
+      const uint8_t *c = src + (e / 256) * 210;
+      int j = (int)(e % 256);
+      float d = h2f_exact(ld_u16(c));
+      uint8_t qlb = c[18 + j / 2];
+      uint32_t nib = (j % 2 == 0) ? (qlb & 15) : (qlb >> 4);
+      uint32_t hb = (c[146 + j / 4] >> (2 * (j % 4))) & 3;
+      int q = (int)(nib | (hb << 4));
+      return __fmul_rn(__fmul_rn(d, (float)(int8_t)c[2 + j / 16]), (float)(q - 32));
     }
     case IFX_TYPE_Q8_K: {  // dequant.rs:210-232
       const uint8_t *c = src + (e / 256) * 292;

@@ -182,6 +182,7 @@ struct TcSeg {
   float *C;
   int64_t ldc;
   int type, rows, kc, kunits, unit_bytes, wt_bytes, wt_qbytes, ctile0, ctiles;
+  uint32_t smask;  // 0x80: Q6_K scale bytes are int8 (llama.cpp), else 0
 };
 
 struct TcArgs {
@@ -326,8 +327,9 @@ __device__ __forceinline__ void tc_emit(const TcSeg &a, const TcRaw &R, int wt, 
         const __half2 v = __hsub2(u2h2(av[r] | 0x64006400u), (r & 1) ? sub1 : sub0);
         av[r] = *reinterpret_cast<const uint32_t *>(&v);
       }
-      m0 *= (float)((R.s0 >> (8 * i)) & 0xffu);  // u8 scale of the 16-column chunk
-      m1 *= (float)((R.s1 >> (8 * i)) & 0xffu);
+      // scale of the 16-column chunk: u8 (the reference) or int8 (smask 0x80)
+      m0 *= (float)(int)(((R.s0 >> (8 * i)) & 0xffu) ^ a.smask) - (float)a.smask;
+      m1 *= (float)(int)(((R.s1 >> (8 * i)) & 0xffu) ^ a.smask) - (float)a.smask;
     } else {  // Q8_0, dequant.rs:93-111: q * d (bytes stored as q + 128)
       const uint4 Q = (i >> 1) ? R.q2 : R.q;  // chunk pair (i / 2), chunk i % 2 of it
       const uint32_t wa = (i & 1) ? Q.z : Q.x, wb = (i & 1) ? Q.w : Q.y;
@@ -560,6 +562,7 @@ ifx_status tc_gemm_run_multi(const QMatrix *const *W, float *const *C, const int
     S.unit_bytes = L.unit_bytes;
     S.wt_bytes = L.wt_bytes;
     S.wt_qbytes = L.wt_qbytes;
+    S.smask = L.q6_s8 ? 0x80u : 0u;
     S.ctile0 = ct;
     S.ctiles = L.ctiles;
     ct += L.ctiles;

@@ -31,7 +31,9 @@ def _f32(a):
 
 def load_opts(device: int = 0, rope_compat: bool = True, use_graphs: bool = True,
               tp_size: int = 1, tp_rank: int = 0, nccl_comm: int | None = None,
-              persistent_decode: bool = True) -> LoadOpts:
+              persistent_decode: bool = True, kquant_layout: str = "reference") -> LoadOpts:
+    """ifx_load_opts; kquant_layout "reference" reads type ids and Q4_K/Q6_K
+    bytes as the reference does, "ggml" reads a file written by llama.cpp."""
     o = LoadOpts()
     lib.ifx_load_opts_default(C.byref(o))
     o.device = device
@@ -41,6 +43,9 @@ def load_opts(device: int = 0, rope_compat: bool = True, use_graphs: bool = True
     o.tp_rank = tp_rank
     o.nccl_comm = nccl_comm
     o.persistent_decode = 1 if persistent_decode else 0
+    if kquant_layout not in ("reference", "ggml"):
+        raise ValueError(f"kquant_layout must be 'reference' or 'ggml', not {kquant_layout!r}")
+    o.kquant_layout = 1 if kquant_layout == "ggml" else 0
     return o
 
 
