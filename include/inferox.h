@@ -193,6 +193,19 @@ ifx_status ifx_prefill_seq(ifx_model *m, ifx_kv_batch *kb, int seq,
 ifx_status ifx_decode_step_batch(ifx_model *m, ifx_kv_batch *kb,
                                  const uint32_t *tokens, float *logits_host,
                                  uint32_t *argmax_host);
+/* No reference counterpart (its KvCache holds one sequence, cache.rs:7-13):
+ * one decode step of the n distinct sequences seqs[0..n) only, for a
+ * serving loop whose requests come and go (continuous batching); the other
+ * sequences keep their caches and lengths. Row i of logits_host [n, vocab]
+ * and argmax_host [n] (both nullable) belongs to seqs[i]. */
+ifx_status ifx_decode_step_batch_seqs(ifx_model *m, ifx_kv_batch *kb,
+                                      const int *seqs, int n,
+                                      const uint32_t *tokens,
+                                      float *logits_host,
+                                      uint32_t *argmax_host);
+/* KvCache::clear (cache.rs:26-28) of sequence `seq` alone, so a new request
+ * can take its place in the batch. */
+ifx_status ifx_kv_batch_reset(ifx_model *m, ifx_kv_batch *kb, int seq);
 /* n_steps greedy steps of every sequence, each step's argmax fed to the next
  * on the device; out_tokens [n_steps, batch] and device_ms are nullable. */
 ifx_status ifx_decode_greedy_batch(ifx_model *m, ifx_kv_batch *kb,

@@ -114,6 +114,8 @@ def _load():
         "ifx_kv_batch_len": (st, [vp, C.c_int, C.POINTER(sz)]),
         "ifx_prefill_seq": (st, [vp, vp, C.c_int, u32p, sz, fp, C.c_int]),
         "ifx_decode_step_batch": (st, [vp, vp, u32p, fp, u32p]),
+        "ifx_decode_step_batch_seqs": (st, [vp, vp, C.POINTER(C.c_int), C.c_int, u32p, fp, u32p]),
+        "ifx_kv_batch_reset": (st, [vp, vp, C.c_int]),
         "ifx_decode_greedy_batch": (st, [vp, vp, u32p, sz, u32p, fp]),
         "ifx_op_dequantize": (st, [C.c_int, vp, sz, vp, sz, vp]),
         "ifx_op_matmul": (st, [vp, vp, vp, sz, sz, sz, vp]),

@@ -43,7 +43,8 @@ __global__ void __launch_bounds__(kAttnThreads) decode_attn_kernel(const __grid_
   const int grp = a.H / a.G, hd = a.hd, NS = a.ns;
   // this sequence's slices of the inputs, caches, partials and output
   const float *qkv = a.qkv + (size_t)b * a.qkv_stride;
-  __half *kcb = a.kc + (size_t)b * a.kv_seq_stride, *vcb = a.vc + (size_t)b * a.kv_seq_stride;
+  const int sq = a.slot ? a.slot[b] : b;  // the sequence whose cache this row extends
+  __half *kcb = a.kc + (size_t)sq * a.kv_seq_stride, *vcb = a.vc + (size_t)sq * a.kv_seq_stride;
   float *part_o = a.part_o + (size_t)b * a.G * NS * grp * hd;
   float2 *part_ml = a.part_ml + (size_t)b * a.G * NS * grp;
   int *counters = a.counters + (size_t)b * a.G;
@@ -66,7 +67,7 @@ __global__ void __launch_bounds__(kAttnThreads) decode_attn_kernel(const __grid_
   // written by kernels that completed before the previous kernel in the
   // stream started its main phase, so this CTA's chunk can be fetched while
   // the QKV GEMV is still draining.
-  const int pos = a.pos[b];
+  const int pos = a.pos[sq];
   const int len = pos + 1;
   const int chunk = (len + NS - 1) / NS;
   const int t0 = s * chunk, t1 = min(len, t0 + chunk);

@@ -24,6 +24,9 @@ struct DecodeAttnArgs {
   // own partials, counters and output row (attn_out + b * H * hd)
   int64_t qkv_stride = 0, kv_seq_stride = 0;
   int batch = 1;
+  // when set, row b's cache and position are those of sequence slot[b]
+  // (a step over a subset of a batch's sequences); workspace rows stay b
+  const int *slot = nullptr;
 };
 
 ifx_status decode_attention(const DecodeAttnArgs &a, cudaStream_t st, bool pdl);

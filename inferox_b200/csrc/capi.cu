@@ -260,6 +260,21 @@ ifx_status ifx_decode_step_batch(ifx_model *m, ifx_kv_batch *kb, const uint32_t 
   IFX_GUARD({ return m->m.decode_batch(kb->kb, tokens, logits_host, argmax_host); })
 }
 
+ifx_status ifx_decode_step_batch_seqs(ifx_model *m, ifx_kv_batch *kb, const int *seqs, int n,
+                                      const uint32_t *tokens, float *logits_host,
+                                      uint32_t *argmax_host) {
+  if (!m || !kb || !seqs || !tokens)
+    return fail(IFX_ERR_INVALID_ARGUMENT, "decode_step_batch_seqs: null argument");
+  if (kb->kb.m != &m->m) return fail(IFX_ERR_INVALID_ARGUMENT, "decode_step_batch_seqs: batch belongs to another model");
+  IFX_GUARD({ return m->m.decode_batch_seqs(kb->kb, seqs, n, tokens, logits_host, argmax_host); })
+}
+
+ifx_status ifx_kv_batch_reset(ifx_model *m, ifx_kv_batch *kb, int seq) {
+  if (!m || !kb) return fail(IFX_ERR_INVALID_ARGUMENT, "kv_batch_reset: null argument");
+  if (kb->kb.m != &m->m) return fail(IFX_ERR_INVALID_ARGUMENT, "kv_batch_reset: batch belongs to another model");
+  IFX_GUARD({ return m->m.reset_seq(kb->kb, seq); })
+}
+
 ifx_status ifx_decode_greedy_batch(ifx_model *m, ifx_kv_batch *kb, const uint32_t *tokens,
                                    size_t n_steps, uint32_t *out_tokens, float *device_ms) {
   if (!m || !kb || !tokens) return fail(IFX_ERR_INVALID_ARGUMENT, "decode_greedy_batch: null argument");

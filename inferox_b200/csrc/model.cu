@@ -151,11 +151,11 @@ __global__ void argmax_rows_kernel(const float *x, int n, unsigned long long *ke
 
 // The step's tokens from the row keys; every sequence's position advances.
 __global__ void argmax_keys_kernel(const unsigned long long *keys, int rows, uint32_t *out,
-                                   int *pos) {
+                                   int *pos, const int *slot) {
   const int i = threadIdx.x;
   if (i < rows) {
     out[i] = (uint32_t)(keys[i] & 0xffffffffull);
-    pos[i] += 1;
+    pos[slot ? slot[i] : i] += 1;
   }
 }
 
@@ -524,6 +524,7 @@ ifx_status KvBatch::create(Model *model, size_t max_seq_len, int nseq) {
   IFX_TRY(dalloc(&ids, (size_t)nseq));
   IFX_TRY(dalloc(&out, (size_t)nseq));
   IFX_TRY(dalloc(&keys, (size_t)nseq));
+  IFX_TRY(dalloc(&slots, (size_t)nseq));
   const size_t kmax = std::max<size_t>(std::max<size_t>(D, F), (size_t)H * hd);
   IFX_CUDA(cudaMalloc(&xf, gemm_small_xfrag_bytes(nseq, (int64_t)kmax)));
   len.assign((size_t)nseq, 0);
@@ -534,7 +535,8 @@ KvBatch::~KvBatch() {
   if (dev >= 0) cudaSetDevice(dev);
   for (void *p : {(void *)k, (void *)v, (void *)pos, (void *)x, (void *)qkv, (void *)attn,
                   (void *)gate, (void *)up, (void *)logits, (void *)part_o, (void *)part_ml,
-                  (void *)counters, (void *)xf, (void *)ids, (void *)out, (void *)keys})
+                  (void *)counters, (void *)xf, (void *)ids, (void *)out, (void *)keys,
+                  (void *)slots})
     if (p) cudaFree(p);
 }
 
@@ -837,9 +839,9 @@ ifx_status Model::prefill_seq(KvBatch &kb, int seq, const uint32_t *ids, size_t 
 // results added atomically, so outputs start zeroed and the residual
 // projections add straight into x), attention runs per (sequence, kv head,
 // split) at each sequence's own position, then the logits and their argmax.
-ifx_status Model::enqueue_decode_batch(KvBatch &kb, cudaStream_t st) {
+ifx_status Model::enqueue_decode_batch(KvBatch &kb, cudaStream_t st, int n, const int *slot_dev) {
   const ifx_config &c = cfg;
-  const int B = kb.batch, D = (int)c.hidden_size, H = (int)Hl, G = (int)Gl, hd = (int)c.head_dim;
+  const int B = n < 0 ? kb.batch : n, D = (int)c.hidden_size, H = (int)Hl, G = (int)Gl, hd = (int)c.head_dim;
   const int F = (int)Fl, V = (int)c.vocab_size, Hh = H * hd;
   const int64_t qkvw = (int64_t)(H + 2 * G) * hd;
   const float eps = c.norm_eps;
@@ -873,6 +875,7 @@ ifx_status Model::enqueue_decode_batch(KvBatch &kb, cudaStream_t st) {
     a.rope_base = c.rope_base;
     a.err = err;
     a.batch = B;
+    a.slot = slot_dev;
     IFX_TRY(decode_attention(a, st, false));
     IFX_TRY(gemm_small_stage_x(kb.attn, nullptr, nullptr, 0.f, GX_PLAIN, B, Hh, kb.xf, st));
     IFX_TRY(gemm_small_run(L.wo, kb.xf, B, kb.x, D, err, st));  // x += attn Wo^T
@@ -889,7 +892,7 @@ ifx_status Model::enqueue_decode_batch(KvBatch &kb, cudaStream_t st) {
   IFX_TRY(gemm_small_run(out_w, kb.xf, B, kb.logits, V, err, st));
   IFX_CUDA(cudaMemsetAsync(kb.keys, 0, sizeof(unsigned long long) * (size_t)B, st));
   argmax_rows_kernel<<<dim3((unsigned)B, kArgmaxParts), 256, 0, st>>>(kb.logits, V, kb.keys);
-  argmax_keys_kernel<<<1, 32, 0, st>>>(kb.keys, B, kb.out, kb.pos);
+  argmax_keys_kernel<<<1, 32, 0, st>>>(kb.keys, B, kb.out, kb.pos, slot_dev);
   IFX_CUDA(cudaGetLastError());
   return IFX_OK;
 }
@@ -915,6 +918,47 @@ ifx_status Model::decode_batch(KvBatch &kb, const uint32_t *tokens, float *logit
   IFX_CUDA(cudaStreamSynchronize(st));
   for (auto &n : kb.len) n += 1;
   return check_err();
+}
+
+// One decode step of the n distinct sequences seqs[0..n) of the batch (a
+// serving loop whose requests come and go: the others keep their caches and
+// positions). Row i of logits_host [n, vocab] / argmax_host [n] is seqs[i].
+ifx_status Model::decode_batch_seqs(KvBatch &kb, const int *seqs, int n, const uint32_t *tokens,
+                                    float *logits_host, uint32_t *argmax_host) {
+  if (n < 1 || n > kb.batch)
+    return fail(IFX_ERR_INVALID_ARGUMENT, "batch step: 1 to batch sequences");
+  std::vector<char> seen((size_t)kb.batch, 0);
+  for (int i = 0; i < n; ++i) {
+    if (seqs[i] < 0 || seqs[i] >= kb.batch) return fail(IFX_ERR_INVALID_ARGUMENT, "batch: no such sequence");
+    if (seen[(size_t)seqs[i]]++) return fail(IFX_ERR_INVALID_ARGUMENT, "batch step: a sequence listed twice");
+    if (tokens[i] >= cfg.vocab_size)
+      return fail(IFX_ERR_INVALID_TENSOR_INDEX,
+                  "tensor index out of bounds: " + std::to_string(tokens[i]));
+    if (kb.len[(size_t)seqs[i]] >= kb.max_seq) return fail(IFX_ERR_INVALID_TENSOR_INDEX, "KV cache is full");
+  }
+  IFX_CUDA(cudaSetDevice(device));
+  cudaStream_t st = stream;
+  IFX_CUDA(cudaMemcpyAsync(kb.ids, tokens, sizeof(uint32_t) * n, cudaMemcpyHostToDevice, st));
+  IFX_CUDA(cudaMemcpyAsync(kb.slots, seqs, sizeof(int) * n, cudaMemcpyHostToDevice, st));
+  IFX_TRY(enqueue_decode_batch(kb, st, n, kb.slots));
+  if (logits_host)
+    IFX_CUDA(cudaMemcpyAsync(logits_host, kb.logits, sizeof(float) * n * cfg.vocab_size,
+                             cudaMemcpyDeviceToHost, st));
+  if (argmax_host)
+    IFX_CUDA(cudaMemcpyAsync(argmax_host, kb.out, sizeof(uint32_t) * n, cudaMemcpyDeviceToHost, st));
+  IFX_CUDA(cudaStreamSynchronize(st));
+  for (int i = 0; i < n; ++i) kb.len[(size_t)seqs[i]] += 1;
+  return check_err();
+}
+
+// KvCache::clear (cache.rs:26-28) for one sequence of the batch.
+ifx_status Model::reset_seq(KvBatch &kb, int seq) {
+  if (seq < 0 || seq >= kb.batch) return fail(IFX_ERR_INVALID_ARGUMENT, "batch: no such sequence");
+  IFX_CUDA(cudaSetDevice(device));
+  IFX_CUDA(cudaMemsetAsync(kb.pos + seq, 0, sizeof(int), stream));
+  IFX_CUDA(cudaStreamSynchronize(stream));
+  kb.len[(size_t)seq] = 0;
+  return IFX_OK;
 }
 
 // n greedy steps of every sequence, each step's argmax fed to the next on

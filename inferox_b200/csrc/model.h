@@ -58,6 +58,7 @@ struct KvBatch {
   int *counters = nullptr;
   uint8_t *xf = nullptr;
   uint32_t *ids = nullptr, *out = nullptr;  // the step's input tokens and argmax
+  int *slots = nullptr;                     // sequences of a subset step
   unsigned long long *keys = nullptr;       // per-sequence argmax keys
   int dev = -1;                             // device of the allocations
   ifx_status create(Model *model, size_t max_seq_len, int nseq);
@@ -126,7 +127,13 @@ struct Model {
                           uint64_t *bytes);
   ifx_status prefill_seq(KvBatch &kb, int seq, const uint32_t *ids, size_t n, float *logits_host,
                          int last_row_only);
-  ifx_status enqueue_decode_batch(KvBatch &kb, cudaStream_t st);
+  // n rows (all kb.batch sequences when n < 0); row i extends sequence
+  // slot_dev[i] when slot_dev is set (device array), else sequence i
+  ifx_status enqueue_decode_batch(KvBatch &kb, cudaStream_t st, int n = -1,
+                                  const int *slot_dev = nullptr);
+  ifx_status decode_batch_seqs(KvBatch &kb, const int *seqs, int n, const uint32_t *tokens,
+                               float *logits_host, uint32_t *argmax_host);
+  ifx_status reset_seq(KvBatch &kb, int seq);
   ifx_status decode_batch(KvBatch &kb, const uint32_t *tokens, float *logits_host,
                           uint32_t *argmax_host);
   ifx_status decode_greedy_batch(KvBatch &kb, const uint32_t *tokens, size_t n, uint32_t *out,

@@ -221,6 +221,26 @@ class KvBatch:
                                         _u32(amax)), "decode_step_batch")
         return (logits.reshape(self.batch, m.vocab) if want_logits else None), amax
 
+    def decode_step_seqs(self, seqs, tokens, want_logits: bool = True):
+        """One step of the listed (distinct) sequences only; row i of the
+        result (logits [n, vocab] or None, argmax [n]) belongs to seqs[i]."""
+        m = self._model
+        s = np.ascontiguousarray(seqs, np.int32)
+        t = np.ascontiguousarray(tokens, np.uint32)
+        if s.size != t.size:
+            raise ValueError("one token per listed sequence")
+        logits = np.empty(max(1, s.size) * m.vocab, np.float32) if want_logits else None
+        amax = np.empty(max(1, s.size), np.uint32)
+        check(lib.ifx_decode_step_batch_seqs(m._h, self._h, s.ctypes.data_as(C.POINTER(C.c_int)),
+                                             int(s.size), _u32(t),
+                                             _f32(logits) if want_logits else None, _u32(amax)),
+              "decode_step_batch_seqs")
+        return (logits[: s.size * m.vocab].reshape(s.size, m.vocab) if want_logits else None), amax[: s.size]
+
+    def reset(self, seq: int) -> None:
+        """KvCache::clear of one sequence, so a new request can take its place."""
+        check(lib.ifx_kv_batch_reset(self._model._h, self._h, seq), "kv_batch_reset")
+
     def decode_greedy(self, tokens, n_steps: int, timed: bool = False):
         """n_steps greedy steps of every sequence: (tokens [n_steps, batch], device_ms)."""
         m = self._model

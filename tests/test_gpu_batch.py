@@ -93,3 +93,48 @@ def test_batched_decode_errors():
     with pytest.raises(IfxError) as e:
         kb.decode_step([1, 2])
     assert e.value.name == "InvalidTensorIndex"
+
+
+def test_subset_steps_and_slot_reuse():
+    """Continuous batching: steps over changing subsets of the sequences, and a
+    slot reset and refilled by a new request, each sequence against the
+    oracle's single-sequence decode."""
+    g = _model("small_q4km")
+    m, o = Model.from_bytes(g), R.Model(g)
+    V, L = int(m.config.vocab_size), int(m.config.n_layers)
+    kb = m.kv_batch(4, 64)
+    okv, toks = {}, {}
+    for s in (0, 2, 3):  # slot 1 starts empty
+        p = synth.prompt_ids(V, 5 + s, seed=60 + s)
+        okv[s] = o.kv_cache(L, 64)
+        kb.prefill(s, p, True)
+        toks[s] = R.argmax(o.prefill(p, okv[s], True)[0])
+
+    def step(seqs):
+        logits, amax = kb.decode_step_seqs(seqs, [toks[s] for s in seqs])
+        for i, s in enumerate(seqs):
+            rl = o.decode_step(toks[s], okv[s])
+            assert _close(logits[i], rl), (seqs, s, float(np.max(np.abs(logits[i] - rl))))
+            assert int(amax[i]) == R.argmax(logits[i])
+            toks[s] = R.argmax(rl)
+
+    for seqs in ([2, 0], [3], [0, 3, 2], [2, 0]):
+        step(seqs)
+    assert [kb.len(s) for s in range(4)] == [5 + 3, 0, 7 + 3, 8 + 2]
+    kb.reset(0)  # a finished request leaves; a new one takes its slot
+    assert kb.len(0) == 0
+    p = synth.prompt_ids(V, 6, seed=99)
+    okv[0] = o.kv_cache(L, 64)
+    kb.prefill(0, p, True)
+    toks[0] = R.argmax(o.prefill(p, okv[0], True)[0])
+    okv[1], toks[1] = o.kv_cache(L, 64), 5  # slot 1 decodes from an empty cache
+    step([1, 0])
+    step([3, 1, 2, 0])
+    logits, _ = kb.decode_step([toks[s] for s in range(4)])  # the whole batch again
+    for s in range(4):
+        assert _close(logits[s], o.decode_step(toks[s], okv[s]))
+    for bad in ([1, 1], [4], []):
+        with pytest.raises(IfxError):
+            kb.decode_step_seqs(bad, [3] * len(bad))
+    with pytest.raises(IfxError):
+        kb.reset(4)
