@@ -26,6 +26,7 @@
 #include "gemm.cuh"
 #include "gemv.cuh"
 #include "kquant.h"
+#include "nvtx3/nvToolsExt.h"
 #include "gguf.h"
 #include "model.h"
 #include "tp.h"
@@ -201,6 +202,15 @@ ifx_status dalloc(T **p, size_t n) {
 
 }  // namespace
 
+// An NVTX range over a host entry point (named "ifx:<what>"), so a timeline
+// tool shows prefill, decode steps and loops; free when no tool listens.
+struct NvtxRange {
+  explicit NvtxRange(const char *name) { nvtxRangePushA(name); }
+  ~NvtxRange() { nvtxRangePop(); }
+  NvtxRange(const NvtxRange &) = delete;
+  NvtxRange &operator=(const NvtxRange &) = delete;
+};
+
 // ------------------------------------------------------------------ load --
 // A tensor's bytes in the reference's block order: llama.cpp-ordered Q4_K /
 // Q6_K blocks (ggml = true) are permuted into `conv` and *type becomes the
@@ -263,6 +273,7 @@ static ifx_status upload_norm(const GgufFile &f, const uint8_t *bytes, size_t le
 }
 
 ifx_status Model::load(const uint8_t *bytes, size_t len, const ifx_load_opts &o) {
+  NvtxRange nvtx_("ifx:load");
   opts = o;
   tp = opts.tp_size;
   rank = opts.tp_rank;
@@ -751,6 +762,7 @@ ifx_status Model::check_err() {
 }
 
 ifx_status Model::decode_step(KvCache &kv, uint32_t token, float *logits_host) {
+  NvtxRange nvtx_("ifx:decode_step");
   if (token >= cfg.vocab_size)
     return fail(IFX_ERR_INVALID_TENSOR_INDEX, "tensor index out of bounds: " + std::to_string(token));
   if (kv.len >= kv.max_seq) return fail(IFX_ERR_INVALID_TENSOR_INDEX, "KV cache is full");
@@ -899,6 +911,7 @@ ifx_status Model::enqueue_decode_batch(KvBatch &kb, cudaStream_t st, int n, cons
 
 ifx_status Model::decode_batch(KvBatch &kb, const uint32_t *tokens, float *logits_host,
                                uint32_t *argmax_host) {
+  NvtxRange nvtx_("ifx:decode_step_batch");
   for (int b = 0; b < kb.batch; ++b) {
     if (tokens[b] >= cfg.vocab_size)
       return fail(IFX_ERR_INVALID_TENSOR_INDEX,
@@ -925,6 +938,7 @@ ifx_status Model::decode_batch(KvBatch &kb, const uint32_t *tokens, float *logit
 // positions). Row i of logits_host [n, vocab] / argmax_host [n] is seqs[i].
 ifx_status Model::decode_batch_seqs(KvBatch &kb, const int *seqs, int n, const uint32_t *tokens,
                                     float *logits_host, uint32_t *argmax_host) {
+  NvtxRange nvtx_("ifx:decode_step_batch_seqs");
   if (n < 1 || n > kb.batch)
     return fail(IFX_ERR_INVALID_ARGUMENT, "batch step: 1 to batch sequences");
   std::vector<char> seen((size_t)kb.batch, 0);
@@ -965,6 +979,7 @@ ifx_status Model::reset_seq(KvBatch &kb, int seq) {
 // the device; out[i * batch + b] is sequence b's token of step i.
 ifx_status Model::decode_greedy_batch(KvBatch &kb, const uint32_t *tokens, size_t n,
                                       uint32_t *out, float *device_ms) {
+  NvtxRange nvtx_("ifx:decode_greedy_batch");
   for (int b = 0; b < kb.batch; ++b) {
     if (tokens[b] >= cfg.vocab_size)
       return fail(IFX_ERR_INVALID_TENSOR_INDEX,
@@ -1011,6 +1026,7 @@ ifx_status Model::decode_greedy_batch(KvBatch &kb, const uint32_t *tokens, size_
 // cache) and forward (kvp null: full attention, no cache).
 ifx_status Model::run_prompt(KvCache *kvp, const uint32_t *ids, size_t n, float *logits_host,
                              int last_row_only) {
+  NvtxRange nvtx_("ifx:prompt");
   const ifx_config &c = cfg;
   for (size_t i = 0; i < n; ++i)
     if (ids[i] >= c.vocab_size)  // forward.rs:453-455, 501-503
@@ -1150,6 +1166,7 @@ ifx_status Model::generate(KvCache &kv, const uint32_t *prompt, size_t n_prompt,
 
 ifx_status Model::decode_greedy(KvCache &kv, uint32_t token, size_t n, uint32_t *out,
                                 float *device_ms) {
+  NvtxRange nvtx_("ifx:decode_greedy");
   if (token >= cfg.vocab_size)
     return fail(IFX_ERR_INVALID_TENSOR_INDEX, "tensor index out of bounds: " + std::to_string(token));
   if (kv.len + n > kv.max_seq) return fail(IFX_ERR_INVALID_TENSOR_INDEX, "KV cache is full");
