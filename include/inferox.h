@@ -101,6 +101,12 @@ typedef struct ifx_load_opts {
                         (types.rs:70-100, dequant.rs:123-199);
                         IFX_KQUANT_GGML: a file written by llama.cpp (ggml
                         ids, ggml block orders, int8 Q6_K scales) */
+  int tp_timeout_ms; /* tensor parallel: longest wait for a call's
+                        collectives (0: 300000). When a peer rank stops, the
+                        call returns IFX_ERR_TIMEOUT (or IFX_ERR_NCCL on an
+                        NCCL error) after aborting the communicator, and the
+                        model refuses further calls: free it, make a new
+                        communicator and load again. */
 } ifx_load_opts;
 
 enum { IFX_KQUANT_REFERENCE = 0, IFX_KQUANT_GGML = 1 };

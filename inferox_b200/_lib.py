@@ -50,7 +50,7 @@ class LoadOpts(C.Structure):
     _fields_ = [
         ("device", C.c_int), ("tp_size", C.c_int), ("tp_rank", C.c_int),
         ("nccl_comm", C.c_void_p), ("rope_compat", C.c_int), ("use_graphs", C.c_int),
-        ("persistent_decode", C.c_int), ("kquant_layout", C.c_int),
+        ("persistent_decode", C.c_int), ("kquant_layout", C.c_int), ("tp_timeout_ms", C.c_int),
     ]
 
 

@@ -763,6 +763,7 @@ ifx_status Model::check_err() {
 
 ifx_status Model::decode_step(KvCache &kv, uint32_t token, float *logits_host) {
   NvtxRange nvtx_("ifx:decode_step");
+  IFX_TRY(tp_usable());
   if (token >= cfg.vocab_size)
     return fail(IFX_ERR_INVALID_TENSOR_INDEX, "tensor index out of bounds: " + std::to_string(token));
   if (kv.len >= kv.max_seq) return fail(IFX_ERR_INVALID_TENSOR_INDEX, "KV cache is full");
@@ -773,7 +774,7 @@ ifx_status Model::decode_step(KvCache &kv, uint32_t token, float *logits_host) {
   if (logits_host)
     IFX_CUDA(cudaMemcpyAsync(logits_host, logits, cfg.vocab_size * sizeof(float),
                              cudaMemcpyDeviceToHost, stream));
-  IFX_CUDA(cudaStreamSynchronize(stream));
+  IFX_TRY(step_sync(stream));
   kv.len += 1;
   return check_err();
 }
@@ -965,6 +966,24 @@ ifx_status Model::decode_batch_seqs(KvBatch &kb, const int *seqs, int n, const u
   return check_err();
 }
 
+ifx_status Model::step_sync(cudaStream_t st) {
+  if (tp <= 1) {
+    IFX_CUDA(cudaStreamSynchronize(st));
+    return IFX_OK;
+  }
+  const double ms = opts.tp_timeout_ms > 0 ? (double)opts.tp_timeout_ms : 300000.0;
+  const ifx_status s = tp_wait(st, (ncclComm_t)comm, nccl, ms);
+  if (s == IFX_ERR_NCCL || s == IFX_ERR_TIMEOUT) comm_aborted = true;
+  return s;
+}
+
+ifx_status Model::tp_usable() const {
+  if (!comm_aborted) return IFX_OK;
+  return fail(IFX_ERR_NCCL,
+              "tensor parallel: the communicator was aborted after a failed call; free the model, "
+              "make a new communicator and load again");
+}
+
 // KvCache::clear (cache.rs:26-28) for one sequence of the batch.
 ifx_status Model::reset_seq(KvBatch &kb, int seq) {
   if (seq < 0 || seq >= kb.batch) return fail(IFX_ERR_INVALID_ARGUMENT, "batch: no such sequence");
@@ -1027,6 +1046,7 @@ ifx_status Model::decode_greedy_batch(KvBatch &kb, const uint32_t *tokens, size_
 ifx_status Model::run_prompt(KvCache *kvp, const uint32_t *ids, size_t n, float *logits_host,
                              int last_row_only) {
   NvtxRange nvtx_("ifx:prompt");
+  IFX_TRY(tp_usable());
   const ifx_config &c = cfg;
   for (size_t i = 0; i < n; ++i)
     if (ids[i] >= c.vocab_size)  // forward.rs:453-455, 501-503
@@ -1139,7 +1159,7 @@ ifx_status Model::run_prompt(KvCache *kvp, const uint32_t *ids, size_t n, float 
     IFX_CUDA(cudaMemcpyAsync(logits, logits_all + (n - 1) * c.vocab_size,
                              c.vocab_size * sizeof(float), cudaMemcpyDeviceToDevice, st));
   }
-  IFX_CUDA(cudaStreamSynchronize(st));
+  IFX_TRY(step_sync(st));
   if (kvp) kvp->len += n;
   return check_err();
 }
@@ -1159,7 +1179,7 @@ ifx_status Model::generate(KvCache &kv, const uint32_t *prompt, size_t n_prompt,
   for (size_t i = 0; i < max_tokens; ++i) IFX_TRY(run_decode(kv));
   if (max_tokens)
     IFX_CUDA(cudaMemcpyAsync(out, kv.tokens, max_tokens * sizeof(uint32_t), cudaMemcpyDeviceToHost, st));
-  IFX_CUDA(cudaStreamSynchronize(st));
+  IFX_TRY(step_sync(st));
   kv.len += max_tokens;
   return check_err();
 }
@@ -1167,6 +1187,7 @@ ifx_status Model::generate(KvCache &kv, const uint32_t *prompt, size_t n_prompt,
 ifx_status Model::decode_greedy(KvCache &kv, uint32_t token, size_t n, uint32_t *out,
                                 float *device_ms) {
   NvtxRange nvtx_("ifx:decode_greedy");
+  IFX_TRY(tp_usable());
   if (token >= cfg.vocab_size)
     return fail(IFX_ERR_INVALID_TENSOR_INDEX, "tensor index out of bounds: " + std::to_string(token));
   if (kv.len + n > kv.max_seq) return fail(IFX_ERR_INVALID_TENSOR_INDEX, "KV cache is full");
@@ -1184,7 +1205,7 @@ ifx_status Model::decode_greedy(KvCache &kv, uint32_t token, size_t n, uint32_t 
   if (device_ms) IFX_CUDA(cudaEventRecord(e1, st));
   if (out && n)
     IFX_CUDA(cudaMemcpyAsync(out, kv.tokens, n * sizeof(uint32_t), cudaMemcpyDeviceToHost, st));
-  IFX_CUDA(cudaStreamSynchronize(st));
+  IFX_TRY(step_sync(st));
   if (device_ms) {
     IFX_CUDA(cudaEventElapsedTime(device_ms, e0, e1));
     cudaEventDestroy(e0);

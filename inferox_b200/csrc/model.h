@@ -134,6 +134,11 @@ struct Model {
   ifx_status decode_batch_seqs(KvBatch &kb, const int *seqs, int n, const uint32_t *tokens,
                                float *logits_host, uint32_t *argmax_host);
   ifx_status reset_seq(KvBatch &kb, int seq);
+  // the end of a call's device work: a bounded wait that aborts the
+  // communicator under tensor parallelism (tp_wait), else a stream sync
+  ifx_status step_sync(cudaStream_t st);
+  ifx_status tp_usable() const;
+  bool comm_aborted = false;
   ifx_status decode_batch(KvBatch &kb, const uint32_t *tokens, float *logits_host,
                           uint32_t *argmax_host);
   ifx_status decode_greedy_batch(KvBatch &kb, const uint32_t *tokens, size_t n, uint32_t *out,

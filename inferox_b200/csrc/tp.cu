@@ -5,8 +5,12 @@
 #include <mutex>
 #include <string>
 
+#include <chrono>
+#include <thread>
+
 #include "quant.cuh"
 #include "tp.h"
+#include "watchdog.h"
 
 namespace ifx {
 
@@ -33,7 +37,8 @@ void resolve() {
   NcclApi a{};
   if (!(sym(h, "ncclGetUniqueId", &a.GetUniqueId) && sym(h, "ncclCommInitRank", &a.CommInitRank) &&
         sym(h, "ncclCommDestroy", &a.CommDestroy) && sym(h, "ncclAllReduce", &a.AllReduce) &&
-        sym(h, "ncclAllGather", &a.AllGather) && sym(h, "ncclGetErrorString", &a.GetErrorString))) {
+        sym(h, "ncclAllGather", &a.AllGather) && sym(h, "ncclGetErrorString", &a.GetErrorString) &&
+        sym(h, "ncclCommGetAsyncError", &a.CommGetAsyncError) && sym(h, "ncclCommAbort", &a.CommAbort))) {
     g_nccl_err = "libnccl.so.2 lacks an entry point the tensor-parallel path needs";
     return;
   }
@@ -50,6 +55,52 @@ ifx_status nccl_api(const NcclApi **out) {
 
 ifx_status nccl_fail(const NcclApi *api, ncclResult_t r, const char *what) {
   return fail(IFX_ERR_NCCL, std::string(what) + ": " + (api ? api->GetErrorString(r) : "error"));
+}
+
+ifx_status tp_wait(cudaStream_t st, ncclComm_t comm, const NcclApi *api, double timeout_ms) {
+  using clk = std::chrono::steady_clock;
+  cudaError_t dev_err = cudaSuccess;
+  ncclResult_t comm_err = ncclSuccess;
+  auto query = [&]() {
+    const cudaError_t e = cudaStreamQuery(st);
+    if (e == cudaSuccess) return 0;
+    if (e == cudaErrorNotReady) return 1;
+    dev_err = e;
+    return -1;
+  };
+  auto comm_error = [&]() {
+    ncclResult_t r = ncclSuccess;
+    if (api->CommGetAsyncError(comm, &r) != ncclSuccess) return false;
+    if (r == ncclSuccess || r == ncclInProgress) return false;
+    comm_err = r;
+    return true;
+  };
+  auto abort = [&]() { api->CommAbort(comm); };
+  auto now_ms = []() {
+    return std::chrono::duration<double, std::milli>(clk::now().time_since_epoch()).count();
+  };
+  // spin (yielding) through the first 50 ms, the length of any normal step,
+  // then poll every 200 us
+  const double t_spin = now_ms() + 50.0;
+  auto pause = [&]() {
+    if (now_ms() < t_spin) std::this_thread::yield();
+    else std::this_thread::sleep_for(std::chrono::microseconds(200));
+  };
+  const WaitEnd end = bounded_wait(query, comm_error, abort, now_ms, pause, timeout_ms);
+  switch (end) {
+    case WaitEnd::Done: return IFX_OK;
+    case WaitEnd::DeviceError:
+      return fail(IFX_ERR_CUDA, std::string("tensor-parallel step: ") + cudaGetErrorString(dev_err));
+    case WaitEnd::CommError:
+      return fail(IFX_ERR_NCCL, std::string("tensor-parallel step: a collective failed (") +
+                                    api->GetErrorString(comm_err) +
+                                    "); the communicator was aborted");
+    case WaitEnd::TimedOut:
+      break;
+  }
+  return fail(IFX_ERR_TIMEOUT, "tensor-parallel step: collectives did not finish within " +
+                                   std::to_string((long long)timeout_ms) +
+                                   " ms (a peer rank stopped?); the communicator was aborted");
 }
 
 ifx_status tp_shard(int type, const uint8_t *bytes, size_t nbytes, uint64_t rows, uint64_t cols,

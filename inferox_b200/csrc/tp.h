@@ -26,11 +26,19 @@ struct NcclApi {
   ncclResult_t (*AllGather)(const void *, void *, size_t, ncclDataType_t, ncclComm_t,
                             cudaStream_t);
   const char *(*GetErrorString)(ncclResult_t);
+  ncclResult_t (*CommGetAsyncError)(ncclComm_t, ncclResult_t *);
+  ncclResult_t (*CommAbort)(ncclComm_t);
 };
 
 // Resolves the entry points once per process.
 ifx_status nccl_api(const NcclApi **out);
 ifx_status nccl_fail(const NcclApi *api, ncclResult_t r, const char *what);
+
+// Waits for `st` (work that includes collectives on `comm`) at most
+// timeout_ms; on an asynchronous NCCL error or at the deadline aborts `comm`
+// (its outstanding kernels end; the communicator is unusable afterwards)
+// and returns IFX_ERR_NCCL / IFX_ERR_TIMEOUT.
+ifx_status tp_wait(cudaStream_t st, ncclComm_t comm, const NcclApi *api, double timeout_ms);
 
 #define IFX_NCCL(api, call)                                           \
   do {                                                                \

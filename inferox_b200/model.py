@@ -31,7 +31,8 @@ def _f32(a):
 
 def load_opts(device: int = 0, rope_compat: bool = True, use_graphs: bool = True,
               tp_size: int = 1, tp_rank: int = 0, nccl_comm: int | None = None,
-              persistent_decode: bool = True, kquant_layout: str = "reference") -> LoadOpts:
+              persistent_decode: bool = True, kquant_layout: str = "reference",
+              tp_timeout_ms: int = 0) -> LoadOpts:
     """ifx_load_opts; kquant_layout "reference" reads type ids and Q4_K/Q6_K
     bytes as the reference does, "ggml" reads a file written by llama.cpp."""
     o = LoadOpts()
@@ -46,6 +47,7 @@ def load_opts(device: int = 0, rope_compat: bool = True, use_graphs: bool = True
     if kquant_layout not in ("reference", "ggml"):
         raise ValueError(f"kquant_layout must be 'reference' or 'ggml', not {kquant_layout!r}")
     o.kquant_layout = 1 if kquant_layout == "ggml" else 0
+    o.tp_timeout_ms = tp_timeout_ms
     return o
 
 
