@@ -414,6 +414,31 @@ ifx_status Model::load(const uint8_t *bytes, size_t len, const ifx_load_opts &o)
   p_wo.resize(cfg.n_layers);
   p_w13.resize(cfg.n_layers);
   p_w2.resize(cfg.n_layers);
+  p_qkv_more.resize(cfg.n_layers);
+  p_w13_more.resize(cfg.n_layers);
+  // the matrices of one fused site grouped by unit width: the group of the
+  // first matrix in `first`, any other group in its own plan in `more`
+  auto plan_site = [&](const QMatrix *const *mats, float *const *ys, int n, int mode,
+                       const float *xin, const float *normw, GemvPlan *first,
+                       std::vector<GemvPlan> *more) -> ifx_status {
+    std::vector<int> kcs;
+    for (int i = 0; i < n; ++i)
+      if (std::find(kcs.begin(), kcs.end(), mats[i]->L.kc) == kcs.end()) kcs.push_back(mats[i]->L.kc);
+    more->resize(kcs.size() - 1);
+    for (size_t g = 0; g < kcs.size(); ++g) {
+      const QMatrix *gm[kGemvMaxSegs];
+      float *gy[kGemvMaxSegs];
+      int gn = 0;
+      for (int i = 0; i < n; ++i)
+        if (mats[i]->L.kc == kcs[g]) {
+          gm[gn] = mats[i];
+          gy[gn++] = ys[i];
+        }
+      IFX_TRY(gemv_plan(gm, gy, gn, mode, xin, nullptr, normw, eps, err,
+                        g == 0 ? first : &(*more)[g - 1]));
+    }
+    return IFX_OK;
+  };
   for (uint64_t l = 0; l < cfg.n_layers; ++l) {
     Layer &L = layers[l];
     const QMatrix *mq[3] = {&L.wq, &L.wk, &L.wv};
@@ -427,9 +452,9 @@ ifx_status Model::load(const uint8_t *bytes, size_t len, const ifx_load_opts &o)
     float *y13[2] = {gu, gu + Fl};
     const QMatrix *m2[1] = {&L.w2};
     float *y2[1] = {acc};
-    IFX_TRY(gemv_plan(mq, yq, 3, GEMV_RMSNORM, x, nullptr, L.attn_norm, eps, err, &p_qkv[l]));
+    IFX_TRY(plan_site(mq, yq, 3, GEMV_RMSNORM, x, L.attn_norm, &p_qkv[l], &p_qkv_more[l]));
     IFX_TRY(gemv_plan(mo, yo, 1, GEMV_PLAIN, attn, nullptr, nullptr, eps, err, &p_wo[l]));
-    IFX_TRY(gemv_plan(m13, y13, 2, GEMV_RMSNORM, x, nullptr, L.ffn_norm, eps, err, &p_w13[l]));
+    IFX_TRY(plan_site(m13, y13, 2, GEMV_RMSNORM, x, L.ffn_norm, &p_w13[l], &p_w13_more[l]));
     IFX_TRY(gemv_plan(m2, y2, 1, GEMV_SWIGLU, gu, gu + Fl, nullptr, eps, err, &p_w2[l]));
     p_w13[l].args.zero_ptr = qkv;  // qkv was consumed by ATT; the next QKV refills it
     p_w13[l].args.zero_n = qkv_n;
@@ -467,6 +492,8 @@ Model::~Model() {
   if (logits_local != logits) F(logits_local);
   for (size_t l = 0; l < p_qkv.size(); ++l) {
     gemv_plan_free(&p_qkv[l]);
+    for (auto &p : p_qkv_more[l]) gemv_plan_free(&p);
+    for (auto &p : p_w13_more[l]) gemv_plan_free(&p);
     gemv_plan_free(&p_wo[l]);
     gemv_plan_free(&p_w13[l]);
     gemv_plan_free(&p_w2[l]);
@@ -567,6 +594,7 @@ ifx_status Model::enqueue_decode(KvCache &kv, cudaStream_t st) {
                   D, (const uint32_t *)next_token, x, logits_local, (int)Vl, qkv, qkv_n));
   for (uint64_t l = 0; l < c.n_layers; ++l) {
     IFX_TRY(gemv_launch(p_qkv[l], st, pdl));
+    for (const GemvPlan &p : p_qkv_more[l]) IFX_TRY(gemv_launch(p, st, pdl));
     DecodeAttnArgs a{};
     a.qkv = qkv;
     a.kc = kv.k + l * kv.per_layer;
@@ -593,12 +621,14 @@ ifx_status Model::enqueue_decode(KvCache &kv, cudaStream_t st) {
       IFX_TRY(gemv_launch(p_wo[l], st, pdl));
       IFX_TRY(tp_partial_end(D, st));
       IFX_TRY(gemv_launch(p_w13[l], st, pdl));
+      for (const GemvPlan &p : p_w13_more[l]) IFX_TRY(gemv_launch(p, st, pdl));
       IFX_TRY(tp_partial_begin(D, st));
       IFX_TRY(gemv_launch(p_w2[l], st, pdl));
       IFX_TRY(tp_partial_end(D, st));
     } else {
       IFX_TRY(gemv_launch(p_wo[l], st, pdl));
       IFX_TRY(gemv_launch(p_w13[l], st, pdl));
+      for (const GemvPlan &p : p_w13_more[l]) IFX_TRY(gemv_launch(p, st, pdl));
       IFX_TRY(gemv_launch(p_w2[l], st, pdl));
     }
   }
@@ -710,6 +740,7 @@ ifx_status Model::build_mega(KvCache &kv) {
   for (uint64_t l = 0; l < c.n_layers; ++l) {
     gemv(p_qkv[l], nullptr, 0);
     ph.back().attn_prefetch = (int)l + 1;  // this layer's K/V rows land during QKV
+    for (const GemvPlan &p : p_qkv_more[l]) gemv(p, nullptr, 0);
     MegaPhase at{};
     at.kind = PH_ATTN;
     at.at.kc = kv.k + l * kv.per_layer;
@@ -720,6 +751,7 @@ ifx_status Model::build_mega(KvCache &kv) {
     ph.push_back(at);
     gemv(p_wo[l], nullptr, 0);  // the attention phase leaves the combined heads in attn
     gemv(p_w13[l], qkv, qkv_n);  // qkv was consumed by ATTN; the next QKV refills it
+    for (const GemvPlan &p : p_w13_more[l]) gemv(p, nullptr, 0);
     gemv(p_w2[l], nullptr, 0);
   }
   gemv(p_logits, nullptr, 0);

@@ -98,6 +98,10 @@ struct Model {
   unsigned long long *amax_key = nullptr;
   int *amax_count = nullptr, *n_out = nullptr;
   std::vector<GemvPlan> p_qkv, p_wo, p_w13, p_w2;
+  // matrices of a fused site whose unit width differs from the first's (a
+  // file that mixes Q8_0 with 256-column types in Q/K/V or gate/up): their
+  // own plans, run right after the site's plan; empty for usual files
+  std::vector<std::vector<GemvPlan>> p_qkv_more, p_w13_more;
   GemvPlan p_logits;
   uint64_t decode_bytes = 0;
   // prefill workspace

@@ -4,7 +4,9 @@ of both signs) loaded with kquant_layout="ggml", against the CPU oracle.
 The file is built here: Q4_K weights quantised by the library and rewritten
 in ggml's nibble order, Q6_K weights from a quantiser that gives each
 16-element group a scale of random sign (as llama.cpp's own quantiser
-does), Q8_0 under ggml's id 8. The oracle runs the same weights decoded by
+does), Q8_0 under ggml's id 8 for ffn_up beside a Q4_K ffn_gate (a unit
+width of 128 beside 256, so the fused gate/up GEMV runs as two plans). The
+oracle runs the same weights decoded by
 ggml's formulas (oracle/ggml_ref.py) and stored as F32 tensors, so the
 comparison covers the load-time permutation, the int8 scale reading in the
 GEMV (persistent decode kernel), the tcgen05 prefill GEMM, the small-batch
