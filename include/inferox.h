@@ -348,7 +348,7 @@ ifx_status ifx_bench_kernel(ifx_model *m, ifx_kv *kv, const char *which,
  * F32 / F16 copied. *type_out receives the reference's type id;
  * *signed_scales_out is 1 for Q6_K, whose scale bytes keep llama.cpp's int8
  * meaning (the reference would read them as u8). Host code; needs no GPU.
- * `dst` holds nbytes; it may equal `src` only for the copied types. */
+ * `dst` holds nbytes and may be `src` itself (converted in place). */
 ifx_status ifx_kquant_from_ggml(uint32_t ggml_type, const void *src,
                                 size_t nbytes, void *dst, int *type_out,
                                 int *signed_scales_out);

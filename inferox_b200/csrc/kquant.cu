@@ -86,14 +86,16 @@ ifx_status ggml_to_reference(int type, const uint8_t *src, size_t nbytes, uint8_
   if (type == IFX_TYPE_Q4_K || type == IFX_TYPE_Q6_K) {
     if (nbytes % (size_t)b.bytes)
       return fail(IFX_ERR_SHAPE, "llama.cpp K-quant data is not a whole number of blocks");
+    uint8_t blk[256];  // one source block, so dst may overlap src
     for (size_t i = 0; i < nbytes; i += (size_t)b.bytes) {
-      if (type == IFX_TYPE_Q4_K) q4k_block(src + i, dst + i);
-      else q6k_block(src + i, dst + i);
+      memcpy(blk, src + i, (size_t)b.bytes);
+      if (type == IFX_TYPE_Q4_K) q4k_block(blk, dst + i);
+      else q6k_block(blk, dst + i);
     }
     *type_out = type == IFX_TYPE_Q6_K ? kTypeQ6KS8 : type;
     return IFX_OK;
   }
-  if (src != dst && nbytes) memcpy(dst, src, nbytes);
+  if (src != dst && nbytes) memmove(dst, src, nbytes);
   *type_out = type;
   return IFX_OK;
 }

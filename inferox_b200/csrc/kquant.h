@@ -13,7 +13,7 @@ namespace ifx {
 int ggml_type_to_reference(uint32_t ggml_type);
 
 // Blocks of `type` (a reference id) written in llama.cpp's order, permuted
-// into the reference's order (src may equal dst only for Q4_0/Q8_0/F32/F16).
+// into the reference's order (dst may be src: converted in place).
 // *type_out is `type`, except kTypeQ6KS8 for Q6_K (int8 scales).
 ifx_status ggml_to_reference(int type, const uint8_t *src, size_t nbytes, uint8_t *dst,
                              int *type_out);

@@ -74,6 +74,17 @@ def test_conversion_decodes_identically(name):
     assert np.array_equal(got.view(np.uint32), want.view(np.uint32))
 
 
+def test_in_place_conversion():
+    rng = np.random.default_rng(11)
+    for gt in (12, 14, 8):
+        raw = _random_blocks(gt, 8, rng)
+        want, _, _ = convert(gt, raw)
+        buf = (C.c_uint8 * len(raw)).from_buffer_copy(raw)
+        t, s = C.c_int(), C.c_int()
+        check(_lib.lib.ifx_kquant_from_ggml(gt, buf, len(raw), buf, C.byref(t), C.byref(s)))
+        assert bytes(buf) == want
+
+
 def test_q4k_permutation_round_trip():
     rng = np.random.default_rng(9)
     ref = _random_blocks(12, 16, rng)
