@@ -259,31 +259,62 @@ def run_ours(args):
         del kb
 
     # tensor-parallel leg (several GPUs, replicas mode): one sequence over all
-    # of them, Megatron split with NCCL all-reduces, device-timed like `value`
+    # of them, Megatron split with NCCL all-reduces, device-timed like `value`.
+    # A failure here (on any rank) must not cost the replicas' line: the
+    # library's collectives are bounded (tp_timeout_ms: a stalled peer turns
+    # into an error on every rank), each rank catches its own error, and the
+    # ranks then agree through one all-reduce whether the leg succeeded.
     tpleg = None
     if world > 1 and not tp_mode and not args.no_tp_leg:
         uid = torch.zeros(128, dtype=torch.uint8, device="cuda")
         if rank == 0:
             uid.copy_(torch.frombuffer(bytearray(tp.unique_id()), dtype=torch.uint8))
         dist.broadcast(uid, 0)
-        tcomm = tp.Comm(bytes(uid.cpu().numpy()), world, rank, local)
-        mt = Model.from_bytes(g, device=local, tp_size=world, tp_rank=rank, nccl_comm=tcomm.handle)
-        kvt = mt.kv_cache(max_seq)
-        p0 = synth.prompt_ids(V, PROMPT, seq_index=0)
-        tpf = time.perf_counter()
-        f0 = int(np.argmax(mt.prefill(p0, kvt, last_row_only=True)[0]))
-        tp_prefill_s = time.perf_counter() - tpf
-        mt.decode_greedy(f0, args.warmup, kvt)
-        dist.barrier()
-        torch.cuda.synchronize()
-        _, tms = mt.decode_greedy(f0, args.steps, kvt, timed=True)
-        t = torch.tensor([tms / args.steps], device="cuda")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        tpleg = {"n_gpus": world, "tok_s": 1000.0 / float(t.item()), "ms_per_step": float(t.item()),
-                 "prefill_tok_s": PROMPT / tp_prefill_s, "scaling": "strong",
-                 "parallelism": f"tp{world} (NCCL all-reduce after Wo and W2)"}
+        tp_err, tp_ms, tp_prefill_s = "", 0.0, 0.0
+        tcomm = mt = kvt = None
+
+        def all_ok(err: str) -> bool:
+            f = torch.tensor([0.0 if err else 1.0], device="cuda")
+            dist.all_reduce(f, op=dist.ReduceOp.MIN)
+            return f.item() > 0
+
+        f0 = 0
+        try:
+            tcomm = tp.Comm(bytes(uid.cpu().numpy()), world, rank, local)
+            mt = Model.from_bytes(g, device=local, tp_size=world, tp_rank=rank,
+                                  nccl_comm=tcomm.handle, tp_timeout_ms=120000)
+            kvt = mt.kv_cache(max_seq)
+            p0 = synth.prompt_ids(V, PROMPT, seq_index=0)
+            tpf = time.perf_counter()
+            f0 = int(np.argmax(mt.prefill(p0, kvt, last_row_only=True)[0]))
+            tp_prefill_s = time.perf_counter() - tpf
+            mt.decode_greedy(f0, args.warmup, kvt)
+        except Exception as e:  # noqa: BLE001 (reported in the line, never fatal)
+            tp_err = repr(e)[:300]
+        if all_ok(tp_err):
+            dist.barrier()
+            torch.cuda.synchronize()
+            try:
+                _, tms = mt.decode_greedy(f0, args.steps, kvt, timed=True)
+                tp_ms = tms / args.steps
+            except Exception as e:  # noqa: BLE001
+                tp_err = repr(e)[:300]
+        elif not tp_err:
+            tp_err = "failed on another rank"
+        ok = torch.tensor([0.0 if tp_err else 1.0, tp_ms], device="cuda")
+        okmin = ok.clone()
+        dist.all_reduce(okmin, op=dist.ReduceOp.MIN)
+        dist.all_reduce(ok, op=dist.ReduceOp.MAX)
+        if okmin[0].item() > 0:
+            t_ms = float(ok[1].item())
+            tpleg = {"n_gpus": world, "tok_s": 1000.0 / t_ms, "ms_per_step": t_ms,
+                     "prefill_tok_s": PROMPT / tp_prefill_s, "scaling": "strong",
+                     "parallelism": f"tp{world} (NCCL all-reduce after Wo and W2)"}
+        else:
+            tpleg = {"n_gpus": world, "error": tp_err or "failed on another rank"}
         del kvt, mt  # the cache's CUDA graph holds NCCL work: release it before the comm
-        tcomm.close()
+        if tcomm is not None:
+            tcomm.close()
 
     # whole-step algorithmic bytes: every weight once + K/V at the mean context
     ctx_mean = ctx0 + args.steps / 2

@@ -106,7 +106,9 @@ typedef struct ifx_load_opts {
                         call returns IFX_ERR_TIMEOUT (or IFX_ERR_NCCL on an
                         NCCL error) after aborting the communicator, and the
                         model refuses further calls: free it, make a new
-                        communicator and load again. */
+                        communicator and load again
+                        (ifx_tp_comm_destroy knows the aborted communicator
+                        is gone and only forgets it). */
 } ifx_load_opts;
 
 enum { IFX_KQUANT_REFERENCE = 0, IFX_KQUANT_GGML = 1 };

@@ -533,7 +533,8 @@ ifx_status ifx_tp_comm_create(const void *id, int nranks, int rank, int device, 
 
 void ifx_tp_comm_destroy(void *comm) {
   const NcclApi *api = nullptr;
-  if (comm && nccl_api(&api) == IFX_OK) api->CommDestroy((ncclComm_t)comm);
+  if (!comm || tp_take_aborted(comm)) return;  // an aborted communicator is already freed
+  if (nccl_api(&api) == IFX_OK) api->CommDestroy((ncclComm_t)comm);
 }
 
 ifx_status ifx_tp_shard(int type, const void *gguf_bytes, size_t nbytes, size_t rows, size_t cols,

@@ -7,6 +7,7 @@
 
 #include <chrono>
 #include <thread>
+#include <unordered_set>
 
 #include "quant.cuh"
 #include "tp.h"
@@ -15,6 +16,8 @@
 namespace ifx {
 
 namespace {
+std::mutex g_aborted_mu;
+std::unordered_set<void *> g_aborted;  // communicators tp_wait aborted
 std::once_flag g_nccl_once;
 NcclApi g_nccl{};
 std::string g_nccl_err;
@@ -57,6 +60,11 @@ ifx_status nccl_fail(const NcclApi *api, ncclResult_t r, const char *what) {
   return fail(IFX_ERR_NCCL, std::string(what) + ": " + (api ? api->GetErrorString(r) : "error"));
 }
 
+bool tp_take_aborted(void *comm) {
+  std::lock_guard<std::mutex> lk(g_aborted_mu);
+  return g_aborted.erase(comm) > 0;
+}
+
 ifx_status tp_wait(cudaStream_t st, ncclComm_t comm, const NcclApi *api, double timeout_ms) {
   using clk = std::chrono::steady_clock;
   cudaError_t dev_err = cudaSuccess;
@@ -75,7 +83,13 @@ ifx_status tp_wait(cudaStream_t st, ncclComm_t comm, const NcclApi *api, double 
     comm_err = r;
     return true;
   };
-  auto abort = [&]() { api->CommAbort(comm); };
+  auto abort = [&]() {
+    {
+      std::lock_guard<std::mutex> lk(g_aborted_mu);
+      g_aborted.insert((void *)comm);
+    }
+    api->CommAbort(comm);
+  };
   auto now_ms = []() {
     return std::chrono::duration<double, std::milli>(clk::now().time_since_epoch()).count();
   };

@@ -40,6 +40,10 @@ ifx_status nccl_fail(const NcclApi *api, ncclResult_t r, const char *what);
 // and returns IFX_ERR_NCCL / IFX_ERR_TIMEOUT.
 ifx_status tp_wait(cudaStream_t st, ncclComm_t comm, const NcclApi *api, double timeout_ms);
 
+// Whether tp_wait aborted `comm` (ncclCommAbort frees it, so it must not be
+// destroyed again); take_aborted() also forgets it.
+bool tp_take_aborted(void *comm);
+
 #define IFX_NCCL(api, call)                                           \
   do {                                                                \
     const ncclResult_t r_ = (call);                                   \
