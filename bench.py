@@ -192,9 +192,9 @@ def run_ours(args):
     m.prefill(prompt, kv, last_row_only=True)
     kv.clear()
     torch.cuda.synchronize()
-    tp = time.perf_counter()
+    t_pf = time.perf_counter()
     lg = m.prefill(prompt, kv, last_row_only=True)
-    prefill_s = time.perf_counter() - tp
+    prefill_s = time.perf_counter() - t_pf
     first = int(np.argmax(lg[0]))
 
     # decode: W untimed steps, then K device-fed steps timed with CUDA events
