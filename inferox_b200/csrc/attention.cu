@@ -465,14 +465,11 @@ __device__ __forceinline__ uint32_t pack_h2(float x, float y) {
 
 template <int HD>
 __global__ void __launch_bounds__(128) prefill_attn_tc_kernel(PrefillAttnArgs a) {
-  // K and V rows (f16) at a stride of HD + 8 halves: the 8 rows a fragment
-  // load or an ldmatrix touches fall on distinct banks; V stays row-major and
-  // its B fragments come from ldmatrix.trans
-  constexpr int KS = HD + 8;
-  static_assert(HD % 16 == 0, "two 8-wide dim tiles per ldmatrix");
+  constexpr int KS = HD + 8;   // K row stride (halves): the 8 rows a fragment load touches
+  constexpr int VS = kTK + 8;  // Vt row stride             fall on distinct banks
   extern __shared__ __align__(16) __half smh[];
   __half *Ks = smh;             // [kTK][KS]
-  __half *Vs = smh + kTK * KS;  // [kTK][KS]
+  __half *Vt = smh + kTK * KS;  // [HD][VS]
   const int hq = blockIdx.x, qb = blockIdx.y, tid = threadIdx.x;
   const int warp = tid >> 5, lane = tid & 31, g = lane >> 2, c = lane & 3;
   const int grp = a.H / a.G, hk = hq / grp;
@@ -516,7 +513,10 @@ __global__ void __launch_bounds__(128) prefill_attn_tc_kernel(PrefillAttnArgs a)
         vv = *reinterpret_cast<const float4 *>(a.v + (size_t)(kb + t) * kstride + hk * HD + d);
       }
       *reinterpret_cast<uint2 *>(Ks + t * KS + d) = make_uint2(pack_h2(kv.x, kv.y), pack_h2(kv.z, kv.w));
-      *reinterpret_cast<uint2 *>(Vs + t * KS + d) = make_uint2(pack_h2(vv.x, vv.y), pack_h2(vv.z, vv.w));
+      Vt[(d + 0) * VS + t] = __float2half_rn(vv.x);
+      Vt[(d + 1) * VS + t] = __float2half_rn(vv.y);
+      Vt[(d + 2) * VS + t] = __float2half_rn(vv.z);
+      Vt[(d + 3) * VS + t] = __float2half_rn(vv.w);
     }
     __syncthreads();
     float sv[kTK / 8][4];
@@ -578,16 +578,12 @@ __global__ void __launch_bounds__(128) prefill_attn_tc_kernel(PrefillAttnArgs a)
       const uint32_t p1 = pack_h2(sv[2 * k2][2], sv[2 * k2][3]);
       const uint32_t p2 = pack_h2(sv[2 * k2 + 1][0], sv[2 * k2 + 1][1]);
       const uint32_t p3 = pack_h2(sv[2 * k2 + 1][2], sv[2 * k2 + 1][3]);
-      // matrices of one ldmatrix.x4.trans: keys +0-7 / +8-15 of this 16-key
-      // step at dim tiles nt and nt + 1; lane l addresses row l & 7 of
-      // matrix l >> 3
-      const int key = k2 * 16 + ((lane >> 3) & 1) * 8 + (lane & 7);
 #pragma unroll
-      for (int nt = 0; nt < HD / 8; nt += 2) {
-        uint32_t b[4];
-        ldsm_x4_t(b, smem_u32(Vs + key * KS + (nt + (lane >> 4)) * 8));
-        mma_16816(o[nt], p0, p1, p2, p3, b[0], b[1], o[nt]);
-        mma_16816(o[nt + 1], p0, p1, p2, p3, b[2], b[3], o[nt + 1]);
+      for (int nt = 0; nt < HD / 8; ++nt) {
+        const __half *vr = Vt + (nt * 8 + g) * VS + k2 * 16 + 2 * c;
+        const uint32_t b0 = *reinterpret_cast<const uint32_t *>(vr);
+        const uint32_t b1 = *reinterpret_cast<const uint32_t *>(vr + 8);
+        mma_16816(o[nt], p0, p1, p2, p3, b0, b1, o[nt]);
       }
     }
   }
@@ -610,7 +606,7 @@ __global__ void __launch_bounds__(128) prefill_attn_tc_kernel(PrefillAttnArgs a)
 
 template <int HD>
 static ifx_status launch_prefill_tc(const PrefillAttnArgs &a, cudaStream_t st) {
-  const size_t smem = (size_t)(2 * kTK * (HD + 8)) * sizeof(__half);
+  const size_t smem = (size_t)(kTK * (HD + 8) + HD * (kTK + 8)) * sizeof(__half);
   dim3 grid(a.H, (a.n + kTQ - 1) / kTQ);
   prefill_attn_tc_kernel<HD><<<grid, 128, smem, st>>>(a);
   IFX_CUDA(cudaGetLastError());
