@@ -13,6 +13,8 @@
 // thread_rng; here the draws come from the device sampler's counter-based
 // generator, seeded from IFX_SEED when set, else from std::random_device.
 // Greedy output (temperature 0, the default) is deterministic either way.
+// IFX_KQUANT_LAYOUT=ggml loads a file written by llama.cpp (ggml type ids and
+// K-quant byte orders; the default, "reference", reads the reference's).
 //
 // Inspect mode prints the header, metadata, tensor table, data layout and
 // the first five tensors' byte ranges in the reference's format
@@ -283,6 +285,13 @@ void generate(const char *model_path, const char *tok_path, const char *prompt, 
               float temperature) {  // main.rs:39-95
   ifx_load_opts o;
   ifx_load_opts_default(&o);
+  // the arguments stay main.rs's; a file written by llama.cpp is announced
+  // through the environment
+  if (const char *k = getenv("IFX_KQUANT_LAYOUT")) {
+    if (!strcmp(k, "ggml")) o.kquant_layout = IFX_KQUANT_GGML;
+    else if (strcmp(k, "reference") != 0)
+      die(std::string("error: IFX_KQUANT_LAYOUT must be 'reference' or 'ggml', not '") + k + "'");
+  }
   ifx_model *m = nullptr;
   if (ifx_model_load(model_path, &o, &m) != IFX_OK)
     die(std::string("error: failed to load model '") + model_path + "': " + last_error());

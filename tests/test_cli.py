@@ -204,3 +204,11 @@ def test_errors_and_usage(tmp_path):
     path, _ = _write(tmp_path, META[:1], [])
     r = subprocess.run([IFX, path, str(tmp_path / "none.json"), "hi"], capture_output=True, text=True)
     assert r.returncode == 1 and r.stderr.startswith("error: failed to load ")
+
+
+def test_kquant_layout_variable(tmp_path):
+    path, _ = _write(tmp_path, META[:1], [])
+    env = dict(os.environ, IFX_KQUANT_LAYOUT="gguf")
+    r = subprocess.run([IFX, path, str(tmp_path / "t.json"), "hi"], capture_output=True, text=True, env=env)
+    assert r.returncode == 1
+    assert "IFX_KQUANT_LAYOUT must be 'reference' or 'ggml'" in r.stderr
