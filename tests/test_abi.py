@@ -120,3 +120,14 @@ def test_integration_binding_declares_every_entry_point():
     doc = open(os.path.join(ROOT, "INTEGRATION.md")).read()
     declared = set(re.findall(r"pub fn (ifx_[a-z0-9_]+)", doc))
     assert set(inferox_b200.header_symbols()) == declared
+
+
+def test_plain_c_caller(tmp_path):
+    """The header compiles as pedantic C99 and a C program links and runs."""
+    exe = tmp_path / "c_caller"
+    libdir = os.path.dirname(_lib.LIB_PATH)
+    subprocess.run(["gcc", "-std=c99", "-Wall", "-Wextra", "-pedantic", "-Werror",
+                    "-I", os.path.join(ROOT, "include"), os.path.join(ROOT, "tests", "cpp", "c_caller.c"),
+                    "-L", libdir, "-linferox_b200", f"-Wl,-rpath,{libdir}", "-o", str(exe)], check=True)
+    r = subprocess.run([str(exe)], capture_output=True, text=True, timeout=120)
+    assert r.returncode == 0 and "c caller ok" in r.stdout, (r.returncode, r.stdout, r.stderr)
