@@ -7,5 +7,7 @@ fallback.
 """
 from ._lib import IfxError, header_symbols, lib  # noqa: F401
 from .model import KvBatch, KvCache, Model, Sampler, load_opts  # noqa: F401
+from .tokenizer import BpeTokenizer  # noqa: F401
 
-__all__ = ["Model", "KvCache", "KvBatch", "Sampler", "IfxError", "load_opts", "lib", "header_symbols"]
+__all__ = ["Model", "KvCache", "KvBatch", "Sampler", "BpeTokenizer", "IfxError", "load_opts", "lib",
+           "header_symbols"]
