@@ -1,0 +1,124 @@
+"""Continuous batching: a greedy serving loop over one KvBatch whose requests
+arrive and finish at different times. No reference counterpart (its
+KvCache holds one sequence, src/model/cache.rs:7-13); each request produces
+exactly what Model::generate (src/model/forward.rs:592-612) produces for it
+alone: the argmax of the prompt's last logits (the last index among equal
+maxima, forward.rs:615-622), then the argmax after feeding each token back.
+
+    srv = Server.for_model(model, slots=16, max_seq=4096)
+    rid = srv.submit(prompt_ids, max_tokens=64)
+    results = srv.run()            # {request id: generated tokens}
+
+Each step() first admits waiting requests into free slots (first come,
+first served: the slot is cleared, the prompt prefilled, its first token
+taken), then runs one decode step of every active slot together
+(ifx_decode_step_batch_seqs: one read of the weights for all of them). A
+request leaves when it has max_tokens tokens or emits `eos`; its slot takes
+the next request on the following step. A finished request's last token is
+not fed back (the reference feeds it and discards the logits), so a request
+needs len(prompt) + max_tokens - 1 cache rows.
+"""
+from __future__ import annotations
+
+from collections import deque
+from dataclasses import dataclass, field
+
+import numpy as np
+
+
+def last_argmax(x) -> int:
+    """argmax with ties going to the last index (forward.rs:615-622)."""
+    x = np.asarray(x)
+    return int(x.size - 1 - np.argmax(x[::-1]))
+
+
+@dataclass
+class _Request:
+    rid: int
+    prompt: np.ndarray
+    max_tokens: int
+    eos: int | None
+    tokens: list = field(default_factory=list)
+    done: bool = False
+
+
+class Server:
+    """Greedy continuous batching over `batch`, any object with KvBatch's
+    `batch`, `max_seq`, `prefill`, `decode_step_seqs` and `reset`."""
+
+    def __init__(self, batch):
+        self.kb = batch
+        self.slots: list[_Request | None] = [None] * batch.batch
+        self.used = [False] * batch.batch  # slot ever held a request (needs a reset)
+        self.waiting: deque[_Request] = deque()
+        self.requests: dict[int, _Request] = {}
+        self._next = 0
+        self.steps = 0  # batched decode steps run
+
+    @classmethod
+    def for_model(cls, model, slots: int, max_seq: int) -> "Server":
+        return cls(model.kv_batch(slots, max_seq))
+
+    def submit(self, prompt, max_tokens: int, eos: int | None = None) -> int:
+        p = np.ascontiguousarray(prompt, np.uint32)
+        if p.size == 0:
+            raise ValueError("empty prompt")
+        if max_tokens < 1:
+            raise ValueError("max_tokens must be at least 1")
+        if p.size + max_tokens - 1 > self.kb.max_seq:
+            raise ValueError(f"prompt ({p.size}) + max_tokens ({max_tokens}) - 1 exceeds the "
+                             f"{self.kb.max_seq}-row cache of a slot")
+        r = _Request(self._next, p, max_tokens, eos)
+        self._next += 1
+        self.requests[r.rid] = r
+        self.waiting.append(r)
+        return r.rid
+
+    def busy(self) -> bool:
+        return bool(self.waiting) or any(s is not None for s in self.slots)
+
+    def result(self, rid: int):
+        r = self.requests[rid]
+        return list(r.tokens) if r.done else None
+
+    def _finish_if_done(self, slot: int) -> None:
+        r = self.slots[slot]
+        if len(r.tokens) >= r.max_tokens or (r.eos is not None and r.tokens[-1] == r.eos):
+            r.done = True
+            self.slots[slot] = None
+
+    def _admit(self) -> None:
+        for slot in range(len(self.slots)):
+            if not self.waiting:
+                return
+            if self.slots[slot] is not None:
+                continue
+            r = self.waiting.popleft()
+            if self.used[slot]:
+                self.kb.reset(slot)
+            self.used[slot] = True
+            logits = self.kb.prefill(slot, r.prompt, True)
+            r.tokens.append(last_argmax(logits[0]))
+            self.slots[slot] = r
+            self._finish_if_done(slot)
+
+    def step(self) -> int:
+        """Admit, then one decode step of every active slot; returns how many
+        sequences the step decoded."""
+        self._admit()
+        seqs = [i for i, r in enumerate(self.slots) if r is not None]
+        if not seqs:
+            return 0
+        toks = [self.slots[i].tokens[-1] for i in seqs]
+        _, amax = self.kb.decode_step_seqs(seqs, toks, want_logits=False)
+        self.steps += 1
+        for i, t in zip(seqs, amax):
+            self.slots[i].tokens.append(int(t))
+            self._finish_if_done(i)
+        return len(seqs)
+
+    def run(self) -> dict[int, list]:
+        """Steps until every submitted request has finished."""
+        while self.busy():
+            self.step()
+        return {rid: list(r.tokens) for rid, r in self.requests.items()}

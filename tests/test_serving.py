@@ -1,0 +1,112 @@
+"""The continuous-batching loop (inferox_b200/serving.py) on CPU against a
+fake batch whose next token depends only on that sequence's own history:
+every request, served among others with slots reused, must produce what
+Model::generate (forward.rs:592-612) produces for it alone. The GPU side of
+the calls it makes (prefill of one slot, a step over a subset of slots, a
+slot reset) is held to the oracle in tests/test_gpu_batch.py."""
+import numpy as np
+import pytest
+
+from inferox_b200.serving import Server, last_argmax
+
+V = 97
+
+
+def _next(history):
+    h = 0
+    for t in history:
+        h = (h * 31 + int(t) + 7) % 1000003
+    return h % V
+
+
+class FakeBatch:
+    def __init__(self, batch, max_seq):
+        self.batch, self.max_seq = batch, max_seq
+        self.hist = [[] for _ in range(batch)]
+        self.prefills, self.resets, self.steps = [], [], 0
+
+    def _grow(self, slot, toks):
+        self.hist[slot].extend(int(t) for t in toks)
+        if len(self.hist[slot]) > self.max_seq:
+            raise RuntimeError("KV cache is full")
+
+    def prefill(self, slot, ids, last_row_only=False):
+        assert last_row_only
+        self.prefills.append(slot)
+        self._grow(slot, ids)
+        want = _next(self.hist[slot])
+        logits = np.zeros((1, V), np.float32)
+        logits[0, want] = 5.0
+        logits[0, (want * 3) % want if want else 0] = 5.0 if want else 0.0  # a tie below `want`
+        return logits
+
+    def decode_step_seqs(self, seqs, tokens, want_logits=True):
+        assert len(set(seqs)) == len(seqs) and len(seqs) == len(tokens)
+        self.steps += 1
+        out = []
+        for s, t in zip(seqs, tokens):
+            self._grow(s, [t])
+            out.append(_next(self.hist[s]))
+        return None, np.array(out, np.uint32)
+
+    def reset(self, slot):
+        self.resets.append(slot)
+        self.hist[slot] = []
+
+
+def _alone(prompt, max_tokens, eos=None):
+    """forward.rs:592-612 on a fresh single-sequence fake, stopping at eos."""
+    fb = FakeBatch(1, 10_000)
+    toks = [last_argmax(fb.prefill(0, prompt, True)[0])]
+    while len(toks) < max_tokens and not (eos is not None and toks[-1] == eos):
+        _, a = fb.decode_step_seqs([0], [toks[-1]])
+        toks.append(int(a[0]))
+    return toks
+
+
+def test_last_argmax_ties():
+    assert last_argmax([1, 3, 3, 0]) == 2
+    assert last_argmax([2.0]) == 0
+
+
+def test_requests_match_their_solo_runs():
+    rng = np.random.default_rng(3)
+    fb = FakeBatch(3, 40)
+    srv = Server(fb)
+    reqs = []
+    for i in range(9):
+        p = rng.integers(3, V, size=int(rng.integers(1, 8)))
+        n = int(rng.integers(1, 12))
+        eos = int(rng.integers(0, V)) if i % 3 == 0 else None
+        reqs.append((srv.submit(p, n, eos), p, n, eos))
+    srv.step()
+    assert len(srv.waiting) == 6  # three slots filled first come, first served
+    out = srv.run()
+    for rid, p, n, eos in reqs:
+        want = _alone(p, n, eos)
+        assert out[rid] == want, (rid, out[rid], want)
+        assert srv.result(rid) == want
+    assert fb.prefills[:3] == [0, 1, 2] and len(fb.prefills) == 9
+    assert sorted(set(fb.resets)) == [0, 1, 2]  # every slot was reused
+    solo_steps = sum(len(_alone(p, n, e)) - 1 for _, p, n, e in reqs)
+    assert srv.steps < solo_steps  # steps were shared between requests
+    assert not srv.busy()
+
+
+def test_limits():
+    fb = FakeBatch(2, 10)
+    srv = Server(fb)
+    with pytest.raises(ValueError):
+        srv.submit([], 3)
+    with pytest.raises(ValueError):
+        srv.submit([5], 0)
+    with pytest.raises(ValueError):
+        srv.submit(list(range(3, 9)), 6)  # 6 + 6 - 1 = 11 rows > 10
+    rid = srv.submit(list(range(3, 8)), 6)  # 5 + 6 - 1 = 10 rows: fits exactly
+    assert srv.result(rid) is None
+    srv.run()
+    assert len(srv.result(rid)) == 6 and len(fb.hist[0]) == 10
+    one = srv.submit([4, 5], 1)  # finishes at admission, no decode step
+    steps = srv.steps
+    srv.run()
+    assert srv.result(one) == _alone([4, 5], 1) and srv.steps == steps
