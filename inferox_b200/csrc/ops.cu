@@ -200,7 +200,18 @@ __global__ void key_to_token_kernel(unsigned long long *key, uint32_t *out) {
 // a radix search over the ordered bits of p picks the threshold value, and
 // elements equal to it are taken in ascending index order (what a stable
 // descending sort does with ties).
+//
+// Every sum of probability mass is exact and therefore independent of the
+// order of additions (the same logits and draw always give the same token):
+// p_i = exp(z_i / T) is held as the 64-bit fixed-point mass
+// m_i = round(p_i * 2^50 / S), S the sum of all p_i, and the cumulative sums
+// behind the top-p cut and the weighted draw are integer sums of m_i. The
+// reference sums f32 values one after another (normalise, cumulative
+// `>= top_p`, renormalise, WeightedIndex's cumulative weights); its pick and
+// this one can differ only where u or top_p lies within that f32 rounding of
+// a cumulative boundary.
 constexpr int kSampThreads = 1024;
+constexpr double kMassOne = 1125899906842624.0;  // 2^50: fixed-point mass of probability 1
 
 struct Cut {
   uint32_t key;   // ordered bits of the threshold value
@@ -215,39 +226,83 @@ __device__ __forceinline__ bool kept(const float *p, size_t i, const Cut &c1, co
   return true;
 }
 
+// Fixed-point mass of one probability (scale = 2^50 / S).
+__device__ __forceinline__ unsigned long long mass_of(float p, double scale) {
+  return __double2ull_rn((double)p * scale);
+}
+
+// Exact block sum of 64-bit integers (every thread gets the total).
+__device__ unsigned long long block_sum_u64(unsigned long long v, unsigned long long *red) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    unsigned long long t = red[threadIdx.x];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
+    if (threadIdx.x == 0) red[0] = t;
+  }
+  __syncthreads();
+  const unsigned long long r = red[0];
+  __syncthreads();
+  return r;
+}
+
+// Block sum of doubles in a fixed order (thread partials over a fixed element
+// mapping, then a fixed shuffle tree), so the result never varies.
+__device__ double block_sum_f64(double v, double *red) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    double t = red[threadIdx.x];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
+    if (threadIdx.x == 0) red[0] = t;
+  }
+  __syncthreads();
+  const double r = red[0];
+  __syncthreads();
+  return r;
+}
+
 // First element (desc value, asc index) at which the running weight reaches
-// the target (>= when inclusive, > otherwise); weight = 1 (count) or p.
+// the target (>= when inclusive, > otherwise); weight = 1 (count) or the
+// element's fixed-point mass. Integer histograms: exact in any order.
 __device__ Cut find_cut(const float *p, size_t n, const Cut &c1, const Cut &c2, bool by_count,
-                        float target, bool inclusive, float *hist, float *scan) {
+                        unsigned long long target, bool inclusive, double scale,
+                        unsigned long long *hist, unsigned long long *scan) {
   const int tid = threadIdx.x;
   uint32_t prefix = 0, pmask = 0;
-  float above = 0.f;
+  unsigned long long above = 0;
   for (int b = 3; b >= 0; --b) {
-    for (int j = tid; j < 256; j += kSampThreads) hist[j] = 0.f;
+    for (int j = tid; j < 256; j += kSampThreads) hist[j] = 0;
     __syncthreads();
     for (size_t i = tid; i < n; i += kSampThreads) {
       if (!kept(p, i, c1, c2)) continue;
-      uint32_t k = ordered_bits(p[i]);
+      const uint32_t k = ordered_bits(p[i]);
       if ((k & pmask) != prefix) continue;
-      atomicAdd(&hist[(k >> (8 * b)) & 255u], by_count ? 1.0f : p[i]);
+      atomicAdd(&hist[(k >> (8 * b)) & 255u], by_count ? 1ull : mass_of(p[i], scale));
     }
     __syncthreads();
     if (tid == 0) {
-      float cum = above;
+      unsigned long long cum = above;
       int sel = -1;
       for (int j = 255; j >= 0; --j) {
-        float nc = cum + hist[j];
+        const unsigned long long nc = cum + hist[j];
         if (inclusive ? (nc >= target) : (nc > target)) {
           sel = j;
           break;
         }
         cum = nc;
       }
-      scan[0] = (float)sel;
+      scan[0] = (unsigned long long)(long long)sel;
       scan[1] = cum;
     }
     __syncthreads();
-    int sel = (int)scan[0];
+    const int sel = (int)(long long)scan[0];
     if (sel < 0) {
       Cut none{0, 0, 0};
       return none;
@@ -258,17 +313,17 @@ __device__ Cut find_cut(const float *p, size_t n, const Cut &c1, const Cut &c2, 
     __syncthreads();
   }
   // ties at `prefix`: walk indices in order (each thread a contiguous chunk)
-  size_t per = (n + kSampThreads - 1) / kSampThreads;
-  size_t lo = tid * per, hi = lo + per < n ? lo + per : n;
-  float mine = 0.f;
+  const size_t per = (n + kSampThreads - 1) / kSampThreads;
+  const size_t lo = tid * per, hi = lo + per < n ? lo + per : n;
+  unsigned long long mine = 0;
   for (size_t i = lo; i < hi; ++i)
-    if (kept(p, i, c1, c2) && ordered_bits(p[i]) == prefix) mine += by_count ? 1.0f : p[i];
+    if (kept(p, i, c1, c2) && ordered_bits(p[i]) == prefix) mine += by_count ? 1ull : mass_of(p[i], scale);
   scan[2 + tid] = mine;
   __syncthreads();
   if (tid == 0) {
-    float run = above;
+    unsigned long long run = above;
     for (int t = 0; t < kSampThreads; ++t) {
-      float v = scan[2 + t];
+      const unsigned long long v = scan[2 + t];
       scan[2 + t] = run;  // exclusive prefix
       run += v;
     }
@@ -277,10 +332,10 @@ __device__ Cut find_cut(const float *p, size_t n, const Cut &c1, const Cut &c2, 
   __shared__ unsigned long long best;
   if (tid == 0) best = ~0ull;
   __syncthreads();
-  float run = scan[2 + tid];
+  unsigned long long run = scan[2 + tid];
   for (size_t i = lo; i < hi; ++i) {
     if (!(kept(p, i, c1, c2) && ordered_bits(p[i]) == prefix)) continue;
-    run += by_count ? 1.0f : p[i];
+    run += by_count ? 1ull : mass_of(p[i], scale);
     if (inclusive ? (run >= target) : (run > target)) {
       atomicMin(&best, (unsigned long long)i);
       break;
@@ -292,17 +347,33 @@ __device__ Cut find_cut(const float *p, size_t n, const Cut &c1, const Cut &c2, 
   return c;
 }
 
-__device__ float block_sum(float v, float *red) {
-  v = warp_sum(v);
-  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+// Largest value, last index on ties (the argmax of the reference).
+__device__ uint32_t block_argmax(const float *x, size_t n, unsigned long long *red) {
+  unsigned long long best = 0;
+  for (size_t i = threadIdx.x; i < n; i += kSampThreads) {
+    const float v = x[i];
+    if (v != v) continue;
+    const unsigned long long k = ((unsigned long long)ordered_bits(v) << 32) | (unsigned long long)i;
+    best = k > best ? k : best;
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const unsigned long long other = __shfl_xor_sync(0xffffffffu, best, o);
+    best = other > best ? other : best;
+  }
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = best;
   __syncthreads();
   if (threadIdx.x < 32) {
-    float t = red[threadIdx.x];
-    t = warp_sum(t);
+    unsigned long long t = red[threadIdx.x];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const unsigned long long other = __shfl_xor_sync(0xffffffffu, t, o);
+      t = other > t ? other : t;
+    }
     if (threadIdx.x == 0) red[0] = t;
   }
   __syncthreads();
-  float r = red[0];
+  const uint32_t r = (uint32_t)(red[0] & 0xffffffffull);
   __syncthreads();
   return r;
 }
@@ -310,9 +381,10 @@ __device__ float block_sum(float v, float *red) {
 __global__ void __launch_bounds__(kSampThreads) sample_kernel(
     const float *logits, float *p, size_t n, float temperature, uint64_t top_k, float top_p,
     float u, int use_hash, uint64_t seed, uint64_t offset, uint32_t *out) {
-  __shared__ float hist[256];
-  __shared__ float scan[2 + kSampThreads];
-  __shared__ float red[32];
+  __shared__ unsigned long long hist[256];
+  __shared__ unsigned long long scan[2 + kSampThreads];
+  __shared__ unsigned long long ured[32];
+  __shared__ double dred[32];
   const int tid = threadIdx.x;
   if (use_hash) {
     // counter-based uniform in [0,1) with 23 random mantissa bits
@@ -322,40 +394,59 @@ __global__ void __launch_bounds__(kSampThreads) sample_kernel(
     z ^= z >> 31;
     u = (float)(z >> 41) * (1.0f / 8388608.0f);
   }
-  float s = 0.f;
+  // sampler.rs:34-38: exp(z / T) with no max subtraction; the exponential is
+  // taken in double and rounded once to f32
+  double s = 0.0;
   for (size_t i = tid; i < n; i += kSampThreads) {
-    float e = expf(logits[i] / temperature);  // sampler.rs:34-38: no max subtraction
+    const float e = (float)exp((double)__fdiv_rn(logits[i], temperature));
     p[i] = e;
-    s += e;
+    s += (double)e;
   }
   __syncthreads();
-  const float S = block_sum(s, red);
+  const double S = block_sum_f64(s, dred);
+  if (!(S > 0.0) || !(S <= 1.7e308)) {
+    // every p underflowed or some overflowed (the reference's normalisation
+    // then yields NaN and its sort panics): take the largest logit instead
+    const uint32_t t = block_argmax(logits, n, ured);
+    if (tid == 0) *out = t;
+    return;
+  }
+  const double scale = kMassOne / S;
+  unsigned long long m = 0;
+  for (size_t i = tid; i < n; i += kSampThreads) m += mass_of(p[i], scale);
+  const unsigned long long M = block_sum_u64(m, ured);
   Cut none{0, 0, 0};
   Cut ck = none, cp = none;
   if (top_k > 0 && top_k < n)
-    ck = find_cut(p, n, none, none, true, (float)top_k, true, hist, scan);
+    ck = find_cut(p, n, none, none, true, (unsigned long long)top_k, true, scale, hist, scan);
   if (top_p < 1.0f) {
-    Cut c = find_cut(p, n, ck, none, false, top_p * S, true, hist, scan);
+    // cumulative normalised mass >= top_p (sampler.rs:49-62); top_p <= 0
+    // keeps the first element, as the reference's first comparison does
+    const double t = (double)top_p * (double)M;
+    const unsigned long long target = t > 0.0 ? (unsigned long long)ceil(t) : 0ull;
+    Cut c = find_cut(p, n, ck, none, false, target, true, scale, hist, scan);
     if (c.found) cp = c;
   }
-  float s2 = 0.f;
+  unsigned long long s2 = 0;
   for (size_t i = tid; i < n; i += kSampThreads)
-    if (kept(p, i, ck, cp)) s2 += p[i];
-  const float S2 = block_sum(s2, red);
+    if (kept(p, i, ck, cp)) s2 += mass_of(p[i], scale);
+  const unsigned long long S2 = block_sum_u64(s2, ured);
+  // the draw: first candidate whose cumulative mass exceeds u * S2 (rand
+  // 0.8.6 WeightedIndex: partition_point of cumulative weights <= chosen)
+  const unsigned long long target = (unsigned long long)floor((double)u * (double)S2);
   if (top_k == 0 && !(top_p < 1.0f)) {
     // Neither filter sorted the candidates, so WeightedIndex walks them in
-    // index order (sampler.rs:45-71): first i with cumsum(p[0..=i]) > u*S2,
-    // else the last index.
+    // index order (sampler.rs:45-71), else the last index.
     const size_t per = (n + kSampThreads - 1) / kSampThreads;
     const size_t lo = tid * per, hi = lo + per < n ? lo + per : n;
-    float mine = 0.f;
-    for (size_t i = lo; i < hi; ++i) mine += p[i];
+    unsigned long long mine = 0;
+    for (size_t i = lo; i < hi; ++i) mine += mass_of(p[i], scale);
     scan[2 + tid] = mine;
     __syncthreads();
     if (tid == 0) {
-      float run = 0.f;
+      unsigned long long run = 0;
       for (int t = 0; t < kSampThreads; ++t) {
-        const float v = scan[2 + t];
+        const unsigned long long v = scan[2 + t];
         scan[2 + t] = run;
         run += v;
       }
@@ -363,10 +454,9 @@ __global__ void __launch_bounds__(kSampThreads) sample_kernel(
     __shared__ unsigned long long first;
     if (tid == 0) first = ~0ull;
     __syncthreads();
-    float run = scan[2 + tid];
-    const float target = u * S2;
+    unsigned long long run = scan[2 + tid];
     for (size_t i = lo; i < hi; ++i) {
-      run += p[i];
+      run += mass_of(p[i], scale);
       if (run > target) {
         atomicMin(&first, (unsigned long long)i);
         break;
@@ -376,18 +466,17 @@ __global__ void __launch_bounds__(kSampThreads) sample_kernel(
     if (tid == 0) *out = (first == ~0ull) ? (uint32_t)(n - 1) : (uint32_t)first;
     return;
   }
-  Cut pick = find_cut(p, n, ck, cp, false, u * S2, false, hist, scan);
+  const Cut pick = find_cut(p, n, ck, cp, false, target, false, scale, hist, scan);
+  __shared__ int resolved;
   if (tid == 0) {
-    if (pick.found && pick.idx != 0xffffffffu) {
-      *out = pick.idx;
-    } else {
-      *out = 0xffffffffu;  // resolved below: smallest kept element
-    }
+    resolved = pick.found && pick.idx != 0xffffffffu;
+    if (resolved) *out = pick.idx;
   }
   __syncthreads();
-  if (*out == 0xffffffffu) {
-    // u*S2 beyond the accumulated mass (rounding): WeightedIndex returns the
-    // last weight, i.e. the smallest kept element (largest index among ties).
+  if (!resolved) {
+    // target beyond the kept mass (not reached for u < 1): WeightedIndex
+    // returns the last weight, i.e. the smallest kept element (largest index
+    // among ties)
     __shared__ unsigned long long low;
     if (tid == 0) low = ~0ull;
     __syncthreads();
