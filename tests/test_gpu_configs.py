@@ -1,6 +1,8 @@
 """Parity at the benchmark shapes, truncated so the CPU oracle finishes in
-seconds: the Llama-3.2-1B-shaped model (tied Q6_K embedding / output) and
-the Llama-3-8B-shaped model, both Q4_K_M, on the persistent decode path.
+seconds: the Llama-3.2-1B-shaped model (tied Q6_K embedding / output), the
+Llama-3-8B-shaped model (64-token prompt, 32 decode steps) and the
+Llama-2-70B-shaped model cut to 4 of its 80 layers (full width: 64 query
+heads over 8 kv heads), all Q4_K_M, on the persistent decode path.
 
 Bar (the north star's): logits within |gpu - ref| <= 2e-2 + 1e-2 |ref|
 and teacher-forced top-1 agreement on at least 99% of the steps. The
@@ -25,9 +27,10 @@ def _close(g, r):
     return np.all(np.abs(g - r) <= ATOL + RTOL * np.abs(r))
 
 
-@pytest.mark.parametrize("name,n_prompt,n_steps", [("1b", 32, 12), ("8b", 16, 6)])
-def test_benchmark_shape_parity(name, n_prompt, n_steps):
-    g = synth.build(name)
+@pytest.mark.parametrize("name,n_prompt,n_steps,layers",
+                         [("1b", 32, 12, 0), ("8b", 64, 32, 0), ("70b", 16, 8, 4)])
+def test_benchmark_shape_parity(name, n_prompt, n_steps, layers):
+    g = synth.build(name, **({"n_layers": layers} if layers else {}))
     m, o = Model.from_bytes(g), R.Model(g)
     L = int(m.config.n_layers)
     V = int(m.config.vocab_size)
