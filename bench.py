@@ -35,8 +35,8 @@ CONFIG = "8b"
 PROMPT = 1024
 METRIC = "decode tok/s @8B Q4_K_M batch 1 as % of HBM roofline; prefill tok/s"
 # DRAM bytes (read + write) per algorithmic byte of decode_mega_kernel, from
-# the ncu capture summarised in profiles/decode_mega_kernel_8b_4layers.md
-# (976.6 MB + 15.1 MB over 973.2 MB); traffic scales with the weight bytes.
+# an ncu capture of the 4-layer 8B-shaped case (976.6 MB + 15.1 MB over
+# 973.2 MB); traffic scales with the weight bytes.
 TRAFFIC_PER_ALGO_BYTE = 1.019
 
 
@@ -98,46 +98,115 @@ class Clocks:
                 "samples": len(rows)}
 
 
+def prompt_ids(vocab: int, n: int, seq_index: int = 0, seed: int = 42):
+    """Seeded uniform prompt ids in [3, vocab): the benchmark's prompts (the
+    same rule as inferox_b200.synth.prompt_ids, restated here so the reference
+    arm needs nothing from the product package)."""
+    import numpy as np
+    return np.random.default_rng(seed + seq_index).integers(3, vocab, size=n, dtype=np.uint32)
+
+
+def shape_overrides(args) -> dict:
+    """Profiling / testing cuts of the 8B shape (--layers, --vocab)."""
+    o = {}
+    if args.layers:
+        o["n_layers"] = args.layers
+    if args.vocab:
+        o["vocab"] = args.vocab
+    return o
+
+
+def bench_config(args) -> dict:
+    """The workload both arms run (identical dicts, so the driver can compare
+    them): decode contexts start after the prompt and the warm-up steps."""
+    ctx0 = PROMPT + args.warmup
+    return {"workload": "llama3-8b-shaped Q4_K_M: 1024-token prompt prefill, then batch-1 greedy decode"
+                        + (f" (profiling case: {args.layers} layers)" if args.layers else "")
+                        + (f" (test case: vocabulary {args.vocab})" if args.vocab else ""),
+            "batch": 1, "prompt_tokens": PROMPT, "decode_context": [ctx0, ctx0 + args.steps],
+            "l2": "no flush needed: 4.6 GB of weights per step >> 126 MB L2"}
+
+
 def cpu_baseline(gguf, steps: int = 1):
     """The reference's CPU path (oracle port, faithful per-call whole-tensor
     dequant, single thread as the reference runs) for `steps` decode steps
-    of the same model from an empty cache."""
+    of the same model at the benchmark's context (the cache is first filled
+    by an untimed threaded prefill of the same 1024-token prompt)."""
     from oracle import refcpu as R
 
+    cores = len(os.sched_getaffinity(0))
+    m = R.Model(gguf)
+    kv = m.kv_cache(int(m.config.n_layers), PROMPT + steps + 8)
+    R.set_threads(cores)
+    R.set_faithful(False)
+    lg = m.prefill(prompt_ids(m.vocab, PROMPT), kv, True)[0]
+    tok = R.argmax(lg)
     R.set_threads(1)
     R.set_faithful(True)
-    m = R.Model(gguf)
-    kv = m.kv_cache(int(m.config.n_layers), 64)
     t0 = time.perf_counter()
-    tok = 5
     for _ in range(steps):
         lg = m.decode_step(tok, kv)
         tok = R.argmax(lg)
     dt = time.perf_counter() - t0
     R.set_faithful(False)
+    R.set_threads(cores)
     return {"value": steps / dt, "unit": "tok/s", "cores": 1, "kind": "port",
-            "sample": f"{steps} faithful decode step(s) of the 8B-shaped Q4_K_M model from an empty "
-                      "cache (per-call whole-tensor dequant + AVX2 matmul_t), 1 host thread"}
+            "sample": f"{steps} faithful decode step(s) of the 8B-shaped Q4_K_M model at context "
+                      f"{PROMPT}-{PROMPT + steps} (per-call whole-tensor dequant + AVX2 matmul_t, "
+                      "as the reference does), 1 host thread, as the reference runs"}
 
 
 def run_reference(args):
+    """The reference's CPU implementation of the decode step (the oracle port:
+    src/model/forward.rs:543-586 with per-call whole-tensor dequantisation,
+    src/gguf/weights.rs:66-74, and the AVX2-order matmul_t, src/ops.rs:106-149)
+    on the same model, prompt and decode contexts as the GPU arm. It loads only
+    the oracle library: the model comes from the oracle's own generator. The
+    dequantisation and the matmuls run on every host thread (bit-identical to
+    one thread); the reference itself is single-threaded, so this is an upper
+    bound on its speed. Under torchrun only rank 0 runs."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
-    from inferox_b200 import synth
+    from oracle import refcpu as R
 
-    g = synth.build(CONFIG)
-    steps = max(1, min(args.steps, 3))
-    base = cpu_baseline(g, steps)
-    line = {"metric": METRIC, "value": base["value"], "unit": "tok/s", "n_gpus": args.gpus,
-            "steps": steps, "warmup": 0, "ms_per_step": 1000.0 / base["value"],
+    cores = len(os.sched_getaffinity(0))
+    R.set_threads(cores)
+    t0 = time.time()
+    g = R.synth_gguf(CONFIG, threads=cores, **shape_overrides(args))
+    m = R.Model(g)
+    L = int(m.config.n_layers)
+    kv = m.kv_cache(L, PROMPT + args.warmup + args.steps + 16)
+    # untimed: the cache brought to the GPU arm's context (prefill of the same
+    # prompt, per-row dequant fused into the dots: the same bits, far faster),
+    # then the W warm-up steps in the reference's own mode
+    R.set_faithful(False)
+    lg = m.prefill(prompt_ids(m.vocab, PROMPT), kv, True)[0]
+    tok = R.argmax(lg)
+    R.set_faithful(True)
+    for _ in range(args.warmup):
+        tok = R.argmax(m.decode_step(tok, kv))
+    setup_s = time.time() - t0
+    ctx0 = len(kv)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        tok = R.argmax(m.decode_step(tok, kv))
+    dt = time.perf_counter() - t0
+    R.set_faithful(False)
+    value = args.steps / dt
+    sample = (f"{args.steps} decode steps (after {args.warmup} warm-up steps) of the 8B-shaped Q4_K_M model "
+              f"at context {ctx0}-{ctx0 + args.steps}, faithful mode (per-call whole-tensor dequant + "
+              f"AVX2-order matmul_t), {cores} host threads")
+    line = {"metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000.0 * dt / args.steps,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
-            "data": "synthetic", "impl": "reference",
-            "config": {"workload": "llama3-8b-shaped Q4_K_M decode, batch 1", "global_batch": 1,
-                       "parallelism": "none (CPU)"},
-            "cpu_baseline": base,
-            "e2e": {"value": base["value"], "unit": "tok/s", "h2d_bytes_per_step": 0,
-                    "d2h_bytes_per_step": 0}}
+            "data": "synthetic (seeded N(0,0.02) weights quantised Q4_K_M; seeded uniform prompt ids)",
+            "impl": "reference", "config": bench_config(args),
+            "placement": f"host CPU, {cores} threads (oracle port of the reference's CPU path)",
+            "cpu_baseline": {"value": value, "unit": "tok/s", "cores": cores, "kind": "port",
+                             "sample": sample},
+            "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+            "setup_s": setup_s}
     print(json.dumps(line), flush=True)
 
 
@@ -168,7 +237,7 @@ def run_ours(args):
     tp_mode = world > 1 and args.tp
     comm = None
     t0 = time.time()
-    g = synth.build(CONFIG, **({"n_layers": args.layers} if args.layers else {}))
+    g = synth.build(CONFIG, **shape_overrides(args))
     t_gen = time.time() - t0
     t0 = time.time()
     if tp_mode:
@@ -345,12 +414,10 @@ def run_ours(args):
         "scaling": "strong" if tp_mode else "weak", "vs_baseline": None,
         "dtype": "q4_k/q6_k weights, f16 tensor-core math, f32 accumulate",
         "data": "synthetic (seeded N(0,0.02) weights quantised Q4_K_M; seeded uniform prompt ids)",
-        "config": {"workload": "llama3-8b-shaped Q4_K_M: 1024-token prompt prefill, then batch-1 greedy decode"
-                               + (f" (profiling case: {L} layers)" if args.layers else ""),
-                   "model": "llama-3-8b-shaped", "global_batch": seqs, "seq_len": PROMPT,
-                   "parallelism": (f"tp{world} (NCCL all-reduce after Wo and W2)" if tp_mode
-                                   else f"replicas x{world}" if world > 1 else "single GPU"),
-                   "l2": "no flush needed: 4.6 GB of weights per step >> 126 MB L2"},
+        "config": bench_config(args),
+        "placement": (f"tp{world} (NCCL all-reduce after Wo and W2)" if tp_mode
+                      else f"replicas x{world}, one sequence per GPU" if world > 1 else "single GPU"),
+        "global_batch": seqs,
         "hbm_roofline": {"bytes_per_step": step_bytes, "achieved_gbs": step_gbs, "peak_gbs": hbm,
                          "frac": step_gbs / hbm, "peak": peak_kind,
                          "roofline_tok_s": hbm * 1e9 / step_bytes},
@@ -418,6 +485,8 @@ def main():
                     help="one independent sequence per GPU (the default with several GPUs)")
     ap.add_argument("--no-tp-leg", action="store_true",
                     help="with several GPUs: skip the tensor-parallel leg")
+    ap.add_argument("--vocab", type=int, default=0,
+                    help="testing only: an 8B-shaped model with this vocabulary size (0 = 128256)")
     ap.add_argument("--layers", type=int, default=0,
                     help="profiling only: an 8B-shaped model with this many layers "
                          "(0 = the full 32); the line's config names it")

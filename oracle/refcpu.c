@@ -878,6 +878,26 @@ int rc_model_tensor_info(const rc_model *m, const char *name, int *type,
 
 /* Weights::tensor_f32_by_index (weights.rs:66-74): whole-tensor dequant into
  * a fresh buffer (caller frees). */
+/* The whole-tensor dequantisation of tensor_f32 split over g_threads threads
+ * at block boundaries (each element still goes through the same formula). */
+typedef struct {
+  int type;
+  const uint8_t *p;
+  float *out;
+  uint64_t nblocks, blk_elems, blk_bytes;
+  int st;
+} dq_ctx;
+static void dq_worker(void *vp, int t, int nt) {
+  dq_ctx *x = (dq_ctx *)vp;
+  uint64_t b0 = x->nblocks * (uint64_t)t / (uint64_t)nt, b1 = x->nblocks * (uint64_t)(t + 1) / (uint64_t)nt;
+  if (b1 <= b0) return;
+  int st = rc_dequantize(x->type, x->p + b0 * x->blk_bytes, (size_t)((b1 - b0) * x->blk_bytes),
+                         x->out + b0 * x->blk_elems, (size_t)((b1 - b0) * x->blk_elems));
+  if (st) x->st = st;
+}
+
+/* Weights::tensor_f32_by_index (weights.rs:66-74): a fresh zeroed buffer of
+ * the whole tensor, dequantised (dequant.rs:34-38). */
 static int tensor_f32(const rc_model *m, int idx, float **out) {
   const uint8_t *p;
   size_t nb;
@@ -885,7 +905,17 @@ static int tensor_f32(const rc_model *m, int idx, float **out) {
   if (st) return st;
   uint64_t n = n_elem(&m->ti[idx]);
   float *buf = (float *)calloc(n ? n : 1, sizeof(float));
-  st = rc_dequantize(m->ti[idx].type, p, nb, buf, (size_t)n);
+  const int type = m->ti[idx].type;
+  const uint64_t be = (type == RC_Q4_0 || type == RC_Q8_0) ? 32
+                      : (type == RC_Q4K || type == RC_Q6K || type == RC_Q8K) ? 256 : 1;
+  const int64_t bb = rc_type_byte_size(type, be);
+  if (g_threads > 1 && bb > 0 && n % be == 0 && (uint64_t)nb == n / be * (uint64_t)bb) {
+    dq_ctx x = {type, p, buf, n / be, be, (uint64_t)bb, 0};
+    par_run(dq_worker, &x, (size_t)(n / be));
+    st = x.st;
+  } else {
+    st = rc_dequantize(type, p, nb, buf, (size_t)n);
+  }
   if (st) { free(buf); return st; }
   *out = buf;
   return RC_OK;

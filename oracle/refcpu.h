@@ -144,6 +144,18 @@ int rc_forward(const rc_model *m, const uint32_t *ids, size_t n,
 int rc_generate(const rc_model *m, rc_kv *kv, const uint32_t *prompt,
                 size_t n_prompt, size_t max_tokens, uint32_t *out);
 
+/* Synthetic benchmark models (synth_ref.c): the workload definition of the
+ * benchmark, independent of the product's generator. */
+typedef struct {
+  uint32_t vocab, dim, n_layers, n_heads, n_kv_heads, ffn, context;
+  float rope_base, norm_eps, sigma;
+  int mix, tied;
+  uint64_t seed;
+  int threads;
+} rc_synth_spec;
+int rc_synth_gguf(const rc_synth_spec *spec, uint8_t **out, size_t *out_len);
+void rc_synth_free(uint8_t *p);
+
 #ifdef __cplusplus
 }
 #endif

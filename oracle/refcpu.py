@@ -51,6 +51,31 @@ class RcConfig(C.Structure):
     ]
 
 
+class RcSynthSpec(C.Structure):
+    _fields_ = [
+        ("vocab", C.c_uint32), ("dim", C.c_uint32), ("n_layers", C.c_uint32),
+        ("n_heads", C.c_uint32), ("n_kv_heads", C.c_uint32), ("ffn", C.c_uint32),
+        ("context", C.c_uint32), ("rope_base", C.c_float), ("norm_eps", C.c_float),
+        ("sigma", C.c_float), ("mix", C.c_int), ("tied", C.c_int), ("seed", C.c_uint64),
+        ("threads", C.c_int),
+    ]
+
+
+# The benchmark's model shapes (the workload definition; mix 0 = all Q8_0,
+# 1 = Q4_K_M). Kept beside the oracle so the reference arm needs nothing from
+# the product package; a CPU test checks they equal the product's table.
+BENCH_CONFIGS = {
+    "tiny": dict(vocab=32000, dim=288, n_layers=6, n_heads=6, n_kv_heads=6, ffn=768, context=256,
+                 rope_base=10000.0, mix=0, tied=0),
+    "1b": dict(vocab=128256, dim=2048, n_layers=16, n_heads=32, n_kv_heads=8, ffn=8192,
+               context=4096, rope_base=500000.0, mix=1, tied=1),
+    "8b": dict(vocab=128256, dim=4096, n_layers=32, n_heads=32, n_kv_heads=8, ffn=14336,
+               context=4096, rope_base=500000.0, mix=1, tied=0),
+    "70b": dict(vocab=32000, dim=8192, n_layers=80, n_heads=64, n_kv_heads=8, ffn=28672,
+                context=4096, rope_base=10000.0, mix=1, tied=0),
+}
+
+
 def build() -> str:
     """Compile the oracle with its Makefile (idempotent)."""
     subprocess.run(["make", "-s", "-C", _HERE], check=True)
@@ -113,6 +138,9 @@ def lib():
         L.rc_decode_step.argtypes = [C.c_void_p, C.c_void_p, C.c_uint32, fp]
         L.rc_forward.argtypes = [C.c_void_p, u32p, sz, fp]
         L.rc_generate.argtypes = [C.c_void_p, C.c_void_p, u32p, sz, sz, u32p]
+        L.rc_synth_gguf.argtypes = [C.POINTER(RcSynthSpec), C.POINTER(C.POINTER(C.c_uint8)),
+                                    C.POINTER(C.c_size_t)]
+        L.rc_synth_free.argtypes = [C.POINTER(C.c_uint8)]
         _lib = L
     return _lib
 
@@ -239,6 +267,28 @@ def set_threads(n: int):
 
 def set_faithful(on: bool):
     lib().rc_set_faithful(1 if on else 0)
+
+
+def synth_gguf(name: str | None = None, seed: int = 1234, threads: int = 0,
+               **overrides) -> np.ndarray:
+    """A benchmark model as a GGUF image (synth_ref.c), e.g. synth_gguf("8b")."""
+    cfg = dict(BENCH_CONFIGS[name]) if name else {}
+    cfg.update(overrides)
+    sp = RcSynthSpec(vocab=cfg["vocab"], dim=cfg["dim"], n_layers=cfg["n_layers"],
+                     n_heads=cfg["n_heads"], n_kv_heads=cfg["n_kv_heads"], ffn=cfg["ffn"],
+                     context=cfg.get("context", 4096), rope_base=cfg.get("rope_base", 10000.0),
+                     norm_eps=cfg.get("norm_eps", 1e-5), sigma=cfg.get("sigma", 0.02),
+                     mix=cfg.get("mix", 1), tied=cfg.get("tied", 0), seed=seed,
+                     threads=threads if threads > 0 else (os.cpu_count() or 1))
+    p = C.POINTER(C.c_uint8)()
+    n = C.c_size_t()
+    _chk(lib().rc_synth_gguf(C.byref(sp), C.byref(p), C.byref(n)), "synth_gguf")
+    try:
+        out = np.empty(n.value, np.uint8)
+        C.memmove(out.ctypes.data, p, n.value)
+    finally:
+        lib().rc_synth_free(p)
+    return out
 
 
 class GgufFile:

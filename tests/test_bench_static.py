@@ -38,3 +38,36 @@ def test_imported_modules_are_not_rebound():
 def test_help_runs_without_a_gpu():
     r = subprocess.run([sys.executable, BENCH, "--help"], capture_output=True, text=True, timeout=120)
     assert r.returncode == 0 and "--gpus" in r.stdout and "--impl" in r.stdout
+
+
+def test_prompts_match_the_product_generator():
+    import numpy as np
+
+    sys.path.insert(0, ROOT)
+    import bench
+    from inferox_b200 import synth
+    for v, n, s in ((128256, 1024, 0), (32000, 17, 3)):
+        assert np.array_equal(bench.prompt_ids(v, n, s), synth.prompt_ids(v, n, seq_index=s))
+
+
+def test_reference_arm_loads_only_the_oracle():
+    """`--impl reference` on a 1-layer, 4096-token-vocabulary cut of the 8B
+    shape: it prints its line
+    with the requested steps and warm-up, the same config the GPU arm reports,
+    and neither imports the product package nor maps its library."""
+    code = (
+        "import json, runpy, sys\n"
+        f"sys.argv = ['bench.py', '--impl', 'reference', '--layers', '1', '--vocab', '4096', '--steps', '2', '--warmup', '3']\n"
+        f"runpy.run_path({BENCH!r}, run_name='__main__')\n"
+        "maps = open('/proc/self/maps').read()\n"
+        "print(json.dumps({'pkg': 'inferox_b200' in sys.modules, 'so': 'libinferox_b200' in maps,"
+        " 'oracle': 'librefcpu' in maps}))\n")
+    r = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True, timeout=900, cwd=ROOT)
+    assert r.returncode == 0, r.stderr[-2000:]
+    import json
+    lines = [json.loads(x) for x in r.stdout.splitlines() if x.startswith("{")]
+    line, seen = lines[0], lines[-1]
+    assert seen == {"pkg": False, "so": False, "oracle": True}
+    assert line["impl"] == "reference" and line["steps"] == 2 and line["warmup"] == 3
+    assert line["config"]["decode_context"] == [1027, 1029]
+    assert line["cpu_baseline"]["cores"] >= 1 and line["value"] > 0
