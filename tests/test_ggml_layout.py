@@ -115,3 +115,25 @@ def test_type_ids_and_errors():
     raw = bytes(range(64))
     conv, tt, sg = convert(0, raw)  # F32: copied
     assert conv == raw and tt == 0 and sg == 0
+
+
+@pytest.mark.parametrize("ggml_type", [2, 8, 12, 14])
+def test_restatement_pinned_by_llama_cpp_gguf_py(ggml_type):
+    """oracle/ggml_ref.py decodes llama.cpp's blocks exactly as llama.cpp's own
+    Python package does (gguf-py 0.19.0, gguf.quants.dequantize, installed in
+    this image): random block bytes with finite f16 scales, every type the
+    ggml load path takes, bit for bit. Q6_K scale bytes take both signs."""
+    gguf = pytest.importorskip("gguf")
+    from gguf import quants
+
+    elems, nbytes = G.BLOCK[ggml_type]
+    nb = 400
+    rng = np.random.default_rng(ggml_type)
+    raw = rng.integers(0, 256, size=(nb, nbytes), dtype=np.uint8)
+    scale_offsets = {2: [0], 8: [0], 12: [0, 2], 14: [208]}[ggml_type]
+    for off in scale_offsets:
+        raw[:, off:off + 2] = (rng.standard_normal(nb) * 0.01).astype(np.float16).view(np.uint8).reshape(nb, 2)
+    raw = raw.reshape(-1)
+    ours = G.dequant(ggml_type, raw)
+    theirs = quants.dequantize(raw.reshape(nb, nbytes), gguf.GGMLQuantizationType(ggml_type))
+    assert np.array_equal(ours, theirs.reshape(-1).astype(np.float32))

@@ -1,13 +1,15 @@
 """A llama.cpp-written GGUF (ggml type ids and block orders, int8 Q6_K scales
 of both signs) loaded with kquant_layout="ggml", against the CPU oracle.
 
-The file is built here: Q4_K weights quantised by the library and rewritten
-in ggml's nibble order, Q6_K weights from a quantiser that gives each
-16-element group a scale of random sign (as llama.cpp's own quantiser
-does), Q8_0 under ggml's id 8 for ffn_up beside a Q4_K ffn_gate (a unit
-width of 128 beside 256, so the fused gate/up GEMV runs as two plans). The
-oracle runs the same weights decoded by
-ggml's formulas (oracle/ggml_ref.py) and stored as F32 tensors, so the
+The file is written by llama.cpp's own writer (gguf-py's GGUFWriter): Q8_0
+blocks from gguf-py's quantiser under ggml's id 8 for ffn_up beside a Q4_K
+ffn_gate (a unit width of 128 beside 256, so the fused gate/up GEMV runs as
+two plans); Q4_K weights quantised by the library and rewritten in ggml's
+nibble order, Q6_K weights from a quantiser that gives each 16-element
+group a scale of random sign (as llama.cpp's own quantiser does) — gguf-py
+has no K-quant quantiser, so these blocks are checked by decoding them with
+gguf-py. The oracle runs the same weights decoded by gguf-py's dequantiser
+(llama.cpp's formulas) and stored as F32 tensors, so the
 comparison covers the load-time permutation, the int8 scale reading in the
 GEMV (persistent decode kernel), the tcgen05 prefill GEMM, the small-batch
 GEMM and the embedding gather, at the logits bar |gpu - ref| <= 2e-2 +
@@ -15,12 +17,16 @@ GEMM and the embedding gather, at the logits bar |gpu - ref| <= 2e-2 +
 gather and the output projection both read int8 scales).
 """
 import os
+import tempfile
 
 import numpy as np
 import pytest
 
 from gguf_builder import GgufBuilder, llama_meta
 from inferox_b200 import IfxError, Model, synth
+
+gguf = pytest.importorskip("gguf")
+from gguf import quants as ggq  # noqa: E402
 from oracle import ggml_ref as G
 from oracle import refcpu as R
 
@@ -49,28 +55,47 @@ def _models(tied: bool):
                  (p + "attn_v.weight", KVH * hd, D, 14), (p + "attn_output.weight", D, D, 12),
                  (p + "ffn_gate.weight", F, D, 12), (p + "ffn_up.weight", F, D, 8),
                  (p + "ffn_down.weight", D, F, 14 if l % 2 == 0 else 12)]
-    g_ggml, g_f32 = GgufBuilder(), GgufBuilder()
-    for g in (g_ggml, g_f32):
-        llama_meta(g, V, D, L, H, KVH, F, CTX, rope_base=500000.0)
+    g_f32 = llama_meta(GgufBuilder(), V, D, L, H, KVH, F, CTX, rope_base=500000.0)
+    w = gguf.GGUFWriter(path=None, arch="llama")
+    w.add_uint32("llama.vocab_size", V)
+    w.add_uint32("llama.embedding_length", D)
+    w.add_uint32("llama.block_count", L)
+    w.add_uint32("llama.attention.head_count", H)
+    w.add_uint32("llama.attention.head_count_kv", KVH)
+    w.add_uint32("llama.feed_forward_length", F)
+    w.add_float32("llama.attention.layer_norm_rms_epsilon", 1e-5)
+    w.add_uint32("llama.context_length", CTX)
+    w.add_float32("llama.rope.freq_base", 500000.0)
     norms = {"output_norm.weight": D}
     for l in range(L):
         norms[f"blk.{l}.attn_norm.weight"] = D
         norms[f"blk.{l}.ffn_norm.weight"] = D
     for name, n in norms.items():
-        w = (1.0 + rng.normal(0, 0.05, n)).astype(np.float32)
-        g_ggml.tensor_f32(name, [n], w)
-        g_f32.tensor_f32(name, [n], w)
+        v = (1.0 + rng.normal(0, 0.05, n)).astype(np.float32)
+        w.add_tensor(name, v)
+        g_f32.tensor_f32(name, [n], v)
     for name, rows, cols, t in mats:
         x = rng.normal(0, 0.02, rows * cols).astype(np.float32)
         if t == 12:
-            raw = G.q4k_reference_to_ggml(synth.quantize(12, x))
+            raw = np.frombuffer(G.q4k_reference_to_ggml(synth.quantize(12, x)), np.uint8)
         elif t == 14:
-            raw = G.quantize_q6k_ggml(x, rng)
+            raw = np.frombuffer(G.quantize_q6k_ggml(x, rng), np.uint8)
         else:
-            raw = synth.quantize(7, x)  # Q8_0 bytes are the same in both formats
-        g_ggml.tensor(name, [cols, rows], t, raw)
-        g_f32.tensor_f32(name, [cols, rows], G.dequant(t, raw))
-    return g_ggml.build(), g_f32.build()
+            raw = ggq.quantize(x.reshape(rows, cols), gguf.GGMLQuantizationType.Q8_0).reshape(-1)
+        qt = gguf.GGMLQuantizationType(t)
+        w.add_tensor(name, raw.reshape(rows, -1), raw_dtype=qt)
+        vals = ggq.dequantize(raw.reshape(rows, -1), qt).reshape(-1).astype(np.float32)
+        assert np.array_equal(vals, G.dequant(t, raw))  # the restatement agrees
+        g_f32.tensor_f32(name, [cols, rows], vals)
+    with tempfile.TemporaryDirectory() as d:
+        path = os.path.join(d, "llama.gguf")
+        w.path = path
+        w.write_header_to_file(path=path)
+        w.write_kv_data_to_file()
+        w.write_tensors_to_file()
+        w.close()
+        data = open(path, "rb").read()
+    return np.frombuffer(data, np.uint8), g_f32.build()
 
 
 @pytest.mark.parametrize("tied", [False, True])
