@@ -5,7 +5,8 @@
  * The reference is a Rust crate with no FFI; its call surface is the Rust API
  * of `ops`, `model` and `sampler`. Each entry point below names the reference
  * item it replaces (path:line inside the reference crate). A Rust `cuda`
- * module would bind these with `extern "C"` declarations.
+ * module binds these with the `extern "C"` declarations of inferox_ffi.rs
+ * (next to this header).
  *
  * Conventions
  *  - Every call returns ifx_status; IFX_OK is 0. ifx_last_error() gives a
@@ -205,7 +206,9 @@ ifx_status ifx_decode_step_batch(ifx_model *m, ifx_kv_batch *kb,
  * one decode step of the n distinct sequences seqs[0..n) only, for a
  * serving loop whose requests come and go (continuous batching); the other
  * sequences keep their caches and lengths. Row i of logits_host [n, vocab]
- * and argmax_host [n] (both nullable) belongs to seqs[i]. */
+ * and argmax_host [n] (both nullable) belongs to seqs[i]. After an error
+ * from a device wait (IFX_ERR_TIMEOUT) the listed sequences' caches are in
+ * an undefined state: reset them (ifx_kv_batch_reset) before reuse. */
 ifx_status ifx_decode_step_batch_seqs(ifx_model *m, ifx_kv_batch *kb,
                                       const int *seqs, int n,
                                       const uint32_t *tokens,
@@ -302,7 +305,9 @@ ifx_status ifx_op_sample_u(const float *logits_dev, size_t n,
  * first call could fall inside a stream capture, make one call on the device
  * before the capture begins. Every call on a device uses the same scratch:
  * calls whose work overlaps in time (other streams, other threads) race, so
- * order them on one stream or serialise them. */
+ * order them on one stream or serialise them. The looked-up address belongs
+ * to the device's current context: after cudaDeviceReset on a device, unload
+ * and reload this library before calling it again on that device. */
 #define IFX_SAMPLE_STATIC_MAX 262144
 ifx_status ifx_op_sample_u_static(const float *logits_dev, size_t n,
                                   const ifx_sampler *s, float u,

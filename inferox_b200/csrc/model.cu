@@ -299,6 +299,9 @@ ifx_status Model::load(const uint8_t *bytes, size_t len, const ifx_load_opts &o)
   if (cfg.vocab_size == 0) return fail(IFX_ERR_SHAPE, "llama.vocab_size is missing or zero");
   const uint64_t D = cfg.hidden_size, H = cfg.n_heads, G = cfg.n_kv_heads, hd = cfg.head_dim;
   const uint64_t F = cfg.intermediate_size, V = cfg.vocab_size;
+  // G == 0 first: the remainder below (and every later H / G) would divide
+  // by zero (the reference's integer division panics there)
+  if (G == 0) return fail(IFX_ERR_SHAPE, "llama.attention.head_count_kv is 0");
   if (H * hd != D || H % G || hd % 2 || cfg.rope_dim > hd || cfg.rope_dim % 2)
     return fail(IFX_ERR_SHAPE, "unsupported head geometry");
   // Megatron split: q/k/v by heads, W1/W3 and the vocab by rows, Wo/W2 by

@@ -94,10 +94,16 @@ class Server:
             if self.slots[slot] is not None:
                 continue
             r = self.waiting.popleft()
-            if self.used[slot]:
-                self.kb.reset(slot)
-            self.used[slot] = True
-            logits = self.kb.prefill(slot, r.prompt, True)
+            try:
+                if self.used[slot]:
+                    self.kb.reset(slot)
+                self.used[slot] = True
+                logits = self.kb.prefill(slot, r.prompt, True)
+            except BaseException:
+                # the request is not lost: it waits at the front again (the
+                # slot is reset before its next use)
+                self.waiting.appendleft(r)
+                raise
             r.tokens.append(last_argmax(logits[0]))
             self.slots[slot] = r
             self._finish_if_done(slot)

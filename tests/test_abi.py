@@ -112,13 +112,17 @@ def test_model_load_rejects_bad_files_before_touching_a_gpu():
     assert _load_status(g.build()) == "TensorNotFound"  # no general.architecture
     g = llama_meta(GgufBuilder(), 100, 64, 1, 4, 4, 128, 32)
     assert _load_status(g.build()) == "TensorNotFound"  # blk.0.* missing
+    # zero kv heads: a Shape error, never an integer division by zero
+    g = llama_meta(GgufBuilder(), 100, 64, 1, 4, 0, 128, 32)
+    assert _load_status(g.build()) == "Shape"
 
 
-def test_integration_binding_declares_every_entry_point():
-    """The Rust extern block a maintainer copies covers the header."""
+def test_rust_binding_declares_every_entry_point():
+    """The Rust extern block a maintainer copies into the reference crate
+    (include/inferox_ffi.rs) declares every entry point of the header."""
     import re
-    doc = open(os.path.join(ROOT, "INTEGRATION.md")).read()
-    declared = set(re.findall(r"pub fn (ifx_[a-z0-9_]+)", doc))
+    src = open(os.path.join(ROOT, "include", "inferox_ffi.rs")).read()
+    declared = set(re.findall(r"pub fn (ifx_[a-z0-9_]+)", src))
     assert set(inferox_b200.header_symbols()) == declared
 
 

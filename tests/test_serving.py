@@ -110,3 +110,31 @@ def test_limits():
     steps = srv.steps
     srv.run()
     assert srv.result(one) == _alone([4, 5], 1) and srv.steps == steps
+
+
+def test_failed_prefill_keeps_the_request():
+    """A prefill that raises (a CUDA or cache error) leaves the request
+    waiting at the front; once the cause is gone it is served as if nothing
+    had happened, in a slot that was reset first."""
+
+    class Flaky(FakeBatch):
+        fail = 1
+
+        def prefill(self, slot, ids, last_row_only=False):
+            if self.fail:
+                self.fail -= 1
+                self.hist[slot].extend([1, 2, 3])  # partial work left behind
+                raise RuntimeError("device error")
+            return super().prefill(slot, ids, last_row_only)
+
+    fb = Flaky(2, 64)
+    srv = Server(fb)
+    prompt = [5, 9, 11]
+    rid = srv.submit(prompt, 6)
+    with pytest.raises(RuntimeError):
+        srv.step()
+    assert srv.result(rid) is None and len(srv.waiting) == 1
+    while srv.busy():
+        srv.step()
+    assert srv.result(rid) == _alone(prompt, 6)
+    assert fb.resets == [0]  # the slot the failed prefill touched was reset
