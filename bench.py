@@ -40,6 +40,13 @@ METRIC = "decode tok/s @8B Q4_K_M batch 1 as % of HBM roofline; prefill tok/s"
 TRAFFIC_PER_ALGO_BYTE = 1.019
 
 
+def bf16_peak():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        return float(json.load(open(p))["bf16_tflops"])
+    return 1590.0
+
+
 def peaks():
     p = os.path.join(ROOT, "MEASURED_PEAKS.json")
     if os.path.exists(p):
@@ -385,6 +392,12 @@ def run_ours(args):
         if tcomm is not None:
             tcomm.close()
 
+    # the dequant-fused matmul microbench at the 8B W1 shape (every type and
+    # batch; the full table is `--microbench`)
+    micro = None
+    if not args.no_microbench and rank == 0 and not tp_mode:
+        micro = run_microbench([(14336, 4096)], reps=3)
+
     # whole-step algorithmic bytes: every weight once + K/V at the mean context
     ctx_mean = ctx0 + args.steps / 2
     # per GPU: under tensor parallelism each rank reads its shard of the
@@ -423,6 +436,7 @@ def run_ours(args):
                          "roofline_tok_s": hbm * 1e9 / step_bytes},
         "prefill": {"tokens": PROMPT, "s": prefill_s, "tok_s": PROMPT / prefill_s},
         "batched_decode": batch,
+        "matmul_microbench": micro,
         "tensor_parallel": tpleg,
         # the dominant kernel is the decode step itself: with the persistent
         # path one launch per token, so achieved = algorithmic step bytes over
@@ -441,6 +455,63 @@ def run_ours(args):
     }
     print(json.dumps(line), flush=True)
     finish()
+
+
+MB_TYPES = {"Q4_0": (2, 4.5), "Q8_0": (7, 8.5), "Q4_K": (12, 4.5), "Q6_K": (14, 6.5625)}
+MB_SHAPES = [(4096, 4096), (14336, 4096), (4096, 14336), (128256, 4096)]
+MB_BATCHES = [1, 8, 64, 512]
+
+
+def _quantize_parallel(ttype: int, x, block: int):
+    """Host quantisation of a large matrix in block-aligned chunks on every
+    core (the library's quantiser releases the GIL through ctypes)."""
+    from concurrent.futures import ThreadPoolExecutor
+
+    import numpy as np
+    from inferox_b200 import synth
+    nblk = x.size // block
+    cores = len(os.sched_getaffinity(0))
+    parts = max(1, min(cores * 2, nblk // 4096))
+    cuts = [x.size * i // parts // block * block for i in range(parts)] + [x.size]
+    with ThreadPoolExecutor(max_workers=cores) as ex:
+        out = list(ex.map(lambda i: synth.quantize(ttype, x[cuts[i]:cuts[i + 1]]), range(parts)))
+    return np.frombuffer(b"".join(out), np.uint8)
+
+
+def run_microbench(shapes, reps: int = 5):
+    """the dequant-fused matmul (what replaces tensor_f32_by_index
+    + matmul_t, src/gguf/dequant.rs:62-199 + src/ops.rs:33-44) for Q4_0, Q8_0,
+    Q4_K and Q6_K weights drawn N(0, 0.02), activations N(0, 1), at batch 1,
+    8, 64 and 512: ms per call (input staging included, weights from HBM),
+    algorithmic GB/s (weights + activations + outputs) against the measured
+    HBM peak and useful TFLOP/s against the measured bf16 peak."""
+    import numpy as np
+    import torch
+    from inferox_b200 import ops
+    hbm, _ = peaks()
+    tflops_peak = bf16_peak()
+    rng = np.random.default_rng(0)
+    rows_out = []
+    for rows, cols in shapes:
+        w = (rng.standard_normal(rows * cols, dtype=np.float32) * np.float32(0.02))
+        for tname, (ttype, bpw) in MB_TYPES.items():
+            blk = 256 if ttype in (12, 14) else 32
+            W = ops.QMatrix(ttype, _quantize_parallel(ttype, w, blk), rows, cols)
+            for B in MB_BATCHES:
+                x = torch.from_numpy(rng.standard_normal(B * cols, dtype=np.float32)).cuda()
+                ms = ops.bench_matmul_t_q(x, W, B, reps)
+                nbytes = rows * cols * bpw / 8 + 4 * B * (rows + cols)
+                fl = 2.0 * B * rows * cols
+                kernel = ("gemv_b1_kernel" if B == 1 else "gemm_kernel (small batch)" if B <= 32
+                          else "tc_gemm_kernel (tcgen05)")
+                rows_out.append({"type": tname, "shape": [rows, cols], "batch": B, "kernel": kernel,
+                                 "ms": ms, "gbs": nbytes / (ms * 1e-3) / 1e9,
+                                 "hbm_frac": nbytes / (ms * 1e-3) / 1e9 / hbm,
+                                 "tflops": fl / (ms * 1e-3) / 1e12,
+                                 "tensor_frac": fl / (ms * 1e-3) / 1e12 / tflops_peak})
+            del W
+        del w
+    return rows_out
 
 
 def run_gemm_case(spec: str):
@@ -485,6 +556,11 @@ def main():
                     help="one independent sequence per GPU (the default with several GPUs)")
     ap.add_argument("--no-tp-leg", action="store_true",
                     help="with several GPUs: skip the tensor-parallel leg")
+    ap.add_argument("--microbench", action="store_true",
+                    help="only the dequant-fused matmul microbench: 4 types x 4 shapes x batch "
+                         "1/8/64/512, one JSON line")
+    ap.add_argument("--no-microbench", action="store_true",
+                    help="skip the one-shape microbench leg of the default run")
     ap.add_argument("--vocab", type=int, default=0,
                     help="testing only: an 8B-shaped model with this vocabulary size (0 = 128256)")
     ap.add_argument("--layers", type=int, default=0,
@@ -495,6 +571,11 @@ def main():
         args.warmup = 3
     if args.gemm:
         run_gemm_case(args.gemm)
+    elif args.microbench:
+        rows = run_microbench(MB_SHAPES)
+        print(json.dumps({"metric": "dequant-fused matmul microbench (configs[1])", "unit": "GB/s | TFLOP/s",
+                          "peaks": {"hbm_gbs": peaks()[0], "bf16_tflops": bf16_peak()},
+                          "rows": rows}), flush=True)
     elif args.impl == "reference":
         run_reference(args)
     else:

@@ -339,6 +339,16 @@ ifx_status ifx_tp_shard(int type, const void *gguf_bytes, size_t nbytes,
  * count (3 + 5 * n_layers). Meaningful once the cache has been decoded into
  * (the persistent plan is built by the first decode step); 0 before that. */
 int ifx_kv_decode_kernels(const ifx_kv *kv);
+/* No reference counterpart (measurement of what replaces
+ * tensor_f32_by_index + matmul_t, forward.rs:366-368 / ops.rs:33-44): time
+ * the fused dequant matmul the token loop runs at batch m — the batch-1 GEMV
+ * for m = 1, the small-batch GEMM for m <= 32, the prefill GEMM above — with
+ * its input staging, `reps` launches each timed alone by CUDA events, with a
+ * 256 MB buffer written between launches so the weights come from HBM.
+ * a_dev [m, cols], c_dev [m, rows] (device). Reports ms per call. */
+ifx_status ifx_bench_matmul_t_q(const float *a_dev, const ifx_qmatrix *w,
+                                float *c_dev, size_t m, int reps,
+                                float *ms_per_call);
 /* No reference counterpart. Launch one of the decode step's fused kernels
  * `reps` times in isolation (cycling through the layers so the weights come
  * from HBM, not L2) and report the CUDA-event time per launch and the

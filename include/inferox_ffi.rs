@@ -69,6 +69,8 @@ extern "C" {
                       out: *mut u32) -> c_int;
     pub fn ifx_decode_greedy(m: *mut IfxModel, kv: *mut IfxKv, token: u32, n_steps: usize,
                              out: *mut u32, device_ms: *mut f32) -> c_int;
+    pub fn ifx_bench_matmul_t_q(a_dev: *const f32, w: *const IfxQMatrix, c_dev: *mut f32, m: usize,
+                                reps: c_int, ms_per_call: *mut f32) -> c_int;
     pub fn ifx_bench_kernel(m: *mut IfxModel, kv: *mut IfxKv, which: *const c_char, reps: c_int,
                             ms_per_launch: *mut f32, bytes_per_launch: *mut u64) -> c_int;
     // batched decode: `batch` independent caches, prefilled one by one, stepped together

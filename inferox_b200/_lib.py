@@ -123,6 +123,7 @@ def _load():
         "ifx_qmatrix_create": (st, [C.c_int, vp, sz, sz, sz, C.c_int, C.POINTER(vp)]),
         "ifx_qmatrix_free": (None, [vp]),
         "ifx_op_matmul_t_q": (st, [vp, vp, vp, sz, vp]),
+        "ifx_bench_matmul_t_q": (st, [vp, vp, vp, sz, C.c_int, fp]),
         "ifx_op_rms_norm_rows": (st, [vp, vp, C.c_float, sz, sz, vp]),
         "ifx_op_silu": (st, [vp, sz, vp]),
         "ifx_op_swiglu": (st, [vp, vp, vp, sz, vp]),

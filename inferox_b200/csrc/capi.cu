@@ -417,6 +417,87 @@ ifx_status ifx_op_matmul_t_q(const float *a_dev, const ifx_qmatrix *w, float *c_
   return s;
 }
 
+// Times the fused dequant matmul the token loop runs at batch m: the batch-1
+// GEMV (x staged inside the kernel), the small-batch GEMM for m <= 32 (decode
+// of several sequences) or the prefill GEMM above that, each with its input
+// staging launch. Every timed launch is bracketed by its own events; between
+// launches a 256 MB buffer is written so the weights come from HBM.
+static ifx_status bench_matmul_t_q(const float *a_dev, const QMatrix &W, float *c_dev, size_t m,
+                                 int reps, float *ms_per_call) {
+  IFX_CUDA(cudaSetDevice(W.device));
+  cudaStream_t st = nullptr;
+  IFX_CUDA(cudaStreamCreateWithFlags(&st, cudaStreamNonBlocking));
+  constexpr size_t kFlush = 256ull << 20;
+  int *err = nullptr;
+  void *flush = nullptr, *xf = nullptr;
+  GemvPlan p;
+  bool planned = false;
+  cudaEvent_t e0 = nullptr, e1 = nullptr;
+  float total = 0.f;
+  ifx_status s = IFX_OK;
+  auto cuda_ok = [&](cudaError_t e, const char *what) {
+    if (e != cudaSuccess && s == IFX_OK) s = cuda_fail(e, what);
+    return s == IFX_OK;
+  };
+  if (cuda_ok(cudaMalloc(&err, sizeof(int)), "cudaMalloc") &&
+      cuda_ok(cudaMemsetAsync(err, 0, sizeof(int), st), "cudaMemset") &&
+      cuda_ok(cudaMalloc(&flush, kFlush), "cudaMalloc") && cuda_ok(cudaEventCreate(&e0), "event") &&
+      cuda_ok(cudaEventCreate(&e1), "event")) {
+    const int64_t M = (int64_t)m, K = W.L.cols, R = W.L.rows;
+    const bool small = m > 1 && M <= kGemmSmallMax;
+    if (m == 1) {
+      const QMatrix *mats[1] = {&W};
+      float *ys[1] = {c_dev};
+      s = gemv_plan(mats, ys, 1, GEMV_PLAIN, a_dev, nullptr, nullptr, 0.f, err, &p);
+      planned = s == IFX_OK;
+    } else {
+      cuda_ok(cudaMalloc(&xf, small ? gemm_small_xfrag_bytes(M, K) : gemm_xfrag_bytes(M, K)), "cudaMalloc");
+    }
+    for (int r = -1; r < reps && s == IFX_OK; ++r) {  // r = -1: untimed first launch
+      // outputs the kernels accumulate into start at zero (outside the timing)
+      if (m == 1 || small) cuda_ok(cudaMemsetAsync(c_dev, 0, sizeof(float) * (size_t)(M * R), st), "cudaMemset");
+      cuda_ok(cudaMemsetAsync(flush, r & 0xff, kFlush, st), "cudaMemset");
+      if (s != IFX_OK) break;
+      cuda_ok(cudaEventRecord(e0, st), "event");
+      if (m == 1) {
+        s = gemv_launch(p, st, false);
+      } else if (small) {
+        s = gemm_small_stage_x(a_dev, nullptr, nullptr, 0.f, GX_PLAIN, M, K, xf, st);
+        if (s == IFX_OK) s = gemm_small_run(W, xf, M, c_dev, R, err, st);
+      } else {
+        s = gemm_stage_x(a_dev, nullptr, nullptr, 0.f, GX_PLAIN, M, K, xf, st);
+        if (s == IFX_OK) s = gemm_run(W, xf, M, c_dev, R, 0, err, st);
+      }
+      if (s != IFX_OK || !cuda_ok(cudaEventRecord(e1, st), "event") ||
+          !cuda_ok(cudaEventSynchronize(e1), "event"))
+        break;
+      float t = 0.f;
+      cuda_ok(cudaEventElapsedTime(&t, e0, e1), "event");
+      if (r >= 0) total += t;
+    }
+    cudaStreamSynchronize(st);
+    int h = 0;
+    cuda_ok(cudaMemcpy(&h, err, sizeof(int), cudaMemcpyDeviceToHost), "cudaMemcpy");
+    if (s == IFX_OK && h) s = fail(IFX_ERR_TIMEOUT, "bench_matmul_t_q: a bounded device wait gave up");
+  }
+  if (planned) gemv_plan_free(&p);
+  if (e0) cudaEventDestroy(e0);
+  if (e1) cudaEventDestroy(e1);
+  cudaFree(xf);
+  cudaFree(flush);
+  cudaFree(err);
+  cudaStreamDestroy(st);
+  if (s == IFX_OK) *ms_per_call = total / (float)reps;
+  return s;
+}
+
+ifx_status ifx_bench_matmul_t_q(const float *a_dev, const ifx_qmatrix *w, float *c_dev, size_t m,
+                                int reps, float *ms_per_call) {
+  if (!a_dev || !w || !c_dev || !ms_per_call) return fail(IFX_ERR_INVALID_ARGUMENT, "bench_matmul_t_q: null");
+  if (m == 0 || reps < 1) return fail(IFX_ERR_INVALID_ARGUMENT, "bench_matmul_t_q: m and reps must be >= 1");
+  IFX_GUARD({ return bench_matmul_t_q(a_dev, w->q, c_dev, m, reps, ms_per_call); })
+}
+
 ifx_status ifx_op_rms_norm_rows(float *x, const float *w, float eps, size_t rows, size_t hidden,
                                 void *stream) {
   if (!x || !w) return fail(IFX_ERR_INVALID_ARGUMENT, "rms_norm_rows: null");

@@ -79,6 +79,17 @@ def matmul_t_q(a: torch.Tensor, w: QMatrix, m: int) -> torch.Tensor:
     return c
 
 
+def bench_matmul_t_q(a: torch.Tensor, w: QMatrix, m: int, reps: int = 10) -> float:
+    """ms per call of the fused dequant matmul the token loop runs at batch m
+    (GEMV at 1, small-batch GEMM up to 32, prefill GEMM above), each launch
+    timed alone with the weights coming from HBM."""
+    _need(a.numel() == m * w.cols, "bench_matmul_t_q shape mismatch")
+    c = torch.empty(m * w.rows, dtype=torch.float32, device=a.device)
+    ms = C.c_float(0.0)
+    check(lib.ifx_bench_matmul_t_q(_p(a), w._h, _p(c), m, reps, C.byref(ms)), "bench_matmul_t_q")
+    return float(ms.value)
+
+
 def rms_norm(x, w, eps):  # ops.rs:155-168 (in place)
     _need(x.numel() == w.numel(), "RMSNorm weight length mismatch")
     check(lib.ifx_op_rms_norm_rows(_p(x), _p(w), eps, 1, w.numel(), _s()), "rms_norm")
