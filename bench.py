@@ -31,9 +31,18 @@ import time
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
-CONFIG = "8b"
-PROMPT = 1024
 METRIC = "decode tok/s @8B Q4_K_M batch 1 as % of HBM roofline; prefill tok/s"
+# The workloads of BASELINE's configs 2-4 (--config): model shape, prompt
+# length, the smallest KV capacity the config names, and the batch of the
+# batched-decode leg (0: none). The default, 8b, is the headline metric's.
+WORKLOADS = {
+    "8b": dict(name="llama3-8b-shaped Q4_K_M", prompt=1024, min_ctx=0, batch=16),
+    "70b": dict(name="llama2-70b-shaped Q4_K_M", prompt=2048, min_ctx=4096, batch=32),
+    "1b": dict(name="llama3.2-1b-shaped Q4_K_M (tied embedding)", prompt=512, min_ctx=2048, batch=0),
+}
+# a faithful single-thread CPU step of these shapes takes minutes: their CPU
+# figures come from 1- and 2-layer cuts of the same width (see cpu_step_time)
+CPU_CUT = {"70b"}
 # DRAM bytes (read + write) per algorithmic byte of decode_mega_kernel, from
 # an ncu capture of the 4-layer 8B-shaped case (976.6 MB + 15.1 MB over
 # 973.2 MB); traffic scales with the weight bytes.
@@ -114,7 +123,7 @@ def prompt_ids(vocab: int, n: int, seq_index: int = 0, seed: int = 42):
 
 
 def shape_overrides(args) -> dict:
-    """Profiling / testing cuts of the 8B shape (--layers, --vocab)."""
+    """Profiling / testing cuts of the configured shape (--layers, --vocab)."""
     o = {}
     if args.layers:
         o["n_layers"] = args.layers
@@ -126,41 +135,65 @@ def shape_overrides(args) -> dict:
 def bench_config(args) -> dict:
     """The workload both arms run (identical dicts, so the driver can compare
     them): decode contexts start after the prompt and the warm-up steps."""
-    ctx0 = PROMPT + args.warmup
-    return {"workload": "llama3-8b-shaped Q4_K_M: 1024-token prompt prefill, then batch-1 greedy decode"
+    wl = WORKLOADS[args.config]
+    ctx0 = wl["prompt"] + args.warmup
+    return {"workload": f"{wl['name']}: {wl['prompt']}-token prompt prefill, then batch-1 greedy decode"
                         + (f" (profiling case: {args.layers} layers)" if args.layers else "")
                         + (f" (test case: vocabulary {args.vocab})" if args.vocab else ""),
-            "batch": 1, "prompt_tokens": PROMPT, "decode_context": [ctx0, ctx0 + args.steps],
-            "l2": "no flush needed: 4.6 GB of weights per step >> 126 MB L2"}
+            "batch": 1, "prompt_tokens": wl["prompt"], "decode_context": [ctx0, ctx0 + args.steps],
+            "l2": "no flush needed: the weights of one step are far larger than the 126 MB L2"}
 
 
-def cpu_baseline(gguf, steps: int = 1):
-    """The reference's CPU path (oracle port, faithful per-call whole-tensor
-    dequant, single thread as the reference runs) for `steps` decode steps
-    of the same model at the benchmark's context (the cache is first filled
-    by an untimed threaded prefill of the same 1024-token prompt)."""
+def cpu_step_time(make_gguf, n_layers: int, prompt: int, warmup: int, steps: int, threads: int):
+    """Seconds per faithful decode step of the oracle port (per-call
+    whole-tensor dequant + AVX2-order matmul_t, as the reference runs) at the
+    benchmark's context: the cache is first filled by an untimed prefill of
+    the same prompt (per-row dequant fused into the dots: the same bits, far
+    faster) and `warmup` faithful steps. make_gguf(n_layers) builds the model;
+    with n_layers = 0 the full model is timed, otherwise 1- and 2-layer cuts of
+    the same width, and the step time is extrapolated linearly to n_layers
+    (every layer costs the same; the embedding and output projection are the
+    fixed part)."""
     from oracle import refcpu as R
 
     cores = len(os.sched_getaffinity(0))
-    m = R.Model(gguf)
-    kv = m.kv_cache(int(m.config.n_layers), PROMPT + steps + 8)
-    R.set_threads(cores)
-    R.set_faithful(False)
-    lg = m.prefill(prompt_ids(m.vocab, PROMPT), kv, True)[0]
-    tok = R.argmax(lg)
-    R.set_threads(1)
-    R.set_faithful(True)
-    t0 = time.perf_counter()
-    for _ in range(steps):
-        lg = m.decode_step(tok, kv)
-        tok = R.argmax(lg)
-    dt = time.perf_counter() - t0
-    R.set_faithful(False)
-    R.set_threads(cores)
-    return {"value": steps / dt, "unit": "tok/s", "cores": 1, "kind": "port",
-            "sample": f"{steps} faithful decode step(s) of the 8B-shaped Q4_K_M model at context "
-                      f"{PROMPT}-{PROMPT + steps} (per-call whole-tensor dequant + AVX2 matmul_t, "
-                      "as the reference does), 1 host thread, as the reference runs"}
+
+    def one(gguf):
+        m = R.Model(gguf)
+        kv = m.kv_cache(int(m.config.n_layers), prompt + warmup + steps + 8)
+        R.set_threads(cores)
+        R.set_faithful(False)
+        tok = R.argmax(m.prefill(prompt_ids(m.vocab, prompt), kv, True)[0])
+        R.set_threads(threads)
+        R.set_faithful(True)
+        for _ in range(warmup):
+            tok = R.argmax(m.decode_step(tok, kv))
+        t0 = time.perf_counter()
+        for _ in range(steps):
+            tok = R.argmax(m.decode_step(tok, kv))
+        dt = (time.perf_counter() - t0) / steps
+        R.set_faithful(False)
+        R.set_threads(cores)
+        return dt
+
+    if not n_layers:
+        return one(make_gguf(0)), "the full model"
+    t1, t2 = one(make_gguf(1)), one(make_gguf(2))
+    return t1 + (n_layers - 1) * (t2 - t1), f"1- and 2-layer cuts extrapolated to {n_layers} layers"
+
+
+def cpu_baseline(args, make_gguf, n_layers: int):
+    """The reference's CPU path, single thread as the reference runs, on a
+    bounded sample of the workload: one faithful decode step at the
+    benchmark's context (the full model, or layer cuts for shapes whose full
+    step takes minutes)."""
+    wl = WORKLOADS[args.config]
+    cut = n_layers if args.config in CPU_CUT and not args.layers else 0
+    dt, what = cpu_step_time(make_gguf, cut, wl["prompt"], 0, 1, 1)
+    return {"value": 1.0 / dt, "unit": "tok/s", "cores": 1, "kind": "port",
+            "sample": f"1 faithful decode step of the {wl['name']} model at context {wl['prompt']} "
+                      f"({what}; per-call whole-tensor dequant + AVX2 matmul_t, as the reference does), "
+                      "1 host thread, as the reference runs"}
 
 
 def run_reference(args):
@@ -179,33 +212,26 @@ def run_reference(args):
 
     cores = len(os.sched_getaffinity(0))
     R.set_threads(cores)
+    wl = WORKLOADS[args.config]
+    full_layers = int(R.BENCH_CONFIGS[args.config]["n_layers"])
+    cut = full_layers if args.config in CPU_CUT and not args.layers else 0
     t0 = time.time()
-    g = R.synth_gguf(CONFIG, threads=cores, **shape_overrides(args))
-    m = R.Model(g)
-    L = int(m.config.n_layers)
-    kv = m.kv_cache(L, PROMPT + args.warmup + args.steps + 16)
-    # untimed: the cache brought to the GPU arm's context (prefill of the same
-    # prompt, per-row dequant fused into the dots: the same bits, far faster),
-    # then the W warm-up steps in the reference's own mode
-    R.set_faithful(False)
-    lg = m.prefill(prompt_ids(m.vocab, PROMPT), kv, True)[0]
-    tok = R.argmax(lg)
-    R.set_faithful(True)
-    for _ in range(args.warmup):
-        tok = R.argmax(m.decode_step(tok, kv))
+
+    def make(n):
+        o = shape_overrides(args)
+        if n:
+            o["n_layers"] = n
+        return R.synth_gguf(args.config, threads=cores, **o)
+
+    dt, what = cpu_step_time(make, cut, wl["prompt"], args.warmup, args.steps, cores)
     setup_s = time.time() - t0
-    ctx0 = len(kv)
-    t0 = time.perf_counter()
-    for _ in range(args.steps):
-        tok = R.argmax(m.decode_step(tok, kv))
-    dt = time.perf_counter() - t0
-    R.set_faithful(False)
-    value = args.steps / dt
-    sample = (f"{args.steps} decode steps (after {args.warmup} warm-up steps) of the 8B-shaped Q4_K_M model "
-              f"at context {ctx0}-{ctx0 + args.steps}, faithful mode (per-call whole-tensor dequant + "
-              f"AVX2-order matmul_t), {cores} host threads")
+    ctx0 = wl["prompt"] + args.warmup
+    value = 1.0 / dt
+    sample = (f"{args.steps} decode steps (after {args.warmup} warm-up steps) of the {wl['name']} model "
+              f"at context {ctx0}-{ctx0 + args.steps} ({what}), faithful mode (per-call whole-tensor "
+              f"dequant + AVX2-order matmul_t), {cores} host threads")
     line = {"metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": args.gpus,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000.0 * dt / args.steps,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000.0 * dt,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
             "data": "synthetic (seeded N(0,0.02) weights quantised Q4_K_M; seeded uniform prompt ids)",
             "impl": "reference", "config": bench_config(args),
@@ -244,7 +270,9 @@ def run_ours(args):
     tp_mode = world > 1 and args.tp
     comm = None
     t0 = time.time()
-    g = synth.build(CONFIG, **shape_overrides(args))
+    wl = WORKLOADS[args.config]
+    PROMPT = wl["prompt"]
+    g = synth.build(args.config, **shape_overrides(args))
     t_gen = time.time() - t0
     t0 = time.time()
     if tp_mode:
@@ -259,7 +287,7 @@ def run_ours(args):
     t_load = time.time() - t0
     cfg = m.config
     L, G, hd, V = int(cfg.n_layers), int(cfg.n_kv_heads), int(cfg.head_dim), int(cfg.vocab_size)
-    max_seq = PROMPT + 2 * (args.warmup + args.steps) + 16
+    max_seq = max(wl["min_ctx"], PROMPT + 2 * (args.warmup + args.steps) + 16)
     kv = m.kv_cache(max_seq)
     prompt = synth.prompt_ids(V, PROMPT, seq_index=0 if tp_mode else rank)
 
@@ -316,8 +344,8 @@ def run_ours(args):
     # prompts, each prefilled, then all 16 decoded together; one weight read
     # per step for the 16 tokens), single GPU only
     batch = None
-    if not tp_mode and args.batch > 1:
-        B = args.batch
+    B = wl["batch"] if args.batch < 0 else args.batch
+    if not tp_mode and B > 1:
         kb = m.kv_batch(B, PROMPT + args.batch_steps + 16)
         firsts = [int(np.argmax(kb.prefill(b, synth.prompt_ids(V, PROMPT, seq_index=b), True)[0]))
                   for b in range(B)]
@@ -396,7 +424,7 @@ def run_ours(args):
     # batch; the full table is `--microbench`)
     micro = None
     if not args.no_microbench and rank == 0 and not tp_mode:
-        micro = run_microbench([(14336, 4096)], reps=3)
+        micro = run_microbench([(14336, 4096)], reps=3) if args.config == "8b" else None
 
     # whole-step algorithmic bytes: every weight once + K/V at the mean context
     ctx_mean = ctx0 + args.steps / 2
@@ -420,12 +448,16 @@ def run_ours(args):
         return
     base = None
     if world == 1 and not args.no_cpu_baseline:
-        base = cpu_baseline(g, 1)
+        def make(n):
+            if not n:
+                return g
+            return synth.build(args.config, **{**shape_overrides(args), "n_layers": n})
+        base = cpu_baseline(args, make, L)
     line = {
         "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True,
         "scaling": "strong" if tp_mode else "weak", "vs_baseline": None,
-        "dtype": "q4_k/q6_k weights, f16 tensor-core math, f32 accumulate",
+        "dtype": "f16 tensor-core operands (exact small-integer weights; activations as hi + lo f16 planes, ~22 bits), f32 accumulate; f16 KV cache",
         "data": "synthetic (seeded N(0,0.02) weights quantised Q4_K_M; seeded uniform prompt ids)",
         "config": bench_config(args),
         "placement": (f"tp{world} (NCCL all-reduce after Wo and W2)" if tp_mode
@@ -546,8 +578,11 @@ def main():
     ap.add_argument("--gemm", default="",
                     help="profiling only: ROWS,COLS,M,TYPE — four calls of the fused dequant "
                          "matmul (ifx_op_matmul_t_q) on a seeded matrix, then exit")
-    ap.add_argument("--batch", type=int, default=16,
-                    help="also time batched decode of this many sequences (0/1: skip)")
+    ap.add_argument("--batch", type=int, default=-1,
+                    help="also time batched decode of this many sequences (0/1: skip; default: "
+                         "the config's, 16 for 8b and 32 for 70b)")
+    ap.add_argument("--config", default="8b", choices=sorted(WORKLOADS),
+                    help="the workload: 8b (the headline metric's, default), 70b or 1b")
     ap.add_argument("--batch-steps", type=int, default=32)
     ap.add_argument("--tp", action="store_true",
                     help="with several GPUs: decode one sequence with tensor parallelism over "
