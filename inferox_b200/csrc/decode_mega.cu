@@ -28,6 +28,7 @@ namespace {
 using namespace gemvdev;
 
 constexpr int kMaxGrp = 8;
+constexpr size_t kMegaRingBytes = 90 * 1024;
 constexpr int kMaxSplitsMega = 128;
 
 __device__ __forceinline__ unsigned ld_acquire(const unsigned *p) {
@@ -581,13 +582,14 @@ __global__ void __launch_bounds__(kGemvThreads, 1) decode_mega_kernel(const __gr
   uint64_t *xbar = reinterpret_cast<uint64_t *>(smem + kGemvBarBytes);
   MegaPhase *s_ph = reinterpret_cast<MegaPhase *>(smem + A.off_ph);     // two records
   const int2 *s_rg = reinterpret_cast<const int2 *>(smem + A.off_rg);   // this CTA's ranges
+  uint32_t *tab = reinterpret_cast<uint32_t *>(smem + A.off_tab);       // ring offsets, lengths
   uint8_t *ring = smem + A.off_ring;
   uint8_t *abuf = smem + A.off_scr;   // attention item buffer
   uint8_t *scr = smem + A.off_stage;  // x staging of the GEMV phases
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
     g_xzero = make_uint4(0u, 0u, 0u, 0u);
-    for (int s = 0; s < A.NS; ++s) {
+    for (int s = 0; s < kRingPos; ++s) {
       mbar_init(&full_bar[s], 1);
       mbar_init(&empty_bar[s], 8);
     }
@@ -615,16 +617,19 @@ __global__ void __launch_bounds__(kGemvThreads, 1) decode_mega_kernel(const __gr
     // producer: every GEMV phase's units for this CTA, back to back
     if (lane == 0) {
       uint32_t it = 0;
+      RingState rs{0u, 0u, 0u};
+      const RingTab rt{tab};
       for (int p = 0; p < A.nph; ++p) {
         const MegaPhase &P = A.ph[p];
         if (P.kind != PH_GEMV) continue;
         const int2 rg = s_rg[p];
         const int n = rg.y - rg.x;
-        if (!gemv_produce(P.g, rg.x, n, it, ring, A.NS, A.slot_bytes, full_bar, empty_bar, A.err))
+        if (!gemv_produce(P.g, rg.x, n, it, ring, (uint32_t)A.ring_bytes, rt, rs, full_bar,
+                          empty_bar, A.err))
           return;  // gemv_produce drained its copies
         it += (uint32_t)n;
       }
-      ring_drain(full_bar, A.NS, it);
+      ring_drain(full_bar, kRingPos, it);
     }
     return;
   }
@@ -665,13 +670,11 @@ __global__ void __launch_bounds__(kGemvThreads, 1) decode_mega_kernel(const __gr
         const int n = rg.y - rg.x;
         if (n > 0) {
           const bool full = n >= P.g.kunits;
-          float *s16 = reinterpret_cast<float *>(scr + (size_t)P.g.win_units * P.g.kc * 4);
-          stage_x(P.g, rg.x, n, full, scr, s16);
+          stage_x(P.g, rg.x, n, full, scr);
           consumer_sync();
           // on a failed wait the warp carries on to the next grid barrier,
           // which sees the error flag and ends the CTA's consumers together
-          gemv_consume(P.g, rg.x, n, it, ring, A.NS, A.slot_bytes, full_bar, empty_bar, scr, s16,
-                       full, A.err);
+          gemv_consume(P.g, rg.x, n, it, ring, tab, full_bar, empty_bar, scr, full, A.err);
           it += (uint32_t)n;
         }
         break;
@@ -753,7 +756,7 @@ ifx_status mega_finalize(MegaPlan *plan, const std::vector<MegaPhase> &phases, i
   for (const MegaPhase &p : phases)
     if (p.kind == PH_GEMV) {
       slot = std::max<size_t>(slot, (size_t)p.g.slot_bytes);
-      size_t w = (size_t)p.g.win_units * (p.g.kc * 4 + p.g.kc / 16 * 4);  // x hi + lo, sums
+      size_t w = (size_t)p.g.win_units * xs_slot_bytes(p.g.kc);  // activation planes, sums
       win = std::max<size_t>(win, w);
     }
   // attention buffer (filled during the QKV phase) and staging area side by side
@@ -765,23 +768,28 @@ ifx_status mega_finalize(MegaPlan *plan, const std::vector<MegaPhase> &phases, i
   constexpr size_t kCap = 220 * 1024;
   A.nph = (int)phases.size();
   A.nph_pad = (A.nph + 1) & ~1;
-  // carve-up: stage barriers | 2 extra barriers | 2 phase records | ranges | ring | scratch
+  // carve-up: stage barriers | 3 extra barriers | 2 phase records | ranges |
+  // ring offsets and lengths | weight ring | scratch
   const size_t off_ph = kGemvBarBytes + 64;
   const size_t off_rg = off_ph + 2 * sizeof(MegaPhase);
-  const size_t off_ring = (off_rg + (size_t)A.nph_pad * sizeof(int2) + 127) & ~(size_t)127;
-  if (off_ring + 2 * slot + scratch > kCap)
+  const size_t off_tab = (off_rg + (size_t)A.nph_pad * sizeof(int2) + 15) & ~(size_t)15;
+  const size_t off_ring = (off_tab + kGemvTabBytes + 127) & ~(size_t)127;
+  // the weight ring takes the rest (units packed back to back), up to
+  // kMegaRingBytes: it must hold two of the largest units, and a deeper ring
+  // measured slower (the bytes still in flight at a phase boundary delay the
+  // staging loads and the grid barrier that come next)
+  if (off_ring + scratch + 2 * slot > kCap)
     return fail(IFX_ERR_UNSUPPORTED, "persistent decode: shared memory plan too large");
-  // even: every use of a slot then belongs to the same consumer half (see
-  // the stage count in gemv_plan)
-  int NS = (int)std::min<size_t>(kGemvMaxStages, (kCap - off_ring - scratch) / slot) & ~1;
-  if (NS < 2) return fail(IFX_ERR_UNSUPPORTED, "persistent decode: ring needs two slots");
-  A.NS = NS;
+  const size_t ring = std::max<size_t>(2 * slot, std::min<size_t>(kMegaRingBytes, kCap - off_ring - scratch)) &
+                      ~(size_t)127;
+  A.ring_bytes = (int)ring;
   A.slot_bytes = (int)slot;
   A.scratch_bytes = (int)scratch;
   A.off_ph = (int)off_ph;
   A.off_rg = (int)off_rg;
+  A.off_tab = (int)off_tab;
   A.off_ring = (int)off_ring;
-  A.off_scr = (int)(off_ring + (size_t)NS * slot);
+  A.off_scr = (int)(off_ring + ring);
   A.off_stage = (int)(A.off_scr + attn_bytes);
   // per-CTA unit ranges of every phase (zero-length outside GEMV phases)
   std::vector<int2> rg((size_t)num_sms * A.nph_pad, make_int2(0, 0));

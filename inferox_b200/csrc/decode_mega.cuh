@@ -30,8 +30,8 @@ struct MegaArgs {
   const int2 *rg;  // [grid][nph_pad]: each CTA's unit range per phase
   int nph_pad;     // nph rounded up to even (rows are 16-byte multiples)
   // dynamic shared memory carve-up (byte offsets)
-  int off_ph, off_rg, off_ring, off_scr, off_stage;  // off_scr: attention buffer
-  int NS, slot_bytes, scratch_bytes;
+  int off_ph, off_rg, off_tab, off_ring, off_scr, off_stage;  // off_scr: attention buffer
+  int ring_bytes, slot_bytes, scratch_bytes;
   unsigned *bar;  // [0] grid barrier counter, [1 + h] finished splits of kv head h;
                   // all zeroed at every launch
   int *err;

@@ -35,18 +35,17 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_b1_kernel(const __grid_c
   extern __shared__ __align__(128) uint8_t smem[];
   uint64_t *full_bar = reinterpret_cast<uint64_t *>(smem);
   uint64_t *empty_bar = full_bar + kGemvMaxStages;
-  uint8_t *ring = smem + kGemvBarBytes;
-  uint8_t *xw = ring + (size_t)a.nstages * a.slot_bytes;
-  float *s16 = reinterpret_cast<float *>(xw + (size_t)a.win_units * a.kc * 4);  // after hi + lo
+  uint32_t *tab = reinterpret_cast<uint32_t *>(smem + kGemvBarBytes);
+  uint8_t *ring = smem + kGemvBarBytes + kGemvTabBytes;
+  uint8_t *xw = ring + a.ring_bytes;  // staged activations (stage_x)
 
   const int2 rg = a.sched[blockIdx.x];
   const int u0 = rg.x, n = rg.y - rg.x;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int NS = a.nstages;
 
   if (threadIdx.x == 0) {
     g_xzero = make_uint4(0u, 0u, 0u, 0u);
-    for (int s = 0; s < NS; ++s) {
+    for (int s = 0; s < kRingPos; ++s) {
       mbar_init(&full_bar[s], 1);
       mbar_init(&empty_bar[s], 8);
     }
@@ -56,8 +55,12 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_b1_kernel(const __grid_c
 
   if (warp == kConsumerWarps) {
     // producer: weights only, so it is safe before griddepcontrol.wait
-    if (lane == 0 && gemv_produce(a, u0, n, 0u, ring, NS, a.slot_bytes, full_bar, empty_bar, a.err))
-      ring_drain(full_bar, NS, (uint32_t)max(n, 0));
+    if (lane == 0) {
+      RingState rs{0u, 0u, 0u};
+      if (gemv_produce(a, u0, n, 0u, ring, (uint32_t)a.ring_bytes, RingTab{tab}, rs,
+                       full_bar, empty_bar, a.err))
+        ring_drain(full_bar, kRingPos, (uint32_t)max(n, 0));
+    }
     return;
   }
 
@@ -70,9 +73,9 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_b1_kernel(const __grid_c
       a.zero_ptr[i] = 0.f;
   if (n <= 0) return;
   const bool full = n >= a.kunits;
-  stage_x(a, u0, n, full, xw, s16);
+  stage_x(a, u0, n, full, xw);
   consumer_sync();
-  gemv_consume(a, u0, n, 0u, ring, NS, a.slot_bytes, full_bar, empty_bar, xw, s16, full, a.err);
+  gemv_consume(a, u0, n, 0u, ring, tab, full_bar, empty_bar, xw, full, a.err);
 }
 
 }  // namespace
@@ -117,13 +120,6 @@ ifx_status gemv_plan(const QMatrix *const *mats, float *const *ys, int nseg, int
   a.eps = eps;
   a.err = err;
   a.slot_bytes = slot;
-  // An even stage count is required: ring position p belongs to consumer
-  // half p & 1, and with an even count every use of a slot belongs to the
-  // same half, which consumes its positions in order. With an odd count the
-  // two halves alternate on a slot, one half can wait on a slot whose
-  // previous use (the other half's) has not landed, and the parity wait then
-  // passes a phase early.
-  a.nstages = std::min(kGemvMaxStages, std::max(2, kGemvRingBytes / slot)) & ~1;
 
   // byte-balanced contiguous ranges, one per CTA
   // one schedule entry per SM (the persistent decode kernel indexes it by
@@ -150,13 +146,15 @@ ifx_status gemv_plan(const QMatrix *const *mats, float *const *ys, int nseg, int
     prev = e;
   }
   a.win_units = win;
-  // shrink the ring until the whole plan fits the per-block shared memory cap
+  // the weight ring takes what the staging window leaves of the shared
+  // memory cap (at most kGemvRingBytes), and must hold two of the largest units
   constexpr size_t kSmemCap = 220 * 1024;
-  const size_t win_bytes = (size_t)win * (a.kc * 4 + a.kc / 16 * 4);  // x hi + lo planes, sums
-  while (a.nstages > 2 && kGemvBarBytes + (size_t)a.nstages * a.slot_bytes + win_bytes > kSmemCap)
-    a.nstages -= 2;
-  const size_t smem = kGemvBarBytes + (size_t)a.nstages * a.slot_bytes + win_bytes;
-  if (smem > kSmemCap) return fail(IFX_ERR_SHAPE, "gemv: shared memory plan too large");
+  const size_t win_bytes = (size_t)win * gemvdev::xs_slot_bytes(a.kc);  // activation planes, sums
+  const size_t fixed = kGemvBarBytes + kGemvTabBytes + win_bytes;
+  const size_t ring = fixed < kSmemCap ? std::min<size_t>(kGemvRingBytes, (kSmemCap - fixed) & ~(size_t)15) : 0;
+  if (ring < 2 * (size_t)slot) return fail(IFX_ERR_SHAPE, "gemv: shared memory plan too large");
+  a.ring_bytes = (int)ring;
+  const size_t smem = fixed + ring;
   IFX_CUDA(cudaMalloc(&plan->d_sched, sizeof(int2) * G));
   IFX_CUDA(cudaMemcpy(plan->d_sched, sched.data(), sizeof(int2) * G, cudaMemcpyHostToDevice));
   a.sched = plan->d_sched;

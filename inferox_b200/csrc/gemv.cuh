@@ -20,6 +20,7 @@ constexpr int kGemvMaxStages = 16;
 constexpr int kGemvThreads = 544;  // 16 consumer warps + 1 producer warp
 constexpr int kGemvRingBytes = 176 * 1024;
 constexpr int kGemvBarBytes = 2 * kGemvMaxStages * 8;  // full + empty mbarriers
+constexpr int kGemvTabBytes = 2 * kGemvMaxStages * 4;  // ring offsets + lengths
 
 struct GemvSeg {
   const uint8_t *w;  // repacked weights (device)
@@ -40,7 +41,9 @@ struct GemvArgs {
   const float *x, *x2, *normw;
   float eps;
   const int2 *sched;  // per CTA [unit_begin, unit_end)
-  int slot_bytes, nstages, win_units;
+  int slot_bytes;  // largest unit of the plan
+  int ring_bytes;  // weight ring (bytes; units packed back to back)
+  int win_units;   // staged activation slots
   int *err;
   float *zero_ptr;    // zeroed by the consumers after griddepcontrol.wait
   int zero_n;         // (a buffer a later kernel accumulates into)

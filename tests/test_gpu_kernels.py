@@ -1,8 +1,9 @@
 """GPU parity of the op-level kernels against the CPU oracle (oracle/refcpu.c).
 
 Integer / byte work (dequantisation, argmax, the AVX2-order matmul_t) must be
-bit-exact. The fused dequant GEMV/GEMM run on tensor cores with f16
-operands and f32 accumulation; their tolerance is derived from f16 rounding:
+bit-exact. The fused dequant matmuls run on tensor cores (the batch-1 GEMV
+with exact integer products over activation planes of ~28 bits, the GEMMs
+with f16 operands and f32 accumulation); their tolerance is
 |y - y_ref| <= TOL * ||w_row * x||_2, TOL stated per test.
 """
 import numpy as np
@@ -97,7 +98,10 @@ def test_gemv_matches_oracle(ttype, rows, cols):
     ref = wd @ x.astype(np.float64)
     scale = np.sqrt((wd * x[None, :]) ** 2 @ np.ones(cols)) + 1e-6
     err = np.abs(y - ref) / scale
-    assert err.max() < 3e-3, (err.max(), np.argmax(err))
+    print(f"gemv type {ttype} {rows}x{cols}: max error {err.max():.2e} of ||w*x||")
+    # integer tensor-core products (exact), activations staged to ~28 bits,
+    # f32 conversions per unit: a few 1e-7 of ||w*x||
+    assert err.max() < 5e-6, (err.max(), np.argmax(err))
 
 
 @pytest.mark.parametrize("ttype,rows,cols,m", [
