@@ -272,7 +272,28 @@ def run_ours(args):
     t0 = time.time()
     wl = WORKLOADS[args.config]
     PROMPT = wl["prompt"]
-    g = synth.build(args.config, **shape_overrides(args))
+    # one GPU: the model in host memory; several: rank 0 writes the GGUF once
+    # to shared memory and every rank maps it (the library mmaps a path), so
+    # N ranks do not each build the whole model
+    gpath = None
+    if world > 1:
+        tag = "_".join(f"{k}{v}" for k, v in sorted(shape_overrides(args).items()))
+        gpath = os.path.join("/dev/shm" if os.path.isdir("/dev/shm") else tempfile.gettempdir(),
+                             f"ifx_bench_{args.config}{'_' + tag if tag else ''}_{os.getpid() if rank == 0 else 0}.gguf")
+        name = torch.zeros(256, dtype=torch.uint8, device="cuda")
+        if rank == 0:
+            synth.build(args.config, **shape_overrides(args)).tofile(gpath)
+            enc = gpath.encode()
+            name[:len(enc)] = torch.frombuffer(bytearray(enc), dtype=torch.uint8)
+        dist.broadcast(name, 0)
+        gpath = bytes(name.cpu().numpy()).rstrip(b"\0").decode()
+        g = None
+    else:
+        g = synth.build(args.config, **shape_overrides(args))
+
+    def load(**kw):
+        return Model.open(gpath, device=local, **kw) if gpath else Model.from_bytes(g, device=local, **kw)
+
     t_gen = time.time() - t0
     t0 = time.time()
     if tp_mode:
@@ -281,9 +302,9 @@ def run_ours(args):
             uid.copy_(torch.frombuffer(bytearray(tp.unique_id()), dtype=torch.uint8))
         dist.broadcast(uid, 0)
         comm = tp.Comm(bytes(uid.cpu().numpy()), world, rank, local)
-        m = Model.from_bytes(g, device=local, tp_size=world, tp_rank=rank, nccl_comm=comm.handle)
+        m = load(tp_size=world, tp_rank=rank, nccl_comm=comm.handle)
     else:
-        m = Model.from_bytes(g, device=local)
+        m = load()
     t_load = time.time() - t0
     cfg = m.config
     L, G, hd, V = int(cfg.n_layers), int(cfg.n_kv_heads), int(cfg.head_dim), int(cfg.vocab_size)
@@ -385,8 +406,7 @@ def run_ours(args):
         f0 = 0
         try:
             tcomm = tp.Comm(bytes(uid.cpu().numpy()), world, rank, local)
-            mt = Model.from_bytes(g, device=local, tp_size=world, tp_rank=rank,
-                                  nccl_comm=tcomm.handle, tp_timeout_ms=120000)
+            mt = load(tp_size=world, tp_rank=rank, nccl_comm=tcomm.handle, tp_timeout_ms=120000)
             kvt = mt.kv_cache(max_seq)
             p0 = synth.prompt_ids(V, PROMPT, seq_index=0)
             tpf = time.perf_counter()
@@ -442,6 +462,8 @@ def run_ours(args):
         if dist:
             dist.barrier()
             dist.destroy_process_group()
+        if gpath and rank == 0 and os.path.exists(gpath):
+            os.remove(gpath)
 
     if rank != 0:
         finish()

@@ -191,6 +191,19 @@ typedef struct ifx_kv_batch ifx_kv_batch;
 ifx_status ifx_kv_batch_create(ifx_model *m, size_t max_seq_len, int batch,
                                ifx_kv_batch **out);
 void ifx_kv_batch_free(ifx_kv_batch *kb);
+/* No reference counterpart: a batch whose caches share a pool of n_pages
+ * pages of 64 positions (every layer and kv head of those positions). A
+ * sequence takes pages as its prefill and decode steps reach them and gives
+ * them back on ifx_kv_batch_reset, so batch * max_seq_len may exceed the
+ * pool: a step that needs a page when none is free fails with
+ * IFX_ERR_OUT_OF_MEMORY and changes no sequence's length. max_seq_len at
+ * most 4096. Results are those of ifx_kv_batch_create's batch. */
+ifx_status ifx_kv_batch_create_paged(ifx_model *m, size_t max_seq_len, int batch,
+                                     size_t n_pages, ifx_kv_batch **out);
+/* Pages of a paged batch that no sequence holds, and the pool size (both 0
+ * for a batch made by ifx_kv_batch_create). */
+ifx_status ifx_kv_batch_pages(const ifx_kv_batch *kb, size_t *free_pages,
+                              size_t *total_pages);
 /* KvCache::len (cache.rs:31-33) of sequence `seq`. */
 ifx_status ifx_kv_batch_len(const ifx_kv_batch *kb, int seq, size_t *len);
 /* Model::prefill (forward.rs:496-538) of sequence `seq` of the batch. */

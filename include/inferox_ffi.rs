@@ -76,6 +76,10 @@ extern "C" {
     // batched decode: `batch` independent caches, prefilled one by one, stepped together
     pub fn ifx_kv_batch_create(m: *mut IfxModel, max_seq: usize, batch: c_int,
                                out: *mut *mut IfxKvBatch) -> c_int;
+    pub fn ifx_kv_batch_create_paged(m: *mut IfxModel, max_seq: usize, batch: c_int,
+                                     n_pages: usize, out: *mut *mut IfxKvBatch) -> c_int;
+    pub fn ifx_kv_batch_pages(kb: *const IfxKvBatch, free_pages: *mut usize,
+                              total_pages: *mut usize) -> c_int;
     pub fn ifx_kv_batch_free(kb: *mut IfxKvBatch);
     pub fn ifx_kv_batch_len(kb: *const IfxKvBatch, seq: c_int, len: *mut usize) -> c_int;
     pub fn ifx_prefill_seq(m: *mut IfxModel, kb: *mut IfxKvBatch, seq: c_int, ids: *const u32,

@@ -110,6 +110,8 @@ def _load():
         "ifx_decode_greedy": (st, [vp, vp, C.c_uint32, sz, u32p, fp]),
         "ifx_bench_kernel": (st, [vp, vp, C.c_char_p, C.c_int, fp, C.POINTER(C.c_uint64)]),
         "ifx_kv_batch_create": (st, [vp, sz, C.c_int, C.POINTER(vp)]),
+        "ifx_kv_batch_create_paged": (st, [vp, sz, C.c_int, sz, C.POINTER(vp)]),
+        "ifx_kv_batch_pages": (st, [vp, C.POINTER(sz), C.POINTER(sz)]),
         "ifx_kv_batch_free": (None, [vp]),
         "ifx_kv_batch_len": (st, [vp, C.c_int, C.POINTER(sz)]),
         "ifx_prefill_seq": (st, [vp, vp, C.c_int, u32p, sz, fp, C.c_int]),

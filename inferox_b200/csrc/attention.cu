@@ -69,12 +69,22 @@ __global__ void __launch_bounds__(kAttnThreads) decode_attn_kernel(const __grid_
   // the QKV GEMV is still draining.
   const int pos = a.pos[sq];
   const int len = pos + 1;
-  const int chunk = (len + NS - 1) / NS;
+  const int chunk = a.page_table ? a.page_rows : (len + NS - 1) / NS;
   const int t0 = s * chunk, t1 = min(len, t0 + chunk);
   const int nk = max(0, t1 - t0);
   const int nold = max(0, min(t1, pos) - t0);  // rows already in the cache
-  __half *kc = kcb + (size_t)h * a.max_seq * hd;
-  __half *vc = vcb + (size_t)h * a.max_seq * hd;
+  // kc / vc address rows by position t (kc + t * hd); a page is indexed from
+  // its first position t0
+  __half *kc, *vc;
+  if (a.page_table) {
+    const int pg = nk > 0 ? a.page_table[(size_t)sq * a.max_pages + s] : 0;
+    const size_t off = (size_t)pg * a.page_stride + (size_t)h * a.page_rows * hd;
+    kc = a.kc + off - (size_t)t0 * hd;
+    vc = a.vc + off - (size_t)t0 * hd;
+  } else {
+    kc = kcb + (size_t)h * a.max_seq * hd;
+    vc = vcb + (size_t)h * a.max_seq * hd;
+  }
   const uint32_t row_bytes = (uint32_t)hd * 2u;
   if (tid == 0) {
     mbar_init(&bar, 1);

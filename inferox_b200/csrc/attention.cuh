@@ -27,6 +27,15 @@ struct DecodeAttnArgs {
   // when set, row b's cache and position are those of sequence slot[b]
   // (a step over a subset of a batch's sequences); workspace rows stay b
   const int *slot = nullptr;
+  // paged cache (no reference counterpart: cache pages shared by the
+  // sequences of a batch): when set, split s of sequence q covers the
+  // page_rows positions of its page page_table[q * max_pages + s], which
+  // holds, for every layer and kv head, page_rows consecutive rows; kc / vc
+  // then point at the layer's rows in page 0 ([G][page_rows][hd]) and
+  // kv_seq_stride is unused
+  const int *page_table = nullptr;
+  int page_rows = 0, max_pages = 0;
+  int64_t page_stride = 0;  // elements per page (all layers and kv heads)
 };
 
 ifx_status decode_attention(const DecodeAttnArgs &a, cudaStream_t st, bool pdl);

@@ -223,18 +223,35 @@ ifx_status ifx_decode_greedy(ifx_model *m, ifx_kv *kv, uint32_t token, size_t n_
   IFX_GUARD({ return m->m.decode_greedy(kv->kv, token, n_steps, out_tokens, device_ms); })
 }
 
+static ifx_status kv_batch_create(ifx_model *m, size_t max_seq_len, int batch, size_t pages,
+                                  ifx_kv_batch **out) {
+  ifx_kv_batch *kb = new ifx_kv_batch();
+  ifx_status s = kb->kb.create(&m->m, max_seq_len, batch, pages);
+  if (s != IFX_OK) {
+    delete kb;
+    return s;
+  }
+  *out = kb;
+  return IFX_OK;
+}
+
 ifx_status ifx_kv_batch_create(ifx_model *m, size_t max_seq_len, int batch, ifx_kv_batch **out) {
   if (!m || !out || !max_seq_len) return fail(IFX_ERR_INVALID_ARGUMENT, "kv_batch_create: bad argument");
-  IFX_GUARD({
-    ifx_kv_batch *kb = new ifx_kv_batch();
-    ifx_status s = kb->kb.create(&m->m, max_seq_len, batch);
-    if (s != IFX_OK) {
-      delete kb;
-      return s;
-    }
-    *out = kb;
-    return IFX_OK;
-  })
+  IFX_GUARD({ return kv_batch_create(m, max_seq_len, batch, 0, out); })
+}
+
+ifx_status ifx_kv_batch_create_paged(ifx_model *m, size_t max_seq_len, int batch, size_t n_pages,
+                                     ifx_kv_batch **out) {
+  if (!m || !out || !max_seq_len || !n_pages || n_pages > (size_t)INT32_MAX)
+    return fail(IFX_ERR_INVALID_ARGUMENT, "kv_batch_create_paged: bad argument");
+  IFX_GUARD({ return kv_batch_create(m, max_seq_len, batch, n_pages, out); })
+}
+
+ifx_status ifx_kv_batch_pages(const ifx_kv_batch *kb, size_t *free_pages, size_t *total_pages) {
+  if (!kb || !free_pages || !total_pages) return fail(IFX_ERR_INVALID_ARGUMENT, "kv_batch_pages: null argument");
+  *free_pages = kb->kb.free_pages.size();
+  *total_pages = kb->kb.n_pages;
+  return IFX_OK;
 }
 
 void ifx_kv_batch_free(ifx_kv_batch *kb) { delete kb; }

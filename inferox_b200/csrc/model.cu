@@ -116,6 +116,21 @@ __global__ void kv_write_kernel(const float *k, const float *v, __half *kc, __ha
   }
 }
 
+// The same rows into a paged cache: position p = start + t is row p % P of
+// page table[p / P]; kc / vc point at this layer's rows in page 0.
+__global__ void kv_write_paged_kernel(const float *k, const float *v, __half *kc, __half *vc, int n,
+                                      int G, int hd, int P, int64_t page_stride, const int *table,
+                                      int start) {
+  const int t = blockIdx.x, p = start + t;
+  const size_t page = (size_t)table[p / P] * (size_t)page_stride;
+  for (int e = threadIdx.x; e < G * hd; e += blockDim.x) {
+    const int g = e / hd, d = e % hd;
+    const size_t dst = page + ((size_t)g * P + p % P) * hd + kv_col(p, d, hd);
+    kc[dst] = __float2half_rn(k[(size_t)t * G * hd + e]);
+    vc[dst] = __float2half_rn(v[(size_t)t * G * hd + e]);
+  }
+}
+
 __global__ void add_int_kernel(int *p, int v) { *p += v; }
 
 // Row-wise argmax of x [rows][n] (last index on ties, NaN skipped:
@@ -530,7 +545,10 @@ KvCache::~KvCache() {
   mega_free(&mega);
 }
 
-ifx_status KvBatch::create(Model *model, size_t max_seq_len, int nseq) {
+constexpr int kPageRows = 64;   // positions per page of a paged batch
+constexpr int kMaxPages = 64;   // pages per sequence (the attention splits)
+
+ifx_status KvBatch::create(Model *model, size_t max_seq_len, int nseq, size_t pages) {
   m = model;
   batch = nseq;
   max_seq = max_seq_len;
@@ -539,19 +557,40 @@ ifx_status KvBatch::create(Model *model, size_t max_seq_len, int nseq) {
   if (nseq < 1 || nseq > kGemmSmallMax)
     return fail(IFX_ERR_INVALID_ARGUMENT, "batched decode: 1 to 32 sequences");
   const int G = (int)m->Gl, H = (int)m->Hl, hd = (int)c.head_dim, grp = H / G;
-  per_layer = (size_t)G * max_seq * hd;
-  // split-K factor: at least two CTAs per SM, and chunks of at most 64 cache
-  // rows (small shared-memory footprint, several CTAs per SM)
-  ns = std::max(1, (2 * kNumSMs + nseq * G - 1) / (nseq * G));
-  ns = std::max(ns, (int)((max_seq + 63) / 64));
-  ns = std::min(ns, 64);
-  while (ns < 64 && decode_attention_smem(grp, hd, (int)max_seq, ns) > 160 * 1024) ++ns;
+  paged = pages > 0;
+  if (paged) {
+    // one attention split per page
+    page_rows = kPageRows;
+    max_pages = (int)((max_seq + kPageRows - 1) / kPageRows);
+    if (max_pages > kMaxPages)
+      return fail(IFX_ERR_INVALID_ARGUMENT, "paged batch: max_seq_len above " +
+                                                std::to_string(kPageRows * kMaxPages));
+    n_pages = pages;
+    page_stride = (int64_t)c.n_layers * G * kPageRows * hd;
+    per_layer = (size_t)G * kPageRows * hd;  // a layer's rows within one page
+    ns = max_pages;
+  } else {
+    per_layer = (size_t)G * max_seq * hd;
+    // split-K factor: at least two CTAs per SM, and chunks of at most 64 cache
+    // rows (small shared-memory footprint, several CTAs per SM)
+    ns = std::max(1, (2 * kNumSMs + nseq * G - 1) / (nseq * G));
+    ns = std::max(ns, (int)((max_seq + 63) / 64));
+    ns = std::min(ns, 64);
+    while (ns < 64 && decode_attention_smem(grp, hd, (int)max_seq, ns) > 160 * 1024) ++ns;
+  }
   const size_t D = c.hidden_size, F = m->Fl, V = c.vocab_size;
   const size_t qkvw = (size_t)(H + 2 * G) * hd;
   dev = m->device;
   IFX_CUDA(cudaSetDevice(m->device));
-  IFX_TRY(dalloc(&k, per_layer * c.n_layers * nseq));
-  IFX_TRY(dalloc(&v, per_layer * c.n_layers * nseq));
+  const size_t cache = paged ? (size_t)page_stride * n_pages : per_layer * c.n_layers * nseq;
+  IFX_TRY(dalloc(&k, cache));
+  IFX_TRY(dalloc(&v, cache));
+  if (paged) {
+    IFX_TRY(dalloc(&table_dev, (size_t)nseq * max_pages));
+    table.assign((size_t)nseq * max_pages, -1);
+    free_pages.clear();
+    for (size_t i = n_pages; i-- > 0;) free_pages.push_back((int)i);  // page 0 handed out first
+  }
   IFX_TRY(dalloc(&pos, (size_t)nseq));
   IFX_TRY(dalloc(&x, nseq * D));
   IFX_TRY(dalloc(&qkv, nseq * qkvw));
@@ -577,8 +616,38 @@ KvBatch::~KvBatch() {
   for (void *p : {(void *)k, (void *)v, (void *)pos, (void *)x, (void *)qkv, (void *)attn,
                   (void *)gate, (void *)up, (void *)logits, (void *)part_o, (void *)part_ml,
                   (void *)counters, (void *)xf, (void *)ids, (void *)out, (void *)keys,
-                  (void *)slots})
+                  (void *)slots, (void *)table_dev})
     if (p) cudaFree(p);
+}
+
+ifx_status KvBatch::reserve(int seq, size_t rows, cudaStream_t st) {
+  if (!paged) return IFX_OK;
+  if (rows > max_seq) return fail(IFX_ERR_INVALID_TENSOR_INDEX, "KV cache is full");
+  int *row = table.data() + (size_t)seq * max_pages;
+  const int need = (int)((rows + page_rows - 1) / page_rows);
+  int have = 0;
+  while (have < max_pages && row[have] >= 0) ++have;
+  if (need <= have) return IFX_OK;
+  if ((size_t)(need - have) > free_pages.size())
+    return fail(IFX_ERR_OUT_OF_MEMORY, "paged batch: the page pool is exhausted (" +
+                                           std::to_string(n_pages) + " pages)");
+  for (int i = have; i < need; ++i) {
+    row[i] = free_pages.back();
+    free_pages.pop_back();
+  }
+  IFX_CUDA(cudaMemcpyAsync(table_dev + (size_t)seq * max_pages + have, row + have,
+                           sizeof(int) * (size_t)(need - have), cudaMemcpyHostToDevice, st));
+  return IFX_OK;
+}
+
+void KvBatch::release(int seq) {
+  if (!paged) return;
+  int *row = table.data() + (size_t)seq * max_pages;
+  for (int i = 0; i < max_pages; ++i)
+    if (row[i] >= 0) {
+      free_pages.push_back(row[i]);
+      row[i] = -1;
+    }
 }
 
 ifx_status KvCache::clear() {
@@ -871,8 +940,20 @@ ifx_status Model::prefill_seq(KvBatch &kb, int seq, const uint32_t *ids, size_t 
   view.m = this;
   view.max_seq = kb.max_seq;
   view.per_layer = kb.per_layer;
-  view.k = kb.k + (size_t)seq * cfg.n_layers * kb.per_layer;
-  view.v = kb.v + (size_t)seq * cfg.n_layers * kb.per_layer;
+  if (kb.paged) {
+    if (kb.len[(size_t)seq] + n > kb.max_seq)
+      return fail(IFX_ERR_INVALID_TENSOR_INDEX, "KV cache is full");
+    IFX_CUDA(cudaSetDevice(device));
+    IFX_TRY(kb.reserve(seq, kb.len[(size_t)seq] + n, stream));
+    view.k = kb.k;
+    view.v = kb.v;
+    view.page_table = kb.table_dev + (size_t)seq * kb.max_pages;
+    view.page_rows = kb.page_rows;
+    view.page_stride = kb.page_stride;
+  } else {
+    view.k = kb.k + (size_t)seq * cfg.n_layers * kb.per_layer;
+    view.v = kb.v + (size_t)seq * cfg.n_layers * kb.per_layer;
+  }
   view.pos = kb.pos + seq;
   view.len = kb.len[(size_t)seq];
   view.mega_tried = true;  // never planned for the persistent kernel
@@ -907,7 +988,13 @@ ifx_status Model::enqueue_decode_batch(KvBatch &kb, cudaStream_t st, int n, cons
     a.qkv_stride = qkvw;
     a.kc = kb.k + l * kb.per_layer;
     a.vc = kb.v + l * kb.per_layer;
-    a.kv_seq_stride = (int64_t)(c.n_layers * kb.per_layer);
+    a.kv_seq_stride = kb.paged ? 0 : (int64_t)(c.n_layers * kb.per_layer);
+    if (kb.paged) {
+      a.page_table = kb.table_dev;
+      a.page_rows = kb.page_rows;
+      a.max_pages = kb.max_pages;
+      a.page_stride = kb.page_stride;
+    }
     a.pos = kb.pos;
     a.part_o = kb.part_o;
     a.part_ml = kb.part_ml;
@@ -956,6 +1043,7 @@ ifx_status Model::decode_batch(KvBatch &kb, const uint32_t *tokens, float *logit
   }
   IFX_CUDA(cudaSetDevice(device));
   cudaStream_t st = stream;
+  for (int b = 0; b < kb.batch; ++b) IFX_TRY(kb.reserve(b, kb.len[(size_t)b] + 1, st));
   IFX_CUDA(cudaMemcpyAsync(kb.ids, tokens, sizeof(uint32_t) * kb.batch, cudaMemcpyHostToDevice, st));
   IFX_TRY(enqueue_decode_batch(kb, st));
   if (logits_host)
@@ -988,6 +1076,7 @@ ifx_status Model::decode_batch_seqs(KvBatch &kb, const int *seqs, int n, const u
   }
   IFX_CUDA(cudaSetDevice(device));
   cudaStream_t st = stream;
+  for (int i = 0; i < n; ++i) IFX_TRY(kb.reserve(seqs[i], kb.len[(size_t)seqs[i]] + 1, st));
   IFX_CUDA(cudaMemcpyAsync(kb.ids, tokens, sizeof(uint32_t) * n, cudaMemcpyHostToDevice, st));
   IFX_CUDA(cudaMemcpyAsync(kb.slots, seqs, sizeof(int) * n, cudaMemcpyHostToDevice, st));
   IFX_TRY(enqueue_decode_batch(kb, st, n, kb.slots));
@@ -1026,6 +1115,7 @@ ifx_status Model::reset_seq(KvBatch &kb, int seq) {
   IFX_CUDA(cudaMemsetAsync(kb.pos + seq, 0, sizeof(int), stream));
   IFX_CUDA(cudaStreamSynchronize(stream));
   kb.len[(size_t)seq] = 0;
+  kb.release(seq);
   return IFX_OK;
 }
 
@@ -1042,6 +1132,7 @@ ifx_status Model::decode_greedy_batch(KvBatch &kb, const uint32_t *tokens, size_
   }
   IFX_CUDA(cudaSetDevice(device));
   cudaStream_t st = stream;
+  for (int b = 0; b < kb.batch; ++b) IFX_TRY(kb.reserve(b, kb.len[(size_t)b] + n, st));
   uint32_t *toks = nullptr;  // every step's tokens, copied out once at the end
   IFX_TRY(dalloc(&toks, std::max<size_t>(1, n) * kb.batch));
   IFX_CUDA(cudaMemcpyAsync(kb.ids, tokens, sizeof(uint32_t) * kb.batch, cudaMemcpyHostToDevice, st));
@@ -1114,9 +1205,15 @@ ifx_status Model::run_prompt(KvCache *kvp, const uint32_t *ids, size_t n, float 
     IFX_TRY(op_rope(w_k, n, G, hd, c.rope_dim, c.rope_base, pos0, st));
     if (kvp) {
       KvCache &kv = *kvp;
-      kv_write_kernel<<<(unsigned)n, 256, 0, st>>>(w_k, w_v, kv.k + l * kv.per_layer,
-                                                   kv.v + l * kv.per_layer, (int)n, G, hd,
-                                                   (int)kv.max_seq, start);
+      if (kv.page_table)
+        kv_write_paged_kernel<<<(unsigned)n, 256, 0, st>>>(w_k, w_v, kv.k + l * kv.per_layer,
+                                                           kv.v + l * kv.per_layer, (int)n, G, hd,
+                                                           kv.page_rows, kv.page_stride,
+                                                           kv.page_table, start);
+      else
+        kv_write_kernel<<<(unsigned)n, 256, 0, st>>>(w_k, w_v, kv.k + l * kv.per_layer,
+                                                     kv.v + l * kv.per_layer, (int)n, G, hd,
+                                                     (int)kv.max_seq, start);
       IFX_CUDA(cudaGetLastError());
     }
     PrefillAttnArgs pa{w_q, w_k, w_v, w_attn, (int)n, H, G, hd, kvp ? 1 : 0};

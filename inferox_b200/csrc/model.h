@@ -31,6 +31,11 @@ struct KvCache {  // KvCache (src/model/cache.rs:7-14), f16 on the device
   float2 *part_ml = nullptr;
   unsigned *bar = nullptr;
   bool owner = true;                  // false: a view into a KvBatch's memory
+  // a view of one sequence of a paged KvBatch: k / v are the page pool,
+  // position t lives in page page_table[t / page_rows] (device array)
+  const int *page_table = nullptr;
+  int page_rows = 0;
+  int64_t page_stride = 0;
   int dev = -1;                       // device of the allocations (the destructor must
                                       // not read the model: it may be freed first)
   ifx_status create(Model *model, size_t max_seq_len);
@@ -61,7 +66,24 @@ struct KvBatch {
   int *slots = nullptr;                     // sequences of a subset step
   unsigned long long *keys = nullptr;       // per-sequence argmax keys
   int dev = -1;                             // device of the allocations
-  ifx_status create(Model *model, size_t max_seq_len, int nseq);
+  // Paged mode (no reference counterpart): k / v are a pool of n_pages pages
+  // of page_rows positions, each holding those rows for every layer and kv
+  // head ([layer][kv_head][page_rows][head_dim]); a sequence takes pages
+  // from the pool as it grows and returns them on reset, so the pool can be
+  // far smaller than batch * max_seq rows. Sequence b's position t is row
+  // t % page_rows of page table[b * max_pages + t / page_rows].
+  bool paged = false;
+  int page_rows = 0, max_pages = 0;
+  size_t n_pages = 0;
+  int64_t page_stride = 0;                  // elements per page
+  int *table_dev = nullptr;                 // [batch][max_pages]
+  std::vector<int> table;                   // host mirror
+  std::vector<int> free_pages;              // pool pages no sequence holds
+  ifx_status create(Model *model, size_t max_seq_len, int nseq, size_t pages = 0);
+  // give sequence `seq` pages for positions [0, rows); fails with no change
+  // when the pool runs out
+  ifx_status reserve(int seq, size_t rows, cudaStream_t st);
+  void release(int seq);
   ~KvBatch();
 };
 

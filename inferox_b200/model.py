@@ -94,9 +94,11 @@ class Model:
     def kv_cache(self, max_seq: int | None = None) -> "KvCache":
         return KvCache(self, max_seq or int(self.config.context_length))
 
-    def kv_batch(self, batch: int, max_seq: int | None = None) -> "KvBatch":
-        """`batch` independent sequences decoded together (one weight read per step)."""
-        return KvBatch(self, batch, max_seq or int(self.config.context_length))
+    def kv_batch(self, batch: int, max_seq: int | None = None, pages: int = 0) -> "KvBatch":
+        """`batch` independent sequences decoded together (one weight read per
+        step). pages > 0: the caches share a pool of that many 64-position
+        pages, taken as sequences grow and returned by reset()."""
+        return KvBatch(self, batch, max_seq or int(self.config.context_length), pages)
 
     def prefill(self, ids, kv: "KvCache", last_row_only: bool = False) -> np.ndarray:
         ids = np.ascontiguousarray(ids, np.uint32)
@@ -184,12 +186,24 @@ class KvCache:
 class KvBatch:
     """`batch` KV caches decoded together: prefill each sequence, then step all."""
 
-    def __init__(self, model: Model, batch: int, max_seq: int):
+    PAGE_ROWS = 64
+
+    def __init__(self, model: Model, batch: int, max_seq: int, pages: int = 0):
         self._model = model
         h = C.c_void_p()
-        check(lib.ifx_kv_batch_create(model._h, max_seq, batch, C.byref(h)), "kv_batch_create")
+        if pages:
+            check(lib.ifx_kv_batch_create_paged(model._h, max_seq, batch, pages, C.byref(h)),
+                  "kv_batch_create_paged")
+        else:
+            check(lib.ifx_kv_batch_create(model._h, max_seq, batch, C.byref(h)), "kv_batch_create")
         self._h = h
         self.batch, self.max_seq = batch, max_seq
+
+    def pages(self) -> tuple[int, int]:
+        """(free pages, pool pages) of a paged batch; (0, 0) otherwise."""
+        f, t = C.c_size_t(0), C.c_size_t(0)
+        check(lib.ifx_kv_batch_pages(self._h, C.byref(f), C.byref(t)), "kv_batch_pages")
+        return int(f.value), int(t.value)
 
     def close(self):
         if getattr(self, "_h", None) is not None and self._h.value:

@@ -17,6 +17,14 @@ request leaves when it has max_tokens tokens or emits `eos`; its slot takes
 the next request on the following step. A finished request's last token is
 not fed back (the reference feeds it and discards the logits), so a request
 needs len(prompt) + max_tokens - 1 cache rows.
+
+Over a paged batch (Server.for_model(..., pages=P): the slots share a pool
+of P cache pages) the pool can run dry. A prefill that finds too few pages
+leaves its request waiting at the front until a finishing request returns
+some; a decode step that finds none preempts the most recently admitted
+request (its slot is reset, returning its pages, and it starts again from
+its prompt when pages are free), then retries with the others. A restarted
+request produces the tokens it would have produced alone.
 """
 from __future__ import annotations
 
@@ -24,6 +32,11 @@ from collections import deque
 from dataclasses import dataclass, field
 
 import numpy as np
+
+
+def _pool_empty(e: BaseException) -> bool:
+    """The error a paged batch raises when its page pool has no page left."""
+    return getattr(e, "name", None) == "OutOfMemory"
 
 
 def last_argmax(x) -> int:
@@ -40,6 +53,8 @@ class _Request:
     eos: int | None
     tokens: list = field(default_factory=list)
     done: bool = False
+    order: int = 0  # admission count when it took its slot
+    restarts: int = 0  # times it was preempted
 
 
 class Server:
@@ -53,11 +68,15 @@ class Server:
         self.waiting: deque[_Request] = deque()
         self.requests: dict[int, _Request] = {}
         self._next = 0
+        self._admitted = 0
         self.steps = 0  # batched decode steps run
+        self.preemptions = 0
+        # paged: a finished request's slot is reset at once, returning its pages
+        self.paged = bool(getattr(batch, "pages", None)) and batch.pages()[1] > 0
 
     @classmethod
-    def for_model(cls, model, slots: int, max_seq: int) -> "Server":
-        return cls(model.kv_batch(slots, max_seq))
+    def for_model(cls, model, slots: int, max_seq: int, pages: int = 0) -> "Server":
+        return cls(model.kv_batch(slots, max_seq, pages))
 
     def submit(self, prompt, max_tokens: int, eos: int | None = None) -> int:
         p = np.ascontiguousarray(prompt, np.uint32)
@@ -86,6 +105,12 @@ class Server:
         if len(r.tokens) >= r.max_tokens or (r.eos is not None and r.tokens[-1] == r.eos):
             r.done = True
             self.slots[slot] = None
+            if self.paged:
+                self.kb.reset(slot)
+                self.used[slot] = False
+
+    def _active(self) -> list[int]:
+        return [i for i, r in enumerate(self.slots) if r is not None]
 
     def _admit(self) -> None:
         for slot in range(len(self.slots)):
@@ -99,24 +124,47 @@ class Server:
                     self.kb.reset(slot)
                 self.used[slot] = True
                 logits = self.kb.prefill(slot, r.prompt, True)
-            except BaseException:
+            except BaseException as e:
                 # the request is not lost: it waits at the front again (the
                 # slot is reset before its next use)
                 self.waiting.appendleft(r)
+                if _pool_empty(e) and self._active():
+                    return  # pages come back when an active request finishes
                 raise
             r.tokens.append(last_argmax(logits[0]))
+            r.order = self._admitted
+            self._admitted += 1
             self.slots[slot] = r
             self._finish_if_done(slot)
+
+    def _preempt(self, seqs: list[int]) -> None:
+        """Return the pages of the most recently admitted of `seqs`; its
+        request starts again from its prompt."""
+        slot = max(seqs, key=lambda i: self.slots[i].order)
+        r = self.slots[slot]
+        self.kb.reset(slot)
+        r.tokens.clear()
+        r.restarts += 1
+        self.slots[slot] = None
+        self.waiting.appendleft(r)
+        self.preemptions += 1
 
     def step(self) -> int:
         """Admit, then one decode step of every active slot; returns how many
         sequences the step decoded."""
         self._admit()
-        seqs = [i for i, r in enumerate(self.slots) if r is not None]
-        if not seqs:
-            return 0
-        toks = [self.slots[i].tokens[-1] for i in seqs]
-        _, amax = self.kb.decode_step_seqs(seqs, toks, want_logits=False)
+        while True:
+            seqs = self._active()
+            if not seqs:
+                return 0
+            toks = [self.slots[i].tokens[-1] for i in seqs]
+            try:
+                _, amax = self.kb.decode_step_seqs(seqs, toks, want_logits=False)
+                break
+            except BaseException as e:
+                if not _pool_empty(e) or len(seqs) == 1:
+                    raise
+                self._preempt(seqs)
         self.steps += 1
         for i, t in zip(seqs, amax):
             self.slots[i].tokens.append(int(t))

@@ -138,3 +138,70 @@ def test_failed_prefill_keeps_the_request():
         srv.step()
     assert srv.result(rid) == _alone(prompt, 6)
     assert fb.resets == [0]  # the slot the failed prefill touched was reset
+
+
+class PoolEmpty(RuntimeError):
+    name = "OutOfMemory"
+
+
+class FakePaged(FakeBatch):
+    """FakeBatch over a shared pool of `pages` pages of 4 rows: a call that
+    needs more pages than are free raises the paged batch's OutOfMemory
+    error and changes nothing, as ifx_kv_batch_create_paged's batch does."""
+
+    ROWS = 4
+
+    def __init__(self, batch, max_seq, pages):
+        super().__init__(batch, max_seq)
+        self.total = pages
+
+    def pages(self):
+        used = sum(-(-len(h) // self.ROWS) for h in self.hist)
+        return self.total - used, self.total
+
+    def _need(self, grow):
+        extra = sum(-(-(len(self.hist[s]) + n) // self.ROWS) - -(-len(self.hist[s]) // self.ROWS)
+                    for s, n in grow.items())
+        if extra > self.pages()[0]:
+            raise PoolEmpty("the page pool is exhausted")
+
+    def prefill(self, slot, ids, last_row_only=False):
+        self._need({slot: len(ids)})
+        return super().prefill(slot, ids, last_row_only)
+
+    def decode_step_seqs(self, seqs, tokens, want_logits=True):
+        self._need({s: 1 for s in seqs})
+        return super().decode_step_seqs(seqs, tokens, want_logits)
+
+
+def test_paged_pool_preempts_and_requests_match_solo_runs():
+    """Four slots over a pool that holds far fewer rows than four full
+    requests: prefills wait for pages, decode steps preempt the youngest
+    request, and every request still produces its solo tokens."""
+    rng = np.random.default_rng(5)
+    fb = FakePaged(4, 64, pages=9)  # 36 rows for 4 slots of up to 64
+    srv = Server(fb)
+    assert srv.paged
+    reqs = []
+    for i in range(10):
+        p = rng.integers(3, V, size=int(rng.integers(2, 10)))
+        n = int(rng.integers(4, 16))
+        reqs.append((srv.submit(p, n), p, n))
+    out = srv.run()
+    for rid, p, n in reqs:
+        assert out[rid] == _alone(p, n), rid
+    assert srv.preemptions > 0
+    assert fb.pages() == (9, 9)  # every page returned
+
+
+def test_paged_pool_too_small_for_one_request():
+    fb = FakePaged(2, 64, pages=2)
+    srv = Server(fb)
+    srv.submit(list(range(3, 12)), 4)  # 9 prompt rows need 3 pages
+    with pytest.raises(PoolEmpty):
+        srv.step()
+    fb2 = FakePaged(2, 64, pages=2)
+    srv2 = Server(fb2)
+    srv2.submit([3, 4, 5], 12)  # fits at admission, outgrows the pool alone
+    with pytest.raises(PoolEmpty):
+        srv2.run()
