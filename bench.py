@@ -243,6 +243,117 @@ def run_reference(args):
     print(json.dumps(line), flush=True)
 
 
+def run_70b_leg(args, dist, rank, world, local, hbm):
+    """The 70B-shaped workload (2048-token prompt, then greedy decode) on all
+    `world` GPUs: tensor parallel with one rank per GPU, or one GPU alone.
+    Device-timed like the main line (max over ranks). A failure on any rank is
+    reported in the result, never fatal: each rank catches its own error and
+    the ranks agree through one all-reduce."""
+    import numpy as np
+    import torch
+    from inferox_b200 import Model, synth, tp
+
+    wl = WORKLOADS["70b"]
+    steps, warm = min(args.steps, 32), 3
+    err, ms, pf_s, kernels, wbytes = "", 0.0, 0.0, 0, 0
+    m = kv = tcomm = None
+    gpath = None
+    t0 = time.time()
+    try:
+        if world > 1:
+            gpath = os.path.join("/dev/shm" if os.path.isdir("/dev/shm") else tempfile.gettempdir(),
+                                 f"ifx_bench_70b_scale_{os.getppid()}.gguf")
+            if rank == 0:
+                synth.build("70b").tofile(gpath + ".part")
+                os.replace(gpath + ".part", gpath)
+    except Exception as e:  # noqa: BLE001
+        err = repr(e)[:300]
+    if dist:
+        dist.barrier()
+    t_gen = time.time() - t0
+    try:
+        if not err:
+            if world > 1:
+                uid = torch.zeros(128, dtype=torch.uint8, device="cuda")
+                if rank == 0:
+                    uid.copy_(torch.frombuffer(bytearray(tp.unique_id()), dtype=torch.uint8))
+                dist.broadcast(uid, 0)
+                tcomm = tp.Comm(bytes(uid.cpu().numpy()), world, rank, local)
+                m = Model.open(gpath, device=local, tp_size=world, tp_rank=rank,
+                               nccl_comm=tcomm.handle, tp_timeout_ms=120000)
+            else:
+                m = Model.from_bytes(synth.build("70b"), device=local)
+            V = int(m.config.vocab_size)
+            kv = m.kv_cache(wl["min_ctx"])
+            prompt = synth.prompt_ids(V, wl["prompt"], seq_index=0)
+            m.prefill(prompt[:64], kv, last_row_only=True)  # first-call costs out of the timing
+            kv.clear()
+            torch.cuda.synchronize()
+            tpf = time.perf_counter()
+            f0 = int(np.argmax(m.prefill(prompt, kv, last_row_only=True)[0]))
+            pf_s = time.perf_counter() - tpf
+            m.decode_greedy(f0, warm, kv)
+            kernels = kv.decode_kernels()
+            wbytes = m.decode_weight_bytes()
+    except Exception as e:  # noqa: BLE001
+        err = repr(e)[:300]
+
+    def all_ok(e: str) -> bool:
+        if not dist:
+            return not e
+        f = torch.tensor([0.0 if e else 1.0], device="cuda")
+        dist.all_reduce(f, op=dist.ReduceOp.MIN)
+        return f.item() > 0
+
+    ctx0 = 0
+    if all_ok(err):
+        if dist:
+            dist.barrier()
+        torch.cuda.synchronize()
+        try:
+            ctx0 = len(kv)
+            _, t = m.decode_greedy(f0, steps, kv, timed=True)
+            ms = t / steps
+        except Exception as e:  # noqa: BLE001
+            err = repr(e)[:300]
+    elif not err:
+        err = "failed on another rank"
+    ok = torch.tensor([0.0 if err else 1.0, ms, pf_s], device="cuda")
+    if dist:
+        okmin = ok.clone()
+        dist.all_reduce(okmin, op=dist.ReduceOp.MIN)
+        dist.all_reduce(ok, op=dist.ReduceOp.MAX)
+        good = okmin[0].item() > 0
+    else:
+        good = not err
+    del kv, m  # before the communicator
+    if tcomm is not None:
+        tcomm.close()
+    if gpath and rank == 0 and os.path.exists(gpath):
+        os.remove(gpath)
+    if not good:
+        return {"n_gpus": world, "error": err or "failed on another rank"}
+    ms, pf_s = float(ok[1].item()), float(ok[2].item())
+    c = synth.CONFIGS["70b"]
+    kvh = c["n_kv_heads"] // world
+    hd = c["dim"] // c["n_heads"]
+    kv_bytes = 2 * c["n_layers"] * kvh * hd * 2 * (ctx0 + steps / 2)
+    per_gpu = wbytes + kv_bytes
+    gbs = per_gpu / (ms * 1e-3) / 1e9
+    return {"workload": f"{wl['name']}: {wl['prompt']}-token prompt prefill, then batch-1 greedy decode",
+            "n_gpus": world, "tok_s": 1000.0 / ms, "tok_s_per_gpu": 1000.0 / ms / world,
+            "ms_per_step": ms, "steps": steps, "warmup": warm, "decode_context": [ctx0, ctx0 + steps],
+            "scaling": "strong",
+            "parallelism": ("single GPU" if world == 1 else f"tp{world}: " + (
+                "persistent kernel, all-reduces over NVLink peer memory inside the step"
+                if kernels == 1 else "per-op kernels, NCCL all-reduce after Wo and W2")),
+            "hbm_roofline": {"bytes_per_step_per_gpu": per_gpu, "achieved_gbs_per_gpu": gbs,
+                             "peak_gbs": hbm, "frac": gbs / hbm,
+                             "roofline_tok_s": hbm * 1e9 / per_gpu},
+            "prefill": {"tokens": wl["prompt"], "s": pf_s, "tok_s": wl["prompt"] / pf_s},
+            "gpu_launches": steps * kernels, "setup_s": {"synth": t_gen}}
+
+
 def run_ours(args):
     import numpy as np
     import torch
@@ -395,7 +506,7 @@ def run_ours(args):
         if rank == 0:
             uid.copy_(torch.frombuffer(bytearray(tp.unique_id()), dtype=torch.uint8))
         dist.broadcast(uid, 0)
-        tp_err, tp_ms, tp_prefill_s = "", 0.0, 0.0
+        tp_err, tp_ms, tp_prefill_s, tp_kernels = "", 0.0, 0.0, 0
         tcomm = mt = kvt = None
 
         def all_ok(err: str) -> bool:
@@ -413,6 +524,7 @@ def run_ours(args):
             f0 = int(np.argmax(mt.prefill(p0, kvt, last_row_only=True)[0]))
             tp_prefill_s = time.perf_counter() - tpf
             mt.decode_greedy(f0, args.warmup, kvt)
+            tp_kernels = kvt.decode_kernels()
         except Exception as e:  # noqa: BLE001 (reported in the line, never fatal)
             tp_err = repr(e)[:300]
         if all_ok(tp_err):
@@ -433,7 +545,9 @@ def run_ours(args):
             t_ms = float(ok[1].item())
             tpleg = {"n_gpus": world, "tok_s": 1000.0 / t_ms, "ms_per_step": t_ms,
                      "prefill_tok_s": PROMPT / tp_prefill_s, "scaling": "strong",
-                     "parallelism": f"tp{world} (NCCL all-reduce after Wo and W2)"}
+                     "parallelism": f"tp{world}: " + (
+                         "persistent kernel, all-reduces over NVLink peer memory inside the step"
+                         if tp_kernels == 1 else "per-op kernels, NCCL all-reduce after Wo and W2")}
         else:
             tpleg = {"n_gpus": world, "error": tp_err or "failed on another rank"}
         del kvt, mt  # the cache's CUDA graph holds NCCL work: release it before the comm
@@ -453,6 +567,17 @@ def run_ours(args):
     kv_bytes = 2 * L * (G // world if tp_mode else G) * hd * 2 * ctx_mean
     step_bytes = m.decode_weight_bytes() + kv_bytes
     step_gbs = step_bytes / (ms_step * 1e-3) / 1e9
+    tp_placement = (f"tp{world}: " + ("persistent kernel, all-reduces over NVLink peer memory inside the step"
+                                      if kernels_per_step == 1 else "per-op kernels, NCCL all-reduce after Wo and W2"))
+
+    # the 70B-shaped config at this GPU count: one
+    # sequence, tensor parallel over all N GPUs (a single GPU at N = 1)
+    scale70 = None
+    if args.config == "8b" and not args.no_70b and not args.layers:
+        del kv, m  # room for the 70B weights
+        kv = m = None
+        torch.cuda.synchronize()
+        scale70 = run_70b_leg(args, dist, rank, world, local, hbm)
 
     def finish():
         nonlocal m, kv
@@ -482,7 +607,7 @@ def run_ours(args):
         "dtype": "f16 tensor-core operands (exact small-integer weights; activations as hi + lo f16 planes, ~22 bits), f32 accumulate; f16 KV cache",
         "data": "synthetic (seeded N(0,0.02) weights quantised Q4_K_M; seeded uniform prompt ids)",
         "config": bench_config(args),
-        "placement": (f"tp{world} (NCCL all-reduce after Wo and W2)" if tp_mode
+        "placement": (tp_placement if tp_mode
                       else f"replicas x{world}, one sequence per GPU" if world > 1 else "single GPU"),
         "global_batch": seqs,
         "hbm_roofline": {"bytes_per_step": step_bytes, "achieved_gbs": step_gbs, "peak_gbs": hbm,
@@ -492,6 +617,7 @@ def run_ours(args):
         "batched_decode": batch,
         "matmul_microbench": micro,
         "tensor_parallel": tpleg,
+        "scale_70b": scale70,
         # the dominant kernel is the decode step itself: with the persistent
         # path one launch per token, so achieved = algorithmic step bytes over
         # the device time of one step
@@ -616,6 +742,9 @@ def main():
     ap.add_argument("--microbench", action="store_true",
                     help="only the dequant-fused matmul microbench: 4 types x 4 shapes x batch "
                          "1/8/64/512, one JSON line")
+    ap.add_argument("--no-70b", action="store_true",
+                    help="skip the 70B-shaped leg of the default run (tensor parallel over all "
+                         "GPUs; one GPU at N = 1)")
     ap.add_argument("--no-microbench", action="store_true",
                     help="skip the one-shape microbench leg of the default run")
     ap.add_argument("--vocab", type=int, default=0,

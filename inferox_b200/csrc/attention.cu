@@ -31,12 +31,65 @@ __host__ __device__ __forceinline__ int attn_rows(int max_seq, int ns) {
   return ((max_seq + ns - 1) / ns + 1 + 15) & ~15;
 }
 
-// TC: scores and P V on tensor cores (head size a multiple of 64, at most four
-// query heads per kv head): S = K Q^T with the chunk-swizzled cache rows as
-// ldmatrix A fragments and the query heads as B columns (column j the hi f16
-// plane of head j, column 4 + j its lo plane), O^T = V^T P the same way with
-// ldmatrix.trans; otherwise FMA loops.
-template <bool TC>
+// Combine the NS partial softmaxes of kv head h (run by the CTA that
+// finished the head's last split): weights exp(m_s - M) / L per split and
+// head, then the weighted sum of the partial outputs. All loads of a phase
+// are issued together (one L2 round trip each) instead of a serial walk.
+__device__ __noinline__ void attn_combine(const float *part_o, const float2 *part_ml,
+                                          float *attn_out, int *counters, int h, int NS,
+                                          int grp, int hd, int tid, int nthr) {
+  __shared__ float c_m[kMaxSplits * kMaxGroup], c_w[kMaxSplits * kMaxGroup], c_M[kMaxGroup],
+      c_L[kMaxGroup];
+  for (int e = tid; e < NS * grp; e += nthr) {
+    const float2 ml = __ldcg(&part_ml[h * NS * grp + e]);
+    c_m[e] = ml.x;
+    c_w[e] = ml.y;
+  }
+  __syncthreads();
+  if (tid < grp) {
+    float M = -INFINITY;
+    for (int t = 0; t < NS; ++t)
+      if (c_w[t * grp + tid] > 0.f) M = fmaxf(M, c_m[t * grp + tid]);
+    float L = 0.f;
+    for (int t = 0; t < NS; ++t)
+      if (c_w[t * grp + tid] > 0.f) L = fmaf(c_w[t * grp + tid], expf(c_m[t * grp + tid] - M), L);
+    c_M[tid] = M;
+    c_L[tid] = L;
+  }
+  __syncthreads();
+  for (int e = tid; e < NS * grp; e += nthr) {
+    const int j = e % grp;
+    c_w[e] = (c_w[e] > 0.f) ? expf(c_m[e] - c_M[j]) / c_L[j] : 0.f;
+  }
+  __syncthreads();
+  const float4 *po4 = reinterpret_cast<const float4 *>(part_o + (size_t)h * NS * grp * hd);
+  float4 *out4 = reinterpret_cast<float4 *>(attn_out + (size_t)h * grp * hd);
+  const int n4 = grp * hd / 4;
+  for (int e4 = tid; e4 < n4; e4 += nthr) {
+    const int j = (e4 * 4) / hd;
+    float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll 8
+    for (int t = 0; t < NS; ++t) {
+      const float w = c_w[t * grp + j];
+      const float4 p = __ldcg(&po4[(size_t)t * n4 + e4]);
+      o.x = fmaf(w, p.x, o.x);
+      o.y = fmaf(w, p.y, o.y);
+      o.z = fmaf(w, p.z, o.z);
+      o.w = fmaf(w, p.w, o.w);
+    }
+    out4[e4] = o;
+  }
+  if (tid == 0) counters[h] = 0;
+}
+
+// W = 4 or 8: scores and P V on tensor cores (head size a multiple of 64, at
+// most W query heads per kv head): S = K Q^T with the chunk-swizzled cache
+// rows as ldmatrix A fragments and the query heads as B columns carrying
+// each head's hi and lo f16 planes, O^T = V^T P the same way with
+// ldmatrix.trans. W = 4: one 8-column tile (column j the hi plane of head j,
+// column 4 + j its lo plane, added across lanes); W = 8: two tiles (hi
+// planes, lo planes). W = 0: FMA loops.
+template <int W>
 __global__ void __launch_bounds__(kAttnThreads) decode_attn_kernel(const __grid_constant__ DecodeAttnArgs a) {
   extern __shared__ __align__(128) uint8_t smraw[];
   const int h = blockIdx.x, s = blockIdx.y, b = blockIdx.z, tid = threadIdx.x;
@@ -53,12 +106,14 @@ __global__ void __launch_bounds__(kAttnThreads) decode_attn_kernel(const __grid_
   __half *Ks = reinterpret_cast<__half *>(smraw);  // [cap][hd]
   __half *Vs = Ks + (size_t)cap * hd;               // [cap][hd]
   // FMA path: q [grp][hd] f32, scores [grp][cap]; tensor-core path: q hi/lo
-  // [8][hd + 8] halves, scores [4][cap], p hi/lo [8][cap + 8] halves
+  // [2][W][hd + 8] halves, scores [W][cap], p hi/lo [2][W][cap + 8] halves
+  constexpr bool TC = W > 0;
+  constexpr int NT = W / 4;  // 8-column B tiles per MMA step
   const int qs_ = hd + 8, ps_ = cap + 8;
   float *qs = reinterpret_cast<float *>(Vs + (size_t)cap * hd);
   __half *qh = Vs + (size_t)cap * hd;
-  float *sc = TC ? reinterpret_cast<float *>(qh + 8 * qs_) : qs + grp * hd;
-  __half *ph = reinterpret_cast<__half *>(sc + 4 * cap);
+  float *sc = TC ? reinterpret_cast<float *>(qh + 2 * W * qs_) : qs + grp * hd;
+  __half *ph = reinterpret_cast<__half *>(sc + W * cap);
   __shared__ float s_m[kMaxGroup], s_l[kMaxGroup];
   __shared__ int s_last;
   __shared__ __align__(8) uint64_t bar;
@@ -107,7 +162,7 @@ __global__ void __launch_bounds__(kAttnThreads) decode_attn_kernel(const __grid_
 
   const float *q = qkv + (size_t)h * grp * hd;
   const int rpos = a.rope_compat ? 0 : pos;
-  for (int e = tid; e < (TC ? 4 : grp) * hd / 2; e += kAttnThreads) {
+  for (int e = tid; e < (TC ? W : grp) * hd / 2; e += kAttnThreads) {
     const int j = e / (hd / 2), i = 2 * (e % (hd / 2));
     float x0 = 0.f, x1 = 0.f;
     if (j < grp) {
@@ -118,7 +173,7 @@ __global__ void __launch_bounds__(kAttnThreads) decode_attn_kernel(const __grid_
     if (TC) {
       const __half2 hi = __floats2half2_rn(x0, x1);
       *reinterpret_cast<__half2 *>(qh + j * qs_ + i) = hi;
-      *reinterpret_cast<__half2 *>(qh + (4 + j) * qs_ + i) =
+      *reinterpret_cast<__half2 *>(qh + (W + j) * qs_ + i) =
           __floats2half2_rn(x0 - __low2float(hi), x1 - __high2float(hi));
     } else {
       qs[j * hd + i] = x0;
@@ -154,33 +209,40 @@ __global__ void __launch_bounds__(kAttnThreads) decode_attn_kernel(const __grid_
       *reinterpret_cast<__half2 *>(Vs + (size_t)nk * hd + 2 * e) = __floats2half2_rn(0.f, 0.f);
     const float isq = 1.0f / sqrtf((float)hd);
     for (int mt = warp; mt < nk16 / 16; mt += kAttnThreads / 32) {
-      float D[4] = {0.f, 0.f, 0.f, 0.f};
+      float D[NT][4] = {};
       const int row = 16 * mt + (lane & 7) + 8 * ((lane >> 3) & 1);
       const int key = kv_col(t0 + row, 0, hd) >> 3;
-      const __half *qp = qh + g * qs_ + 2 * c;  // column g: plane g / 4, head g % 4
       for (int ks = 0; ks < hd / 16; ++ks) {
         uint32_t av[4];
         ldsm_x4(av, smem_u32(Ks + (size_t)row * hd + (((2 * ks + (lane >> 4)) ^ key) << 3)));
-        mma_16816(D, av[0], av[1], av[2], av[3], *reinterpret_cast<const uint32_t *>(qp + 16 * ks),
-                  *reinterpret_cast<const uint32_t *>(qp + 16 * ks + 8), D);
-      }
 #pragma unroll
-      for (int i2 = 0; i2 < 4; ++i2) D[i2] += __shfl_xor_sync(0xffffffffu, D[i2], 2);  // hi + lo
-      if (c < 2) {
+        for (int t = 0; t < NT; ++t) {
+          // tile t, column g: row 8 t + g of qh (W = 4: plane g / 4, head g % 4)
+          const __half *qp = qh + (8 * t + g) * qs_ + 2 * c + 16 * ks;
+          mma_16816(D[t], av[0], av[1], av[2], av[3], *reinterpret_cast<const uint32_t *>(qp),
+                    *reinterpret_cast<const uint32_t *>(qp + 8), D[t]);
+        }
+      }
+      float S[4];
+#pragma unroll
+      for (int i2 = 0; i2 < 4; ++i2)  // hi + lo
+        S[i2] = NT == 2 ? D[0][i2] + D[NT - 1][i2]
+                        : D[0][i2] + __shfl_xor_sync(0xffffffffu, D[0][i2], 2);
+      if (NT == 2 || c < 2) {
         const int ra = 16 * mt + g, rb = ra + 8;
 #pragma unroll
         for (int jj = 0; jj < 2; ++jj) {
           const int j2 = 2 * c + jj;
           if (j2 < grp) {
-            sc[j2 * cap + ra] = ra < nk ? D[jj] * isq : -INFINITY;  // forward.rs:396
-            sc[j2 * cap + rb] = rb < nk ? D[2 + jj] * isq : -INFINITY;
+            sc[j2 * cap + ra] = ra < nk ? S[jj] * isq : -INFINITY;  // forward.rs:396
+            sc[j2 * cap + rb] = rb < nk ? S[2 + jj] * isq : -INFINITY;
           }
         }
       }
     }
     __syncthreads();
-    {  // softmax statistics of this split (warp j = head j); p as hi/lo planes
-      const int j2 = warp;
+    for (int j2 = warp; j2 < W; j2 += kAttnThreads / 32) {
+      // softmax statistics of this split (head j2); p as hi/lo planes
       float m = -INFINITY;
       if (j2 < grp)
         for (int t = lane; t < nk; t += 32) m = fmaxf(m, sc[j2 * cap + t]);
@@ -190,7 +252,7 @@ __global__ void __launch_bounds__(kAttnThreads) decode_attn_kernel(const __grid_
         const float p = (j2 < grp && t < nk) ? expf(sc[j2 * cap + t] - m) : 0.f;
         const __half hp = __float2half_rn(p);
         ph[j2 * ps_ + t] = hp;
-        ph[(4 + j2) * ps_ + t] = __float2half_rn(p - __half2float(hp));
+        ph[(W + j2) * ps_ + t] = __float2half_rn(p - __half2float(hp));
         l += p;
       }
       l = warp_sum(l);
@@ -201,25 +263,31 @@ __global__ void __launch_bounds__(kAttnThreads) decode_attn_kernel(const __grid_
     }
     __syncthreads();
     for (int mt = warp; mt < hd / 16; mt += kAttnThreads / 32) {
-      float D[4] = {0.f, 0.f, 0.f, 0.f};
-      const __half *pp = ph + g * ps_ + 2 * c;
+      float D[NT][4] = {};
       for (int ks = 0; ks < nk16 / 16; ++ks) {
         const int t = 16 * ks + (lane & 7) + 8 * (lane >> 4);
         const int ch = (2 * mt + ((lane >> 3) & 1)) ^ (kv_col(t0 + t, 0, hd) >> 3);
         uint32_t av[4];
         ldsm_x4_t(av, smem_u32(Vs + (size_t)t * hd + (ch << 3)));
-        mma_16816(D, av[0], av[1], av[2], av[3], *reinterpret_cast<const uint32_t *>(pp + 16 * ks),
-                  *reinterpret_cast<const uint32_t *>(pp + 16 * ks + 8), D);
-      }
 #pragma unroll
-      for (int i2 = 0; i2 < 4; ++i2) D[i2] += __shfl_xor_sync(0xffffffffu, D[i2], 2);
-      if (c < 2) {
+        for (int tt = 0; tt < NT; ++tt) {
+          const __half *pp = ph + (8 * tt + g) * ps_ + 2 * c + 16 * ks;
+          mma_16816(D[tt], av[0], av[1], av[2], av[3], *reinterpret_cast<const uint32_t *>(pp),
+                    *reinterpret_cast<const uint32_t *>(pp + 8), D[tt]);
+        }
+      }
+      float O[4];
+#pragma unroll
+      for (int i2 = 0; i2 < 4; ++i2)
+        O[i2] = NT == 2 ? D[0][i2] + D[NT - 1][i2]
+                        : D[0][i2] + __shfl_xor_sync(0xffffffffu, D[0][i2], 2);
+      if (NT == 2 || c < 2) {
 #pragma unroll
         for (int jj = 0; jj < 2; ++jj) {
           const int j2 = 2 * c + jj;
           if (j2 < grp) {
-            po[j2 * hd + 16 * mt + g] = D[jj];
-            po[j2 * hd + 16 * mt + g + 8] = D[2 + jj];
+            po[j2 * hd + 16 * mt + g] = O[jj];
+            po[j2 * hd + 16 * mt + g + 8] = O[2 + jj];
           }
         }
       }
@@ -286,50 +354,280 @@ __global__ void __launch_bounds__(kAttnThreads) decode_attn_kernel(const __grid_
   __syncthreads();
   if (!s_last) return;
   __threadfence();
-  // Combine the NS partial softmaxes of this kv head. All loads of a phase
-  // are issued together (one L2 round trip each) instead of a serial walk.
-  __shared__ float c_m[kMaxSplits * kMaxGroup], c_w[kMaxSplits * kMaxGroup], c_M[kMaxGroup],
-      c_L[kMaxGroup];
-  for (int e = tid; e < NS * grp; e += kAttnThreads) {
-    const float2 ml = __ldcg(&part_ml[h * NS * grp + e]);
-    c_m[e] = ml.x;
-    c_w[e] = ml.y;
-  }
-  __syncthreads();
-  if (tid < grp) {
-    float M = -INFINITY;
-    for (int t = 0; t < NS; ++t)
-      if (c_w[t * grp + tid] > 0.f) M = fmaxf(M, c_m[t * grp + tid]);
-    float L = 0.f;
-    for (int t = 0; t < NS; ++t)
-      if (c_w[t * grp + tid] > 0.f) L = fmaf(c_w[t * grp + tid], expf(c_m[t * grp + tid] - M), L);
-    c_M[tid] = M;
-    c_L[tid] = L;
-  }
-  __syncthreads();
-  for (int e = tid; e < NS * grp; e += kAttnThreads) {
-    const int j = e % grp;
-    c_w[e] = (c_w[e] > 0.f) ? expf(c_m[e] - c_M[j]) / c_L[j] : 0.f;
-  }
-  __syncthreads();
-  const float4 *po4 = reinterpret_cast<const float4 *>(part_o + (size_t)h * NS * grp * hd);
-  float4 *out4 = reinterpret_cast<float4 *>(attn_out + (size_t)h * grp * hd);
-  const int n4 = grp * hd / 4;
-  for (int e4 = tid; e4 < n4; e4 += kAttnThreads) {
-    const int j = (e4 * 4) / hd;
-    float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll 8
-    for (int t = 0; t < NS; ++t) {
-      const float w = c_w[t * grp + j];
-      const float4 p = __ldcg(&po4[(size_t)t * n4 + e4]);
-      o.x = fmaf(w, p.x, o.x);
-      o.y = fmaf(w, p.y, o.y);
-      o.z = fmaf(w, p.z, o.z);
-      o.w = fmaf(w, p.w, o.w);
+  attn_combine(part_o, part_ml, attn_out, counters, h, NS, grp, hd, tid, kAttnThreads);
+}
+
+// ------------------------------------------------------ decode, streamed --
+// Split-K decode attention for head sizes 64 and 128 with at most eight
+// query heads per kv head, written for many cached rows per CTA (the batched
+// step, long contexts). A split covers consecutive 16-row tiles of one
+// sequence's kv head; warp w of the CTA takes tiles w, w + 4, ... and keeps
+// its own online softmax (flash decoding), so no CTA-wide barrier sits in
+// the loop. Each warp double-buffers its tiles: lane 0 bulk-copies tile
+// i + 2 while the warp computes tile i.
+//
+// Per tile, on tensor cores (mma.m16n8k16, f16 in, f32 accumulate):
+//   S^T = Q K^T  with Q as the A operand, rows 0-7 the hi f16 planes of the
+//                query heads and rows 8-15 their lo planes (about 22 bits;
+//                rows beyond the group are zero), K^T from ldmatrix on the
+//                chunk-swizzled cache rows; lane (g, c) ends with head g's
+//                hi and lo scores of positions 8 nt + 2c (+1), added in-lane;
+//   O += P V     with P re-used from the score registers as the A operand
+//                (rows 0-7 hi planes, 8-15 lo planes of the probabilities)
+//                and V from ldmatrix.trans; the hi and lo halves of O are
+//                added at the end.
+// The four warps' (m, l, O) are merged through shared memory into the
+// split's partial, and the CTA that finishes a kv head's last split combines
+// the partials (the same format and combine as decode_attn_kernel).
+constexpr int kFlashWarps = 4;
+constexpr int kFlashRows = 16;  // cache rows per tile
+
+template <int HD>
+__host__ __device__ constexpr int flash_smem_bytes() {
+  // stages [warp][2][K tile | V tile] halves, Q [16][HD + 8] halves, 8 mbarriers
+  return kFlashWarps * 2 * 2 * kFlashRows * HD * 2 + 16 * (HD + 8) * 2 + kFlashWarps * 2 * 8;
+}
+
+template <int HD>
+__global__ void __launch_bounds__(kFlashWarps * 32, 3)
+    decode_attn_flash_kernel(const __grid_constant__ DecodeAttnArgs a) {
+  constexpr int KSTEPS = HD / 16, NDT = HD / 8, TH = kFlashRows * HD, QS = HD + 8;
+  extern __shared__ __align__(128) uint8_t smraw[];
+  __half *stage = reinterpret_cast<__half *>(smraw);  // [warp][2][2][TH]
+  __half *qsm = stage + kFlashWarps * 2 * 2 * TH;      // [16][QS]
+  uint64_t *bars = reinterpret_cast<uint64_t *>(qsm + 16 * QS);  // [warp][2]
+  __shared__ float s_m[kFlashWarps][kMaxGroup], s_l[kFlashWarps][kMaxGroup];
+  __shared__ int s_last;
+  const int h = blockIdx.x, s = blockIdx.y, b = blockIdx.z, tid = threadIdx.x;
+  const int warp = tid >> 5, lane = tid & 31, g = lane >> 2, c = lane & 3;
+  const int grp = a.H / a.G, NS = a.ns;
+  const float *qkv = a.qkv + (size_t)b * a.qkv_stride;
+  const int sq = a.slot ? a.slot[b] : b;
+  float *part_o = a.part_o + (size_t)b * a.G * NS * grp * HD;
+  float2 *part_ml = a.part_ml + (size_t)b * a.G * NS * grp;
+  int *counters = a.counters + (size_t)b * a.G;
+  float *attn_out = a.attn_out + (size_t)b * a.H * HD;
+
+  // cache row t of this sequence's kv head h (paged: a page holds page_rows
+  // rows of every layer and kv head; a 16-row tile never straddles pages)
+  auto row_off = [&](int t) -> size_t {
+    if (a.page_table) {
+      const int pg = a.page_table[(size_t)sq * a.max_pages + t / a.page_rows];
+      return (size_t)pg * a.page_stride + ((size_t)h * a.page_rows + t % a.page_rows) * HD;
     }
-    out4[e4] = o;
+    return (size_t)sq * a.kv_seq_stride + ((size_t)h * a.max_seq + t) * HD;
+  };
+
+  // tiles of this split (the sequence's rows 0..pos, pos the new token)
+  const int pos = a.pos[sq];
+  const int ntile = (pos + 1 + kFlashRows - 1) / kFlashRows;
+  const int per = (ntile + NS - 1) / NS;
+  const int tb = min(ntile, s * per), te = min(ntile, tb + per);
+  __half *myst = stage + (size_t)warp * 2 * 2 * TH;
+  uint64_t *mybar = bars + warp * 2;
+  // rows of tile T that come from the cache (those before pos)
+  uint32_t iss[2] = {0u, 0u}, done[2] = {0u, 0u};  // lane 0: copies issued / waited per stage
+  auto issue = [&](int T, int st) {
+    ++iss[st];
+    const int t0 = T * kFlashRows;
+    const int nold = max(0, min(t0 + kFlashRows, pos) - t0);
+    __half *dk = myst + (size_t)st * 2 * TH;
+    if (nold > 0) {
+      const size_t off = row_off(t0);
+      mbar_arrive_expect_tx(&mybar[st], 2u * (uint32_t)nold * HD * 2u);
+      bulk_g2s(dk, a.kc + off, (uint32_t)nold * HD * 2u, &mybar[st]);
+      bulk_g2s(dk + TH, a.vc + off, (uint32_t)nold * HD * 2u, &mybar[st]);
+    } else {
+      mbar_arrive(&mybar[st]);
+    }
+  };
+  if (lane == 0) {
+    mbar_init(&mybar[0], 1);
+    mbar_init(&mybar[1], 1);
+    fence_mbar_init();
+    // the cached rows were written by kernels that completed before the
+    // previous kernel in the stream began its main phase
+    if (tb + warp < te) issue(tb + warp, 0);
+    if (tb + warp + kFlashWarps < te) issue(tb + warp + kFlashWarps, 1);
   }
-  if (tid == 0) counters[h] = 0;
+
+  pdl_wait();
+  pdl_launch();
+
+  if (a.zero_ptr && b == 0) {
+    const int nb = a.G * NS, bi = h * NS + s;
+    for (int i = bi * blockDim.x + tid; i < a.zero_n; i += nb * blockDim.x) a.zero_ptr[i] = 0.f;
+  }
+  // the query heads of this kv head, rotated, as hi / lo f16 rows of Q
+  const int rpos = a.rope_compat ? 0 : pos;
+  {
+    const float *q = qkv + (size_t)h * grp * HD;
+    for (int e = tid; e < 8 * HD / 2; e += kFlashWarps * 32) {
+      const int j = e / (HD / 2), i = 2 * (e % (HD / 2));
+      float x0 = 0.f, x1 = 0.f;
+      if (j < grp) {
+        x0 = q[j * HD + i];
+        x1 = q[j * HD + i + 1];
+        if (i < a.rope_dim) rope_pair(x0, x1, i, a.rope_dim, a.rope_base, rpos);
+      }
+      const __half2 hi = __floats2half2_rn(x0, x1);
+      *reinterpret_cast<__half2 *>(qsm + j * QS + i) = hi;
+      *reinterpret_cast<__half2 *>(qsm + (8 + j) * QS + i) =
+          __floats2half2_rn(x0 - __low2float(hi), x1 - __high2float(hi));
+    }
+  }
+  __syncthreads();
+  uint32_t qa[KSTEPS][4];
+#pragma unroll
+  for (int ks = 0; ks < KSTEPS; ++ks)
+    ldsm_x4(qa[ks], smem_u32(qsm + (lane & 15) * QS + ks * 16 + (lane >> 4) * 8));
+
+  float o[NDT][4];
+#pragma unroll
+  for (int i = 0; i < NDT; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
+  float m_run = -INFINITY, l_run = 0.f;
+  const float isq = 1.0f / sqrtf((float)HD);
+  // ldmatrix row addresses of this lane: K (non-trans) and V (trans)
+  const int krow = (lane & 7) + 8 * (lane >> 4), kch = (lane >> 3) & 1;
+  const int vrow = (lane & 7) + 8 * ((lane >> 3) & 1), vch = lane >> 4;
+  bool ok = true;
+  for (int i = 0;; ++i) {
+    const int T = tb + warp + kFlashWarps * i;
+    if (T >= te) break;
+    const int st = i & 1;
+    ok = __all_sync(0xffffffffu, mbar_wait(&mybar[st], (uint32_t)(i >> 1) & 1u, a.err, 306));
+    if (!ok) break;  // the error flag is set; the host reports a timeout
+    ++done[st];
+    __half *Ks = myst + (size_t)st * 2 * TH, *Vs = Ks + TH;
+    const int t0 = T * kFlashRows;
+    if (pos < t0 + kFlashRows) {
+      // the last tile: append this token's K/V (forward.rs:375-378), K
+      // rotated like q, into the cache and this tile; rows beyond it zero
+      const int r = pos - t0;
+      const float *kn = qkv + (size_t)a.H * HD + (size_t)h * HD;
+      const float *vn = qkv + (size_t)(a.H + a.G) * HD + (size_t)h * HD;
+      const size_t off = row_off(pos);
+      for (int e = lane; e < HD / 2; e += 32) {
+        const int ii = 2 * e;
+        float x0 = kn[ii], x1 = kn[ii + 1];
+        if (ii < a.rope_dim) rope_pair(x0, x1, ii, a.rope_dim, a.rope_base, rpos);
+        const __half2 kh = __floats2half2_rn(x0, x1), vh = __floats2half2_rn(vn[ii], vn[ii + 1]);
+        const int ip = kv_col(pos, ii, HD);
+        *reinterpret_cast<__half2 *>(a.kc + off + ip) = kh;
+        *reinterpret_cast<__half2 *>(a.vc + off + ip) = vh;
+        *reinterpret_cast<__half2 *>(Ks + r * HD + ip) = kh;
+        *reinterpret_cast<__half2 *>(Vs + r * HD + ip) = vh;
+      }
+      for (int e = lane; e < (kFlashRows - 1 - r) * HD / 2; e += 32) {
+        reinterpret_cast<__half2 *>(Ks + (r + 1) * HD)[e] = __floats2half2_rn(0.f, 0.f);
+        reinterpret_cast<__half2 *>(Vs + (r + 1) * HD)[e] = __floats2half2_rn(0.f, 0.f);
+      }
+      __syncwarp();
+    }
+    // S^T = Q K^T over the tile's 16 rows (two 8-position n-tiles)
+    float sacc[2][4] = {};
+#pragma unroll
+    for (int ks = 0; ks < KSTEPS; ++ks) {
+      uint32_t kb[4];
+      ldsm_x4(kb, smem_u32(Ks + krow * HD + (((2 * ks + kch) ^ (krow & 7)) << 3)));
+      mma_16816(sacc[0], qa[ks][0], qa[ks][1], qa[ks][2], qa[ks][3], kb[0], kb[1], sacc[0]);
+      mma_16816(sacc[1], qa[ks][0], qa[ks][1], qa[ks][2], qa[ks][3], kb[2], kb[3], sacc[1]);
+    }
+    float sv[2][2];
+    float mt = -INFINITY;
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        const int t = t0 + 8 * nt + 2 * c + j;
+        sv[nt][j] = t <= pos ? (sacc[nt][j] + sacc[nt][2 + j]) * isq : -INFINITY;  // forward.rs:396
+        mt = fmaxf(mt, sv[nt][j]);
+      }
+    mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, 1));
+    mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, 2));
+    const float m_new = fmaxf(m_run, mt);  // finite: row t0 <= pos is in every tile
+    const float alpha = expf(m_run - m_new);
+    m_run = m_new;
+    uint32_t pa[4];
+    float psum = 0.f;
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt) {
+      const float p0 = expf(sv[nt][0] - m_new), p1 = expf(sv[nt][1] - m_new);
+      psum += p0 + p1;
+      const __half2 hp = __floats2half2_rn(p0, p1);
+      const __half2 lp = __floats2half2_rn(p0 - __low2float(hp), p1 - __high2float(hp));
+      pa[2 * nt] = *reinterpret_cast<const uint32_t *>(&hp);
+      pa[2 * nt + 1] = *reinterpret_cast<const uint32_t *>(&lp);
+    }
+    l_run = l_run * alpha + psum;
+#pragma unroll
+    for (int nd = 0; nd < NDT; ++nd) {
+      o[nd][0] *= alpha;
+      o[nd][1] *= alpha;
+      o[nd][2] *= alpha;
+      o[nd][3] *= alpha;
+    }
+    // O += P V: B = V (k = position, n = dimension) from ldmatrix.trans
+#pragma unroll
+    for (int nd = 0; nd < NDT; nd += 2) {
+      uint32_t vb[4];
+      ldsm_x4_t(vb, smem_u32(Vs + vrow * HD + (((nd + vch) ^ (vrow & 7)) << 3)));
+      mma_16816(o[nd], pa[0], pa[1], pa[2], pa[3], vb[0], vb[1], o[nd]);
+      mma_16816(o[nd + 1], pa[0], pa[1], pa[2], pa[3], vb[2], vb[3], o[nd + 1]);
+    }
+    __syncwarp();  // every lane has read this stage
+    if (lane == 0 && T + 2 * kFlashWarps < te) issue(T + 2 * kFlashWarps, st);
+  }
+  // leave no copy in flight after an early exit: wait (bounded) for the
+  // stages this warp issued but did not consume
+  if (lane == 0)
+    for (int i = 0; i < 2; ++i)
+      if (iss[i] > done[i]) mbar_wait(&mybar[i], (iss[i] - 1u) & 1u, nullptr, 0);
+  l_run += __shfl_xor_sync(0xffffffffu, l_run, 1);
+  l_run += __shfl_xor_sync(0xffffffffu, l_run, 2);
+  __syncthreads();  // every warp is done with its stages: reuse them
+  float *mo = reinterpret_cast<float *>(stage);  // [warp][8][HD]
+  if (g < grp) {
+#pragma unroll
+    for (int nd = 0; nd < NDT; ++nd) {
+      float *dst = mo + ((size_t)warp * 8 + g) * HD + 8 * nd + 2 * c;
+      dst[0] = o[nd][0] + o[nd][2];
+      dst[1] = o[nd][1] + o[nd][3];
+    }
+    if (c == 0) {
+      s_m[warp][g] = m_run;
+      s_l[warp][g] = l_run;
+    }
+  }
+  __syncthreads();
+  float *po = part_o + (size_t)(h * NS + s) * grp * HD;
+  for (int e = tid; e < grp * HD; e += kFlashWarps * 32) {
+    const int j = e / HD;
+    float M = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < kFlashWarps; ++w) M = fmaxf(M, s_m[w][j]);
+    float O = 0.f;
+    if (M != -INFINITY)
+#pragma unroll
+      for (int w = 0; w < kFlashWarps; ++w)
+        if (s_m[w][j] != -INFINITY) O = fmaf(expf(s_m[w][j] - M), mo[((size_t)w * 8 + j) * HD + (e % HD)], O);
+    po[e] = O;
+  }
+  if (tid < grp) {
+    float M = -INFINITY, L = 0.f;
+    for (int w = 0; w < kFlashWarps; ++w) M = fmaxf(M, s_m[w][tid]);
+    if (M != -INFINITY)
+      for (int w = 0; w < kFlashWarps; ++w)
+        if (s_m[w][tid] != -INFINITY) L = fmaf(s_l[w][tid], expf(s_m[w][tid] - M), L);
+    part_ml[(h * NS + s) * grp + tid] = make_float2(M, L);  // l = 0 marks an empty split
+  }
+  __threadfence();
+  __syncthreads();
+  if (tid == 0) s_last = atomicAdd(&counters[h], 1) == NS - 1;
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+  attn_combine(part_o, part_ml, attn_out, counters, h, NS, grp, HD, tid, kFlashWarps * 32);
 }
 
 // ------------------------------------------------------------ prefill ----
@@ -427,44 +725,69 @@ __global__ void __launch_bounds__(128) prefill_attn_kernel(PrefillAttnArgs a) {
 
 }  // namespace
 
-static bool attn_tc_shape(int grp, int hd) { return hd % 64 == 0 && hd <= 256 && grp <= 4; }
+// head slots per plane of the tensor-core items (4 or 8), 0 for the FMA loops
+static int attn_tc_slots(int grp, int hd) {
+  if (hd % 64 || hd > 256 || grp > 8) return 0;
+  return grp <= 4 ? 4 : 8;
+}
 
 int decode_attention_smem(int grp, int hd, int max_seq, int ns) {
-  const int cap = attn_rows(max_seq, ns);
-  if (attn_tc_shape(grp, hd))
-    return 2 * cap * hd * 2 + 8 * (hd + 8) * 2 + 4 * cap * 4 + 8 * (cap + 8) * 2;
+  const int cap = attn_rows(max_seq, ns), W = attn_tc_slots(grp, hd);
+  if (W) return 2 * cap * hd * 2 + 2 * W * (hd + 8) * 2 + W * cap * 4 + 2 * W * (cap + 8) * 2;
   return 2 * cap * hd * 2 + (grp * hd + grp * cap) * (int)sizeof(float);
+}
+
+template <int HD>
+static ifx_status launch_flash(const DecodeAttnArgs &a, cudaStream_t st, bool pdl) {
+  // splits: about three CTAs per SM over the whole batch, at least two
+  // tiles per warp, and no more than the caller's partial buffers hold
+  DecodeAttnArgs f = a;
+  const int tiles = (a.max_seq + kFlashRows - 1) / kFlashRows;
+  const int want = std::max(1, 3 * kNumSMs / std::max(1, a.G * a.batch));
+  f.ns = std::max(1, std::min({a.ns, want, kMaxSplits, (tiles + 2 * kFlashWarps - 1) / (2 * kFlashWarps)}));
+  constexpr int smem = flash_smem_bytes<HD>();
+  static bool attr = false;
+  if (!attr) {
+    IFX_CUDA(cudaFuncSetAttribute(decode_attn_flash_kernel<HD>,
+                                  cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    attr = true;
+  }
+  IFX_CUDA(launch(decode_attn_flash_kernel<HD>, dim3(a.G, f.ns, a.batch), dim3(kFlashWarps * 32),
+                  (size_t)smem, st, pdl, f));
+  return IFX_OK;
 }
 
 ifx_status decode_attention(const DecodeAttnArgs &a, cudaStream_t st, bool pdl) {
   const int grp = a.H / a.G;
-  if (grp > kMaxGroup || a.hd > 256 || a.hd % 8 || a.ns > kMaxSplits)
+  if (a.G < 1 || a.H % a.G || grp > kMaxGroup || a.ns < 1)
     return fail(IFX_ERR_UNSUPPORTED, "attention shape");
+  // the streamed kernel for the tensor-core head sizes (any number of
+  // pages: its splits are its own, at most the caller's)
+  if (a.hd == 128) return launch_flash<128>(a, st, pdl);
+  if (a.hd == 64) return launch_flash<64>(a, st, pdl);
+  if (a.hd > 256 || a.hd % 8 || a.ns > kMaxSplits) return fail(IFX_ERR_UNSUPPORTED, "attention shape");
   const size_t smem = (size_t)decode_attention_smem(grp, a.hd, a.max_seq, a.ns);
   if (smem > 200 * 1024) return fail(IFX_ERR_UNSUPPORTED, "attention: KV chunk too large for shared memory");
-  const bool tc = attn_tc_shape(grp, a.hd);
-  static size_t attr[2] = {0, 0};
-  if (smem > attr[tc]) {  // the static arrays count against the 48 KB default too
-    IFX_CUDA(cudaFuncSetAttribute(tc ? decode_attn_kernel<true> : decode_attn_kernel<false>,
-                                  cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-    attr[tc] = smem;
+  const int W = attn_tc_slots(grp, a.hd), k = W / 4;
+  void (*const kern[3])(DecodeAttnArgs) = {decode_attn_kernel<0>, decode_attn_kernel<4>,
+                                           decode_attn_kernel<8>};
+  static size_t attr[3] = {0, 0, 0};
+  if (smem > attr[k]) {  // the static arrays count against the 48 KB default too
+    IFX_CUDA(cudaFuncSetAttribute(kern[k], cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    attr[k] = smem;
   }
-  if (tc)
-    IFX_CUDA(launch(decode_attn_kernel<true>, dim3(a.G, a.ns, a.batch), dim3(kAttnThreads), smem,
-                    st, pdl, a));
-  else
-    IFX_CUDA(launch(decode_attn_kernel<false>, dim3(a.G, a.ns, a.batch), dim3(kAttnThreads), smem,
-                    st, pdl, a));
+  IFX_CUDA(launch(kern[k], dim3(a.G, a.ns, a.batch), dim3(kAttnThreads), smem, st, pdl, a));
   return IFX_OK;
 }
 
 // Prefill attention on tensor cores (flash-attention style): a CTA takes one
 // query head and 64 query rows (4 warps x 16), streams 64-key blocks of K
 // and V (f32 from the prefill workspace, converted to f16 into shared
-// memory; V transposed), computes S = Q K^T with mma.m16n8k16 (f16 in, f32
-// accumulate), applies the causal chunk mask (key <= query row, keys of this
-// chunk only: forward.rs:266-274), keeps an online softmax per row in
-// registers and accumulates O += P V with P re-used from the S fragments.
+// memory, both row-major with padded rows), computes S = Q K^T with
+// mma.m16n8k16 (f16 in, f32 accumulate), applies the causal chunk mask (key
+// <= query row, keys of this chunk only: forward.rs:266-274), keeps an online
+// softmax per row in registers and accumulates O += P V with P re-used from
+// the S fragments and V's B fragments taken with ldmatrix.trans.
 constexpr int kTQ = 64;  // query rows per CTA
 constexpr int kTK = 64;  // keys per block
 
@@ -475,11 +798,11 @@ __device__ __forceinline__ uint32_t pack_h2(float x, float y) {
 
 template <int HD>
 __global__ void __launch_bounds__(128) prefill_attn_tc_kernel(PrefillAttnArgs a) {
-  constexpr int KS = HD + 8;   // K row stride (halves): the 8 rows a fragment load touches
-  constexpr int VS = kTK + 8;  // Vt row stride             fall on distinct banks
+  constexpr int KS = HD + 8;   // K / V row stride (halves): the 8 rows a fragment load
+                               // touches fall on distinct banks
   extern __shared__ __align__(16) __half smh[];
   __half *Ks = smh;             // [kTK][KS]
-  __half *Vt = smh + kTK * KS;  // [HD][VS]
+  __half *Vs = smh + kTK * KS;  // [kTK][KS]
   const int hq = blockIdx.x, qb = blockIdx.y, tid = threadIdx.x;
   const int warp = tid >> 5, lane = tid & 31, g = lane >> 2, c = lane & 3;
   const int grp = a.H / a.G, hk = hq / grp;
@@ -523,10 +846,7 @@ __global__ void __launch_bounds__(128) prefill_attn_tc_kernel(PrefillAttnArgs a)
         vv = *reinterpret_cast<const float4 *>(a.v + (size_t)(kb + t) * kstride + hk * HD + d);
       }
       *reinterpret_cast<uint2 *>(Ks + t * KS + d) = make_uint2(pack_h2(kv.x, kv.y), pack_h2(kv.z, kv.w));
-      Vt[(d + 0) * VS + t] = __float2half_rn(vv.x);
-      Vt[(d + 1) * VS + t] = __float2half_rn(vv.y);
-      Vt[(d + 2) * VS + t] = __float2half_rn(vv.z);
-      Vt[(d + 3) * VS + t] = __float2half_rn(vv.w);
+      *reinterpret_cast<uint2 *>(Vs + t * KS + d) = make_uint2(pack_h2(vv.x, vv.y), pack_h2(vv.z, vv.w));
     }
     __syncthreads();
     float sv[kTK / 8][4];
@@ -588,12 +908,15 @@ __global__ void __launch_bounds__(128) prefill_attn_tc_kernel(PrefillAttnArgs a)
       const uint32_t p1 = pack_h2(sv[2 * k2][2], sv[2 * k2][3]);
       const uint32_t p2 = pack_h2(sv[2 * k2 + 1][0], sv[2 * k2 + 1][1]);
       const uint32_t p3 = pack_h2(sv[2 * k2 + 1][2], sv[2 * k2 + 1][3]);
+      // B = V[keys 16 k2 .. + 15][dims]: ldmatrix.trans of (keys 0-7 | 8-15) x
+      // (dims of n-tiles nt | nt + 1) gives b0, b1 of both n-tiles
+      const int vkey = k2 * 16 + (lane & 7) + 8 * ((lane >> 3) & 1);
 #pragma unroll
-      for (int nt = 0; nt < HD / 8; ++nt) {
-        const __half *vr = Vt + (nt * 8 + g) * VS + k2 * 16 + 2 * c;
-        const uint32_t b0 = *reinterpret_cast<const uint32_t *>(vr);
-        const uint32_t b1 = *reinterpret_cast<const uint32_t *>(vr + 8);
-        mma_16816(o[nt], p0, p1, p2, p3, b0, b1, o[nt]);
+      for (int nt = 0; nt < HD / 8; nt += 2) {
+        uint32_t b[4];
+        ldsm_x4_t(b, smem_u32(Vs + vkey * KS + (nt + (lane >> 4)) * 8));
+        mma_16816(o[nt], p0, p1, p2, p3, b[0], b[1], o[nt]);
+        mma_16816(o[nt + 1], p0, p1, p2, p3, b[2], b[3], o[nt + 1]);
       }
     }
   }
@@ -616,7 +939,7 @@ __global__ void __launch_bounds__(128) prefill_attn_tc_kernel(PrefillAttnArgs a)
 
 template <int HD>
 static ifx_status launch_prefill_tc(const PrefillAttnArgs &a, cudaStream_t st) {
-  const size_t smem = (size_t)(kTK * (HD + 8) + HD * (kTK + 8)) * sizeof(__half);
+  const size_t smem = (size_t)(2 * kTK * (HD + 8)) * sizeof(__half);
   dim3 grid(a.H, (a.n + kTQ - 1) / kTQ);
   prefill_attn_tc_kernel<HD><<<grid, 128, smem, st>>>(a);
   IFX_CUDA(cudaGetLastError());

@@ -1,5 +1,5 @@
 // Shared helpers for the sm_100a kernels: status plumbing, PTX wrappers for
-// mbarriers, bulk async copies (TMA, 1-D, no multicast), programmatic
+// mbarriers, bulk async copies (TMA, 1-D, one destination CTA), programmatic
 // dependent launch, and the m16n8k16 f16 tensor-core MMA.
 #pragma once
 #include <cuda_fp16.h>

@@ -37,6 +37,43 @@ __device__ __forceinline__ unsigned ld_acquire(const unsigned *p) {
   return v;
 }
 
+// Generic addressing: the peer buffers are CUDA IPC mappings.
+__device__ __forceinline__ unsigned ld_acquire_sys(const unsigned *p) {
+  unsigned v;
+  asm volatile("ld.acquire.sys.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+__device__ __forceinline__ void st_release_sys(unsigned *p, unsigned v) {
+  asm volatile("st.release.sys.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+__device__ __forceinline__ uint64_t global_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+// Bounded wait (one thread) until the epoch at `flag`, written by another
+// rank, reaches e; false (error flag set to `code`) after limit_ns of wall
+// time (another rank may legitimately start its step later than this one)
+// or as soon as another thread has raised the error flag.
+__device__ bool wait_epoch(const unsigned *flag, unsigned e, int *err, int code, uint64_t limit_ns) {
+  const uint64_t t0 = global_ns();
+  uint32_t spins = 0;
+  while ((int)(ld_acquire_sys(flag) - e) < 0) {
+    if ((++spins & 63u) == 0) {
+      if (*(volatile int *)err) return false;
+      if (global_ns() - t0 > limit_ns) {
+        atomicExch(err, code);
+        return false;
+      }
+      if (spins > 4096u) __nanosleep(256);
+    }
+  }
+  return true;
+}
+
 // Grid barrier over all CTAs (consumer warps only). Bounded: polling stops
 // after 2^24 polls (well over a second) or as soon as any thread has raised
 // the error flag.
@@ -271,15 +308,20 @@ __device__ __noinline__ void attn_item(const MegaArgs &A, const MegaAttn &at, in
   consumer_sync();  // the buffer is reused by the next item
 }
 
-// The same item on tensor cores (head size a multiple of 64, at most four
+// The same item on tensor cores (head size a multiple of 64, at most eight
 // query heads per kv head): S = K Q^T with the cached K rows as the A operand
 // (ldmatrix from the chunk-swizzled rows, conflict-free) and the query heads
-// as B columns — column j the hi f16 plane of head j, column 4 + j its lo
-// plane (about 22 bits), added across lanes afterwards; softmax statistics
-// over the item's rows; O = V^T P with V^T from ldmatrix.trans and P as hi/lo
-// columns the same way. Output format as attn_item.
+// as B columns carrying each head's hi and lo f16 planes (about 22 bits),
+// added afterwards; softmax statistics over the item's rows; O = V^T P with
+// V^T from ldmatrix.trans and P as hi/lo columns the same way. Up to four
+// heads share one 8-column tile (column j the hi plane of head j, column
+// 4 + j its lo plane, added across lanes); five to eight heads take two
+// tiles (hi planes, lo planes). Output format as attn_item.
+template <int W>
 __device__ __noinline__ void attn_item_tc(const MegaArgs &A, const MegaAttn &at, int h, int s,
                                           int pos, uint8_t *abuf) {
+  static_assert(W == 4 || W == 8, "head slots per plane");
+  constexpr int NT = W / 4;  // 8-column B tiles per MMA step
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, c = lane & 3;
   const int hd = A.hd, grp = A.H / A.G, NS = A.nsa;
   const AttnSpan sp = attn_span(pos, NS, s);
@@ -288,14 +330,14 @@ __device__ __noinline__ void attn_item_tc(const MegaArgs &A, const MegaAttn &at,
   const int qs = hd + 8, ps = cap + 8;  // padded row strides (conflict-free B loads)
   __half *Ks = reinterpret_cast<__half *>(abuf);  // [cap][hd], rows chunk-swizzled
   __half *Vs = Ks + (size_t)cap * hd;               // [cap][hd]
-  __half *qh = Vs + (size_t)cap * hd;               // [2][4][qs]
-  float *sc = reinterpret_cast<float *>(qh + 2 * 4 * qs);  // [4][cap]
-  __half *ph = reinterpret_cast<__half *>(sc + 4 * cap);   // [2][4][ps]
-  float *stat = reinterpret_cast<float *>(ph + 2 * 4 * ps);  // [4][2]
+  __half *qh = Vs + (size_t)cap * hd;               // [2][W][qs]: plane, head
+  float *sc = reinterpret_cast<float *>(qh + 2 * W * qs);  // [W][cap]
+  __half *ph = reinterpret_cast<__half *>(sc + W * cap);   // [2][W][ps]
+  float *stat = reinterpret_cast<float *>(ph + 2 * W * ps);  // [W][2]
   // RoPE at position 0 is the identity (the reference's decode, forward.rs:371-372)
   const int rpos = A.rope_compat ? 0 : pos;
   const float *q = A.qkv + (size_t)h * grp * hd;
-  for (int e = tid; e < 4 * hd / 2; e += kConsumerThreads) {
+  for (int e = tid; e < W * hd / 2; e += kConsumerThreads) {
     const int j = e / (hd / 2), i = 2 * (e % (hd / 2));
     float x0 = 0.f, x1 = 0.f;
     if (j < grp) {
@@ -305,7 +347,7 @@ __device__ __noinline__ void attn_item_tc(const MegaArgs &A, const MegaAttn &at,
     }
     const __half2 hi = __floats2half2_rn(x0, x1);
     *reinterpret_cast<__half2 *>(qh + j * qs + i) = hi;
-    *reinterpret_cast<__half2 *>(qh + (4 + j) * qs + i) =
+    *reinterpret_cast<__half2 *>(qh + (W + j) * qs + i) =
         __floats2half2_rn(x0 - __low2float(hi), x1 - __high2float(hi));
   }
   if (t0 <= pos && pos < sp.t1) {  // append this token's K/V (forward.rs:375-378)
@@ -333,33 +375,38 @@ __device__ __noinline__ void attn_item_tc(const MegaArgs &A, const MegaAttn &at,
   // scores: warp w takes 16-row tile w
   const float isq = 1.0f / sqrtf((float)hd);
   for (int mt = warp; mt < nk16 / 16; mt += kConsumerWarps) {
-    float D[4] = {0.f, 0.f, 0.f, 0.f};
+    float D[NT][4] = {};
     const int row = 16 * mt + (lane & 7) + 8 * ((lane >> 3) & 1);
     const int key = kv_col(t0 + row, 0, hd) >> 3;
-    const __half *qp = qh + g * qs + 2 * c;  // column g: plane g / 4, head g % 4
     for (int ks = 0; ks < hd / 16; ++ks) {
       uint32_t a[4];
       ldsm_x4(a, smem_u32(Ks + (size_t)row * hd + (((2 * ks + (lane >> 4)) ^ key) << 3)));
-      const uint32_t b0 = *reinterpret_cast<const uint32_t *>(qp + 16 * ks);
-      const uint32_t b1 = *reinterpret_cast<const uint32_t *>(qp + 16 * ks + 8);
-      mma_16816(D, a[0], a[1], a[2], a[3], b0, b1, D);
-    }
 #pragma unroll
-    for (int i = 0; i < 4; ++i) D[i] += __shfl_xor_sync(0xffffffffu, D[i], 2);  // hi + lo
-    if (c < 2) {
+      for (int t = 0; t < NT; ++t) {
+        // tile t, column g: row 8 t + g of qh (W = 4: plane g / 4, head g % 4)
+        const __half *qp = qh + (8 * t + g) * qs + 2 * c + 16 * ks;
+        mma_16816(D[t], a[0], a[1], a[2], a[3], *reinterpret_cast<const uint32_t *>(qp),
+                  *reinterpret_cast<const uint32_t *>(qp + 8), D[t]);
+      }
+    }
+    float S[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i)  // hi + lo
+      S[i] = NT == 2 ? D[0][i] + D[NT - 1][i] : D[0][i] + __shfl_xor_sync(0xffffffffu, D[0][i], 2);
+    if (NT == 2 || c < 2) {
       const int ra = 16 * mt + g, rb = ra + 8;
 #pragma unroll
       for (int jj = 0; jj < 2; ++jj) {
         const int j = 2 * c + jj;
         if (j < grp) {
-          sc[j * cap + ra] = ra < nk ? D[jj] * isq : -INFINITY;
-          sc[j * cap + rb] = rb < nk ? D[2 + jj] * isq : -INFINITY;
+          sc[j * cap + ra] = ra < nk ? S[jj] * isq : -INFINITY;
+          sc[j * cap + rb] = rb < nk ? S[2 + jj] * isq : -INFINITY;
         }
       }
     }
   }
   consumer_sync();
-  if (warp < 4) {  // softmax statistics of this split, head j = warp; p as hi/lo planes
+  if (warp < W) {  // softmax statistics of this split, head j = warp; p as hi/lo planes
     const int j = warp;
     float m = -INFINITY;
     if (j < grp)
@@ -370,7 +417,7 @@ __device__ __noinline__ void attn_item_tc(const MegaArgs &A, const MegaAttn &at,
       const float p = (j < grp && t < nk) ? expf(sc[j * cap + t] - m) : 0.f;
       const __half hp = __float2half_rn(p);
       ph[j * ps + t] = hp;
-      ph[(4 + j) * ps + t] = __float2half_rn(p - __half2float(hp));
+      ph[(W + j) * ps + t] = __float2half_rn(p - __half2float(hp));
       l += p;
     }
     l = warp_sum(l);
@@ -383,26 +430,30 @@ __device__ __noinline__ void attn_item_tc(const MegaArgs &A, const MegaAttn &at,
   // O^T = V^T P: warp w takes dims [16 w, 16 w + 16)
   float *po = A.part_o + (size_t)(h * NS + s) * grp * hd;
   for (int mt = warp; mt < hd / 16; mt += kConsumerWarps) {
-    float D[4] = {0.f, 0.f, 0.f, 0.f};
-    const __half *pp = ph + g * ps + 2 * c;
+    float D[NT][4] = {};
     for (int ks = 0; ks < nk16 / 16; ++ks) {
       const int t = 16 * ks + (lane & 7) + 8 * (lane >> 4);
       const int chunk = (2 * mt + ((lane >> 3) & 1)) ^ (kv_col(t0 + t, 0, hd) >> 3);
       uint32_t a[4];
       ldsm_x4_t(a, smem_u32(Vs + (size_t)t * hd + (chunk << 3)));
-      const uint32_t b0 = *reinterpret_cast<const uint32_t *>(pp + 16 * ks);
-      const uint32_t b1 = *reinterpret_cast<const uint32_t *>(pp + 16 * ks + 8);
-      mma_16816(D, a[0], a[1], a[2], a[3], b0, b1, D);
-    }
 #pragma unroll
-    for (int i = 0; i < 4; ++i) D[i] += __shfl_xor_sync(0xffffffffu, D[i], 2);
-    if (c < 2) {
+      for (int tt = 0; tt < NT; ++tt) {
+        const __half *pp = ph + (8 * tt + g) * ps + 2 * c + 16 * ks;
+        mma_16816(D[tt], a[0], a[1], a[2], a[3], *reinterpret_cast<const uint32_t *>(pp),
+                  *reinterpret_cast<const uint32_t *>(pp + 8), D[tt]);
+      }
+    }
+    float O[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+      O[i] = NT == 2 ? D[0][i] + D[NT - 1][i] : D[0][i] + __shfl_xor_sync(0xffffffffu, D[0][i], 2);
+    if (NT == 2 || c < 2) {
 #pragma unroll
       for (int jj = 0; jj < 2; ++jj) {
         const int j = 2 * c + jj;
         if (j < grp) {
-          po[j * hd + 16 * mt + g] = D[jj];
-          po[j * hd + 16 * mt + g + 8] = D[2 + jj];
+          po[j * hd + 16 * mt + g] = O[jj];
+          po[j * hd + 16 * mt + g + 8] = O[2 + jj];
         }
       }
     }
@@ -539,13 +590,86 @@ __device__ __noinline__ void combine_kv_head(const MegaArgs &A, int h, float *wb
   }
 }
 
+// All-reduce of one vector across the ranks, inside the step. CTA b owns
+// slice b (float4 granularity): it pushes its slice of ar_src to every rank's
+// receive row for this rank (peer stores over NVLink), zeroes it, raises its
+// flag on every rank, waits until every rank's CTA b has raised its flag
+// here, then adds the ranks' slices in rank order into ar_dst. Every rank
+// adds the same values in the same order, so ar_dst stays identical on all
+// ranks. Receive rows alternate between two parities: a rank pushes epoch
+// e + 1 only after every rank's CTA b pushed epoch e, which each did after
+// reading its epoch e - 1 slices.
+__device__ __noinline__ void phase_allreduce(const MegaArgs &A, const MegaPhase &P, unsigned ar0) {
+  const int tid = threadIdx.x, b = blockIdx.x, N = A.nranks, me = A.rank;
+  const MegaPeers &pr = A.peers;
+  const unsigned e = ar0 + (unsigned)P.ar_index;
+  const size_t row4 = (size_t)pr.row_floats / 4;
+  const int n4 = P.ar_n / 4, per = (n4 + (int)gridDim.x - 1) / (int)gridDim.x;
+  const int lo = min(n4, b * per), hi = min(n4, lo + per);
+  const size_t par_off = (size_t)(e & 1u) * kMaxRanks * row4;
+  float4 *src = reinterpret_cast<float4 *>(P.ar_src);
+  for (int i = lo + tid; i < hi; i += kConsumerThreads) {
+    const float4 v = __ldcg(src + i);
+    src[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int r = 0; r < N; ++r)
+      __stcg(reinterpret_cast<float4 *>(pr.buf[r]) + par_off + (size_t)me * row4 + i, v);
+  }
+  __threadfence_system();
+  consumer_sync();
+  if (tid < N)
+    st_release_sys(reinterpret_cast<unsigned *>(pr.buf[tid] + pr.off_flags) + (size_t)b * kMaxRanks + me, e);
+  if (tid < N)
+    wait_epoch(reinterpret_cast<const unsigned *>(pr.buf[me] + pr.off_flags) + (size_t)b * kMaxRanks + tid,
+               e, A.err, 410, pr.wait_ns);
+  consumer_sync();
+  const float4 *rv = reinterpret_cast<const float4 *>(pr.buf[me]) + par_off;
+  float4 *dst = reinterpret_cast<float4 *>(P.ar_dst);
+  for (int i = lo + tid; i < hi; i += kConsumerThreads) {
+    float4 t = __ldcg(rv + i);
+    for (int r = 1; r < N; ++r) {
+      const float4 u = __ldcg(rv + (size_t)r * row4 + i);
+      t.x += u.x;
+      t.y += u.y;
+      t.z += u.z;
+      t.w += u.w;
+    }
+    float4 x = dst[i];
+    x.x += t.x;
+    x.y += t.y;
+    x.z += t.z;
+    x.w += t.w;
+    dst[i] = x;
+  }
+}
+
+// The maximum argmax key over the ranks (one thread of one CTA per rank):
+// each rank's key goes to every rank, then each takes the maximum.
+__device__ unsigned long long keys_max(const MegaArgs &A, unsigned long long k, unsigned e) {
+  const MegaPeers &pr = A.peers;
+  const int N = A.nranks, me = A.rank;
+  const size_t slot = (size_t)(e & 1u) * kMaxRanks;
+  for (int r = 0; r < N; ++r)
+    reinterpret_cast<volatile unsigned long long *>(pr.buf[r] + pr.off_keys)[slot + me] = k;
+  __threadfence_system();
+  for (int r = 0; r < N; ++r) st_release_sys(reinterpret_cast<unsigned *>(pr.buf[r] + pr.off_kflags) + me, e);
+  for (int r = 0; r < N; ++r)
+    if (!wait_epoch(reinterpret_cast<const unsigned *>(pr.buf[me] + pr.off_kflags) + r, e, A.err, 411,
+                    pr.wait_ns))
+      return k;
+  const volatile unsigned long long *keys =
+      reinterpret_cast<const volatile unsigned long long *>(pr.buf[me] + pr.off_keys) + slot;
+  for (int r = 0; r < N; ++r) k = keys[r] > k ? keys[r] : k;
+  return k;
+}
+
 __device__ __noinline__ void phase_argmax(const MegaArgs &A, float *scr) {
   const int tid = threadIdx.x;
   unsigned long long best = 0;
   for (int i = blockIdx.x * kConsumerThreads + tid; i < A.V; i += gridDim.x * kConsumerThreads) {
     const float v = __ldcg(&A.logits[i]);
     if (v != v) continue;
-    const unsigned long long k = ((unsigned long long)ordered_bits(v) << 32) | (unsigned)i;
+    // the global index (this rank's vocab slice starts at v0)
+    const unsigned long long k = ((unsigned long long)ordered_bits(v) << 32) | (unsigned)(i + A.v0);
     best = k > best ? k : best;
   }
 #pragma unroll
@@ -561,7 +685,13 @@ __device__ __noinline__ void phase_argmax(const MegaArgs &A, float *scr) {
     last = (atomicAdd(A.amax_count, 1) == (int)gridDim.x - 1);
     if (last) {
       __threadfence();
-      const unsigned long long k = atomicAdd(A.amax_key, 0ull);
+      unsigned long long k = atomicAdd(A.amax_key, 0ull);
+      if (A.nranks > 1) {
+        // every CTA read the epochs when the step began, grid barriers ago
+        k = keys_max(A, k, A.peers.epoch[1] + 1u);
+        A.peers.epoch[0] += (unsigned)A.n_ar;
+        A.peers.epoch[1] += 1u;
+      }
       const uint32_t tok = (uint32_t)(k & 0xffffffffull);
       *A.next_token = tok;
       A.tokens[*A.n_out] = tok;
@@ -638,6 +768,8 @@ __global__ void __launch_bounds__(kGemvThreads, 1) decode_mega_kernel(const __gr
   int issued = 1, landed = 0;    // phase-record copies (thread 0's view)
   int kv_issued = 0, kv_done = 0;  // K/V row fetches (thread 0's view)
   const int pos = *A.pos;        // this step's position (advanced after the last phase)
+  // all-reduces done before this step (advanced by the argmax phase's last CTA)
+  const unsigned ar0 = A.nranks > 1 ? *(volatile unsigned *)A.peers.epoch : 0u;
   __shared__ int s_kv_ok, s_last;
   for (int p = 0; p < A.nph; ++p) {
     // the record of phase p was requested during phase p - 1 into the buffer
@@ -695,8 +827,10 @@ __global__ void __launch_bounds__(kGemvThreads, 1) decode_mega_kernel(const __gr
           }
           consumer_sync();
           const int h = item % A.G;
-          if (A.attn_tc)
-            attn_item_tc(A, P.at, h, item / A.G, pos, abuf);
+          if (A.attn_tc == 8)
+            attn_item_tc<8>(A, P.at, h, item / A.G, pos, abuf);
+          else if (A.attn_tc)
+            attn_item_tc<4>(A, P.at, h, item / A.G, pos, abuf);
           else
             attn_item(A, P.at, h, item / A.G, pos, abuf);
           // split-K fixup: the CTA that finishes kv head h's last split
@@ -718,6 +852,9 @@ __global__ void __launch_bounds__(kGemvThreads, 1) decode_mega_kernel(const __gr
       }
       case PH_ARGMAX:
         phase_argmax(A, reinterpret_cast<float *>(scr));
+        break;
+      case PH_ALLREDUCE:
+        phase_allreduce(A, P, ar0);
         break;
       default:
         break;
@@ -741,10 +878,21 @@ int mega_attn_splits(int G, int max_seq, int num_sms) {
 size_t mega_attn_scratch(int grp, int hd, int max_seq, int nsa) {
   const size_t cap = (size_t)attn_cap(max_seq, nsa);
   const size_t scalar = 2 * cap * hd * 2 + (size_t)grp * hd * 4 + (size_t)grp * cap * 4 + (size_t)grp * 8 + 64;
-  // tensor-core items: K, V | q hi/lo [2][4][hd + 8] | scores [4][cap] | p hi/lo [2][4][cap + 8] | stats
-  const size_t tc = 2 * cap * hd * 2 + 2 * 4 * ((size_t)hd + 8) * 2 + 4 * cap * 4 +
-                    2 * 4 * (cap + 8) * 2 + 4 * 8 + 64;
+  // tensor-core items: K, V | q hi/lo [2][W][hd + 8] | scores [W][cap] | p hi/lo [2][W][cap + 8]
+  // | stats, W = 4 or 8 head slots per plane
+  const size_t W = grp <= 4 ? 4 : 8;
+  const size_t tc = 2 * cap * hd * 2 + 2 * W * ((size_t)hd + 8) * 2 + W * cap * 4 +
+                    2 * W * (cap + 8) * 2 + W * 8 + 64;
   return std::max(scalar, tc);
+}
+
+size_t mega_peer_bytes(int n, int grid, MegaPeers *layout) {
+  const size_t row = ((size_t)n + 63) / 64 * 64;  // floats, 256-byte rows
+  layout->row_floats = (int)row;
+  layout->off_flags = 2 * kMaxRanks * row * sizeof(float);
+  layout->off_keys = layout->off_flags + ((size_t)grid * kMaxRanks * sizeof(unsigned) + 255) / 256 * 256;
+  layout->off_kflags = layout->off_keys + 2 * kMaxRanks * sizeof(unsigned long long);
+  return layout->off_kflags + 256;
 }
 
 ifx_status mega_finalize(MegaPlan *plan, const std::vector<MegaPhase> &phases, int num_sms) {

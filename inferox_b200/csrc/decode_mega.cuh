@@ -5,7 +5,9 @@
 
 namespace ifx {
 
-enum MegaKind { PH_EMBED = 0, PH_GEMV = 1, PH_ATTN = 2, PH_ARGMAX = 4 };
+enum MegaKind { PH_EMBED = 0, PH_GEMV = 1, PH_ATTN = 2, PH_ARGMAX = 4, PH_ALLREDUCE = 5 };
+
+constexpr int kMaxRanks = 8;
 
 struct MegaAttn {
   __half *kc, *vc;  // this layer's caches [G][max_seq][hd]
@@ -22,6 +24,27 @@ struct __align__(16) MegaPhase {
   int zero_n;
   int attn_prefetch;  // layer + 1 on the QKV GEMV: during it, fetch this CTA's first
                       // attention item's cached K/V rows of that layer (0: none)
+  // PH_ALLREDUCE (tensor parallelism): ar_dst[i] += sum over ranks of their
+  // ar_src[i] (i < ar_n); ar_src is left zeroed. ar_index counts the
+  // all-reduces of the step from 1.
+  float *ar_src, *ar_dst;
+  int ar_n, ar_index;
+};
+
+// Tensor parallelism inside the persistent kernel: every rank owns one
+// buffer that all ranks map (CUDA IPC), laid out as
+//   recv  [2][kMaxRanks][row_floats] f32  slices pushed by each rank, two parities
+//   flags [grid][kMaxRanks] u32          epoch of the last push of CTA b by rank r
+//   keys  [2][kMaxRanks] u64            each rank's argmax key, two parities
+//   kflags [kMaxRanks] u32               epoch of rank r's last key
+// Epochs only grow (counters in `epoch`, advanced by the kernel itself), so
+// nothing is ever reset between steps.
+struct MegaPeers {
+  char *buf[kMaxRanks];  // rank r's buffer as mapped in this process (buf[rank]: own)
+  size_t off_flags, off_keys, off_kflags;
+  int row_floats;
+  unsigned *epoch;  // [0] all-reduces so far, [1] steps so far (this rank's device memory)
+  uint64_t wait_ns;  // a wait for another rank gives up (error flag) after this long
 };
 
 struct MegaArgs {
@@ -43,7 +66,7 @@ struct MegaArgs {
   float *part_o;
   float2 *part_ml;
   int H, G, hd, max_seq, nsa, rope_compat, rope_dim;
-  int attn_tc;  // 1: attention items on tensor cores (head size a multiple of 64, <= 4 q heads per kv head)
+  int attn_tc;  // 4 / 8: attention items on tensor cores with that many head slots (head size a multiple of 64); 0: FMA loops
   float rope_base;
   const float *qkv;
   const __half *kc0, *vc0;  // layer 0 of the K and V caches
@@ -53,6 +76,10 @@ struct MegaArgs {
   int *amax_count;
   uint32_t *tokens;
   int *n_out;
+  // tensor parallelism (nranks 1: none)
+  int rank, nranks, v0;  // v0: global index of this rank's first logit
+  int n_ar;              // all-reduce phases per step
+  MegaPeers peers;
 };
 
 struct MegaPlan {
@@ -67,6 +94,8 @@ struct MegaPlan {
 int mega_attn_splits(int G, int max_seq, int num_sms);
 // Shared-memory bytes the attention phase needs.
 size_t mega_attn_scratch(int grp, int hd, int max_seq, int nsa);
+// Bytes of one rank's peer buffer for vectors of up to n floats.
+size_t mega_peer_bytes(int n, int grid, MegaPeers *layout);
 ifx_status mega_finalize(MegaPlan *plan, const std::vector<MegaPhase> &phases, int num_sms);
 ifx_status mega_launch(const MegaPlan &plan, cudaStream_t st);
 void mega_free(MegaPlan *plan);

@@ -412,6 +412,7 @@ ifx_status Model::load(const uint8_t *bytes, size_t len, const ifx_load_opts &o)
     IFX_TRY(dalloc(&y, D));
     IFX_TRY(dalloc(&logits_local, Vl));
     IFX_TRY(dalloc(&key_global, 1));
+    if (opts.persistent_decode) IFX_TRY(setup_peers());
   } else {
     logits_local = logits;
   }
@@ -508,6 +509,10 @@ Model::~Model() {
                                      y, key_global, logits_all_local})
     F(v);
   if (logits_local != logits) F(logits_local);
+  for (int r = 0; r < kMaxRanks; ++r)
+    if (r != rank && peers.buf[r]) cudaIpcCloseMemHandle(peers.buf[r]);
+  F(peer_buf);
+  F(mega_epoch);
   for (size_t l = 0; l < p_qkv.size(); ++l) {
     gemv_plan_free(&p_qkv[l]);
     for (auto &p : p_qkv_more[l]) gemv_plan_free(&p);
@@ -747,19 +752,67 @@ ifx_status Model::tp_partial_end(size_t n, cudaStream_t st, const float *part, f
   return IFX_OK;
 }
 
+// The persistent kernel's all-reduce buffers under tensor parallelism: each
+// rank allocates one, zeroes it, and maps every other rank's through CUDA
+// IPC (handles exchanged with an NCCL all-gather, which also orders every
+// rank's zeroing before any rank's first push). The persistent path is used
+// only when every rank mapped every buffer (an all-reduce of the outcome),
+// so all ranks take the same path; otherwise the per-op kernels run with
+// NCCL between them.
+ifx_status Model::setup_peers() {
+  const size_t bytes = mega_peer_bytes((int)cfg.hidden_size, kNumSMs, &peers);
+  IFX_CUDA(cudaMalloc(&peer_buf, bytes));
+  IFX_CUDA(cudaMemsetAsync(peer_buf, 0, bytes, stream));
+  IFX_TRY(dalloc(&mega_epoch, 2));
+  cudaIpcMemHandle_t h{};
+  int ok = cudaIpcGetMemHandle(&h, peer_buf) == cudaSuccess ? 1 : 0;
+  cudaGetLastError();
+  constexpr size_t hb = sizeof(cudaIpcMemHandle_t);
+  char *dh = nullptr;
+  IFX_CUDA(cudaMalloc(&dh, hb * (size_t)tp + sizeof(int)));
+  int *dok = reinterpret_cast<int *>(dh + hb * (size_t)tp);
+  IFX_CUDA(cudaMemcpyAsync(dh + hb * (size_t)rank, &h, hb, cudaMemcpyHostToDevice, stream));
+  IFX_NCCL(nccl, nccl->AllGather(dh + hb * (size_t)rank, dh, hb, ncclUint8, (ncclComm_t)comm, stream));
+  std::vector<cudaIpcMemHandle_t> all((size_t)tp);
+  IFX_CUDA(cudaMemcpyAsync(all.data(), dh, hb * (size_t)tp, cudaMemcpyDeviceToHost, stream));
+  IFX_CUDA(cudaStreamSynchronize(stream));
+  for (int r = 0; r < kMaxRanks; ++r) peers.buf[r] = nullptr;
+  peers.buf[rank] = peer_buf;
+  for (int r = 0; r < tp && ok; ++r) {
+    if (r == rank) continue;
+    void *p = nullptr;
+    if (cudaIpcOpenMemHandle(&p, all[(size_t)r], cudaIpcMemLazyEnablePeerAccess) == cudaSuccess)
+      peers.buf[r] = static_cast<char *>(p);
+    else
+      ok = 0;
+    cudaGetLastError();
+  }
+  IFX_CUDA(cudaMemcpyAsync(dok, &ok, sizeof(int), cudaMemcpyHostToDevice, stream));
+  IFX_NCCL(nccl, nccl->AllReduce(dok, dok, 1, ncclInt32, ncclMin, (ncclComm_t)comm, stream));
+  IFX_CUDA(cudaMemcpyAsync(&ok, dok, sizeof(int), cudaMemcpyDeviceToHost, stream));
+  IFX_CUDA(cudaStreamSynchronize(stream));
+  cudaFree(dh);
+  peers.epoch = mega_epoch;
+  // the host-side bound of the collectives, 20 s unless set
+  peers.wait_ns = (uint64_t)(opts.tp_timeout_ms > 0 ? opts.tp_timeout_ms : 20000) * 1000000ull;
+  peers_ok = ok != 0;
+  return IFX_OK;
+}
+
 // The persistent decode plan of a cache: the token step as a phase list.
 ifx_status Model::build_mega(KvCache &kv) {
   kv.mega_tried = true;
   const ifx_config &c = cfg;
-  const int H = (int)c.n_heads, G = (int)c.n_kv_heads, hd = (int)c.head_dim;
-  if (tp > 1) return IFX_OK;  // the all-reduces run between the per-op kernels
+  // this rank's heads (all of them at tp 1)
+  const int H = (int)Hl, G = (int)Gl, hd = (int)c.head_dim;
+  if (tp > 1 && !peers_ok) return IFX_OK;  // the all-reduces run between the per-op kernels
   if (hd % 8 || hd > 256 || H % G || H / G > 8) return IFX_OK;  // separate kernels instead
   int dev_sms = 0;
   IFX_CUDA(cudaDeviceGetAttribute(&dev_sms, cudaDevAttrMultiProcessorCount, device));
   if (dev_sms != kNumSMs) return IFX_OK;
   MegaArgs &A = kv.mega.args;
   A.nsa = mega_attn_splits(G, (int)kv.max_seq, kNumSMs);
-  A.attn_tc = (hd % 64 == 0 && hd <= 256 && H / G <= 4) ? 1 : 0;
+  A.attn_tc = (hd % 64 == 0 && hd <= 256 && H / G <= 8) ? (H / G <= 4 ? 4 : 8) : 0;
   IFX_TRY(dalloc(&kv.part_o, (size_t)H * A.nsa * hd));
   IFX_TRY(dalloc(&kv.part_ml, (size_t)H * A.nsa));
   IFX_TRY(dalloc(&kv.bar, 1 + (size_t)G));  // barrier counter + per-kv-head split counters
@@ -768,11 +821,16 @@ ifx_status Model::build_mega(KvCache &kv) {
   A.emb = emb_raw;
   A.emb_type = emb_type;
   A.D = (int)c.hidden_size;
-  A.V = (int)c.vocab_size;
+  A.V = (int)Vl;  // this rank's vocab slice
+  A.v0 = (int)v0;
+  A.rank = rank;
+  A.nranks = tp;
+  A.peers = peers;
+  A.n_ar = tp > 1 ? 2 * (int)c.n_layers : 0;
   A.next_token = next_token;
   A.x = x;
   A.attn = attn;
-  A.logits = logits;
+  A.logits = logits_local;
   A.part_o = kv.part_o;
   A.part_ml = kv.part_ml;
   A.H = H;
@@ -808,9 +866,23 @@ ifx_status Model::build_mega(KvCache &kv) {
     m.zero_n = zn;
     ph.push_back(m);
   };
-  simple(PH_EMBED, logits, (int)c.vocab_size);
+  // tensor parallelism: Wo and W2 accumulate this rank's partial sums into
+  // y, and an all-reduce phase adds every rank's into x (and zeroes y)
+  int n_ar = 0;
+  auto allreduce = [&]() {
+    MegaPhase m{};
+    m.kind = PH_ALLREDUCE;
+    m.ar_src = y;
+    m.ar_dst = x;
+    m.ar_n = (int)c.hidden_size;
+    m.ar_index = ++n_ar;
+    ph.push_back(m);
+  };
+  if (tp > 1 && c.hidden_size % 4) return IFX_OK;  // the all-reduce moves float4s
+  simple(PH_EMBED, logits_local, (int)Vl);
   for (uint64_t l = 0; l < c.n_layers; ++l) {
-    gemv(p_qkv[l], nullptr, 0);
+    if (l == 0 && tp > 1) gemv(p_qkv[l], y, (int)c.hidden_size);  // the all-reduces re-zero it
+    else gemv(p_qkv[l], nullptr, 0);
     ph.back().attn_prefetch = (int)l + 1;  // this layer's K/V rows land during QKV
     for (const GemvPlan &p : p_qkv_more[l]) gemv(p, nullptr, 0);
     MegaPhase at{};
@@ -819,12 +891,14 @@ ifx_status Model::build_mega(KvCache &kv) {
     at.at.vc = kv.v + l * kv.per_layer;
     at.at.layer = (int)l;
     at.zero_ptr = gu;  // consumed by the previous layer's W2, refilled by W13
-    at.zero_n = (int)(2 * c.intermediate_size);
+    at.zero_n = (int)(2 * Fl);  // this rank's W1 / W3 rows
     ph.push_back(at);
     gemv(p_wo[l], nullptr, 0);  // the attention phase leaves the combined heads in attn
+    if (tp > 1) allreduce();
     gemv(p_w13[l], qkv, qkv_n);  // qkv was consumed by ATTN; the next QKV refills it
     for (const GemvPlan &p : p_w13_more[l]) gemv(p, nullptr, 0);
     gemv(p_w2[l], nullptr, 0);
+    if (tp > 1) allreduce();
   }
   gemv(p_logits, nullptr, 0);
   simple(PH_ARGMAX, nullptr, 0);
@@ -837,9 +911,14 @@ ifx_status Model::build_mega(KvCache &kv) {
   return IFX_OK;
 }
 
-ifx_status Model::run_decode(KvCache &kv) {
+ifx_status Model::run_decode(KvCache &kv, bool gather_logits) {
   if (opts.persistent_decode && !kv.mega_tried) IFX_TRY(build_mega(kv));
-  if (kv.mega_ready) return mega_launch(kv.mega, stream);
+  if (kv.mega_ready) {
+    IFX_TRY(mega_launch(kv.mega, stream));
+    if (tp > 1 && gather_logits)
+      IFX_NCCL(nccl, nccl->AllGather(logits_local, logits, Vl, ncclFloat32, (ncclComm_t)comm, stream));
+    return IFX_OK;
+  }
   if (!opts.use_graphs) return enqueue_decode(kv, stream);
   if (!kv.graph) {
     cudaGraph_t g;
@@ -860,6 +939,10 @@ ifx_status Model::check_err() {
   IFX_CUDA(cudaMemcpy(&h, err, sizeof(int), cudaMemcpyDeviceToHost));
   if (h) {
     cudaMemset(err, 0, sizeof(int));
+    // under tensor parallelism the ranks may now disagree on where the step
+    // stopped (the persistent kernel's all-reduce epochs, the collectives):
+    // refuse further calls, as after an aborted communicator
+    if (tp > 1) comm_aborted = true;
     return fail(IFX_ERR_TIMEOUT, "a bounded device wait gave up (code " + std::to_string(h) + ")");
   }
   return IFX_OK;
@@ -1308,7 +1391,7 @@ ifx_status Model::generate(KvCache &kv, const uint32_t *prompt, size_t n_prompt,
   IFX_CUDA(launch(argmax_step_kernel, dim3(kNumSMs), dim3(256), 0, st, false, (const float *)logits,
                   (int)cfg.vocab_size, amax_key, amax_count, next_token, kv.tokens, n_out, kv.pos, 1, 0,
                   0, 1));
-  for (size_t i = 0; i < max_tokens; ++i) IFX_TRY(run_decode(kv));
+  for (size_t i = 0; i < max_tokens; ++i) IFX_TRY(run_decode(kv, i + 1 == max_tokens));
   if (max_tokens)
     IFX_CUDA(cudaMemcpyAsync(out, kv.tokens, max_tokens * sizeof(uint32_t), cudaMemcpyDeviceToHost, st));
   IFX_TRY(step_sync(st));
@@ -1333,7 +1416,7 @@ ifx_status Model::decode_greedy(KvCache &kv, uint32_t token, size_t n, uint32_t 
     IFX_CUDA(cudaEventCreate(&e1));
     IFX_CUDA(cudaEventRecord(e0, st));
   }
-  for (size_t i = 0; i < n; ++i) IFX_TRY(run_decode(kv));
+  for (size_t i = 0; i < n; ++i) IFX_TRY(run_decode(kv, i + 1 == n));
   if (device_ms) IFX_CUDA(cudaEventRecord(e1, st));
   if (out && n)
     IFX_CUDA(cudaMemcpyAsync(out, kv.tokens, n * sizeof(uint32_t), cudaMemcpyDeviceToHost, st));

@@ -97,6 +97,13 @@ struct Model {
   const struct NcclApi *nccl = nullptr;
   uint64_t Hl = 0, Gl = 0, Fl = 0, Vl = 0, v0 = 0;
   float *y = nullptr;               // partial sums of the row-parallel layers
+  // the persistent kernel's all-reduce buffers (every rank's, mapped here
+  // by CUDA IPC); peers_ok only when every rank mapped every other's
+  MegaPeers peers{};
+  char *peer_buf = nullptr;
+  unsigned *mega_epoch = nullptr;
+  bool peers_ok = false;
+  ifx_status setup_peers();
   float *logits_local = nullptr;    // this rank's vocab slice (== logits at tp 1)
   unsigned long long *key_global = nullptr;
   float *w_y = nullptr;             // prefill partial sums [n][D]
@@ -139,7 +146,9 @@ struct Model {
   ifx_status load(const uint8_t *bytes, size_t len, const ifx_load_opts &o);
   ifx_status enqueue_decode(KvCache &kv, cudaStream_t st);
   ifx_status build_mega(KvCache &kv);
-  ifx_status run_decode(KvCache &kv);
+  // gather_logits: under tensor parallelism, also gather the vocab slices
+  // into logits (the persistent kernel leaves each rank's slice only)
+  ifx_status run_decode(KvCache &kv, bool gather_logits = true);
   ifx_status decode_step(KvCache &kv, uint32_t token, float *logits_host);
   ifx_status prefill(KvCache &kv, const uint32_t *ids, size_t n, float *logits_host, int last_row_only);
   ifx_status forward(const uint32_t *ids, size_t n, float *logits_host, int last_row_only);

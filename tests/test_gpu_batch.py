@@ -29,12 +29,17 @@ def _close(g, r):
 def _model(name):
     if name == "1b":
         return synth.build("1b")
+    if name in ("grp6", "grp8"):  # 6 / 8 query heads per kv head (the 70B shape has 8)
+        heads = 12 if name == "grp6" else 16
+        return synth.build(None, vocab=2048, dim=64 * heads, n_layers=2, n_heads=heads, n_kv_heads=2,
+                           ffn=1024, context=128, rope_base=10000.0, mix=1, seed=33)
     mix = 1 if name == "small_q4km" else 0  # Q4_K_M mix, or all Q8_0
     return synth.build(None, vocab=2048, dim=512, n_layers=2, n_heads=8, n_kv_heads=2, ffn=1024,
                        context=128, rope_base=500000.0, mix=mix, seed=31)
 
 
-@pytest.mark.parametrize("name,batch,steps", [("small_q4km", 5, 4), ("small_q8", 3, 3), ("1b", 3, 2)])
+@pytest.mark.parametrize("name,batch,steps", [("small_q4km", 5, 4), ("small_q8", 3, 3), ("1b", 3, 2),
+                                              ("grp6", 3, 3), ("grp8", 4, 3)])
 def test_batched_decode_matches_oracle(name, batch, steps):
     g = _model(name)
     m, o = Model.from_bytes(g), R.Model(g)
@@ -138,3 +143,23 @@ def test_subset_steps_and_slot_reuse():
             kb.decode_step_seqs(bad, [3] * len(bad))
     with pytest.raises(IfxError):
         kb.reset(4)
+
+
+@pytest.mark.parametrize("name", ["grp6", "grp8"])
+def test_single_sequence_decode_wide_groups(name):
+    """The persistent kernel's tensor-core attention with two 8-column tiles
+    (five to eight query heads per kv head) against the oracle, past one
+    split of cached rows."""
+    g = _model(name)
+    m, o = Model.from_bytes(g), R.Model(g)
+    V, L = int(m.config.vocab_size), int(m.config.n_layers)
+    kv, okv = m.kv_cache(128), o.kv_cache(L, 128)
+    p = synth.prompt_ids(V, 90, seed=5)
+    gl, rl = m.prefill(p, kv, True)[0], o.prefill(p, okv, True)[0]
+    assert _close(gl, rl)
+    tok = R.argmax(rl)
+    for i in range(6):
+        gl, rl = m.decode_step(tok, kv), o.decode_step(tok, okv)
+        assert _close(gl, rl), (i, float(np.max(np.abs(gl - rl))))
+        tok = R.argmax(rl)
+    assert kv.decode_kernels() == 1

@@ -4,10 +4,13 @@ Two spawned ranks, each on its own GPU, load the same synthetic GGUF with
 tp_size 2 through a communicator made by the library (ifx_tp_unique_id /
 ifx_tp_comm_create), run a prefill and greedy decode steps, and hand their
 (all-gathered, hence full) logits to the parent, which holds them to the
-oracle at the parity bar and to each other bit for bit. The ranks do no
+oracle at the parity bar and to each other bit for bit. Decode runs both
+ways: the persistent kernel with its all-reduces over peer memory inside
+the step, and the per-op kernels with NCCL between them. The ranks do no
 checking themselves, so neither can leave the other waiting in a
-collective; the parent kills both if they do not report in time. Skipped
-with fewer than two GPUs.
+collective; the parent kills both if they do not report in time. NVLS is
+off (NCCL_NVLS_ENABLE=0) and the kernel's own waits use plain peer loads.
+Skipped with fewer than two GPUs.
 """
 import os
 
@@ -25,12 +28,13 @@ ATOL, RTOL = 2e-2, 1e-2
 R.set_threads(os.cpu_count() or 8)
 
 
-def _rank(rank, world, uid, g, prompt, steps, q):
+def _rank(rank, world, uid, g, prompt, steps, q, persistent):
     try:
         os.environ["NCCL_NVLS_ENABLE"] = "0"
         from inferox_b200 import Model
         comm = tp.Comm(uid, world, rank, rank)
-        m = Model.from_bytes(g, device=rank, tp_size=world, tp_rank=rank, nccl_comm=comm.handle)
+        m = Model.from_bytes(g, device=rank, tp_size=world, tp_rank=rank, nccl_comm=comm.handle,
+                             persistent_decode=persistent)
         kv = m.kv_cache(128)
         out = {"prefill_last": m.prefill(prompt, kv, True)[0]}
         out["prefill_all"] = m.prefill(prompt, m.kv_cache(128), False)
@@ -52,12 +56,15 @@ def _close(a, b):
     return np.all(np.abs(a - b) <= ATOL + RTOL * np.abs(b))
 
 
-@pytest.mark.parametrize("mix", [1, 0])  # Q4_K_M mix; all Q8_0
-def test_tp2_matches_oracle(mix):
+@pytest.mark.parametrize("mix,persistent,heads", [(1, True, 8), (0, True, 8), (1, False, 8),
+                                                  (0, False, 8), (1, True, 16)])
+def test_tp2_matches_oracle(mix, persistent, heads):
+    """mix 1: Q4_K_M, 0: all Q8_0; heads 16 over 2 kv heads: 8 query heads
+    per kv head on each rank, as in the 70B shape."""
     if torch.cuda.device_count() < 2:
         pytest.skip("needs two GPUs")
-    g = synth.build(None, vocab=2048, dim=512, n_layers=2, n_heads=8, n_kv_heads=2, ffn=1024,
-                    context=128, rope_base=500000.0, mix=mix, seed=21)
+    g = synth.build(None, vocab=2048, dim=64 * heads, n_layers=2, n_heads=heads, n_kv_heads=2,
+                    ffn=1024, context=128, rope_base=500000.0, mix=mix, seed=21)
     prompt = synth.prompt_ids(2048, 10, seed=3)
     o = R.Model(g)
     okv = o.kv_cache(2, 128)
@@ -73,7 +80,8 @@ def test_tp2_matches_oracle(mix):
     uid = tp.unique_id()
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    procs = [ctx.Process(target=_rank, args=(r, 2, uid, g, prompt, steps, q)) for r in range(2)]
+    procs = [ctx.Process(target=_rank, args=(r, 2, uid, g, prompt, steps, q, persistent))
+             for r in range(2)]
     for p in procs:
         p.start()
     res = {}
@@ -96,4 +104,5 @@ def test_tp2_matches_oracle(mix):
     for i, r in enumerate(ref_dec):
         assert _close(a["decode"][i], r), (i, float(np.max(np.abs(a["decode"][i] - r))))
     assert np.array_equal(a["greedy"], b["greedy"])
-    assert a["kernels"] == 3 + 5 * 2  # per-op kernels with the collectives between them
+    # the persistent kernel, or the per-op kernels with the collectives between them
+    assert a["kernels"] == (1 if persistent else 3 + 5 * 2)
