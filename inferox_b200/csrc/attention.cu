@@ -357,6 +357,102 @@ __global__ void __launch_bounds__(kAttnThreads) decode_attn_kernel(const __grid_
   attn_combine(part_o, part_ml, attn_out, counters, h, NS, grp, hd, tid, kAttnThreads);
 }
 
+// ------------------------------------------------------ decode, small heads --
+// Head sizes that are not a multiple of 8 (the reference's own test fixtures
+// use 4-wide heads): one CTA per (kv head, sequence) with plain loads of
+// every cached row and an exact softmax over the whole context, in the
+// reference's order (forward.rs:379-414): scores q.k / sqrt(d), max, exp,
+// sum, then the weighted sum of V divided by the sum.
+__global__ void __launch_bounds__(128) decode_attn_small_kernel(const __grid_constant__ DecodeAttnArgs a) {
+  extern __shared__ float sml[];  // q [grp][hd] | scores [max_seq]
+  __shared__ float red[4], s_val;
+  const int h = blockIdx.x, b = blockIdx.z, tid = threadIdx.x;
+  const int grp = a.H / a.G, hd = a.hd;
+  const float *qkv = a.qkv + (size_t)b * a.qkv_stride;
+  const int sq = a.slot ? a.slot[b] : b;
+  float *attn_out = a.attn_out + (size_t)b * a.H * hd;
+  auto row_off = [&](int t) -> size_t {
+    if (a.page_table) {
+      const int pg = a.page_table[(size_t)sq * a.max_pages + t / a.page_rows];
+      return (size_t)pg * a.page_stride + ((size_t)h * a.page_rows + t % a.page_rows) * hd;
+    }
+    return (size_t)sq * a.kv_seq_stride + ((size_t)h * a.max_seq + t) * hd;
+  };
+  pdl_wait();
+  pdl_launch();
+  if (a.zero_ptr && b == 0)
+    for (int i = h * 128 + tid; i < a.zero_n; i += a.G * 128) a.zero_ptr[i] = 0.f;
+  const int pos = a.pos[sq], len = pos + 1;
+  const int rpos = a.rope_compat ? 0 : pos;
+  float *qs = sml, *sc = sml + grp * hd;
+  const float *q = qkv + (size_t)h * grp * hd;
+  for (int e = tid; e < grp * hd / 2; e += 128) {
+    const int j = e / (hd / 2), i = 2 * (e % (hd / 2));
+    float x0 = q[j * hd + i], x1 = q[j * hd + i + 1];
+    if (i < a.rope_dim) rope_pair(x0, x1, i, a.rope_dim, a.rope_base, rpos);
+    qs[j * hd + i] = x0;
+    qs[j * hd + i + 1] = x1;
+  }
+  {  // append this token's K/V (forward.rs:375-378), K rotated like q
+    const float *kn = qkv + (size_t)a.H * hd + (size_t)h * hd;
+    const float *vn = qkv + (size_t)(a.H + a.G) * hd + (size_t)h * hd;
+    const size_t off = row_off(pos);
+    for (int e = tid; e < hd / 2; e += 128) {
+      const int i = 2 * e;
+      float x0 = kn[i], x1 = kn[i + 1];
+      if (i < a.rope_dim) rope_pair(x0, x1, i, a.rope_dim, a.rope_base, rpos);
+      const int ip = kv_col(pos, i, hd);
+      a.kc[off + ip] = __float2half_rn(x0);
+      a.kc[off + ip + 1] = __float2half_rn(x1);
+      a.vc[off + ip] = __float2half_rn(vn[i]);
+      a.vc[off + ip + 1] = __float2half_rn(vn[i + 1]);
+    }
+  }
+  __syncthreads();
+  const float sqd = sqrtf((float)hd);
+  auto block_reduce = [&](float v, bool is_max) -> float {
+    for (int o = 16; o; o >>= 1) {
+      const float w = __shfl_xor_sync(0xffffffffu, v, o);
+      v = is_max ? fmaxf(v, w) : v + w;
+    }
+    if ((tid & 31) == 0) red[tid >> 5] = v;
+    __syncthreads();
+    if (tid == 0) {
+      float r = red[0];
+      for (int i = 1; i < 4; ++i) r = is_max ? fmaxf(r, red[i]) : r + red[i];
+      s_val = r;
+    }
+    __syncthreads();
+    const float r = s_val;
+    __syncthreads();
+    return r;
+  };
+  for (int j = 0; j < grp; ++j) {
+    float mx = -INFINITY;
+    for (int t = tid; t < len; t += 128) {
+      const __half *kr = a.kc + row_off(t);
+      float acc = 0.f;
+      for (int d = 0; d < hd; ++d) acc = fmaf(qs[j * hd + d], __half2float(kr[kv_col(t, d, hd)]), acc);
+      sc[t] = acc / sqd;  // forward.rs:396
+      mx = fmaxf(mx, sc[t]);
+    }
+    mx = block_reduce(mx, true);
+    float sum = 0.f;
+    for (int t = tid; t < len; t += 128) {
+      const float p = expf(sc[t] - mx);
+      sc[t] = p;
+      sum += p;
+    }
+    sum = block_reduce(sum, false);  // also orders the score writes before the reads below
+    for (int d = tid; d < hd; d += 128) {
+      float o = 0.f;
+      for (int t = 0; t < len; ++t) o = fmaf(sc[t], __half2float(a.vc[row_off(t) + kv_col(t, d, hd)]), o);
+      attn_out[(size_t)(h * grp + j) * hd + d] = o / sum;
+    }
+    __syncthreads();  // sc is reused by the next head
+  }
+}
+
 // ------------------------------------------------------ decode, streamed --
 // Split-K decode attention for head sizes 64 and 128 with at most eight
 // query heads per kv head, written for many cached rows per CTA (the batched
@@ -427,13 +523,14 @@ __global__ void __launch_bounds__(kFlashWarps * 32, 3)
   uint64_t *mybar = bars + warp * 2;
   // rows of tile T that come from the cache (those before pos)
   uint32_t iss[2] = {0u, 0u}, done[2] = {0u, 0u};  // lane 0: copies issued / waited per stage
-  auto issue = [&](int T, int st) {
+  // off: row_off of the tile's first row (read ahead: a paged cache costs a
+  // page-table load)
+  auto issue = [&](int T, int st, size_t off) {
     ++iss[st];
     const int t0 = T * kFlashRows;
     const int nold = max(0, min(t0 + kFlashRows, pos) - t0);
     __half *dk = myst + (size_t)st * 2 * TH;
     if (nold > 0) {
-      const size_t off = row_off(t0);
       mbar_arrive_expect_tx(&mybar[st], 2u * (uint32_t)nold * HD * 2u);
       bulk_g2s(dk, a.kc + off, (uint32_t)nold * HD * 2u, &mybar[st]);
       bulk_g2s(dk + TH, a.vc + off, (uint32_t)nold * HD * 2u, &mybar[st]);
@@ -447,8 +544,9 @@ __global__ void __launch_bounds__(kFlashWarps * 32, 3)
     fence_mbar_init();
     // the cached rows were written by kernels that completed before the
     // previous kernel in the stream began its main phase
-    if (tb + warp < te) issue(tb + warp, 0);
-    if (tb + warp + kFlashWarps < te) issue(tb + warp + kFlashWarps, 1);
+    if (tb + warp < te) issue(tb + warp, 0, row_off((tb + warp) * kFlashRows));
+    if (tb + warp + kFlashWarps < te)
+      issue(tb + warp + kFlashWarps, 1, row_off((tb + warp + kFlashWarps) * kFlashRows));
   }
 
   pdl_wait();
@@ -495,6 +593,9 @@ __global__ void __launch_bounds__(kFlashWarps * 32, 3)
     const int T = tb + warp + kFlashWarps * i;
     if (T >= te) break;
     const int st = i & 1;
+    // the cache offset of the tile this stage takes next, loaded before the wait
+    const bool more = T + 2 * kFlashWarps < te;
+    const size_t next_off = (lane == 0 && more) ? row_off((T + 2 * kFlashWarps) * kFlashRows) : 0;
     ok = __all_sync(0xffffffffu, mbar_wait(&mybar[st], (uint32_t)(i >> 1) & 1u, a.err, 306));
     if (!ok) break;  // the error flag is set; the host reports a timeout
     ++done[st];
@@ -576,7 +677,7 @@ __global__ void __launch_bounds__(kFlashWarps * 32, 3)
       mma_16816(o[nd + 1], pa[0], pa[1], pa[2], pa[3], vb[2], vb[3], o[nd + 1]);
     }
     __syncwarp();  // every lane has read this stage
-    if (lane == 0 && T + 2 * kFlashWarps < te) issue(T + 2 * kFlashWarps, st);
+    if (lane == 0 && more) issue(T + 2 * kFlashWarps, st, next_off);
   }
   // leave no copy in flight after an early exit: wait (bounded) for the
   // stages this warp issued but did not consume
@@ -765,6 +866,18 @@ ifx_status decode_attention(const DecodeAttnArgs &a, cudaStream_t st, bool pdl) 
   // pages: its splits are its own, at most the caller's)
   if (a.hd == 128) return launch_flash<128>(a, st, pdl);
   if (a.hd == 64) return launch_flash<64>(a, st, pdl);
+  if (a.hd % 8 && a.hd % 2 == 0) {  // narrow heads: one CTA per kv head and sequence
+    const size_t smem = (size_t)(grp * a.hd + a.max_seq) * sizeof(float);
+    if (smem > 200 * 1024) return fail(IFX_ERR_UNSUPPORTED, "attention: context too long for small heads");
+    static size_t attr = 0;
+    if (smem > 48 * 1024 && smem > attr) {
+      IFX_CUDA(cudaFuncSetAttribute(decode_attn_small_kernel,
+                                    cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+      attr = smem;
+    }
+    IFX_CUDA(launch(decode_attn_small_kernel, dim3(a.G, 1, a.batch), dim3(128), smem, st, pdl, a));
+    return IFX_OK;
+  }
   if (a.hd > 256 || a.hd % 8 || a.ns > kMaxSplits) return fail(IFX_ERR_UNSUPPORTED, "attention shape");
   const size_t smem = (size_t)decode_attention_smem(grp, a.hd, a.max_seq, a.ns);
   if (smem > 200 * 1024) return fail(IFX_ERR_UNSUPPORTED, "attention: KV chunk too large for shared memory");

@@ -8,6 +8,7 @@
 #include <new>
 #include <string>
 
+#include "dense.cuh"
 #include "gemm.cuh"
 #include "gemv.cuh"
 #include "model.h"
@@ -360,7 +361,9 @@ ifx_status ifx_qmatrix_create(int type, const void *gguf_bytes_host, size_t nbyt
   IFX_GUARD({
     ifx_qmatrix *w = new ifx_qmatrix();
     w->q.device = device;
-    if (!make_layout(type, (int64_t)rows, (int64_t)cols, &w->q.L)) {
+    const bool dense = dense_type(type);  // F32 / F16 / Q8_K: dequantised f32 rows
+    if (dense) make_dense_layout((int64_t)rows, (int64_t)cols, type, &w->q.L);
+    if (!dense && !make_layout(type, (int64_t)rows, (int64_t)cols, &w->q.L)) {
       delete w;
       return fail(IFX_ERR_UNSUPPORTED, "qmatrix_create: unsupported type or shape");
     }
@@ -374,7 +377,10 @@ ifx_status ifx_qmatrix_create(int type, const void *gguf_bytes_host, size_t nbyt
     cudaError_t e = cudaMalloc(&staging, nbytes);
     if (e == cudaSuccess) e = cudaMemcpy(staging, gguf_bytes_host, nbytes, cudaMemcpyHostToDevice);
     if (e == cudaSuccess) e = cudaMalloc(&w->q.d, w->q.L.total_bytes);
-    ifx_status s = e == cudaSuccess ? repack_to_device(w->q.L, staging, w->q.d, 0) : cuda_fail(e, "qmatrix_create");
+    ifx_status s = e != cudaSuccess ? cuda_fail(e, "qmatrix_create")
+                   : dense ? op_dequantize(type, staging, nbytes, reinterpret_cast<float *>(w->q.d),
+                                           rows * cols, 0)
+                           : repack_to_device(w->q.L, staging, w->q.d, 0);
     if (s == IFX_OK) {
       e = cudaDeviceSynchronize();
       if (e != cudaSuccess) s = cuda_fail(e, "qmatrix repack");
@@ -417,8 +423,10 @@ ifx_status ifx_op_matmul_t_q(const float *a_dev, const ifx_qmatrix *w, float *c_
     gemv_plan_free(&p);
   } else {
     void *xf = nullptr;
-    IFX_CUDA(cudaMalloc(&xf, gemm_xfrag_bytes((int64_t)m, W.L.cols)));
-    s = gemm_stage_x(a_dev, nullptr, nullptr, 0.f, GX_PLAIN, (int64_t)m, W.L.cols, xf, st);
+    IFX_CUDA(cudaMalloc(&xf, std::max(gemm_xfrag_bytes((int64_t)m, W.L.cols),
+                                      (size_t)m * W.L.cols * sizeof(float))));
+    s = W.L.dense ? dense_stage(a_dev, nullptr, nullptr, 0.f, GX_PLAIN, (int64_t)m, W.L.cols, xf, st)
+                  : gemm_stage_x(a_dev, nullptr, nullptr, 0.f, GX_PLAIN, (int64_t)m, W.L.cols, xf, st);
     if (s == IFX_OK) s = gemm_run(W, xf, (int64_t)m, c_dev, W.L.rows, 0, err, st);
     cudaStreamSynchronize(st);
     cudaFree(xf);
@@ -512,6 +520,7 @@ ifx_status ifx_bench_matmul_t_q(const float *a_dev, const ifx_qmatrix *w, float 
                                 int reps, float *ms_per_call) {
   if (!a_dev || !w || !c_dev || !ms_per_call) return fail(IFX_ERR_INVALID_ARGUMENT, "bench_matmul_t_q: null");
   if (m == 0 || reps < 1) return fail(IFX_ERR_INVALID_ARGUMENT, "bench_matmul_t_q: m and reps must be >= 1");
+  if (w->q.L.dense) return fail(IFX_ERR_UNSUPPORTED, "bench_matmul_t_q: times the fused quantised kernels only");
   IFX_GUARD({ return bench_matmul_t_q(a_dev, w->q, c_dev, m, reps, ms_per_call); })
 }
 

@@ -11,6 +11,7 @@
 #include <algorithm>
 
 #include "gemm.cuh"
+#include "dense.cuh"
 
 namespace ifx {
 
@@ -32,7 +33,7 @@ __device__ __forceinline__ float silu_g(float v) {
 // row) and writes them into the fragment layout [mblock][chunk][plane][nt]
 // [lane][4 halves] of blocks of 8 * NT tokens, then the per-token 32-column
 // sums.
-constexpr int kStageCols = 2048;
+constexpr int kStageCols = 256;  // 8 warps: one column per thread
 
 __global__ void stage_x_kernel(const float *X, const float *X2, const float *normw, float eps,
                                int mode, int64_t M, int64_t K, int NT, __half *out) {
@@ -126,6 +127,79 @@ struct GemmArgs {
   uint32_t smask;  // 0x80: Q6_K scale bytes are int8 (llama.cpp), else 0
   int *err;
 };
+
+// Q4_K unit with the 6-bit sub-scale folded into the A operand: sc * q
+// (rows g) and 16 sc * q (rows g+8, high nibbles) are integers of at most 10
+// significant bits, exact in f16, made by one f16x2 FMA per register
+// ((1024 + q) sc - 1024 sc, a single rounding of an exact result). The
+// MMAs then accumulate a whole 256-column unit, d is applied once per unit,
+// and the mins term sum_g m_g S_g (S_g the staged group sums of x) is one
+// more k16 MMA per token tile (A = the eight 6-bit mins of each row, B = the
+// group sums as hi/lo f16), scaled by dmin. Two accumulators (even and odd
+// chunks) keep the MMA chains short.
+template <int NT>
+__device__ __forceinline__ void gemm_unit_q4k(const uint8_t *wt, const uint8_t *xs, const float *sx,
+                                              int lane, float (&acc)[NT][4]) {
+  const int g = lane >> 2, c = lane & 3;
+  const __half2 b1024 = __float2half2_rn(1024.f), m1024 = __float2half2_rn(-1024.f);
+  const uint4 hA = *reinterpret_cast<const uint4 *>(wt + 2048 + 16 * g);
+  const uint4 hB = *reinterpret_cast<const uint4 *>(wt + 2048 + 16 * (g + 8));
+  const float dA = h2f((uint16_t)prmt(hA.x, hA.y, 0x0073u));
+  const float dmA = h2f((uint16_t)prmt(hA.z, hA.w, 0x0073u));
+  const float dB = h2f((uint16_t)prmt(hB.x, hB.y, 0x0073u)) * 0.0625f;
+  const float dmB = h2f((uint16_t)prmt(hB.z, hB.w, 0x0073u));
+  const uint32_t *wq = reinterpret_cast<const uint32_t *>(wt);
+  float ua[2][NT][4];
+#pragma unroll
+  for (int p = 0; p < 2; ++p)
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) ua[p][nt][0] = ua[p][nt][1] = ua[p][nt][2] = ua[p][nt][3] = 0.f;
+  const uint32_t hw[2][4] = {{hA.x, hA.y, hA.z, hA.w}, {hB.x, hB.y, hB.z, hB.w}};
+#pragma unroll
+  for (int gi = 0; gi < 8; ++gi) {
+    const int sh = 6 * (gi & 1);
+    const uint32_t sa = (hw[0][gi >> 1] >> sh) & 63u, sb = (hw[1][gi >> 1] >> sh) & 63u;
+    const __half2 scA = __hsub2(u2h(0x64006400u | sa | (sa << 16)), b1024);  // exact
+    const __half2 scB = __hsub2(u2h(0x64006400u | sb | (sb << 16)), b1024);
+    const __half2 ngA = __hmul2(scA, m1024), ngB = __hmul2(scB, m1024);      // -1024 sc, exact
+#pragma unroll
+    for (int cc = 0; cc < 2; ++cc) {
+      const int ch = 2 * gi + cc;
+      const uint32_t wd = wq[((ch / 4) * 32 + lane) * 4 + ch % 4];
+      const uint32_t hi = wd >> 8;
+      const uint32_t a0 = h2u(__hfma2(u2h((wd & 0x000F000Fu) | 0x64006400u), scA, ngA));
+      const uint32_t a1 = h2u(__hfma2(u2h((wd & 0x00F000F0u) | 0x64006400u), scB, ngB));
+      const uint32_t a2 = h2u(__hfma2(u2h((hi & 0x000F000Fu) | 0x64006400u), scA, ngA));
+      const uint32_t a3 = h2u(__hfma2(u2h((hi & 0x00F000F0u) | 0x64006400u), scB, ngB));
+      const uint2 *xb = reinterpret_cast<const uint2 *>(xs + (size_t)ch * xchunk_bytes(NT)) + lane;
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt) {
+        const uint2 bh = xb[nt * 32], bl = xb[NT * 32 + nt * 32];
+        mma_16816(ua[cc][nt], a0, a1, a2, a3, bh.x, bh.y, ua[cc][nt]);
+        mma_16816(ua[cc][nt], a0, a1, a2, a3, bl.x, bl.y, ua[cc][nt]);
+      }
+    }
+  }
+  // mins: A row g = (m_2c, m_2c+1) of row g, row g+8 the same of row g+8
+  // (k = group, groups 8-15 absent); B = (S_2c, S_2c+1) of token g as hi/lo
+  const uint32_t fA = hw[0][c], fB = hw[1][c];
+  const uint32_t am0 = h2u(__hsub2(u2h(0x64006400u | ((fA >> 12) & 63u) | (((fA >> 18) & 63u) << 16)), b1024));
+  const uint32_t am1 = h2u(__hsub2(u2h(0x64006400u | ((fB >> 12) & 63u) | (((fB >> 18) & 63u) << 16)), b1024));
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt) {
+    const int tok = 8 * nt + g;
+    const float s0 = sx[(2 * c) * (8 * NT) + tok], s1 = sx[(2 * c + 1) * (8 * NT) + tok];
+    const __half2 sh2 = __floats2half2_rn(s0, s1);
+    const __half2 sl2 = __floats2half2_rn(s0 - __low2float(sh2), s1 - __high2float(sh2));
+    float mc[4] = {0.f, 0.f, 0.f, 0.f};
+    mma_16816(mc, am0, am1, 0u, 0u, h2u(sh2), 0u, mc);
+    mma_16816(mc, am0, am1, 0u, 0u, h2u(sl2), 0u, mc);
+    acc[nt][0] = fmaf(dA, ua[0][nt][0] + ua[1][nt][0], fmaf(-dmA, mc[0], acc[nt][0]));
+    acc[nt][1] = fmaf(dA, ua[0][nt][1] + ua[1][nt][1], fmaf(-dmA, mc[1], acc[nt][1]));
+    acc[nt][2] = fmaf(dB, ua[0][nt][2] + ua[1][nt][2], fmaf(-dmB, mc[2], acc[nt][2]));
+    acc[nt][3] = fmaf(dB, ua[0][nt][3] + ua[1][nt][3], fmaf(-dmB, mc[3], acc[nt][3]));
+  }
+}
 
 template <int TYPE, int NT>
 __device__ __forceinline__ void gemm_unit(const uint8_t *wt, const uint8_t *xs, const float *sx,
@@ -252,7 +326,7 @@ __device__ __forceinline__ void gemm_unit(const uint8_t *wt, const uint8_t *xs, 
 // takes a contiguous share of the row tile's units, results added
 // atomically).
 template <int NT>
-__global__ void __launch_bounds__(kGThreads, 1) gemm_kernel(const __grid_constant__ GemmArgs a) {
+__global__ void __launch_bounds__(kGThreads, NT <= 2 ? 3 : 1) gemm_kernel(const __grid_constant__ GemmArgs a) {
   extern __shared__ __align__(128) uint8_t smem[];
   uint64_t *full_bar = reinterpret_cast<uint64_t *>(smem);
   uint64_t *empty_bar = full_bar + kGStages;
@@ -310,7 +384,7 @@ __global__ void __launch_bounds__(kGThreads, 1) gemm_kernel(const __grid_constan
     const uint8_t *xs = base + a.unit_bytes;
     const float *sx = reinterpret_cast<const float *>(xs + a.kc / 16 * xchunk_bytes(NT));
     switch (a.type) {
-      case IFX_TYPE_Q4_K: gemm_unit<IFX_TYPE_Q4_K, NT>(wt, xs, sx, a.kc, a.wt_qbytes, a.smask, lane, acc); break;
+      case IFX_TYPE_Q4_K: gemm_unit_q4k<NT>(wt, xs, sx, lane, acc); break;
       case IFX_TYPE_Q6_K: gemm_unit<IFX_TYPE_Q6_K, NT>(wt, xs, sx, a.kc, a.wt_qbytes, a.smask, lane, acc); break;
       case IFX_TYPE_Q4_0: gemm_unit<IFX_TYPE_Q4_0, NT>(wt, xs, sx, a.kc, a.wt_qbytes, a.smask, lane, acc); break;
       default: gemm_unit<IFX_TYPE_Q8_0, NT>(wt, xs, sx, a.kc, a.wt_qbytes, a.smask, lane, acc); break;
@@ -423,6 +497,10 @@ static ifx_status launch_sync(const QMatrix &W, const void *xfrag, int64_t M, fl
 ifx_status gemm_run_multi(const QMatrix *const *W, float *const *C, const int64_t *ldc, int n,
                           const void *xfrag, int64_t M, int accumulate, int *err,
                           cudaStream_t st) {
+  if (n >= 1 && W[0]->L.dense) {
+    for (int i = 0; i < n; ++i) IFX_TRY(dense_gemm(*W[i], xfrag, M, C[i], ldc[i], accumulate, st));
+    return IFX_OK;
+  }
   if (n >= 1 && tc_gemm_eligible(W[0]->L.cols))
     return tc_gemm_run_multi(W, C, ldc, n, xfrag, M, accumulate, err, st);
   for (int i = 0; i < n; ++i) IFX_TRY(gemm_run(*W[i], xfrag, M, C[i], ldc[i], accumulate, err, st));
@@ -431,12 +509,14 @@ ifx_status gemm_run_multi(const QMatrix *const *W, float *const *C, const int64_
 
 ifx_status gemm_run(const QMatrix &W, const void *xfrag, int64_t M, float *C, int64_t ldc,
                     int accumulate, int *err, cudaStream_t st) {
+  if (W.L.dense) return dense_gemm(W, xfrag, M, C, ldc, accumulate, st);
   if (tc_gemm_eligible(W.L.cols)) return tc_gemm_run(W, xfrag, M, C, ldc, accumulate, err, st);
   return launch_sync<kGemmTokens / 8>(W, xfrag, M, C, ldc, accumulate, 1, err, st);
 }
 
 ifx_status gemm_small_run(const QMatrix &W, const void *xfrag, int64_t M, float *C, int64_t ldc,
                           int *err, cudaStream_t st) {
+  if (W.L.dense) return dense_gemm(W, xfrag, M, C, ldc, 1, st);
   if (M > kGemmSmallMax) return fail(IFX_ERR_UNSUPPORTED, "gemm: small batch above 32 tokens");
   // enough K splits for about two CTAs per SM, never more than the units
   const int ksplit = std::max(1, std::min(W.L.kunits, (2 * kNumSMs + W.L.ctiles - 1) / W.L.ctiles));

@@ -24,6 +24,7 @@
 #include <cstring>
 
 #include "gemv.cuh"
+#include "dense.cuh"
 #include "gemv_dev.cuh"
 
 namespace ifx {
@@ -84,6 +85,32 @@ ifx_status gemv_plan(const QMatrix *const *mats, float *const *ys, int nseg, int
                      const float *x, const float *x2, const float *normw, float eps, int *err,
                      GemvPlan *plan) {
   if (nseg < 1 || nseg > kGemvMaxSegs) return fail(IFX_ERR_INVALID_ARGUMENT, "gemv: nseg");
+  if (mats[0]->L.dense) {  // dense f32 matrices (dense.cu): no units, no schedule
+    GemvArgs a{};
+    a.nseg = nseg;
+    a.K = (int)mats[0]->L.cols;
+    uint64_t wbytes = 0;
+    for (int i = 0; i < nseg; ++i) {
+      if (!mats[i]->L.dense || mats[i]->L.cols != a.K)
+        return fail(IFX_ERR_SHAPE, "gemv: dense segments must share K");
+      a.seg[i].w = mats[i]->d;
+      a.seg[i].y = ys[i];
+      a.seg[i].rows = (int)mats[i]->L.rows;
+      wbytes += mats[i]->L.total_bytes;
+    }
+    a.mode = mode;
+    a.x = x;
+    a.x2 = x2;
+    a.normw = normw;
+    a.eps = eps;
+    a.err = err;
+    *plan = GemvPlan{};
+    plan->dense = 1;
+    plan->weight_bytes = wbytes;
+    IFX_TRY(dense_gemv_plan(a, &plan->grid, &plan->smem));
+    plan->args = a;
+    return IFX_OK;
+  }
   GemvArgs a{};
   a.nseg = nseg;
   a.kc = mats[0]->L.kc;
@@ -188,6 +215,7 @@ void gemv_plan_free(GemvPlan *plan) {
 }
 
 ifx_status gemv_launch(const GemvPlan &plan, cudaStream_t stream, bool pdl) {
+  if (plan.dense) return dense_gemv_launch(plan.args, plan.grid, plan.smem, stream, pdl);
   IFX_CUDA(launch(gemv_b1_kernel, dim3(plan.grid), dim3(kGemvThreads), plan.smem, stream, pdl,
                   plan.args));
   return IFX_OK;

@@ -55,6 +55,7 @@ struct GemvPlan {
   size_t smem = 0;
   int2 *d_sched = nullptr;  // owned by the plan's creator
   uint64_t weight_bytes = 0;
+  int dense = 0;  // dense f32 segments (dense.cu): no unit schedule
 };
 
 // Builds a byte-balanced schedule over `mats` (all with the same K and

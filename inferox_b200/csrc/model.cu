@@ -23,6 +23,7 @@
 #include <vector>
 
 #include "attention.cuh"
+#include "dense.cuh"
 #include "gemm.cuh"
 #include "gemv.cuh"
 #include "kquant.h"
@@ -245,7 +246,7 @@ static ifx_status reference_order(bool ggml, const uint8_t **src, uint64_t size,
 static ifx_status upload_matrix(const GgufFile &f, const uint8_t *bytes, size_t len, int idx,
                                 uint64_t rows, uint64_t cols, uint8_t *staging, cudaStream_t st,
                                 QMatrix *out, int tp = 1, int rank = 0, int split_k = 0,
-                                bool ggml = false) {
+                                bool ggml = false, bool dense = false) {
   uint64_t start, size;
   IFX_TRY(gguf_tensor_range(f, len, idx, &start, &size));
   const GgufTensor &t = f.tensors[idx];
@@ -262,6 +263,14 @@ static ifx_status upload_matrix(const GgufFile &f, const uint8_t *bytes, size_t 
     else rows /= tp;
     src = shard.data();
     size = shard.size();
+  }
+  if (dense) {  // row-major f32 with the reference's dequantisation (weights.rs:66-74)
+    make_dense_layout((int64_t)rows, (int64_t)cols, type, &out->L);
+    IFX_CUDA(cudaMemcpyAsync(staging, src, size, cudaMemcpyHostToDevice, st));
+    IFX_CUDA(cudaMalloc(&out->d, out->L.total_bytes));
+    IFX_TRY(op_dequantize(type, staging, size, reinterpret_cast<float *>(out->d), rows * cols, st));
+    IFX_CUDA(cudaStreamSynchronize(st));
+    return IFX_OK;
   }
   if (!make_layout(type, (int64_t)rows, (int64_t)cols, &out->L))
     return fail(IFX_ERR_UNSUPPORTED,
@@ -364,23 +373,30 @@ ifx_status Model::load(const uint8_t *bytes, size_t len, const ifx_load_opts &o)
     if (s != IFX_OK && st == IFX_OK) st = s;
     return s == IFX_OK;
   };
+  // a checkpoint with any dense (F32 / F16 / Q8_K) matrix runs every matrix
+  // dense: dequantised once to f32, as the reference does per call
+  dense = dense_type((int)f.tensors[i_out >= 0 ? i_out : i_emb].type);
+  for (uint64_t l = 0; l < cfg.n_layers; ++l)
+    for (int s = 1; s < 9; ++s)
+      if (s != 5 && dense_type((int)f.tensors[idx[l][s]].type)) dense = true;
+  const bool dn = dense;
   layers.resize(cfg.n_layers);
   for (uint64_t l = 0; l < cfg.n_layers && st == IFX_OK; ++l) {
     Layer &L = layers[l];
     guard(upload_norm(f, bytes, len, idx[l][0], D, staging, stream, &L.attn_norm)) &&
-        guard(upload_matrix(f, bytes, len, idx[l][1], D, D, staging, stream, &L.wq, tp, rank, 0, ggml)) &&
-        guard(upload_matrix(f, bytes, len, idx[l][2], G * hd, D, staging, stream, &L.wk, tp, rank, 0, ggml)) &&
-        guard(upload_matrix(f, bytes, len, idx[l][3], G * hd, D, staging, stream, &L.wv, tp, rank, 0, ggml)) &&
-        guard(upload_matrix(f, bytes, len, idx[l][4], D, D, staging, stream, &L.wo, tp, rank, 1, ggml)) &&
+        guard(upload_matrix(f, bytes, len, idx[l][1], D, D, staging, stream, &L.wq, tp, rank, 0, ggml, dn)) &&
+        guard(upload_matrix(f, bytes, len, idx[l][2], G * hd, D, staging, stream, &L.wk, tp, rank, 0, ggml, dn)) &&
+        guard(upload_matrix(f, bytes, len, idx[l][3], G * hd, D, staging, stream, &L.wv, tp, rank, 0, ggml, dn)) &&
+        guard(upload_matrix(f, bytes, len, idx[l][4], D, D, staging, stream, &L.wo, tp, rank, 1, ggml, dn)) &&
         guard(upload_norm(f, bytes, len, idx[l][5], D, staging, stream, &L.ffn_norm)) &&
-        guard(upload_matrix(f, bytes, len, idx[l][6], F, D, staging, stream, &L.w1, tp, rank, 0, ggml)) &&
-        guard(upload_matrix(f, bytes, len, idx[l][7], F, D, staging, stream, &L.w3, tp, rank, 0, ggml)) &&
-        guard(upload_matrix(f, bytes, len, idx[l][8], D, F, staging, stream, &L.w2, tp, rank, 1, ggml));
+        guard(upload_matrix(f, bytes, len, idx[l][6], F, D, staging, stream, &L.w1, tp, rank, 0, ggml, dn)) &&
+        guard(upload_matrix(f, bytes, len, idx[l][7], F, D, staging, stream, &L.w3, tp, rank, 0, ggml, dn)) &&
+        guard(upload_matrix(f, bytes, len, idx[l][8], D, F, staging, stream, &L.w2, tp, rank, 1, ggml, dn));
   }
   if (st == IFX_OK) guard(upload_norm(f, bytes, len, i_onorm, D, staging, stream, &out_norm));
   if (st == IFX_OK)
     guard(upload_matrix(f, bytes, len, i_out >= 0 ? i_out : i_emb, V, D, staging, stream, &out_w,
-                        tp, rank, 0, ggml));
+                        tp, rank, 0, ggml, dn));
   if (st == IFX_OK) {
     uint64_t s0, sz;
     if (guard(gguf_tensor_range(f, len, i_emb, &s0, &sz))) {
@@ -611,7 +627,8 @@ ifx_status KvBatch::create(Model *model, size_t max_seq_len, int nseq, size_t pa
   IFX_TRY(dalloc(&keys, (size_t)nseq));
   IFX_TRY(dalloc(&slots, (size_t)nseq));
   const size_t kmax = std::max<size_t>(std::max<size_t>(D, F), (size_t)H * hd);
-  IFX_CUDA(cudaMalloc(&xf, gemm_small_xfrag_bytes(nseq, (int64_t)kmax)));
+  IFX_CUDA(cudaMalloc(&xf, std::max(gemm_small_xfrag_bytes(nseq, (int64_t)kmax),
+                                    (size_t)nseq * kmax * sizeof(float))));
   len.assign((size_t)nseq, 0);
   return IFX_OK;
 }
@@ -806,6 +823,7 @@ ifx_status Model::build_mega(KvCache &kv) {
   // this rank's heads (all of them at tp 1)
   const int H = (int)Hl, G = (int)Gl, hd = (int)c.head_dim;
   if (tp > 1 && !peers_ok) return IFX_OK;  // the all-reduces run between the per-op kernels
+  if (dense) return IFX_OK;                 // the dense kernels run per op
   if (hd % 8 || hd > 256 || H % G || H / G > 8) return IFX_OK;  // separate kernels instead
   int dev_sms = 0;
   IFX_CUDA(cudaDeviceGetAttribute(&dev_sms, cudaDevAttrMultiProcessorCount, device));
@@ -911,6 +929,18 @@ ifx_status Model::build_mega(KvCache &kv) {
   return IFX_OK;
 }
 
+ifx_status Model::stage_rows(const float *X, const float *X2, const float *normw, float eps,
+                             int mode, int64_t M, int64_t K, void *buf, cudaStream_t st) {
+  if (dense) return dense_stage(X, X2, normw, eps, mode, M, K, buf, st);
+  return gemm_stage_x(X, X2, normw, eps, mode, M, K, buf, st);
+}
+
+ifx_status Model::stage_small(const float *X, const float *X2, const float *normw, float eps,
+                              int mode, int64_t M, int64_t K, void *buf, cudaStream_t st) {
+  if (dense) return dense_stage(X, X2, normw, eps, mode, M, K, buf, st);
+  return gemm_small_stage_x(X, X2, normw, eps, mode, M, K, buf, st);
+}
+
 ifx_status Model::run_decode(KvCache &kv, bool gather_logits) {
   if (opts.persistent_decode && !kv.mega_tried) IFX_TRY(build_mega(kv));
   if (kv.mega_ready) {
@@ -976,7 +1006,9 @@ ifx_status Model::ensure_ws(size_t n) {
   const ifx_config &c = cfg;
   const size_t D = c.hidden_size, Hh = Hl * c.head_dim, kvd = Gl * c.head_dim;
   const size_t F = Fl;
-  const size_t xf = gemm_xfrag_bytes((int64_t)n, (int64_t)std::max(D, F));
+  // staged inputs: the fused kernels' fragments, or plain f32 rows (dense)
+  const size_t xf = std::max(gemm_xfrag_bytes((int64_t)n, (int64_t)std::max(D, F)),
+                             n * std::max(std::max(D, F), Hh) * sizeof(float));
   const size_t floats = n * (D + Hh + 2 * kvd + Hh + 2 * F + (tp > 1 ? D : 0));
   IFX_CUDA(cudaMalloc(&ws, floats * sizeof(float) + xf + 1024));
   IFX_CUDA(cudaMalloc(&ids_dev, n * sizeof(uint32_t)));
@@ -1062,7 +1094,7 @@ ifx_status Model::enqueue_decode_batch(KvBatch &kb, cudaStream_t st, int n, cons
   for (uint64_t l = 0; l < c.n_layers; ++l) {
     Layer &L = layers[l];
     IFX_CUDA(cudaMemsetAsync(kb.qkv, 0, sizeof(float) * (size_t)B * qkvw, st));
-    IFX_TRY(gemm_small_stage_x(kb.x, nullptr, L.attn_norm, eps, GX_RMSNORM, B, D, kb.xf, st));
+    IFX_TRY(stage_small(kb.x, nullptr, L.attn_norm, eps, GX_RMSNORM, B, D, kb.xf, st));
     IFX_TRY(gemm_small_run(L.wq, kb.xf, B, kb.qkv, qkvw, err, st));
     IFX_TRY(gemm_small_run(L.wk, kb.xf, B, kb.qkv + Hh, qkvw, err, st));
     IFX_TRY(gemm_small_run(L.wv, kb.xf, B, kb.qkv + Hh + G * hd, qkvw, err, st));
@@ -1095,18 +1127,18 @@ ifx_status Model::enqueue_decode_batch(KvBatch &kb, cudaStream_t st, int n, cons
     a.batch = B;
     a.slot = slot_dev;
     IFX_TRY(decode_attention(a, st, false));
-    IFX_TRY(gemm_small_stage_x(kb.attn, nullptr, nullptr, 0.f, GX_PLAIN, B, Hh, kb.xf, st));
+    IFX_TRY(stage_small(kb.attn, nullptr, nullptr, 0.f, GX_PLAIN, B, Hh, kb.xf, st));
     IFX_TRY(gemm_small_run(L.wo, kb.xf, B, kb.x, D, err, st));  // x += attn Wo^T
     IFX_CUDA(cudaMemsetAsync(kb.gate, 0, sizeof(float) * (size_t)B * F, st));
     IFX_CUDA(cudaMemsetAsync(kb.up, 0, sizeof(float) * (size_t)B * F, st));
-    IFX_TRY(gemm_small_stage_x(kb.x, nullptr, L.ffn_norm, eps, GX_RMSNORM, B, D, kb.xf, st));
+    IFX_TRY(stage_small(kb.x, nullptr, L.ffn_norm, eps, GX_RMSNORM, B, D, kb.xf, st));
     IFX_TRY(gemm_small_run(L.w1, kb.xf, B, kb.gate, F, err, st));
     IFX_TRY(gemm_small_run(L.w3, kb.xf, B, kb.up, F, err, st));
-    IFX_TRY(gemm_small_stage_x(kb.gate, kb.up, nullptr, 0.f, GX_SWIGLU, B, F, kb.xf, st));
+    IFX_TRY(stage_small(kb.gate, kb.up, nullptr, 0.f, GX_SWIGLU, B, F, kb.xf, st));
     IFX_TRY(gemm_small_run(L.w2, kb.xf, B, kb.x, D, err, st));  // x += swiglu W2^T
   }
   IFX_CUDA(cudaMemsetAsync(kb.logits, 0, sizeof(float) * (size_t)B * V, st));
-  IFX_TRY(gemm_small_stage_x(kb.x, nullptr, out_norm, eps, GX_RMSNORM, B, D, kb.xf, st));
+  IFX_TRY(stage_small(kb.x, nullptr, out_norm, eps, GX_RMSNORM, B, D, kb.xf, st));
   IFX_TRY(gemm_small_run(out_w, kb.xf, B, kb.logits, V, err, st));
   IFX_CUDA(cudaMemsetAsync(kb.keys, 0, sizeof(unsigned long long) * (size_t)B, st));
   argmax_rows_kernel<<<dim3((unsigned)B, kArgmaxParts), 256, 0, st>>>(kb.logits, V, kb.keys);
@@ -1277,7 +1309,7 @@ ifx_status Model::run_prompt(KvCache *kvp, const uint32_t *ids, size_t n, float 
   const int pos0 = opts.rope_compat ? 0 : start;  // forward.rs:243-244 ignores cache_start
   for (uint64_t l = 0; l < c.n_layers; ++l) {
     Layer &L = layers[l];
-    IFX_TRY(gemm_stage_x(w_x, nullptr, L.attn_norm, c.norm_eps, GX_RMSNORM, N, D, w_xf, st));
+    IFX_TRY(stage_rows(w_x, nullptr, L.attn_norm, c.norm_eps, GX_RMSNORM, N, D, w_xf, st));
     {  // Wq, Wk, Wv over one staged input
       const QMatrix *ws[3] = {&L.wq, &L.wk, &L.wv};
       float *cs[3] = {w_q, w_k, w_v};
@@ -1301,7 +1333,7 @@ ifx_status Model::run_prompt(KvCache *kvp, const uint32_t *ids, size_t n, float 
     }
     PrefillAttnArgs pa{w_q, w_k, w_v, w_attn, (int)n, H, G, hd, kvp ? 1 : 0};
     IFX_TRY(prefill_attention(pa, st));
-    IFX_TRY(gemm_stage_x(w_attn, nullptr, nullptr, 0.f, GX_PLAIN, N, Hh, w_xf, st));
+    IFX_TRY(stage_rows(w_attn, nullptr, nullptr, 0.f, GX_PLAIN, N, Hh, w_xf, st));
     if (tp > 1) {
       IFX_TRY(tp_partial_begin((size_t)N * D, st, w_y, w_x));
       IFX_TRY(gemm_run(L.wo, w_xf, N, w_y, D, 1, err, st));
@@ -1309,14 +1341,14 @@ ifx_status Model::run_prompt(KvCache *kvp, const uint32_t *ids, size_t n, float 
     } else {
       IFX_TRY(gemm_run(L.wo, w_xf, N, w_x, D, 1, err, st));
     }
-    IFX_TRY(gemm_stage_x(w_x, nullptr, L.ffn_norm, c.norm_eps, GX_RMSNORM, N, D, w_xf, st));
+    IFX_TRY(stage_rows(w_x, nullptr, L.ffn_norm, c.norm_eps, GX_RMSNORM, N, D, w_xf, st));
     {  // W1, W3 over one staged input
       const QMatrix *ws[2] = {&L.w1, &L.w3};
       float *cs[2] = {w_gate, w_up};
       const int64_t ls[2] = {F, F};
       IFX_TRY(gemm_run_multi(ws, cs, ls, 2, w_xf, N, 0, err, st));
     }
-    IFX_TRY(gemm_stage_x(w_gate, w_up, nullptr, 0.f, GX_SWIGLU, N, F, w_xf, st));
+    IFX_TRY(stage_rows(w_gate, w_up, nullptr, 0.f, GX_SWIGLU, N, F, w_xf, st));
     if (tp > 1) {
       IFX_TRY(tp_partial_begin((size_t)N * D, st, w_y, w_x));
       IFX_TRY(gemm_run(L.w2, w_xf, N, w_y, D, 1, err, st));
@@ -1351,7 +1383,7 @@ ifx_status Model::run_prompt(KvCache *kvp, const uint32_t *ids, size_t n, float 
       IFX_CUDA(cudaMalloc(&logits_all, need * sizeof(float)));
       logits_all_n = need;
     }
-    IFX_TRY(gemm_stage_x(w_x, nullptr, out_norm, c.norm_eps, GX_RMSNORM, N, D, w_xf, st));
+    IFX_TRY(stage_rows(w_x, nullptr, out_norm, c.norm_eps, GX_RMSNORM, N, D, w_xf, st));
     if (tp > 1) {
       // [n][Vl] per rank, gathered rank-major, then interleaved to [n][V]
       const size_t loc = n * Vl;

@@ -149,6 +149,15 @@ struct Model {
   // gather_logits: under tensor parallelism, also gather the vocab slices
   // into logits (the persistent kernel leaves each rank's slice only)
   ifx_status run_decode(KvCache &kv, bool gather_logits = true);
+  // dense f32 matmul weights (a checkpoint with F32 / F16 / Q8_K matrices):
+  // every matrix is kept dequantised and the dense kernels of dense.cu run
+  bool dense = false;
+  // f(X) staging for the GEMMs: the fused kernels' fragment formats, or the
+  // plain f32 rows of the dense path
+  ifx_status stage_rows(const float *X, const float *X2, const float *normw, float eps, int mode,
+                        int64_t M, int64_t K, void *buf, cudaStream_t st);
+  ifx_status stage_small(const float *X, const float *X2, const float *normw, float eps, int mode,
+                         int64_t M, int64_t K, void *buf, cudaStream_t st);
   ifx_status decode_step(KvCache &kv, uint32_t token, float *logits_host);
   ifx_status prefill(KvCache &kv, const uint32_t *ids, size_t n, float *logits_host, int last_row_only);
   ifx_status forward(const uint32_t *ids, size_t n, float *logits_host, int last_row_only);

@@ -41,6 +41,7 @@ struct QLayout {
   int unit_bytes = 0;
   uint64_t total_bytes = 0;
   int q6_s8 = 0;     // Q6_K scale bytes are int8 (llama.cpp), not u8
+  int dense = 0;     // row-major f32 (dequantised F32 / F16 / Q8_K), not units
 };
 
 // Largest unit that still fits the GEMV's shared-memory stage.

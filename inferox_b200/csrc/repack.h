@@ -13,6 +13,7 @@ struct QMatrix {
   // Quantised bytes of the original GGUF blocks for this matrix (what a
   // decode step must stream from HBM).
   uint64_t gguf_bytes() const {
+    if (L.dense) return L.total_bytes;  // streamed as f32
     BlockInfo b = block_info(L.type);
     return (uint64_t)(L.rows * L.cols / b.elems) * b.bytes;
   }
