@@ -121,7 +121,9 @@ typedef struct ifx_kv ifx_kv;
 
 /* Model::open (src/model/mod.rs:64-92): parse the GGUF (file.rs:57-116),
  * read the config, wire blk.{i}.* tensors, then upload and repack every
- * weight once (the per-call dequant of weights.rs:66-74 disappears). */
+ * weight once (the per-call dequant of weights.rs:66-74 disappears). A file
+ * with any F32, F16 or Q8_K matmul weight loads every matmul weight
+ * dequantised to f32 and runs the dense kernels (no persistent decode). */
 ifx_status ifx_model_load(const char *path, const ifx_load_opts *opts,
                           ifx_model **out);
 /* Same, from a GGUF image already in host memory (no file). */
@@ -261,8 +263,10 @@ ifx_status ifx_op_matmul(const float *a, const float *b, float *c, size_t m,
 ifx_status ifx_op_matmul_t(const float *a, const float *b, float *c, size_t m,
                            size_t n, size_t k, void *stream);
 
-/* A quantised weight matrix [rows, cols] uploaded and repacked for the fused
- * kernels. Replaces tensor_f32_by_index's dequant (weights.rs:66-74). */
+/* A weight matrix [rows, cols] uploaded for the matmul kernels. Replaces
+ * tensor_f32_by_index's dequant (weights.rs:66-74). Q4_0, Q8_0, Q4_K and
+ * Q6_K are repacked for the fused dequant kernels; F32, F16 and Q8_K are
+ * dequantised once to f32 (dequant.rs:10-52, 201-232) for the dense ones. */
 typedef struct ifx_qmatrix ifx_qmatrix;
 ifx_status ifx_qmatrix_create(int type, const void *gguf_bytes_host,
                               size_t nbytes, size_t rows, size_t cols,
