@@ -1050,6 +1050,244 @@ __global__ void __launch_bounds__(128) prefill_attn_tc_kernel(PrefillAttnArgs a)
   }
 }
 
+// Causal prefill attention streamed from the KV cache: a CTA takes one kv
+// head and 16 RT query rows of every one of its query heads (8 warps: warp
+// w = head w / RT, row tile w % RT), so each 64-key tile of K and V is
+// fetched once for all of them, as f16 rows bulk-copied from the cache the
+// chunk was just written to (double-buffered; thread 0 refills a stage
+// once all eight warps have released it). Per tile and warp: S = Q K^T
+// (mma.m16n8k16, K from ldmatrix on the position-swizzled rows), the causal
+// chunk mask (key <= row, forward.rs:266-274), an online softmax in
+// registers, O += P V with P re-used from the S fragments and V from
+// ldmatrix.trans. Q and P are single f16 planes and accumulation is f32, as
+// in prefill_attn_tc_kernel.
+constexpr int kPFK = 64;  // keys per tile
+
+template <int HD>
+__host__ __device__ constexpr int pflash_smem_bytes() {
+  return 2 * 2 * kPFK * HD * 2 + 4 * 8;
+}
+
+template <int HD, int RT>
+__global__ void __launch_bounds__(256, 1) prefill_attn_flash_kernel(const __grid_constant__ PrefillAttnArgs a) {
+  constexpr int KSTEPS = HD / 16, NDT = HD / 8, TH = kPFK * HD;
+  extern __shared__ __align__(128) uint8_t smraw[];
+  __half *stage = reinterpret_cast<__half *>(smraw);                // [2][K | V][64][HD]
+  uint64_t *full = reinterpret_cast<uint64_t *>(stage + 2 * 2 * TH);  // [2]
+  uint64_t *empty = full + 2;                                       // [2]
+  const int h = blockIdx.x, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int g = lane >> 2, c = lane & 3;
+  const int grp = a.H / a.G;
+  const int j = warp / RT, rt = warp % RT;   // query head (within the group), row tile
+  const bool active = j < grp;
+  const int hq = h * grp + (active ? j : 0);
+  const int r0 = blockIdx.y * 16 * RT;        // the CTA's first query row
+  const int row_a = r0 + rt * 16 + g, row_b = row_a + 8;
+  const int qstride = a.H * HD;
+  const int kend = min(a.n, r0 + 16 * RT);    // keys this CTA needs (causal)
+  const int ntile = (kend + kPFK - 1) / kPFK;
+  auto row_off = [&](int p) -> size_t {       // absolute position p of this kv head
+    if (a.page_table)
+      return (size_t)a.page_table[p / a.page_rows] * a.page_stride +
+             ((size_t)h * a.page_rows + p % a.page_rows) * HD;
+    return ((size_t)h * a.max_seq + p) * HD;
+  };
+  // tile i: keys [64 i, min(64 i + 64, kend)), positions start + key; a
+  // paged tile splits where a page ends
+  auto issue = [&](int i) {
+    const int st = i & 1, k0 = i * kPFK, nk = min(kPFK, kend - k0);
+    __half *dk = stage + (size_t)st * 2 * TH;
+    mbar_arrive_expect_tx(&full[st], 2u * (uint32_t)nk * HD * 2u);
+    int r = 0;
+    while (r < nk) {
+      const int p = a.start + k0 + r;
+      int run = nk - r;
+      if (a.page_table) run = min(run, a.page_rows - p % a.page_rows);
+      const size_t off = row_off(p);
+      bulk_g2s(dk + (size_t)r * HD, a.kc + off, (uint32_t)run * HD * 2u, &full[st]);
+      bulk_g2s(dk + TH + (size_t)r * HD, a.vc + off, (uint32_t)run * HD * 2u, &full[st]);
+      r += run;
+    }
+  };
+  // Rows of a short last tile are never copied: start every stage at zero so
+  // such a row holds zeros or an earlier tile's finite values (its P is 0,
+  // and 0 times a NaN pattern would not be). The bulk copies write after the
+  // proxy fence.
+  for (int e = tid; e < 2 * 2 * TH / 8; e += 256) reinterpret_cast<uint4 *>(stage)[e] = make_uint4(0u, 0u, 0u, 0u);
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  __syncthreads();
+  int issued = 0;  // thread 0: tiles issued
+  if (tid == 0) {
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 8);
+    }
+    fence_mbar_init();
+    issue(0);
+    issued = 1;
+    if (ntile > 1) {
+      issue(1);
+      issued = 2;
+    }
+  }
+  // this warp's 16 query rows as A fragments (single f16 plane)
+  uint32_t qa[KSTEPS][4];
+  {
+    const bool va = active && row_a < a.n, vb = active && row_b < a.n;
+    const float *qra = a.q + (size_t)(va ? row_a : 0) * qstride + hq * HD;
+    const float *qrb = a.q + (size_t)(vb ? row_b : 0) * qstride + hq * HD;
+#pragma unroll
+    for (int ks = 0; ks < KSTEPS; ++ks) {
+      const int d0 = ks * 16 + 2 * c;
+      const float2 x0 = va ? *reinterpret_cast<const float2 *>(qra + d0) : make_float2(0.f, 0.f);
+      const float2 x1 = vb ? *reinterpret_cast<const float2 *>(qrb + d0) : make_float2(0.f, 0.f);
+      const float2 x2 = va ? *reinterpret_cast<const float2 *>(qra + d0 + 8) : make_float2(0.f, 0.f);
+      const float2 x3 = vb ? *reinterpret_cast<const float2 *>(qrb + d0 + 8) : make_float2(0.f, 0.f);
+      qa[ks][0] = pack_h2(x0.x, x0.y);
+      qa[ks][1] = pack_h2(x1.x, x1.y);
+      qa[ks][2] = pack_h2(x2.x, x2.y);
+      qa[ks][3] = pack_h2(x3.x, x3.y);
+    }
+  }
+  __syncthreads();  // the barriers are initialised
+  float o[NDT][4];
+#pragma unroll
+  for (int nt = 0; nt < NDT; ++nt) o[nt][0] = o[nt][1] = o[nt][2] = o[nt][3] = 0.f;
+  float m_a = -INFINITY, m_b = -INFINITY, l_a = 0.f, l_b = 0.f;
+  const float scale = 1.0f / sqrtf((float)HD);
+  const int krow = (lane & 7) + 8 * (lane >> 4), kch = (lane >> 3) & 1;
+  const int vrow = (lane & 7) + 8 * ((lane >> 3) & 1), vch = lane >> 4;
+  bool ok = true;
+  int waited = 0;
+  for (int i = 0; i < ntile; ++i) {
+    const int st = i & 1, k0 = i * kPFK;
+    ok = __all_sync(0xffffffffu, mbar_wait(&full[st], (uint32_t)(i >> 1) & 1u, a.err, 307));
+    if (!ok) break;
+    waited = i + 1;
+    const __half *Ks = stage + (size_t)st * 2 * TH, *Vs = Ks + TH;
+    const int sw = a.start + k0;  // swizzle key of smem row r: (sw + r) & 7
+    float sv[kPFK / 8][4];
+#pragma unroll
+    for (int nt2 = 0; nt2 < kPFK / 16; ++nt2) {  // key n-tiles 2 nt2, 2 nt2 + 1
+      float s0[4] = {0.f, 0.f, 0.f, 0.f}, s1[4] = {0.f, 0.f, 0.f, 0.f};
+      const int r = 16 * nt2 + krow;
+#pragma unroll
+      for (int ks = 0; ks < KSTEPS; ++ks) {
+        uint32_t kb[4];
+        ldsm_x4(kb, smem_u32(Ks + r * HD + (((2 * ks + kch) ^ ((sw + r) & 7)) << 3)));
+        mma_16816(s0, qa[ks][0], qa[ks][1], qa[ks][2], qa[ks][3], kb[0], kb[1], s0);
+        mma_16816(s1, qa[ks][0], qa[ks][1], qa[ks][2], qa[ks][3], kb[2], kb[3], s1);
+      }
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        sv[2 * nt2][e] = s0[e];
+        sv[2 * nt2 + 1][e] = s1[e];
+      }
+    }
+    float mx_a = -INFINITY, mx_b = -INFINITY;
+#pragma unroll
+    for (int nt = 0; nt < kPFK / 8; ++nt)
+#pragma unroll
+      for (int jj = 0; jj < 2; ++jj) {
+        const int key = k0 + nt * 8 + 2 * c + jj;
+        const bool kin = key < kend;
+        sv[nt][jj] = (kin && key <= row_a) ? sv[nt][jj] * scale : -INFINITY;
+        sv[nt][2 + jj] = (kin && key <= row_b) ? sv[nt][2 + jj] * scale : -INFINITY;
+        mx_a = fmaxf(mx_a, sv[nt][jj]);
+        mx_b = fmaxf(mx_b, sv[nt][2 + jj]);
+      }
+    mx_a = fmaxf(mx_a, __shfl_xor_sync(0xffffffffu, mx_a, 1));
+    mx_a = fmaxf(mx_a, __shfl_xor_sync(0xffffffffu, mx_a, 2));
+    mx_b = fmaxf(mx_b, __shfl_xor_sync(0xffffffffu, mx_b, 1));
+    mx_b = fmaxf(mx_b, __shfl_xor_sync(0xffffffffu, mx_b, 2));
+    const float mn_a = fmaxf(m_a, mx_a), mn_b = fmaxf(m_b, mx_b);
+    const float al_a = mn_a == -INFINITY ? 1.f : expf(m_a - mn_a);
+    const float al_b = mn_b == -INFINITY ? 1.f : expf(m_b - mn_b);
+    m_a = mn_a;
+    m_b = mn_b;
+    l_a *= al_a;
+    l_b *= al_b;
+#pragma unroll
+    for (int nt = 0; nt < NDT; ++nt) {
+      o[nt][0] *= al_a;
+      o[nt][1] *= al_a;
+      o[nt][2] *= al_b;
+      o[nt][3] *= al_b;
+    }
+#pragma unroll
+    for (int nt = 0; nt < kPFK / 8; ++nt)
+#pragma unroll
+      for (int jj = 0; jj < 2; ++jj) {
+        const float pa = sv[nt][jj] == -INFINITY ? 0.f : expf(sv[nt][jj] - mn_a);
+        const float pb = sv[nt][2 + jj] == -INFINITY ? 0.f : expf(sv[nt][2 + jj] - mn_b);
+        sv[nt][jj] = pa;
+        sv[nt][2 + jj] = pb;
+        l_a += pa;
+        l_b += pb;
+      }
+#pragma unroll
+    for (int k2 = 0; k2 < kPFK / 16; ++k2) {
+      const uint32_t p0 = pack_h2(sv[2 * k2][0], sv[2 * k2][1]);
+      const uint32_t p1 = pack_h2(sv[2 * k2][2], sv[2 * k2][3]);
+      const uint32_t p2 = pack_h2(sv[2 * k2 + 1][0], sv[2 * k2 + 1][1]);
+      const uint32_t p3 = pack_h2(sv[2 * k2 + 1][2], sv[2 * k2 + 1][3]);
+      const int r = 16 * k2 + vrow;
+#pragma unroll
+      for (int nd = 0; nd < NDT; nd += 2) {
+        uint32_t vb[4];
+        ldsm_x4_t(vb, smem_u32(Vs + r * HD + (((nd + vch) ^ ((sw + r) & 7)) << 3)));
+        mma_16816(o[nd], p0, p1, p2, p3, vb[0], vb[1], o[nd]);
+        mma_16816(o[nd + 1], p0, p1, p2, p3, vb[2], vb[3], o[nd + 1]);
+      }
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[st]);
+    if (tid == 0 && i + 2 < ntile) {  // refill this stage once every warp released it
+      if (!mbar_wait(&empty[st], (uint32_t)(i >> 1) & 1u, a.err, 308)) {
+        ok = false;
+      } else {
+        issue(i + 2);
+        issued = i + 3;
+      }
+    }
+  }
+  // no copy may outlive the CTA: thread 0 waits (bounded) for every issued
+  // tile that no warp waited for
+  if (tid == 0)
+    for (int i = waited; i < issued; ++i) mbar_wait(&full[i & 1], (uint32_t)(i >> 1) & 1u, nullptr, 0);
+  if (!active) return;
+  l_a += __shfl_xor_sync(0xffffffffu, l_a, 1);
+  l_a += __shfl_xor_sync(0xffffffffu, l_a, 2);
+  l_b += __shfl_xor_sync(0xffffffffu, l_b, 1);
+  l_b += __shfl_xor_sync(0xffffffffu, l_b, 2);
+  const float ia = 1.0f / l_a, ib = 1.0f / l_b;
+#pragma unroll
+  for (int nt = 0; nt < NDT; ++nt) {
+    const int d = nt * 8 + 2 * c;
+    if (row_a < a.n)
+      *reinterpret_cast<float2 *>(a.out + (size_t)row_a * qstride + hq * HD + d) =
+          make_float2(o[nt][0] * ia, o[nt][1] * ia);
+    if (row_b < a.n)
+      *reinterpret_cast<float2 *>(a.out + (size_t)row_b * qstride + hq * HD + d) =
+          make_float2(o[nt][2] * ib, o[nt][3] * ib);
+  }
+}
+
+template <int HD, int RT>
+static ifx_status launch_prefill_flash(const PrefillAttnArgs &a, cudaStream_t st) {
+  constexpr int smem = pflash_smem_bytes<HD>();
+  static bool attr = false;
+  if (!attr) {
+    IFX_CUDA(cudaFuncSetAttribute(prefill_attn_flash_kernel<HD, RT>,
+                                  cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    attr = true;
+  }
+  const dim3 grid((unsigned)a.G, (unsigned)((a.n + 16 * RT - 1) / (16 * RT)));
+  prefill_attn_flash_kernel<HD, RT><<<grid, 256, smem, st>>>(a);
+  IFX_CUDA(cudaGetLastError());
+  return IFX_OK;
+}
+
 template <int HD>
 static ifx_status launch_prefill_tc(const PrefillAttnArgs &a, cudaStream_t st) {
   const size_t smem = (size_t)(2 * kTK * (HD + 8)) * sizeof(__half);
@@ -1060,6 +1298,22 @@ static ifx_status launch_prefill_tc(const PrefillAttnArgs &a, cudaStream_t st) {
 }
 
 ifx_status prefill_attention(const PrefillAttnArgs &a, cudaStream_t st) {
+  // causal prefill into a cache: the streamed kernel (8 warps = the kv
+  // head's query heads x row tiles)
+  const int grp = a.G > 0 ? a.H / a.G : 0;
+  if (a.kc && a.causal && a.err && (a.hd == 64 || a.hd == 128) && grp > 0 && 8 % grp == 0) {
+    const int rt = 8 / grp;
+    if (a.hd == 128) {
+      if (rt == 1) return launch_prefill_flash<128, 1>(a, st);
+      if (rt == 2) return launch_prefill_flash<128, 2>(a, st);
+      if (rt == 4) return launch_prefill_flash<128, 4>(a, st);
+      return launch_prefill_flash<128, 8>(a, st);
+    }
+    if (rt == 1) return launch_prefill_flash<64, 1>(a, st);
+    if (rt == 2) return launch_prefill_flash<64, 2>(a, st);
+    if (rt == 4) return launch_prefill_flash<64, 4>(a, st);
+    return launch_prefill_flash<64, 8>(a, st);
+  }
   switch (a.hd) {  // tensor-core path for the common head sizes
     case 48: return launch_prefill_tc<48>(a, st);
     case 64: return launch_prefill_tc<64>(a, st);

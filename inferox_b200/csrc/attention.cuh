@@ -50,6 +50,17 @@ struct PrefillAttnArgs {
   float *out;       // [n][H*hd]
   int n, H, G, hd;
   int causal = 1;   // 0: every row attends to every key (Model::forward, forward.rs:100-150)
+  // when set (a causal prefill into a KV cache): this layer's cache, whose
+  // rows start .. start + n - 1 already hold the chunk's K/V (f16, columns
+  // swizzled by position); the streamed kernel reads its K/V tiles there.
+  // Paged caches as in DecodeAttnArgs (kc / vc at the layer's rows of page
+  // 0, page p of the sequence at page_table[p]).
+  const __half *kc = nullptr, *vc = nullptr;
+  int start = 0, max_seq = 0;
+  const int *page_table = nullptr;
+  int page_rows = 0;
+  int64_t page_stride = 0;
+  int *err = nullptr;
 };
 ifx_status prefill_attention(const PrefillAttnArgs &a, cudaStream_t st);
 

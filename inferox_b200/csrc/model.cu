@@ -635,6 +635,7 @@ ifx_status KvBatch::create(Model *model, size_t max_seq_len, int nseq, size_t pa
 
 KvBatch::~KvBatch() {
   if (dev >= 0) cudaSetDevice(dev);
+  if (graph) cudaGraphExecDestroy(graph);
   for (void *p : {(void *)k, (void *)v, (void *)pos, (void *)x, (void *)qkv, (void *)attn,
                   (void *)gate, (void *)up, (void *)logits, (void *)part_o, (void *)part_ml,
                   (void *)counters, (void *)xf, (void *)ids, (void *)out, (void *)keys,
@@ -1236,6 +1237,38 @@ ifx_status Model::reset_seq(KvBatch &kb, int seq) {
 
 // n greedy steps of every sequence, each step's argmax fed to the next on
 // the device; out[i * batch + b] is sequence b's token of step i.
+// One full-batch step with its argmax fed back as the next step's ids: a
+// CUDA graph replay once a first step has run eagerly (the launch sequence
+// does not change between steps: positions and page tables live on the
+// device, pages are reserved before the loop).
+ifx_status Model::step_batch_fed(KvBatch &kb, cudaStream_t st) {
+  auto enqueue = [&]() -> ifx_status {
+    IFX_TRY(enqueue_decode_batch(kb, st));
+    IFX_CUDA(cudaMemcpyAsync(kb.ids, kb.out, sizeof(uint32_t) * kb.batch, cudaMemcpyDeviceToDevice, st));
+    return IFX_OK;
+  };
+  if (!opts.use_graphs || !kb.warm) {
+    kb.warm = true;
+    return enqueue();
+  }
+  if (!kb.graph) {
+    cudaGraph_t g;
+    IFX_CUDA(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal));
+    ifx_status s = enqueue();
+    cudaError_t e = cudaStreamEndCapture(st, &g);
+    if (s != IFX_OK) return s;
+    if (e != cudaSuccess) return cuda_fail(e, "cudaStreamEndCapture");
+    e = cudaGraphInstantiate(&kb.graph, g, 0);
+    cudaGraphDestroy(g);
+    if (e != cudaSuccess) {
+      kb.graph = nullptr;
+      return cuda_fail(e, "cudaGraphInstantiate");
+    }
+  }
+  IFX_CUDA(cudaGraphLaunch(kb.graph, st));
+  return IFX_OK;
+}
+
 ifx_status Model::decode_greedy_batch(KvBatch &kb, const uint32_t *tokens, size_t n,
                                       uint32_t *out, float *device_ms) {
   NvtxRange nvtx_("ifx:decode_greedy_batch");
@@ -1259,10 +1292,7 @@ ifx_status Model::decode_greedy_batch(KvBatch &kb, const uint32_t *tokens, size_
   }
   ifx_status s = IFX_OK;
   for (size_t i = 0; i < n && s == IFX_OK; ++i) {
-    s = enqueue_decode_batch(kb, st);
-    if (s == IFX_OK)
-      s = cuda_ok(cudaMemcpyAsync(kb.ids, kb.out, sizeof(uint32_t) * kb.batch,
-                                  cudaMemcpyDeviceToDevice, st));
+    s = step_batch_fed(kb, st);
     if (s == IFX_OK)
       s = cuda_ok(cudaMemcpyAsync(toks + i * kb.batch, kb.out, sizeof(uint32_t) * kb.batch,
                                   cudaMemcpyDeviceToDevice, st));
@@ -1332,6 +1362,17 @@ ifx_status Model::run_prompt(KvCache *kvp, const uint32_t *ids, size_t n, float 
       IFX_CUDA(cudaGetLastError());
     }
     PrefillAttnArgs pa{w_q, w_k, w_v, w_attn, (int)n, H, G, hd, kvp ? 1 : 0};
+    if (kvp) {  // the chunk's K/V rows were just written to the cache: stream them from there
+      const KvCache &kv = *kvp;
+      pa.kc = kv.k + l * kv.per_layer;
+      pa.vc = kv.v + l * kv.per_layer;
+      pa.start = start;
+      pa.max_seq = (int)kv.max_seq;
+      pa.page_table = kv.page_table;
+      pa.page_rows = kv.page_rows;
+      pa.page_stride = kv.page_stride;
+      pa.err = err;
+    }
     IFX_TRY(prefill_attention(pa, st));
     IFX_TRY(stage_rows(w_attn, nullptr, nullptr, 0.f, GX_PLAIN, N, Hh, w_xf, st));
     if (tp > 1) {

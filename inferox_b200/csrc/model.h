@@ -79,6 +79,10 @@ struct KvBatch {
   int *table_dev = nullptr;                 // [batch][max_pages]
   std::vector<int> table;                   // host mirror
   std::vector<int> free_pages;              // pool pages no sequence holds
+  // the full-batch step (kernels + the argmax fed back as the next ids),
+  // captured after one eager step has run (first-call attribute setup)
+  cudaGraphExec_t graph = nullptr;
+  bool warm = false;
   ifx_status create(Model *model, size_t max_seq_len, int nseq, size_t pages = 0);
   // give sequence `seq` pages for positions [0, rows); fails with no change
   // when the pool runs out
@@ -149,6 +153,7 @@ struct Model {
   // gather_logits: under tensor parallelism, also gather the vocab slices
   // into logits (the persistent kernel leaves each rank's slice only)
   ifx_status run_decode(KvCache &kv, bool gather_logits = true);
+  ifx_status step_batch_fed(KvBatch &kb, cudaStream_t st);
   // dense f32 matmul weights (a checkpoint with F32 / F16 / Q8_K matrices):
   // every matrix is kept dequantised and the dense kernels of dense.cu run
   bool dense = false;
