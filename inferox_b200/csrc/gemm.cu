@@ -36,7 +36,17 @@ __device__ __forceinline__ float silu_g(float v) {
 constexpr int kStageCols = 256;  // 8 warps: one column per thread
 
 __global__ void stage_x_kernel(const float *X, const float *X2, const float *normw, float eps,
-                               int mode, int64_t M, int64_t K, int NT, __half *out) {
+                               int mode, int64_t M, int64_t K, int NT, __half *out, StageZero z) {
+  // launched with programmatic serialization: X is read after the previous
+  // grid completes; the next grid (a GEMM) may start fetching its weights
+  pdl_wait();
+  pdl_launch();
+  {  // buffers the following GEMMs accumulate into start at zero
+    const int64_t nb = (int64_t)gridDim.x * gridDim.y, b = (int64_t)blockIdx.y * gridDim.x + blockIdx.x;
+    for (int i = 0; i < 2; ++i)
+      if (z.p[i])
+        for (int64_t e = b * blockDim.x + threadIdx.x; e < z.n[i]; e += nb * blockDim.x) z.p[i][e] = 0.f;
+  }
   const int64_t t = blockIdx.x;  // token (row), may be >= M for padding
   const int64_t kbeg = (int64_t)blockIdx.y * kStageCols;
   const int64_t kend = std::min<int64_t>(K, kbeg + kStageCols);
@@ -110,6 +120,12 @@ __device__ __forceinline__ float s2f8(uint32_t v, uint32_t smask, float bias) {
 }
 __device__ __forceinline__ __half2 u2h(uint32_t u) { return *reinterpret_cast<__half2 *>(&u); }
 
+// Word i of v by selects (a dynamic index into a register array would go
+// through local memory).
+__device__ __forceinline__ uint32_t word4(const uint4 &v, int i) {
+  return i == 0 ? v.x : i == 1 ? v.y : i == 2 ? v.z : v.w;
+}
+
 // (v - sub) * scale + add with v the magic-biased f16 pair in `bits`.
 __device__ __forceinline__ uint32_t deq(uint32_t bits, __half2 sub, __half2 scale, __half2 add) {
   return h2u(__hfma2(__hsub2(u2h(bits), sub), scale, add));
@@ -148,24 +164,25 @@ __device__ __forceinline__ void gemm_unit_q4k(const uint8_t *wt, const uint8_t *
   const float dmA = h2f((uint16_t)prmt(hA.z, hA.w, 0x0073u));
   const float dB = h2f((uint16_t)prmt(hB.x, hB.y, 0x0073u)) * 0.0625f;
   const float dmB = h2f((uint16_t)prmt(hB.z, hB.w, 0x0073u));
-  const uint32_t *wq = reinterpret_cast<const uint32_t *>(wt);
+  const uint4 *wq4 = reinterpret_cast<const uint4 *>(wt);  // a lane's 4 chunks per 16 bytes
   float ua[2][NT][4];
 #pragma unroll
   for (int p = 0; p < 2; ++p)
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt) ua[p][nt][0] = ua[p][nt][1] = ua[p][nt][2] = ua[p][nt][3] = 0.f;
-  const uint32_t hw[2][4] = {{hA.x, hA.y, hA.z, hA.w}, {hB.x, hB.y, hB.z, hB.w}};
+  uint4 q4 = make_uint4(0u, 0u, 0u, 0u);
 #pragma unroll
   for (int gi = 0; gi < 8; ++gi) {
+    if ((gi & 1) == 0) q4 = wq4[(gi >> 1) * 32 + lane];  // chunks 2 gi .. 2 gi + 3 (conflict-free)
     const int sh = 6 * (gi & 1);
-    const uint32_t sa = (hw[0][gi >> 1] >> sh) & 63u, sb = (hw[1][gi >> 1] >> sh) & 63u;
+    const uint32_t sa = (word4(hA, gi >> 1) >> sh) & 63u, sb = (word4(hB, gi >> 1) >> sh) & 63u;
     const __half2 scA = __hsub2(u2h(0x64006400u | sa | (sa << 16)), b1024);  // exact
     const __half2 scB = __hsub2(u2h(0x64006400u | sb | (sb << 16)), b1024);
     const __half2 ngA = __hmul2(scA, m1024), ngB = __hmul2(scB, m1024);      // -1024 sc, exact
 #pragma unroll
     for (int cc = 0; cc < 2; ++cc) {
       const int ch = 2 * gi + cc;
-      const uint32_t wd = wq[((ch / 4) * 32 + lane) * 4 + ch % 4];
+      const uint32_t wd = word4(q4, ch & 3);
       const uint32_t hi = wd >> 8;
       const uint32_t a0 = h2u(__hfma2(u2h((wd & 0x000F000Fu) | 0x64006400u), scA, ngA));
       const uint32_t a1 = h2u(__hfma2(u2h((wd & 0x00F000F0u) | 0x64006400u), scB, ngB));
@@ -182,7 +199,7 @@ __device__ __forceinline__ void gemm_unit_q4k(const uint8_t *wt, const uint8_t *
   }
   // mins: A row g = (m_2c, m_2c+1) of row g, row g+8 the same of row g+8
   // (k = group, groups 8-15 absent); B = (S_2c, S_2c+1) of token g as hi/lo
-  const uint32_t fA = hw[0][c], fB = hw[1][c];
+  const uint32_t fA = word4(hA, c), fB = word4(hB, c);
   const uint32_t am0 = h2u(__hsub2(u2h(0x64006400u | ((fA >> 12) & 63u) | (((fA >> 18) & 63u) << 16)), b1024));
   const uint32_t am1 = h2u(__hsub2(u2h(0x64006400u | ((fB >> 12) & 63u) | (((fB >> 18) & 63u) << 16)), b1024));
 #pragma unroll
@@ -201,53 +218,48 @@ __device__ __forceinline__ void gemm_unit_q4k(const uint8_t *wt, const uint8_t *
   }
 }
 
+// Q6_K, Q4_0 and Q8_0 units (Q4_K: gemm_unit_q4k). Weight words are read
+// 16 bytes per lane (a lane's words of four 16-column chunks: conflict-free)
+// in blocks of four chunks; each scale group's MMAs go into `tmp`, which
+// the group's f32 scale then adds into `acc`.
 template <int TYPE, int NT>
 __device__ __forceinline__ void gemm_unit(const uint8_t *wt, const uint8_t *xs, const float *sx,
                                           int kc, int wt_qbytes, uint32_t smask, int lane,
                                           float (&acc)[NT][4]) {
-  const int g = lane >> 2, c = lane & 3;
+  const int g = lane >> 2;
   // chunks per scale group: Q6_K scales every 16 columns, the others every 32
   constexpr int cpg = (TYPE == IFX_TYPE_Q6_K) ? 1 : 2;
-  const int ngr = kc / 16 / cpg;
-  const __half2 b1024 = __float2half2_rn(1024.f);
-  // per-row quantities shared by every group of the unit, read once: Q4_K
-  // d/dmin and the 16-byte row headers, Q6_K d
-  float dA = 0.f, dB = 0.f, dmA = 0.f, dmB = 0.f;
-  uint4 hA = make_uint4(0u, 0u, 0u, 0u), hB = hA;
-  if (TYPE == IFX_TYPE_Q4_K) {
-    hA = *reinterpret_cast<const uint4 *>(wt + 2048 + 16 * g);
-    hB = *reinterpret_cast<const uint4 *>(wt + 2048 + 16 * (g + 8));
-    dA = h2f((uint16_t)prmt(hA.x, hA.y, 0x0073u));
-    dmA = h2f((uint16_t)prmt(hA.z, hA.w, 0x0073u));
-    dB = h2f((uint16_t)prmt(hB.x, hB.y, 0x0073u));
-    dmB = h2f((uint16_t)prmt(hB.z, hB.w, 0x0073u));
-  } else if (TYPE == IFX_TYPE_Q6_K) {
+  float dA = 0.f, dB = 0.f;
+  if (TYPE == IFX_TYPE_Q6_K) {
     dA = h2f(*reinterpret_cast<const uint16_t *>(wt + 3072 + 256 + 2 * g));
     dB = h2f(*reinterpret_cast<const uint16_t *>(wt + 3072 + 256 + 2 * (g + 8))) * 0.0625f;
   }
+  const uint4 *w4 = reinterpret_cast<const uint4 *>(wt);
+  float tmp[NT][4];
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt) tmp[nt][0] = tmp[nt][1] = tmp[nt][2] = tmp[nt][3] = 0.f;
+  const int nch = kc / 16;  // Q8_0 units may end in a partial block (kc 32, 96, 160)
 #pragma unroll 1
-  for (int gi = 0; gi < ngr; ++gi) {
-    float tmp[NT][4];
+  for (int cb = 0; cb < (nch + 3) / 4; ++cb) {
+    uint4 qa = make_uint4(0u, 0u, 0u, 0u), qb = qa, hw = qa;
+    if (TYPE == IFX_TYPE_Q8_0) {  // a lane's 16 bytes hold two chunks
+      qa = w4[(2 * cb) * 32 + lane];
+      if (4 * cb + 2 < nch) qb = w4[(2 * cb + 1) * 32 + lane];
+    } else {
+      qa = w4[cb * 32 + lane];
+    }
+    if (TYPE == IFX_TYPE_Q6_K) hw = reinterpret_cast<const uint4 *>(wt + 2048)[(cb >> 1) * 32 + lane];
 #pragma unroll
-    for (int nt = 0; nt < NT; ++nt) tmp[nt][0] = tmp[nt][1] = tmp[nt][2] = tmp[nt][3] = 0.f;
-#pragma unroll
-    for (int cc = 0; cc < cpg; ++cc) {
-      const int ch = gi * cpg + cc;
+    for (int j = 0; j < 4; ++j) {
+      const int ch = 4 * cb + j;
+      if (ch >= nch) break;
       // exact integer A fragments; rows g+8 come from the high nibble and
-      // carry a factor 16 (Q4_K, Q6_K, Q4_0), folded into their scale below
+      // carry a factor 16 (Q6_K, Q4_0), folded into their scale below
       uint32_t a[4];
-      if (TYPE == IFX_TYPE_Q4_K) {
-        const uint32_t wd = reinterpret_cast<const uint32_t *>(wt)[((ch / 4) * 32 + lane) * 4 + ch % 4];
-        const uint32_t hi = wd >> 8;
-        a[0] = h2u(__hsub2(u2h((wd & 0x000F000Fu) | 0x64006400u), b1024));
-        a[1] = h2u(__hsub2(u2h((wd & 0x00F000F0u) | 0x64006400u), b1024));
-        a[2] = h2u(__hsub2(u2h((hi & 0x000F000Fu) | 0x64006400u), b1024));
-        a[3] = h2u(__hsub2(u2h((hi & 0x00F000F0u) | 0x64006400u), b1024));
-      } else if (TYPE == IFX_TYPE_Q6_K) {
-        const uint32_t wd = reinterpret_cast<const uint32_t *>(wt)[((ch / 4) * 32 + lane) * 4 + ch % 4];
-        const int t = ch / 2;
-        uint32_t H = reinterpret_cast<const uint32_t *>(wt + 2048)[((t / 4) * 32 + lane) * 4 + t % 4];
-        if (ch & 1) H >>= 8;
+      if (TYPE == IFX_TYPE_Q6_K) {
+        const uint32_t wd = word4(qa, j);
+        uint32_t H = word4(hw, 2 * (cb & 1) + (j >> 1));
+        if (j & 1) H >>= 8;
         const __half2 sub0 = __float2half2_rn(1056.f), sub1 = __float2half2_rn(1536.f);
         const uint32_t hi = wd >> 8, H4 = H >> 4;
         a[0] = h2u(__hsub2(u2h((wd & 0x000F000Fu) | ((H & 0x00030003u) << 4) | 0x64006400u), sub0));
@@ -255,7 +267,7 @@ __device__ __forceinline__ void gemm_unit(const uint8_t *wt, const uint8_t *xs, 
         a[2] = h2u(__hsub2(u2h((hi & 0x000F000Fu) | ((H4 & 0x00030003u) << 4) | 0x64006400u), sub0));
         a[3] = h2u(__hsub2(u2h((hi & 0x00F000F0u) | ((H4 & 0x000C000Cu) << 6) | 0x64006400u), sub1));
       } else if (TYPE == IFX_TYPE_Q4_0) {
-        const uint32_t wd = reinterpret_cast<const uint32_t *>(wt)[((ch / 4) * 32 + lane) * 4 + ch % 4];
+        const uint32_t wd = word4(qa, j);
         const __half2 sub0 = __float2half2_rn(1032.f), sub1 = __float2half2_rn(1152.f);
         const uint32_t hi = wd >> 8;
         a[0] = h2u(__hsub2(u2h((wd & 0x000F000Fu) | 0x64006400u), sub0));
@@ -263,12 +275,13 @@ __device__ __forceinline__ void gemm_unit(const uint8_t *wt, const uint8_t *xs, 
         a[2] = h2u(__hsub2(u2h((hi & 0x000F000Fu) | 0x64006400u), sub0));
         a[3] = h2u(__hsub2(u2h((hi & 0x00F000F0u) | 0x64006400u), sub1));
       } else {  // Q8_0: bytes q + 128
-        const uint2 w2 = reinterpret_cast<const uint2 *>(wt)[((ch / 2) * 32 + lane) * 2 + ch % 2];
+        const uint4 &q = (j < 2) ? qa : qb;
+        const uint32_t w0 = (j & 1) ? q.z : q.x, w1 = (j & 1) ? q.w : q.y;
         const __half2 sub = __float2half2_rn(1152.f);
-        a[0] = h2u(__hsub2(u2h(prmt(w2.x, 0x64646464u, 0x4140u)), sub));
-        a[1] = h2u(__hsub2(u2h(prmt(w2.x, 0x64646464u, 0x4342u)), sub));
-        a[2] = h2u(__hsub2(u2h(prmt(w2.y, 0x64646464u, 0x4140u)), sub));
-        a[3] = h2u(__hsub2(u2h(prmt(w2.y, 0x64646464u, 0x4342u)), sub));
+        a[0] = h2u(__hsub2(u2h(prmt(w0, 0x64646464u, 0x4140u)), sub));
+        a[1] = h2u(__hsub2(u2h(prmt(w0, 0x64646464u, 0x4342u)), sub));
+        a[2] = h2u(__hsub2(u2h(prmt(w1, 0x64646464u, 0x4140u)), sub));
+        a[3] = h2u(__hsub2(u2h(prmt(w1, 0x64646464u, 0x4342u)), sub));
       }
       const uint2 *xb = reinterpret_cast<const uint2 *>(xs + (size_t)ch * xchunk_bytes(NT)) + lane;
 #pragma unroll
@@ -277,46 +290,28 @@ __device__ __forceinline__ void gemm_unit(const uint8_t *wt, const uint8_t *xs, 
         mma_16816(tmp[nt], a[0], a[1], a[2], a[3], bh.x, bh.y, tmp[nt]);
         mma_16816(tmp[nt], a[0], a[1], a[2], a[3], bl.x, bl.y, tmp[nt]);
       }
-    }
-    // this group's scales for rows g (sA) and g+8 (sB), f32
-    float sA, sB, mA = 0.f, mB = 0.f;
-    if (TYPE == IFX_TYPE_Q4_K) {
-      // repacked header (repack.cu): word c' = the 6-bit fields of groups
-      // (2c', 2c'+1) | byte c' of (d, dmin) << 24
-      const int wsel = gi >> 1, sh = 6 * (gi & 1);
-      const uint32_t fA = wsel == 0 ? hA.x : wsel == 1 ? hA.y : wsel == 2 ? hA.z : hA.w;
-      const uint32_t fB = wsel == 0 ? hB.x : wsel == 1 ? hB.y : wsel == 2 ? hB.z : hB.w;
-      sA = dA * u2f6(fA >> sh);
-      sB = dB * u2f6(fB >> sh) * 0.0625f;
-      mA = dmA * u2f6(fA >> (12 + sh));
-      mB = dmB * u2f6(fB >> (12 + sh));
-    } else if (TYPE == IFX_TYPE_Q6_K) {
-      const uint8_t *scb = wt + 3072;
-      const float sbias = 8388608.0f + (float)smask;
-      sA = dA * s2f8(scb[16 * g + gi], smask, sbias);
-      sB = dB * s2f8(scb[16 * (g + 8) + gi], smask, sbias);
-    } else {
-      const int nb = kc / 32;
-      sA = h2f(*reinterpret_cast<const uint16_t *>(wt + wt_qbytes + (g * nb + gi) * 2));
-      sB = h2f(*reinterpret_cast<const uint16_t *>(wt + wt_qbytes + ((g + 8) * nb + gi) * 2));
-      if (TYPE == IFX_TYPE_Q4_0) sB *= 0.0625f;
-    }
-#pragma unroll
-    for (int nt = 0; nt < NT; ++nt) {
-      acc[nt][0] = fmaf(sA, tmp[nt][0], acc[nt][0]);
-      acc[nt][1] = fmaf(sA, tmp[nt][1], acc[nt][1]);
-      acc[nt][2] = fmaf(sB, tmp[nt][2], acc[nt][2]);
-      acc[nt][3] = fmaf(sB, tmp[nt][3], acc[nt][3]);
-    }
-    if (TYPE == IFX_TYPE_Q4_K) {  // - dmin * min * sum_k x_k over the group, per token
-      const float *sg = sx + gi * (8 * NT) + 2 * c;
+      if ((j + 1) % cpg) continue;
+      // the group ends: its scales for rows g (sA) and g+8 (sB), f32
+      const int gi = ch / cpg;
+      float sA, sB;
+      if (TYPE == IFX_TYPE_Q6_K) {
+        const uint8_t *scb = wt + 3072;
+        const float sbias = 8388608.0f + (float)smask;
+        sA = dA * s2f8(scb[16 * g + gi], smask, sbias);
+        sB = dB * s2f8(scb[16 * (g + 8) + gi], smask, sbias);
+      } else {
+        const int nb = kc / 32;
+        sA = h2f(*reinterpret_cast<const uint16_t *>(wt + wt_qbytes + (g * nb + gi) * 2));
+        sB = h2f(*reinterpret_cast<const uint16_t *>(wt + wt_qbytes + ((g + 8) * nb + gi) * 2));
+        if (TYPE == IFX_TYPE_Q4_0) sB *= 0.0625f;
+      }
 #pragma unroll
       for (int nt = 0; nt < NT; ++nt) {
-        const float2 xs2 = *reinterpret_cast<const float2 *>(sg + nt * 8);
-        acc[nt][0] = fmaf(-mA, xs2.x, acc[nt][0]);
-        acc[nt][1] = fmaf(-mA, xs2.y, acc[nt][1]);
-        acc[nt][2] = fmaf(-mB, xs2.x, acc[nt][2]);
-        acc[nt][3] = fmaf(-mB, xs2.y, acc[nt][3]);
+        acc[nt][0] = fmaf(sA, tmp[nt][0], acc[nt][0]);
+        acc[nt][1] = fmaf(sA, tmp[nt][1], acc[nt][1]);
+        acc[nt][2] = fmaf(sB, tmp[nt][2], acc[nt][2]);
+        acc[nt][3] = fmaf(sB, tmp[nt][3], acc[nt][3]);
+        tmp[nt][0] = tmp[nt][1] = tmp[nt][2] = tmp[nt][3] = 0.f;
       }
     }
   }
@@ -349,29 +344,44 @@ __global__ void __launch_bounds__(kGThreads, NT <= 2 ? 3 : 1) gemm_kernel(const 
   }
   __syncthreads();
 
+  // programmatic serialization: the next grid may start its weight fetch;
+  // this grid's weights do not depend on the previous grid, its staged
+  // activations do (read after griddepcontrol.wait)
+  pdl_launch();
   if (warp == 8) {
     if (lane == 0) {
+      auto xcopy = [&](int i) {
+        const int st = i % kGStages, u = u0 + i;
+        uint8_t *dst = ring + (size_t)st * stage_bytes;
+        const uint8_t *xsrc =
+            a.x + ((size_t)mb * a.nch_total + (size_t)u * (a.kc / 16)) * xchunk_bytes(NT);
+        const uint8_t *ssrc = reinterpret_cast<const uint8_t *>(
+            a.sums + ((size_t)mb * (a.nch_total / 2) + (size_t)u * (a.kc / 32)) * tokb);
+        bulk_g2s(dst + a.unit_bytes, xsrc, (uint32_t)xbytes, &full_bar[st]);
+        bulk_g2s(dst + a.unit_bytes + xbytes, ssrc, (uint32_t)sbytes, &full_bar[st]);
+      };
+      const int pre = min(n, kGStages);
       for (int i = 0; i < n; ++i) {
         const int st = i % kGStages;
         const uint32_t ph = (uint32_t)(i / kGStages) & 1u;
         if (i >= kGStages && !mbar_wait(&empty_bar[st], ph ^ 1u, a.err, 201)) break;
         uint8_t *dst = ring + (size_t)st * stage_bytes;
-        const int u = u0 + i;
-        const uint8_t *wsrc = a.w + ((size_t)ctile * a.kunits + u) * a.unit_bytes;
-        const uint8_t *xsrc =
-            a.x + ((size_t)mb * a.nch_total + (size_t)u * (a.kc / 16)) * xchunk_bytes(NT);
-        const uint8_t *ssrc = reinterpret_cast<const uint8_t *>(
-            a.sums + ((size_t)mb * (a.nch_total / 2) + (size_t)u * (a.kc / 32)) * tokb);
+        const uint8_t *wsrc = a.w + ((size_t)ctile * a.kunits + u0 + i) * a.unit_bytes;
         mbar_arrive_expect_tx(&full_bar[st], (uint32_t)stage_bytes);
         bulk_g2s(dst, wsrc, (uint32_t)a.unit_bytes, &full_bar[st]);
-        bulk_g2s(dst + a.unit_bytes, xsrc, (uint32_t)xbytes, &full_bar[st]);
-        bulk_g2s(dst + a.unit_bytes + xbytes, ssrc, (uint32_t)sbytes, &full_bar[st]);
+        if (i + 1 == pre) {  // the first stages' weights are on their way
+          pdl_wait();
+          for (int k = 0; k < pre; ++k) xcopy(k);
+        } else if (i >= pre) {
+          xcopy(i);
+        }
       }
     }
     return;
   }
 
   if (n == 0) return;  // an empty K split (the producer issued nothing either)
+  pdl_wait();  // the outputs were zeroed (or hold the residual) by earlier grids
   float acc[NT][4];
 #pragma unroll
   for (int i = 0; i < NT; ++i) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.f;
@@ -434,13 +444,13 @@ size_t gemm_xfrag_bytes(int64_t M, int64_t K) {
 size_t gemm_small_xfrag_bytes(int64_t M, int64_t K) { return xfrag_bytes(M, K, small_nt(M)); }
 
 static ifx_status stage_sync(const float *X, const float *X2, const float *normw, float eps,
-                             int mode, int64_t M, int64_t K, int NT, void *xfrag, cudaStream_t st) {
+                             int mode, int64_t M, int64_t K, int NT, void *xfrag, cudaStream_t st,
+                             StageZero z = StageZero{}, bool pdl = false) {
   if (K % 32) return fail(IFX_ERR_SHAPE, "gemm: K must be a multiple of 32");
   const int64_t tokb = 8 * NT, mpad = (M + tokb - 1) / tokb * tokb;
   const dim3 grid((unsigned)mpad, (unsigned)((K + kStageCols - 1) / kStageCols));
-  stage_x_kernel<<<grid, 256, 0, st>>>(X, X2, normw, eps, mode, M, K, NT,
-                                       reinterpret_cast<__half *>(xfrag));
-  IFX_CUDA(cudaGetLastError());
+  IFX_CUDA(launch(stage_x_kernel, grid, dim3(256), 0, st, pdl, X, X2, normw, eps, mode, M, K, NT,
+                  reinterpret_cast<__half *>(xfrag), z));
   return IFX_OK;
 }
 
@@ -452,14 +462,16 @@ ifx_status gemm_stage_x(const float *X, const float *X2, const float *normw, flo
 }
 
 ifx_status gemm_small_stage_x(const float *X, const float *X2, const float *normw, float eps,
-                              int mode, int64_t M, int64_t K, void *xfrag, cudaStream_t st) {
+                              int mode, int64_t M, int64_t K, void *xfrag, cudaStream_t st,
+                              StageZero zero, bool pdl) {
   if (M > kGemmSmallMax) return fail(IFX_ERR_UNSUPPORTED, "gemm: small batch above 32 tokens");
-  return stage_sync(X, X2, normw, eps, mode, M, K, small_nt(M), xfrag, st);
+  return stage_sync(X, X2, normw, eps, mode, M, K, small_nt(M), xfrag, st, zero, pdl);
 }
 
 template <int NT>
 static ifx_status launch_sync(const QMatrix &W, const void *xfrag, int64_t M, float *C,
-                              int64_t ldc, int accumulate, int ksplit, int *err, cudaStream_t st) {
+                              int64_t ldc, int accumulate, int ksplit, int *err, cudaStream_t st,
+                              bool pdl = false) {
   GemmArgs a{};
   a.w = W.d;
   a.x = reinterpret_cast<const uint8_t *>(xfrag);
@@ -489,8 +501,7 @@ static ifx_status launch_sync(const QMatrix &W, const void *xfrag, int64_t M, fl
     attr = smem;
   }
   dim3 grid((unsigned)((M + 8 * NT - 1) / (8 * NT)), (unsigned)W.L.ctiles, (unsigned)ksplit);
-  gemm_kernel<NT><<<grid, kGThreads, smem, st>>>(a);
-  IFX_CUDA(cudaGetLastError());
+  IFX_CUDA(launch(gemm_kernel<NT>, grid, dim3(kGThreads), smem, st, pdl, a));
   return IFX_OK;
 }
 
@@ -520,8 +531,8 @@ ifx_status gemm_small_run(const QMatrix &W, const void *xfrag, int64_t M, float 
   if (M > kGemmSmallMax) return fail(IFX_ERR_UNSUPPORTED, "gemm: small batch above 32 tokens");
   // enough K splits for about two CTAs per SM, never more than the units
   const int ksplit = std::max(1, std::min(W.L.kunits, (2 * kNumSMs + W.L.ctiles - 1) / W.L.ctiles));
-  if (small_nt(M) == 2) return launch_sync<2>(W, xfrag, M, C, ldc, 1, ksplit, err, st);
-  return launch_sync<4>(W, xfrag, M, C, ldc, 1, ksplit, err, st);
+  if (small_nt(M) == 2) return launch_sync<2>(W, xfrag, M, C, ldc, 1, ksplit, err, st, true);
+  return launch_sync<4>(W, xfrag, M, C, ldc, 1, ksplit, err, st, true);
 }
 
 }  // namespace ifx

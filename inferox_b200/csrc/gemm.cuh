@@ -28,8 +28,17 @@ ifx_status gemm_run(const QMatrix &W, const void *xfrag, int64_t M, float *C, in
 // initial value (zeros, or the residual the result is added to).
 constexpr int kGemmSmallMax = 32;
 size_t gemm_small_xfrag_bytes(int64_t M, int64_t K);
+// Up to two f32 buffers the staging kernel zeroes (after the previous grid
+// completes) for the GEMMs that follow it to accumulate into.
+struct StageZero {
+  float *p[2] = {nullptr, nullptr};
+  int64_t n[2] = {0, 0};
+};
+// pdl: launched with programmatic serialization (the small-batch GEMMs
+// are, so their weight fetch overlaps the staging before them).
 ifx_status gemm_small_stage_x(const float *X, const float *X2, const float *normw, float eps,
-                              int mode, int64_t M, int64_t K, void *xfrag, cudaStream_t st);
+                              int mode, int64_t M, int64_t K, void *xfrag, cudaStream_t st,
+                              StageZero zero = StageZero{}, bool pdl = false);
 ifx_status gemm_small_run(const QMatrix &W, const void *xfrag, int64_t M, float *C, int64_t ldc,
                           int *err, cudaStream_t st);
 

@@ -937,9 +937,14 @@ ifx_status Model::stage_rows(const float *X, const float *X2, const float *normw
 }
 
 ifx_status Model::stage_small(const float *X, const float *X2, const float *normw, float eps,
-                              int mode, int64_t M, int64_t K, void *buf, cudaStream_t st) {
-  if (dense) return dense_stage(X, X2, normw, eps, mode, M, K, buf, st);
-  return gemm_small_stage_x(X, X2, normw, eps, mode, M, K, buf, st);
+                              int mode, int64_t M, int64_t K, void *buf, cudaStream_t st,
+                              StageZero zero) {
+  if (dense) {
+    for (int i = 0; i < 2; ++i)
+      if (zero.p[i]) IFX_CUDA(cudaMemsetAsync(zero.p[i], 0, sizeof(float) * (size_t)zero.n[i], st));
+    return dense_stage(X, X2, normw, eps, mode, M, K, buf, st);
+  }
+  return gemm_small_stage_x(X, X2, normw, eps, mode, M, K, buf, st, zero, true);
 }
 
 ifx_status Model::run_decode(KvCache &kv, bool gather_logits) {
@@ -1094,8 +1099,10 @@ ifx_status Model::enqueue_decode_batch(KvBatch &kb, cudaStream_t st, int n, cons
   IFX_CUDA(cudaGetLastError());
   for (uint64_t l = 0; l < c.n_layers; ++l) {
     Layer &L = layers[l];
-    IFX_CUDA(cudaMemsetAsync(kb.qkv, 0, sizeof(float) * (size_t)B * qkvw, st));
-    IFX_TRY(stage_small(kb.x, nullptr, L.attn_norm, eps, GX_RMSNORM, B, D, kb.xf, st));
+    StageZero zq;  // the QKV GEMMs accumulate into qkv
+    zq.p[0] = kb.qkv;
+    zq.n[0] = (int64_t)B * qkvw;
+    IFX_TRY(stage_small(kb.x, nullptr, L.attn_norm, eps, GX_RMSNORM, B, D, kb.xf, st, zq));
     IFX_TRY(gemm_small_run(L.wq, kb.xf, B, kb.qkv, qkvw, err, st));
     IFX_TRY(gemm_small_run(L.wk, kb.xf, B, kb.qkv + Hh, qkvw, err, st));
     IFX_TRY(gemm_small_run(L.wv, kb.xf, B, kb.qkv + Hh + G * hd, qkvw, err, st));
@@ -1127,19 +1134,23 @@ ifx_status Model::enqueue_decode_batch(KvBatch &kb, cudaStream_t st, int n, cons
     a.err = err;
     a.batch = B;
     a.slot = slot_dev;
-    IFX_TRY(decode_attention(a, st, false));
+    IFX_TRY(decode_attention(a, st, true));
     IFX_TRY(stage_small(kb.attn, nullptr, nullptr, 0.f, GX_PLAIN, B, Hh, kb.xf, st));
     IFX_TRY(gemm_small_run(L.wo, kb.xf, B, kb.x, D, err, st));  // x += attn Wo^T
-    IFX_CUDA(cudaMemsetAsync(kb.gate, 0, sizeof(float) * (size_t)B * F, st));
-    IFX_CUDA(cudaMemsetAsync(kb.up, 0, sizeof(float) * (size_t)B * F, st));
-    IFX_TRY(stage_small(kb.x, nullptr, L.ffn_norm, eps, GX_RMSNORM, B, D, kb.xf, st));
+    StageZero zf;  // W1 / W3 accumulate into gate / up
+    zf.p[0] = kb.gate;
+    zf.p[1] = kb.up;
+    zf.n[0] = zf.n[1] = (int64_t)B * F;
+    IFX_TRY(stage_small(kb.x, nullptr, L.ffn_norm, eps, GX_RMSNORM, B, D, kb.xf, st, zf));
     IFX_TRY(gemm_small_run(L.w1, kb.xf, B, kb.gate, F, err, st));
     IFX_TRY(gemm_small_run(L.w3, kb.xf, B, kb.up, F, err, st));
     IFX_TRY(stage_small(kb.gate, kb.up, nullptr, 0.f, GX_SWIGLU, B, F, kb.xf, st));
     IFX_TRY(gemm_small_run(L.w2, kb.xf, B, kb.x, D, err, st));  // x += swiglu W2^T
   }
-  IFX_CUDA(cudaMemsetAsync(kb.logits, 0, sizeof(float) * (size_t)B * V, st));
-  IFX_TRY(stage_small(kb.x, nullptr, out_norm, eps, GX_RMSNORM, B, D, kb.xf, st));
+  StageZero zl;  // the logits GEMM accumulates into logits
+  zl.p[0] = kb.logits;
+  zl.n[0] = (int64_t)B * V;
+  IFX_TRY(stage_small(kb.x, nullptr, out_norm, eps, GX_RMSNORM, B, D, kb.xf, st, zl));
   IFX_TRY(gemm_small_run(out_w, kb.xf, B, kb.logits, V, err, st));
   IFX_CUDA(cudaMemsetAsync(kb.keys, 0, sizeof(unsigned long long) * (size_t)B, st));
   argmax_rows_kernel<<<dim3((unsigned)B, kArgmaxParts), 256, 0, st>>>(kb.logits, V, kb.keys);

@@ -6,6 +6,7 @@
 
 #include "common.cuh"
 #include "decode_mega.cuh"
+#include "gemm.cuh"
 #include "gemv.cuh"
 #include "repack.h"
 
@@ -161,8 +162,11 @@ struct Model {
   // plain f32 rows of the dense path
   ifx_status stage_rows(const float *X, const float *X2, const float *normw, float eps, int mode,
                         int64_t M, int64_t K, void *buf, cudaStream_t st);
+  // zero: buffers the following GEMMs accumulate into (zeroed by the
+  // staging kernel after the previous grid completes)
   ifx_status stage_small(const float *X, const float *X2, const float *normw, float eps, int mode,
-                         int64_t M, int64_t K, void *buf, cudaStream_t st);
+                         int64_t M, int64_t K, void *buf, cudaStream_t st,
+                         StageZero zero = StageZero{});
   ifx_status decode_step(KvCache &kv, uint32_t token, float *logits_host);
   ifx_status prefill(KvCache &kv, const uint32_t *ids, size_t n, float *logits_host, int last_row_only);
   ifx_status forward(const uint32_t *ids, size_t n, float *logits_host, int last_row_only);
