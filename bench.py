@@ -44,9 +44,9 @@ WORKLOADS = {
 # figures come from 1- and 2-layer cuts of the same width (see cpu_step_time)
 CPU_CUT = {"70b"}
 # DRAM bytes (read + write) per algorithmic byte of decode_mega_kernel, from
-# an ncu capture of the 4-layer 8B-shaped case (976.6 MB + 15.1 MB over
-# 973.2 MB); traffic scales with the weight bytes.
-TRAFFIC_PER_ALGO_BYTE = 1.019
+# an ncu capture of the 4-layer 8B-shaped case (974.5 MB + 11.8 MB over
+# 973.3 MB); traffic scales with the weight bytes.
+TRAFFIC_PER_ALGO_BYTE = 1.013
 
 
 def bf16_peak():
