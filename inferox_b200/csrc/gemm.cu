@@ -131,16 +131,27 @@ __device__ __forceinline__ uint32_t deq(uint32_t bits, __half2 sub, __half2 scal
   return h2u(__hfma2(__hsub2(u2h(bits), sub), scale, add));
 }
 
-struct GemmArgs {
+// One matrix of a launch: its row tiles are blockIdx.y in [ctile0, ctile0 +
+// its ctiles).
+struct GemmSeg {
   const uint8_t *w;
+  float *C;
+  int64_t ldc;
+  int type, rows, unit_bytes, wt_bytes, wt_qbytes, ctile0;
+  uint32_t smask;  // 0x80: Q6_K scale bytes are int8 (llama.cpp), else 0
+};
+constexpr int kGemmMaxSegs = 3;
+
+struct GemmArgs {
+  GemmSeg seg[kGemmMaxSegs];  // matrices sharing K and the staged input
+  int nseg;
   const uint8_t *x;   // staged fragments
   const float *sums;  // per-token sums of x over 32-column groups
-  float *C;
-  int64_t ldc, M;
-  int type, rows, kc, kunits, unit_bytes, wt_bytes, wt_qbytes, nch_total;
+  int64_t M;
+  int kc, kunits, nch_total;
+  int max_unit;    // the largest unit of the segments: a stage's weight slot
   int accumulate;  // C += result (else C = result)
   int atomic;      // C += result with atomic adds (K split over gridDim.z CTAs)
-  uint32_t smask;  // 0x80: Q6_K scale bytes are int8 (llama.cpp), else 0
   int *err;
 };
 
@@ -328,9 +339,14 @@ __global__ void __launch_bounds__(kGThreads, NT <= 2 ? 3 : 1) gemm_kernel(const 
   constexpr int tokb = 8 * NT;
   const int xbytes = a.kc / 16 * xchunk_bytes(NT);           // x hi + lo of the unit's columns
   const int sbytes = a.kc / 32 * tokb * (int)sizeof(float);  // per-token group sums
-  const int stage_bytes = a.unit_bytes + xbytes + sbytes;
+  const int stage_bytes = a.max_unit + xbytes + sbytes;
   uint8_t *ring = smem + 128;
-  const int mb = blockIdx.x, ctile = blockIdx.y;
+  int si = 0;  // this CTA's matrix
+#pragma unroll
+  for (int i = 1; i < kGemmMaxSegs; ++i)
+    if (i < a.nseg && (int)blockIdx.y >= a.seg[i].ctile0) si = i;
+  const GemmSeg S = a.seg[si];
+  const int mb = blockIdx.x, ctile = blockIdx.y - S.ctile0;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int upc = (a.kunits + gridDim.z - 1) / gridDim.z;  // units per K split
   const int u0 = blockIdx.z * upc, n = max(0, min(a.kunits, u0 + upc) - u0);
@@ -357,8 +373,8 @@ __global__ void __launch_bounds__(kGThreads, NT <= 2 ? 3 : 1) gemm_kernel(const 
             a.x + ((size_t)mb * a.nch_total + (size_t)u * (a.kc / 16)) * xchunk_bytes(NT);
         const uint8_t *ssrc = reinterpret_cast<const uint8_t *>(
             a.sums + ((size_t)mb * (a.nch_total / 2) + (size_t)u * (a.kc / 32)) * tokb);
-        bulk_g2s(dst + a.unit_bytes, xsrc, (uint32_t)xbytes, &full_bar[st]);
-        bulk_g2s(dst + a.unit_bytes + xbytes, ssrc, (uint32_t)sbytes, &full_bar[st]);
+        bulk_g2s(dst + a.max_unit, xsrc, (uint32_t)xbytes, &full_bar[st]);
+        bulk_g2s(dst + a.max_unit + xbytes, ssrc, (uint32_t)sbytes, &full_bar[st]);
       };
       const int pre = min(n, kGStages);
       for (int i = 0; i < n; ++i) {
@@ -366,9 +382,9 @@ __global__ void __launch_bounds__(kGThreads, NT <= 2 ? 3 : 1) gemm_kernel(const 
         const uint32_t ph = (uint32_t)(i / kGStages) & 1u;
         if (i >= kGStages && !mbar_wait(&empty_bar[st], ph ^ 1u, a.err, 201)) break;
         uint8_t *dst = ring + (size_t)st * stage_bytes;
-        const uint8_t *wsrc = a.w + ((size_t)ctile * a.kunits + u0 + i) * a.unit_bytes;
-        mbar_arrive_expect_tx(&full_bar[st], (uint32_t)stage_bytes);
-        bulk_g2s(dst, wsrc, (uint32_t)a.unit_bytes, &full_bar[st]);
+        const uint8_t *wsrc = S.w + ((size_t)ctile * a.kunits + u0 + i) * S.unit_bytes;
+        mbar_arrive_expect_tx(&full_bar[st], (uint32_t)(S.unit_bytes + xbytes + sbytes));
+        bulk_g2s(dst, wsrc, (uint32_t)S.unit_bytes, &full_bar[st]);
         if (i + 1 == pre) {  // the first stages' weights are on their way
           pdl_wait();
           for (int k = 0; k < pre; ++k) xcopy(k);
@@ -390,14 +406,14 @@ __global__ void __launch_bounds__(kGThreads, NT <= 2 ? 3 : 1) gemm_kernel(const 
     const uint32_t ph = (uint32_t)(i / kGStages) & 1u;
     if (!mbar_wait(&full_bar[st], ph, a.err, 202)) return;
     const uint8_t *base = ring + (size_t)st * stage_bytes;
-    const uint8_t *wt = base + (size_t)warp * a.wt_bytes;
-    const uint8_t *xs = base + a.unit_bytes;
+    const uint8_t *wt = base + (size_t)warp * S.wt_bytes;
+    const uint8_t *xs = base + a.max_unit;
     const float *sx = reinterpret_cast<const float *>(xs + a.kc / 16 * xchunk_bytes(NT));
-    switch (a.type) {
+    switch (S.type) {
       case IFX_TYPE_Q4_K: gemm_unit_q4k<NT>(wt, xs, sx, lane, acc); break;
-      case IFX_TYPE_Q6_K: gemm_unit<IFX_TYPE_Q6_K, NT>(wt, xs, sx, a.kc, a.wt_qbytes, a.smask, lane, acc); break;
-      case IFX_TYPE_Q4_0: gemm_unit<IFX_TYPE_Q4_0, NT>(wt, xs, sx, a.kc, a.wt_qbytes, a.smask, lane, acc); break;
-      default: gemm_unit<IFX_TYPE_Q8_0, NT>(wt, xs, sx, a.kc, a.wt_qbytes, a.smask, lane, acc); break;
+      case IFX_TYPE_Q6_K: gemm_unit<IFX_TYPE_Q6_K, NT>(wt, xs, sx, a.kc, S.wt_qbytes, S.smask, lane, acc); break;
+      case IFX_TYPE_Q4_0: gemm_unit<IFX_TYPE_Q4_0, NT>(wt, xs, sx, a.kc, S.wt_qbytes, S.smask, lane, acc); break;
+      default: gemm_unit<IFX_TYPE_Q8_0, NT>(wt, xs, sx, a.kc, S.wt_qbytes, S.smask, lane, acc); break;
     }
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty_bar[st]);
@@ -411,8 +427,8 @@ __global__ void __launch_bounds__(kGThreads, NT <= 2 ? 3 : 1) gemm_kernel(const 
     for (int j = 0; j < 4; ++j) {
       const int row = r0 + ((j & 2) ? 8 : 0);
       const int64_t tok = (int64_t)mb * tokb + nt * 8 + 2 * c + (j & 1);
-      if (row < a.rows && tok < a.M) {
-        float *p = a.C + tok * a.ldc + row;
+      if (row < S.rows && tok < a.M) {
+        float *p = S.C + tok * S.ldc + row;
         if (a.atomic) red_add_f32(p, acc[nt][j]);
         else *p = a.accumulate ? (*p + acc[nt][j]) : acc[nt][j];
       }
@@ -468,30 +484,45 @@ ifx_status gemm_small_stage_x(const float *X, const float *X2, const float *norm
   return stage_sync(X, X2, normw, eps, mode, M, K, small_nt(M), xfrag, st, zero, pdl);
 }
 
+// n (<= 3) matrices with the same K and unit width over one staged input:
+// their row tiles side by side in one launch (blockIdx.y), K split over
+// gridDim.z CTAs (results added atomically when ksplit > 1).
 template <int NT>
-static ifx_status launch_sync(const QMatrix &W, const void *xfrag, int64_t M, float *C,
-                              int64_t ldc, int accumulate, int ksplit, int *err, cudaStream_t st,
-                              bool pdl = false) {
+static ifx_status launch_sync(const QMatrix *const *W, float *const *C, const int64_t *ldc, int n,
+                              const void *xfrag, int64_t M, int accumulate, int ksplit, int *err,
+                              cudaStream_t st, bool pdl = false) {
+  if (n < 1 || n > kGemmMaxSegs) return fail(IFX_ERR_INVALID_ARGUMENT, "gemm: 1 to 3 matrices");
   GemmArgs a{};
-  a.w = W.d;
+  a.nseg = n;
   a.x = reinterpret_cast<const uint8_t *>(xfrag);
-  a.sums = reinterpret_cast<const float *>(a.x + xfrag_frag_bytes(M, W.L.cols, NT));
-  a.C = C;
-  a.ldc = ldc;
+  a.sums = reinterpret_cast<const float *>(a.x + xfrag_frag_bytes(M, W[0]->L.cols, NT));
   a.M = M;
-  a.type = W.L.type;
-  a.rows = (int)W.L.rows;
-  a.kc = W.L.kc;
-  a.kunits = W.L.kunits;
-  a.unit_bytes = W.L.unit_bytes;
-  a.wt_bytes = W.L.wt_bytes;
-  a.wt_qbytes = W.L.wt_qbytes;
-  a.smask = W.L.q6_s8 ? 0x80u : 0u;
-  a.nch_total = (int)(W.L.cols / 16);
+  a.kc = W[0]->L.kc;
+  a.kunits = W[0]->L.kunits;
+  a.nch_total = (int)(W[0]->L.cols / 16);
+  int ctiles = 0;
+  for (int i = 0; i < n; ++i) {
+    const QLayout &L = W[i]->L;
+    if (L.kc != a.kc || L.cols != W[0]->L.cols)
+      return fail(IFX_ERR_SHAPE, "gemm: fused matrices must share K and unit width");
+    GemmSeg &S = a.seg[i];
+    S.w = W[i]->d;
+    S.C = C[i];
+    S.ldc = ldc[i];
+    S.type = L.type;
+    S.rows = (int)L.rows;
+    S.unit_bytes = L.unit_bytes;
+    S.wt_bytes = L.wt_bytes;
+    S.wt_qbytes = L.wt_qbytes;
+    S.smask = L.q6_s8 ? 0x80u : 0u;
+    S.ctile0 = ctiles;
+    ctiles += L.ctiles;
+    a.max_unit = std::max(a.max_unit, L.unit_bytes);
+  }
   a.accumulate = accumulate;
   a.atomic = ksplit > 1 ? 1 : 0;
   a.err = err;
-  const size_t smem = 128 + (size_t)kGStages * (a.unit_bytes + a.kc / 16 * xchunk_bytes(NT) +
+  const size_t smem = 128 + (size_t)kGStages * (a.max_unit + a.kc / 16 * xchunk_bytes(NT) +
                                                 a.kc / 32 * 8 * NT * sizeof(float));
   if (smem > 226 * 1024) return fail(IFX_ERR_UNSUPPORTED, "gemm: shared memory plan too large");
   static size_t attr = 0;
@@ -500,9 +531,19 @@ static ifx_status launch_sync(const QMatrix &W, const void *xfrag, int64_t M, fl
                                   (int)smem));
     attr = smem;
   }
-  dim3 grid((unsigned)((M + 8 * NT - 1) / (8 * NT)), (unsigned)W.L.ctiles, (unsigned)ksplit);
+  dim3 grid((unsigned)((M + 8 * NT - 1) / (8 * NT)), (unsigned)ctiles, (unsigned)ksplit);
   IFX_CUDA(launch(gemm_kernel<NT>, grid, dim3(kGThreads), smem, st, pdl, a));
   return IFX_OK;
+}
+
+template <int NT>
+static ifx_status launch_sync(const QMatrix &W, const void *xfrag, int64_t M, float *C,
+                              int64_t ldc, int accumulate, int ksplit, int *err, cudaStream_t st,
+                              bool pdl = false) {
+  const QMatrix *w[1] = {&W};
+  float *c[1] = {C};
+  const int64_t l[1] = {ldc};
+  return launch_sync<NT>(w, c, l, 1, xfrag, M, accumulate, ksplit, err, st, pdl);
 }
 
 ifx_status gemm_run_multi(const QMatrix *const *W, float *const *C, const int64_t *ldc, int n,
@@ -523,6 +564,25 @@ ifx_status gemm_run(const QMatrix &W, const void *xfrag, int64_t M, float *C, in
   if (W.L.dense) return dense_gemm(W, xfrag, M, C, ldc, accumulate, st);
   if (tc_gemm_eligible(W.L.cols)) return tc_gemm_run(W, xfrag, M, C, ldc, accumulate, err, st);
   return launch_sync<kGemmTokens / 8>(W, xfrag, M, C, ldc, accumulate, 1, err, st);
+}
+
+ifx_status gemm_small_run_multi(const QMatrix *const *W, float *const *C, const int64_t *ldc,
+                                int n, const void *xfrag, int64_t M, int *err, cudaStream_t st) {
+  if (n >= 1 && W[0]->L.dense) {
+    for (int i = 0; i < n; ++i) IFX_TRY(dense_gemm(*W[i], xfrag, M, C[i], ldc[i], 1, st));
+    return IFX_OK;
+  }
+  if (M > kGemmSmallMax) return fail(IFX_ERR_UNSUPPORTED, "gemm: small batch above 32 tokens");
+  for (int i = 1; i < n; ++i)  // different unit widths run as separate launches
+    if (W[i]->L.kc != W[0]->L.kc) {
+      for (int k = 0; k < n; ++k) IFX_TRY(gemm_small_run(*W[k], xfrag, M, C[k], ldc[k], err, st));
+      return IFX_OK;
+    }
+  int ctiles = 0;
+  for (int i = 0; i < n; ++i) ctiles += W[i]->L.ctiles;
+  const int ksplit = std::max(1, std::min(W[0]->L.kunits, (2 * kNumSMs + ctiles - 1) / ctiles));
+  if (small_nt(M) == 2) return launch_sync<2>(W, C, ldc, n, xfrag, M, 1, ksplit, err, st, true);
+  return launch_sync<4>(W, C, ldc, n, xfrag, M, 1, ksplit, err, st, true);
 }
 
 ifx_status gemm_small_run(const QMatrix &W, const void *xfrag, int64_t M, float *C, int64_t ldc,

@@ -41,6 +41,10 @@ ifx_status gemm_small_stage_x(const float *X, const float *X2, const float *norm
                               StageZero zero = StageZero{}, bool pdl = false);
 ifx_status gemm_small_run(const QMatrix &W, const void *xfrag, int64_t M, float *C, int64_t ldc,
                           int *err, cudaStream_t st);
+// n (<= 3) matrices over one staged input in one launch (Wq/Wk/Wv, W1/W3);
+// separate launches when their unit widths differ.
+ifx_status gemm_small_run_multi(const QMatrix *const *W, float *const *C, const int64_t *ldc,
+                                int n, const void *xfrag, int64_t M, int *err, cudaStream_t st);
 
 // The tensor-memory (tcgen05) GEMM of tcgemm.cu: used by gemm_stage_x and
 // gemm_run whenever K is a multiple of 64 (the mma.sync kernel above covers

@@ -1103,9 +1103,12 @@ ifx_status Model::enqueue_decode_batch(KvBatch &kb, cudaStream_t st, int n, cons
     zq.p[0] = kb.qkv;
     zq.n[0] = (int64_t)B * qkvw;
     IFX_TRY(stage_small(kb.x, nullptr, L.attn_norm, eps, GX_RMSNORM, B, D, kb.xf, st, zq));
-    IFX_TRY(gemm_small_run(L.wq, kb.xf, B, kb.qkv, qkvw, err, st));
-    IFX_TRY(gemm_small_run(L.wk, kb.xf, B, kb.qkv + Hh, qkvw, err, st));
-    IFX_TRY(gemm_small_run(L.wv, kb.xf, B, kb.qkv + Hh + G * hd, qkvw, err, st));
+    {  // Wq, Wk, Wv in one launch
+      const QMatrix *ws[3] = {&L.wq, &L.wk, &L.wv};
+      float *cs[3] = {kb.qkv, kb.qkv + Hh, kb.qkv + Hh + G * hd};
+      const int64_t ls[3] = {qkvw, qkvw, qkvw};
+      IFX_TRY(gemm_small_run_multi(ws, cs, ls, 3, kb.xf, B, err, st));
+    }
     DecodeAttnArgs a{};
     a.qkv = kb.qkv;
     a.qkv_stride = qkvw;
@@ -1142,8 +1145,12 @@ ifx_status Model::enqueue_decode_batch(KvBatch &kb, cudaStream_t st, int n, cons
     zf.p[1] = kb.up;
     zf.n[0] = zf.n[1] = (int64_t)B * F;
     IFX_TRY(stage_small(kb.x, nullptr, L.ffn_norm, eps, GX_RMSNORM, B, D, kb.xf, st, zf));
-    IFX_TRY(gemm_small_run(L.w1, kb.xf, B, kb.gate, F, err, st));
-    IFX_TRY(gemm_small_run(L.w3, kb.xf, B, kb.up, F, err, st));
+    {  // W1, W3 in one launch
+      const QMatrix *ws[2] = {&L.w1, &L.w3};
+      float *cs[2] = {kb.gate, kb.up};
+      const int64_t ls[2] = {F, F};
+      IFX_TRY(gemm_small_run_multi(ws, cs, ls, 2, kb.xf, B, err, st));
+    }
     IFX_TRY(stage_small(kb.gate, kb.up, nullptr, 0.f, GX_SWIGLU, B, F, kb.xf, st));
     IFX_TRY(gemm_small_run(L.w2, kb.xf, B, kb.x, D, err, st));  // x += swiglu W2^T
   }
