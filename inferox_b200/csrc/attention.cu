@@ -478,21 +478,21 @@ __global__ void __launch_bounds__(128) decode_attn_small_kernel(const __grid_con
 constexpr int kFlashWarps = 4;
 constexpr int kFlashRows = 16;  // cache rows per tile
 
-template <int HD>
+template <int HD, int WARPS>
 __host__ __device__ constexpr int flash_smem_bytes() {
-  // stages [warp][2][K tile | V tile] halves, Q [16][HD + 8] halves, 8 mbarriers
-  return kFlashWarps * 2 * 2 * kFlashRows * HD * 2 + 16 * (HD + 8) * 2 + kFlashWarps * 2 * 8;
+  // stages [warp][2][K tile | V tile] halves, Q [16][HD + 8] halves, 2 mbarriers per warp
+  return WARPS * 2 * 2 * kFlashRows * HD * 2 + 16 * (HD + 8) * 2 + WARPS * 2 * 8;
 }
 
-template <int HD>
-__global__ void __launch_bounds__(kFlashWarps * 32, 3)
+template <int HD, int WARPS>
+__global__ void __launch_bounds__(WARPS * 32, WARPS == 4 ? 3 : 1)
     decode_attn_flash_kernel(const __grid_constant__ DecodeAttnArgs a) {
   constexpr int KSTEPS = HD / 16, NDT = HD / 8, TH = kFlashRows * HD, QS = HD + 8;
   extern __shared__ __align__(128) uint8_t smraw[];
   __half *stage = reinterpret_cast<__half *>(smraw);  // [warp][2][2][TH]
-  __half *qsm = stage + kFlashWarps * 2 * 2 * TH;      // [16][QS]
+  __half *qsm = stage + WARPS * 2 * 2 * TH;      // [16][QS]
   uint64_t *bars = reinterpret_cast<uint64_t *>(qsm + 16 * QS);  // [warp][2]
-  __shared__ float s_m[kFlashWarps][kMaxGroup], s_l[kFlashWarps][kMaxGroup];
+  __shared__ float s_m[WARPS][kMaxGroup], s_l[WARPS][kMaxGroup];
   __shared__ int s_last;
   const int h = blockIdx.x, s = blockIdx.y, b = blockIdx.z, tid = threadIdx.x;
   const int warp = tid >> 5, lane = tid & 31, g = lane >> 2, c = lane & 3;
@@ -545,8 +545,8 @@ __global__ void __launch_bounds__(kFlashWarps * 32, 3)
     // the cached rows were written by kernels that completed before the
     // previous kernel in the stream began its main phase
     if (tb + warp < te) issue(tb + warp, 0, row_off((tb + warp) * kFlashRows));
-    if (tb + warp + kFlashWarps < te)
-      issue(tb + warp + kFlashWarps, 1, row_off((tb + warp + kFlashWarps) * kFlashRows));
+    if (tb + warp + WARPS < te)
+      issue(tb + warp + WARPS, 1, row_off((tb + warp + WARPS) * kFlashRows));
   }
 
   pdl_wait();
@@ -560,7 +560,7 @@ __global__ void __launch_bounds__(kFlashWarps * 32, 3)
   const int rpos = a.rope_compat ? 0 : pos;
   {
     const float *q = qkv + (size_t)h * grp * HD;
-    for (int e = tid; e < 8 * HD / 2; e += kFlashWarps * 32) {
+    for (int e = tid; e < 8 * HD / 2; e += WARPS * 32) {
       const int j = e / (HD / 2), i = 2 * (e % (HD / 2));
       float x0 = 0.f, x1 = 0.f;
       if (j < grp) {
@@ -590,12 +590,12 @@ __global__ void __launch_bounds__(kFlashWarps * 32, 3)
   const int vrow = (lane & 7) + 8 * ((lane >> 3) & 1), vch = lane >> 4;
   bool ok = true;
   for (int i = 0;; ++i) {
-    const int T = tb + warp + kFlashWarps * i;
+    const int T = tb + warp + WARPS * i;
     if (T >= te) break;
     const int st = i & 1;
     // the cache offset of the tile this stage takes next, loaded before the wait
-    const bool more = T + 2 * kFlashWarps < te;
-    const size_t next_off = (lane == 0 && more) ? row_off((T + 2 * kFlashWarps) * kFlashRows) : 0;
+    const bool more = T + 2 * WARPS < te;
+    const size_t next_off = (lane == 0 && more) ? row_off((T + 2 * WARPS) * kFlashRows) : 0;
     ok = __all_sync(0xffffffffu, mbar_wait(&mybar[st], (uint32_t)(i >> 1) & 1u, a.err, 306));
     if (!ok) break;  // the error flag is set; the host reports a timeout
     ++done[st];
@@ -677,7 +677,7 @@ __global__ void __launch_bounds__(kFlashWarps * 32, 3)
       mma_16816(o[nd + 1], pa[0], pa[1], pa[2], pa[3], vb[2], vb[3], o[nd + 1]);
     }
     __syncwarp();  // every lane has read this stage
-    if (lane == 0 && more) issue(T + 2 * kFlashWarps, st, next_off);
+    if (lane == 0 && more) issue(T + 2 * WARPS, st, next_off);
   }
   // leave no copy in flight after an early exit: wait (bounded) for the
   // stages this warp issued but did not consume
@@ -701,24 +701,42 @@ __global__ void __launch_bounds__(kFlashWarps * 32, 3)
     }
   }
   __syncthreads();
+  if (NS == 1) {  // one split: the merged warps are the whole softmax
+    for (int e = tid; e < grp * HD; e += WARPS * 32) {
+      const int j = e / HD;
+      float M = -INFINITY;
+#pragma unroll
+      for (int w = 0; w < WARPS; ++w) M = fmaxf(M, s_m[w][j]);
+      float O = 0.f, Lw = 0.f;
+#pragma unroll
+      for (int w = 0; w < WARPS; ++w)
+        if (s_m[w][j] != -INFINITY) {
+          const float f = expf(s_m[w][j] - M);
+          O = fmaf(f, mo[((size_t)w * 8 + j) * HD + (e % HD)], O);
+          Lw = fmaf(s_l[w][j], f, Lw);
+        }
+      attn_out[(size_t)h * grp * HD + e] = O / Lw;
+    }
+    return;
+  }
   float *po = part_o + (size_t)(h * NS + s) * grp * HD;
-  for (int e = tid; e < grp * HD; e += kFlashWarps * 32) {
+  for (int e = tid; e < grp * HD; e += WARPS * 32) {
     const int j = e / HD;
     float M = -INFINITY;
 #pragma unroll
-    for (int w = 0; w < kFlashWarps; ++w) M = fmaxf(M, s_m[w][j]);
+    for (int w = 0; w < WARPS; ++w) M = fmaxf(M, s_m[w][j]);
     float O = 0.f;
     if (M != -INFINITY)
 #pragma unroll
-      for (int w = 0; w < kFlashWarps; ++w)
+      for (int w = 0; w < WARPS; ++w)
         if (s_m[w][j] != -INFINITY) O = fmaf(expf(s_m[w][j] - M), mo[((size_t)w * 8 + j) * HD + (e % HD)], O);
     po[e] = O;
   }
   if (tid < grp) {
     float M = -INFINITY, L = 0.f;
-    for (int w = 0; w < kFlashWarps; ++w) M = fmaxf(M, s_m[w][tid]);
+    for (int w = 0; w < WARPS; ++w) M = fmaxf(M, s_m[w][tid]);
     if (M != -INFINITY)
-      for (int w = 0; w < kFlashWarps; ++w)
+      for (int w = 0; w < WARPS; ++w)
         if (s_m[w][tid] != -INFINITY) L = fmaf(s_l[w][tid], expf(s_m[w][tid] - M), L);
     part_ml[(h * NS + s) * grp + tid] = make_float2(M, L);  // l = 0 marks an empty split
   }
@@ -728,7 +746,7 @@ __global__ void __launch_bounds__(kFlashWarps * 32, 3)
   __syncthreads();
   if (!s_last) return;
   __threadfence();
-  attn_combine(part_o, part_ml, attn_out, counters, h, NS, grp, HD, tid, kFlashWarps * 32);
+  attn_combine(part_o, part_ml, attn_out, counters, h, NS, grp, HD, tid, WARPS * 32);
 }
 
 // ------------------------------------------------------------ prefill ----
@@ -838,24 +856,37 @@ int decode_attention_smem(int grp, int hd, int max_seq, int ns) {
   return 2 * cap * hd * 2 + (grp * hd + grp * cap) * (int)sizeof(float);
 }
 
-template <int HD>
-static ifx_status launch_flash(const DecodeAttnArgs &a, cudaStream_t st, bool pdl) {
-  // splits: about three CTAs per SM over the whole batch, at least two
-  // tiles per warp, and no more than the caller's partial buffers hold
-  DecodeAttnArgs f = a;
-  const int tiles = (a.max_seq + kFlashRows - 1) / kFlashRows;
-  const int want = std::max(1, 3 * kNumSMs / std::max(1, a.G * a.batch));
-  f.ns = std::max(1, std::min({a.ns, want, kMaxSplits, (tiles + 2 * kFlashWarps - 1) / (2 * kFlashWarps)}));
-  constexpr int smem = flash_smem_bytes<HD>();
+template <int HD, int WARPS>
+static ifx_status launch_flash_w(const DecodeAttnArgs &f, cudaStream_t st, bool pdl) {
+  constexpr int smem = flash_smem_bytes<HD, WARPS>();
   static bool attr = false;
   if (!attr) {
-    IFX_CUDA(cudaFuncSetAttribute(decode_attn_flash_kernel<HD>,
+    IFX_CUDA(cudaFuncSetAttribute(decode_attn_flash_kernel<HD, WARPS>,
                                   cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
     attr = true;
   }
-  IFX_CUDA(launch(decode_attn_flash_kernel<HD>, dim3(a.G, f.ns, a.batch), dim3(kFlashWarps * 32),
+  IFX_CUDA(launch(decode_attn_flash_kernel<HD, WARPS>, dim3(f.G, f.ns, f.batch), dim3(WARPS * 32),
                   (size_t)smem, st, pdl, f));
   return IFX_OK;
+}
+
+template <int HD>
+static ifx_status launch_flash(const DecodeAttnArgs &a, cudaStream_t st, bool pdl) {
+  // Many (sequence, kv head) pairs (a batch): one 8-warp CTA per pair and
+  // SM, each streaming the whole context (no split combine). Few pairs:
+  // 4-warp CTAs, about three per SM, the context split among them (at
+  // least two tiles per warp) and no more splits than the caller's
+  // partial buffers hold.
+  DecodeAttnArgs f = a;
+  const int tiles = (a.max_seq + kFlashRows - 1) / kFlashRows;
+  const int pairs = std::max(1, a.G * a.batch);
+  if (pairs >= kNumSMs / 2 && tiles >= 32) {
+    f.ns = std::max(1, std::min({a.ns, kNumSMs / pairs, tiles / 32}));
+    return launch_flash_w<HD, 8>(f, st, pdl);
+  }
+  const int want = std::max(1, 3 * kNumSMs / pairs);
+  f.ns = std::max(1, std::min({a.ns, want, kMaxSplits, (tiles + 2 * kFlashWarps - 1) / (2 * kFlashWarps)}));
+  return launch_flash_w<HD, kFlashWarps>(f, st, pdl);
 }
 
 ifx_status decode_attention(const DecodeAttnArgs &a, cudaStream_t st, bool pdl) {

@@ -590,55 +590,77 @@ __device__ __noinline__ void combine_kv_head(const MegaArgs &A, int h, float *wb
   }
 }
 
-// All-reduce of one vector across the ranks, inside the step. CTA b owns
-// slice b (float4 granularity): it pushes its slice of ar_src to every rank's
-// receive row for this rank (peer stores over NVLink), zeroes it, raises its
-// flag on every rank, waits until every rank's CTA b has raised its flag
-// here, then adds the ranks' slices in rank order into ar_dst. Every rank
-// adds the same values in the same order, so ar_dst stays identical on all
-// ranks. Receive rows alternate between two parities: a rank pushes epoch
-// e + 1 only after every rank's CTA b pushed epoch e, which each did after
-// reading its epoch e - 1 slices.
+// All-reduce of one vector across the ranks, inside the step. Each element
+// travels as one 64-bit word, the epoch in the high half and the f32 bits
+// in the low half, written with a single relaxed system-scope store into
+// every rank's receive row for this rank: a receiver that reads the epoch
+// in a word has that word's value too, so no fence and no separate flag
+// sit between a push and its use (one NVLink crossing). CTA b owns a slice
+// of the elements; its threads push their elements, zero them in ar_src,
+// then wait (bounded) for every rank's word of each element and add the
+// ranks' values in rank order into ar_dst, so ar_dst stays identical on
+// all ranks. Receive rows alternate between two parities: a rank pushes
+// epoch e + 1 only after it has read every rank's epoch-e words of its
+// slice, which every rank wrote after finishing epoch e - 1.
+__device__ __forceinline__ void st_relaxed_sys_u64(unsigned long long *p, unsigned long long v) {
+  asm volatile("st.relaxed.sys.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+
+__device__ __forceinline__ unsigned long long ld_relaxed_sys_u64(const unsigned long long *p) {
+  unsigned long long v;
+  asm volatile("ld.relaxed.sys.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// Bounded wait for the word of epoch e at p (written by another rank);
+// false (error flag set to `code`) after limit_ns or once another thread
+// has raised the error flag.
+__device__ bool wait_word(const unsigned long long *p, unsigned e, unsigned long long *out, int *err,
+                          int code, uint64_t limit_ns) {
+  uint64_t t0 = 0;
+  for (uint32_t spins = 0;; ++spins) {
+    const unsigned long long w = ld_relaxed_sys_u64(p);
+    if ((unsigned)(w >> 32) == e) {
+      *out = w;
+      return true;
+    }
+    if ((spins & 63u) == 63u) {
+      if (*(volatile int *)err) return false;
+      const uint64_t t = global_ns();
+      if (!t0) t0 = t;
+      else if (t - t0 > limit_ns) {
+        atomicExch(err, code);
+        return false;
+      }
+    }
+  }
+}
+
 __device__ __noinline__ void phase_allreduce(const MegaArgs &A, const MegaPhase &P, unsigned ar0) {
   const int tid = threadIdx.x, b = blockIdx.x, N = A.nranks, me = A.rank;
   const MegaPeers &pr = A.peers;
   const unsigned e = ar0 + (unsigned)P.ar_index;
-  const size_t row4 = (size_t)pr.row_floats / 4;
-  const int n4 = P.ar_n / 4, per = (n4 + (int)gridDim.x - 1) / (int)gridDim.x;
-  const int lo = min(n4, b * per), hi = min(n4, lo + per);
-  const size_t par_off = (size_t)(e & 1u) * kMaxRanks * row4;
-  float4 *src = reinterpret_cast<float4 *>(P.ar_src);
+  const size_t row = (size_t)pr.row_floats;
+  const int n = P.ar_n, per = (n + (int)gridDim.x - 1) / (int)gridDim.x;
+  const int lo = min(n, b * per), hi = min(n, lo + per);
+  const size_t par_off = (size_t)(e & 1u) * kMaxRanks * row;
   for (int i = lo + tid; i < hi; i += kConsumerThreads) {
-    const float4 v = __ldcg(src + i);
-    src[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+    const float v = __ldcg(P.ar_src + i);
+    P.ar_src[i] = 0.f;
+    const unsigned long long w = ((unsigned long long)e << 32) | __float_as_uint(v);
     for (int r = 0; r < N; ++r)
-      __stcg(reinterpret_cast<float4 *>(pr.buf[r]) + par_off + (size_t)me * row4 + i, v);
+      st_relaxed_sys_u64(reinterpret_cast<unsigned long long *>(pr.buf[r]) + par_off + (size_t)me * row + i, w);
   }
-  __threadfence_system();
-  consumer_sync();
-  if (tid < N)
-    st_release_sys(reinterpret_cast<unsigned *>(pr.buf[tid] + pr.off_flags) + (size_t)b * kMaxRanks + me, e);
-  if (tid < N)
-    wait_epoch(reinterpret_cast<const unsigned *>(pr.buf[me] + pr.off_flags) + (size_t)b * kMaxRanks + tid,
-               e, A.err, 410, pr.wait_ns);
-  consumer_sync();
-  const float4 *rv = reinterpret_cast<const float4 *>(pr.buf[me]) + par_off;
-  float4 *dst = reinterpret_cast<float4 *>(P.ar_dst);
+  const unsigned long long *rv = reinterpret_cast<const unsigned long long *>(pr.buf[me]) + par_off;
   for (int i = lo + tid; i < hi; i += kConsumerThreads) {
-    float4 t = __ldcg(rv + i);
-    for (int r = 1; r < N; ++r) {
-      const float4 u = __ldcg(rv + (size_t)r * row4 + i);
-      t.x += u.x;
-      t.y += u.y;
-      t.z += u.z;
-      t.w += u.w;
+    float t = 0.f;
+    for (int r = 0; r < N; ++r) {
+      unsigned long long w = 0;
+      wait_word(rv + (size_t)r * row + i, e, &w, A.err, 410, pr.wait_ns);  // on failure the step reports it
+      const float u = __uint_as_float((unsigned)w);
+      t = r == 0 ? u : t + u;
     }
-    float4 x = dst[i];
-    x.x += t.x;
-    x.y += t.y;
-    x.z += t.z;
-    x.w += t.w;
-    dst[i] = x;
+    P.ar_dst[i] += t;
   }
 }
 
@@ -870,7 +892,10 @@ __global__ void __launch_bounds__(kGemvThreads, 1) decode_mega_kernel(const __gr
 }  // namespace
 
 int mega_attn_splits(int G, int max_seq, int num_sms) {
-  int ns = std::max(1, num_sms / std::max(1, G));
+  // at most 18 splits per kv head unless the rows demand more: the split
+  // combine of the last CTA per kv head grows with the split count (37
+  // splits at 4 kv heads per rank made it a 7 us tail per layer)
+  int ns = std::max(1, std::min(num_sms / std::max(1, G), 18));
   ns = std::max(ns, (max_seq + 79) / 80);  // at most ~80 cached rows per item
   return std::min(ns, kMaxSplitsMega);
 }
@@ -887,9 +912,9 @@ size_t mega_attn_scratch(int grp, int hd, int max_seq, int nsa) {
 }
 
 size_t mega_peer_bytes(int n, int grid, MegaPeers *layout) {
-  const size_t row = ((size_t)n + 63) / 64 * 64;  // floats, 256-byte rows
+  const size_t row = ((size_t)n + 63) / 64 * 64;  // elements (64-bit words), 512-byte rows
   layout->row_floats = (int)row;
-  layout->off_flags = 2 * kMaxRanks * row * sizeof(float);
+  layout->off_flags = 2 * kMaxRanks * row * sizeof(unsigned long long);
   layout->off_keys = layout->off_flags + ((size_t)grid * kMaxRanks * sizeof(unsigned) + 255) / 256 * 256;
   layout->off_kflags = layout->off_keys + 2 * kMaxRanks * sizeof(unsigned long long);
   return layout->off_kflags + 256;

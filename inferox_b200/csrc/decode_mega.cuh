@@ -33,8 +33,9 @@ struct __align__(16) MegaPhase {
 
 // Tensor parallelism inside the persistent kernel: every rank owns one
 // buffer that all ranks map (CUDA IPC), laid out as
-//   recv  [2][kMaxRanks][row_floats] f32  slices pushed by each rank, two parities
-//   flags [grid][kMaxRanks] u32          epoch of the last push of CTA b by rank r
+//   recv  [2][kMaxRanks][row_floats] u64  elements pushed by each rank, two
+//                                        parities: epoch << 32 | f32 bits
+//   (off_flags) [grid][kMaxRanks] u32    reserved
 //   keys  [2][kMaxRanks] u64            each rank's argmax key, two parities
 //   kflags [kMaxRanks] u32               epoch of rank r's last key
 // Epochs only grow (counters in `epoch`, advanced by the kernel itself), so

@@ -163,3 +163,29 @@ def test_single_sequence_decode_wide_groups(name):
         assert _close(gl, rl), (i, float(np.max(np.abs(gl - rl))))
         tok = R.argmax(rl)
     assert kv.decode_kernels() == 1
+
+
+@pytest.mark.parametrize("paged", [False, True])
+def test_wide_batch_long_context(paged):
+    """16 sequences x 8 kv heads (128 pairs, as in the 8B batch-16 step) at
+    contexts of 300-700 positions: the attention runs one 8-warp CTA per
+    (sequence, kv head) streaming its whole context with no split combine.
+    Every sequence's logits against the oracle's single-sequence decode."""
+    g = synth.build(None, vocab=1024, dim=1024, n_layers=2, n_heads=16, n_kv_heads=8, ffn=1024,
+                    context=1024, rope_base=500000.0, mix=1, seed=71)
+    m, o = Model.from_bytes(g), R.Model(g)
+    V, L = int(m.config.vocab_size), int(m.config.n_layers)
+    B, max_seq = 16, 768
+    kb = m.kv_batch(B, max_seq, pages=B * 12 if paged else 0)
+    prompts = [synth.prompt_ids(V, 300 + 25 * b, seed=90 + b) for b in range(B)]
+    okv = [o.kv_cache(L, max_seq) for _ in range(B)]
+    toks = []
+    for b in range(B):
+        kb.prefill(b, prompts[b], True)
+        toks.append(R.argmax(o.prefill(prompts[b], okv[b], True)[0]))
+    for step in range(2):
+        logits, _ = kb.decode_step(toks)
+        for b in range(B):
+            rl = o.decode_step(toks[b], okv[b])
+            assert _close(logits[b], rl), (step, b, float(np.max(np.abs(logits[b] - rl))))
+            toks[b] = R.argmax(rl)
