@@ -101,6 +101,12 @@ __device__ __forceinline__ void ring_drain(uint64_t *full_bar, int NS, uint32_t 
   }
 }
 
+// Orders this thread's view of earlier shared-memory accesses (generic
+// proxy) before bulk copies it issues next (async proxy).
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
 // 1-D bulk async copy global -> shared, completion counted on an mbarrier.
 // dst, src and bytes must be 16-byte aligned / multiples of 16.
 __device__ __forceinline__ void bulk_g2s(void *dst_smem, const void *src_gmem, uint32_t bytes,

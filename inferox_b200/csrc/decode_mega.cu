@@ -74,18 +74,28 @@ __device__ bool wait_epoch(const unsigned *flag, unsigned e, int *err, int code,
   return true;
 }
 
+// Copies phase record `src` into shared memory with plain 16-byte loads
+// (one warp; no bulk copy, so nothing queues behind the weight ring's copies
+// in the CTA's copy engine).
+__device__ __forceinline__ void load_record(MegaPhase *dst, const MegaPhase *src, int lane) {
+  constexpr int kWords = (int)(sizeof(MegaPhase) / 16);
+  const uint4 *s4 = reinterpret_cast<const uint4 *>(src);
+  uint4 *d4 = reinterpret_cast<uint4 *>(dst);
+  for (int i = lane; i < kWords; i += 32) d4[i] = __ldg(s4 + i);
+}
+
 // Grid barrier over all CTAs (consumer warps only). Bounded: polling stops
 // after 2^24 polls (well over a second) or as soon as any thread has raised
-// the error flag.
+// the error flag, which every poll reads beside the counter (the flag costs
+// no extra round trip once the counter is reached).
 // Returns false (the same value in every consumer thread of the CTA) when the
 // error flag is set, so the CTA's consumers leave together; the host then
 // reports IFX_ERR_TIMEOUT.
 //
-// Thread 0 also waits (bounded) for the shared-memory copy of the next phase
-// record (mbarrier `rec`, phase parity `rec_par`) and folds a failed wait
-// into the same verdict, so every consumer thread sees one answer.
-__device__ bool grid_barrier(unsigned *bar, unsigned target, int *err, uint64_t *rec,
-                             uint32_t rec_par) {
+// While thread 0 waits, warp 1 copies the next phase's record `next` into
+// `rec` (the buffer of two phases back, which every consumer has finished).
+__device__ bool grid_barrier(unsigned *bar, unsigned target, int *err, MegaPhase *rec,
+                             const MegaPhase *next) {
   __shared__ int s_err;
   consumer_sync();
   if (threadIdx.x == 0) {
@@ -93,26 +103,23 @@ __device__ bool grid_barrier(unsigned *bar, unsigned target, int *err, uint64_t 
     // above) become visible to any CTA that acquires the counter
     asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(bar) : "memory");
     uint32_t spins = 0;
-    while (ld_acquire(bar) < target) {
+    int e = 0;
+    while (true) {
+      const unsigned c = ld_acquire(bar);
+      e = *(volatile int *)err;
+      if (c >= target || e) break;
       if (++spins > (1u << 24)) {
         atomicExch(err, 401);
+        e = 401;
         break;
       }
-      if ((spins & 255u) == 0 && *(volatile int *)err) break;
     }
-    const bool rec_ok = mbar_wait(rec, rec_par, err, 404);
-    s_err = rec_ok ? *(volatile int *)err : 1;
+    s_err = e;
+  } else if ((threadIdx.x >> 5) == 1) {
+    load_record(rec, next, threadIdx.x & 31);
   }
   consumer_sync();
   return s_err == 0;
-}
-
-// Same verdict for phase 0 (no grid barrier before it).
-__device__ bool first_record(uint64_t *rec, int *err) {
-  __shared__ int s_ok;
-  if (threadIdx.x == 0) s_ok = mbar_wait(rec, 0u, err, 404) ? 1 : 0;
-  consumer_sync();
-  return s_ok != 0;
 }
 
 __device__ __forceinline__ void rope_pair_m(float &a, float &b, int i, int rope_dim, float base,
@@ -730,7 +737,8 @@ __global__ void __launch_bounds__(kGemvThreads, 1) decode_mega_kernel(const __gr
   extern __shared__ __align__(128) uint8_t smem[];
   uint64_t *full_bar = reinterpret_cast<uint64_t *>(smem);
   uint64_t *empty_bar = full_bar + kGemvMaxStages;
-  // [0] phase records, [1] ranges, [2] cached K/V rows of an attention item
+  // [0] cached K/V rows of a CTA's first attention item of a layer (fetched
+  // by the producer), [1] ranges, [2] cached K/V rows of further items
   uint64_t *xbar = reinterpret_cast<uint64_t *>(smem + kGemvBarBytes);
   MegaPhase *s_ph = reinterpret_cast<MegaPhase *>(smem + A.off_ph);     // two records
   const int2 *s_rg = reinterpret_cast<const int2 *>(smem + A.off_rg);   // this CTA's ranges
@@ -739,8 +747,12 @@ __global__ void __launch_bounds__(kGemvThreads, 1) decode_mega_kernel(const __gr
   uint8_t *abuf = smem + A.off_scr;   // attention item buffer
   uint8_t *scr = smem + A.off_stage;  // x staging of the GEMV phases
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  // the phase the consumers have entered (written by consumer thread 0 after
+  // each grid barrier; read by the producer before it refills abuf)
+  __shared__ volatile int s_phase;
   if (threadIdx.x == 0) {
     g_xzero = make_uint4(0u, 0u, 0u, 0u);
+    s_phase = -1;
     for (int s = 0; s < kRingPos; ++s) {
       mbar_init(&full_bar[s], 1);
       mbar_init(&empty_bar[s], 8);
@@ -751,61 +763,76 @@ __global__ void __launch_bounds__(kGemvThreads, 1) decode_mega_kernel(const __gr
     fence_mbar_init();
   }
   __syncthreads();
-  if (threadIdx.x == 0) {  // this CTA's range table and the first phase record
+  if (threadIdx.x == 0) {  // this CTA's range table
     const uint32_t rg_bytes = (uint32_t)(A.nph_pad * sizeof(int2));
     mbar_arrive_expect_tx(&xbar[1], rg_bytes);
     bulk_g2s(smem + A.off_rg, A.rg + (size_t)blockIdx.x * A.nph_pad, rg_bytes, &xbar[1]);
-    mbar_arrive_expect_tx(&xbar[0], (uint32_t)sizeof(MegaPhase));
-    bulk_g2s(&s_ph[0], &A.ph[0], (uint32_t)sizeof(MegaPhase), &xbar[0]);
   }
+  if (warp == 1) load_record(&s_ph[0], &A.ph[0], lane);  // the first phase record
   // every thread waits for the range table; the CTA then agrees on the outcome
+  // (the barrier also publishes the first record)
   const bool have_rg = __syncthreads_and(mbar_wait(&xbar[1], 0u, A.err, 403)) != 0;
-  if (!have_rg) {
-    if (threadIdx.x == 0) mbar_wait(&xbar[0], 0u, nullptr, 0);  // first record copy lands
-    return;
-  }
+  if (!have_rg) return;
 
+  const int pos = *A.pos;  // this step's position (advanced after the last phase)
+  const bool has_item = (int)blockIdx.x < A.G * A.nsa;  // the CTA's first attention item
   if (warp == kConsumerWarps) {
-    // producer: every GEMV phase's units for this CTA, back to back
+    // producer: every GEMV phase's units for this CTA, back to back; at each
+    // QKV phase, first the cached K/V rows of the CTA's first attention item
+    // of that layer (once the consumers have left the previous attention
+    // phase, whose items used the buffer)
     if (lane == 0) {
       uint32_t it = 0;
       RingState rs{0u, 0u, 0u};
       const RingTab rt{tab};
-      for (int p = 0; p < A.nph; ++p) {
+      int last_attn = -1, kv_fetches = 0;
+      bool ok = true;
+      for (int p = 0; p < A.nph && ok; ++p) {
         const MegaPhase &P = A.ph[p];
+        if (P.kind == PH_ATTN) last_attn = p;
         if (P.kind != PH_GEMV) continue;
+        if (P.attn_prefetch && has_item) {
+          uint32_t spins = 0;
+          while (s_phase <= last_attn) {
+            if (++spins > kSpinLimit || ((spins & 1023u) == 0 && *(volatile int *)A.err)) {
+              ok = false;
+              break;
+            }
+            __nanosleep(64);
+          }
+          if (!ok) break;
+          fence_proxy_async_smem();  // the consumers' reads of abuf come before the copy
+          attn_fetch(A, P.attn_prefetch - 1, blockIdx.x % A.G, blockIdx.x / A.G, pos, abuf, &xbar[0]);
+          ++kv_fetches;
+        }
         const int2 rg = s_rg[p];
         const int n = rg.y - rg.x;
         if (!gemv_produce(P.g, rg.x, n, it, ring, (uint32_t)A.ring_bytes, rt, rs, full_bar,
-                          empty_bar, A.err))
-          return;  // gemv_produce drained its copies
+                          empty_bar, A.err)) {
+          ok = false;  // gemv_produce drained its copies
+          break;
+        }
         it += (uint32_t)n;
       }
-      ring_drain(full_bar, kRingPos, it);
+      if (ok) ring_drain(full_bar, kRingPos, it);
+      // leave no K/V copy in flight (its phase completes when its bytes land)
+      if (kv_fetches > 0) mbar_wait(&xbar[0], (uint32_t)(kv_fetches - 1) & 1u, nullptr, 0);
     }
     return;
   }
 
   uint32_t it = 0;
-  int issued = 1, landed = 0;    // phase-record copies (thread 0's view)
-  int kv_issued = 0, kv_done = 0;  // K/V row fetches (thread 0's view)
-  const int pos = *A.pos;        // this step's position (advanced after the last phase)
+  int kv_issued = 0, kv_done = 0;  // K/V row fetches of further items (thread 0's view)
+  int kv_first = 0;                // producer-fetched first items consumed
   // all-reduces done before this step (advanced by the argmax phase's last CTA)
   const unsigned ar0 = A.nranks > 1 ? *(volatile unsigned *)A.peers.epoch : 0u;
   __shared__ int s_kv_ok, s_last;
   for (int p = 0; p < A.nph; ++p) {
-    // the record of phase p was requested during phase p - 1 into the buffer
-    // of phase p - 2, which every consumer finished before the last barrier
-    const bool ok = p > 0 ? grid_barrier(A.bar, (unsigned)p * gridDim.x, A.err, &xbar[0],
-                                         (uint32_t)p & 1u)
-                          : first_record(&xbar[0], A.err);
-    if (!ok) break;  // the same answer in every consumer thread
-    landed = p + 1;
-    if (threadIdx.x == 0 && p + 1 < A.nph) {
-      mbar_arrive_expect_tx(&xbar[0], (uint32_t)sizeof(MegaPhase));
-      bulk_g2s(&s_ph[(p + 1) & 1], &A.ph[p + 1], (uint32_t)sizeof(MegaPhase), &xbar[0]);
-      issued = p + 2;
-    }
+    // the record of phase p is loaded during the barrier into the buffer of
+    // phase p - 2, which every consumer finished before the last barrier
+    if (p > 0 && !grid_barrier(A.bar, (unsigned)p * gridDim.x, A.err, &s_ph[p & 1], &A.ph[p]))
+      break;  // the same answer in every consumer thread
+    if (threadIdx.x == 0) s_phase = p;
     const MegaPhase &P = s_ph[p & 1];
     if (P.zero_ptr)
       for (int i = blockIdx.x * kConsumerThreads + threadIdx.x; i < P.zero_n;
@@ -816,10 +843,6 @@ __global__ void __launch_bounds__(kGemvThreads, 1) decode_mega_kernel(const __gr
         phase_embed(A);
         break;
       case PH_GEMV: {
-        if (P.attn_prefetch && threadIdx.x == 0 && (int)blockIdx.x < A.G * A.nsa) {
-          attn_fetch(A, P.attn_prefetch - 1, blockIdx.x % A.G, blockIdx.x / A.G, pos, abuf, &xbar[2]);
-          ++kv_issued;
-        }
         const int2 rg = s_rg[p];
         const int n = rg.y - rg.x;
         if (n > 0) {
@@ -837,15 +860,19 @@ __global__ void __launch_bounds__(kGemvThreads, 1) decode_mega_kernel(const __gr
         const int items = A.G * A.nsa;
         for (int item = blockIdx.x; item < items; item += gridDim.x) {
           if (threadIdx.x == 0) {
-            // the first item's rows were fetched during the QKV phase
-            if (item != (int)blockIdx.x) {
+            // the first item's rows were fetched by the producer ahead of the
+            // QKV phase; further items' rows are fetched here.
+            // A failed wait leaves garbage rows; the next grid barrier then
+            // ends the step with the error flag set
+            if (item == (int)blockIdx.x) {
+              s_kv_ok = mbar_wait(&xbar[0], (uint32_t)kv_first & 1u, A.err, 405);
+              ++kv_first;
+            } else {
               attn_fetch(A, P.at.layer, item % A.G, item / A.G, pos, abuf, &xbar[2]);
               ++kv_issued;
+              s_kv_ok = mbar_wait(&xbar[2], (uint32_t)kv_done & 1u, A.err, 405);
+              ++kv_done;
             }
-            // a failed wait leaves garbage rows; the next grid barrier then
-            // ends the step with the error flag set
-            s_kv_ok = mbar_wait(&xbar[2], (uint32_t)kv_done & 1u, A.err, 405);
-            ++kv_done;
           }
           consumer_sync();
           const int h = item % A.G;
@@ -882,9 +909,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) decode_mega_kernel(const __gr
         break;
     }
   }
-  // leave no record copy in flight: after an early exit the last requested
-  // record (copy number issued - 1) may still be landing
-  if (threadIdx.x == 0 && issued > landed) mbar_wait(&xbar[0], (uint32_t)(issued - 1) & 1u, nullptr, 0);
+  // leave no K/V copy of this thread in flight
   if (threadIdx.x == 0 && kv_issued > kv_done) mbar_wait(&xbar[2], (uint32_t)kv_done & 1u, nullptr, 0);
   (void)s_kv_ok;
 }
