@@ -5,7 +5,7 @@
 // GEMV; logits GEMV; argmax). The attention phase's split-K partials are
 // combined by the CTA that finishes each kv head's last split, and the cached
 // K/V rows of each CTA's first attention item are bulk-copied into shared
-// memory during the QKV phase. Phases that read the previous phase's
+// memory by the producer warp ahead of the QKV phase. Phases that read the previous phase's
 // output are separated by a grid barrier (atomic counter with a bounded
 // spin). The producer warp does not take part in the barriers: weights do
 // not depend on activations, so it streams every GEMV phase's units for its
