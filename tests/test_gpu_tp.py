@@ -1,16 +1,16 @@
-"""Tensor-parallel decode and prefill on two GPUs against the CPU oracle.
+"""Tensor-parallel decode and prefill on 2, 4 and 8 GPUs against the CPU oracle.
 
-Two spawned ranks, each on its own GPU, load the same synthetic GGUF with
-tp_size 2 through a communicator made by the library (ifx_tp_unique_id /
+Spawned ranks, each on its own GPU, load the same synthetic GGUF with
+tp_size equal to the rank count through a communicator made by the library (ifx_tp_unique_id /
 ifx_tp_comm_create), run a prefill and greedy decode steps, and hand their
 (all-gathered, hence full) logits to the parent, which holds them to the
 oracle at the parity bar and to each other bit for bit. Decode runs both
 ways: the persistent kernel with its all-reduces over peer memory inside
 the step, and the per-op kernels with NCCL between them. The ranks do no
-checking themselves, so neither can leave the other waiting in a
-collective; the parent kills both if they do not report in time. NVLS is
+checking themselves, so none can leave another waiting in a
+collective; the parent kills them all if they do not report in time. NVLS is
 off (NCCL_NVLS_ENABLE=0) and the kernel's own waits use plain peer loads.
-Skipped with fewer than two GPUs.
+Each case is skipped when the box has fewer GPUs than it has ranks.
 """
 import os
 
@@ -56,15 +56,13 @@ def _close(a, b):
     return np.all(np.abs(a - b) <= ATOL + RTOL * np.abs(b))
 
 
-@pytest.mark.parametrize("mix,persistent,heads", [(1, True, 8), (0, True, 8), (1, False, 8),
-                                                  (0, False, 8), (1, True, 16)])
-def test_tp2_matches_oracle(mix, persistent, heads):
-    """mix 1: Q4_K_M, 0: all Q8_0; heads 16 over 2 kv heads: 8 query heads
-    per kv head on each rank, as in the 70B shape."""
-    if torch.cuda.device_count() < 2:
-        pytest.skip("needs two GPUs")
-    g = synth.build(None, vocab=2048, dim=64 * heads, n_layers=2, n_heads=heads, n_kv_heads=2,
-                    ffn=1024, context=128, rope_base=500000.0, mix=mix, seed=21)
+def _run(world, mix, persistent, heads, kv_heads):
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+    # each rank's slice of the FFN rows (W2's columns) is a whole 256-column super-block
+    g = synth.build(None, vocab=2048, dim=64 * heads, n_layers=2, n_heads=heads,
+                    n_kv_heads=kv_heads, ffn=max(1024, 256 * world), context=128,
+                    rope_base=500000.0, mix=mix, seed=21)
     prompt = synth.prompt_ids(2048, 10, seed=3)
     o = R.Model(g)
     okv = o.kv_cache(2, 128)
@@ -80,8 +78,8 @@ def test_tp2_matches_oracle(mix, persistent, heads):
     uid = tp.unique_id()
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    procs = [ctx.Process(target=_rank, args=(r, 2, uid, g, prompt, steps, q, persistent))
-             for r in range(2)]
+    procs = [ctx.Process(target=_rank, args=(r, world, uid, g, prompt, steps, q, persistent))
+             for r in range(world)]
     for p in procs:
         p.start()
     res = {}
@@ -94,15 +92,32 @@ def test_tp2_matches_oracle(mix, persistent, heads):
             p.join(timeout=30)
             if p.is_alive():
                 p.kill()
-    for r in (0, 1):
+    for r in range(world):
         assert isinstance(res.get(r), dict), res.get(r)
-    a, b = res[0], res[1]
-    for k in ("prefill_last", "prefill_all", "decode"):
-        assert np.array_equal(a[k], b[k]), k  # gathered logits are the same on both ranks
+    a = res[0]
+    for r in range(1, world):  # gathered logits are the same on every rank
+        for k in ("prefill_last", "prefill_all", "decode"):
+            assert np.array_equal(a[k], res[r][k]), (r, k)
+        assert np.array_equal(a["greedy"], res[r]["greedy"]), r
     assert _close(a["prefill_last"], ref_last), float(np.max(np.abs(a["prefill_last"] - ref_last)))
     assert _close(a["prefill_all"], ref_all), float(np.max(np.abs(a["prefill_all"] - ref_all)))
     for i, r in enumerate(ref_dec):
         assert _close(a["decode"][i], r), (i, float(np.max(np.abs(a["decode"][i] - r))))
-    assert np.array_equal(a["greedy"], b["greedy"])
     # the persistent kernel, or the per-op kernels with the collectives between them
     assert a["kernels"] == (1 if persistent else 3 + 5 * 2)
+
+
+@pytest.mark.parametrize("mix,persistent,heads", [(1, True, 8), (0, True, 8), (1, False, 8),
+                                                  (0, False, 8), (1, True, 16)])
+def test_tp2_matches_oracle(mix, persistent, heads):
+    """mix 1: Q4_K_M, 0: all Q8_0; heads 16 over 2 kv heads: 8 query heads
+    per kv head on each rank, as in the 70B shape."""
+    _run(2, mix, persistent, heads, 2)
+
+
+@pytest.mark.parametrize("world,persistent,heads", [(4, True, 16), (4, False, 16), (8, True, 32),
+                                                    (8, False, 32)])
+def test_tp4_tp8_match_oracle(world, persistent, heads):
+    """Four and eight ranks, one kv head each (the 8B shape's split at tp8,
+    the 70B shape's at tp8 with 32 query heads: 4 per kv head), Q4_K_M."""
+    _run(world, 1, persistent, heads, world)
