@@ -155,6 +155,16 @@ __host__ __device__ __forceinline__ int attn_cap(int max_seq, int nsa) {
   return ((max_seq + nsa - 1) / nsa + 1 + 15) & ~15;
 }
 
+// Splits per kv head for this step: the fewest that keep every item within
+// the rows one item's buffer holds (ceil(max_seq / A.nsa), A.nsa splits of
+// a full cache), but at least A.nsa_base (the count that spreads the items
+// over the SMs). A short context in a large cache thus takes fewer rounds of
+// items and a smaller combine.
+__device__ __forceinline__ int step_splits(const MegaArgs &A, int pos) {
+  const int rmax = (A.max_seq + A.nsa - 1) / A.nsa;
+  return min(A.nsa, max(A.nsa_base, (pos + 1 + rmax - 1) / rmax));
+}
+
 __device__ __forceinline__ AttnSpan attn_span(int pos, int nsa, int s) {
   const int len = pos + 1;
   const int chunk = (len + nsa - 1) / nsa;
@@ -169,9 +179,9 @@ __device__ __forceinline__ AttnSpan attn_span(int pos, int nsa, int s) {
 // Thread 0: bulk-copy the cached K and V rows [t0, t0 + nold) of kv head h
 // (layer `layer`) into the attention buffer, completing on `kvbar`. With no
 // rows the barrier is completed by a plain arrive.
-__device__ __noinline__ void attn_fetch(const MegaArgs &A, int layer, int h, int s, int pos, uint8_t *abuf,
-                           uint64_t *kvbar) {
-  const AttnSpan sp = attn_span(pos, A.nsa, s);
+__device__ __noinline__ void attn_fetch(const MegaArgs &A, int layer, int h, int s, int pos, int ns,
+                                       uint8_t *abuf, uint64_t *kvbar) {
+  const AttnSpan sp = attn_span(pos, ns, s);
   const int hd = A.hd;
   const int cap = attn_cap(A.max_seq, A.nsa);
   const uint32_t bytes = (uint32_t)sp.nold * (uint32_t)hd * 2u;
@@ -190,12 +200,12 @@ __device__ __noinline__ void attn_fetch(const MegaArgs &A, int layer, int h, int
 // qkv), softmax statistics, P.V; partial (max, sum, output) to global.
 // The cached rows must have landed (kvbar waited by the caller).
 __device__ __noinline__ void attn_item(const MegaArgs &A, const MegaAttn &at, int h, int s, int pos,
-                          uint8_t *abuf) {
+                                      int NS, uint8_t *abuf) {
   const int tid = threadIdx.x;
-  const int hd = A.hd, grp = A.H / A.G, NS = A.nsa;
+  const int hd = A.hd, grp = A.H / A.G;
   const AttnSpan sp = attn_span(pos, NS, s);
   const int t0 = sp.t0, nk = sp.nk;
-  const int cap = attn_cap(A.max_seq, NS);
+  const int cap = attn_cap(A.max_seq, A.nsa);
   const int n16 = hd / 8;  // 16-byte chunks per row
   const uint4 *Ks = reinterpret_cast<const uint4 *>(abuf);             // [cap][n16]
   uint4 *Vs4 = reinterpret_cast<uint4 *>(abuf + (size_t)cap * hd * 2);  // [cap][n16]
@@ -326,14 +336,14 @@ __device__ __noinline__ void attn_item(const MegaArgs &A, const MegaAttn &at, in
 // tiles (hi planes, lo planes). Output format as attn_item.
 template <int W>
 __device__ __noinline__ void attn_item_tc(const MegaArgs &A, const MegaAttn &at, int h, int s,
-                                          int pos, uint8_t *abuf) {
+                                          int pos, int NS, uint8_t *abuf) {
   static_assert(W == 4 || W == 8, "head slots per plane");
   constexpr int NT = W / 4;  // 8-column B tiles per MMA step
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, c = lane & 3;
-  const int hd = A.hd, grp = A.H / A.G, NS = A.nsa;
+  const int hd = A.hd, grp = A.H / A.G;
   const AttnSpan sp = attn_span(pos, NS, s);
   const int t0 = sp.t0, nk = sp.nk, nk16 = (nk + 15) & ~15;
-  const int cap = attn_cap(A.max_seq, NS);
+  const int cap = attn_cap(A.max_seq, A.nsa);
   const int qs = hd + 8, ps = cap + 8;  // padded row strides (conflict-free B loads)
   __half *Ks = reinterpret_cast<__half *>(abuf);  // [cap][hd], rows chunk-swizzled
   __half *Vs = Ks + (size_t)cap * hd;               // [cap][hd]
@@ -483,9 +493,9 @@ __device__ __noinline__ void attn_item_tc(const MegaArgs &A, const MegaAttn &at,
 // form the weights; one memory round trip instead of three.
 constexpr int kCombineLoads = 12;
 
-__device__ __forceinline__ void combine_kv_head_fast(const MegaArgs &A, int h, float *wbuf) {
+__device__ __forceinline__ void combine_kv_head_fast(const MegaArgs &A, int h, int NS, float *wbuf) {
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int hd = A.hd, grp = A.H / A.G, NS = A.nsa;
+  const int hd = A.hd, grp = A.H / A.G;
   float2 *ml = reinterpret_cast<float2 *>(wbuf);  // [grp][NS]
   float *wn = wbuf + 2 * grp * NS;                 // [grp][NS]
   const int F = grp * hd / 4;                      // output float4s
@@ -547,11 +557,11 @@ __device__ __forceinline__ void combine_kv_head_fast(const MegaArgs &A, int h, f
   if (mine && half == 0) reinterpret_cast<float4 *>(A.attn + (size_t)h * grp * hd)[f] = o;
 }
 
-__device__ __noinline__ void combine_kv_head(const MegaArgs &A, int h, float *wbuf) {
+__device__ __noinline__ void combine_kv_head(const MegaArgs &A, int h, int NS, float *wbuf) {
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int hd = A.hd, grp = A.H / A.G, NS = A.nsa;
+  const int hd = A.hd, grp = A.H / A.G;
   if (grp * hd <= 512 && NS <= 2 * kCombineLoads && NS <= 128 && grp <= 8) {
-    combine_kv_head_fast(A, h, wbuf);
+    combine_kv_head_fast(A, h, NS, wbuf);
     return;
   }
   float2 *ml = reinterpret_cast<float2 *>(wbuf);  // [grp][NS]
@@ -775,7 +785,8 @@ __global__ void __launch_bounds__(kGemvThreads, 1) decode_mega_kernel(const __gr
   if (!have_rg) return;
 
   const int pos = *A.pos;  // this step's position (advanced after the last phase)
-  const bool has_item = (int)blockIdx.x < A.G * A.nsa;  // the CTA's first attention item
+  const int nsa = step_splits(A, pos);                // attention splits per kv head this step
+  const bool has_item = (int)blockIdx.x < A.G * nsa;  // the CTA's first attention item
   if (warp == kConsumerWarps) {
     // producer: every GEMV phase's units for this CTA, back to back; at each
     // QKV phase, first the cached K/V rows of the CTA's first attention item
@@ -802,7 +813,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) decode_mega_kernel(const __gr
           }
           if (!ok) break;
           fence_proxy_async_smem();  // the consumers' reads of abuf come before the copy
-          attn_fetch(A, P.attn_prefetch - 1, blockIdx.x % A.G, blockIdx.x / A.G, pos, abuf, &xbar[0]);
+          attn_fetch(A, P.attn_prefetch - 1, blockIdx.x % A.G, blockIdx.x / A.G, pos, nsa, abuf, &xbar[0]);
           ++kv_fetches;
         }
         const int2 rg = s_rg[p];
@@ -857,7 +868,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) decode_mega_kernel(const __gr
         break;
       }
       case PH_ATTN: {
-        const int items = A.G * A.nsa;
+        const int items = A.G * nsa;
         for (int item = blockIdx.x; item < items; item += gridDim.x) {
           if (threadIdx.x == 0) {
             // the first item's rows were fetched by the producer ahead of the
@@ -868,7 +879,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) decode_mega_kernel(const __gr
               s_kv_ok = mbar_wait(&xbar[0], (uint32_t)kv_first & 1u, A.err, 405);
               ++kv_first;
             } else {
-              attn_fetch(A, P.at.layer, item % A.G, item / A.G, pos, abuf, &xbar[2]);
+              attn_fetch(A, P.at.layer, item % A.G, item / A.G, pos, nsa, abuf, &xbar[2]);
               ++kv_issued;
               s_kv_ok = mbar_wait(&xbar[2], (uint32_t)kv_done & 1u, A.err, 405);
               ++kv_done;
@@ -877,23 +888,23 @@ __global__ void __launch_bounds__(kGemvThreads, 1) decode_mega_kernel(const __gr
           consumer_sync();
           const int h = item % A.G;
           if (A.attn_tc == 8)
-            attn_item_tc<8>(A, P.at, h, item / A.G, pos, abuf);
+            attn_item_tc<8>(A, P.at, h, item / A.G, pos, nsa, abuf);
           else if (A.attn_tc)
-            attn_item_tc<4>(A, P.at, h, item / A.G, pos, abuf);
+            attn_item_tc<4>(A, P.at, h, item / A.G, pos, nsa, abuf);
           else
-            attn_item(A, P.at, h, item / A.G, pos, abuf);
+            attn_item(A, P.at, h, item / A.G, pos, nsa, abuf);
           // split-K fixup: the CTA that finishes kv head h's last split
           // combines the head (release by every item, acquire by the last)
           if (threadIdx.x == 0) {
             __threadfence();
             // the counters run over all layers of the step (zeroed per launch)
             s_last = atomicAdd(&A.bar[1 + h], 1u) ==
-                     (unsigned)((P.at.layer + 1) * A.nsa) - 1u;
+                     (unsigned)((P.at.layer + 1) * nsa) - 1u;
           }
           consumer_sync();
           if (s_last) {
             __threadfence();
-            combine_kv_head(A, h, reinterpret_cast<float *>(abuf));
+            combine_kv_head(A, h, nsa, reinterpret_cast<float *>(abuf));
             consumer_sync();  // the buffer is reused by the next item
           }
         }
@@ -916,11 +927,15 @@ __global__ void __launch_bounds__(kGemvThreads, 1) decode_mega_kernel(const __gr
 
 }  // namespace
 
-int mega_attn_splits(int G, int max_seq, int num_sms) {
+int mega_attn_splits_base(int G, int num_sms) {
   // at most 18 splits per kv head unless the rows demand more: the split
   // combine of the last CTA per kv head grows with the split count (37
   // splits at 4 kv heads per rank made it a 7 us tail per layer)
-  int ns = std::max(1, std::min(num_sms / std::max(1, G), 18));
+  return std::max(1, std::min(num_sms / std::max(1, G), 18));
+}
+
+int mega_attn_splits(int G, int max_seq, int num_sms) {
+  int ns = mega_attn_splits_base(G, num_sms);
   ns = std::max(ns, (max_seq + 79) / 80);  // at most ~80 cached rows per item
   return std::min(ns, kMaxSplitsMega);
 }

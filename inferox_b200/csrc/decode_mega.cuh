@@ -66,7 +66,10 @@ struct MegaArgs {
   float *x, *attn, *logits;
   float *part_o;
   float2 *part_ml;
-  int H, G, hd, max_seq, nsa, rope_compat, rope_dim;
+  int H, G, hd, max_seq, rope_compat, rope_dim;
+  // attention splits per kv head: nsa for a full cache (it sizes the item
+  // buffer and the partials), at least nsa_base in any step
+  int nsa, nsa_base;
   int attn_tc;  // 4 / 8: attention items on tensor cores with that many head slots (head size a multiple of 64); 0: FMA loops
   float rope_base;
   const float *qkv;
@@ -91,8 +94,10 @@ struct MegaPlan {
   int grid = 0;
 };
 
-// Attention split count for a cache of max_seq rows with G kv heads.
+// Attention split count for a cache of max_seq rows with G kv heads, and the
+// fewest splits a step uses (the count that spreads items over the SMs).
 int mega_attn_splits(int G, int max_seq, int num_sms);
+int mega_attn_splits_base(int G, int num_sms);
 // Shared-memory bytes the attention phase needs.
 size_t mega_attn_scratch(int grp, int hd, int max_seq, int nsa);
 // Bytes of one rank's peer buffer for vectors of up to n floats.

@@ -831,6 +831,7 @@ ifx_status Model::build_mega(KvCache &kv) {
   if (dev_sms != kNumSMs) return IFX_OK;
   MegaArgs &A = kv.mega.args;
   A.nsa = mega_attn_splits(G, (int)kv.max_seq, kNumSMs);
+  A.nsa_base = std::min(A.nsa, mega_attn_splits_base(G, kNumSMs));
   A.attn_tc = (hd % 64 == 0 && hd <= 256 && H / G <= 8) ? (H / G <= 4 ? 4 : 8) : 0;
   IFX_TRY(dalloc(&kv.part_o, (size_t)H * A.nsa * hd));
   IFX_TRY(dalloc(&kv.part_ml, (size_t)H * A.nsa));

@@ -122,3 +122,32 @@ def test_long_greedy_matches_stepping():
             gap = abs(float(lg[tok]) - float(lg[int(toks[i])]))
             assert gap <= 1e-3, (i, gap)
             break
+
+
+def test_short_context_in_large_cache():
+    """A 512-token context in a 4096-position cache: the persistent kernel
+    splits each kv head's attention by the context's length (18 splits of
+    ~29 rows) rather than by the cache's (52), so the combine and the item
+    count follow the context; logits held to the oracle as above."""
+    kw, _ = CASES["70b_geometry"]
+    g = synth.build(None, **kw)
+    m, o = Model.from_bytes(g), R.Model(g)
+    L, V = int(m.config.n_layers), int(m.config.vocab_size)
+    n_prompt, steps = 512, 24
+    prompt = synth.prompt_ids(V, n_prompt, seq_index=9)
+    kv, okv = m.kv_cache(4096), o.kv_cache(L, 4096)
+    gl = m.prefill(prompt, kv, True)[0]
+    rl = o.prefill(prompt, okv, True)[0]
+    assert _close(gl, rl), float(np.max(np.abs(gl - rl)))
+    agree = int(R.argmax(gl) == R.argmax(rl))
+    tok = R.argmax(rl)
+    worst = 0.0
+    for i in range(steps):
+        gl, rl = m.decode_step(tok, kv), o.decode_step(tok, okv)
+        worst = max(worst, float(np.max(np.abs(gl - rl))))
+        assert _close(gl, rl), (i, worst)
+        agree += int(R.argmax(gl) == R.argmax(rl))
+        tok = R.argmax(rl)
+    print(f"short context in a large cache: worst decode logit |d| {worst:.2e}, top-1 {agree}/{steps + 1}")
+    assert agree >= 0.99 * (steps + 1), (agree, steps + 1)
+    assert kv.decode_kernels() == 1
